@@ -1,0 +1,338 @@
+/*
+ * magnetar_cuda.h -- C ABI of the B200 (sm_100a) CUDA execution provider for the Magnetar
+ * runtime.  Drop-in for the operator path of astorise/Magnetar-provider-CUDA: the reference
+ * serves the Runtime through the Rust trait `ProviderExecutionApi` implemented by
+ * `CudaExecutor` (src/executor.rs:2244-2565) over launch wrappers `CudaKernels::<op>`
+ * (src/kernels.rs:794-7132) that JIT-compile src/kernels.cu with NVRTC.  Here the kernels
+ * are precompiled sm_100a code and every entry point below is a plain C function a Rust
+ * `extern "C"` block binds directly.
+ *
+ * Conventions
+ *  - Every function returns an mg_status; MG_OK is 0.  On failure the calling thread's
+ *    mg_last_error() holds a redacted detail string (never a pointer or handle), mirroring
+ *    CudaError{code, detail} (src/error.rs:49-52).
+ *  - Work is stream-ordered on the device's stream; calls return after enqueue.  Only
+ *    downloads and the data-dependent flag checks (embedding ids, softmax rows) wait for the
+ *    device, as in the reference (src/kernels.rs:3984-3997, 4371-4378).
+ *  - Op outputs follow the reference's output-offer rule (src/executor.rs:1276-1321): when
+ *    *out is non-NULL and holds the output's dtype and element count it is written in place
+ *    (its shape is set to the result's); otherwise a new buffer is allocated from the
+ *    device's stream-ordered pool and returned in *out.
+ */
+#ifndef MAGNETAR_CUDA_H
+#define MAGNETAR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MG_ABI_VERSION 1
+#define MG_MAX_RANK 8
+
+/* Status codes.  1..9 mirror CudaErrorCode one-to-one (src/error.rs:14-42) so a Rust shim
+ * maps them into KernelError exactly as src/error.rs:97-134 does; 10..13 are the
+ * KernelError variants the executor raises itself (src/executor.rs:1422-2027). */
+typedef enum mg_status {
+    MG_OK = 0,
+    MG_SHAPE_UNSUPPORTED = 1,      /* CudaErrorCode::ShapeUnsupported */
+    MG_DTYPE_UNSUPPORTED = 2,      /* CudaErrorCode::DTypeUnsupported */
+    MG_LAYOUT_UNSUPPORTED = 3,     /* CudaErrorCode::LayoutUnsupported */
+    MG_EXECUTION_FAILED = 4,       /* CudaErrorCode::ExecutionFailed */
+    MG_OUT_OF_DEVICE_MEMORY = 5,   /* CudaErrorCode::OutOfDeviceMemory */
+    MG_COMPILATION_FAILED = 6,     /* CudaErrorCode::CompilationFailed (never raised: no JIT) */
+    MG_DRIVER_FAILED = 7,          /* CudaErrorCode::DriverFailed */
+    MG_DEVICE_UNAVAILABLE = 8,     /* CudaErrorCode::DeviceUnavailable */
+    MG_CAPTURE_UNSUPPORTED = 9,    /* CudaErrorCode::CaptureUnsupported */
+    MG_KERNEL_NOT_FOUND = 10,      /* KernelError::KernelNotFound */
+    MG_ATTRIBUTE_UNSUPPORTED = 11, /* KernelError::KernelAttributeUnsupported */
+    MG_INVALID_ARGUMENT = 12,      /* a NULL handle or out-parameter */
+    MG_KERNEL_TIMEOUT = 13         /* KernelError::KernelTimeout (deadline_millis == 0) */
+} mg_status;
+
+/* Element types: f32 everywhere, f16/bf16 for add-half/mul-half
+ * (CudaHalfDType, src/kernels.rs:211-215). */
+typedef enum mg_dtype { MG_F32 = 0, MG_F16 = 1, MG_BF16 = 2 } mg_dtype;
+
+typedef struct mg_device mg_device;     /* CudaKernels + its stream (src/kernels.rs:538-616) */
+typedef struct mg_buffer mg_buffer;     /* CudaDeviceBuffer / CudaHalfBuffer (src/kernels.rs:211-276) */
+typedef struct mg_executor mg_executor; /* CudaExecutor (src/executor.rs:91-118) */
+typedef struct mg_comm mg_comm;         /* one rank of a tensor-parallel group (src/multi.rs) */
+
+/* ---------------------------------------------------------------------------------- */
+/* Library, errors                                                                     */
+/* ---------------------------------------------------------------------------------- */
+int mg_abi_version(void);
+/* Detail of the calling thread's last failure ("" when none). */
+const char* mg_last_error(void);
+/* Human-readable name of a status ("ShapeUnsupported", ...). */
+const char* mg_status_name(mg_status status);
+
+/* ---------------------------------------------------------------------------------- */
+/* Devices -- replaces CudaProvider::for_device + device discovery                     */
+/* (src/provider.rs:119-192, src/device.rs:41-92)                                      */
+/* ---------------------------------------------------------------------------------- */
+typedef struct mg_device_info {
+    int ordinal;
+    char name[96];
+    int sm_major, sm_minor; /* "sm_XY" */
+    int sm_count;
+    uint64_t total_bytes, free_bytes;
+} mg_device_info;
+
+/* Number of visible CUDA devices; 0 (and MG_OK) when no driver/device is present. */
+mg_status mg_device_count(int* count);
+/* Opens device `ordinal`: creates its stream and stream-ordered memory pool.  Returns
+ * MG_DEVICE_UNAVAILABLE when there is no such device or it is not sm_100 (graceful
+ * unavailability, src/provider.rs:149-192). */
+mg_status mg_device_open(int ordinal, mg_device** out);
+mg_status mg_device_close(mg_device* device);
+mg_status mg_device_get_info(mg_device* device, mg_device_info* info);
+/* Waits for all work on the device's stream. */
+mg_status mg_device_synchronize(mg_device* device);
+/* The device's cudaStream_t (as void*). */
+void* mg_device_stream(mg_device* device);
+/* Makes the device enqueue on `stream` (a cudaStream_t of the same device) instead of
+ * its own; NULL restores its own stream. */
+mg_status mg_device_set_stream(mg_device* device, void* stream);
+/* Upload/download counters (src/kernels.rs:546-552, 1453-1466). */
+mg_status mg_device_counters(mg_device* device, uint64_t* uploads, uint64_t* downloads);
+/* Number of kernels this library has launched on the device since it was opened. */
+uint64_t mg_device_launch_count(mg_device* device);
+
+/* ---------------------------------------------------------------------------------- */
+/* Buffers -- CudaKernels::{upload, upload_half, download, download_half,              */
+/* download_rows, zeros} (src/kernels.rs:1630-1641, 2118-2171, 2118-2138)              */
+/* ---------------------------------------------------------------------------------- */
+mg_status mg_buffer_create(mg_device* device, mg_dtype dtype, int rank, const uint64_t* shape,
+                           mg_buffer** out);
+/* A zero-filled buffer set on the device, with no upload (src/kernels.rs zeros). */
+mg_status mg_buffer_zeros(mg_device* device, mg_dtype dtype, int rank, const uint64_t* shape,
+                          mg_buffer** out);
+/* A non-owning view of caller-owned device memory (e.g. a framework tensor). */
+mg_status mg_buffer_wrap(mg_device* device, mg_dtype dtype, int rank, const uint64_t* shape,
+                         void* device_ptr, mg_buffer** out);
+mg_status mg_buffer_release(mg_buffer* buffer);
+/* Raw bytes in the buffer's own dtype: `bytes` must equal the buffer's byte size. */
+mg_status mg_buffer_upload(mg_buffer* buffer, const void* host, uint64_t bytes);
+mg_status mg_buffer_download(const mg_buffer* buffer, void* host, uint64_t bytes);
+/* f32 host values, encoded on the device to the buffer's dtype with the reference's
+ * round-to-nearest-even and NaN rules (src/half_precision.rs:48-117). */
+mg_status mg_buffer_upload_f32(mg_buffer* buffer, const float* host, uint64_t count);
+/* The buffer's values decoded to f32 on the host side of the call. */
+mg_status mg_buffer_download_f32(const mg_buffer* buffer, float* host, uint64_t count);
+/* Rows [first_row, first_row + rows) of a rank-2 f32 buffer (src/kernels.rs download_rows);
+ * MG_SHAPE_UNSUPPORTED when the range is outside the buffer. */
+mg_status mg_buffer_download_rows(const mg_buffer* buffer, uint64_t first_row, uint64_t rows,
+                                  float* host, uint64_t count);
+mg_status mg_buffer_shape(const mg_buffer* buffer, int* rank, uint64_t* shape /* [MG_MAX_RANK] */);
+mg_status mg_buffer_dtype(const mg_buffer* buffer, mg_dtype* dtype);
+mg_status mg_buffer_reshape(mg_buffer* buffer, int rank, const uint64_t* shape);
+void* mg_buffer_device_ptr(const mg_buffer* buffer);
+
+/* ---------------------------------------------------------------------------------- */
+/* Kernels -- one entry per advertised hot-path operator, with the validation of the    */
+/* matching CudaKernels method.                                                          */
+/* ---------------------------------------------------------------------------------- */
+
+/* add: same shape, or b a [cols]/[1, cols] row broadcast over a (src/kernels.rs:2956-3015) */
+mg_status mg_add(mg_device* d, const mg_buffer* a, const mg_buffer* b, mg_buffer** out);
+/* mul: same shape, or b of shape [1] scaling every element (src/kernels.rs:3017-3037,
+ * src/executor.rs:1917-1927) */
+mg_status mg_mul(mg_device* d, const mg_buffer* a, const mg_buffer* b, mg_buffer** out);
+/* residual-add: add's rules (src/kernels.rs:3039-3046) */
+mg_status mg_residual_add(mg_device* d, const mg_buffer* input, const mg_buffer* residual,
+                          mg_buffer** out);
+/* x * factor (src/kernels.cu:95-100; embedding's `scale`) */
+mg_status mg_scale(mg_device* d, const mg_buffer* x, float factor, mg_buffer** out);
+/* silu(x) = x * (1 / (1 + exp(-x))) (src/kernels.rs:3103-3118) */
+mg_status mg_silu(mg_device* d, const mg_buffer* x, mg_buffer** out);
+/* silu(gate) * up (src/kernels.rs:4492-4523) */
+mg_status mg_silu_mul(mg_device* d, const mg_buffer* gate, const mg_buffer* up, mg_buffer** out);
+/* Half-precision add/mul on f16 or bf16 buffers, bit-exact with the reference's integer
+ * decode -> f32 op -> RNE encode (src/kernels.rs:2227-2266, src/kernels.cu:2806-2939).
+ * Both inputs must share shape and dtype. */
+mg_status mg_add_half(mg_device* d, const mg_buffer* a, const mg_buffer* b, mg_buffer** out);
+mg_status mg_mul_half(mg_device* d, const mg_buffer* a, const mg_buffer* b, mg_buffer** out);
+/* The executor's f32-resident form of add-half/mul-half (src/executor.rs:1970-2013):
+ * f32 buffers in and out, each value passed through `dtype` exactly as the reference's
+ * host round trip does, with no host traffic.  op: 0 add, 1 mul. */
+mg_status mg_half_binary_f32(mg_device* d, const mg_buffer* a, const mg_buffer* b, mg_dtype dtype,
+                             int op, mg_buffer** out);
+
+/* embedding: rank-2 f32 table [vocab, dim], f32 ids holding integers; out [num_ids, dim].
+ * An id that is negative, non-integer or >= vocab fails the call with
+ * MG_SHAPE_UNSUPPORTED after the device reports it (src/kernels.rs:3833-3997).
+ * has_scale != 0 multiplies the rows by `scale` (src/executor.rs:1502-1518). */
+mg_status mg_embedding(mg_device* d, const mg_buffer* table, const mg_buffer* ids, int has_scale,
+                       float scale, mg_buffer** out);
+
+/* rmsnorm (src/kernels.rs:4013-4104): weight NULL for the scale-less form; weight [cols],
+ * [1, cols], the input's shape or [rows, cols]; head_count/head_dimension both 0, or both
+ * positive for per-head normalisation.  epsilon must be positive. */
+mg_status mg_rmsnorm(mg_device* d, const mg_buffer* x, const mg_buffer* weight, float epsilon,
+                     uint64_t head_count, uint64_t head_dimension, mg_buffer** out);
+
+/* rope (src/kernels.rs:4224-4355).  pairing: 0 interleaved (2i, 2i+1), 1 half-split
+ * (i, i + dimension/2).  banded_factor == 0 disables banded scaling; yarn_factor == 0
+ * disables YaRN (yarn_low/high are the correction range, amplitude the attention factor);
+ * rotated_pairs == UINT64_MAX rotates every pair. */
+typedef struct mg_rope_params {
+    float base;  /* default 10000 */
+    float scale; /* default 1 */
+    uint64_t dimension;
+    uint64_t position_offset;
+    uint64_t head_count; /* default 1 */
+    int pairing;
+    float banded_factor, low_freq_factor, high_freq_factor, original_context_length;
+    uint64_t rotated_pairs;
+    float yarn_factor, yarn_low, yarn_high, amplitude;
+} mg_rope_params;
+mg_status mg_rope(mg_device* d, const mg_buffer* x, const mg_rope_params* params, mg_buffer** out);
+
+/* softmax over the rows of a rank-2 buffer; MG_EXECUTION_FAILED when a row has no finite
+ * maximum (src/kernels.rs:4357-4386). */
+mg_status mg_softmax(mg_device* d, const mg_buffer* x, mg_buffer** out);
+
+/* matmul C = op(A) op(B) (+ addend), f32 (src/kernels.rs:4388-4436, 5518-5789).
+ * Rank-2 operands; transpose flags as the reference's transpose_a/transpose_b. */
+mg_status mg_matmul(mg_device* d, const mg_buffer* a, const mg_buffer* b, int transpose_a,
+                    int transpose_b, mg_buffer** out);
+/* matmul + bias row [n] or [1, n] (matmul-bias) */
+mg_status mg_matmul_bias(mg_device* d, const mg_buffer* a, const mg_buffer* b, const mg_buffer* bias,
+                         int transpose_a, int transpose_b, mg_buffer** out);
+/* matmul + residual [m, n] (matmul-residual) */
+mg_status mg_matmul_residual(mg_device* d, const mg_buffer* a, const mg_buffer* b,
+                             const mg_buffer* residual, int transpose_a, int transpose_b,
+                             mg_buffer** out);
+/* silu(A gate) * (A up) (gated-matmul, src/kernels.rs:4529-4917) */
+mg_status mg_gated_matmul(mg_device* d, const mg_buffer* a, const mg_buffer* gate,
+                          const mg_buffer* up, int transpose_a, int transpose_b, mg_buffer** out);
+
+/* attention (src/kernels.rs:6505-6884): q [seq, heads*D], k [kv_rows, kv_heads*D],
+ * v [kv_rows, kv_heads*Dv] -> out [seq, heads*Dv].  kv_head_count 0 = head_count;
+ * value_dimension 0 = head_dimension; window_size < 0 = none (requires causal);
+ * key_count < 0 = all kv rows; has_scale 0 = 1/sqrt(D). */
+typedef struct mg_attention_params {
+    uint64_t head_count;
+    uint64_t head_dimension;
+    uint64_t kv_head_count;
+    uint64_t value_dimension;
+    int64_t window_size;
+    int causal;
+    int64_t key_count;
+    int has_scale;
+    float scale;
+} mg_attention_params;
+mg_status mg_attention(mg_device* d, const mg_buffer* q, const mg_buffer* k, const mg_buffer* v,
+                       const mg_attention_params* params, mg_buffer** out);
+
+/* ---------------------------------------------------------------------------------- */
+/* Executor -- ProviderExecutionApi over a tensor table keyed by resource id             */
+/* (src/executor.rs:91-118, 1191-1321, 1422-2027, 2244-2565)                             */
+/* ---------------------------------------------------------------------------------- */
+typedef enum mg_attr_kind { MG_ATTR_INT = 0, MG_ATTR_FLOAT = 1, MG_ATTR_BOOL = 2, MG_ATTR_STRING = 3 } mg_attr_kind;
+
+/* One OperatorAttributeValue (Integer | Float | Boolean | String). */
+typedef struct mg_attribute {
+    const char* name;
+    int kind;
+    int64_t int_value; /* MG_ATTR_INT, MG_ATTR_BOOL (0/1) */
+    double float_value;
+    const char* string_value;
+} mg_attribute;
+
+/* One KernelInvocation: kernel name, input resource ids (with each input's descriptor
+ * dtype, NULL = all f32), one output id, attributes, deadline (-1 = none, 0 = already
+ * expired -> MG_KERNEL_TIMEOUT, src/executor.rs:1202-1210). */
+typedef struct mg_invocation {
+    const char* kernel;
+    int input_count;
+    const char* const* inputs;
+    const int* input_dtypes;
+    const char* output;
+    int attribute_count;
+    const mg_attribute* attributes;
+    int64_t deadline_millis;
+} mg_invocation;
+
+mg_status mg_executor_create(mg_device* device, mg_executor** out);
+mg_status mg_executor_destroy(mg_executor* executor);
+/* write_tensor / write_weight_tensor: HostTensor {shape, f32 data} (src/executor.rs:2339-2372).
+ * Writing an id replaces (and frees) its previous buffer. */
+mg_status mg_executor_write_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape,
+                                   const float* data);
+mg_status mg_executor_write_weight_tensor(mg_executor* ex, const char* id, int rank,
+                                          const uint64_t* shape, const float* data);
+mg_status mg_executor_write_zeroed_tensor(mg_executor* ex, const char* id, int rank,
+                                          const uint64_t* shape);
+/* Binds an existing device buffer (not copied) as resource `id`; the executor takes
+ * ownership of the handle. */
+mg_status mg_executor_adopt_buffer(mg_executor* ex, const char* id, mg_buffer* buffer);
+/* Borrowed handle of resource `id` (valid until it is rewritten or released). */
+mg_status mg_executor_buffer(mg_executor* ex, const char* id, mg_buffer** out);
+/* read_tensor: MG_SHAPE_UNSUPPORTED when `capacity` is too small, MG_EXECUTION_FAILED
+ * when there is no such resource. */
+mg_status mg_executor_read_tensor(mg_executor* ex, const char* id, float* data, uint64_t capacity,
+                                  int* rank, uint64_t* shape);
+mg_status mg_executor_read_tensor_rows(mg_executor* ex, const char* id, uint64_t first_row,
+                                       uint64_t rows, float* data, uint64_t capacity);
+/* *released = 1 when a resource was dropped (src/executor.rs release_tensor). */
+mg_status mg_executor_release_tensor(mg_executor* ex, const char* id, int* released);
+/* *present = 0 when the id is not resident. */
+mg_status mg_executor_resident_shape(mg_executor* ex, const char* id, int* present, int* rank,
+                                     uint64_t* shape);
+mg_status mg_executor_copy_tensor(mg_executor* ex, const char* from, const char* to);
+/* submit_kernel + complete_kernel in one call: runs the invocation on the stream. */
+mg_status mg_executor_submit_kernel(mg_executor* ex, const mg_invocation* invocation);
+mg_status mg_executor_synchronize(mg_executor* ex);
+/* Step capture (src/executor.rs:177-376): invocations between begin and end are recorded
+ * into one CUDA graph, replayed by mg_executor_replay_step.  Invocations that need a host
+ * read while captured (softmax) fail with MG_CAPTURE_UNSUPPORTED; embedding ids are
+ * checked once the replayed step has run. */
+mg_status mg_executor_begin_step_capture(mg_executor* ex);
+mg_status mg_executor_end_step_capture(mg_executor* ex);
+mg_status mg_executor_abort_step_capture(mg_executor* ex);
+mg_status mg_executor_replay_step(mg_executor* ex);
+/* `count` back-to-back replays, then one embedding-id check covering all of them (the flag
+ * is sticky across replays and reset by the check). */
+mg_status mg_executor_replay_steps(mg_executor* ex, int count);
+/* Observation log (src/executor.rs:1082-1100): counts of Started/Completed/Failed. */
+mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t* completed,
+                                   uint64_t* failed);
+
+/* ---------------------------------------------------------------------------------- */
+/* Tensor parallel -- src/multi.rs, src/multi/tensor_parallel.rs                        */
+/* One process per GPU; ranks join an NCCL communicator from a 128-byte unique id.      */
+/* ---------------------------------------------------------------------------------- */
+#define MG_COMM_ID_BYTES 128
+mg_status mg_comm_unique_id(unsigned char id[MG_COMM_ID_BYTES]);
+mg_status mg_comm_init(mg_device* device, int rank, int world, const unsigned char id[MG_COMM_ID_BYTES],
+                       mg_comm** out);
+mg_status mg_comm_destroy(mg_comm* comm);
+/* In-place sum of an f32 buffer across the group (replaces the serial reduce-to-root +
+ * copy-back of src/multi/tensor_parallel.rs:697-734). */
+mg_status mg_comm_all_reduce(mg_comm* comm, mg_buffer* buffer);
+/* The [start, end) share of `extent` that `member` of `parts` holds, aligned to 32 when
+ * every part can hold at least one 32-block (src/multi/tensor_parallel.rs:82-86, 300-307). */
+mg_status mg_tp_share(uint64_t extent, int parts, int member, uint64_t* start, uint64_t* end);
+/* The tensor-parallel SwiGLU MLP of one rank: h = silu(x G_s) * (x U_s) on the rank's
+ * column shards, y = h D_s on its row shard, then the sum over ranks, the all-reduce
+ * chunked along tokens so that it overlaps the down projection. */
+mg_status mg_tp_mlp(mg_comm* comm, const mg_buffer* x, const mg_buffer* gate_shard,
+                    const mg_buffer* up_shard, const mg_buffer* down_shard, int chunks,
+                    mg_buffer** out);
+/* Executor-level plan (src/multi.rs:543-562): weight ids split by columns (kind 0) or
+ * rows (kind 1) across the communicator's ranks; write_weight_tensor then keeps this
+ * rank's share, and invocations reading a row-split weight are all-reduced. */
+mg_status mg_executor_attach_comm(mg_executor* ex, mg_comm* comm);
+mg_status mg_executor_apply_tensor_parallel(mg_executor* ex, int count, const char* const* weight_ids,
+                                            const int* kinds);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAGNETAR_CUDA_H */

@@ -1,0 +1,214 @@
+"""ctypes binding of ``libmagnetar_cuda.so`` (declared in ``include/magnetar_cuda.h``).
+
+This is the same binding a Rust ``extern "C"`` block would make: opaque handles, plain
+pointers and sizes, an ``mg_status`` return code.  There is no CPU fallback: when the
+library is missing every entry point raises instead of computing anything.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libmagnetar_cuda.so")
+CSRC = os.path.join(_HERE, "csrc")
+
+MG_MAX_RANK = 8
+F32, F16, BF16 = 0, 1, 2
+ATTR_INT, ATTR_FLOAT, ATTR_BOOL, ATTR_STRING = 0, 1, 2, 3
+
+# mg_status -> the reference's CudaErrorCode / KernelError names (src/error.rs:14-42).
+STATUS_NAMES = {
+    0: "Ok", 1: "ShapeUnsupported", 2: "DTypeUnsupported", 3: "LayoutUnsupported",
+    4: "ExecutionFailed", 5: "OutOfDeviceMemory", 6: "CompilationFailed", 7: "DriverFailed",
+    8: "DeviceUnavailable", 9: "CaptureUnsupported", 10: "KernelNotFound",
+    11: "KernelAttributeUnsupported", 12: "InvalidArgument", 13: "KernelTimeout",
+}
+
+
+class CudaError(RuntimeError):
+    """A failed call: ``code`` is the status name, ``detail`` the redacted diagnostic."""
+
+    def __init__(self, status: int, detail: str):
+        self.status = status
+        self.code = STATUS_NAMES.get(status, f"Status{status}")
+        self.detail = detail
+        super().__init__(f"{self.code}: {detail}")
+
+
+class RopeParams(ctypes.Structure):
+    _fields_ = [
+        ("base", ctypes.c_float), ("scale", ctypes.c_float),
+        ("dimension", ctypes.c_uint64), ("position_offset", ctypes.c_uint64),
+        ("head_count", ctypes.c_uint64), ("pairing", ctypes.c_int),
+        ("banded_factor", ctypes.c_float), ("low_freq_factor", ctypes.c_float),
+        ("high_freq_factor", ctypes.c_float), ("original_context_length", ctypes.c_float),
+        ("rotated_pairs", ctypes.c_uint64),
+        ("yarn_factor", ctypes.c_float), ("yarn_low", ctypes.c_float),
+        ("yarn_high", ctypes.c_float), ("amplitude", ctypes.c_float),
+    ]
+
+
+class AttentionParams(ctypes.Structure):
+    _fields_ = [
+        ("head_count", ctypes.c_uint64), ("head_dimension", ctypes.c_uint64),
+        ("kv_head_count", ctypes.c_uint64), ("value_dimension", ctypes.c_uint64),
+        ("window_size", ctypes.c_int64), ("causal", ctypes.c_int),
+        ("key_count", ctypes.c_int64), ("has_scale", ctypes.c_int), ("scale", ctypes.c_float),
+    ]
+
+
+class DeviceInfo(ctypes.Structure):
+    _fields_ = [
+        ("ordinal", ctypes.c_int), ("name", ctypes.c_char * 96),
+        ("sm_major", ctypes.c_int), ("sm_minor", ctypes.c_int), ("sm_count", ctypes.c_int),
+        ("total_bytes", ctypes.c_uint64), ("free_bytes", ctypes.c_uint64),
+    ]
+
+
+class Attribute(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("int_value", ctypes.c_int64),
+        ("float_value", ctypes.c_double), ("string_value", ctypes.c_char_p),
+    ]
+
+
+class Invocation(ctypes.Structure):
+    _fields_ = [
+        ("kernel", ctypes.c_char_p), ("input_count", ctypes.c_int),
+        ("inputs", ctypes.POINTER(ctypes.c_char_p)), ("input_dtypes", ctypes.POINTER(ctypes.c_int)),
+        ("output", ctypes.c_char_p), ("attribute_count", ctypes.c_int),
+        ("attributes", ctypes.POINTER(Attribute)), ("deadline_millis", ctypes.c_int64),
+    ]
+
+
+_P = ctypes.c_void_p
+_PP = ctypes.POINTER(ctypes.c_void_p)
+_U64 = ctypes.c_uint64
+_U64P = ctypes.POINTER(ctypes.c_uint64)
+_I = ctypes.c_int
+_IP = ctypes.POINTER(ctypes.c_int)
+_F = ctypes.c_float
+_S = ctypes.c_char_p
+
+# name -> argtypes (every function returns mg_status unless listed in _RESTYPES)
+SIGNATURES = {
+    "mg_abi_version": [],
+    "mg_last_error": [],
+    "mg_status_name": [_I],
+    "mg_device_count": [_IP],
+    "mg_device_open": [_I, _PP],
+    "mg_device_close": [_P],
+    "mg_device_get_info": [_P, ctypes.POINTER(DeviceInfo)],
+    "mg_device_synchronize": [_P],
+    "mg_device_stream": [_P],
+    "mg_device_set_stream": [_P, _P],
+    "mg_device_counters": [_P, _U64P, _U64P],
+    "mg_device_launch_count": [_P],
+    "mg_buffer_create": [_P, _I, _I, _U64P, _PP],
+    "mg_buffer_zeros": [_P, _I, _I, _U64P, _PP],
+    "mg_buffer_wrap": [_P, _I, _I, _U64P, _P, _PP],
+    "mg_buffer_release": [_P],
+    "mg_buffer_upload": [_P, _P, _U64],
+    "mg_buffer_download": [_P, _P, _U64],
+    "mg_buffer_upload_f32": [_P, _P, _U64],
+    "mg_buffer_download_f32": [_P, _P, _U64],
+    "mg_buffer_download_rows": [_P, _U64, _U64, _P, _U64],
+    "mg_buffer_shape": [_P, _IP, _U64P],
+    "mg_buffer_dtype": [_P, _IP],
+    "mg_buffer_reshape": [_P, _I, _U64P],
+    "mg_buffer_device_ptr": [_P],
+    "mg_add": [_P, _P, _P, _PP],
+    "mg_mul": [_P, _P, _P, _PP],
+    "mg_residual_add": [_P, _P, _P, _PP],
+    "mg_scale": [_P, _P, _F, _PP],
+    "mg_silu": [_P, _P, _PP],
+    "mg_silu_mul": [_P, _P, _P, _PP],
+    "mg_add_half": [_P, _P, _P, _PP],
+    "mg_mul_half": [_P, _P, _P, _PP],
+    "mg_half_binary_f32": [_P, _P, _P, _I, _I, _PP],
+    "mg_embedding": [_P, _P, _P, _I, _F, _PP],
+    "mg_rmsnorm": [_P, _P, _P, _F, _U64, _U64, _PP],
+    "mg_rope": [_P, _P, ctypes.POINTER(RopeParams), _PP],
+    "mg_softmax": [_P, _P, _PP],
+    "mg_matmul": [_P, _P, _P, _I, _I, _PP],
+    "mg_matmul_bias": [_P, _P, _P, _P, _I, _I, _PP],
+    "mg_matmul_residual": [_P, _P, _P, _P, _I, _I, _PP],
+    "mg_gated_matmul": [_P, _P, _P, _P, _I, _I, _PP],
+    "mg_attention": [_P, _P, _P, _P, ctypes.POINTER(AttentionParams), _PP],
+    "mg_executor_create": [_P, _PP],
+    "mg_executor_destroy": [_P],
+    "mg_executor_write_tensor": [_P, _S, _I, _U64P, _P],
+    "mg_executor_write_weight_tensor": [_P, _S, _I, _U64P, _P],
+    "mg_executor_write_zeroed_tensor": [_P, _S, _I, _U64P],
+    "mg_executor_adopt_buffer": [_P, _S, _P],
+    "mg_executor_buffer": [_P, _S, _PP],
+    "mg_executor_read_tensor": [_P, _S, _P, _U64, _IP, _U64P],
+    "mg_executor_read_tensor_rows": [_P, _S, _U64, _U64, _P, _U64],
+    "mg_executor_release_tensor": [_P, _S, _IP],
+    "mg_executor_resident_shape": [_P, _S, _IP, _IP, _U64P],
+    "mg_executor_copy_tensor": [_P, _S, _S],
+    "mg_executor_submit_kernel": [_P, ctypes.POINTER(Invocation)],
+    "mg_executor_synchronize": [_P],
+    "mg_executor_begin_step_capture": [_P],
+    "mg_executor_end_step_capture": [_P],
+    "mg_executor_abort_step_capture": [_P],
+    "mg_executor_replay_step": [_P],
+    "mg_executor_replay_steps": [_P, _I],
+    "mg_executor_observations": [_P, _U64P, _U64P, _U64P],
+    "mg_comm_unique_id": [ctypes.c_char_p],
+    "mg_comm_init": [_P, _I, _I, ctypes.c_char_p, _PP],
+    "mg_comm_destroy": [_P],
+    "mg_comm_all_reduce": [_P, _P],
+    "mg_tp_share": [_U64, _I, _I, _U64P, _U64P],
+    "mg_tp_mlp": [_P, _P, _P, _P, _P, _I, _PP],
+    "mg_executor_attach_comm": [_P, _P],
+    "mg_executor_apply_tensor_parallel": [_P, _I, ctypes.POINTER(ctypes.c_char_p), _IP],
+}
+
+_RESTYPES = {
+    "mg_abi_version": ctypes.c_int,
+    "mg_last_error": ctypes.c_char_p,
+    "mg_status_name": ctypes.c_char_p,
+    "mg_device_stream": ctypes.c_void_p,
+    "mg_device_launch_count": ctypes.c_uint64,
+    "mg_buffer_device_ptr": ctypes.c_void_p,
+}
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compiles the native library for sm_100a with the committed Makefile (nvcc)."""
+    jobs = str(max(1, min(16, os.cpu_count() or 1)))
+    if force:
+        subprocess.run(["make", "-C", CSRC, "clean"], check=True, stdout=subprocess.DEVNULL)
+    subprocess.run(["make", "-C", CSRC, "-j", jobs], check=True, stdout=subprocess.DEVNULL)
+    return LIB_PATH
+
+
+def lib():
+    """The loaded library; raises (never falls back) when it is not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise CudaError(6, f"native library missing at {LIB_PATH}: run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        detail = lib().mg_last_error()
+        raise CudaError(status, detail.decode() if detail else "")
+
+
+def shape_array(shape):
+    arr = (ctypes.c_uint64 * max(1, len(shape)))(*[int(s) for s in shape])
+    return arr

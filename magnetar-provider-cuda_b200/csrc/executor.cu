@@ -1,0 +1,727 @@
+// The executor behind the C ABI: ProviderExecutionApi over a device tensor table keyed by
+// resource id.  Mirrors `CudaExecutor` (src/executor.rs:91-118, 1191-1321, 1422-2027):
+//
+//  - write_tensor / write_weight_tensor upload a HostTensor and replace the id's buffer;
+//  - submit_kernel dispatches by kernel name, parsing the attributes the reference parses
+//    with the same defaults and refusals, runs on the device stream, and stores the output
+//    under the invocation's output id, offering that id's previous buffer for reuse (the
+//    output-offer rule, src/executor.rs:1276-1321); a failed dispatch leaves the id's
+//    previous value in place;
+//  - step capture records the invocations into one CUDA graph and replays it, checking the
+//    embedding-id flag after each replay (src/executor.rs:177-376, src/kernels.rs:1022-1350);
+//  - with a tensor-parallel plan, weights keep this rank's share and every invocation that
+//    reads a row-split weight is summed across ranks (src/multi/tensor_parallel.rs:440-539).
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace mg {
+mg_status comm_all_reduce_buffer(mg_comm* comm, Buffer* b);
+int comm_rank(mg_comm* comm);
+int comm_world(mg_comm* comm);
+}  // namespace mg
+
+using namespace mg;
+
+struct mg_executor {
+    Device* device = nullptr;
+    mg_device* handle = nullptr;
+    std::map<std::string, Buffer*> storage;
+    std::mutex lock;
+    uint64_t started = 0, completed = 0, failed = 0;
+    // step capture
+    bool capturing = false;
+    bool capture_has_embedding = false;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    bool step_has_embedding = false;
+    uint64_t launches_at_capture = 0, graph_kernels = 0;  // kernels one replay launches
+    // tensor parallel
+    mg_comm* comm = nullptr;
+    std::map<std::string, int> plan;            // weight id -> 0 columns, 1 rows
+    std::set<std::string> sharded;              // activations holding a column share
+};
+
+namespace {
+
+struct Attrs {
+    const mg_invocation* inv;
+    const mg_attribute* find(const char* name) const {
+        for (int i = 0; i < inv->attribute_count; i++)
+            if (inv->attributes[i].name && strcmp(inv->attributes[i].name, name) == 0) return &inv->attributes[i];
+        return nullptr;
+    }
+    // src/executor.rs:1176-1185: only a Boolean counts, anything else is the default.
+    bool boolean(const char* name, bool dflt) const {
+        const mg_attribute* a = find(name);
+        return a && a->kind == MG_ATTR_BOOL ? a->int_value != 0 : dflt;
+    }
+    // src/executor.rs:1141-1150
+    float flt(const char* name, float dflt) const {
+        const mg_attribute* a = find(name);
+        return a && a->kind == MG_ATTR_FLOAT ? (float)a->float_value : dflt;
+    }
+    // src/executor.rs:1153-1164: present and not a Float is refused.
+    mg_status flt_opt(const char* name, bool* present, float* value) const {
+        const mg_attribute* a = find(name);
+        *present = false;
+        if (!a) return MG_OK;
+        if (a->kind != MG_ATTR_FLOAT) return fail(MG_ATTRIBUTE_UNSUPPORTED, "%s must be a float", name);
+        *present = true;
+        *value = (float)a->float_value;
+        return MG_OK;
+    }
+    // src/executor.rs:1166-1174: a non-negative Integer, else absent.
+    bool integer(const char* name, uint64_t* value) const {
+        const mg_attribute* a = find(name);
+        if (a && a->kind == MG_ATTR_INT && a->int_value >= 0) {
+            *value = (uint64_t)a->int_value;
+            return true;
+        }
+        return false;
+    }
+    const char* string(const char* name) const {
+        const mg_attribute* a = find(name);
+        return a && a->kind == MG_ATTR_STRING ? a->string_value : nullptr;
+    }
+};
+
+mg_status store_replace(mg_executor* ex, const std::string& id, Buffer* b) {
+    auto it = ex->storage.find(id);
+    if (it != ex->storage.end() && it->second != b) buffer_free(it->second);
+    ex->storage[id] = b;
+    return MG_OK;
+}
+
+mg_status get_input(mg_executor* ex, const mg_invocation* inv, int index, Buffer** out) {
+    if (index >= inv->input_count || !inv->inputs || !inv->inputs[index])
+        return fail(MG_EXECUTION_FAILED, "missing input at index %d", index);
+    auto it = ex->storage.find(inv->inputs[index]);
+    if (it == ex->storage.end())
+        return fail(MG_EXECUTION_FAILED, "no materialized data for input resource %s", inv->inputs[index]);
+    *out = it->second;
+    return MG_OK;
+}
+
+// src/executor.rs:1238-1249: accumulation_dtype, when given, must be f32.
+mg_status require_f32_accumulation(const Attrs& at) {
+    const char* s = at.string("accumulation_dtype");
+    if (s && strcmp(s, "f32") != 0 && strcmp(s, "float32") != 0 && strcmp(s, "Float32") != 0)
+        return fail(MG_DTYPE_UNSUPPORTED, "the CUDA Provider only accumulates in f32; requested %s", s);
+    return MG_OK;
+}
+
+// YaRN's correction range (the published algorithm: the dimension index whose wavelength
+// completes `rotations` turns over the original context), clamped to [0, dimension - 1].
+void yarn_correction_range(double beta_fast, double beta_slow, uint64_t dimension, double base, double original,
+                           float* low, float* high) {
+    auto corr = [&](double rotations) {
+        return (double)dimension * std::log(original / (rotations * 2.0 * M_PI)) / (2.0 * std::log(base));
+    };
+    double lo = std::floor(corr(beta_fast)), hi = std::ceil(corr(beta_slow));
+    lo = lo < 0 ? 0 : lo;
+    hi = hi > (double)(dimension - 1) ? (double)(dimension - 1) : hi;
+    *low = (float)lo;
+    *high = (float)hi;
+}
+
+inline mg_buffer* H(Buffer* b) { return reinterpret_cast<mg_buffer*>(b); }
+
+// The body of run_invocation_with_offer (src/executor.rs:1422-2027).  `out` holds the
+// offered previous output buffer (or null) and receives the result.
+mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
+    const char* name = inv->kernel;
+    Attrs at{inv};
+    mg_device* dh = ex->handle;
+    Buffer *a = nullptr, *b = nullptr, *c = nullptr;
+    if (!strcmp(name, "matmul") || !strcmp(name, "matmul-bias") || !strcmp(name, "matmul-residual") ||
+        !strcmp(name, "gated-matmul")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        const int ta = at.boolean("transpose_a", false), tb = at.boolean("transpose_b", false);
+        MG_TRY(require_f32_accumulation(at));
+        if (!strcmp(name, "matmul")) return mg_matmul(dh, H(a), H(b), ta, tb, out);
+        MG_TRY(get_input(ex, inv, 2, &c));
+        if (!strcmp(name, "matmul-bias")) return mg_matmul_bias(dh, H(a), H(b), H(c), ta, tb, out);
+        if (!strcmp(name, "matmul-residual")) return mg_matmul_residual(dh, H(a), H(b), H(c), ta, tb, out);
+        return mg_gated_matmul(dh, H(a), H(b), H(c), ta, tb, out);
+    }
+    if (!strcmp(name, "silu-mul")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        return mg_silu_mul(dh, H(a), H(b), out);
+    }
+    if (!strcmp(name, "embedding")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        bool has_scale;
+        float scale = 1.0f;
+        MG_TRY(at.flt_opt("scale", &has_scale, &scale));
+        if (ex->capturing) ex->capture_has_embedding = true;
+        return mg_embedding(dh, H(a), H(b), has_scale ? 1 : 0, scale, out);
+    }
+    if (!strcmp(name, "rmsnorm")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        if (inv->input_count > 1) MG_TRY(get_input(ex, inv, 1, &b));
+        const mg_attribute* ws = at.find("with_scale");
+        if (ws && ws->kind == MG_ATTR_BOOL && (ws->int_value != 0) != (b != nullptr))
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm with_scale %s contradicts its %d input(s)",
+                        ws->int_value ? "true" : "false", inv->input_count);
+        uint64_t hc = 0, hd = 0;
+        bool have_hc = false, have_hd = false;
+        for (const char* key : {"head_count", "head_dimension"}) {
+            const mg_attribute* h = at.find(key);
+            if (!h) continue;
+            if (h->kind != MG_ATTR_INT || h->int_value <= 0)
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm %s must be a positive integer", key);
+            if (!strcmp(key, "head_count")) { hc = (uint64_t)h->int_value; have_hc = true; }
+            else { hd = (uint64_t)h->int_value; have_hd = true; }
+        }
+        if (have_hc != have_hd)
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm head_count and head_dimension go together");
+        const float eps = at.flt("epsilon", 1e-6f);
+        return mg_rmsnorm(dh, H(a), b ? H(b) : nullptr, eps, hc, hd, out);
+    }
+    if (!strcmp(name, "rope")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        mg_rope_params p;
+        memset(&p, 0, sizeof p);
+        p.base = at.flt("base", 10000.0f);
+        p.scale = at.flt("scale", 1.0f);
+        if (!at.integer("dimension", &p.dimension)) return fail(MG_ATTRIBUTE_UNSUPPORTED, "dimension");
+        const char* mode = at.string("position_mode");
+        if (mode && strcmp(mode, "sequential") != 0)
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_mode '%s' is not implemented", mode);
+        const mg_attribute* po = at.find("position_offset");
+        if (po) {
+            if (po->kind != MG_ATTR_INT) return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_offset must be an integer");
+            if (po->int_value < 0)
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_offset %lld must not be negative", (long long)po->int_value);
+            p.position_offset = (uint64_t)po->int_value;
+        }
+        if (!at.integer("head_count", &p.head_count)) p.head_count = 1;
+        const mg_attribute* pr = at.find("rotation_pairing");
+        p.pairing = 0;
+        if (pr) {
+            if (pr->kind != MG_ATTR_STRING) return fail(MG_ATTRIBUTE_UNSUPPORTED, "rotation_pairing must be a string");
+            if (!strcmp(pr->string_value, "interleaved")) p.pairing = 0;
+            else if (!strcmp(pr->string_value, "half_split")) p.pairing = 1;
+            else return fail(MG_ATTRIBUTE_UNSUPPORTED, "rotation_pairing '%s' is not implemented", pr->string_value);
+        }
+        const char* fs = at.string("frequency_scaling");
+        p.amplitude = 1.0f;
+        if (fs && !strcmp(fs, "yarn")) {
+            const float factor = at.flt("factor", 0.0f);
+            const float original = at.flt("original_context_length", 0.0f);
+            if (!(factor > 0.0f) || !(original > 0.0f))
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "yarn needs a positive factor and original_context_length");
+            p.yarn_factor = factor;
+            yarn_correction_range(at.flt("beta_fast", 32.0f), at.flt("beta_slow", 1.0f), p.dimension, p.base, original,
+                                  &p.yarn_low, &p.yarn_high);
+            p.amplitude = at.flt("attention_factor", 1.0f);
+        } else if (fs && !strcmp(fs, "banded")) {
+            p.banded_factor = at.flt("factor", 0.0f);
+            p.low_freq_factor = at.flt("low_freq_factor", 0.0f);
+            p.high_freq_factor = at.flt("high_freq_factor", 0.0f);
+            p.original_context_length = at.flt("original_context_length", 0.0f);
+            if (!(p.banded_factor > 0.0f) || !(p.low_freq_factor > 0.0f) || !(p.high_freq_factor > p.low_freq_factor) ||
+                !(p.original_context_length > 0.0f))
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "banded frequency scaling needs factor > 0, 0 < low < high and a context length");
+        } else if (fs) {
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "frequency_scaling '%s' is not implemented", fs);
+        }
+        p.rotated_pairs = UINT64_MAX;
+        const mg_attribute* prf = at.find("partial_rotary_factor");
+        if (prf) {
+            if (prf->kind != MG_ATTR_FLOAT || !(prf->float_value > 0.0) || prf->float_value > 1.0)
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "partial_rotary_factor must be a float in (0, 1]");
+            p.rotated_pairs = (uint64_t)std::floor(prf->float_value * (double)p.dimension / 2.0);
+        }
+        return mg_rope(dh, H(a), &p, out);
+    }
+    if (!strcmp(name, "attention")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        MG_TRY(get_input(ex, inv, 2, &c));
+        mg_attention_params p;
+        memset(&p, 0, sizeof p);
+        if (!at.integer("head_count", &p.head_count)) return fail(MG_ATTRIBUTE_UNSUPPORTED, "head_count");
+        if (!at.integer("head_dimension", &p.head_dimension)) return fail(MG_ATTRIBUTE_UNSUPPORTED, "head_dimension");
+        uint64_t v;
+        p.kv_head_count = at.integer("kv_head_count", &v) ? v : 0;
+        p.window_size = at.integer("window_size", &v) ? (int64_t)v : -1;
+        p.causal = at.boolean("causal", false);
+        const char* mk = at.string("attention_mask_kind");
+        if (mk) {
+            bool expected;
+            if (!strcmp(mk, "causal")) expected = true;
+            else if (!strcmp(mk, "bidirectional")) expected = false;
+            else return fail(MG_ATTRIBUTE_UNSUPPORTED, "attention_mask_kind '%s' is not implemented", mk);
+            if (expected != (p.causal != 0))
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "attention_mask_kind '%s' is inconsistent with causal=%s", mk,
+                            p.causal ? "true" : "false");
+        }
+        p.key_count = at.integer("key_count", &v) ? (int64_t)v : -1;
+        bool has_scale;
+        float scale = 0.0f;
+        MG_TRY(at.flt_opt("scale", &has_scale, &scale));
+        p.has_scale = has_scale;
+        p.scale = scale;
+        const mg_attribute* vd = at.find("value_head_dimension");
+        if (vd) {
+            if (vd->kind != MG_ATTR_INT || vd->int_value <= 0)
+                return fail(MG_ATTRIBUTE_UNSUPPORTED, "value_head_dimension must be a positive integer");
+            p.value_dimension = (uint64_t)vd->int_value;
+        }
+        if (at.find("value_head_stride") || at.find("latent_kv_width"))
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "latent and strided-value attention forms are not implemented");
+        return mg_attention(dh, H(a), H(b), H(c), &p, out);
+    }
+    if (!strcmp(name, "softmax")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        return mg_softmax(dh, H(a), out);
+    }
+    if (!strcmp(name, "silu")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        return mg_silu(dh, H(a), out);
+    }
+    if (!strcmp(name, "activation")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        const char* kind = at.string("kind");
+        if (kind && !strcmp(kind, "silu")) return mg_silu(dh, H(a), out);
+        if (kind && !strcmp(kind, "scale")) {
+            bool present;
+            float f = 1.0f;
+            MG_TRY(at.flt_opt("factor", &present, &f));
+            if (!present) return fail(MG_ATTRIBUTE_UNSUPPORTED, "scale needs a factor");
+            return mg_scale(dh, H(a), f, out);
+        }
+        return fail(MG_ATTRIBUTE_UNSUPPORTED, "activation kind %s is not implemented", kind ? kind : "(none)");
+    }
+    if (!strcmp(name, "add")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        return mg_add(dh, H(a), H(b), out);
+    }
+    if (!strcmp(name, "mul")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        return mg_mul(dh, H(a), H(b), out);
+    }
+    if (!strcmp(name, "residual-add")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        return mg_residual_add(dh, H(a), H(b), out);
+    }
+    if (!strcmp(name, "add-half") || !strcmp(name, "mul-half")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        // src/executor.rs:71-79: the first input's descriptor names the half dtype.
+        const int dt = inv->input_dtypes ? inv->input_dtypes[0] : MG_F32;
+        if (dt != MG_F16 && dt != MG_BF16)
+            return fail(MG_DTYPE_UNSUPPORTED, "%s needs an f16 or bf16 input descriptor", name);
+        const int op = !strcmp(name, "mul-half");
+        if (a->dtype == MG_F32) return mg_half_binary_f32(dh, H(a), H(b), (mg_dtype)dt, op, out);
+        return op ? mg_mul_half(dh, H(a), H(b), out) : mg_add_half(dh, H(a), H(b), out);
+    }
+    return fail(MG_KERNEL_NOT_FOUND, "kernel '%s' is not provided", name);
+}
+
+// Role of an invocation's output under the tensor-parallel plan
+// (src/multi/tensor_parallel.rs:136-150): 2 partial (reads a row-split weight),
+// 1 sharded (reads a column share), 0 replicated.
+int tp_role(mg_executor* ex, const mg_invocation* inv) {
+    int role = 0;
+    for (int i = 0; i < inv->input_count; i++) {
+        const std::string id = inv->inputs[i];
+        auto it = ex->plan.find(id);
+        if (it != ex->plan.end()) {
+            if (it->second == 1) return 2;
+            role = 1;
+        } else if (ex->sharded.count(id)) {
+            role = 1;
+        }
+    }
+    return role;
+}
+
+mg_status upload_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape, const float* data) {
+    Buffer* nb = nullptr;
+    MG_TRY(buffer_new(ex->device, MG_F32, rank, shape, &nb));
+    if (nb->count) {
+        cudaError_t e = cudaMemcpyAsync(nb->ptr, data, nb->count * 4, cudaMemcpyHostToDevice, ex->device->stream);
+        if (e != cudaSuccess) {
+            buffer_free(nb);
+            return from_cuda(e, "CUDA device upload failed");
+        }
+    }
+    ex->device->uploads.fetch_add(1);
+    store_replace(ex, id, nb);
+    ex->sharded.erase(id);
+    return MG_OK;
+}
+
+}  // namespace
+
+namespace mg {
+// [start, end) share of `extent` for `member` of `parts`, aligned to 32-element blocks when
+// every part can hold one (src/multi/tensor_parallel.rs:82-86, 300-307).
+void tp_share(uint64_t extent, int parts, int member, uint64_t* start, uint64_t* end) {
+    const uint64_t granule = (extent % 32 == 0 && extent >= 32ull * (uint64_t)parts) ? 32 : 1;
+    const uint64_t units = extent / granule;
+    *start = units * (uint64_t)member / (uint64_t)parts * granule;
+    *end = units * (uint64_t)(member + 1) / (uint64_t)parts * granule;
+}
+}  // namespace mg
+
+extern "C" {
+
+mg_status mg_tp_share(uint64_t extent, int parts, int member, uint64_t* start, uint64_t* end) {
+    if (!start || !end) return fail(MG_INVALID_ARGUMENT, "null argument");
+    if (parts <= 0 || member < 0 || member >= parts) return fail(MG_SHAPE_UNSUPPORTED, "member %d of %d parts", member, parts);
+    tp_share(extent, parts, member, start, end);
+    return MG_OK;
+}
+
+mg_status mg_executor_create(mg_device* h, mg_executor** out) {
+    MG_TRY(device_check(h));
+    if (!out) return fail(MG_INVALID_ARGUMENT, "null output parameter");
+    mg_executor* ex = new (std::nothrow) mg_executor();
+    if (!ex) return fail(MG_EXECUTION_FAILED, "host allocation failed");
+    ex->device = dev(h);
+    ex->handle = h;
+    *out = ex;
+    return MG_OK;
+}
+
+mg_status mg_executor_destroy(mg_executor* ex) {
+    if (!ex) return MG_OK;
+    cudaSetDevice(ex->device->ordinal);
+    if (ex->graph_exec) cudaGraphExecDestroy(ex->graph_exec);
+    if (ex->graph) cudaGraphDestroy(ex->graph);
+    for (auto& kv : ex->storage) buffer_free(kv.second);
+    delete ex;
+    return MG_OK;
+}
+
+mg_status mg_executor_write_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape, const float* data) {
+    if (!ex || !id || (rank > 0 && !shape)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    MG_TRY(device_check(ex->handle));
+    return upload_tensor(ex, id, rank, shape, data);
+}
+
+mg_status mg_executor_write_weight_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape,
+                                          const float* data) {
+    if (!ex || !id || (rank > 0 && !shape)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    MG_TRY(device_check(ex->handle));
+    auto it = ex->plan.find(id);
+    if (!ex->comm || it == ex->plan.end() || rank == 0) return upload_tensor(ex, id, rank, shape, data);
+    // This rank's share (src/multi/tensor_parallel.rs:206-236).
+    const int parts = comm_world(ex->comm), member = comm_rank(ex->comm);
+    uint64_t local[MG_MAX_RANK];
+    for (int i = 0; i < rank; i++) local[i] = shape[i];
+    uint64_t count = 1;
+    for (int i = 0; i < rank; i++) count *= shape[i];
+    std::vector<float> part;
+    if (it->second == 0) {  // columns: last dimension
+        const uint64_t cols = shape[rank - 1], rows = cols ? count / cols : 0;
+        uint64_t s, e;
+        tp_share(cols, parts, member, &s, &e);
+        local[rank - 1] = e - s;
+        part.resize(rows * (e - s));
+        for (uint64_t r = 0; r < rows; r++)
+            memcpy(&part[r * (e - s)], data + r * cols + s, (e - s) * sizeof(float));
+    } else {  // rows: first dimension
+        const uint64_t rows = shape[0], per = rows ? count / rows : 0;
+        uint64_t s, e;
+        tp_share(rows, parts, member, &s, &e);
+        local[0] = e - s;
+        part.assign(data + s * per, data + e * per);
+    }
+    return upload_tensor(ex, id, rank, local, part.data());
+}
+
+mg_status mg_executor_write_zeroed_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape) {
+    if (!ex || !id || (rank > 0 && !shape)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    MG_TRY(device_check(ex->handle));
+    Buffer* nb = nullptr;
+    MG_TRY(buffer_new(ex->device, MG_F32, rank, shape, &nb));
+    mg_status s = k::fill_zero(ex->device, nb->ptr, nb->count * 4);
+    if (s != MG_OK) {
+        buffer_free(nb);
+        return s;
+    }
+    store_replace(ex, id, nb);
+    ex->sharded.erase(id);
+    return MG_OK;
+}
+
+mg_status mg_executor_adopt_buffer(mg_executor* ex, const char* id, mg_buffer* b) {
+    if (!ex || !id || !b) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (buf(b)->device != ex->device) return fail(MG_INVALID_ARGUMENT, "buffer belongs to another device");
+    store_replace(ex, id, buf(b));
+    ex->sharded.erase(id);
+    return MG_OK;
+}
+
+mg_status mg_executor_buffer(mg_executor* ex, const char* id, mg_buffer** out) {
+    if (!ex || !id || !out) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    auto it = ex->storage.find(id);
+    if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", id);
+    *out = H(it->second);
+    return MG_OK;
+}
+
+mg_status mg_executor_read_tensor(mg_executor* ex, const char* id, float* data, uint64_t capacity, int* rank,
+                                  uint64_t* shape) {
+    if (!ex || !id) return fail(MG_INVALID_ARGUMENT, "null argument");
+    Buffer* b;
+    {
+        std::lock_guard<std::mutex> g(ex->lock);
+        auto it = ex->storage.find(id);
+        if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", id);
+        b = it->second;
+    }
+    if (rank) *rank = b->rank;
+    if (shape)
+        for (int i = 0; i < b->rank; i++) shape[i] = b->shape[i];
+    if (!data) return MG_OK;
+    if (capacity < b->count)
+        return fail(MG_SHAPE_UNSUPPORTED, "%llu values cannot hold resource %s of shape %s", (unsigned long long)capacity, id,
+                    shape_str(b).c_str());
+    return mg_buffer_download_f32(H(b), data, b->count);
+}
+
+mg_status mg_executor_read_tensor_rows(mg_executor* ex, const char* id, uint64_t first_row, uint64_t rows, float* data,
+                                       uint64_t capacity) {
+    if (!ex || !id) return fail(MG_INVALID_ARGUMENT, "null argument");
+    Buffer* b;
+    {
+        std::lock_guard<std::mutex> g(ex->lock);
+        auto it = ex->storage.find(id);
+        if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", id);
+        b = it->second;
+    }
+    if (b->rank != 2) return fail(MG_SHAPE_UNSUPPORTED, "row reads need a rank-2 resource, got %s", shape_str(b).c_str());
+    if (capacity < rows * b->shape[1]) return fail(MG_SHAPE_UNSUPPORTED, "row read does not fit %llu values", (unsigned long long)capacity);
+    return mg_buffer_download_rows(H(b), first_row, rows, data, rows * b->shape[1]);
+}
+
+mg_status mg_executor_release_tensor(mg_executor* ex, const char* id, int* released) {
+    if (!ex || !id) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    auto it = ex->storage.find(id);
+    int r = 0;
+    if (it != ex->storage.end()) {
+        cudaSetDevice(ex->device->ordinal);
+        buffer_free(it->second);
+        ex->storage.erase(it);
+        r = 1;
+    }
+    ex->plan.erase(id);
+    ex->sharded.erase(id);
+    if (released) *released = r;
+    return MG_OK;
+}
+
+mg_status mg_executor_resident_shape(mg_executor* ex, const char* id, int* present, int* rank, uint64_t* shape) {
+    if (!ex || !id || !present) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    auto it = ex->storage.find(id);
+    *present = it != ex->storage.end();
+    if (*present) {
+        if (rank) *rank = it->second->rank;
+        if (shape)
+            for (int i = 0; i < it->second->rank; i++) shape[i] = it->second->shape[i];
+    }
+    return MG_OK;
+}
+
+mg_status mg_executor_copy_tensor(mg_executor* ex, const char* from, const char* to) {
+    if (!ex || !from || !to) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    MG_TRY(device_check(ex->handle));
+    auto it = ex->storage.find(from);
+    if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", from);
+    if (!strcmp(from, to)) return MG_OK;
+    Buffer* src = it->second;
+    Buffer* nb = nullptr;
+    MG_TRY(buffer_new(ex->device, src->dtype, src->rank, src->shape, &nb));
+    cudaError_t e = cudaMemcpyAsync(nb->ptr, src->ptr, src->count * dtype_size(src->dtype), cudaMemcpyDeviceToDevice,
+                                    ex->device->stream);
+    if (e != cudaSuccess) {
+        buffer_free(nb);
+        return from_cuda(e, "copying a resource");
+    }
+    store_replace(ex, to, nb);
+    if (ex->sharded.count(from)) ex->sharded.insert(to);
+    else ex->sharded.erase(to);
+    return MG_OK;
+}
+
+mg_status mg_executor_submit_kernel(mg_executor* ex, const mg_invocation* inv) {
+    if (!ex || !inv || !inv->kernel || !inv->output) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    ex->started++;
+    // src/executor.rs:1202-1210: an already-expired deadline is a timeout.
+    if (inv->deadline_millis == 0) {
+        ex->failed++;
+        return fail(MG_KERNEL_TIMEOUT, "kernel '%s' deadline expired before dispatch", inv->kernel);
+    }
+    mg_status s = device_check(ex->handle);
+    if (s != MG_OK) {
+        ex->failed++;
+        return s;
+    }
+    const std::string out_id = inv->output;
+    // Offer the output id's previous buffer unless the invocation also reads it.
+    mg_buffer* offered = nullptr;
+    bool reads_output = false;
+    for (int i = 0; i < inv->input_count; i++)
+        if (inv->inputs && inv->inputs[i] && out_id == inv->inputs[i]) reads_output = true;
+    auto prev = ex->storage.find(out_id);
+    // Kernels that fail on data after writing (an invalid embedding id, a non-finite softmax
+    // row) get a fresh buffer, so that a failure leaves the previous value intact.
+    const bool data_checked = !strcmp(inv->kernel, "embedding") || !strcmp(inv->kernel, "softmax");
+    if (prev != ex->storage.end() && !reads_output && !data_checked && prev->second->owned) offered = H(prev->second);
+    mg_buffer* result = offered;
+    const int role = ex->comm ? tp_role(ex, inv) : 0;
+    s = dispatch(ex, inv, &result);
+    if (s == MG_OK && role == 2) s = comm_all_reduce_buffer(ex->comm, buf(result));
+    if (s != MG_OK) {
+        // The previous value stays; a fresh buffer made for this call is dropped.
+        if (result && result != offered) buffer_free(buf(result));
+        ex->failed++;
+        return s;
+    }
+    store_replace(ex, out_id, buf(result));
+    if (role == 1) ex->sharded.insert(out_id);
+    else ex->sharded.erase(out_id);
+    ex->completed++;
+    return MG_OK;
+}
+
+mg_status mg_executor_synchronize(mg_executor* ex) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    return mg_device_synchronize(ex->handle);
+}
+
+mg_status mg_executor_begin_step_capture(mg_executor* ex) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (ex->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "a step capture is already in progress");
+    MG_TRY(device_check(ex->handle));
+    Device* d = ex->device;
+    MG_CUDA(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed), "beginning a step capture");
+    ex->capturing = true;
+    d->capturing = true;
+    ex->capture_has_embedding = false;
+    ex->launches_at_capture = d->launches.load();
+    return MG_OK;
+}
+
+mg_status mg_executor_end_step_capture(mg_executor* ex) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (!ex->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "no step capture is in progress");
+    Device* d = ex->device;
+    cudaGraph_t gph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(d->stream, &gph);
+    ex->capturing = d->capturing = false;
+    flush_deferred_frees(d);
+    if (e != cudaSuccess) {
+        if (gph) cudaGraphDestroy(gph);
+        return from_cuda(e, "ending the step capture");
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, gph, 0);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(gph);
+        return from_cuda(e, "instantiating the step graph");
+    }
+    if (ex->graph_exec) cudaGraphExecDestroy(ex->graph_exec);
+    if (ex->graph) cudaGraphDestroy(ex->graph);
+    ex->graph = gph;
+    ex->graph_exec = exec;
+    ex->step_has_embedding = ex->capture_has_embedding;
+    // Captured launches did not run; count them when a replay runs them.
+    ex->graph_kernels = d->launches.load() - ex->launches_at_capture;
+    d->launches.fetch_sub(ex->graph_kernels);
+    return MG_OK;
+}
+
+mg_status mg_executor_abort_step_capture(mg_executor* ex) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (!ex->capturing) return MG_OK;
+    cudaGraph_t gph = nullptr;
+    cudaStreamEndCapture(ex->device->stream, &gph);
+    cudaGetLastError();
+    if (gph) cudaGraphDestroy(gph);
+    ex->capturing = ex->device->capturing = false;
+    flush_deferred_frees(ex->device);
+    return MG_OK;
+}
+
+mg_status mg_executor_replay_steps(mg_executor* ex, int count) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
+    MG_TRY(device_check(ex->handle));
+    Device* d = ex->device;
+    for (int i = 0; i < count; i++) {
+        MG_CUDA(cudaGraphLaunch(ex->graph_exec, d->stream), "replaying the captured step");
+        d->launches.fetch_add(ex->graph_kernels);
+    }
+    if (ex->step_has_embedding) {
+        // The id flag is sticky across the replays: one read covers them all, then resets.
+        MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading the id flag");
+        MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
+        MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
+        if (d->host_flags[0])
+            return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
+    }
+    return MG_OK;
+}
+
+mg_status mg_executor_replay_step(mg_executor* ex) { return mg_executor_replay_steps(ex, 1); }
+
+mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t* completed, uint64_t* failed) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (started) *started = ex->started;
+    if (completed) *completed = ex->completed;
+    if (failed) *failed = ex->failed;
+    return MG_OK;
+}
+
+mg_status mg_executor_attach_comm(mg_executor* ex, mg_comm* comm) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    ex->comm = comm;
+    return MG_OK;
+}
+
+mg_status mg_executor_apply_tensor_parallel(mg_executor* ex, int count, const char* const* ids, const int* kinds) {
+    if (!ex || (count > 0 && (!ids || !kinds))) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (!ex->comm) return fail(MG_EXECUTION_FAILED, "a tensor-parallel plan needs a communicator (mg_executor_attach_comm)");
+    for (int i = 0; i < count; i++)
+        if (kinds[i] != 0 && kinds[i] != 1) return fail(MG_ATTRIBUTE_UNSUPPORTED, "weight shard kind %d is not implemented", kinds[i]);
+    ex->plan.clear();
+    for (int i = 0; i < count; i++) ex->plan[ids[i]] = kinds[i];
+    return MG_OK;
+}
+
+}  // extern "C"

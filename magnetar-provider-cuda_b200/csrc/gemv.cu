@@ -1,0 +1,203 @@
+// matmul for few rows (M <= 16): the decode-side GEMV path, bound by streaming B once.
+//
+// The reference gives each output column a 16-warp split-K over k with a fixed-order
+// combine (src/kernels.cu:1351-1391, 1460-1513: `matmul_split_k{,_rows}_kernel`).  Here a
+// CTA owns a 128-column tile of B and one slice of k; each warp streams whole 512-byte rows
+// of its tile with 16-byte loads (four rows in flight per warp) and applies them to every
+// row of A, which sits in shared memory.  Warps combine in a fixed order, each CTA writes
+// one partial per (slice, row, column) to a workspace, and a second kernel sums the slices
+// in slice order and applies the addend (bias row / residual) or the SwiGLU gate -- so the
+// result is deterministic, and B (the 64 MB weight at K = N = 4096) is read exactly once.
+#include "internal.h"
+
+namespace mg {
+namespace {
+
+constexpr int kMaxRows = 16;     // M handled by this path
+constexpr int kCols = 128;       // columns per CTA: 32 lanes x float4
+constexpr int kWarps = 8;
+constexpr int kRowsInFlight = 4; // B rows each warp loads before using them
+
+__device__ __forceinline__ float4 ld_stream(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// partial[(z * slices + slice) * m * n + row * n + col]; z selects B (0) or B2 (1).
+template <int M>
+__global__ void __launch_bounds__(kWarps * 32) gemv_partial_kernel(const float* __restrict__ a,
+                                                                    const float* __restrict__ b,
+                                                                    const float* __restrict__ b2,
+                                                                    float* __restrict__ partial, uint64_t m,
+                                                                    uint64_t n, uint64_t k, uint64_t slice_len,
+                                                                    int transpose_a) {
+    extern __shared__ float smem[];
+    float* a_s = smem;                      // [M][slice_len]
+    float* red = smem + M * slice_len;      // [kWarps][kCols]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t col0 = (uint64_t)blockIdx.x * kCols;
+    const uint64_t slice = blockIdx.y;
+    const uint64_t k0 = slice * slice_len;
+    const uint64_t k1 = min(k, k0 + slice_len);
+    const float* w = blockIdx.z ? b2 : b;
+
+    // Stage A[:, k0:k1] (transposed storage reads A^T[k][m]).
+    for (uint64_t i = threadIdx.x; i < (uint64_t)M * slice_len; i += blockDim.x) {
+        const uint64_t r = i / slice_len, kk = k0 + i % slice_len;
+        float v = 0.0f;
+        if (r < m && kk < k1) v = transpose_a ? a[kk * m + r] : a[r * k + kk];
+        a_s[i] = v;
+    }
+    __syncthreads();
+
+    const uint64_t col = col0 + 4 * lane;
+    const bool full = col + 3 < n;
+    float acc[M][4];
+#pragma unroll
+    for (int r = 0; r < M; r++) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+
+    uint64_t kk = k0 + warp;
+    for (; kk + (kRowsInFlight - 1) * kWarps < k1; kk += kRowsInFlight * kWarps) {
+        float4 bv[kRowsInFlight];
+#pragma unroll
+        for (int u = 0; u < kRowsInFlight; u++) {
+            const float* rowp = w + (kk + u * kWarps) * n + col;
+            if (full) bv[u] = ld_stream(reinterpret_cast<const float4*>(rowp));
+            else {
+                bv[u].x = col < n ? rowp[0] : 0.f;
+                bv[u].y = col + 1 < n ? rowp[1] : 0.f;
+                bv[u].z = col + 2 < n ? rowp[2] : 0.f;
+                bv[u].w = 0.f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kRowsInFlight; u++) {
+            const uint64_t kl = kk + u * kWarps - k0;
+#pragma unroll
+            for (int r = 0; r < M; r++) {
+                const float av = a_s[r * slice_len + kl];
+                acc[r][0] += av * bv[u].x;
+                acc[r][1] += av * bv[u].y;
+                acc[r][2] += av * bv[u].z;
+                acc[r][3] += av * bv[u].w;
+            }
+        }
+    }
+    for (; kk < k1; kk += kWarps) {
+        const float* rowp = w + kk * n + col;
+        float4 bv;
+        if (full) bv = ld_stream(reinterpret_cast<const float4*>(rowp));
+        else {
+            bv.x = col < n ? rowp[0] : 0.f;
+            bv.y = col + 1 < n ? rowp[1] : 0.f;
+            bv.z = col + 2 < n ? rowp[2] : 0.f;
+            bv.w = 0.f;
+        }
+        const uint64_t kl = kk - k0;
+#pragma unroll
+        for (int r = 0; r < M; r++) {
+            const float av = a_s[r * slice_len + kl];
+            acc[r][0] += av * bv.x;
+            acc[r][1] += av * bv.y;
+            acc[r][2] += av * bv.z;
+            acc[r][3] += av * bv.w;
+        }
+    }
+
+    // Fixed-order combine of the warps, one output row at a time.
+    float* out_base = partial + ((uint64_t)blockIdx.z * gridDim.y + slice) * m * n;
+#pragma unroll
+    for (int r = 0; r < M; r++) {
+        if (r >= (int)m) break;
+        __syncthreads();
+        *reinterpret_cast<float4*>(&red[warp * kCols + 4 * lane]) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        __syncthreads();
+        if (threadIdx.x < kCols) {
+            float s = 0.0f;
+#pragma unroll
+            for (int wi = 0; wi < kWarps; wi++) s += red[wi * kCols + threadIdx.x];
+            const uint64_t c = col0 + threadIdx.x;
+            if (c < n) out_base[r * n + c] = s;
+        }
+    }
+}
+
+// out = sum over slices (in order) [+ addend] or silu(gate) * up when gated.
+__global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                                          uint64_t m, uint64_t n, uint64_t slices,
+                                                          const float* __restrict__ addend, int addend_mode,
+                                                          int gated) {
+    const uint64_t total = m * n;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (uint64_t sl = 0; sl < slices; sl++) s += partial[sl * total + i];
+        if (gated) {
+            float u = 0.0f;
+            for (uint64_t sl = 0; sl < slices; sl++) u += partial[(slices + sl) * total + i];
+            s = (s * (1.0f / (1.0f + expf(-s)))) * u;
+        } else if (addend_mode == 1) {
+            s += addend[i % n];
+        } else if (addend_mode == 2) {
+            s += addend[i];
+        }
+        out[i] = s;
+    }
+}
+
+template <int M>
+void launch_partial(Device* d, dim3 grid, size_t smem, const k::GemmArgs& g, float* partial, uint64_t slice_len) {
+    gemv_partial_kernel<M><<<grid, kWarps * 32, smem, d->stream>>>(g.a, g.b, g.b2, partial, g.m, g.n, g.k, slice_len,
+                                                                   g.transpose_a);
+}
+
+}  // namespace
+
+namespace k {
+
+// Eligible when M <= 16, B is not transposed and its rows are 16-byte aligned.
+bool gemv_eligible(const GemmArgs& g) {
+    return g.m >= 1 && g.m <= kMaxRows && !g.transpose_b && g.n % 4 == 0 &&
+           (reinterpret_cast<uintptr_t>(g.b) & 15) == 0 && (!g.b2 || (reinterpret_cast<uintptr_t>(g.b2) & 15) == 0);
+}
+
+mg_status gemv(Device* d, const GemmArgs& g) {
+    const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
+    // Enough slices of k for about four CTAs per SM, each slice a multiple of the rows the
+    // warps consume per step and at most 512 rows (A's slice fits shared memory).
+    const uint64_t ctas_wanted = (uint64_t)d->sm_count * 4 / (g.gated ? 2 : 1);
+    uint64_t slices = (ctas_wanted + col_tiles - 1) / col_tiles;
+    const uint64_t step = kWarps * kRowsInFlight;
+    uint64_t slice_len = (g.k + slices - 1) / slices;
+    slice_len = ((slice_len + step - 1) / step) * step;
+    if (slice_len > 512) slice_len = 512;
+    if (slice_len < step) slice_len = step;
+    slices = (g.k + slice_len - 1) / slice_len;
+    if (slices == 0) slices = 1;
+    const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
+    const size_t smem = ((size_t)mp * slice_len + kWarps * kCols) * sizeof(float);
+    const int zs = g.gated ? 2 : 1;
+    float* partial = nullptr;
+    MG_TRY(scratch(d, 0, (size_t)zs * slices * g.m * g.n * sizeof(float), (void**)&partial));
+    dim3 grid((unsigned)col_tiles, (unsigned)slices, (unsigned)zs);
+    switch (mp) {
+        case 1: launch_partial<1>(d, grid, smem, g, partial, slice_len); break;
+        case 2: launch_partial<2>(d, grid, smem, g, partial, slice_len); break;
+        case 4: launch_partial<4>(d, grid, smem, g, partial, slice_len); break;
+        case 8: launch_partial<8>(d, grid, smem, g, partial, slice_len); break;
+        default: launch_partial<16>(d, grid, smem, g, partial, slice_len); break;
+    }
+    MG_TRY(launched(d, "gemv kernel launch"));
+    uint64_t total = g.m * g.n;
+    uint64_t blocks = (total + 255) / 256;
+    if (blocks > (uint64_t)d->sm_count * 8) blocks = (uint64_t)d->sm_count * 8;
+    gemv_reduce_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, d->stream>>>(partial, g.out, g.m, g.n, slices,
+                                                                              g.addend, g.addend_mode, g.gated);
+    return launched(d, "gemv reduce kernel launch");
+}
+
+}  // namespace k
+}  // namespace mg

@@ -1,0 +1,165 @@
+// Internal declarations shared by the provider's translation units: device and buffer
+// objects behind the C ABI, the status/error plumbing, and the launch functions of every
+// kernel.  Nothing here is part of the ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/magnetar_cuda.h"
+
+namespace mg {
+
+// ---- errors --------------------------------------------------------------------------
+// Sets the calling thread's last-error detail and returns `status`.
+mg_status fail(mg_status status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Maps a CUDA runtime error to the reference's categories (src/error.rs:71-91).
+mg_status from_cuda(cudaError_t err, const char* what);
+void clear_error();
+
+#define MG_TRY(expr)                          \
+    do {                                      \
+        mg_status _s = (expr);                \
+        if (_s != MG_OK) return _s;           \
+    } while (0)
+
+#define MG_CUDA(expr, what)                              \
+    do {                                                 \
+        cudaError_t _e = (expr);                         \
+        if (_e != cudaSuccess) return mg::from_cuda(_e, what); \
+    } while (0)
+
+// ---- device ----------------------------------------------------------------------------
+struct Device {
+    int ordinal = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;  // where work is enqueued
+    cudaMemPool_t pool = nullptr;
+    int sm_count = 148;
+    int sm_major = 10, sm_minor = 0;
+    std::atomic<uint64_t> uploads{0}, downloads{0}, launches{0};
+    // Device-side status words of the data-dependent checks: [0] invalid embedding id,
+    // [1] non-finite softmax row.  Pinned host mirror for the read back.
+    int* flags = nullptr;
+    int* host_flags = nullptr;
+    bool capturing = false;
+    // Workspaces grown on demand (see scratch()); freed in stream order.
+    void* scratch_ptr[8] = {nullptr};
+    size_t scratch_bytes[8] = {0};
+    // Allocations made while a step capture records the stream use plain cudaMalloc (a
+    // captured graph must keep addressing the same memory on every replay); frees requested
+    // during a capture wait until the capture ends.
+    std::set<void*> plain_allocs;
+    std::vector<void*> deferred_frees;
+};
+
+// Frees the allocations deferred while a capture was recording.
+void flush_deferred_frees(Device* d);
+
+mg_status device_check(mg_device* d);
+inline Device* dev(mg_device* d) { return reinterpret_cast<Device*>(d); }
+
+// Stream-ordered allocation from the device pool.
+mg_status device_alloc(Device* d, size_t bytes, void** ptr);
+void device_free(Device* d, void* ptr);
+
+// Scratch memory: a per-device growable workspace (stream-ordered, reused across calls).
+mg_status scratch(Device* d, int slot, size_t bytes, void** ptr);
+
+// ---- buffers -----------------------------------------------------------------------------
+struct Buffer {
+    Device* device = nullptr;
+    mg_dtype dtype = MG_F32;
+    int rank = 0;
+    uint64_t shape[MG_MAX_RANK] = {0};
+    void* ptr = nullptr;
+    uint64_t count = 0;  // elements
+    bool owned = true;
+};
+
+inline Buffer* buf(mg_buffer* b) { return reinterpret_cast<Buffer*>(b); }
+inline const Buffer* buf(const mg_buffer* b) { return reinterpret_cast<const Buffer*>(b); }
+inline size_t dtype_size(mg_dtype t) { return t == MG_F32 ? 4 : 2; }
+const char* dtype_name(mg_dtype t);
+std::string shape_str(const Buffer* b);
+bool same_shape(const Buffer* a, const Buffer* b);
+
+mg_status buffer_new(Device* d, mg_dtype dtype, int rank, const uint64_t* shape, Buffer** out);
+void buffer_free(Buffer* b);
+// Output-offer rule: reuse *out when it matches (dtype, element count), else allocate.
+mg_status output_for(Device* d, mg_dtype dtype, int rank, const uint64_t* shape, mg_buffer** out,
+                     Buffer** result);
+
+// ---- launches (all enqueue on `stream`, return cudaGetLastError() mapped) ---------------
+namespace k {
+mg_status add(Device* d, const float* a, const float* b, float* out, uint64_t n);
+mg_status bias_add(Device* d, const float* a, const float* bias, float* out, uint64_t cols, uint64_t n);
+mg_status mul(Device* d, const float* a, const float* b, float* out, uint64_t n);
+mg_status mul_scalar(Device* d, const float* a, const float* b, float* out, uint64_t n);
+mg_status scale(Device* d, const float* x, float* out, float factor, uint64_t n);
+mg_status silu(Device* d, const float* x, float* out, uint64_t n);
+mg_status silu_mul(Device* d, const float* g, const float* u, float* out, uint64_t n);
+mg_status half_binary(Device* d, const uint16_t* a, const uint16_t* b, uint16_t* out, uint64_t n,
+                      mg_dtype dtype, int op);
+mg_status half_binary_f32(Device* d, const float* a, const float* b, float* out, uint64_t n,
+                          mg_dtype dtype, int op);
+mg_status encode_half(Device* d, const float* in, uint16_t* out, uint64_t n, mg_dtype dtype);
+mg_status decode_half(Device* d, const uint16_t* in, float* out, uint64_t n, mg_dtype dtype);
+mg_status fill_zero(Device* d, void* ptr, uint64_t bytes);
+
+mg_status embedding(Device* d, const float* table, const float* ids, float* out, uint64_t dim,
+                    uint64_t num_ids, uint64_t vocab, int* flag, int has_scale, float scale);
+mg_status rmsnorm(Device* d, const float* x, const float* w, float* out, uint64_t rows,
+                  uint64_t cols, uint64_t w_stride, float eps);
+struct RopeArgs {
+    uint64_t rows, cols, half, dimension, position_offset, head_count, rotated_pairs;
+    float base, scale, banded_factor, low_freq_factor, high_freq_factor, original_context_length;
+    float yarn_factor, yarn_low, yarn_high, amplitude;
+    int half_split;
+};
+mg_status rope(Device* d, const float* x, float* out, const RopeArgs& a);
+mg_status softmax(Device* d, const float* x, float* out, uint64_t rows, uint64_t cols, int* flag);
+
+// matmul family.  lda/ldb describe row-major storage; transposes select the index order.
+struct GemmArgs {
+    const float* a;
+    const float* b;   // or gate
+    const float* b2;  // up (gated) or nullptr
+    float* out;
+    const float* addend;
+    int addend_mode;  // 0 none, 1 row [n], 2 full [m, n]
+    uint64_t m, n, k;
+    int transpose_a, transpose_b;
+    int gated;
+};
+mg_status gemm(Device* d, const GemmArgs& g);
+
+struct AttentionArgs {
+    const float* q;
+    const float* k;
+    const float* v;
+    float* out;
+    uint64_t seq_len, kv_seq_len, head_count, kv_head_count, head_dim, value_dim;
+    uint64_t q_model_dim, kv_model_dim, v_model_dim;
+    int causal;
+    int64_t window;  // -1 none
+    uint64_t query_position_offset;
+    float scale;
+};
+mg_status attention(Device* d, const AttentionArgs& a);
+}  // namespace k
+
+inline mg_status launched(Device* d, const char* what) {
+    d->launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return from_cuda(e, what);
+    return MG_OK;
+}
+
+}  // namespace mg

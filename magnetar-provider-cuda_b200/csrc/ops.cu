@@ -1,0 +1,543 @@
+// C ABI of the kernel entry points: each validates its operands exactly as the matching
+// `CudaKernels` method of the reference does (shape errors -> ShapeUnsupported, non-f32 ->
+// DTypeUnsupported), picks the output buffer by the output-offer rule, and enqueues the
+// kernel.  Citations are to src/kernels.rs of astorise/Magnetar-provider-CUDA.
+#include <cmath>
+#include <cstring>
+
+#include "internal.h"
+
+using namespace mg;
+
+namespace {
+
+mg_status need(const mg_buffer* b, const char* what) {
+    if (!b) return fail(MG_INVALID_ARGUMENT, "null %s buffer", what);
+    return MG_OK;
+}
+
+// Kernels read f32 operands only (src/kernels.rs:1375-1383).
+mg_status require_f32(const Buffer* b, const char* what) {
+    if (b->dtype != MG_F32)
+        return fail(MG_DTYPE_UNSUPPORTED, "%s does not read %s operands", what, dtype_name(b->dtype));
+    return MG_OK;
+}
+
+mg_status same_device(Device* d, const Buffer* b) {
+    if (b->device != d) return fail(MG_INVALID_ARGUMENT, "buffer belongs to another device");
+    return MG_OK;
+}
+
+// src/kernels.rs:7134-7142
+mg_status rows_cols(const Buffer* b, uint64_t* rows, uint64_t* cols) {
+    if (b->rank != 2) return fail(MG_SHAPE_UNSUPPORTED, "expected rank-2 tensor, got shape %s", shape_str(b).c_str());
+    *rows = b->shape[0];
+    *cols = b->shape[1];
+    return MG_OK;
+}
+
+bool is_row(const Buffer* b, uint64_t n) {
+    return (b->rank == 1 && b->shape[0] == n) || (b->rank == 2 && b->shape[0] == 1 && b->shape[1] == n);
+}
+
+// Waits for the stream and reads the device status words (the reference's flag reads).
+mg_status read_flags(Device* d, int* host) {
+    MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, 4 * sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading a status flag");
+    MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the device");
+    memcpy(host, d->host_flags, 4 * sizeof(int));
+    d->downloads.fetch_add(1);
+    return MG_OK;
+}
+
+// add with same-shape or row broadcast (src/kernels.rs:2956-3015)
+mg_status add_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_buffer** out, const char* what) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    MG_TRY(require_f32(a, what));
+    MG_TRY(require_f32(b, what));
+    if (same_shape(a, b)) {
+        Buffer* o;
+        MG_TRY(output_for(d, MG_F32, a->rank, a->shape, out, &o));
+        return k::add(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, a->count);
+    }
+    if (a->rank == 0) return fail(MG_SHAPE_UNSUPPORTED, "add expects at least one dimension");
+    const uint64_t cols = a->shape[a->rank - 1];
+    if (!is_row(b, cols))
+        return fail(MG_SHAPE_UNSUPPORTED, "add expects b to match a's shape %s or broadcast as [%llu]/[1, %llu], got %s",
+                    shape_str(a).c_str(), (unsigned long long)cols, (unsigned long long)cols, shape_str(b).c_str());
+    if (cols == 0 || a->count % cols != 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "add data length %llu is not divisible by broadcast dimension %llu",
+                    (unsigned long long)a->count, (unsigned long long)cols);
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, a->rank, a->shape, out, &o));
+    return k::bias_add(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, cols, a->count);
+}
+
+mg_status unary_prep(mg_device* h, const mg_buffer* xh, mg_buffer** out, const char* what, Device** d, const Buffer** x,
+                     Buffer** o) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(xh, "input"));
+    *d = dev(h);
+    *x = buf(xh);
+    MG_TRY(same_device(*d, *x));
+    MG_TRY(require_f32(*x, what));
+    return output_for(*d, MG_F32, (*x)->rank, (*x)->shape, out, o);
+}
+
+mg_status half_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_buffer** out, int op) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    // src/kernels.rs:2227-2266: both operands share shape and half dtype.
+    if (a->dtype == MG_F32 || b->dtype == MG_F32)
+        return fail(MG_DTYPE_UNSUPPORTED, "%s expects f16 or bf16 operands", op ? "mul-half" : "add-half");
+    if (a->dtype != b->dtype)
+        return fail(MG_DTYPE_UNSUPPORTED, "%s operands differ in dtype: %s vs %s", op ? "mul-half" : "add-half",
+                    dtype_name(a->dtype), dtype_name(b->dtype));
+    if (!same_shape(a, b))
+        return fail(MG_SHAPE_UNSUPPORTED, "shape mismatch: %s vs %s", shape_str(a).c_str(), shape_str(b).c_str());
+    Buffer* o;
+    MG_TRY(output_for(d, a->dtype, a->rank, a->shape, out, &o));
+    return k::half_binary(d, (const uint16_t*)a->ptr, (const uint16_t*)b->ptr, (uint16_t*)o->ptr, a->count, a->dtype, op);
+}
+
+enum AddendMode { kNone = 0, kRow = 1, kFull = 2 };
+
+// src/kernels.rs:5518-5580: shapes, transposes and the addend's shape.
+mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, const mg_buffer* b2h,
+                      const mg_buffer* addh, int addend_mode, int ta, int tb, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    uint64_t ar, ac, br, bc;
+    MG_TRY(rows_cols(a, &ar, &ac));
+    MG_TRY(rows_cols(b, &br, &bc));
+    const uint64_t m = ta ? ac : ar, kk = ta ? ar : ac;
+    const uint64_t k2 = tb ? bc : br, n = tb ? br : bc;
+    if (kk != k2)
+        return fail(MG_SHAPE_UNSUPPORTED, "matmul inner dimension mismatch: %llu vs %llu", (unsigned long long)kk,
+                    (unsigned long long)k2);
+    const Buffer* b2 = nullptr;
+    if (b2h) {
+        b2 = buf(b2h);
+        MG_TRY(same_device(d, b2));
+        if (!same_shape(b, b2))
+            return fail(MG_SHAPE_UNSUPPORTED, "gated-matmul expects gate and up to share a shape, got %s and %s",
+                        shape_str(b).c_str(), shape_str(b2).c_str());
+        MG_TRY(require_f32(b2, "gated-matmul's up"));
+    }
+    const Buffer* add = nullptr;
+    if (addh) {
+        add = buf(addh);
+        MG_TRY(same_device(d, add));
+        if (addend_mode == kRow && !is_row(add, n))
+            return fail(MG_SHAPE_UNSUPPORTED, "matmul-bias bias shape must be [%llu] or [1, %llu], got %s",
+                        (unsigned long long)n, (unsigned long long)n, shape_str(add).c_str());
+        if (addend_mode == kFull && !(add->rank == 2 && add->shape[0] == m && add->shape[1] == n))
+            return fail(MG_SHAPE_UNSUPPORTED, "matmul-residual residual shape must be [%llu, %llu], got %s",
+                        (unsigned long long)m, (unsigned long long)n, shape_str(add).c_str());
+    }
+    MG_TRY(require_f32(a, "matmul's a"));
+    MG_TRY(require_f32(b, "matmul's b"));
+    if (add) MG_TRY(require_f32(add, "a fused matmul's addend"));
+    const uint64_t shape[2] = {m, n};
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
+    k::GemmArgs g;
+    g.a = (const float*)a->ptr;
+    g.b = (const float*)b->ptr;
+    g.b2 = b2 ? (const float*)b2->ptr : nullptr;
+    g.out = (float*)o->ptr;
+    g.addend = add ? (const float*)add->ptr : nullptr;
+    g.addend_mode = add ? addend_mode : kNone;
+    g.m = m;
+    g.n = n;
+    g.k = kk;
+    g.transpose_a = ta;
+    g.transpose_b = tb;
+    g.gated = b2 ? 1 : 0;
+    return k::gemm(d, g);
+}
+
+}  // namespace
+
+extern "C" {
+
+mg_status mg_add(mg_device* h, const mg_buffer* a, const mg_buffer* b, mg_buffer** out) {
+    return add_impl(h, a, b, out, "add");
+}
+
+// src/kernels.rs:3039-3046
+mg_status mg_residual_add(mg_device* h, const mg_buffer* input, const mg_buffer* residual, mg_buffer** out) {
+    return add_impl(h, input, residual, out, "residual-add");
+}
+
+// src/kernels.rs:3017-3037; a [1] second operand scales every element (src/executor.rs:1917-1927)
+mg_status mg_mul(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    MG_TRY(require_f32(a, "mul"));
+    MG_TRY(require_f32(b, "mul"));
+    const bool scalar = b->rank == 1 && b->shape[0] == 1 && !same_shape(a, b);
+    if (!scalar && !same_shape(a, b))
+        return fail(MG_SHAPE_UNSUPPORTED, "shape mismatch: %s vs %s", shape_str(a).c_str(), shape_str(b).c_str());
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, a->rank, a->shape, out, &o));
+    if (scalar) return k::mul_scalar(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, a->count);
+    return k::mul(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, a->count);
+}
+
+mg_status mg_scale(mg_device* h, const mg_buffer* xh, float factor, mg_buffer** out) {
+    Device* d;
+    const Buffer* x;
+    Buffer* o;
+    MG_TRY(unary_prep(h, xh, out, "scale", &d, &x, &o));
+    return k::scale(d, (const float*)x->ptr, (float*)o->ptr, factor, x->count);
+}
+
+mg_status mg_silu(mg_device* h, const mg_buffer* xh, mg_buffer** out) {
+    Device* d;
+    const Buffer* x;
+    Buffer* o;
+    MG_TRY(unary_prep(h, xh, out, "silu", &d, &x, &o));
+    return k::silu(d, (const float*)x->ptr, (float*)o->ptr, x->count);
+}
+
+// src/kernels.rs:4492-4523
+mg_status mg_silu_mul(mg_device* h, const mg_buffer* gh, const mg_buffer* uh, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(gh, "gate"));
+    MG_TRY(need(uh, "up"));
+    Device* d = dev(h);
+    const Buffer* g = buf(gh);
+    const Buffer* u = buf(uh);
+    MG_TRY(same_device(d, g));
+    MG_TRY(same_device(d, u));
+    MG_TRY(require_f32(g, "silu-mul"));
+    MG_TRY(require_f32(u, "silu-mul"));
+    if (!same_shape(g, u))
+        return fail(MG_SHAPE_UNSUPPORTED, "silu-mul expects gate and up to share a shape, got %s and %s",
+                    shape_str(g).c_str(), shape_str(u).c_str());
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, g->rank, g->shape, out, &o));
+    return k::silu_mul(d, (const float*)g->ptr, (const float*)u->ptr, (float*)o->ptr, g->count);
+}
+
+mg_status mg_add_half(mg_device* h, const mg_buffer* a, const mg_buffer* b, mg_buffer** out) {
+    return half_impl(h, a, b, out, 0);
+}
+
+mg_status mg_mul_half(mg_device* h, const mg_buffer* a, const mg_buffer* b, mg_buffer** out) {
+    return half_impl(h, a, b, out, 1);
+}
+
+mg_status mg_half_binary_f32(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_dtype dtype, int op,
+                             mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    if (dtype != MG_F16 && dtype != MG_BF16)
+        return fail(MG_DTYPE_UNSUPPORTED, "add-half/mul-half need an f16 or bf16 descriptor, got %s", dtype_name(dtype));
+    MG_TRY(require_f32(a, "an f32-resident half op"));
+    MG_TRY(require_f32(b, "an f32-resident half op"));
+    if (!same_shape(a, b))
+        return fail(MG_SHAPE_UNSUPPORTED, "shape mismatch: %s vs %s", shape_str(a).c_str(), shape_str(b).c_str());
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, a->rank, a->shape, out, &o));
+    return k::half_binary_f32(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, a->count, dtype, op ? 1 : 0);
+}
+
+// src/kernels.rs:3833-3997 (f32 table path) and the executor's `scale` (src/executor.rs:1502-1518)
+mg_status mg_embedding(mg_device* h, const mg_buffer* th, const mg_buffer* ih, int has_scale, float scale,
+                       mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(th, "table"));
+    MG_TRY(need(ih, "ids"));
+    Device* d = dev(h);
+    const Buffer* t = buf(th);
+    const Buffer* ids = buf(ih);
+    MG_TRY(same_device(d, t));
+    MG_TRY(same_device(d, ids));
+    uint64_t vocab, dim;
+    MG_TRY(rows_cols(t, &vocab, &dim));
+    MG_TRY(require_f32(ids, "the embedding lookup's ids"));
+    MG_TRY(require_f32(t, "the embedding lookup's table"));
+    const uint64_t shape[2] = {ids->count, dim};
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
+    if (!d->capturing) MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
+    MG_TRY(k::embedding(d, (const float*)t->ptr, (const float*)ids->ptr, (float*)o->ptr, dim, ids->count, vocab,
+                        d->flags, has_scale, scale));
+    if (d->capturing) return MG_OK;  // checked once the captured step has run
+    int flags[4];
+    MG_TRY(read_flags(d, flags));
+    if (flags[0])
+        return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
+    return MG_OK;
+}
+
+// src/kernels.rs:4013-4104
+mg_status mg_rmsnorm(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, float epsilon, uint64_t head_count,
+                     uint64_t head_dimension, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(xh, "input"));
+    Device* d = dev(h);
+    const Buffer* x = buf(xh);
+    MG_TRY(same_device(d, x));
+    MG_TRY(require_f32(x, "rmsnorm"));
+    const Buffer* w = wh ? buf(wh) : nullptr;
+    if (w) {
+        MG_TRY(same_device(d, w));
+        MG_TRY(require_f32(w, "rmsnorm"));
+    }
+    if (x->rank == 0) return fail(MG_SHAPE_UNSUPPORTED, "RMSNorm expects at least one dimension");
+    const uint64_t row_width = x->shape[x->rank - 1];
+    const bool heads = head_count != 0 || head_dimension != 0;
+    uint64_t cols = row_width;
+    if (heads) {
+        if (head_count == 0 || head_dimension == 0 || head_count * head_dimension != row_width ||
+            row_width / head_count != head_dimension)
+            return fail(MG_SHAPE_UNSUPPORTED, "RMSNorm's %llu heads of %llu do not tile rows of %llu",
+                        (unsigned long long)head_count, (unsigned long long)head_dimension, (unsigned long long)row_width);
+        cols = head_dimension;
+    }
+    if (cols == 0 || x->count % cols != 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "RMSNorm data length %llu is not divisible by hidden dimension %llu",
+                    (unsigned long long)x->count, (unsigned long long)cols);
+    const uint64_t rows = x->count / cols;
+    uint64_t w_stride = 0;
+    if (w) {
+        if (is_row(w, cols)) {
+            w_stride = 0;
+        } else if (!heads && (same_shape(w, x) || (w->rank == 2 && w->shape[0] == rows && w->shape[1] == cols))) {
+            w_stride = cols;
+        } else {
+            return fail(MG_SHAPE_UNSUPPORTED,
+                        "RMSNorm weight shape must be [%llu], [1, %llu], input shape %s, or [%llu, %llu], got %s",
+                        (unsigned long long)cols, (unsigned long long)cols, shape_str(x).c_str(),
+                        (unsigned long long)rows, (unsigned long long)cols, shape_str(w).c_str());
+        }
+    }
+    if (!(epsilon > 0.0f)) return fail(MG_SHAPE_UNSUPPORTED, "RMSNorm epsilon must be positive");
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, x->rank, x->shape, out, &o));
+    return k::rmsnorm(d, (const float*)x->ptr, w ? (const float*)w->ptr : nullptr, (float*)o->ptr, rows, cols, w_stride,
+                      epsilon);
+}
+
+// src/kernels.rs:4224-4355
+mg_status mg_rope(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(xh, "input"));
+    if (!pp) return fail(MG_INVALID_ARGUMENT, "null rope parameters");
+    Device* d = dev(h);
+    const Buffer* x = buf(xh);
+    MG_TRY(same_device(d, x));
+    MG_TRY(require_f32(x, "rope"));
+    const mg_rope_params& p = *pp;
+    if (p.banded_factor > 0.0f && p.yarn_factor > 0.0f)
+        return fail(MG_SHAPE_UNSUPPORTED, "RoPE takes one frequency scaling, not banded and YaRN together");
+    uint64_t rows, cols;
+    MG_TRY(rows_cols(x, &rows, &cols));
+    if (p.head_count == 0 || cols % p.head_count != 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "RoPE head_count %llu must be positive and evenly divide the row width %llu",
+                    (unsigned long long)p.head_count, (unsigned long long)cols);
+    const uint64_t head_width = cols / p.head_count;
+    if (p.dimension == 0 || p.dimension % 2 != 0 || p.dimension > head_width)
+        return fail(MG_SHAPE_UNSUPPORTED,
+                    "RoPE dimension %llu must be positive, even, and at most the head width %llu",
+                    (unsigned long long)p.dimension, (unsigned long long)head_width);
+    if (!std::isfinite(p.base) || p.base <= 0.0f) return fail(MG_SHAPE_UNSUPPORTED, "RoPE base must be finite and positive");
+    if (!std::isfinite(p.scale) || p.scale <= 0.0f)
+        return fail(MG_SHAPE_UNSUPPORTED, "RoPE scale must be finite and positive");
+    if (p.pairing != 0 && p.pairing != 1) return fail(MG_SHAPE_UNSUPPORTED, "RoPE pairing %d is not implemented", p.pairing);
+    const uint64_t half = p.dimension / 2;
+    // src/kernels.rs:7184-7202: rows * head_count * half must not overflow.
+    if (p.head_count != 0 && half != 0 &&
+        (rows > UINT64_MAX / p.head_count || rows * p.head_count > UINT64_MAX / half))
+        return fail(MG_SHAPE_UNSUPPORTED, "RoPE launch size overflows: rows %llu * head_count %llu * half %llu",
+                    (unsigned long long)rows, (unsigned long long)p.head_count, (unsigned long long)half);
+    if (half * sizeof(float2) > 200 * 1024)
+        return fail(MG_SHAPE_UNSUPPORTED, "RoPE dimension %llu exceeds the supported 51200 pairs", (unsigned long long)p.dimension);
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, x->rank, x->shape, out, &o));
+    k::RopeArgs a;
+    a.rows = rows;
+    a.cols = cols;
+    a.half = half;
+    a.dimension = p.dimension;
+    a.position_offset = p.position_offset;
+    a.head_count = p.head_count;
+    a.rotated_pairs = p.rotated_pairs < half ? p.rotated_pairs : half;
+    a.base = p.base;
+    a.scale = p.scale;
+    a.banded_factor = p.banded_factor;
+    a.low_freq_factor = p.low_freq_factor;
+    a.high_freq_factor = p.high_freq_factor;
+    a.original_context_length = p.original_context_length;
+    a.yarn_factor = p.yarn_factor;
+    a.yarn_low = p.yarn_low;
+    a.yarn_high = p.yarn_high;
+    a.amplitude = p.yarn_factor > 0.0f ? p.amplitude : 1.0f;
+    a.half_split = p.pairing;
+    return k::rope(d, (const float*)x->ptr, (float*)o->ptr, a);
+}
+
+// src/kernels.rs:4357-4386
+mg_status mg_softmax(mg_device* h, const mg_buffer* xh, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(xh, "input"));
+    Device* d = dev(h);
+    const Buffer* x = buf(xh);
+    MG_TRY(same_device(d, x));
+    MG_TRY(require_f32(x, "softmax"));
+    uint64_t rows, cols;
+    MG_TRY(rows_cols(x, &rows, &cols));
+    if (d->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "softmax reads its row flag on the host and cannot be captured");
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, x->shape, out, &o));
+    MG_CUDA(cudaMemsetAsync(d->flags + 1, 0, sizeof(int), d->stream), "resetting the softmax flag");
+    MG_TRY(k::softmax(d, (const float*)x->ptr, (float*)o->ptr, rows, cols, d->flags + 1));
+    int flags[4];
+    MG_TRY(read_flags(d, flags));
+    if (flags[1]) return fail(MG_EXECUTION_FAILED, "softmax has a row with no finite entry to normalize");
+    return MG_OK;
+}
+
+mg_status mg_matmul(mg_device* h, const mg_buffer* a, const mg_buffer* b, int ta, int tb, mg_buffer** out) {
+    return matmul_impl(h, a, b, nullptr, nullptr, kNone, ta, tb, out);
+}
+
+mg_status mg_matmul_bias(mg_device* h, const mg_buffer* a, const mg_buffer* b, const mg_buffer* bias, int ta, int tb,
+                         mg_buffer** out) {
+    if (!bias) return fail(MG_INVALID_ARGUMENT, "null bias buffer");
+    return matmul_impl(h, a, b, nullptr, bias, kRow, ta, tb, out);
+}
+
+mg_status mg_matmul_residual(mg_device* h, const mg_buffer* a, const mg_buffer* b, const mg_buffer* residual, int ta,
+                             int tb, mg_buffer** out) {
+    if (!residual) return fail(MG_INVALID_ARGUMENT, "null residual buffer");
+    return matmul_impl(h, a, b, nullptr, residual, kFull, ta, tb, out);
+}
+
+mg_status mg_gated_matmul(mg_device* h, const mg_buffer* a, const mg_buffer* gate, const mg_buffer* up, int ta, int tb,
+                          mg_buffer** out) {
+    if (!up) return fail(MG_INVALID_ARGUMENT, "null up buffer");
+    return matmul_impl(h, a, gate, up, nullptr, kNone, ta, tb, out);
+}
+
+// src/kernels.rs:6505-6629
+mg_status mg_attention(mg_device* h, const mg_buffer* qh, const mg_buffer* kh, const mg_buffer* vh,
+                       const mg_attention_params* pp, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(qh, "q"));
+    MG_TRY(need(kh, "k"));
+    MG_TRY(need(vh, "v"));
+    if (!pp) return fail(MG_INVALID_ARGUMENT, "null attention parameters");
+    Device* d = dev(h);
+    const Buffer* q = buf(qh);
+    const Buffer* kb = buf(kh);
+    const Buffer* v = buf(vh);
+    MG_TRY(same_device(d, q));
+    MG_TRY(same_device(d, kb));
+    MG_TRY(same_device(d, v));
+    MG_TRY(require_f32(q, "attention"));
+    MG_TRY(require_f32(kb, "attention"));
+    MG_TRY(require_f32(v, "attention"));
+    const mg_attention_params& p = *pp;
+    const uint64_t head_count = p.head_count, head_dim = p.head_dimension;
+    const uint64_t value_dim = p.value_dimension ? p.value_dimension : head_dim;
+    if (value_dim == head_dim && !same_shape(kb, v))
+        return fail(MG_SHAPE_UNSUPPORTED, "shape mismatch: %s vs %s", shape_str(kb).c_str(), shape_str(v).c_str());
+    float scale;
+    if (p.has_scale) {
+        if (!std::isfinite(p.scale) || !(p.scale > 0.0f))
+            return fail(MG_SHAPE_UNSUPPORTED, "attention scale %g must be finite and positive", (double)p.scale);
+        scale = p.scale;
+    } else {
+        scale = 1.0f / sqrtf((float)head_dim);
+    }
+    const uint64_t kv_heads = p.kv_head_count ? p.kv_head_count : head_count;
+    if (head_count == 0 || head_dim == 0 || kv_heads == 0 || value_dim == 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "head_count, kv_head_count, and head_dimension must all be positive");
+    if (head_count % kv_heads != 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "head_count %llu must be an exact multiple of kv_head_count %llu",
+                    (unsigned long long)head_count, (unsigned long long)kv_heads);
+    if (p.window_size == 0) return fail(MG_SHAPE_UNSUPPORTED, "window_size must be positive; a zero window admits no keys");
+    if (p.window_size > 0 && !p.causal)
+        return fail(MG_SHAPE_UNSUPPORTED, "window_size is only defined for causal attention");
+    uint64_t seq_len, q_model_dim, kv_rows, kv_model_dim, v_rows, v_model_dim;
+    MG_TRY(rows_cols(q, &seq_len, &q_model_dim));
+    MG_TRY(rows_cols(kb, &kv_rows, &kv_model_dim));
+    const uint64_t kv_seq_len = p.key_count >= 0 ? (uint64_t)p.key_count : kv_rows;
+    if (kv_seq_len > kv_rows)
+        return fail(MG_SHAPE_UNSUPPORTED, "key_count %llu exceeds the %llu rows of K/V", (unsigned long long)kv_seq_len,
+                    (unsigned long long)kv_rows);
+    if (seq_len > kv_seq_len)
+        return fail(MG_SHAPE_UNSUPPORTED, "q sequence length %llu cannot exceed k/v sequence length %llu",
+                    (unsigned long long)seq_len, (unsigned long long)kv_seq_len);
+    if (head_count * head_dim != q_model_dim)
+        return fail(MG_SHAPE_UNSUPPORTED, "head_count * head_dimension must equal q row width %llu, got %llu * %llu",
+                    (unsigned long long)q_model_dim, (unsigned long long)head_count, (unsigned long long)head_dim);
+    if (kv_heads * head_dim != kv_model_dim)
+        return fail(MG_SHAPE_UNSUPPORTED,
+                    "kv_head_count * head_dimension must equal k/v row width %llu, got %llu * %llu",
+                    (unsigned long long)kv_model_dim, (unsigned long long)kv_heads, (unsigned long long)head_dim);
+    MG_TRY(rows_cols(v, &v_rows, &v_model_dim));
+    if (v_rows != kv_rows || kv_heads * value_dim != v_model_dim)
+        return fail(MG_SHAPE_UNSUPPORTED,
+                    "v must hold %llu rows of kv_head_count * value_dimension = %llu * %llu, got %s",
+                    (unsigned long long)kv_rows, (unsigned long long)kv_heads, (unsigned long long)value_dim,
+                    shape_str(v).c_str());
+    const uint64_t shape[2] = {seq_len, head_count * value_dim};
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
+    k::AttentionArgs a;
+    a.q = (const float*)q->ptr;
+    a.k = (const float*)kb->ptr;
+    a.v = (const float*)v->ptr;
+    a.out = (float*)o->ptr;
+    a.seq_len = seq_len;
+    a.kv_seq_len = kv_seq_len;
+    a.head_count = head_count;
+    a.kv_head_count = kv_heads;
+    a.head_dim = head_dim;
+    a.value_dim = value_dim;
+    a.q_model_dim = q_model_dim;
+    a.kv_model_dim = kv_model_dim;
+    a.v_model_dim = v_model_dim;
+    a.causal = p.causal ? 1 : 0;
+    a.window = p.window_size > 0 ? p.window_size : -1;
+    a.query_position_offset = kv_seq_len - seq_len;
+    a.scale = scale;
+    return k::attention(d, a);
+}
+
+}  // extern "C"

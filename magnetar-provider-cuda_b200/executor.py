@@ -1,0 +1,231 @@
+"""``CudaExecutor``: the provider's ``ProviderExecutionApi`` surface for one device.
+
+Mirrors ``impl ProviderExecutionApi for CudaExecutor`` (``src/executor.rs:2244-2565``):
+tensors live in a device table keyed by resource id; ``submit_kernel`` runs an invocation
+by kernel name with the reference's attribute rules and keeps the output resident; only
+``read_tensor``/``read_tensor_rows`` bring data back to the host.  Everything runs in the
+native library (``src/executor.rs:1422-2027`` is restated in ``csrc/executor.cu``).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Dict, Iterable, List, Mapping, Optional, Sequence, Union
+
+import numpy as np
+
+from . import _native as N
+from ._native import CudaError, check
+from .kernels import CudaKernels, DeviceBuffer
+
+AttrValue = Union[bool, int, float, str]
+
+
+@dataclass
+class KernelInvocation:
+    """One ``KernelInvocation``: kernel name, input ids, output id, attributes."""
+
+    kernel: str
+    inputs: Sequence[str]
+    output: str
+    attributes: Mapping[str, AttrValue] = field(default_factory=dict)
+    input_dtypes: Optional[Sequence[str]] = None  # descriptor dtypes, e.g. ["f16", "f16"]
+    deadline_millis: Optional[int] = None
+
+
+@dataclass
+class KernelResult:
+    """``KernelResult``: success, or the failure's category and detail (kernel failures
+    are reported inside the result, not raised, as ``src/executor.rs:1223-1231``)."""
+
+    invocation_kernel: str
+    output: str
+    success: bool
+    error_code: Optional[str] = None
+    error_detail: Optional[str] = None
+
+
+def _attributes(attrs: Mapping[str, AttrValue]):
+    arr = (N.Attribute * max(1, len(attrs)))()
+    keep = []
+    for i, (name, value) in enumerate(attrs.items()):
+        a = arr[i]
+        bname = name.encode()
+        keep.append(bname)
+        a.name = bname
+        if isinstance(value, bool):
+            a.kind, a.int_value = N.ATTR_BOOL, int(value)
+        elif isinstance(value, int):
+            a.kind, a.int_value = N.ATTR_INT, value
+        elif isinstance(value, float):
+            a.kind, a.float_value = N.ATTR_FLOAT, value
+        elif isinstance(value, str):
+            s = value.encode()
+            keep.append(s)
+            a.kind, a.string_value = N.ATTR_STRING, s
+        else:
+            raise TypeError(f"attribute {name}: unsupported value {value!r}")
+    return arr, keep
+
+
+class CudaExecutor:
+    """Executor of one device (``CudaExecutor``)."""
+
+    def __init__(self, kernels: CudaKernels):
+        self.kernels = kernels
+        h = ctypes.c_void_p()
+        check(N.lib().mg_executor_create(kernels.handle, ctypes.byref(h)))
+        self._h = h
+        self._comm = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if self._h and self._h.value:
+            N.lib().mg_executor_destroy(self._h)
+            self._h = ctypes.c_void_p(0)
+
+    # ---- tensors ------------------------------------------------------------------------
+    def write_tensor(self, id: str, data, shape: Optional[Sequence[int]] = None) -> None:
+        a = np.ascontiguousarray(data, dtype=np.float32)
+        shape = tuple(a.shape) if shape is None else tuple(shape)
+        check(N.lib().mg_executor_write_tensor(self._h, id.encode(), len(shape), N.shape_array(shape),
+                                               a.ctypes.data))
+
+    def write_weight_tensor(self, id: str, data, shape: Optional[Sequence[int]] = None) -> None:
+        """A weight: under a tensor-parallel plan only this rank's share is kept."""
+        a = np.ascontiguousarray(data, dtype=np.float32)
+        shape = tuple(a.shape) if shape is None else tuple(shape)
+        check(N.lib().mg_executor_write_weight_tensor(self._h, id.encode(), len(shape),
+                                                      N.shape_array(shape), a.ctypes.data))
+
+    def write_zeroed_tensor(self, id: str, shape: Sequence[int]) -> None:
+        check(N.lib().mg_executor_write_zeroed_tensor(self._h, id.encode(), len(shape), N.shape_array(shape)))
+
+    def adopt(self, id: str, buf: DeviceBuffer) -> None:
+        """Binds an existing device buffer as resource ``id`` (ownership moves here)."""
+        check(N.lib().mg_executor_adopt_buffer(self._h, id.encode(), buf.handle))
+        buf._h = ctypes.c_void_p(0)
+
+    def buffer(self, id: str) -> DeviceBuffer:
+        """A borrowed view of resource ``id`` (valid until it is rewritten)."""
+        h = ctypes.c_void_p()
+        check(N.lib().mg_executor_buffer(self._h, id.encode(), ctypes.byref(h)))
+        return _BorrowedBuffer(h.value, self.kernels, self)
+
+    def resident_shape(self, id: str) -> Optional[tuple]:
+        present, rank = ctypes.c_int(), ctypes.c_int()
+        dims = (ctypes.c_uint64 * N.MG_MAX_RANK)()
+        check(N.lib().mg_executor_resident_shape(self._h, id.encode(), ctypes.byref(present),
+                                                 ctypes.byref(rank), dims))
+        return tuple(int(dims[i]) for i in range(rank.value)) if present.value else None
+
+    def read_tensor(self, id: str) -> Optional[np.ndarray]:
+        shape = self.resident_shape(id)
+        if shape is None:
+            return None
+        out = np.empty(shape, dtype=np.float32)
+        rank = ctypes.c_int()
+        dims = (ctypes.c_uint64 * N.MG_MAX_RANK)()
+        check(N.lib().mg_executor_read_tensor(self._h, id.encode(), out.ctypes.data, out.size,
+                                              ctypes.byref(rank), dims))
+        return out
+
+    def read_tensor_rows(self, id: str, first_row: int, rows: int) -> Optional[np.ndarray]:
+        shape = self.resident_shape(id)
+        if shape is None or len(shape) != 2 or first_row + rows > shape[0]:
+            return None
+        out = np.empty((rows, shape[1]), dtype=np.float32)
+        check(N.lib().mg_executor_read_tensor_rows(self._h, id.encode(), first_row, rows, out.ctypes.data,
+                                                   out.size))
+        return out
+
+    def release_tensor(self, id: str) -> bool:
+        r = ctypes.c_int()
+        check(N.lib().mg_executor_release_tensor(self._h, id.encode(), ctypes.byref(r)))
+        return bool(r.value)
+
+    def copy_tensor(self, src: str, dst: str) -> None:
+        check(N.lib().mg_executor_copy_tensor(self._h, src.encode(), dst.encode()))
+
+    # ---- kernels ------------------------------------------------------------------------
+    def _invocation(self, inv: KernelInvocation):
+        ids = [s.encode() for s in inv.inputs]
+        inputs = (ctypes.c_char_p * max(1, len(ids)))(*ids)
+        dtypes = None
+        if inv.input_dtypes is not None:
+            codes = [{"f32": N.F32, "f16": N.F16, "bf16": N.BF16}[d] for d in inv.input_dtypes]
+            dtypes = (ctypes.c_int * max(1, len(codes)))(*codes)
+        attrs, keep = _attributes(inv.attributes)
+        c = N.Invocation()
+        c.kernel = inv.kernel.encode()
+        c.input_count = len(ids)
+        c.inputs = ctypes.cast(inputs, ctypes.POINTER(ctypes.c_char_p))
+        c.input_dtypes = ctypes.cast(dtypes, ctypes.POINTER(ctypes.c_int)) if dtypes is not None else None
+        c.output = inv.output.encode()
+        c.attribute_count = len(inv.attributes)
+        c.attributes = ctypes.cast(attrs, ctypes.POINTER(N.Attribute))
+        c.deadline_millis = -1 if inv.deadline_millis is None else int(inv.deadline_millis)
+        return c, (ids, inputs, dtypes, attrs, keep)
+
+    def run(self, inv: KernelInvocation) -> None:
+        """Runs an invocation; raises ``CudaError`` on failure."""
+        c, _keep = self._invocation(inv)
+        check(N.lib().mg_executor_submit_kernel(self._h, ctypes.byref(c)))
+
+    def submit_kernel(self, inv: KernelInvocation) -> KernelResult:
+        """``submit_kernel`` + ``complete_kernel``: failures come back inside the result."""
+        try:
+            self.run(inv)
+            return KernelResult(inv.kernel, inv.output, True)
+        except CudaError as e:
+            return KernelResult(inv.kernel, inv.output, False, e.code, e.detail)
+
+    def synchronize(self) -> None:
+        check(N.lib().mg_executor_synchronize(self._h))
+
+    # ---- step capture ---------------------------------------------------------------------
+    def begin_step_capture(self) -> None:
+        check(N.lib().mg_executor_begin_step_capture(self._h))
+
+    def end_step_capture(self) -> None:
+        check(N.lib().mg_executor_end_step_capture(self._h))
+
+    def abort_step_capture(self) -> None:
+        check(N.lib().mg_executor_abort_step_capture(self._h))
+
+    def replay_step(self) -> None:
+        check(N.lib().mg_executor_replay_step(self._h))
+
+    def replay_steps(self, count: int) -> None:
+        """``count`` replays back to back with one embedding-id check for all of them."""
+        check(N.lib().mg_executor_replay_steps(self._h, int(count)))
+
+    def observations(self) -> Dict[str, int]:
+        s, c, f = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        check(N.lib().mg_executor_observations(self._h, ctypes.byref(s), ctypes.byref(c), ctypes.byref(f)))
+        return {"started": s.value, "completed": c.value, "failed": f.value}
+
+    # ---- tensor parallel -------------------------------------------------------------------
+    def attach_comm(self, comm) -> None:
+        self._comm = comm
+        check(N.lib().mg_executor_attach_comm(self._h, comm.handle if comm is not None else None))
+
+    def apply_tensor_parallel(self, plan: Mapping[str, str]) -> None:
+        """``apply_tensor_parallel``: weight id -> "columns" | "rows"."""
+        ids = [k.encode() for k in plan]
+        kinds = [{"columns": 0, "rows": 1}[v] for v in plan.values()]
+        arr = (ctypes.c_char_p * max(1, len(ids)))(*ids)
+        karr = (ctypes.c_int * max(1, len(kinds)))(*kinds)
+        check(N.lib().mg_executor_apply_tensor_parallel(self._h, len(ids), arr, karr))
+
+
+class _BorrowedBuffer(DeviceBuffer):
+    """A view of an executor-owned buffer; releasing it does nothing."""
+
+    __slots__ = ()
+
+    def release(self) -> None:
+        self._h = ctypes.c_void_p(0)

@@ -1,0 +1,184 @@
+"""GPU: the executor's ProviderExecutionApi behaviour (src/executor.rs) and the decoder-layer
+chain against the oracle."""
+import importlib
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+KI = None
+
+
+def inv(*args, **kw):
+    mpc = importlib.import_module("magnetar-provider-cuda_b200")
+    return mpc.KernelInvocation(*args, **kw)
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def test_write_read_and_release(executor):
+    x = np.arange(12, dtype=np.float32).reshape(4, 3)
+    executor.write_tensor("x", x)
+    np.testing.assert_array_equal(executor.read_tensor("x"), x)
+    np.testing.assert_array_equal(executor.read_tensor_rows("x", 3, 1), x[3:])
+    np.testing.assert_array_equal(executor.read_tensor_rows("x", 1, 2), x[1:3])
+    assert executor.read_tensor_rows("x", 3, 2) is None
+    assert executor.resident_shape("x") == (4, 3)
+    assert executor.release_tensor("x") and not executor.release_tensor("x")
+    assert executor.read_tensor("x") is None
+
+
+def test_zeroed_tensor_needs_no_upload(executor):
+    before = executor.kernels.upload_count()
+    executor.write_zeroed_tensor("z", (5, 3))
+    assert executor.kernels.upload_count() == before
+    np.testing.assert_array_equal(executor.read_tensor("z"), np.zeros((5, 3), np.float32))
+
+
+def test_back_to_back_kernels_do_not_round_trip_through_host(executor, oracle):
+    # src/tests_conformance.rs:970-1004
+    a = np.array([[1, 2], [3, 4]], np.float32)
+    b = np.array([[5, 6], [7, 8]], np.float32)
+    executor.write_tensor("a", a)
+    executor.write_tensor("b", b)
+    k = executor.kernels
+    up, down = k.upload_count(), k.download_count()
+    executor.run(inv("add", ["a", "b"], "sum"))
+    executor.run(inv("mul", ["sum", "b"], "prod"))
+    assert k.upload_count() == up and k.download_count() == down
+    np.testing.assert_array_equal(executor.read_tensor("prod"), (a + b) * b)
+    assert k.download_count() == down + 1
+
+
+def test_dispatch_errors_are_categorised(executor):
+    executor.write_tensor("a", np.ones((2, 2), np.float32))
+    r = executor.submit_kernel(inv("no-such-kernel", ["a"], "o"))
+    assert not r.success and r.error_code == "KernelNotFound"
+    r = executor.submit_kernel(inv("add", ["a", "missing"], "o"))
+    assert not r.success and r.error_code == "ExecutionFailed"
+    r = executor.submit_kernel(inv("add", ["a", "a"], "o", deadline_millis=0))
+    assert not r.success and r.error_code == "KernelTimeout"
+    r = executor.submit_kernel(inv("rope", ["a"], "o"))  # no dimension
+    assert not r.success and r.error_code == "KernelAttributeUnsupported"
+    r = executor.submit_kernel(inv("rope", ["a"], "o", {"dimension": 2, "rotation_pairing": "neox"}))
+    assert not r.success and r.error_code == "KernelAttributeUnsupported"
+    r = executor.submit_kernel(inv("matmul", ["a", "a"], "o", {"accumulation_dtype": "bf16"}))
+    assert not r.success and r.error_code == "DTypeUnsupported"
+    r = executor.submit_kernel(inv("rmsnorm", ["a"], "o", {"with_scale": True}))
+    assert not r.success and r.error_code == "KernelAttributeUnsupported"
+    obs = executor.observations()
+    assert obs["failed"] >= 7
+
+
+def test_failed_dispatch_keeps_previous_output(executor):
+    executor.write_tensor("t", np.ones((4, 2), np.float32))
+    executor.write_tensor("ids", np.array([0, 1], np.float32))
+    executor.run(inv("embedding", ["t", "ids"], "e"))
+    prev = executor.read_tensor("e")
+    executor.write_tensor("bad", np.array([0, 9], np.float32))
+    r = executor.submit_kernel(inv("embedding", ["t", "bad"], "e"))
+    assert not r.success and r.error_code == "ShapeUnsupported"
+    np.testing.assert_array_equal(executor.read_tensor("e"), prev)
+
+
+def test_output_buffer_is_reused(executor):
+    executor.write_tensor("a", np.ones((64, 64), np.float32))
+    executor.run(inv("add", ["a", "a"], "o"))
+    p1 = executor.buffer("o").data_ptr()
+    executor.run(inv("mul", ["a", "a"], "o"))
+    assert executor.buffer("o").data_ptr() == p1
+    np.testing.assert_array_equal(executor.read_tensor("o"), np.ones((64, 64), np.float32))
+
+
+def test_half_ops_through_the_executor(executor, oracle):
+    a = np.array([1.0, 2.5, 3.0, -4.25, 0.1, 100.0], np.float32)
+    b = np.array([6.0, 0.2, 4.0, 3.0, 0.2, -99.5], np.float32)
+    executor.write_tensor("a", a)
+    executor.write_tensor("b", b)
+    for dtype in ("f16", "bf16"):
+        for op in ("add", "mul"):
+            executor.run(inv(f"{op}-half", ["a", "b"], "o", input_dtypes=[dtype, dtype]))
+            exp = oracle.half_binary_f32(a, b, dtype, op)
+            np.testing.assert_array_equal(executor.read_tensor("o").view(np.uint32), exp.view(np.uint32))
+    r = executor.submit_kernel(inv("add-half", ["a", "b"], "o"))
+    assert not r.success and r.error_code == "DTypeUnsupported"
+
+
+def test_attribute_defaults_follow_the_reference(executor, oracle):
+    r = np.random.default_rng(0)
+    x = r.standard_normal((16, 32)).astype(np.float32)
+    w = r.standard_normal(32).astype(np.float32)
+    executor.write_tensor("x", x)
+    executor.write_tensor("w", w)
+    executor.run(inv("rmsnorm", ["x", "w"], "n"))  # epsilon defaults to 1e-6
+    assert rel(executor.read_tensor("n"), oracle.rmsnorm(x, w, 1e-6)) < 1e-5
+    executor.run(inv("rope", ["x"], "r", {"dimension": 8, "head_count": 4}))  # base 10000, interleaved
+    assert rel(executor.read_tensor("r"), oracle.rope(x, dimension=8, head_count=4)) < 1e-5
+    executor.run(inv("attention", ["x", "x", "x"], "at", {"head_count": 4, "head_dimension": 8}))  # not causal
+    assert rel(executor.read_tensor("at"), oracle.attention(x, x, x, 4, 8)) < 1e-4
+    executor.run(inv("activation", ["x"], "s", {"kind": "scale", "factor": 0.25}))
+    np.testing.assert_array_equal(executor.read_tensor("s"), x * np.float32(0.25))
+
+
+def _oracle_layer(orc, cfg, w):
+    x, bad = orc.embedding(w["table"], w["ids"])
+    assert not bad
+    h = orc.rmsnorm(x, w["attn_norm"], cfg.eps)
+    q, k, v = (orc.matmul(h, w[n]) for n in ("wq", "wk", "wv"))
+    q = orc.rope(q, base=cfg.rope_theta, dimension=cfg.head_dim, head_count=cfg.heads)
+    k = orc.rope(k, base=cfg.rope_theta, dimension=cfg.head_dim, head_count=cfg.heads)
+    a = orc.attention(q, k, v, cfg.heads, cfg.head_dim, causal=True)
+    x2 = orc.matmul(a, w["wo"], addend=x, addend_mode=2)
+    h2 = orc.rmsnorm(x2, w["mlp_norm"], cfg.eps)
+    g = orc.gated_matmul(h2, w["wg"], w["wu"])
+    return orc.matmul(g, w["wd"], addend=x2, addend_mode=2)
+
+
+def test_decoder_layer_matches_oracle_and_capture_replays(executor, oracle):
+    layer = importlib.import_module("magnetar-provider-cuda_b200.layer")
+    cfg = layer.DecoderLayerConfig()
+    w = layer.make_inputs(cfg, seed=0)
+    layer.load(executor, w)
+    layer.forward(executor, cfg)
+    got = executor.read_tensor("out")
+    exp = _oracle_layer(oracle, cfg, w)
+    assert rel(got, exp) <= 1e-4
+    # step capture: the replayed graph produces the same values
+    layer.capture(executor, cfg)
+    executor.write_zeroed_tensor("scratch", (1,))
+    executor.replay_steps(3)
+    np.testing.assert_array_equal(executor.read_tensor("out"), got)
+    # a new id vector written into the same buffer flows through the replay
+    ids2 = np.random.default_rng(1).integers(0, cfg.vocab, cfg.seq).astype(np.float32)
+    buf = executor.buffer("ids")
+    from importlib import import_module
+    executor.kernels  # same device
+    import ctypes
+    native = import_module("magnetar-provider-cuda_b200._native")
+    native.check(native.lib().mg_buffer_upload(buf.handle, ids2.ctypes.data, ids2.nbytes))
+    executor.replay_step()
+    w2 = dict(w, ids=ids2)
+    assert rel(executor.read_tensor("out"), _oracle_layer(oracle, cfg, w2)) <= 1e-4
+    # an invalid id is reported after the replay
+    bad = ids2.copy()
+    bad[5] = cfg.vocab + 3
+    native.check(native.lib().mg_buffer_upload(buf.handle, bad.ctypes.data, bad.nbytes))
+    from importlib import import_module as im
+    mpc = im("magnetar-provider-cuda_b200")
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_step()
+    assert e.value.code == "ShapeUnsupported"
+
+
+def test_softmax_cannot_be_captured(executor):
+    executor.write_tensor("x", np.ones((2, 4), np.float32))
+    executor.run(inv("softmax", ["x"], "s"))
+    executor.begin_step_capture()
+    r = executor.submit_kernel(inv("softmax", ["x"], "s"))
+    executor.abort_step_capture()
+    assert not r.success and r.error_code == "CaptureUnsupported"

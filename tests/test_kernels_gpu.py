@@ -1,0 +1,397 @@
+"""GPU parity: every hot-path kernel, called through the C ABI, against the CPU oracle on the
+same seeded inputs.  Bars: bit-exact for embedding gathers, add/mul/residual-add and the
+half-precision ops; relative L2 <= 1e-5 for elementwise/norm/rope/softmax; <= 1e-4 for
+matmul and attention."""
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL_ELEMENTWISE = 1e-5
+TOL_MATMUL = 1e-4
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def rng(seed=0):
+    return np.random.default_rng(seed)
+
+
+# ---------------------------------------------------------------------------------- elementwise
+@pytest.mark.parametrize("shape", [(8, 16), (3, 5), (1000, 37), (512, 4096)])
+def test_add_mul_residual_bit_exact(kernels, oracle, shape):
+    r = rng(1)
+    a = r.standard_normal(shape).astype(np.float32)
+    b = r.standard_normal(shape).astype(np.float32)
+    da, db = kernels.upload(a), kernels.upload(b)
+    np.testing.assert_array_equal(kernels.download(kernels.add(da, db)), oracle.add(a, b))
+    np.testing.assert_array_equal(kernels.download(kernels.mul(da, db)), oracle.mul(a, b))
+    np.testing.assert_array_equal(kernels.download(kernels.residual_add(da, db)), oracle.add(a, b))
+
+
+@pytest.mark.parametrize("cols,bshape", [(6, (6,)), (6, (1, 6)), (4096, (4096,)), (37, (37,))])
+def test_broadcast_add_and_scalar_mul(kernels, oracle, cols, bshape):
+    r = rng(2)
+    a = r.standard_normal((9, cols)).astype(np.float32)
+    b = r.standard_normal(bshape).astype(np.float32)
+    out = kernels.download(kernels.add(kernels.upload(a), kernels.upload(b)))
+    np.testing.assert_array_equal(out, oracle.add(a, b.reshape(-1)))
+    s = np.array([1.75], np.float32)
+    np.testing.assert_array_equal(kernels.download(kernels.mul(kernels.upload(a), kernels.upload(s))), a * s[0])
+
+
+def test_shape_mismatch_is_refused(kernels, mpc):
+    a = kernels.upload(np.zeros((2, 3), np.float32))
+    b = kernels.upload(np.zeros((3, 2), np.float32))
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.add(a, b)
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.mul(a, b)
+    assert e.value.code == "ShapeUnsupported"
+
+
+@pytest.mark.parametrize("n", [7, 4096, 1 << 20])
+def test_silu_and_silu_mul(kernels, oracle, n):
+    r = rng(3)
+    g = (r.standard_normal(n) * 4).astype(np.float32)
+    u = r.standard_normal(n).astype(np.float32)
+    assert rel(kernels.download(kernels.silu(kernels.upload(g))), oracle.silu(g)) <= TOL_ELEMENTWISE
+    assert rel(kernels.download(kernels.silu_mul(kernels.upload(g), kernels.upload(u))),
+               oracle.silu_mul(g, u)) <= TOL_ELEMENTWISE
+
+
+# ---------------------------------------------------------------------------------- half ops
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("op", ["add", "mul"])
+def test_half_ops_bit_exact_on_every_pattern_class(kernels, oracle, dtype, op):
+    r = rng(4)
+    n = 1 << 18
+    a = r.integers(0, 65536, n, dtype=np.uint32).astype(np.uint16)
+    b = r.integers(0, 65536, n, dtype=np.uint16 if False else np.uint32).astype(np.uint16)
+    a[:65536] = np.arange(65536, dtype=np.uint16)  # every pattern once
+    da, db = kernels.upload_raw(a, dtype), kernels.upload_raw(b, dtype)
+    fn = kernels.add_half if op == "add" else kernels.mul_half
+    got = kernels.download_raw(fn(da, db))
+    exp = oracle.half_binary(a, b, dtype, op)
+    bad = np.nonzero(got != exp)[0]
+    assert bad.size == 0, [(hex(a[i]), hex(b[i]), hex(got[i]), hex(exp[i])) for i in bad[:8]]
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_half_ops_on_reference_fixtures(kernels, oracle, dtype):
+    a = np.array([1.0, 2.5, 3.0, -4.25, 0.1, 100.0], np.float32).reshape(2, 3)
+    b = np.array([6.0, 0.2, 4.0, 3.0, 0.2, -99.5], np.float32).reshape(2, 3)
+    da, db = kernels.upload(a, dtype), kernels.upload(b, dtype)
+    for op, fn in (("add", kernels.add_half), ("mul", kernels.mul_half)):
+        got = kernels.download(fn(da, db))
+        exp = oracle.half_binary_f32(a, b, dtype, op)
+        np.testing.assert_array_equal(got.view(np.uint32), exp.view(np.uint32))
+        got32 = kernels.download(kernels.half_binary_f32(kernels.upload(a), kernels.upload(b), dtype, op))
+        np.testing.assert_array_equal(got32.view(np.uint32), exp.view(np.uint32))
+
+
+def test_half_ops_refuse_mismatches(kernels, mpc):
+    a = kernels.upload(np.ones(2, np.float32), "f16")
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.add_half(a, kernels.upload(np.ones(3, np.float32), "f16"))
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.add_half(a, kernels.upload(np.ones(2, np.float32), "bf16"))
+    assert e.value.code == "DTypeUnsupported"
+
+
+def test_half_upload_download_round_trip(kernels, oracle):
+    bits = np.arange(65536, dtype=np.uint16)
+    for dtype in ("f16", "bf16"):
+        vals = oracle.decode_half(bits, dtype)
+        got = kernels.download(kernels.upload_raw(bits, dtype))
+        np.testing.assert_array_equal(got.view(np.uint32), vals.view(np.uint32))
+        enc = kernels.download_raw(kernels.upload(vals, dtype))
+        np.testing.assert_array_equal(enc, oracle.encode_half(vals, dtype))
+
+
+# ---------------------------------------------------------------------------------- embedding
+@pytest.mark.parametrize("vocab,dim,n", [(32000, 512, 128), (50, 7, 33), (1000, 4096, 64)])
+def test_embedding_bit_exact(kernels, oracle, vocab, dim, n):
+    r = rng(5)
+    table = r.standard_normal((vocab, dim)).astype(np.float32)
+    ids = r.integers(0, vocab, n).astype(np.float32)
+    got = kernels.download(kernels.embedding_lookup(kernels.upload(table), kernels.upload(ids)))
+    exp, bad = oracle.embedding(table, ids)
+    assert not bad
+    np.testing.assert_array_equal(got, exp)
+    got = kernels.download(kernels.embedding_lookup(kernels.upload(table), kernels.upload(ids), scale=0.5))
+    np.testing.assert_array_equal(got, oracle.scale(exp, 0.5))
+
+
+@pytest.mark.parametrize("bad_id", [-1.0, 1.5, 50.0, float("nan"), float("inf")])
+def test_embedding_invalid_ids_fail(kernels, mpc, bad_id):
+    table = kernels.upload(np.ones((50, 8), np.float32))
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.embedding_lookup(table, kernels.upload(np.array([3.0, bad_id], np.float32)))
+    assert e.value.code == "ShapeUnsupported"
+    # the flag is reset: a valid lookup afterwards succeeds
+    kernels.embedding_lookup(table, kernels.upload(np.array([3.0], np.float32)))
+
+
+# ---------------------------------------------------------------------------------- rmsnorm
+@pytest.mark.parametrize("shape", [(128, 512), (64, 4096), (7, 300), (3, 8192), (2, 20000)])
+def test_rmsnorm(kernels, oracle, shape):
+    r = rng(6)
+    x = r.standard_normal(shape).astype(np.float32)
+    w = (1 + 0.1 * r.standard_normal(shape[-1])).astype(np.float32)
+    got = kernels.download(kernels.rmsnorm(kernels.upload(x), kernels.upload(w), 1e-5))
+    assert rel(got, oracle.rmsnorm(x, w, 1e-5)) <= TOL_ELEMENTWISE
+    got = kernels.download(kernels.rmsnorm(kernels.upload(x), None, 1e-5))
+    assert rel(got, oracle.rmsnorm(x, None, 1e-5)) <= TOL_ELEMENTWISE
+
+
+def test_rmsnorm_forms(kernels, oracle, mpc):
+    r = rng(7)
+    x = r.standard_normal((6, 256)).astype(np.float32)
+    w_row = r.standard_normal((6, 256)).astype(np.float32)
+    got = kernels.download(kernels.rmsnorm(kernels.upload(x), kernels.upload(w_row), 1e-6))
+    assert rel(got, oracle.rmsnorm(x, w_row, 1e-6)) <= TOL_ELEMENTWISE
+    w_head = r.standard_normal(64).astype(np.float32)
+    got = kernels.download(kernels.rmsnorm(kernels.upload(x), kernels.upload(w_head), 1e-6, heads=(4, 64)))
+    assert rel(got, oracle.rmsnorm(x, w_head, 1e-6, heads=(4, 64))) <= TOL_ELEMENTWISE
+    w1 = r.standard_normal((1, 256)).astype(np.float32)
+    got = kernels.download(kernels.rmsnorm(kernels.upload(x), kernels.upload(w1), 1e-6))
+    assert rel(got, oracle.rmsnorm(x, w1.reshape(-1), 1e-6)) <= TOL_ELEMENTWISE
+    with pytest.raises(mpc.CudaError):
+        kernels.rmsnorm(kernels.upload(x), kernels.upload(w_head), 0.0)
+    with pytest.raises(mpc.CudaError):
+        kernels.rmsnorm(kernels.upload(x), kernels.upload(w_head), 1e-6, heads=(3, 64))
+
+
+# ---------------------------------------------------------------------------------- rope
+ROPE_CASES = [
+    dict(shape=(128, 512), head_count=8, dimension=64, base=10000.0),
+    dict(shape=(256, 4096), head_count=32, dimension=128, base=500000.0),
+    dict(shape=(64, 512), head_count=8, dimension=64, base=10000.0, pairing="half_split", position_offset=1000),
+    dict(shape=(3, 12), head_count=2, dimension=4, base=10000.0),
+    dict(shape=(3, 12), head_count=2, dimension=4, base=10000.0, pairing="half_split"),
+    dict(shape=(40, 256), head_count=2, dimension=96, base=10000.0, rotated_pairs=20),
+    dict(shape=(40, 256), head_count=4, dimension=64, base=500000.0, banded=(8.0, 1.0, 4.0, 8192.0)),
+    dict(shape=(40, 256), head_count=4, dimension=64, base=10000.0, yarn=(4.0, 3.0, 20.0, 1.1)),
+    dict(shape=(5, 30), head_count=3, dimension=6, base=100.0, scale=0.5),
+]
+
+
+@pytest.mark.parametrize("case", ROPE_CASES)
+def test_rope(kernels, oracle, case):
+    c = dict(case)
+    shape = c.pop("shape")
+    pairing = c.pop("pairing", "interleaved")
+    x = rng(8).standard_normal(shape).astype(np.float32)
+    got = kernels.download(kernels.rope(kernels.upload(x), pairing=pairing, **c))
+    exp = oracle.rope(x, half_split=pairing == "half_split", **c)
+    assert rel(got, exp) <= TOL_ELEMENTWISE
+
+
+def test_rope_validation(kernels, mpc):
+    x = kernels.upload(np.zeros((4, 12), np.float32))
+    for kw in (dict(head_count=5, dimension=2), dict(head_count=2, dimension=3), dict(head_count=2, dimension=8),
+               dict(head_count=2, dimension=4, base=-1.0)):
+        with pytest.raises(mpc.CudaError) as e:
+            kernels.rope(x, **kw)
+        assert e.value.code == "ShapeUnsupported"
+
+
+# ---------------------------------------------------------------------------------- softmax
+@pytest.mark.parametrize("shape", [(1000, 2048), (64, 100), (33, 513), (16, 5000), (4096, 128)])
+def test_softmax(kernels, oracle, shape):
+    x = (rng(9).standard_normal(shape) * 2).astype(np.float32)
+    got = kernels.download(kernels.softmax_rows(kernels.upload(x)))
+    exp, flag = oracle.softmax(x)
+    assert not flag
+    assert rel(got, exp) <= TOL_ELEMENTWISE
+
+
+def test_softmax_non_finite_row_fails(kernels, mpc):
+    x = np.zeros((4, 64), np.float32)
+    x[2] = -np.inf
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.softmax_rows(kernels.upload(x))
+    assert e.value.code == "ExecutionFailed"
+    x[2] = 0
+    kernels.softmax_rows(kernels.upload(x))
+
+
+# ---------------------------------------------------------------------------------- matmul
+MATMUL_SHAPES = [
+    (1, 4096, 512), (1, 1000, 70), (3, 129, 64), (16, 4096, 4096), (4, 50, 40),
+    (17, 64, 96), (128, 512, 512), (128, 512, 1376), (128, 1376, 512), (200, 904, 136),
+    (256, 1024, 768), (300, 129, 65), (513, 257, 130),
+]
+
+
+@pytest.mark.parametrize("m,k,n", MATMUL_SHAPES)
+def test_matmul(kernels, oracle, m, k, n):
+    r = rng(10)
+    a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
+    b = (r.standard_normal((k, n))).astype(np.float32)
+    got = kernels.download(kernels.matmul(kernels.upload(a), kernels.upload(b)))
+    assert rel(got, oracle.matmul(a, b)) <= TOL_MATMUL
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 300, 70), (16, 256, 128), (130, 200, 96)])
+@pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
+def test_matmul_transposed(kernels, oracle, m, k, n, ta, tb):
+    r = rng(11)
+    a = r.standard_normal((k, m) if ta else (m, k)).astype(np.float32)
+    b = r.standard_normal((n, k) if tb else (k, n)).astype(np.float32)
+    got = kernels.download(kernels.matmul(kernels.upload(a), kernels.upload(b), ta, tb))
+    assert rel(got, oracle.matmul(a, b, ta, tb)) <= TOL_MATMUL
+
+
+@pytest.mark.parametrize("m", [1, 16, 128, 300])
+def test_matmul_bias_and_residual(kernels, oracle, m):
+    r = rng(12)
+    k, n = 256, 192
+    a = r.standard_normal((m, k)).astype(np.float32)
+    b = r.standard_normal((k, n)).astype(np.float32)
+    bias = r.standard_normal(n).astype(np.float32)
+    res = r.standard_normal((m, n)).astype(np.float32)
+    da, db = kernels.upload(a), kernels.upload(b)
+    got = kernels.download(kernels.matmul_bias(da, db, kernels.upload(bias)))
+    assert rel(got, oracle.matmul(a, b, addend=bias, addend_mode=1)) <= TOL_MATMUL
+    got = kernels.download(kernels.matmul_residual(da, db, kernels.upload(res)))
+    assert rel(got, oracle.matmul(a, b, addend=res, addend_mode=2)) <= TOL_MATMUL
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 512, 1376), (16, 512, 256), (128, 512, 1376), (200, 300, 136)])
+def test_gated_matmul(kernels, oracle, m, k, n):
+    r = rng(13)
+    a = r.standard_normal((m, k)).astype(np.float32)
+    g = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    u = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    got = kernels.download(kernels.gated_matmul(kernels.upload(a), kernels.upload(g), kernels.upload(u)))
+    assert rel(got, oracle.gated_matmul(a, g, u)) <= TOL_MATMUL
+
+
+@pytest.mark.parametrize("m,k,n", [(70, 900, 130), (200, 904, 136)])
+def test_matmul_keeps_f32_activation_precision(kernels, m, k, n):
+    # src/tests_conformance.rs:807-846
+    a = np.full((m, k), 1.0 + 2.0 ** -12, np.float32)
+    w = np.abs(rng(21).standard_normal((k, n)).astype(np.float32))
+    w = (w.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    got = kernels.download(kernels.matmul(kernels.upload(a), kernels.upload(w))).astype(np.float64)
+    exp = (1.0 + 2.0 ** -12) * w.astype(np.float64).sum(axis=0)
+    assert np.all(np.abs(got - exp) <= 5e-5 * exp)
+
+
+def test_matmul_near_f32_max_stays_finite(kernels):
+    # src/tests_conformance.rs:852-880
+    m, k, n = 64, 256, 256
+    a = np.full((m, k), np.finfo(np.float32).max, np.float32)
+    b = np.full((k, n), 2.0 ** -120, np.float32)
+    got = kernels.download(kernels.matmul(kernels.upload(a), kernels.upload(b)))
+    exp = float(np.finfo(np.float32).max) * 2.0 ** -120 * k
+    assert np.all(np.isfinite(got)) and np.all(np.abs(got / exp - 1) < 1e-4)
+
+
+def test_matmul_shape_errors(kernels, mpc):
+    a = kernels.upload(np.zeros((4, 5), np.float32))
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.matmul(a, kernels.upload(np.zeros((4, 5), np.float32)))
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.matmul(kernels.upload(np.zeros(5, np.float32)), a)
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.matmul_bias(a, kernels.upload(np.zeros((5, 3), np.float32)), kernels.upload(np.zeros(4, np.float32)))
+    assert e.value.code == "ShapeUnsupported"
+
+
+# ---------------------------------------------------------------------------------- attention
+ATTN_CASES = [
+    dict(seq=128, kv=128, heads=8, kvh=8, d=64, causal=True),
+    dict(seq=200, kv=200, heads=4, kvh=4, d=128, causal=True),
+    dict(seq=70, kv=70, heads=4, kvh=2, d=64, causal=True),
+    dict(seq=33, kv=33, heads=2, kvh=2, d=64, causal=False),
+    dict(seq=64, kv=64, heads=4, kvh=1, d=64, causal=True, window=16),
+    dict(seq=20, kv=100, heads=2, kvh=2, d=128, causal=True),
+    dict(seq=20, kv=100, heads=2, kvh=2, d=64, causal=True, key_count=60),
+    dict(seq=40, kv=40, heads=2, kvh=2, d=64, causal=True, scale=0.3),
+    dict(seq=37, kv=37, heads=3, kvh=3, d=48, causal=True),
+    dict(seq=30, kv=30, heads=2, kvh=2, d=64, causal=True, vd=32),
+    dict(seq=1, kv=300, heads=4, kvh=2, d=64, causal=True),
+    dict(seq=3, kv=3, heads=1, kvh=1, d=2, causal=True),
+]
+
+
+@pytest.mark.parametrize("c", ATTN_CASES)
+def test_attention(kernels, oracle, c):
+    r = rng(14)
+    vd = c.get("vd", c["d"])
+    q = r.standard_normal((c["seq"], c["heads"] * c["d"])).astype(np.float32)
+    k = r.standard_normal((c["kv"], c["kvh"] * c["d"])).astype(np.float32)
+    v = r.standard_normal((c["kv"], c["kvh"] * vd)).astype(np.float32)
+    kw = dict(kv_head_count=c["kvh"], window_size=c.get("window"), causal=c["causal"],
+              key_count=c.get("key_count"), scale=c.get("scale"), value_dimension=c.get("vd"))
+    got = kernels.download(kernels.attention(kernels.upload(q), kernels.upload(k), kernels.upload(v),
+                                             c["heads"], c["d"], **kw))
+    exp = oracle.attention(q, k, v, c["heads"], c["d"], **kw)
+    assert rel(got, exp) <= TOL_MATMUL
+
+
+def test_attention_large_values_stay_finite(kernels):
+    # src/tests_conformance.rs:884-914
+    rows = 70
+    q = np.zeros((rows, 64), np.float32)
+    v = np.full((rows, 64), 1e38, np.float32)
+    got = kernels.download(kernels.attention(kernels.upload(q), kernels.upload(q), kernels.upload(v), 1, 64,
+                                             causal=True))
+    assert np.all(np.isfinite(got)) and np.all(np.abs(got / 1e38 - 1) < 1e-4)
+
+
+def test_attention_validation(kernels, mpc):
+    q = kernels.upload(np.zeros((4, 8), np.float32))
+    for kw in (dict(head_count=3, head_dimension=4), dict(head_count=2, head_dimension=4, kv_head_count=3),
+               dict(head_count=2, head_dimension=4, window_size=0, causal=True),
+               dict(head_count=2, head_dimension=4, window_size=2, causal=False),
+               dict(head_count=2, head_dimension=4, key_count=9),
+               dict(head_count=2, head_dimension=4, scale=-1.0)):
+        with pytest.raises(mpc.CudaError) as e:
+            kernels.attention(q, q, q, **kw)
+        assert e.value.code == "ShapeUnsupported", kw
+
+
+# ---------------------------------------------------------------------------------- full-size properties
+def test_full_size_memory_bound_suite_properties(kernels, oracle):
+    """Config 4 sizes: [8192, 4096] through add (bit-exact vs numpy), rmsnorm rows have unit
+    RMS before the gain, softmax rows sum to one."""
+    r = rng(15)
+    x = r.standard_normal((8192, 4096)).astype(np.float32)
+    y = r.standard_normal((8192, 4096)).astype(np.float32)
+    dx, dy = kernels.upload(x), kernels.upload(y)
+    np.testing.assert_array_equal(kernels.download(kernels.add(dx, dy)), x + y)
+    n = kernels.download(kernels.rmsnorm(dx, None, 1e-5))
+    rms = np.sqrt((n.astype(np.float64) ** 2).mean(axis=1))
+    assert np.all(np.abs(rms - 1) < 1e-4)
+    s = kernels.download(kernels.softmax_rows(kernels.upload(x[:2048, :2048] * 2)))
+    assert np.all(np.abs(s.astype(np.float64).sum(axis=1) - 1) < 1e-5)
+
+
+def test_gemm_sweep_full_size_linearity(kernels):
+    """Config 2 size (M=2048, N=K=4096): A(B1 + B2) == A B1 + A B2 within the matmul bar."""
+    r = rng(16)
+    k = 4096
+    a = (r.standard_normal((2048, k)) / math.sqrt(k)).astype(np.float32)
+    b1 = (r.standard_normal((k, k)) / math.sqrt(k)).astype(np.float32)
+    b2 = (r.standard_normal((k, k)) / math.sqrt(k)).astype(np.float32)
+    da = kernels.upload(a)
+    lhs = kernels.download(kernels.matmul(da, kernels.upload(b1 + b2)))
+    rhs = kernels.download(kernels.add(kernels.matmul(da, kernels.upload(b1)), kernels.matmul(da, kernels.upload(b2))))
+    assert rel(lhs, rhs) <= TOL_MATMUL
+    # and a row sample against float64
+    exp = a[:8].astype(np.float64) @ (b1 + b2).astype(np.float64)
+    assert rel(lhs[:8], exp) <= TOL_MATMUL
