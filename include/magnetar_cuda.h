@@ -207,6 +207,20 @@ mg_status mg_matmul_bias(mg_device* d, const mg_buffer* a, const mg_buffer* b, c
 mg_status mg_matmul_residual(mg_device* d, const mg_buffer* a, const mg_buffer* b,
                              const mg_buffer* residual, int transpose_a, int transpose_b,
                              mg_buffer** out);
+/* matmul C[m, n] = A[m, k] B[k, n] for 1 <= m <= 16 that allocates nothing.
+ * No counterpart in the reference: it is an extra entry point for callers that cannot
+ * allocate device memory when they multiply -- a runtime whose device memory is already
+ * fully handed out under a fixed budget, or a latency-critical thread that must not enter
+ * the driver's allocator.  The caller owns a, b and out (row-major f32, b 16-byte aligned,
+ * n a multiple of 4); the split-k partial sums live in a workspace compiled into the library,
+ * MG_GEMV_FIXED_WORKSPACE_BYTES per GPU that loads it, held until the process exits.  A
+ * shape whose partials need more than that fails with MG_SHAPE_UNSUPPORTED.  The first call
+ * on a device looks up the workspace's address (make that first call before any stream
+ * capture); calls on one device share the workspace, so calls that overlap on the GPU race.
+ * `stream` is a cudaStream_t of device `device_ordinal` (NULL: the default stream). */
+#define MG_GEMV_FIXED_WORKSPACE_BYTES (8u << 20)
+mg_status mg_matmul_gemv_fixed(int device_ordinal, void* stream, const float* a, const float* b, float* out,
+                               uint64_t m, uint64_t k, uint64_t n);
 /* silu(A gate) * (A up) (gated-matmul, src/kernels.rs:4529-4917) */
 mg_status mg_gated_matmul(mg_device* d, const mg_buffer* a, const mg_buffer* gate,
                           const mg_buffer* up, int transpose_a, int transpose_b, mg_buffer** out);

@@ -136,6 +136,7 @@ SIGNATURES = {
     "mg_matmul_bias": [_P, _P, _P, _P, _I, _I, _PP],
     "mg_matmul_residual": [_P, _P, _P, _P, _I, _I, _PP],
     "mg_gated_matmul": [_P, _P, _P, _P, _I, _I, _PP],
+    "mg_matmul_gemv_fixed": [_I, _P, _P, _P, _P, _U64, _U64, _U64],
     "mg_attention": [_P, _P, _P, _P, ctypes.POINTER(AttentionParams), _PP],
     "mg_executor_create": [_P, _PP],
     "mg_executor_destroy": [_P],

@@ -201,3 +201,124 @@ mg_status gemv(Device* d, const GemmArgs& g) {
 
 }  // namespace k
 }  // namespace mg
+
+// =========================================================================================
+// Fixed-workspace variant: the same two kernels, with the split-k partials kept in a
+// workspace that lives inside the loaded library instead of coming from an allocator.
+//
+// Some callers cannot allocate device memory at the moment they multiply: a runtime whose
+// device memory is already fully handed out under a fixed admission budget, or a
+// latency-critical thread that must never enter the driver's allocator (which can block
+// on a lock or on device-wide synchronisation).  For them, mg_matmul_gemv_fixed takes only
+// caller-owned inputs and outputs and a stream, and keeps its partial sums in
+// g_gemv_fixed_workspace below.
+//
+// That array is a file-scope __device__ variable: every GPU that loads this library holds
+// one copy (MG_GEMV_FIXED_WORKSPACE_BYTES) until the process exits.  Host code cannot use
+// its name as a device address, so the first call on each device looks the address up
+// with cudaGetSymbolAddress while that device is current, and later calls reuse it.  All
+// calls on a device share the one array and it keeps whatever the last call left there:
+// every call overwrites each partial it reads, so nothing needs clearing, but calls that
+// overlap on the GPU (different streams, no ordering between them) race on it.
+// =========================================================================================
+#include <mutex>
+
+namespace {
+
+constexpr uint64_t kFixedWorkspaceFloats = MG_GEMV_FIXED_WORKSPACE_BYTES / sizeof(float);
+static __device__ __align__(256) float g_gemv_fixed_workspace[kFixedWorkspaceFloats];
+
+struct FixedDevice {
+    bool ready = false;
+    float* workspace = nullptr;
+    int sm_count = 0;
+};
+constexpr int kMaxFixedDevices = 64;
+FixedDevice g_fixed_devices[kMaxFixedDevices];
+std::mutex g_fixed_mutex;
+
+// Looks up the workspace's device address and the SM count of `ordinal`, once.
+mg_status fixed_setup(int ordinal, FixedDevice** out) {
+    if (ordinal < 0 || ordinal >= kMaxFixedDevices)
+        return mg::fail(MG_DEVICE_UNAVAILABLE, "device ordinal %d is outside 0..%d", ordinal, kMaxFixedDevices - 1);
+    std::lock_guard<std::mutex> lock(g_fixed_mutex);
+    FixedDevice& fd = g_fixed_devices[ordinal];
+    if (!fd.ready) {
+        int previous = 0;
+        MG_CUDA(cudaGetDevice(&previous), "reading the current device");
+        MG_CUDA(cudaSetDevice(ordinal), "selecting the device");
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_gemv_fixed_workspace);
+        int sms = 0;
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ordinal);
+        cudaSetDevice(previous);
+        if (e != cudaSuccess) return mg::from_cuda(e, "locating the fixed gemv workspace");
+        fd.workspace = static_cast<float*>(ptr);
+        fd.sm_count = sms;
+        fd.ready = true;
+    }
+    *out = &fd;
+    return MG_OK;
+}
+
+}  // namespace
+
+extern "C" mg_status mg_matmul_gemv_fixed(int device_ordinal, void* stream, const float* a, const float* b,
+                                          float* out, uint64_t m, uint64_t k, uint64_t n) {
+    using namespace mg;
+    if (!a || !b || !out) return fail(MG_INVALID_ARGUMENT, "null operand");
+    if (m < 1 || m > kMaxRows) return fail(MG_SHAPE_UNSUPPORTED, "fixed-workspace gemv takes 1..16 rows, got %llu",
+                                           (unsigned long long)m);
+    if (k == 0 || n == 0 || n % 4 != 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "fixed-workspace gemv needs k > 0 and n a positive multiple of 4, got k %llu n %llu",
+                    (unsigned long long)k, (unsigned long long)n);
+    if ((reinterpret_cast<uintptr_t>(b) & 15) != 0)
+        return fail(MG_LAYOUT_UNSUPPORTED, "fixed-workspace gemv needs b aligned to 16 bytes");
+    FixedDevice* fd = nullptr;
+    MG_TRY(fixed_setup(device_ordinal, &fd));
+    // The split of k the allocating path would choose for this device.
+    const uint64_t col_tiles = (n + kCols - 1) / kCols;
+    const uint64_t ctas_wanted = (uint64_t)fd->sm_count * 4;
+    uint64_t slices = (ctas_wanted + col_tiles - 1) / col_tiles;
+    const uint64_t step = kWarps * kRowsInFlight;
+    uint64_t slice_len = (k + slices - 1) / slices;
+    slice_len = ((slice_len + step - 1) / step) * step;
+    if (slice_len > 512) slice_len = 512;
+    if (slice_len < step) slice_len = step;
+    slices = (k + slice_len - 1) / slice_len;
+    if (slices == 0) slices = 1;
+    if (slices > 65535 || col_tiles > 0x7FFFFFFFull)
+        return fail(MG_SHAPE_UNSUPPORTED, "fixed-workspace gemv shape exceeds the launch grid");
+    const uint64_t need = slices * m * n;
+    if (need > kFixedWorkspaceFloats)
+        return fail(MG_SHAPE_UNSUPPORTED,
+                    "fixed-workspace gemv needs %llu bytes of partial sums for m %llu k %llu n %llu; the fixed "
+                    "workspace holds %llu bytes",
+                    (unsigned long long)(need * sizeof(float)), (unsigned long long)m, (unsigned long long)k,
+                    (unsigned long long)n, (unsigned long long)MG_GEMV_FIXED_WORKSPACE_BYTES);
+    int previous = 0;
+    MG_CUDA(cudaGetDevice(&previous), "reading the current device");
+    MG_CUDA(cudaSetDevice(device_ordinal), "selecting the device");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int mp = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : m <= 8 ? 8 : 16;
+    const size_t smem = ((size_t)mp * slice_len + kWarps * kCols) * sizeof(float);
+    dim3 grid((unsigned)col_tiles, (unsigned)slices, 1);
+    float* partial = fd->workspace;
+    switch (mp) {
+        case 1: gemv_partial_kernel<1><<<grid, kWarps * 32, smem, s>>>(a, b, nullptr, partial, m, n, k, slice_len, 0); break;
+        case 2: gemv_partial_kernel<2><<<grid, kWarps * 32, smem, s>>>(a, b, nullptr, partial, m, n, k, slice_len, 0); break;
+        case 4: gemv_partial_kernel<4><<<grid, kWarps * 32, smem, s>>>(a, b, nullptr, partial, m, n, k, slice_len, 0); break;
+        case 8: gemv_partial_kernel<8><<<grid, kWarps * 32, smem, s>>>(a, b, nullptr, partial, m, n, k, slice_len, 0); break;
+        default: gemv_partial_kernel<16><<<grid, kWarps * 32, smem, s>>>(a, b, nullptr, partial, m, n, k, slice_len, 0); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        uint64_t blocks = (m * n + 255) / 256;
+        if (blocks > (uint64_t)fd->sm_count * 8) blocks = (uint64_t)fd->sm_count * 8;
+        gemv_reduce_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, s>>>(partial, out, m, n, slices, nullptr, 0, 0);
+        e = cudaGetLastError();
+    }
+    cudaSetDevice(previous);
+    if (e != cudaSuccess) return from_cuda(e, "fixed-workspace gemv launch");
+    return MG_OK;
+}
