@@ -173,6 +173,13 @@ def run_reference(args, world, rank):
 
 
 # ------------------------------------------------------------------------------------ our arm
+def gpu_busy(torch, us: float = 200.0):
+    """Keeps the stream busy for about `us` microseconds (a spin kernel), so that the host
+    has enqueued the timed work before the start event executes: the events then bracket
+    device time only, not the host's launch latency."""
+    torch.cuda._sleep(int(us * 2000))  # ~2 GHz cycles
+
+
 def time_events(torch, fn, iters, flush=None, warmup=2):
     """Per-iteration device time (ms) on the current stream, L2 flushed before each."""
     for _ in range(warmup):
@@ -183,6 +190,7 @@ def time_events(torch, fn, iters, flush=None, warmup=2):
             flush()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
+        gpu_busy(torch)
         s.record()
         fn()
         e.record()
@@ -204,16 +212,20 @@ def measure_tf32_peak(torch):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops):
-    """Configs 2-4: each kernel timed alone (CUDA events, L2 flushed), as % of its roofline."""
+def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
+    """Configs 2-4: each kernel timed alone (CUDA events, L2 flushed), as % of its roofline.
+    ``filt`` keeps only the cases whose name contains it."""
     results = []
     flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
 
     def flush():
         flush_buf.zero_()
 
+    def want(name):
+        return filt is None or filt in name
+
     hbm = peaks["hbm_gbs"]
-    eff = tf32_tflops / 3.0
+    eff = tf32_tflops / 3.0 if tf32_tflops > 0 else float("nan")
 
     def add(name, config, ms, bound, work):
         if bound == "hbm":
@@ -228,71 +240,84 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops):
                             "peak_basis": "3xTF32-effective = measured cuBLAS TF32 / 3",
                             "frac": round(achieved / eff, 4)})
 
+    def timed(fn, n=iters, warmup=2):
+        return statistics.median(time_events(torch, fn, n, flush, warmup=warmup))
+
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
     W = kernels.wrap_tensor
 
     # config 2: f32 matmul sweep, N = K = 4096
     K = N = 4096
-    b = torch.randn(K, N, device="cuda", generator=g) / math.sqrt(K)
-    for M in (1, 16, 128, 2048, 8192):
-        a = torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)
-        c = torch.empty(M, N, device="cuda")
-        da, db, dc = W(a), W(b), W(c)
-        ms = statistics.median(time_events(torch, lambda: kernels.matmul(da, db, out=dc), 5, flush))
-        flops = 2.0 * M * N * K
-        if M <= 16:
-            add(f"matmul M={M}", "configs[1]", ms, "hbm", 4.0 * (M * K + K * N + M * N))
-        else:
-            add(f"matmul M={M}", "configs[1]", ms, "tensor", flops)
-        del a, c
+    if any(want(f"matmul M={M}") for M in (1, 16, 128, 2048, 8192)):
+        b = torch.randn(K, N, device="cuda", generator=g) / math.sqrt(K)
+        for M in (1, 16, 128, 2048, 8192):
+            if not want(f"matmul M={M}"):
+                continue
+            a = torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)
+            c = torch.empty(M, N, device="cuda")
+            da, db, dc = W(a), W(b), W(c)
+            ms = timed(lambda: kernels.matmul(da, db, out=dc))
+            if M <= 16:
+                add(f"matmul M={M}", "configs[1]", ms, "hbm", 4.0 * (M * K + K * N + M * N))
+            else:
+                add(f"matmul M={M}", "configs[1]", ms, "tensor", 2.0 * M * N * K)
+            del a, c
+        del b
     # config 3: causal attention b4 h32 d128 s2048 (batch folded into 128 heads)
     S, H, D = 2048, 4 * 32, 128
-    q = torch.randn(S, H * D, device="cuda", generator=g)
-    k_ = torch.randn(S, H * D, device="cuda", generator=g)
-    v = torch.randn(S, H * D, device="cuda", generator=g)
-    o = torch.empty(S, H * D, device="cuda")
-    dq, dk, dv, do = W(q), W(k_), W(v), W(o)
-    ms = statistics.median(time_events(
-        torch, lambda: kernels.attention(dq, dk, dv, H, D, causal=True, out=do), 3, flush, warmup=1))
-    add("attention causal b4 h32 d128 s2048", "configs[2]", ms, "tensor", 4.0 * H * S * S * D / 2)
-    del q, k_, v, o
+    name = "attention causal b4 h32 d128 s2048"
+    if want(name):
+        q = torch.randn(S, H * D, device="cuda", generator=g)
+        k_ = torch.randn(S, H * D, device="cuda", generator=g)
+        v = torch.randn(S, H * D, device="cuda", generator=g)
+        o = torch.empty(S, H * D, device="cuda")
+        dq, dk, dv, do = W(q), W(k_), W(v), W(o)
+        ms = timed(lambda: kernels.attention(dq, dk, dv, H, D, causal=True, out=do), max(3, iters // 2), 1)
+        add(name, "configs[2]", ms, "tensor", 4.0 * H * S * S * D / 2)
+        del q, k_, v, o
     # config 3': softmax rows [262144, 2048]
-    x = torch.randn(262144, 2048, device="cuda", generator=g) * 2
-    y = torch.empty_like(x)
-    dx, dy = W(x), W(y)
-    ms = statistics.median(time_events(torch, lambda: kernels.softmax_rows(dx, out=dy), 3, flush, warmup=1))
-    add("softmax [262144,2048]", "configs[2]", ms, "hbm", 2.0 * x.numel() * 4)
-    del x, y
+    name = "softmax [262144,2048]"
+    if want(name):
+        x = torch.randn(262144, 2048, device="cuda", generator=g) * 2
+        y = torch.empty_like(x)
+        dx, dy = W(x), W(y)
+        ms = timed(lambda: kernels.softmax_rows(dx, out=dy), max(3, iters // 2), 1)
+        add(name, "configs[2]", ms, "hbm", 2.0 * x.numel() * 4)
+        del x, y
     # config 4: memory-bound suite on [8192, 4096]
     R, C = 8192, 4096
-    x = torch.randn(R, C, device="cuda", generator=g)
-    y = torch.randn(R, C, device="cuda", generator=g)
-    o = torch.empty(R, C, device="cuda")
-    gain = 1 + 0.1 * torch.randn(C, device="cuda", generator=g)
-    dx, dy, do, dg = W(x), W(y), W(o), W(gain)
-    nb = R * C * 4
-    suite = [
-        ("rmsnorm", lambda: kernels.rmsnorm(dx, dg, 1e-5, out=do), 2 * nb + C * 4),
-        ("rope h32x128 theta5e5", lambda: kernels.rope(dx, base=500000.0, dimension=128, head_count=32, out=do),
-         2 * nb),
-        ("silu", lambda: kernels.silu(dx, out=do), 2 * nb),
-        ("add", lambda: kernels.add(dx, dy, out=do), 3 * nb),
-        ("mul", lambda: kernels.mul(dx, dy, out=do), 3 * nb),
-        ("residual-add", lambda: kernels.residual_add(dx, dy, out=do), 3 * nb),
-    ]
-    for name, fn, work in suite:
-        ms = statistics.median(time_events(torch, fn, 5, flush))
-        add(f"{name} [8192,4096]", "configs[3]", ms, "hbm", work)
+    names = ["rmsnorm", "rope h32x128 theta5e5", "silu", "add", "mul", "residual-add"]
+    if any(want(f"{n} [8192,4096]") for n in names):
+        x = torch.randn(R, C, device="cuda", generator=g)
+        y = torch.randn(R, C, device="cuda", generator=g)
+        o = torch.empty(R, C, device="cuda")
+        gain = 1 + 0.1 * torch.randn(C, device="cuda", generator=g)
+        dx, dy, do, dg = W(x), W(y), W(o), W(gain)
+        nb = R * C * 4
+        suite = [
+            ("rmsnorm", lambda: kernels.rmsnorm(dx, dg, 1e-5, out=do), 2 * nb + C * 4),
+            ("rope h32x128 theta5e5",
+             lambda: kernels.rope(dx, base=500000.0, dimension=128, head_count=32, out=do), 2 * nb),
+            ("silu", lambda: kernels.silu(dx, out=do), 2 * nb),
+            ("add", lambda: kernels.add(dx, dy, out=do), 3 * nb),
+            ("mul", lambda: kernels.mul(dx, dy, out=do), 3 * nb),
+            ("residual-add", lambda: kernels.residual_add(dx, dy, out=do), 3 * nb),
+        ]
+        for nm, fn, work in suite:
+            if want(f"{nm} [8192,4096]"):
+                add(f"{nm} [8192,4096]", "configs[3]", timed(fn), "hbm", work)
+        del x, y, o
     for dt, tdt in (("f16", torch.float16), ("bf16", torch.bfloat16)):
+        if not any(want(f"{op} {dt} [8192,4096]") for op in ("add-half", "mul-half")):
+            continue
         ha = (torch.rand(R, C, device="cuda", generator=g) * 16 - 8).to(tdt)
         hb = (torch.rand(R, C, device="cuda", generator=g) * 16 - 8).to(tdt)
         ho = torch.empty_like(ha)
         dha, dhb, dho = W(ha), W(hb), W(ho)
         for op, fn in (("add-half", kernels.add_half), ("mul-half", kernels.mul_half)):
-            ms = statistics.median(time_events(torch, lambda: fn(dha, dhb, out=dho), 5, flush))
-            add(f"{op} {dt} [8192,4096]", "configs[3]", ms, "hbm", 3 * R * C * 2)
-    del x, y, o
+            if want(f"{op} {dt} [8192,4096]"):
+                add(f"{op} {dt} [8192,4096]", "configs[3]", timed(lambda: fn(dha, dhb, out=dho)), "hbm", 3 * R * C * 2)
     torch.cuda.synchronize()
     return results
 
@@ -362,6 +387,13 @@ def run_ours(args, world, rank, local):
     kernels.set_stream(stream.cuda_stream)
     peaks = load_peaks()
 
+    if args.only_suite is not None:
+        res = kernel_suite(torch, mpc, kernels, peaks, 0.0, filt=args.only_suite, iters=args.steps)
+        if rank == 0:
+            print(json.dumps({"only_suite": args.only_suite, "kernels": res}), flush=True)
+        provider.close()
+        return
+
     cfg = layer.DecoderLayerConfig()
     w = layer.make_inputs(cfg, seed=rank)
     layer.load(ex, w)
@@ -386,11 +418,13 @@ def run_ours(args, world, rank, local):
             flush()
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
+            gpu_busy(torch)
             s.record()
-            ex.replay_steps(1)
+            ex.launch_step()
             e.record()
             e.synchronize()
             step_ms.append(s.elapsed_time(e))
+        ex.check_steps()  # the embedding-id check of all timed steps
         torch.cuda.synchronize()
     launches = kernels.launch_count() - launches0
     total_ms = sum(step_ms)
@@ -513,6 +547,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-suite", action="store_true", help="skip the per-kernel roofline suite")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP")
+    ap.add_argument("--only-suite", default=None, metavar="FILTER",
+                    help="profiling aid: run only the suite cases whose name contains FILTER, --steps times each")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -131,6 +131,11 @@ mg_status mg_buffer_shape(const mg_buffer* buffer, int* rank, uint64_t* shape /*
 mg_status mg_buffer_dtype(const mg_buffer* buffer, mg_dtype* dtype);
 mg_status mg_buffer_reshape(mg_buffer* buffer, int rank, const uint64_t* shape);
 void* mg_buffer_device_ptr(const mg_buffer* buffer);
+/* Marks a buffer as a weight (its contents change rarely): the tensor-core matmul then keeps
+ * the buffer's K-major tf32 operand form after first use instead of re-deriving it on every
+ * call, as the reference prepares compact weights at upload (src/kernels.rs:1667-1723).  Any
+ * write to the buffer drops the prepared form. */
+mg_status mg_buffer_set_weight(mg_buffer* buffer, int is_weight);
 
 /* ---------------------------------------------------------------------------------- */
 /* Kernels -- one entry per advertised hot-path operator, with the validation of the    */
@@ -313,6 +318,10 @@ mg_status mg_executor_replay_step(mg_executor* ex);
 /* `count` back-to-back replays, then one embedding-id check covering all of them (the flag
  * is sticky across replays and reset by the check). */
 mg_status mg_executor_replay_steps(mg_executor* ex, int count);
+/* One replay with no embedding-id check (the flag accumulates) ... */
+mg_status mg_executor_launch_step(mg_executor* ex);
+/* ... and the check of every replay since the last check (waits for the device). */
+mg_status mg_executor_check_steps(mg_executor* ex);
 /* Observation log (src/executor.rs:1082-1100): counts of Started/Completed/Failed. */
 mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t* completed,
                                    uint64_t* failed);

@@ -119,6 +119,7 @@ SIGNATURES = {
     "mg_buffer_dtype": [_P, _IP],
     "mg_buffer_reshape": [_P, _I, _U64P],
     "mg_buffer_device_ptr": [_P],
+    "mg_buffer_set_weight": [_P, _I],
     "mg_add": [_P, _P, _P, _PP],
     "mg_mul": [_P, _P, _P, _PP],
     "mg_residual_add": [_P, _P, _P, _PP],
@@ -157,6 +158,8 @@ SIGNATURES = {
     "mg_executor_abort_step_capture": [_P],
     "mg_executor_replay_step": [_P],
     "mg_executor_replay_steps": [_P, _I],
+    "mg_executor_launch_step": [_P],
+    "mg_executor_check_steps": [_P],
     "mg_executor_observations": [_P, _U64P, _U64P, _U64P],
     "mg_comm_unique_id": [ctypes.c_char_p],
     "mg_comm_init": [_P, _I, _I, ctypes.c_char_p, _PP],

@@ -351,9 +351,11 @@ int tp_role(mg_executor* ex, const mg_invocation* inv) {
     return role;
 }
 
-mg_status upload_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape, const float* data) {
+mg_status upload_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape, const float* data,
+                        bool weight = false) {
     Buffer* nb = nullptr;
     MG_TRY(buffer_new(ex->device, MG_F32, rank, shape, &nb));
+    nb->is_weight = weight;
     if (nb->count) {
         cudaError_t e = cudaMemcpyAsync(nb->ptr, data, nb->count * 4, cudaMemcpyHostToDevice, ex->device->stream);
         if (e != cudaSuccess) {
@@ -423,7 +425,7 @@ mg_status mg_executor_write_weight_tensor(mg_executor* ex, const char* id, int r
     std::lock_guard<std::mutex> g(ex->lock);
     MG_TRY(device_check(ex->handle));
     auto it = ex->plan.find(id);
-    if (!ex->comm || it == ex->plan.end() || rank == 0) return upload_tensor(ex, id, rank, shape, data);
+    if (!ex->comm || it == ex->plan.end() || rank == 0) return upload_tensor(ex, id, rank, shape, data, true);
     // This rank's share (src/multi/tensor_parallel.rs:206-236).
     const int parts = comm_world(ex->comm), member = comm_rank(ex->comm);
     uint64_t local[MG_MAX_RANK];
@@ -446,7 +448,7 @@ mg_status mg_executor_write_weight_tensor(mg_executor* ex, const char* id, int r
         local[0] = e - s;
         part.assign(data + s * per, data + e * per);
     }
-    return upload_tensor(ex, id, rank, local, part.data());
+    return upload_tensor(ex, id, rank, local, part.data(), true);
 }
 
 mg_status mg_executor_write_zeroed_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape) {
@@ -680,10 +682,13 @@ mg_status mg_executor_replay_steps(mg_executor* ex, int count) {
     if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
     MG_TRY(device_check(ex->handle));
     Device* d = ex->device;
-    for (int i = 0; i < count; i++) {
+    // count < 0: one launch and no check; 0: the check only.
+    const int launches = count < 0 ? 1 : count;
+    for (int i = 0; i < launches; i++) {
         MG_CUDA(cudaGraphLaunch(ex->graph_exec, d->stream), "replaying the captured step");
         d->launches.fetch_add(ex->graph_kernels);
     }
+    if (count < 0) return MG_OK;
     if (ex->step_has_embedding) {
         // The id flag is sticky across the replays: one read covers them all, then resets.
         MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading the id flag");
@@ -696,6 +701,10 @@ mg_status mg_executor_replay_steps(mg_executor* ex, int count) {
 }
 
 mg_status mg_executor_replay_step(mg_executor* ex) { return mg_executor_replay_steps(ex, 1); }
+
+mg_status mg_executor_launch_step(mg_executor* ex) { return mg_executor_replay_steps(ex, -1); }
+
+mg_status mg_executor_check_steps(mg_executor* ex) { return mg_executor_replay_steps(ex, 0); }
 
 mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t* completed, uint64_t* failed) {
     if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");

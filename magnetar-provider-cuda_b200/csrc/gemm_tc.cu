@@ -3,20 +3,24 @@
 //
 // The reference runs every f32-weight matmul of M >= 64 on the CUDA cores
 // (`matmul_split_k_tile_kernel`, src/kernels.cu:1643-1693) and keeps its tensor-core
-// kernels (`mma.sync` bf16, src/tensor_kernels.cu:393-705) for bf16-exact weights.  Here:
+// kernels (`mma.sync` bf16, src/tensor_kernels.cu:393-705) for bf16-exact weights.  Here each
+// operand x enters the MMA as two tf32 terms, x = hi + lo with hi = tf32(x) (rounded;
+// truncated instead when rounding would overflow a finite value to infinity) and
+// lo = tf32(x - hi), and the kernel accumulates lo*hi + hi*lo + hi*hi in f32 TMEM -- the
+// dropped lo*lo term is below 2^-22 relative, far inside the f32 contract's 1e-4 rel-L2.
 //
-//  1. A split pass writes each operand as two K-major tf32 terms, x = hi + lo with
-//     hi = tf32(x) (rounded, truncated instead when rounding would overflow a finite
-//     value to infinity) and lo = tf32(x - hi).  B (row-major [K, N]) is transposed to
-//     [N, K] in the same pass, so both operands feed the MMA K-major.
-//  2. The GEMM kernel: one 128 x BN output tile per CTA.  Warp 0 issues TMA loads of
-//     A.hi, A.lo, B.hi, B.lo (32 k-columns = one 128-byte swizzle row per tile row) into a
-//     STAGES-deep ring; warp 1 allocates TMEM and issues, per 8-wide k step, the three
-//     products lo*hi + hi*lo + hi*hi into one f32 accumulator (the dropped lo*lo term is
-//     below 2^-22 relative); warps 2-5 read the accumulator back with tcgen05.ld and apply
-//     the addend (bias row / residual) or the SwiGLU gate before storing.
-//  Error of each product is about 2^-22 relative, well inside the f32 contract's 1e-4
-//  relative-L2 bound for matmul.
+// One CTA computes a 128 x BN output tile over a range of k:
+//   warp 0      TMA producer: 32-column k-blocks (one 128-byte swizzle row per tile row) of
+//               A and B into a STAGES-deep shared-memory ring;
+//   warp 1      allocates TMEM and issues the MMAs (one thread), committing each stage back;
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator, bias / residual / SwiGLU, store --
+//               or, when k is split across CTAs, the raw partial tile to a workspace that a
+//               fixed-order reduction kernel finishes;
+//   warps 6-9   (when A arrives as raw f32) split each A tile into its hi/lo terms in shared
+//               memory, in place, so no separate pass over A is needed.
+// B comes either from a weight's prepared hi/lo form (built once, kept with the weight) or
+// from a per-call split pass that also transposes it to K-major.  Small output grids (the
+// decoder layer's M = 128) use narrower tiles and split k so that every SM has work.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -39,11 +43,10 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128;
-constexpr int BK = 32;  // f32 k-columns per stage: one 128-byte swizzle row
-constexpr int kThreadsTC = 192;
+constexpr int BK = 32;       // f32 k-columns per stage: one 128-byte swizzle row
 constexpr int kGroupM = 16;  // rasterisation: M-tiles walked together for L2 reuse
 
-// ---- split pass ------------------------------------------------------------------------------
+// ---- operand split ----------------------------------------------------------------------------
 __device__ __forceinline__ float tf32_round(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -57,12 +60,33 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     lo = tf32_round(x - h);
 }
 
-// src [rows, k] (row stride ld) -> hi/lo [rows, kp], zero past k.
+__device__ __forceinline__ void split4(float4 v, float4& hi, float4& lo) {
+    split_tf32(v.x, hi.x, lo.x);
+    split_tf32(v.y, hi.y, lo.y);
+    split_tf32(v.z, hi.z, lo.z);
+    split_tf32(v.w, hi.w, lo.w);
+}
+
+// src [rows, k] (row stride ld) -> hi/lo [rows, kp], zero past k.  16-byte vectors when the
+// rows allow it.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, uint64_t ld, uint64_t rows,
                                                          uint64_t k, float* __restrict__ hi, float* __restrict__ lo,
-                                                         uint64_t kp) {
+                                                         uint64_t kp, int vec) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {  // k == kp, k % 4 == 0, 16-byte aligned
+        const uint64_t n4 = rows * kp / 4;
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        for (uint64_t i = t0; i < n4; i += stride) {
+            float4 h, l;
+            split4(s4[i], h, l);
+            reinterpret_cast<float4*>(hi)[i] = h;
+            reinterpret_cast<float4*>(lo)[i] = l;
+        }
+        return;
+    }
     const uint64_t total = rows * kp;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    for (uint64_t i = t0; i < total; i += stride) {
         const uint64_t r = i / kp, c = i % kp;
         float h = 0.0f, l = 0.0f;
         if (c < k) split_tf32(src[r * ld + c], h, l);
@@ -71,19 +95,20 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     }
 }
 
-// src [r_count, c_count] row-major -> hi/lo [c_count, rp] with dst[c][r] = src[r][c].
+// src [r_count, c_count] row-major -> hi/lo [c_count, rp] with dst[c][r] = src[r][c], through
+// 64 x 64 shared-memory tiles.
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ src, uint64_t r_count,
                                                               uint64_t c_count, float* __restrict__ hi,
                                                               float* __restrict__ lo, uint64_t rp) {
-    __shared__ float tile[32][33];
-    const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
-    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
-    for (int j = ty; j < 32; j += 8) {
+    __shared__ float tile[64][65];
+    const uint64_t c0 = (uint64_t)blockIdx.x * 64, r0 = (uint64_t)blockIdx.y * 64;
+    const int tx = threadIdx.x % 64, ty = threadIdx.x / 64;  // 64 x 4
+    for (int j = ty; j < 64; j += 4) {
         const uint64_t r = r0 + j, c = c0 + tx;
         tile[j][tx] = (r < r_count && c < c_count) ? src[r * c_count + c] : 0.0f;
     }
     __syncthreads();
-    for (int j = ty; j < 32; j += 8) {
+    for (int j = ty; j < 64; j += 4) {
         const uint64_t c = c0 + j, r = r0 + tx;
         if (c < c_count && r < rp) {
             float h, l;
@@ -99,45 +124,50 @@ struct TcParams {
     float* out;
     const float* addend;
     int addend_mode;
-    int gated;
     uint64_t m, n, k;
     int tiles_m, tiles_n;
-    int* error;  // device word set when a wait times out
+    int kb_per_split;  // k-blocks each CTA of a split handles
+    int splits;
+    float* partial;    // split-k workspace [NB][splits][m][n] (splits > 1)
+    int* error;        // device word set when a wait times out
 };
 
-template <int BN, int NB, int STAGES>
+template <int BN, int NB, int STAGES, bool A_RAW>
 struct TcShape {
-    static constexpr int kATile = BM * BK * 4;          // bytes of one A term tile
-    static constexpr int kBTile = BN * BK * 4;          // bytes of one B term tile
+    static constexpr int kATile = BM * BK * 4;  // bytes of one A term tile
+    static constexpr int kBTile = BN * BK * 4;  // bytes of one B term tile
     static constexpr int kStage = 2 * kATile + NB * 2 * kBTile;
-    static constexpr int kSmem = STAGES * kStage + 1024 /* align */ + 256 /* barriers */;
-    static constexpr uint32_t kTmemCols = NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
+    static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + NB * 2 * kBTile;  // TMA bytes per stage
+    static constexpr int kSmem = STAGES * kStage + 1024 /* align */ + 512 /* barriers */;
+    static constexpr uint32_t kTmemCols =
+        NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
+    static constexpr int kThreads = A_RAW ? 320 : 192;
 };
 
-template <int BN, int NB, int STAGES>
-__global__ void __launch_bounds__(kThreadsTC, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+template <int BN, int NB, int STAGES, bool A_RAW>
+__global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                    const __grid_constant__ CUtensorMap map_b2hi, const __grid_constant__ CUtensorMap map_b2lo,
                    TcParams p) {
-    using S = TcShape<BN, NB, STAGES>;
+    using S = TcShape<BN, NB, STAGES, A_RAW>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* base_ptr = smem_raw + (base - raw);
     const uint32_t bar_base = base + STAGES * S::kStage;
     uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + STAGES * S::kStage);
-    // bars[0..STAGES): full, [STAGES..2*STAGES): empty, [2*STAGES]: accumulator ready
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 2 * STAGES + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 2);
-    (void)bars;
+    // bars: [0, S) full (TMA), [S, 2S) empty (MMA done), [2S, 3S) converted, [3S] accumulator
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * STAGES + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 2);
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
     auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
-    const uint32_t accum_bar = bar_base + 8u * (2 * STAGES);
+    auto conv_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + s); };
+    const uint32_t accum_bar = bar_base + 8u * (3 * STAGES);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-    // Grouped rasterisation of the 1-D grid over (tiles_m, tiles_n).
+    // Grouped rasterisation of the output tiles (blockIdx.x); blockIdx.y is the k split.
     const int tile = blockIdx.x;
     const int group_size = kGroupM * p.tiles_n;
     const int group = tile / group_size;
@@ -146,20 +176,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int tm = first_m + (tile % group_size) % rows_in_group;
     const int tn = (tile % group_size) / rows_in_group;
     const int m0 = tm * BM, n0 = tn * BN;
-    const int num_kb = (int)((p.k + BK - 1) / BK);
+    const int num_kb_total = (int)((p.k + BK - 1) / BK);
+    const int kb0 = blockIdx.y * p.kb_per_split;
+    const int num_kb = min(num_kb_total, kb0 + p.kb_per_split) - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
+            mbar_init(conv_bar(s), 128);
         }
         mbar_init(accum_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tensormap(&map_ahi);
-        prefetch_tensormap(&map_alo);
+        prefetch_tensormap(&map_a0);
+        if (!A_RAW) prefetch_tensormap(&map_a1);
         prefetch_tensormap(&map_bhi);
         prefetch_tensormap(&map_blo);
         if (NB == 2) {
@@ -179,9 +212,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------------
         if (lane == 0) {
-            for (int kb = 0; kb < num_kb; kb++) {
-                const int s = kb % STAGES;
-                const uint32_t phase = (uint32_t)(kb / STAGES) & 1u;
+            for (int i = 0; i < num_kb; i++) {
+                const int s = i % STAGES;
+                const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
                 if (!mbar_wait(empty_bar(s), phase ^ 1u)) {
                     *abort_flag = 1;
                     atomicExch(p.error, 1);
@@ -189,10 +222,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 }
                 if (*abort_flag) break;
                 const uint32_t st = base + s * S::kStage;
-                mbar_arrive_expect_tx(full_bar(s), S::kStage);
-                const int kx = kb * BK;
-                tma_load_2d(st, &map_ahi, full_bar(s), kx, m0);
-                tma_load_2d(st + S::kATile, &map_alo, full_bar(s), kx, m0);
+                mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
+                const int kx = (kb0 + i) * BK;
+                tma_load_2d(st, &map_a0, full_bar(s), kx, m0);
+                if (!A_RAW) tma_load_2d(st + S::kATile, &map_a1, full_bar(s), kx, m0);
                 tma_load_2d(st + 2 * S::kATile, &map_bhi, full_bar(s), kx, n0);
                 tma_load_2d(st + 2 * S::kATile + S::kBTile, &map_blo, full_bar(s), kx, n0);
                 if (NB == 2) {
@@ -207,10 +240,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
             bool ok = true;
-            for (int kb = 0; kb < num_kb; kb++) {
-                const int s = kb % STAGES;
-                const uint32_t phase = (uint32_t)(kb / STAGES) & 1u;
-                if (!mbar_wait(full_bar(s), phase)) {
+            for (int i = 0; i < num_kb; i++) {
+                const int s = i % STAGES;
+                const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
+                if (!mbar_wait(full_bar(s), phase) || (A_RAW && !mbar_wait(conv_bar(s), phase))) {
                     *abort_flag = 1;
                     atomicExch(p.error, 1);
                     ok = false;
@@ -231,7 +264,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         const uint32_t bt = st + 2 * S::kATile + z * 2 * S::kBTile;
                         const uint64_t bhi = desc_k_sw128(bt), blo = desc_k_sw128(bt + S::kBTile);
                         const uint32_t d = tmem + (uint32_t)(z * BN);
-                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                         mma_tf32(d, alo + koff, bhi + koff, idesc, acc);
                         mma_tf32(d, ahi + koff, blo + koff, idesc, 1u);
                         mma_tf32(d, ahi + koff, bhi + koff, idesc, 1u);
@@ -243,6 +276,33 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             else mbar_arrive(accum_bar);  // release the epilogue
         }
         __syncwarp();
+    } else if (warp >= 6) {
+        // ---- A converter: raw f32 tile -> hi (in place) + lo ------------------------------
+        if (A_RAW) {
+            const int t = threadIdx.x - 192;  // 0..127
+            for (int i = 0; i < num_kb; i++) {
+                const int s = i % STAGES;
+                const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
+                if (!mbar_wait(full_bar(s), phase)) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    // still arrive so that the MMA warp does not wait for us
+                }
+                float4* a_hi = reinterpret_cast<float4*>(base_ptr + s * S::kStage);
+                float4* a_lo = reinterpret_cast<float4*>(base_ptr + s * S::kStage + S::kATile);
+#pragma unroll
+                for (int j = 0; j < S::kATile / 16 / 128; j++) {
+                    const int idx = t + j * 128;
+                    float4 h, l;
+                    split4(a_hi[idx], h, l);
+                    a_hi[idx] = h;
+                    a_lo[idx] = l;
+                }
+                fence_proxy_async();  // make the generic-proxy writes visible to tcgen05.mma
+                mbar_arrive(conv_bar(s));
+                if (*abort_flag) break;
+            }
+        }
     } else {
         // ---- epilogue: warps 2..5 own TMEM lane quarters (warp % 4) ----------------------
         const int q = warp % 4;
@@ -254,9 +314,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (ready) {
             const uint64_t row = (uint64_t)m0 + q * 32 + lane;
             const bool row_ok = row < p.m;
+            const bool direct = p.splits == 1;
             const bool vec = (p.n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
                              (p.addend_mode != 2 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0) &&
-                             (p.addend_mode != 1 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0);
+                             (p.addend_mode != 1 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0) &&
+                             (direct || (reinterpret_cast<uintptr_t>(p.partial) & 15) == 0);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
@@ -266,6 +328,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 tc_wait_ld();
                 if (!row_ok) continue;
                 const uint64_t col0 = (uint64_t)n0 + c0;
+                if (!direct) {
+                    // raw partial sums of this k split; the reduction applies addend / gate
+#pragma unroll
+                    for (int z = 0; z < NB; z++) {
+                        const float* src = z ? u : v;
+                        float* dst = p.partial + (((uint64_t)z * p.splits + blockIdx.y) * p.m + row) * p.n;
+                        if (vec && col0 + 32 <= p.n) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(dst + col0 + j) =
+                                    make_float4(src[j], src[j + 1], src[j + 2], src[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                if (col0 + j < p.n) dst[col0 + j] = src[j];
+                        }
+                    }
+                    continue;
+                }
                 float* orow = p.out + row * p.n;
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
@@ -300,6 +381,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
 }
 
+// Split-k finish: out = sum over splits in split order [+ addend] (or silu(gate) * up).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                                            uint64_t m, uint64_t n, int splits, int gated,
+                                                            const float* __restrict__ addend, int addend_mode) {
+    const uint64_t total = m * n;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int z = 0; z < splits; z++) s += partial[(uint64_t)z * total + i];
+        if (gated) {
+            float u = 0.0f;
+            for (int z = 0; z < splits; z++) u += partial[(uint64_t)(splits + z) * total + i];
+            s = (s * (1.0f / (1.0f + expf(-s)))) * u;
+        } else if (addend_mode == 1) {
+            s += addend[i % n];
+        } else if (addend_mode == 2) {
+            s += addend[i];
+        }
+        out[i] = s;
+    }
+}
+
 // ---- host side ---------------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -314,12 +416,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// K-major [rows, kp] f32 matrix, box [box_rows, 32] with 128-byte swizzle.
-mg_status make_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t kp, uint32_t box_rows) {
+// K-major [rows, cols] f32 matrix (row stride ld elements), box [box_rows, 32] with 128-byte
+// swizzle.
+mg_status make_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
     auto fn = encode_fn();
     if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
-    cuuint64_t dims[2] = {kp, rows};
-    cuuint64_t strides[1] = {kp * sizeof(float)};
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * sizeof(float)};
     cuuint32_t box[2] = {BK, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
@@ -339,40 +442,47 @@ inline unsigned grid_cap(const Device* d, uint64_t items) {
 mg_status split_operand(Device* d, const float* src, uint64_t rows, uint64_t k, bool kmajor, float* hi, float* lo,
                         uint64_t kp) {
     if (kmajor) {
-        split_rows_kernel<<<grid_cap(d, rows * kp), 256, 0, d->stream>>>(src, k, rows, k, hi, lo, kp);
+        const int vec = k == kp && k % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+        split_rows_kernel<<<grid_cap(d, vec ? rows * kp / 4 : rows * kp), 256, 0, d->stream>>>(src, k, rows, k, hi, lo,
+                                                                                              kp, vec);
     } else {
-        dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((kp + 31) / 32));
+        dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((kp + 63) / 64));
         if (grid.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "matmul inner dimension %llu is too large", (unsigned long long)k);
         split_transpose_kernel<<<grid, 256, 0, d->stream>>>(src, k, rows, hi, lo, kp);
     }
     return launched(d, "operand split kernel launch");
 }
 
-template <int BN, int NB, int STAGES>
-mg_status launch_tc(Device* d, const k::GemmArgs& g, const CUtensorMap* maps, int* err) {
-    using S = TcShape<BN, NB, STAGES>;
+template <int BN, int NB, int STAGES, bool A_RAW>
+mg_status launch_tc(Device* d, const TcParams& p, const CUtensorMap* maps) {
+    using S = TcShape<BN, NB, STAGES, A_RAW>;
+    static_assert(S::kSmem <= 227 * 1024, "shared memory budget");
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
-        MG_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, NB, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+        MG_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, NB, STAGES, A_RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     S::kSmem),
                 "configuring the tensor-core matmul");
         configured[d->ordinal & 63] = true;
     }
-    TcParams p;
-    p.out = g.out;
-    p.addend = g.addend;
-    p.addend_mode = g.addend_mode;
-    p.gated = g.gated;
-    p.m = g.m;
-    p.n = g.n;
-    p.k = g.k;
-    p.tiles_m = (int)((g.m + BM - 1) / BM);
-    p.tiles_n = (int)((g.n + BN - 1) / BN);
-    p.error = err;
     const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
     if (tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "matmul has too many output tiles");
-    gemm_tc_kernel<BN, NB, STAGES><<<(unsigned)tiles, kThreadsTC, S::kSmem, d->stream>>>(
-        maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
+    dim3 grid((unsigned)tiles, (unsigned)p.splits);
+    gemm_tc_kernel<BN, NB, STAGES, A_RAW><<<grid, S::kThreads, S::kSmem, d->stream>>>(maps[0], maps[1], maps[2], maps[3],
+                                                                                      maps[4], maps[5], p);
     return launched(d, "tensor-core matmul launch");
+}
+
+template <int NB, bool A_RAW>
+mg_status launch_bn(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
+    if constexpr (NB == 2) {
+        if (bn == 128) return launch_tc<128, NB, 2, A_RAW>(d, p, maps);
+        if (bn == 64) return launch_tc<64, NB, 3, A_RAW>(d, p, maps);
+        return launch_tc<32, NB, 4, A_RAW>(d, p, maps);
+    } else {
+        if (bn == 128) return launch_tc<128, NB, 3, A_RAW>(d, p, maps);
+        if (bn == 64) return launch_tc<64, NB, 4, A_RAW>(d, p, maps);
+        return launch_tc<32, NB, 5, A_RAW>(d, p, maps);
+    }
 }
 
 bool tensor_cores_enabled() {
@@ -384,43 +494,122 @@ bool tensor_cores_enabled() {
     return enabled == 1;
 }
 
+// Output tile width: the widest of 128 / 64 / 32 columns that still gives every SM a tile,
+// so that small matmuls (the decoder layer's M = 128) spread over more CTAs.
+int pick_bn(const Device* d, uint64_t m, uint64_t n) {
+    const uint64_t tm = (m + BM - 1) / BM;
+    if (tm * ((n + 127) / 128) >= (uint64_t)d->sm_count) return 128;
+    if (tm * ((n + 63) / 64) >= (uint64_t)d->sm_count) return 64;
+    return 32;
+}
+
 }  // namespace
 
 namespace k {
 
 mg_status gemm_tc(Device* d, const GemmArgs& g) {
-    const uint64_t kp = (g.k + 3) & ~3ull;  // TMA row strides are multiples of 16 bytes
+    const uint64_t kp = gemm_kp(g.k);  // TMA row strides are multiples of 16 bytes
     const int nb = g.gated ? 2 : 1;
-    float *a_split = nullptr, *b_split = nullptr;
-    MG_TRY(scratch(d, 1, 2 * g.m * kp * sizeof(float), (void**)&a_split));
-    MG_TRY(scratch(d, 2, (size_t)nb * 2 * g.n * kp * sizeof(float), (void**)&b_split));
-    float* ahi = a_split;
-    float* alo = a_split + g.m * kp;
-    // A is K-major unless transposed; B (row-major [K, N]) is K-major only when transposed.
-    MG_TRY(split_operand(d, g.a, g.m, g.k, !g.transpose_a, ahi, alo, kp));
-    float* bhi[2];
-    float* blo[2];
-    for (int z = 0; z < nb; z++) {
-        bhi[z] = b_split + (size_t)z * 2 * g.n * kp;
-        blo[z] = bhi[z] + g.n * kp;
-        MG_TRY(split_operand(d, z ? g.b2 : g.b, g.n, g.k, g.transpose_b != 0, bhi[z], blo[z], kp));
+    // A: raw through TMA (split inside the kernel) when it is K-major with 16-byte rows and
+    // small -- this saves a launch, but the in-kernel split costs shared-memory bandwidth in
+    // the main loop, so large A (M = 2048: 0.48 vs 0.45 ms measured) takes a split pass.
+    const bool a_raw = !g.transpose_a && g.k % 4 == 0 && (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 && g.m <= 512;
+    const float* ahi = g.a;
+    const float* alo = nullptr;
+    if (!a_raw) {
+        float* a_split = nullptr;
+        MG_TRY(scratch(d, 1, 2 * g.m * kp * sizeof(float), (void**)&a_split));
+        MG_TRY(split_operand(d, g.a, g.m, g.k, !g.transpose_a, a_split, a_split + g.m * kp, kp));
+        ahi = a_split;
+        alo = a_split + g.m * kp;
     }
-    constexpr int BN = 128;
+    const float* bhi[2];
+    const float* blo[2];
+    bool need_split = false;
+    for (int z = 0; z < nb; z++) need_split |= g.b_prep[z] == nullptr;
+    float* b_split = nullptr;
+    if (need_split) MG_TRY(scratch(d, 2, (size_t)nb * 2 * g.n * kp * sizeof(float), (void**)&b_split));
+    for (int z = 0; z < nb; z++) {
+        if (g.b_prep[z]) {
+            bhi[z] = g.b_prep[z];
+            blo[z] = g.b_prep[z] + g.n * kp;
+        } else {
+            float* hi = b_split + (size_t)z * 2 * g.n * kp;
+            float* lo = hi + g.n * kp;
+            MG_TRY(split_operand(d, z ? g.b2 : g.b, g.n, g.k, g.transpose_b != 0, hi, lo, kp));
+            bhi[z] = hi;
+            blo[z] = lo;
+        }
+    }
+    const int bn = pick_bn(d, g.m, g.n);
+    TcParams p;
+    p.out = g.out;
+    p.addend = g.addend;
+    p.addend_mode = g.addend_mode;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.tiles_m = (int)((g.m + BM - 1) / BM);
+    p.tiles_n = (int)((g.n + bn - 1) / bn);
+    p.error = d->flags + 2;
+    // Split k when the output grid leaves SMs idle, keeping at least 4 k-blocks per split.
+    const int num_kb = (int)((g.k + BK - 1) / BK);
+    const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
+    int splits = 1;
+    if (tiles < (uint64_t)d->sm_count && num_kb >= 8) {
+        splits = (int)((d->sm_count + tiles - 1) / tiles);
+        if (splits > num_kb / 4) splits = num_kb / 4;
+        if (splits < 1) splits = 1;
+    }
+    p.kb_per_split = (num_kb + splits - 1) / splits;
+    p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
+    p.partial = nullptr;
+    if (p.splits > 1)
+        MG_TRY(scratch(d, 3, (size_t)nb * p.splits * g.m * g.n * sizeof(float), (void**)&p.partial));
     CUtensorMap maps[6];
-    MG_TRY(make_map(&maps[0], ahi, g.m, kp, BM));
-    MG_TRY(make_map(&maps[1], alo, g.m, kp, BM));
-    MG_TRY(make_map(&maps[2], bhi[0], g.n, kp, BN));
-    MG_TRY(make_map(&maps[3], blo[0], g.n, kp, BN));
+    if (a_raw) {
+        MG_TRY(make_map(&maps[0], ahi, g.m, g.k, g.k, BM));
+        maps[1] = maps[0];
+    } else {
+        MG_TRY(make_map(&maps[0], ahi, g.m, kp, kp, BM));
+        MG_TRY(make_map(&maps[1], alo, g.m, kp, kp, BM));
+    }
+    MG_TRY(make_map(&maps[2], bhi[0], g.n, kp, kp, bn));
+    MG_TRY(make_map(&maps[3], blo[0], g.n, kp, kp, bn));
     if (nb == 2) {
-        MG_TRY(make_map(&maps[4], bhi[1], g.n, kp, BN));
-        MG_TRY(make_map(&maps[5], blo[1], g.n, kp, BN));
+        MG_TRY(make_map(&maps[4], bhi[1], g.n, kp, kp, bn));
+        MG_TRY(make_map(&maps[5], blo[1], g.n, kp, kp, bn));
     } else {
         maps[4] = maps[2];
         maps[5] = maps[3];
     }
-    int* err = d->flags + 2;
-    if (nb == 2) return launch_tc<BN, 2, 2>(d, g, maps, err);
-    return launch_tc<BN, 1, 3>(d, g, maps, err);
+    mg_status s;
+    if (nb == 2) s = a_raw ? launch_bn<2, true>(d, bn, p, maps) : launch_bn<2, false>(d, bn, p, maps);
+    else s = a_raw ? launch_bn<1, true>(d, bn, p, maps) : launch_bn<1, false>(d, bn, p, maps);
+    MG_TRY(s);
+    if (p.splits > 1) {
+        splitk_reduce_kernel<<<grid_cap(d, g.m * g.n), 256, 0, d->stream>>>(p.partial, g.out, g.m, g.n, p.splits, nb == 2,
+                                                                           g.addend, g.addend_mode);
+        MG_TRY(launched(d, "split-k reduction launch"));
+    }
+    return MG_OK;
+}
+
+bool gemm_uses_tensor_cores(uint64_t m, uint64_t n, uint64_t k, int transpose_b, const float* b) {
+    if (m == 0 || n == 0 || k == 0) return false;
+    GemmArgs probe{};
+    probe.m = m;
+    probe.n = n;
+    probe.k = k;
+    probe.transpose_b = transpose_b;
+    probe.b = b;
+    if (gemv_eligible(probe)) return false;
+    return tensor_cores_enabled() && m > 16;
+}
+
+mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int transposed, float* dst) {
+    const uint64_t kp = gemm_kp(k);
+    return split_operand(d, b, n, k, transposed != 0, dst, dst + n * kp, kp);
 }
 
 mg_status gemm(Device* d, const GemmArgs& g) {

@@ -8,7 +8,13 @@
 // one partial per (slice, row, column) to a workspace, and a second kernel sums the slices
 // in slice order and applies the addend (bias row / residual) or the SwiGLU gate -- so the
 // result is deterministic, and B (the 64 MB weight at K = N = 4096) is read exactly once.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace mg {
 namespace {
@@ -154,6 +160,159 @@ void launch_partial(Device* d, dim3 grid, size_t smem, const k::GemmArgs& g, flo
                                                                    g.transpose_a);
 }
 
+// ---- TMA-staged streaming of B ---------------------------------------------------------------
+// A producer lane streams [kChunkRows x 128] tiles of B (16 KB) into a kStages-deep shared
+// ring with TMA; every warp takes 4 consecutive rows of each tile and multiplies them by the
+// matching 4 columns of A (one 16-byte shared load per row of A), so ~96 KB of B is in flight
+// per CTA regardless of the warps' arithmetic.
+constexpr int kChunkRows = 32;
+constexpr int kStages = 6;
+constexpr int kChunkBytes = kChunkRows * kCols * 4;
+
+template <int M>
+__global__ void __launch_bounds__(kWarps * 32) gemv_tma_kernel(const __grid_constant__ CUtensorMap map_b,
+                                                                const __grid_constant__ CUtensorMap map_b2,
+                                                                const float* __restrict__ a, float* __restrict__ partial,
+                                                                uint64_t m, uint64_t n, uint64_t k, uint64_t slice_len,
+                                                                int transpose_a, int* error) {
+    extern __shared__ uint8_t smem_raw[];
+    using namespace sm100;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 127u) & ~127u;
+    uint8_t* base_ptr = smem_raw + (base - raw);
+    float* ring = reinterpret_cast<float*>(base_ptr);                        // [kStages][32][128]
+    float* a_s = ring + kStages * kChunkRows * kCols;                          // [M][slice_len]
+    float* red = a_s + M * slice_len;                                          // [kWarps][kCols]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + kWarps * kCols);        // full[kStages], empty[kStages]
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t col0 = (uint64_t)blockIdx.x * kCols;
+    const uint64_t slice = blockIdx.y;
+    const uint64_t k0 = slice * slice_len;
+    const uint64_t k1 = min(k, k0 + slice_len);
+    const int chunks = (int)((k1 - k0 + kChunkRows - 1) / kChunkRows);
+    const CUtensorMap* map = blockIdx.z ? &map_b2 : &map_b;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), kWarps);
+        }
+        fence_barrier_init();
+    }
+    // Stage A[:, k0:k1] (zero past k1 so a partial last tile multiplies zero rows of B).
+    for (uint64_t i = threadIdx.x; i < (uint64_t)M * slice_len; i += blockDim.x) {
+        const uint64_t r = i / slice_len, kk = k0 + i % slice_len;
+        float v = 0.0f;
+        if (r < m && kk < k1) v = transpose_a ? a[kk * m + r] : a[r * k + kk];
+        a_s[i] = v;
+    }
+    __syncthreads();
+    // The producer keeps kStages tiles in flight; it is lane 0 of warp 0, which also computes.
+    int issued = 0;
+    auto issue = [&](int c) {
+        const int s = c % kStages;
+        mbar_arrive_expect_tx(full_bar(s), kChunkBytes);
+        tma_load_2d(base + (uint32_t)(s * kChunkBytes), map, full_bar(s), (int)col0, (int)(k0 + (uint64_t)c * kChunkRows));
+    };
+    if (threadIdx.x == 0) {
+        prefetch_tensormap(map);
+        for (; issued < min(chunks, kStages); issued++) issue(issued);
+    }
+
+    float acc[M][4];
+#pragma unroll
+    for (int r = 0; r < M; r++) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < chunks; c++) {
+        const int s = c % kStages;
+        const uint32_t phase = (uint32_t)(c / kStages) & 1u;
+        if (!mbar_wait(full_bar(s), phase)) {
+            ok = false;
+            atomicExch(error, 1);
+            break;
+        }
+        const float* tile = ring + s * kChunkRows * kCols;
+        const int rr = warp * 4;  // this warp's 4 rows of the tile
+        float4 bv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) bv[u] = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+        const uint64_t kl = (uint64_t)c * kChunkRows + rr;  // row within the slice (multiple of 4)
+#pragma unroll
+        for (int r = 0; r < M; r++) {
+            const float4 av = *reinterpret_cast<const float4*>(a_s + r * slice_len + kl);
+            const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                acc[r][0] += aa[u] * bv[u].x;
+                acc[r][1] += aa[u] * bv[u].y;
+                acc[r][2] += aa[u] * bv[u].z;
+                acc[r][3] += aa[u] * bv[u].w;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(s));
+        if (threadIdx.x == 0 && issued < chunks) {
+            // refill the stage just drained once every warp has released it
+            const int rs = issued % kStages;
+            const uint32_t rphase = (uint32_t)(issued / kStages - 1) & 1u;
+            if (!mbar_wait(empty_bar(rs), rphase)) {
+                atomicExch(error, 1);
+            } else {
+                issue(issued);
+            }
+            issued++;
+        }
+    }
+    (void)ok;
+    // Fixed-order combine of the warps, one output row at a time.
+    float* out_base = partial + ((uint64_t)blockIdx.z * gridDim.y + slice) * m * n;
+#pragma unroll
+    for (int r = 0; r < M; r++) {
+        if (r >= (int)m) break;
+        __syncthreads();
+        *reinterpret_cast<float4*>(&red[warp * kCols + 4 * lane]) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        __syncthreads();
+        if (threadIdx.x < kCols) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int wi = 0; wi < kWarps; wi++) sum += red[wi * kCols + threadIdx.x];
+            const uint64_t cidx = col0 + threadIdx.x;
+            if (cidx < n) out_base[r * n + cidx] = sum;
+        }
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 gemv_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major [k, n] f32 B, box [kChunkRows x kCols], no swizzle.
+mg_status gemv_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n) {
+    auto fn = gemv_encode_fn();
+    if (!fn) return mg::fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {n, k};
+    cuuint64_t strides[1] = {n * sizeof(float)};
+    cuuint32_t box[2] = {kCols, kChunkRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(b), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return mg::fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
 }  // namespace
 
 namespace k {
@@ -164,7 +323,60 @@ bool gemv_eligible(const GemmArgs& g) {
            (reinterpret_cast<uintptr_t>(g.b) & 15) == 0 && (!g.b2 || (reinterpret_cast<uintptr_t>(g.b2) & 15) == 0);
 }
 
+template <int M>
+mg_status launch_tma(Device* d, dim3 grid, size_t smem, const CUtensorMap* maps, const GemmArgs& g, float* partial,
+                     uint64_t slice_len) {
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(gemv_tma_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                "configuring the gemv kernel");
+        configured[d->ordinal & 63] = true;
+    }
+    gemv_tma_kernel<M><<<grid, kWarps * 32, smem, d->stream>>>(maps[0], maps[1], g.a, partial, g.m, g.n, g.k, slice_len,
+                                                                g.transpose_a, d->flags + 2);
+    return launched(d, "gemv kernel launch");
+}
+
+// The TMA-staged path: about two CTAs per SM, each streaming one k-slice of one 128-column
+// tile of B.
+mg_status gemv_tma(Device* d, const GemmArgs& g) {
+    const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
+    const int zs = g.gated ? 2 : 1;
+    const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
+    const uint64_t max_slice = (uint64_t)(8192 / mp) / kChunkRows * kChunkRows;  // A's slice <= 32 KB
+    uint64_t slices = ((uint64_t)d->sm_count * 2 / zs + col_tiles - 1) / col_tiles;
+    if (slices < 1) slices = 1;
+    uint64_t slice_len = (g.k + slices - 1) / slices;
+    slice_len = ((slice_len + kChunkRows - 1) / kChunkRows) * kChunkRows;
+    if (slice_len > max_slice) slice_len = max_slice;
+    slices = (g.k + slice_len - 1) / slice_len;
+    if (slices > 65535) return fail(MG_SHAPE_UNSUPPORTED, "gemv inner dimension %llu is too large", (unsigned long long)g.k);
+    const size_t smem = 128 + (size_t)kStages * kChunkBytes + ((size_t)mp * slice_len + kWarps * kCols) * sizeof(float) +
+                        2 * kStages * sizeof(uint64_t);
+    float* partial = nullptr;
+    MG_TRY(scratch(d, 0, (size_t)zs * slices * g.m * g.n * sizeof(float), (void**)&partial));
+    CUtensorMap maps[2];
+    MG_TRY(gemv_map(&maps[0], g.b, g.k, g.n));
+    if (g.gated) MG_TRY(gemv_map(&maps[1], g.b2, g.k, g.n));
+    else maps[1] = maps[0];
+    dim3 grid((unsigned)col_tiles, (unsigned)slices, (unsigned)zs);
+    switch (mp) {
+        case 1: MG_TRY(launch_tma<1>(d, grid, smem, maps, g, partial, slice_len)); break;
+        case 2: MG_TRY(launch_tma<2>(d, grid, smem, maps, g, partial, slice_len)); break;
+        case 4: MG_TRY(launch_tma<4>(d, grid, smem, maps, g, partial, slice_len)); break;
+        case 8: MG_TRY(launch_tma<8>(d, grid, smem, maps, g, partial, slice_len)); break;
+        default: MG_TRY(launch_tma<16>(d, grid, smem, maps, g, partial, slice_len)); break;
+    }
+    const uint64_t total = g.m * g.n;
+    uint64_t blocks = (total + 255) / 256;
+    if (blocks > (uint64_t)d->sm_count * 8) blocks = (uint64_t)d->sm_count * 8;
+    gemv_reduce_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, d->stream>>>(partial, g.out, g.m, g.n, slices,
+                                                                              g.addend, g.addend_mode, g.gated);
+    return launched(d, "gemv reduce kernel launch");
+}
+
 mg_status gemv(Device* d, const GemmArgs& g) {
+    if (g.n <= (1ull << 31) && g.k <= (1ull << 31)) return gemv_tma(d, g);
     const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
     // Enough slices of k for about four CTAs per SM, each slice a multiple of the rows the
     // warps consume per step and at most 512 rows (A's slice fits shared memory).

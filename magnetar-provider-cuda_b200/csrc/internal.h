@@ -81,7 +81,17 @@ struct Buffer {
     void* ptr = nullptr;
     uint64_t count = 0;  // elements
     bool owned = true;
+    // A weight keeps the tensor-core matmul's operand form of itself once a matmul has read
+    // it: the K-major tf32 hi/lo terms ([n, kp] each, hi first), built on first use with the
+    // transpose flag it was read with, and dropped whenever the buffer's contents change.
+    bool is_weight = false;
+    float* prep = nullptr;
+    uint64_t prep_n = 0, prep_k = 0, prep_kp = 0;
+    int prep_transposed = -1;
 };
+
+// Drops a weight's prepared operand form (its contents are about to change).
+void buffer_drop_prep(Buffer* b);
 
 inline Buffer* buf(mg_buffer* b) { return reinterpret_cast<Buffer*>(b); }
 inline const Buffer* buf(const mg_buffer* b) { return reinterpret_cast<const Buffer*>(b); }
@@ -137,8 +147,17 @@ struct GemmArgs {
     uint64_t m, n, k;
     int transpose_a, transpose_b;
     int gated;
+    // Prepared tensor-core forms of b / b2 (K-major tf32 hi, lo: [n, kp]); null = split per call.
+    const float* b_prep[2];
 };
 mg_status gemm(Device* d, const GemmArgs& g);
+// Round-up of k the tensor-core path stores operands with.
+inline uint64_t gemm_kp(uint64_t k) { return (k + 3) & ~3ull; }
+// Fills dst ([n, kp] hi then [n, kp] lo) with the K-major tf32 terms of B ([k, n] row-major,
+// or [n, k] when transposed).
+mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int transposed, float* dst);
+// Whether a matmul of these dimensions takes the tensor-core path (and so reads a prepared B).
+bool gemm_uses_tensor_cores(uint64_t m, uint64_t n, uint64_t k, int transpose_b, const float* b);
 
 struct AttentionArgs {
     const float* q;

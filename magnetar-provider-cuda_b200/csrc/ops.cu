@@ -114,6 +114,33 @@ mg_status half_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_b
 
 enum AddendMode { kNone = 0, kRow = 1, kFull = 2 };
 
+// The prepared tensor-core operand form of a weight read as matmul B, built on first use.
+mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int transposed, const float** out) {
+    *out = nullptr;
+    if (!cb || !cb->is_weight) return MG_OK;
+    Buffer* b = const_cast<Buffer*>(cb);  // the prepared form is a cache of the buffer's contents
+    if (b->prep && b->prep_n == n && b->prep_k == k && b->prep_transposed == transposed) {
+        *out = b->prep;
+        return MG_OK;
+    }
+    buffer_drop_prep(b);
+    const uint64_t kp = k::gemm_kp(k);
+    void* mem = nullptr;
+    MG_TRY(device_alloc(d, 2 * n * kp * sizeof(float), &mem));
+    mg_status s = k::gemm_prepare_b(d, (const float*)b->ptr, k, n, transposed, (float*)mem);
+    if (s != MG_OK) {
+        device_free(d, mem);
+        return s;
+    }
+    b->prep = (float*)mem;
+    b->prep_n = n;
+    b->prep_k = k;
+    b->prep_kp = kp;
+    b->prep_transposed = transposed;
+    *out = b->prep;
+    return MG_OK;
+}
+
 // src/kernels.rs:5518-5580: shapes, transposes and the addend's shape.
 mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, const mg_buffer* b2h,
                       const mg_buffer* addh, int addend_mode, int ta, int tb, mg_buffer** out) {
@@ -172,6 +199,11 @@ mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
     g.transpose_a = ta;
     g.transpose_b = tb;
     g.gated = b2 ? 1 : 0;
+    g.b_prep[0] = g.b_prep[1] = nullptr;
+    if (k::gemm_uses_tensor_cores(m, n, kk, tb, g.b)) {
+        MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0]));
+        if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1]));
+    }
     return k::gemm(d, g);
 }
 

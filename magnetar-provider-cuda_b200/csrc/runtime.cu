@@ -173,8 +173,16 @@ mg_status buffer_new(Device* d, mg_dtype dtype, int rank, const uint64_t* shape,
     return MG_OK;
 }
 
+void buffer_drop_prep(Buffer* b) {
+    if (b->prep) device_free(b->device, b->prep);
+    b->prep = nullptr;
+    b->prep_n = b->prep_k = b->prep_kp = 0;
+    b->prep_transposed = -1;
+}
+
 void buffer_free(Buffer* b) {
     if (!b) return;
+    buffer_drop_prep(b);
     if (b->owned && b->ptr) device_free(b->device, b->ptr);
     delete b;
 }
@@ -186,6 +194,8 @@ mg_status output_for(Device* d, mg_dtype dtype, int rank, const uint64_t* shape,
     if (!shape_count(rank, shape, &count)) return fail(MG_SHAPE_UNSUPPORTED, "output element count overflows");
     Buffer* o = buf(*out);
     if (o && o->device == d && o->dtype == dtype && o->count == count) {
+        buffer_drop_prep(o);  // its contents are about to change
+        o->is_weight = false;
         o->rank = rank;
         for (int i = 0; i < rank; i++) o->shape[i] = shape[i];
         *result = o;
@@ -409,6 +419,7 @@ mg_status mg_buffer_upload(mg_buffer* h, const void* host, uint64_t bytes) {
         return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes cannot fill a %s buffer of shape %s",
                     (unsigned long long)bytes, dtype_name(b->dtype), shape_str(b).c_str());
     MG_CUDA(cudaSetDevice(b->device->ordinal), "selecting the device");
+    buffer_drop_prep(b);
     if (bytes) MG_CUDA(cudaMemcpyAsync(b->ptr, host, bytes, cudaMemcpyHostToDevice, b->device->stream), "uploading");
     b->device->uploads.fetch_add(1);
     return MG_OK;
@@ -518,5 +529,16 @@ mg_status mg_buffer_reshape(mg_buffer* h, int rank, const uint64_t* shape) {
 }
 
 void* mg_buffer_device_ptr(const mg_buffer* h) { return h ? buf(h)->ptr : nullptr; }
+
+mg_status mg_buffer_set_weight(mg_buffer* h, int is_weight) {
+    if (!h) return fail(MG_INVALID_ARGUMENT, "null buffer");
+    Buffer* b = buf(h);
+    if (!is_weight) {
+        cudaSetDevice(b->device->ordinal);
+        buffer_drop_prep(b);
+    }
+    b->is_weight = is_weight != 0;
+    return MG_OK;
+}
 
 }  // extern "C"

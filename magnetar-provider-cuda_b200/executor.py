@@ -201,7 +201,17 @@ class CudaExecutor:
 
     def replay_steps(self, count: int) -> None:
         """``count`` replays back to back with one embedding-id check for all of them."""
+        if count < 1:
+            raise ValueError("count must be positive")
         check(N.lib().mg_executor_replay_steps(self._h, int(count)))
+
+    def launch_step(self) -> None:
+        """One replay without the embedding-id check (``check_steps`` checks later)."""
+        check(N.lib().mg_executor_launch_step(self._h))
+
+    def check_steps(self) -> None:
+        """Checks the embedding ids of every replay since the last check."""
+        check(N.lib().mg_executor_check_steps(self._h))
 
     def observations(self) -> Dict[str, int]:
         s, c, f = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
