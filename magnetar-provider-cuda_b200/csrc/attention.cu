@@ -191,7 +191,12 @@ __global__ void __launch_bounds__(256) attention_generic_kernel(AttnP p) {
 
 namespace k {
 
+bool attention_tc_eligible(const AttentionArgs& a);
+mg_status attention_tc(Device* d, const AttentionArgs& a);
+
 mg_status attention(Device* d, const AttentionArgs& a) {
+    if (a.seq_len == 0 || a.head_count == 0) return MG_OK;
+    if (attention_tc_eligible(a)) return attention_tc(d, a);
     AttnP p;
     p.q = a.q;
     p.k = a.k;

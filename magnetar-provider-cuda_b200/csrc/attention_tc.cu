@@ -1,0 +1,475 @@
+// Fused causal / windowed / GQA attention on the 5th-generation tensor cores.
+//
+// The reference's tensor-core prefill (`attention_tcp{,128}_kernel`, src/tensor_kernels.cu:
+// 755-1022) splits each f32 operand into bfloat16 hi + lo terms and forms
+// hi*hi + hi*lo + lo*hi for both S = Q K^T and O = P V.  This kernel keeps that precision model
+// on tcgen05:
+//   * a split pass writes Q and K as bf16 hi/lo (same layout) and V as bf16 hi/lo transposed
+//     per kv head ([kv_heads * D, keys]), so every MMA operand is K-major;
+//   * a CTA serves 128 queries of one head.  Warp 0 loads Q once and 64-key tiles of K and
+//     V^T with TMA; warp 1 issues the MMAs (S into TMEM columns [0, 64), P.V into [128, 128+D));
+//     warps 4-7 -- one TMEM lane quarter each, one query row per thread -- read S, apply the
+//     masks, run the online softmax, write P (normalised by the running sum) as bf16 hi/lo in
+//     the 128-byte-swizzled layout the MMA reads, and fold each tile's P.V into a register
+//     copy of the output.
+// The output is kept as a weighted MEAN of V rows at every step (O <- O * l_old*a/l_new +
+// (P/l_new) V), so it never exceeds the largest |v| -- the reference's overflow-safety
+// invariant for large finite V (src/tests_conformance.rs:884-914).  A query with no admitted
+// key outputs zeros.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace mg {
+namespace {
+
+using namespace sm100;
+
+constexpr int AQ = 128;   // queries per CTA (MMA M)
+constexpr int AKV = 64;   // keys per iteration (one 128-byte swizzle row of bf16)
+constexpr int kAttnTcThreads = 256;
+
+// ---- split pass -----------------------------------------------------------------------------
+__device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
+    __nv_bfloat16 h = __float2bfloat16_rn(x);
+    float hf = __bfloat162float(h);
+    if (isinf(hf) && !isinf(x)) {  // rounding overflowed a finite value: truncate instead
+        const uint16_t t = (uint16_t)(__float_as_uint(x) >> 16);
+        h = __ushort_as_bfloat16(t);
+        hf = __bfloat162float(h);
+    }
+    hi = __bfloat16_as_ushort(h);
+    lo = __bfloat16_as_ushort(__float2bfloat16_rn(x - hf));
+}
+
+// [rows, cols] f32 -> bf16 hi / lo in the same layout.
+__global__ void __launch_bounds__(256) split_bf16_rows_kernel(const float* __restrict__ src, uint16_t* __restrict__ hi,
+                                                              uint16_t* __restrict__ lo, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += stride) {
+        const float4 v = reinterpret_cast<const float4*>(src)[i];
+        uint16_t h[4], l[4];
+        split_bf16(v.x, h[0], l[0]);
+        split_bf16(v.y, h[1], l[1]);
+        split_bf16(v.z, h[2], l[2]);
+        split_bf16(v.w, h[3], l[3]);
+        reinterpret_cast<uint2*>(hi)[i] = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+        reinterpret_cast<uint2*>(lo)[i] = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+    }
+}
+
+// v [keys, width] f32 -> hi / lo [width, keys_p] bf16 (dst[c][r] = v[r][c]), zero past keys.
+__global__ void __launch_bounds__(256) split_bf16_transpose_kernel(const float* __restrict__ v, uint64_t keys,
+                                                                   uint64_t width, uint16_t* __restrict__ hi,
+                                                                   uint16_t* __restrict__ lo, uint64_t keys_p) {
+    __shared__ float tile[32][33];
+    const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
+    for (int j = ty; j < 32; j += 8) {
+        const uint64_t r = r0 + j, c = c0 + tx;
+        tile[j][tx] = (r < keys && c < width) ? v[r * width + c] : 0.0f;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        const uint64_t c = c0 + j, r = r0 + tx;
+        if (c < width && r < keys_p) {
+            uint16_t h, l;
+            split_bf16(tile[tx][j], h, l);
+            hi[c * keys_p + r] = h;
+            lo[c * keys_p + r] = l;
+        }
+    }
+}
+
+// ---- the attention kernel -----------------------------------------------------------------------
+struct AttnTcParams {
+    float* out;
+    uint64_t seq_len, kv_seq_len, group, out_dim;
+    int causal;
+    int64_t window;  // -1: none
+    uint64_t qpos0;  // position of query 0
+    float scale;
+    int q_tiles;
+    int* error;
+};
+
+template <int D>
+struct AttnShape {
+    static constexpr int kQAtom = AQ * 128;          // [128 rows][64 bf16]
+    static constexpr int kQ = (D / 64) * kQAtom;     // one term of the Q tile
+    static constexpr int kKAtom = AKV * 128;         // [64 keys][64 bf16]
+    static constexpr int kK = (D / 64) * kKAtom;     // one term of a K tile
+    static constexpr int kV = D * 128;               // one term of a V^T tile: [D][64 keys]
+    static constexpr int kP = AQ * 128;              // one term of P: [128][64 keys]
+    static constexpr int kOffQ = 0, kOffK = 2 * kQ, kOffV = kOffK + 2 * kK, kOffP = kOffV + 2 * kV;
+    static constexpr int kBytes = kOffP + 2 * kP;
+    static constexpr int kSmem = kBytes + 1024 + 256;
+    static constexpr uint32_t kTmemCols = 256;       // S: [0, 64), P.V: [128, 128 + D)
+    static constexpr uint32_t kColPV = 128;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAttnTcThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
+                        const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
+                        const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
+                        AttnTcParams p) {
+    using S = AttnShape<D>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t bars[8];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* base_ptr = smem_raw + (base - raw);
+    const uint32_t b0 = smem_u32(bars);
+    const uint32_t q_full = b0, k_full = b0 + 8, k_empty = b0 + 16, v_full = b0 + 24, v_empty = b0 + 32,
+                   s_full = b0 + 40, p_full = b0 + 48, pv_full = b0 + 56;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    // Heavy (late) query tiles first: causal tiles near the end see the most keys.
+    const int qt = p.q_tiles - 1 - (int)blockIdx.x;
+    const uint64_t head = blockIdx.y;
+    const uint64_t kvh = head / p.group;
+    const uint64_t q0 = (uint64_t)qt * AQ;
+    const uint64_t q_last = min(q0 + AQ, p.seq_len) - 1;
+    // Keys this tile can admit: [key_lo, key_hi).
+    uint64_t key_hi = p.causal ? min(p.kv_seq_len, p.qpos0 + q_last + 1) : p.kv_seq_len;
+    uint64_t key_lo = 0;
+    if (p.window >= 0) {
+        const uint64_t back = p.window > 0 ? (uint64_t)p.window - 1 : 0;
+        const uint64_t pos = p.qpos0 + q0;
+        key_lo = pos > back ? pos - back : 0;
+    }
+    const uint64_t kv0 = (key_lo / AKV) * AKV;
+    const int n_kv = key_hi > kv0 ? (int)((key_hi - kv0 + AKV - 1) / AKV) : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(k_full, 1);
+        mbar_init(k_empty, 1);
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 128);
+        mbar_init(pv_full, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tmem_slot), S::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer --------------------------------------------------------------------
+        if (lane == 0 && n_kv > 0) {
+            mbar_arrive_expect_tx(q_full, 2 * S::kQ);
+            for (int a = 0; a < D / 64; a++) {
+                tma_load_2d(base + S::kOffQ + a * S::kQAtom, &map_qhi, q_full, (int)(head * D + a * 64), (int)q0);
+                tma_load_2d(base + S::kOffQ + S::kQ + a * S::kQAtom, &map_qlo, q_full, (int)(head * D + a * 64), (int)q0);
+            }
+            for (int j = 0; j < n_kv; j++) {
+                const int key0 = (int)(kv0 + (uint64_t)j * AKV);
+                const uint32_t ph = (uint32_t)(j - 1) & 1u;
+                if (j > 0 && !mbar_wait(k_empty, ph)) {
+                    abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                mbar_arrive_expect_tx(k_full, 2 * S::kK);
+                for (int a = 0; a < D / 64; a++) {
+                    tma_load_2d(base + S::kOffK + a * S::kKAtom, &map_khi, k_full, (int)(kvh * D + a * 64), key0);
+                    tma_load_2d(base + S::kOffK + S::kK + a * S::kKAtom, &map_klo, k_full, (int)(kvh * D + a * 64), key0);
+                }
+                if (j > 0 && !mbar_wait(v_empty, ph)) {
+                    abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                mbar_arrive_expect_tx(v_full, 2 * S::kV);
+                tma_load_2d(base + S::kOffV, &map_vhi, v_full, key0, (int)(kvh * D));
+                tma_load_2d(base + S::kOffV + S::kV, &map_vlo, v_full, key0, (int)(kvh * D));
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- MMA issuer --------------------------------------------------------------------------
+        if (lane == 0 && n_kv > 0) {
+            constexpr uint32_t idesc_s = idesc_bf16(AQ, AKV);
+            constexpr uint32_t idesc_o = idesc_bf16(AQ, D);
+            const uint32_t tS = tmem, tO = tmem + S::kColPV;
+            bool ok = mbar_wait(q_full, 0);
+            for (int j = 0; j < n_kv && ok; j++) {
+                const uint32_t ph = (uint32_t)j & 1u;
+                if (!mbar_wait(k_full, ph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // S = Q K^T over D in steps of 16 (32 bytes of a 128-byte swizzle row)
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t off = (uint32_t)(kk % 4) * 32;
+                    const uint32_t qa = base + S::kOffQ + (kk / 4) * S::kQAtom + off;
+                    const uint32_t kb = base + S::kOffK + (kk / 4) * S::kKAtom + off;
+                    const uint64_t qhi = desc_k_sw128(qa), qlo = desc_k_sw128(qa + S::kQ);
+                    const uint64_t khi = desc_k_sw128(kb), klo = desc_k_sw128(kb + S::kK);
+                    mma_bf16(tS, qlo, khi, idesc_s, kk > 0 ? 1u : 0u);
+                    mma_bf16(tS, qhi, klo, idesc_s, 1u);
+                    mma_bf16(tS, qhi, khi, idesc_s, 1u);
+                }
+                tc_commit(k_empty);
+                tc_commit(s_full);
+                if (!mbar_wait(p_full, ph) || !mbar_wait(v_full, ph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // P.V over the tile's 64 keys in steps of 16
+#pragma unroll
+                for (int kk = 0; kk < AKV / 16; kk++) {
+                    const uint32_t off = (uint32_t)kk * 32;
+                    const uint32_t pa = base + S::kOffP + off;
+                    const uint32_t vb = base + S::kOffV + off;
+                    const uint64_t phi = desc_k_sw128(pa), plo = desc_k_sw128(pa + S::kP);
+                    const uint64_t vhi = desc_k_sw128(vb), vlo = desc_k_sw128(vb + S::kV);
+                    mma_bf16(tO, plo, vhi, idesc_o, kk > 0 ? 1u : 0u);
+                    mma_bf16(tO, phi, vlo, idesc_o, 1u);
+                    mma_bf16(tO, phi, vhi, idesc_o, 1u);
+                }
+                tc_commit(v_empty);
+                tc_commit(pv_full);
+            }
+            if (!ok) {
+                abort_flag = 1;
+                atomicExch(p.error, 1);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ---- softmax / output: one query row per thread ------------------------------------------
+        const int qq = warp % 4;
+        const int r = qq * 32 + lane;
+        const uint64_t qi = q0 + r;
+        const bool live = qi < p.seq_len;
+        const uint64_t qpos = p.qpos0 + qi;
+        const uint64_t row_hi = p.causal ? min(p.kv_seq_len, qpos + 1) : p.kv_seq_len;
+        uint64_t row_lo = 0;
+        if (p.window >= 0) {
+            const uint64_t back = p.window > 0 ? (uint64_t)p.window - 1 : 0;
+            row_lo = qpos > back ? qpos - back : 0;
+            if (row_lo > row_hi) row_lo = row_hi;
+        }
+        const uint32_t lane_base = tmem + ((uint32_t)(qq * 32) << 16);
+        float o[D];
+#pragma unroll
+        for (int d = 0; d < D; d++) o[d] = 0.0f;
+        float m = __int_as_float(0xff800000), l = 0.0f;
+        uint8_t* p_hi = base_ptr + S::kOffP + r * 128;
+        uint8_t* p_lo = p_hi + S::kP;
+        bool ok = true;
+        for (int j = 0; j < n_kv; j++) {
+            const uint32_t ph = (uint32_t)j & 1u;
+            const bool got = mbar_wait(s_full, ph);
+            if (!__all_sync(0xffffffffu, got && !abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[AKV];
+#pragma unroll
+            for (int c = 0; c < AKV; c += 16) tmem_ld16(lane_base + c, s + c);
+            tc_wait_ld();
+            const uint64_t key0 = kv0 + (uint64_t)j * AKV;
+            float tmax = __int_as_float(0xff800000);
+#pragma unroll
+            for (int c = 0; c < AKV; c++) {
+                const uint64_t key = key0 + c;
+                const bool valid = live && key >= row_lo && key < row_hi;
+                s[c] = valid ? s[c] * p.scale : __int_as_float(0xff800000);
+                tmax = fmaxf(tmax, s[c]);
+            }
+            const float m_new = fmaxf(m, tmax);
+            float alpha = 0.0f, psum = 0.0f;
+            if (m_new != __int_as_float(0xff800000)) {
+                alpha = m == __int_as_float(0xff800000) ? 0.0f : expf(m - m_new);
+#pragma unroll
+                for (int c = 0; c < AKV; c++) {
+                    s[c] = s[c] == __int_as_float(0xff800000) ? 0.0f : expf(s[c] - m_new);
+                    psum += s[c];
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < AKV; c++) s[c] = 0.0f;
+            }
+            const float l_new = l * alpha + psum;
+            const float inv = l_new > 0.0f ? 1.0f / l_new : 0.0f;
+            const float keep = l_new > 0.0f ? (l * alpha) * inv : 0.0f;
+            // P / l_new as bf16 hi / lo, 16-byte chunk c of row r at chunk (c ^ (r % 8)).
+#pragma unroll
+            for (int c = 0; c < AKV / 8; c++) {
+                uint16_t h[8], lo8[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) split_bf16(s[c * 8 + e] * inv, h[e], lo8[e]);
+                const int sw = (c ^ (r & 7)) * 16;
+                *reinterpret_cast<uint4*>(p_hi + sw) =
+                    make_uint4(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16),
+                               h[4] | ((uint32_t)h[5] << 16), h[6] | ((uint32_t)h[7] << 16));
+                *reinterpret_cast<uint4*>(p_lo + sw) =
+                    make_uint4(lo8[0] | ((uint32_t)lo8[1] << 16), lo8[2] | ((uint32_t)lo8[3] << 16),
+                               lo8[4] | ((uint32_t)lo8[5] << 16), lo8[6] | ((uint32_t)lo8[7] << 16));
+            }
+            fence_proxy_async();  // the P writes are read by tcgen05.mma
+            mbar_arrive(p_full);
+            const bool got_pv = mbar_wait(pv_full, ph);
+            if (!__all_sync(0xffffffffu, got_pv && !abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < D; c += 16) {
+                float pv[16];
+                tmem_ld16(lane_base + S::kColPV + c, pv);
+                tc_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; e++) o[c + e] = o[c + e] * keep + pv[e];
+            }
+            m = m_new;
+            l = l_new;
+        }
+        if (!ok) atomicExch(p.error, 1);
+        if (live) {
+            float* orow = p.out + qi * p.out_dim + head * D;
+#pragma unroll
+            for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::kTmemCols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// bf16 [rows, cols] (row stride ld elements), box [box_rows, 64] with 128-byte swizzle.
+mg_status bf16_map(CUtensorMap* map, const uint16_t* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+    auto fn = attn_encode_fn();
+    if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
+inline unsigned grid_for_n(const Device* d, uint64_t items) {
+    uint64_t want = (items + 255) / 256, cap = (uint64_t)d->sm_count * 8;
+    return (unsigned)(want < 1 ? 1 : want > cap ? cap : want);
+}
+
+template <int D>
+mg_status launch_attention_tc(Device* d, const k::AttentionArgs& a, const CUtensorMap* maps, int q_tiles) {
+    using S = AttnShape<D>;
+    static_assert(S::kSmem <= 227 * 1024, "shared memory budget");
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(attention_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+                "configuring the attention kernel");
+        configured[d->ordinal & 63] = true;
+    }
+    AttnTcParams p;
+    p.out = a.out;
+    p.seq_len = a.seq_len;
+    p.kv_seq_len = a.kv_seq_len;
+    p.group = a.head_count / a.kv_head_count;
+    p.out_dim = a.head_count * a.value_dim;
+    p.causal = a.causal;
+    p.window = a.window;
+    p.qpos0 = a.query_position_offset;
+    p.scale = a.scale;
+    p.q_tiles = q_tiles;
+    p.error = d->flags + 2;
+    dim3 grid((unsigned)q_tiles, (unsigned)a.head_count);
+    attention_tc_kernel<D><<<grid, kAttnTcThreads, S::kSmem, d->stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
+                                                                          maps[5], p);
+    return launched(d, "tensor-core attention launch");
+}
+
+}  // namespace
+
+namespace k {
+
+bool attention_tc_eligible(const AttentionArgs& a) {
+    const bool aligned = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                           reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out)) & 15) == 0;
+    return aligned && (a.head_dim == 64 || a.head_dim == 128) && a.value_dim == a.head_dim &&
+           a.q_model_dim == a.head_count * a.head_dim && a.kv_model_dim == a.kv_head_count * a.head_dim &&
+           a.v_model_dim == a.kv_model_dim && a.seq_len > 0 && a.kv_seq_len > 0 && a.head_count <= 65535 &&
+           a.kv_seq_len < (1ull << 31) && a.q_model_dim < (1ull << 31);
+}
+
+mg_status attention_tc(Device* d, const AttentionArgs& a) {
+    const uint64_t S = a.seq_len, Skv = a.kv_seq_len, qd = a.q_model_dim, kvd = a.kv_model_dim;
+    const uint64_t skv_p = (Skv + 7) & ~7ull;  // V^T rows are 16-byte multiples
+    const size_t q_elems = S * qd, k_elems = Skv * kvd, vt_elems = kvd * skv_p;
+    uint16_t* ws = nullptr;
+    MG_TRY(scratch(d, 4, 2 * (q_elems + k_elems + vt_elems) * sizeof(uint16_t), (void**)&ws));
+    uint16_t* qhi = ws;
+    uint16_t* qlo = qhi + q_elems;
+    uint16_t* khi = qlo + q_elems;
+    uint16_t* klo = khi + k_elems;
+    uint16_t* vhi = klo + k_elems;
+    uint16_t* vlo = vhi + vt_elems;
+    split_bf16_rows_kernel<<<grid_for_n(d, q_elems / 4), 256, 0, d->stream>>>(a.q, qhi, qlo, q_elems);
+    MG_TRY(launched(d, "attention split launch"));
+    split_bf16_rows_kernel<<<grid_for_n(d, k_elems / 4), 256, 0, d->stream>>>(a.k, khi, klo, k_elems);
+    MG_TRY(launched(d, "attention split launch"));
+    dim3 tg((unsigned)((kvd + 31) / 32), (unsigned)((skv_p + 31) / 32));
+    if (tg.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the split pass");
+    split_bf16_transpose_kernel<<<tg, 256, 0, d->stream>>>(a.v, Skv, kvd, vhi, vlo, skv_p);
+    MG_TRY(launched(d, "attention split launch"));
+    const int D = (int)a.head_dim;
+    CUtensorMap maps[6];
+    MG_TRY(bf16_map(&maps[0], qhi, S, qd, qd, AQ));
+    MG_TRY(bf16_map(&maps[1], qlo, S, qd, qd, AQ));
+    MG_TRY(bf16_map(&maps[2], khi, Skv, kvd, kvd, AKV));
+    MG_TRY(bf16_map(&maps[3], klo, Skv, kvd, kvd, AKV));
+    MG_TRY(bf16_map(&maps[4], vhi, kvd, Skv, skv_p, (uint32_t)D));
+    MG_TRY(bf16_map(&maps[5], vlo, kvd, Skv, skv_p, (uint32_t)D));
+    const int q_tiles = (int)((S + AQ - 1) / AQ);
+    if (D == 64) return launch_attention_tc<64>(d, a, maps, q_tiles);
+    return launch_attention_tc<128>(d, a, maps, q_tiles);
+}
+
+}  // namespace k
+}  // namespace mg

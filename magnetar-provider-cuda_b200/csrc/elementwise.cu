@@ -209,6 +209,27 @@ __device__ __forceinline__ uint32_t half_op(uint32_t a, uint32_t b) {
     return hencode<DT>(OP == 0 ? x + y : x * y);
 }
 
+// Two halves packed in 32 bits.  For f16 the packed hardware conversions do the work: the
+// decode is exact for every non-NaN pattern, a NaN input makes the f32 op return the
+// canonical NaN whatever its payload, and the RNE encode matches the reference for every
+// non-NaN result -- so only NaN results need the reference's encoding rule applied.
+template <int DT, int OP>
+__device__ __forceinline__ uint32_t half_op2(uint32_t a, uint32_t b) {
+    if constexpr (DT == MG_F16) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&a));
+        const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&b));
+        const float r0 = OP == 0 ? x.x + y.x : x.x * y.x;
+        const float r1 = OP == 0 ? x.y + y.y : x.y * y.y;
+        const __half2 h = __floats2half2_rn(r0, r1);
+        uint32_t bits = *reinterpret_cast<const uint32_t*>(&h);
+        if (r0 != r0) bits = (bits & 0xFFFF0000u) | f16_encode(r0);
+        if (r1 != r1) bits = (bits & 0x0000FFFFu) | (f16_encode(r1) << 16);
+        return bits;
+    } else {
+        return half_op<DT, OP>(a & 0xFFFFu, b & 0xFFFFu) | (half_op<DT, OP>(a >> 16, b >> 16) << 16);
+    }
+}
+
 // src/kernels.cu:2913-2939 over 8 halves per 16-byte access.
 template <int DT, int OP>
 __global__ void __launch_bounds__(kThreads) half_binary_kernel(const uint16_t* __restrict__ a,
@@ -237,11 +258,7 @@ __global__ void __launch_bounds__(kThreads) half_binary_kernel(const uint16_t* _
                 uint4 r;
                 uint32_t* rs = &r.x;
 #pragma unroll
-                for (int w = 0; w < 4; w++) {
-                    uint32_t lo = half_op<DT, OP>(xs[w] & 0xFFFFu, ys[w] & 0xFFFFu);
-                    uint32_t hi = half_op<DT, OP>(xs[w] >> 16, ys[w] >> 16);
-                    rs[w] = lo | (hi << 16);
-                }
+                for (int w = 0; w < 4; w++) rs[w] = half_op2<DT, OP>(xs[w], ys[w]);
                 o8[i + u * stride] = r;
             }
         }

@@ -13,14 +13,15 @@
 //   warp 0      TMA producer: 32-column k-blocks (one 128-byte swizzle row per tile row) of
 //               A and B into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM and issues the MMAs (one thread), committing each stage back;
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator, bias / residual / SwiGLU, store --
-//               or, when k is split across CTAs, the raw partial tile to a workspace that a
-//               fixed-order reduction kernel finishes;
+//   warps 2-5   stage the accumulator (tcgen05.ld) in the drained shared-memory ring;
 //   warps 6-9   (when A arrives as raw f32) split each A tile into its hi/lo terms in shared
 //               memory, in place, so no separate pass over A is needed.
+// When the output grid alone would leave SMs idle, k is split across the CTAs of a thread-block
+// cluster; the cluster then reduces its staged partial tiles through distributed shared memory
+// and every thread writes finished rows (bias / residual / SwiGLU applied) with coalesced stores.
 // B comes either from a weight's prepared hi/lo form (built once, kept with the weight) or
-// from a per-call split pass that also transposes it to K-major.  Small output grids (the
-// decoder layer's M = 128) use narrower tiles and split k so that every SM has work.
+// from a per-call split pass that also transposes it to K-major.
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -45,6 +46,7 @@ using namespace sm100;
 constexpr int BM = 128;
 constexpr int BK = 32;       // f32 k-columns per stage: one 128-byte swizzle row
 constexpr int kGroupM = 16;  // rasterisation: M-tiles walked together for L2 reuse
+constexpr int kMaxSplits = 8;  // k splits of one tile: the CTAs of one portable cluster
 
 // ---- operand split ----------------------------------------------------------------------------
 __device__ __forceinline__ float tf32_round(float x) {
@@ -127,8 +129,7 @@ struct TcParams {
     uint64_t m, n, k;
     int tiles_m, tiles_n;
     int kb_per_split;  // k-blocks each CTA of a split handles
-    int splits;
-    float* partial;    // split-k workspace [NB][splits][m][n] (splits > 1)
+    int splits;        // CTAs per cluster (blockIdx.y), each over its own range of k
     int* error;        // device word set when a wait times out
 };
 
@@ -138,12 +139,21 @@ struct TcShape {
     static constexpr int kBTile = BN * BK * 4;  // bytes of one B term tile
     static constexpr int kStage = 2 * kATile + NB * 2 * kBTile;
     static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + NB * 2 * kBTile;  // TMA bytes per stage
+    static constexpr int kLd = BN + 4;                                            // staged tile row stride
+    static constexpr int kStageTile = BM * kLd * 4;                               // bytes of one staged tile
+    static_assert(NB * kStageTile <= STAGES * kStage, "the staged output fits the drained ring");
     static constexpr int kSmem = STAGES * kStage + 1024 /* align */ + 512 /* barriers */;
     static constexpr uint32_t kTmemCols =
         NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
     static constexpr int kThreads = A_RAW ? 320 : 192;
 };
 
+// The CTAs of one output tile form a cluster along blockIdx.y, each multiplying its own range
+// of k.  After the main loop every CTA stages its f32 accumulator in its own (drained) shared
+// memory; then each CTA sums one band of rows across the cluster's staged tiles through
+// distributed shared memory, in cluster-rank order, and writes the finished band with
+// coalesced stores (bias / residual / SwiGLU applied).  One kernel, deterministic, and the
+// partial sums never leave the chip.
 template <int BN, int NB, int STAGES, bool A_RAW>
 __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
@@ -178,7 +188,23 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
     const int m0 = tm * BM, n0 = tn * BN;
     const int num_kb_total = (int)((p.k + BK - 1) / BK);
     const int kb0 = blockIdx.y * p.kb_per_split;
-    const int num_kb = min(num_kb_total, kb0 + p.kb_per_split) - kb0;
+    const int num_kb = max(0, min(num_kb_total, kb0 + p.kb_per_split) - kb0);
+
+    // TMA loads of one stage (the producer's job).
+    auto issue = [&](int i) {
+        const int s = i % STAGES;
+        const uint32_t st = base + s * S::kStage;
+        mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
+        const int kx = (kb0 + i) * BK;
+        tma_load_2d(st, &map_a0, full_bar(s), kx, m0);
+        if (!A_RAW) tma_load_2d(st + S::kATile, &map_a1, full_bar(s), kx, m0);
+        tma_load_2d(st + 2 * S::kATile, &map_bhi, full_bar(s), kx, n0);
+        tma_load_2d(st + 2 * S::kATile + S::kBTile, &map_blo, full_bar(s), kx, n0);
+        if (NB == 2) {
+            tma_load_2d(st + 2 * S::kATile + 2 * S::kBTile, &map_b2hi, full_bar(s), kx, n0);
+            tma_load_2d(st + 2 * S::kATile + 3 * S::kBTile, &map_b2lo, full_bar(s), kx, n0);
+        }
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -189,16 +215,9 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
         mbar_init(accum_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
-    }
-    if (warp == 0 && lane == 0) {
-        prefetch_tensormap(&map_a0);
-        if (!A_RAW) prefetch_tensormap(&map_a1);
-        prefetch_tensormap(&map_bhi);
-        prefetch_tensormap(&map_blo);
-        if (NB == 2) {
-            prefetch_tensormap(&map_b2hi);
-            prefetch_tensormap(&map_b2lo);
-        }
+        // The first stages are free: start their loads before the set-up barrier so that the
+        // memory latency overlaps TMEM allocation.
+        for (int i = 0; i < min(STAGES, num_kb); i++) issue(i);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32((const void*)tmem_slot), S::kTmemCols);
@@ -208,11 +227,12 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    float* staged = reinterpret_cast<float*>(base_ptr);  // [NB][BM][kLd] once the ring has drained
 
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------------
         if (lane == 0) {
-            for (int i = 0; i < num_kb; i++) {
+            for (int i = STAGES; i < num_kb; i++) {
                 const int s = i % STAGES;
                 const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
                 if (!mbar_wait(empty_bar(s), phase ^ 1u)) {
@@ -221,17 +241,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
                     break;
                 }
                 if (*abort_flag) break;
-                const uint32_t st = base + s * S::kStage;
-                mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
-                const int kx = (kb0 + i) * BK;
-                tma_load_2d(st, &map_a0, full_bar(s), kx, m0);
-                if (!A_RAW) tma_load_2d(st + S::kATile, &map_a1, full_bar(s), kx, m0);
-                tma_load_2d(st + 2 * S::kATile, &map_bhi, full_bar(s), kx, n0);
-                tma_load_2d(st + 2 * S::kATile + S::kBTile, &map_blo, full_bar(s), kx, n0);
-                if (NB == 2) {
-                    tma_load_2d(st + 2 * S::kATile + 2 * S::kBTile, &map_b2hi, full_bar(s), kx, n0);
-                    tma_load_2d(st + 2 * S::kATile + 3 * S::kBTile, &map_b2lo, full_bar(s), kx, n0);
-                }
+                issue(i);
             }
         }
         __syncwarp();
@@ -272,7 +282,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
                 }
                 tc_commit(empty_bar(s));  // frees the stage once these MMAs have read it
             }
-            if (ok) tc_commit(accum_bar);
+            if (ok && num_kb > 0) tc_commit(accum_bar);
             else mbar_arrive(accum_bar);  // release the epilogue
         }
         __syncwarp();
@@ -304,101 +314,101 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
             }
         }
     } else {
-        // ---- epilogue: warps 2..5 own TMEM lane quarters (warp % 4) ----------------------
+        // ---- epilogue, part 1: warps 2..5 stage their TMEM lane quarter (warp % 4) ------
         const int q = warp % 4;
         const bool waited = mbar_wait(accum_bar, 0);
         if (!waited) atomicExch(p.error, 1);
         tc_fence_after();
         // tcgen05.ld is warp-collective: the whole warp reads the accumulator or none of it.
-        const bool ready = __all_sync(0xffffffffu, waited && !*abort_flag);
-        if (ready) {
-            const uint64_t row = (uint64_t)m0 + q * 32 + lane;
-            const bool row_ok = row < p.m;
-            const bool direct = p.splits == 1;
-            const bool vec = (p.n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
-                             (p.addend_mode != 2 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0) &&
-                             (p.addend_mode != 1 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0) &&
-                             (direct || (reinterpret_cast<uintptr_t>(p.partial) & 15) == 0);
+        const bool ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_kb > 0);
+        const int r = q * 32 + lane;  // this thread's row of the tile
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+#pragma unroll
+            for (int z = 0; z < NB; z++) {
                 float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-                float u[32];
-                if (NB == 2) tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), u);
-                tc_wait_ld();
-                if (!row_ok) continue;
-                const uint64_t col0 = (uint64_t)n0 + c0;
-                if (!direct) {
-                    // raw partial sums of this k split; the reduction applies addend / gate
-#pragma unroll
-                    for (int z = 0; z < NB; z++) {
-                        const float* src = z ? u : v;
-                        float* dst = p.partial + (((uint64_t)z * p.splits + blockIdx.y) * p.m + row) * p.n;
-                        if (vec && col0 + 32 <= p.n) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(dst + col0 + j) =
-                                    make_float4(src[j], src[j + 1], src[j + 2], src[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                if (col0 + j < p.n) dst[col0 + j] = src[j];
-                        }
-                    }
-                    continue;
-                }
-                float* orow = p.out + row * p.n;
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    float s = v[j];
-                    if (NB == 2) {
-                        s = (s * (1.0f / (1.0f + expf(-s)))) * u[j];
-                    } else if (p.addend_mode == 1) {
-                        if (col0 + j < p.n) s += p.addend[col0 + j];
-                    } else if (p.addend_mode == 2) {
-                        if (col0 + j < p.n) s += p.addend[row * p.n + col0 + j];
-                    }
-                    v[j] = s;
-                }
-                if (vec && col0 + 32 <= p.n) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(orow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                if (ready) {
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(z * BN + c0), v);
+                    tc_wait_ld();
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (col0 + j < p.n) orow[col0 + j] = v[j];
+                    for (int j = 0; j < 32; j++) v[j] = 0.0f;
                 }
+                float* dst = staged + (size_t)z * BM * S::kLd + (size_t)r * S::kLd + c0;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             }
         }
     }
 
+    // ---- epilogue, part 2: every thread of the cluster reduces one band of rows ----------
+    cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
     tc_fence_before();
     __syncthreads();
+    cluster.sync();  // every CTA of the tile has staged its partial tile
+    {
+        const int splits = (int)cluster.num_blocks();
+        const int rank = (int)cluster.block_rank();
+        const float* src[8][NB];
+#pragma unroll
+        for (int s = 0; s < 8; s++)
+#pragma unroll
+            for (int z = 0; z < NB; z++)
+                src[s][z] = s < splits ? cluster.map_shared_rank(staged + (size_t)z * BM * S::kLd, (unsigned)s) : nullptr;
+        const int band = (BM + splits - 1) / splits;
+        const int r_begin = rank * band, r_end = min(BM, r_begin + band);
+        constexpr int kVec = BN / 4;  // float4 per row
+        const bool vec = (p.n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
+                         (p.addend_mode == 0 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0);
+        for (int e = threadIdx.x; e < (r_end - r_begin) * kVec; e += blockDim.x) {
+            const int lr = r_begin + e / kVec, c4 = (e % kVec) * 4;
+            const uint64_t row = (uint64_t)m0 + lr, col = (uint64_t)n0 + c4;
+            if (row >= p.m || col >= p.n) continue;
+            float4 acc[NB];
+#pragma unroll
+            for (int z = 0; z < NB; z++) {
+                acc[z] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s = 0; s < splits; s++) {
+                    const float4 t = *reinterpret_cast<const float4*>(src[s][z] + (size_t)lr * S::kLd + c4);
+                    acc[z].x += t.x;
+                    acc[z].y += t.y;
+                    acc[z].z += t.z;
+                    acc[z].w += t.w;
+                }
+            }
+            float o[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+            if (NB == 2) {
+                const float u[4] = {acc[NB - 1].x, acc[NB - 1].y, acc[NB - 1].z, acc[NB - 1].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) o[j] = (o[j] * (1.0f / (1.0f + expf(-o[j])))) * u[j];
+            }
+            float* orow = p.out + row * p.n;
+            if (vec && col + 4 <= p.n) {
+                if (p.addend_mode == 1) {
+                    const float4 b = *reinterpret_cast<const float4*>(p.addend + col);
+                    o[0] += b.x, o[1] += b.y, o[2] += b.z, o[3] += b.w;
+                } else if (p.addend_mode == 2) {
+                    const float4 b = *reinterpret_cast<const float4*>(p.addend + row * p.n + col);
+                    o[0] += b.x, o[1] += b.y, o[2] += b.z, o[3] += b.w;
+                }
+                *reinterpret_cast<float4*>(orow + col) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (col + j >= p.n) break;
+                    float s = o[j];
+                    if (p.addend_mode == 1) s += p.addend[col + j];
+                    else if (p.addend_mode == 2) s += p.addend[row * p.n + col + j];
+                    orow[col + j] = s;
+                }
+            }
+        }
+    }
+    cluster.sync();  // the peers have finished reading this CTA's staged tile
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, S::kTmemCols);
-    }
-}
-
-// Split-k finish: out = sum over splits in split order [+ addend] (or silu(gate) * up).
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, float* __restrict__ out,
-                                                            uint64_t m, uint64_t n, int splits, int gated,
-                                                            const float* __restrict__ addend, int addend_mode) {
-    const uint64_t total = m * n;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-        float s = 0.0f;
-        for (int z = 0; z < splits; z++) s += partial[(uint64_t)z * total + i];
-        if (gated) {
-            float u = 0.0f;
-            for (int z = 0; z < splits; z++) u += partial[(uint64_t)(splits + z) * total + i];
-            s = (s * (1.0f / (1.0f + expf(-s)))) * u;
-        } else if (addend_mode == 1) {
-            s += addend[i % n];
-        } else if (addend_mode == 2) {
-            s += addend[i];
-        }
-        out[i] = s;
     }
 }
 
@@ -466,9 +476,21 @@ mg_status launch_tc(Device* d, const TcParams& p, const CUtensorMap* maps) {
     }
     const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
     if (tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "matmul has too many output tiles");
-    dim3 grid((unsigned)tiles, (unsigned)p.splits);
-    gemm_tc_kernel<BN, NB, STAGES, A_RAW><<<grid, S::kThreads, S::kSmem, d->stream>>>(maps[0], maps[1], maps[2], maps[3],
-                                                                                      maps[4], maps[5], p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits, 1);
+    cfg.blockDim = dim3(S::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)p.splits;  // the k splits of one tile share a cluster
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, NB, STAGES, A_RAW>, maps[0], maps[1], maps[2], maps[3], maps[4],
+                               maps[5], p),
+            "tensor-core matmul launch");
     return launched(d, "tensor-core matmul launch");
 }
 
@@ -494,13 +516,15 @@ bool tensor_cores_enabled() {
     return enabled == 1;
 }
 
-// Output tile width: the widest of 128 / 64 / 32 columns that still gives every SM a tile,
-// so that small matmuls (the decoder layer's M = 128) spread over more CTAs.
+// Output tile width.  Narrow MMAs cost about as much issue time as wide ones (measured: a
+// 128 x 32 tile spends ~1.5 us per k-block, a 128 x 128 tile ~0.6 us), so tiles stay 128 wide
+// and small output grids get their parallelism from splitting k; only a narrow n narrows them.
 int pick_bn(const Device* d, uint64_t m, uint64_t n) {
-    const uint64_t tm = (m + BM - 1) / BM;
-    if (tm * ((n + 127) / 128) >= (uint64_t)d->sm_count) return 128;
-    if (tm * ((n + 63) / 64) >= (uint64_t)d->sm_count) return 64;
-    return 32;
+    (void)d;
+    (void)m;
+    if (n <= 32) return 32;
+    if (n <= 64) return 64;
+    return 128;
 }
 
 }  // namespace
@@ -552,20 +576,18 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
     p.tiles_m = (int)((g.m + BM - 1) / BM);
     p.tiles_n = (int)((g.n + bn - 1) / bn);
     p.error = d->flags + 2;
-    // Split k when the output grid leaves SMs idle, keeping at least 4 k-blocks per split.
+    // Split k when the output grid leaves SMs idle, keeping at least 2 k-blocks per split.
     const int num_kb = (int)((g.k + BK - 1) / BK);
     const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
     int splits = 1;
-    if (tiles < (uint64_t)d->sm_count && num_kb >= 8) {
+    if (tiles < (uint64_t)d->sm_count && num_kb >= 4) {
         splits = (int)((d->sm_count + tiles - 1) / tiles);
-        if (splits > num_kb / 4) splits = num_kb / 4;
+        if (splits > num_kb / 2) splits = num_kb / 2;
+        if (splits > kMaxSplits) splits = kMaxSplits;  // a portable cluster holds 8 CTAs
         if (splits < 1) splits = 1;
     }
     p.kb_per_split = (num_kb + splits - 1) / splits;
     p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
-    p.partial = nullptr;
-    if (p.splits > 1)
-        MG_TRY(scratch(d, 3, (size_t)nb * p.splits * g.m * g.n * sizeof(float), (void**)&p.partial));
     CUtensorMap maps[6];
     if (a_raw) {
         MG_TRY(make_map(&maps[0], ahi, g.m, g.k, g.k, BM));
@@ -587,11 +609,6 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
     if (nb == 2) s = a_raw ? launch_bn<2, true>(d, bn, p, maps) : launch_bn<2, false>(d, bn, p, maps);
     else s = a_raw ? launch_bn<1, true>(d, bn, p, maps) : launch_bn<1, false>(d, bn, p, maps);
     MG_TRY(s);
-    if (p.splits > 1) {
-        splitk_reduce_kernel<<<grid_cap(d, g.m * g.n), 256, 0, d->stream>>>(p.partial, g.out, g.m, g.n, p.splits, nb == 2,
-                                                                           g.addend, g.addend_mode);
-        MG_TRY(launched(d, "split-k reduction launch"));
-    }
     return MG_OK;
 }
 

@@ -168,26 +168,43 @@ void launch_partial(Device* d, dim3 grid, size_t smem, const k::GemmArgs& g, flo
 constexpr int kChunkRows = 32;
 constexpr int kStages = 6;
 constexpr int kChunkBytes = kChunkRows * kCols * 4;
+constexpr uint64_t kMaxCounterTiles = 1u << 16;  // Device::counters entries
 
+struct GemvTmaArgs {
+    const float* a;
+    float* partial;  // [zs][slices][m][n]
+    float* out;
+    const float* addend;
+    int addend_mode;
+    int gated;
+    uint64_t m, n, k, slice_len;
+    int transpose_a;
+    int* error;
+    unsigned int* counters;  // per column tile; zero between calls (the last CTA resets it)
+};
+
+// Warps 0-7 compute; warp 8 is the TMA producer.  The last CTA to finish a column tile sums
+// that tile's partials over the slices (in slice order) and writes the output, so no second
+// kernel is needed.
 template <int M>
-__global__ void __launch_bounds__(kWarps * 32) gemv_tma_kernel(const __grid_constant__ CUtensorMap map_b,
-                                                                const __grid_constant__ CUtensorMap map_b2,
-                                                                const float* __restrict__ a, float* __restrict__ partial,
-                                                                uint64_t m, uint64_t n, uint64_t k, uint64_t slice_len,
-                                                                int transpose_a, int* error) {
+__global__ void __launch_bounds__((kWarps + 1) * 32) gemv_tma_kernel(const __grid_constant__ CUtensorMap map_b,
+                                                                      const __grid_constant__ CUtensorMap map_b2,
+                                                                      GemvTmaArgs p) {
     extern __shared__ uint8_t smem_raw[];
     using namespace sm100;
+    __shared__ unsigned int s_last;
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 127u) & ~127u;
     uint8_t* base_ptr = smem_raw + (base - raw);
     float* ring = reinterpret_cast<float*>(base_ptr);                        // [kStages][32][128]
     float* a_s = ring + kStages * kChunkRows * kCols;                          // [M][slice_len]
-    float* red = a_s + M * slice_len;                                          // [kWarps][kCols]
+    float* red = a_s + M * p.slice_len;                                        // [kWarps][kCols]
     uint64_t* bars = reinterpret_cast<uint64_t*>(red + kWarps * kCols);        // full[kStages], empty[kStages]
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t m = p.m, n = p.n, k = p.k, slice_len = p.slice_len;
     const uint64_t col0 = (uint64_t)blockIdx.x * kCols;
     const uint64_t slice = blockIdx.y;
     const uint64_t k0 = slice * slice_len;
@@ -206,74 +223,69 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_tma_kernel(const __grid_cons
     for (uint64_t i = threadIdx.x; i < (uint64_t)M * slice_len; i += blockDim.x) {
         const uint64_t r = i / slice_len, kk = k0 + i % slice_len;
         float v = 0.0f;
-        if (r < m && kk < k1) v = transpose_a ? a[kk * m + r] : a[r * k + kk];
+        if (r < m && kk < k1) v = p.transpose_a ? p.a[kk * m + r] : p.a[r * k + kk];
         a_s[i] = v;
     }
     __syncthreads();
-    // The producer keeps kStages tiles in flight; it is lane 0 of warp 0, which also computes.
-    int issued = 0;
-    auto issue = [&](int c) {
-        const int s = c % kStages;
-        mbar_arrive_expect_tx(full_bar(s), kChunkBytes);
-        tma_load_2d(base + (uint32_t)(s * kChunkBytes), map, full_bar(s), (int)col0, (int)(k0 + (uint64_t)c * kChunkRows));
-    };
-    if (threadIdx.x == 0) {
-        prefetch_tensormap(map);
-        for (; issued < min(chunks, kStages); issued++) issue(issued);
-    }
 
     float acc[M][4];
 #pragma unroll
     for (int r = 0; r < M; r++) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
-    bool ok = true;
-    for (int c = 0; c < chunks; c++) {
-        const int s = c % kStages;
-        const uint32_t phase = (uint32_t)(c / kStages) & 1u;
-        if (!mbar_wait(full_bar(s), phase)) {
-            ok = false;
-            atomicExch(error, 1);
-            break;
-        }
-        const float* tile = ring + s * kChunkRows * kCols;
-        const int rr = warp * 4;  // this warp's 4 rows of the tile
-        float4 bv[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) bv[u] = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
-        const uint64_t kl = (uint64_t)c * kChunkRows + rr;  // row within the slice (multiple of 4)
-#pragma unroll
-        for (int r = 0; r < M; r++) {
-            const float4 av = *reinterpret_cast<const float4*>(a_s + r * slice_len + kl);
-            const float aa[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                acc[r][0] += aa[u] * bv[u].x;
-                acc[r][1] += aa[u] * bv[u].y;
-                acc[r][2] += aa[u] * bv[u].z;
-                acc[r][3] += aa[u] * bv[u].w;
+    if (warp == kWarps) {
+        // ---- producer: keep the ring full -------------------------------------------------
+        if (lane == 0) {
+            prefetch_tensormap(map);
+            for (int c = 0; c < chunks; c++) {
+                const int s = c % kStages;
+                if (c >= kStages && !mbar_wait(empty_bar(s), (uint32_t)(c / kStages - 1) & 1u)) {
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                mbar_arrive_expect_tx(full_bar(s), kChunkBytes);
+                tma_load_2d(base + (uint32_t)(s * kChunkBytes), map, full_bar(s), (int)col0,
+                            (int)(k0 + (uint64_t)c * kChunkRows));
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(s));
-        if (threadIdx.x == 0 && issued < chunks) {
-            // refill the stage just drained once every warp has released it
-            const int rs = issued % kStages;
-            const uint32_t rphase = (uint32_t)(issued / kStages - 1) & 1u;
-            if (!mbar_wait(empty_bar(rs), rphase)) {
-                atomicExch(error, 1);
-            } else {
-                issue(issued);
+    } else {
+        for (int c = 0; c < chunks; c++) {
+            const int s = c % kStages;
+            const uint32_t phase = (uint32_t)(c / kStages) & 1u;
+            if (!mbar_wait(full_bar(s), phase)) {
+                atomicExch(p.error, 1);
+                break;
             }
-            issued++;
+            const float* tile = ring + s * kChunkRows * kCols;
+            const int rr = warp * 4;  // this warp's 4 rows of the tile
+            float4 bv[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) bv[u] = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));  // the stage's data is in registers
+            const uint64_t kl = (uint64_t)c * kChunkRows + rr;  // row within the slice (multiple of 4)
+#pragma unroll
+            for (int r = 0; r < M; r++) {
+                const float4 av = *reinterpret_cast<const float4*>(a_s + r * slice_len + kl);
+                const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    acc[r][0] += aa[u] * bv[u].x;
+                    acc[r][1] += aa[u] * bv[u].y;
+                    acc[r][2] += aa[u] * bv[u].z;
+                    acc[r][3] += aa[u] * bv[u].w;
+                }
+            }
         }
     }
-    (void)ok;
     // Fixed-order combine of the warps, one output row at a time.
-    float* out_base = partial + ((uint64_t)blockIdx.z * gridDim.y + slice) * m * n;
+    float* out_base = p.partial + ((uint64_t)blockIdx.z * gridDim.y + slice) * m * n;
 #pragma unroll
     for (int r = 0; r < M; r++) {
         if (r >= (int)m) break;
         __syncthreads();
-        *reinterpret_cast<float4*>(&red[warp * kCols + 4 * lane]) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        if (warp < kWarps)
+            *reinterpret_cast<float4*>(&red[warp * kCols + 4 * lane]) =
+                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
         __syncthreads();
         if (threadIdx.x < kCols) {
             float sum = 0.0f;
@@ -283,6 +295,36 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_tma_kernel(const __grid_cons
             if (cidx < n) out_base[r * n + cidx] = sum;
         }
     }
+    // The last CTA of this column tile (over slices and gate/up) finishes it.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int total = gridDim.y * gridDim.z;
+        s_last = atomicAdd(&p.counters[blockIdx.x], 1u) == total - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const uint64_t slices = gridDim.y;
+    const uint64_t mn = m * n;
+    for (uint64_t i = threadIdx.x; i < m * kCols; i += blockDim.x) {
+        const uint64_t r = i / kCols, cidx = col0 + i % kCols;
+        if (cidx >= n) continue;
+        const uint64_t off = r * n + cidx;
+        float s = 0.0f;
+        for (uint64_t sl = 0; sl < slices; sl++) s += __ldcg(p.partial + sl * mn + off);
+        if (p.gated) {
+            float u = 0.0f;
+            for (uint64_t sl = 0; sl < slices; sl++) u += __ldcg(p.partial + (slices + sl) * mn + off);
+            s = (s * (1.0f / (1.0f + expf(-s)))) * u;
+        } else if (p.addend_mode == 1) {
+            s += p.addend[cidx];
+        } else if (p.addend_mode == 2) {
+            s += p.addend[off];
+        }
+        p.out[off] = s;
+    }
+    if (threadIdx.x == 0) p.counters[blockIdx.x] = 0u;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 gemv_encode_fn() {
@@ -332,8 +374,21 @@ mg_status launch_tma(Device* d, dim3 grid, size_t smem, const CUtensorMap* maps,
                 "configuring the gemv kernel");
         configured[d->ordinal & 63] = true;
     }
-    gemv_tma_kernel<M><<<grid, kWarps * 32, smem, d->stream>>>(maps[0], maps[1], g.a, partial, g.m, g.n, g.k, slice_len,
-                                                                g.transpose_a, d->flags + 2);
+    GemvTmaArgs p;
+    p.a = g.a;
+    p.partial = partial;
+    p.out = g.out;
+    p.addend = g.addend;
+    p.addend_mode = g.addend_mode;
+    p.gated = g.gated;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.slice_len = slice_len;
+    p.transpose_a = g.transpose_a;
+    p.error = d->flags + 2;
+    p.counters = d->counters;
+    gemv_tma_kernel<M><<<grid, (kWarps + 1) * 32, smem, d->stream>>>(maps[0], maps[1], p);
     return launched(d, "gemv kernel launch");
 }
 
@@ -344,7 +399,9 @@ mg_status gemv_tma(Device* d, const GemmArgs& g) {
     const int zs = g.gated ? 2 : 1;
     const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
     const uint64_t max_slice = (uint64_t)(8192 / mp) / kChunkRows * kChunkRows;  // A's slice <= 32 KB
-    uint64_t slices = ((uint64_t)d->sm_count * 2 / zs + col_tiles - 1) / col_tiles;
+    if (col_tiles > kMaxCounterTiles) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
+    // One wave: at most two CTAs per SM over all column tiles and slices.
+    uint64_t slices = (uint64_t)d->sm_count * 2 / zs / col_tiles;
     if (slices < 1) slices = 1;
     uint64_t slice_len = (g.k + slices - 1) / slices;
     slice_len = ((slice_len + kChunkRows - 1) / kChunkRows) * kChunkRows;
@@ -367,12 +424,7 @@ mg_status gemv_tma(Device* d, const GemmArgs& g) {
         case 8: MG_TRY(launch_tma<8>(d, grid, smem, maps, g, partial, slice_len)); break;
         default: MG_TRY(launch_tma<16>(d, grid, smem, maps, g, partial, slice_len)); break;
     }
-    const uint64_t total = g.m * g.n;
-    uint64_t blocks = (total + 255) / 256;
-    if (blocks > (uint64_t)d->sm_count * 8) blocks = (uint64_t)d->sm_count * 8;
-    gemv_reduce_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, d->stream>>>(partial, g.out, g.m, g.n, slices,
-                                                                              g.addend, g.addend_mode, g.gated);
-    return launched(d, "gemv reduce kernel launch");
+    return MG_OK;
 }
 
 mg_status gemv(Device* d, const GemmArgs& g) {

@@ -48,6 +48,9 @@ struct Device {
     // [1] non-finite softmax row.  Pinned host mirror for the read back.
     int* flags = nullptr;
     int* host_flags = nullptr;
+    // Arrival counters of kernels whose last CTA finishes a tile (65,536 entries, zero
+    // between kernels: the finishing CTA resets its entry).
+    unsigned int* counters = nullptr;
     bool capturing = false;
     // Workspaces grown on demand (see scratch()); freed in stream order.
     void* scratch_ptr[8] = {nullptr};

@@ -243,6 +243,55 @@ __global__ void __launch_bounds__(256) rope_kernel(const float* __restrict__ x, 
     }
 }
 
+// A warp per row for 16-byte-aligned rows: lane j owns float4 column j (and j + 32, ...) of
+// every head, evaluates the rotation of that float4's pairs once for the row, and applies it
+// to the same float4 of all heads -- each head's 32 float4 form one coalesced 512-byte access.
+__global__ void __launch_bounds__(256) rope_warp_kernel(const float* __restrict__ x, float* __restrict__ out, RopeK p) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * 8;
+    const uint64_t hw4 = p.head_width >> 2;
+    for (uint64_t row = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < p.rows; row += warps) {
+        const float4* in = reinterpret_cast<const float4*>(x + row * p.cols);
+        float4* o = reinterpret_cast<float4*>(out + row * p.cols);
+        for (uint64_t q = lane; q < hw4; q += 32) {
+            const uint64_t col = q << 2;
+            if (!p.half_split) {
+                if (col < p.dimension) {
+                    const float2 r0 = rope_cs(p, row, col >> 1), r1 = rope_cs(p, row, (col >> 1) + 1);
+                    for (uint64_t h = 0; h < p.head_count; h++) {
+                        float4 v = in[h * hw4 + q], y;
+                        y.x = v.x * r0.x - v.y * r0.y;
+                        y.y = v.x * r0.y + v.y * r0.x;
+                        y.z = v.z * r1.x - v.w * r1.y;
+                        y.w = v.z * r1.y + v.w * r1.x;
+                        o[h * hw4 + q] = y;
+                    }
+                } else {
+                    for (uint64_t h = 0; h < p.head_count; h++) o[h * hw4 + q] = in[h * hw4 + q];
+                }
+            } else {
+                if (col >= p.dimension) {
+                    for (uint64_t h = 0; h < p.head_count; h++) o[h * hw4 + q] = in[h * hw4 + q];
+                } else if (col < p.half) {
+                    const uint64_t q2 = q + (p.half >> 2);
+                    const float2 r0 = rope_cs(p, row, col), r1 = rope_cs(p, row, col + 1);
+                    const float2 r2 = rope_cs(p, row, col + 2), r3 = rope_cs(p, row, col + 3);
+                    for (uint64_t h = 0; h < p.head_count; h++) {
+                        const float4 a = in[h * hw4 + q], b = in[h * hw4 + q2];
+                        float4 ya, yb;
+                        ya.x = a.x * r0.x - b.x * r0.y; yb.x = a.x * r0.y + b.x * r0.x;
+                        ya.y = a.y * r1.x - b.y * r1.y; yb.y = a.y * r1.y + b.y * r1.x;
+                        ya.z = a.z * r2.x - b.z * r2.y; yb.z = a.z * r2.y + b.z * r2.x;
+                        ya.w = a.w * r3.x - b.w * r3.y; yb.w = a.w * r3.y + b.w * r3.x;
+                        o[h * hw4 + q] = ya;
+                        o[h * hw4 + q2] = yb;
+                    }
+                }
+            }
+        }
+    }
+}
+
 // =====================================================================================
 // softmax rows (src/kernels.cu:1243-1259): out = expf(x - max) / sum(expf(x - max)).
 // A row whose max is not finite raises the device flag and is written as zeros.
@@ -403,6 +452,10 @@ mg_status rope(Device* d, const float* x, float* out, const RopeArgs& a) {
     if (p.half_split) vec = vec && p.half % 4 == 0;
     else vec = vec && p.dimension % 4 == 0;
     p.vec = vec ? 1 : 0;
+    if (p.vec) {
+        rope_warp_kernel<<<cap_grid(d, (a.rows + 7) / 8, 8), 256, 0, d->stream>>>(x, out, p);
+        return launched(d, "rope kernel launch");
+    }
     size_t smem = p.half * sizeof(float2);
     if (smem > 48 * 1024) {
         MG_CUDA(cudaFuncSetAttribute(rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),

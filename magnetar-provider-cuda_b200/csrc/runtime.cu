@@ -294,9 +294,12 @@ mg_status mg_device_open(int ordinal, mg_device** out) {
     cudaMemPoolSetAttribute(d->pool, cudaMemPoolAttrReleaseThreshold, &keep);
     e = cudaMalloc(&d->flags, 64);
     if (e == cudaSuccess) e = cudaMemset(d->flags, 0, 64);
+    if (e == cudaSuccess) e = cudaMalloc(&d->counters, (1u << 16) * sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(d->counters, 0, (1u << 16) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMallocHost(&d->host_flags, 64);
     if (e != cudaSuccess) {
         if (d->flags) cudaFree(d->flags);
+        if (d->counters) cudaFree(d->counters);
         cudaMemPoolDestroy(d->pool);
         cudaStreamDestroy(d->own_stream);
         delete d;
@@ -316,6 +319,7 @@ mg_status mg_device_close(mg_device* h) {
     cudaStreamSynchronize(d->stream);
     cudaStreamSynchronize(d->own_stream);
     cudaFree(d->flags);
+    cudaFree(d->counters);
     cudaFreeHost(d->host_flags);
     cudaMemPoolDestroy(d->pool);
     cudaStreamDestroy(d->own_stream);

@@ -325,6 +325,10 @@ ATTN_CASES = [
     dict(seq=30, kv=30, heads=2, kvh=2, d=64, causal=True, vd=32),
     dict(seq=1, kv=300, heads=4, kvh=2, d=64, causal=True),
     dict(seq=3, kv=3, heads=1, kvh=1, d=2, causal=True),
+    dict(seq=640, kv=640, heads=2, kvh=2, d=128, causal=True),
+    dict(seq=384, kv=512, heads=4, kvh=2, d=64, causal=False),
+    dict(seq=300, kv=300, heads=2, kvh=1, d=128, causal=True, window=100),
+    dict(seq=129, kv=1000, heads=2, kvh=2, d=64, causal=True, key_count=777),
 ]
 
 
