@@ -32,7 +32,7 @@ using namespace sm100;
 
 constexpr int AQ = 128;   // queries per CTA (MMA M)
 constexpr int AKV = 64;   // keys per iteration (one 128-byte swizzle row of bf16)
-constexpr int kAttnTcThreads = 256;
+constexpr int kAttnTcThreads = 384;  // 12 warps: producer, MMA, 2 idle, 8 softmax
 
 // ---- split pass -----------------------------------------------------------------------------
 __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
@@ -109,10 +109,16 @@ struct AttnShape {
     static constexpr int kOffQ = 0, kOffK = 2 * kQ, kOffV = kOffK + 2 * kK, kOffP = kOffV + 2 * kV;
     static constexpr int kBytes = kOffP + 2 * kP;
     static constexpr int kSmem = kBytes + 1024 + 256;
-    static constexpr uint32_t kTmemCols = 256;       // S: [0, 64), P.V: [128, 128 + D)
+    static constexpr uint32_t kTmemCols = 256;       // S: [0, 64) and [64, 128), P.V: [128, 128 + D)
     static constexpr uint32_t kColPV = 128;
+    static constexpr int kHalfD = D / 2;             // output columns per softmax thread
 };
 
+// Warp roles: 0 TMA producer; 1 MMA issuer; 4..11 softmax, two threads per query row (warp w
+// reads TMEM lane quarter w % 4; warps 4-7 take key columns [0, 32) of each tile and output
+// columns [0, D/2), warps 8-11 the other halves), exchanging row max and sum through shared
+// memory.  The MMA runs one S tile ahead (S is double-buffered in TMEM), so the next tile's
+// Q.K^T overlaps this tile's softmax.
 template <int D>
 __global__ void __launch_bounds__(kAttnTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
@@ -121,15 +127,16 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                         AttnTcParams p) {
     using S = AttnShape<D>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bars[8];
+    __shared__ uint64_t bars[9];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    __shared__ float red_max[2][AQ], red_sum[2][AQ];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* base_ptr = smem_raw + (base - raw);
     const uint32_t b0 = smem_u32(bars);
     const uint32_t q_full = b0, k_full = b0 + 8, k_empty = b0 + 16, v_full = b0 + 24, v_empty = b0 + 32,
-                   s_full = b0 + 40, p_full = b0 + 48, pv_full = b0 + 56;
+                   p_full = b0 + 40, pv_full = b0 + 48, s_full0 = b0 + 56;  // s_full[2] at 56, 64
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
     // Heavy (late) query tiles first: causal tiles near the end see the most keys.
@@ -139,7 +146,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     const uint64_t q0 = (uint64_t)qt * AQ;
     const uint64_t q_last = min(q0 + AQ, p.seq_len) - 1;
     // Keys this tile can admit: [key_lo, key_hi).
-    uint64_t key_hi = p.causal ? min(p.kv_seq_len, p.qpos0 + q_last + 1) : p.kv_seq_len;
+    const uint64_t key_hi = p.causal ? min(p.kv_seq_len, p.qpos0 + q_last + 1) : p.kv_seq_len;
     uint64_t key_lo = 0;
     if (p.window >= 0) {
         const uint64_t back = p.window > 0 ? (uint64_t)p.window - 1 : 0;
@@ -155,9 +162,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         mbar_init(k_empty, 1);
         mbar_init(v_full, 1);
         mbar_init(v_empty, 1);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 128);
+        mbar_init(p_full, 256);
         mbar_init(pv_full, 1);
+        mbar_init(s_full0, 1);
+        mbar_init(s_full0 + 8, 1);
         abort_flag = 0;
         fence_barrier_init();
     }
@@ -171,7 +179,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     const uint32_t tmem = tmem_slot;
 
     if (warp == 0) {
-        // ---- TMA producer --------------------------------------------------------------------
+        // ---- TMA producer ----------------------------------------------------------------------
         if (lane == 0 && n_kv > 0) {
             mbar_arrive_expect_tx(q_full, 2 * S::kQ);
             for (int a = 0; a < D / 64; a++) {
@@ -207,16 +215,12 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         if (lane == 0 && n_kv > 0) {
             constexpr uint32_t idesc_s = idesc_bf16(AQ, AKV);
             constexpr uint32_t idesc_o = idesc_bf16(AQ, D);
-            const uint32_t tS = tmem, tO = tmem + S::kColPV;
-            bool ok = mbar_wait(q_full, 0);
-            for (int j = 0; j < n_kv && ok; j++) {
-                const uint32_t ph = (uint32_t)j & 1u;
-                if (!mbar_wait(k_full, ph)) {
-                    ok = false;
-                    break;
-                }
+            const uint32_t tO = tmem + S::kColPV;
+            // S(j) = Q K(j)^T into TMEM columns [64 * (j % 2), +64), then frees K's buffer.
+            auto issue_s = [&](int j) -> bool {
+                if (!mbar_wait(k_full, (uint32_t)j & 1u)) return false;
                 tc_fence_after();
-                // S = Q K^T over D in steps of 16 (32 bytes of a 128-byte swizzle row)
+                const uint32_t tS = tmem + (uint32_t)(j & 1) * AKV;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
                     const uint32_t off = (uint32_t)(kk % 4) * 32;
@@ -229,7 +233,16 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                     mma_bf16(tS, qhi, khi, idesc_s, 1u);
                 }
                 tc_commit(k_empty);
-                tc_commit(s_full);
+                tc_commit(s_full0 + 8u * (uint32_t)(j & 1));
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0) && issue_s(0);
+            for (int j = 0; j < n_kv && ok; j++) {
+                if (j + 1 < n_kv && !issue_s(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t ph = (uint32_t)j & 1u;
                 if (!mbar_wait(p_full, ph) || !mbar_wait(v_full, ph)) {
                     ok = false;
                     break;
@@ -257,102 +270,116 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         }
         __syncwarp();
     } else if (warp >= 4) {
-        // ---- softmax / output: one query row per thread ------------------------------------------
+        // ---- softmax / output: two threads per query row --------------------------------------
+        constexpr float kLog2e = 1.4426950408889634f;
         const int qq = warp % 4;
+        const int hf = (warp - 4) / 4;  // which half of the key / output columns
         const int r = qq * 32 + lane;
         const uint64_t qi = q0 + r;
         const bool live = qi < p.seq_len;
         const uint64_t qpos = p.qpos0 + qi;
-        const uint64_t row_hi = p.causal ? min(p.kv_seq_len, qpos + 1) : p.kv_seq_len;
+        const uint64_t row_hi = live ? (p.causal ? min(p.kv_seq_len, qpos + 1) : p.kv_seq_len) : 0;
         uint64_t row_lo = 0;
         if (p.window >= 0) {
             const uint64_t back = p.window > 0 ? (uint64_t)p.window - 1 : 0;
             row_lo = qpos > back ? qpos - back : 0;
             if (row_lo > row_hi) row_lo = row_hi;
         }
+        const float scale2 = p.scale * kLog2e;  // scores in log2 units
         const uint32_t lane_base = tmem + ((uint32_t)(qq * 32) << 16);
-        float o[D];
+        float o[S::kHalfD];
 #pragma unroll
-        for (int d = 0; d < D; d++) o[d] = 0.0f;
+        for (int d = 0; d < S::kHalfD; d++) o[d] = 0.0f;
         float m = __int_as_float(0xff800000), l = 0.0f;
         uint8_t* p_hi = base_ptr + S::kOffP + r * 128;
         uint8_t* p_lo = p_hi + S::kP;
-        bool ok = true;
+        // Every softmax warp runs every iteration (the named barriers below need all 256
+        // threads); a wait that times out marks the CTA failed and later waits are skipped.
+        bool failed = false;
         for (int j = 0; j < n_kv; j++) {
             const uint32_t ph = (uint32_t)j & 1u;
-            const bool got = mbar_wait(s_full, ph);
-            if (!__all_sync(0xffffffffu, got && !abort_flag)) {
-                ok = false;
-                break;
-            }
+            if (!failed && !mbar_wait(s_full0 + 8u * (uint32_t)(j & 1), (uint32_t)(j >> 1) & 1u)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
             tc_fence_after();
-            float s[AKV];
-#pragma unroll
-            for (int c = 0; c < AKV; c += 16) tmem_ld16(lane_base + c, s + c);
+            float s[32];
+            tmem_ld32(lane_base + (uint32_t)(j & 1) * AKV + (uint32_t)hf * 32, s);
             tc_wait_ld();
-            const uint64_t key0 = kv0 + (uint64_t)j * AKV;
+            const uint64_t key0 = kv0 + (uint64_t)j * AKV + (uint64_t)hf * 32;
             float tmax = __int_as_float(0xff800000);
+            if (key0 >= row_lo && key0 + 32 <= row_hi) {  // interior: every key admitted
 #pragma unroll
-            for (int c = 0; c < AKV; c++) {
-                const uint64_t key = key0 + c;
-                const bool valid = live && key >= row_lo && key < row_hi;
-                s[c] = valid ? s[c] * p.scale : __int_as_float(0xff800000);
-                tmax = fmaxf(tmax, s[c]);
+                for (int c = 0; c < 32; c++) {
+                    s[c] *= scale2;
+                    tmax = fmaxf(tmax, s[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    const uint64_t key = key0 + c;
+                    s[c] = (key >= row_lo && key < row_hi) ? s[c] * scale2 : __int_as_float(0xff800000);
+                    tmax = fmaxf(tmax, s[c]);
+                }
             }
-            const float m_new = fmaxf(m, tmax);
+            red_max[hf][r] = tmax;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            const float m_new = fmaxf(m, fmaxf(red_max[0][r], red_max[1][r]));
             float alpha = 0.0f, psum = 0.0f;
             if (m_new != __int_as_float(0xff800000)) {
-                alpha = m == __int_as_float(0xff800000) ? 0.0f : expf(m - m_new);
+                alpha = m == __int_as_float(0xff800000) ? 0.0f : exp2f(m - m_new);
 #pragma unroll
-                for (int c = 0; c < AKV; c++) {
-                    s[c] = s[c] == __int_as_float(0xff800000) ? 0.0f : expf(s[c] - m_new);
+                for (int c = 0; c < 32; c++) {
+                    s[c] = exp2f(s[c] - m_new);  // masked (-inf) scores give 0
                     psum += s[c];
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < AKV; c++) s[c] = 0.0f;
+                for (int c = 0; c < 32; c++) s[c] = 0.0f;
             }
-            const float l_new = l * alpha + psum;
+            red_sum[hf][r] = psum;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            const float l_new = l * alpha + (red_sum[0][r] + red_sum[1][r]);
             const float inv = l_new > 0.0f ? 1.0f / l_new : 0.0f;
             const float keep = l_new > 0.0f ? (l * alpha) * inv : 0.0f;
-            // P / l_new as bf16 hi / lo, 16-byte chunk c of row r at chunk (c ^ (r % 8)).
+            // P / l_new as bf16 hi / lo: 16-byte chunk c of row r lives at chunk (c ^ (r % 8)).
 #pragma unroll
-            for (int c = 0; c < AKV / 8; c++) {
-                uint16_t h[8], lo8[8];
+            for (int cc = 0; cc < 4; cc++) {
+                const int c = hf * 4 + cc;
+                uint32_t h[4], lo4[4];
 #pragma unroll
-                for (int e = 0; e < 8; e++) split_bf16(s[c * 8 + e] * inv, h[e], lo8[e]);
+                for (int e = 0; e < 4; e++) {
+                    const float x0 = s[cc * 8 + 2 * e] * inv, x1 = s[cc * 8 + 2 * e + 1] * inv;
+                    const __nv_bfloat162 hb = __floats2bfloat162_rn(x0, x1);
+                    const float2 hf2 = __bfloat1622float2(hb);
+                    const __nv_bfloat162 lb = __floats2bfloat162_rn(x0 - hf2.x, x1 - hf2.y);
+                    h[e] = *reinterpret_cast<const uint32_t*>(&hb);
+                    lo4[e] = *reinterpret_cast<const uint32_t*>(&lb);
+                }
                 const int sw = (c ^ (r & 7)) * 16;
-                *reinterpret_cast<uint4*>(p_hi + sw) =
-                    make_uint4(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16),
-                               h[4] | ((uint32_t)h[5] << 16), h[6] | ((uint32_t)h[7] << 16));
-                *reinterpret_cast<uint4*>(p_lo + sw) =
-                    make_uint4(lo8[0] | ((uint32_t)lo8[1] << 16), lo8[2] | ((uint32_t)lo8[3] << 16),
-                               lo8[4] | ((uint32_t)lo8[5] << 16), lo8[6] | ((uint32_t)lo8[7] << 16));
+                *reinterpret_cast<uint4*>(p_hi + sw) = make_uint4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<uint4*>(p_lo + sw) = make_uint4(lo4[0], lo4[1], lo4[2], lo4[3]);
             }
             fence_proxy_async();  // the P writes are read by tcgen05.mma
             mbar_arrive(p_full);
-            const bool got_pv = mbar_wait(pv_full, ph);
-            if (!__all_sync(0xffffffffu, got_pv && !abort_flag)) {
-                ok = false;
-                break;
-            }
+            if (!failed && !mbar_wait(pv_full, ph)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < D; c += 16) {
-                float pv[16];
-                tmem_ld16(lane_base + S::kColPV + c, pv);
+            for (int c = 0; c < S::kHalfD; c += 32) {
+                float pv[32];
+                tmem_ld32(lane_base + S::kColPV + (uint32_t)(hf * S::kHalfD + c), pv);
                 tc_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 16; e++) o[c + e] = o[c + e] * keep + pv[e];
+                for (int e = 0; e < 32; e++) o[c + e] = o[c + e] * keep + pv[e];
             }
             m = m_new;
             l = l_new;
         }
-        if (!ok) atomicExch(p.error, 1);
+        if (failed) atomicExch(p.error, 1);
         if (live) {
-            float* orow = p.out + qi * p.out_dim + head * D;
+            float* orow = p.out + qi * p.out_dim + head * D + hf * S::kHalfD;
 #pragma unroll
-            for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+            for (int d = 0; d < S::kHalfD; d += 4)
+                *reinterpret_cast<float4*>(orow + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
         }
     }
 
