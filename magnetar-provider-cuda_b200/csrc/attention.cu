@@ -50,6 +50,7 @@ __device__ __forceinline__ void key_range(const AttnP& p, uint64_t pos, uint64_t
 
 template <int DPT>  // float4 chunks per thread: head_dim = 16 * DPT
 __global__ void __launch_bounds__(kAttnThreads) attention_tile_kernel(AttnP p) {
+    pdl_enter();
     constexpr int D = 16 * DPT;
     __shared__ float4 ks[KT][D / 4];
     __shared__ float4 vs[KT][D / 4];
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_tile_kernel(AttnP p) {
 // Any head / value dimension: one warp per (head, query), keys one at a time, lanes over
 // dimensions, with the same weighted-mean online update.
 __global__ void __launch_bounds__(256) attention_generic_kernel(AttnP p) {
+    pdl_enter();
     const uint64_t warp_id = (uint64_t)blockIdx.x * 8 + threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     if (warp_id >= p.head_count * p.seq_len) return;
@@ -187,6 +189,189 @@ __global__ void __launch_bounds__(256) attention_generic_kernel(AttnP p) {
     }
 }
 
+// ---- short key spans: the whole span resident in shared memory ------------------------------
+// When every CTA's admitted keys fit in shared memory (a short sequence, or a short window),
+// the softmax needs no online merge: a CTA of 256 threads serves kShortQ queries of one head,
+// copies the span of K and V once (cp.async), then
+//   1. scores: one thread per key, kShortQ dot products against the broadcast Q rows;
+//   2. one warp per query row: max, exp, sum, and the weights divided by the sum -- the
+//      reference's order (src/kernels.cu:1899-1958) -- masked keys weigh exactly 0;
+//   3. P.V: one thread per output column and kShortQ * D / 256 queries.
+// This launches one kernel with ceil(S / 8) * H CTAs and no split pass, so a decoder layer's
+// attention (S = 128) is one short kernel instead of a tensor-core pipeline that would keep
+// only H CTAs busy.
+constexpr int kShortQ = 8;
+constexpr int kShortThreads = 256;
+
+// Key capacity limit per head dimension (shared memory: about 560 B a key at D = 64).
+template <int D>
+constexpr uint32_t short_cap_limit() {
+    return D <= 32 ? 512 : D <= 64 ? 384 : 192;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Shared-memory plan for `cap` keys: K rows padded to D + 4 floats (an odd number of 16-byte
+// chunks, so one thread per key reads conflict-free), V rows dense, Q, and P [kShortQ][cap].
+template <int D>
+struct ShortPlan {
+    static constexpr int kKStride = D + 4;
+    __host__ __device__ static uint32_t off_v(uint32_t cap) { return cap * kKStride * 4; }
+    __host__ __device__ static uint32_t off_q(uint32_t cap) { return off_v(cap) + cap * D * 4; }
+    __host__ __device__ static uint32_t off_p(uint32_t cap) { return off_q(cap) + kShortQ * D * 4; }
+    __host__ __device__ static uint32_t bytes(uint32_t cap) { return off_p(cap) + kShortQ * cap * 4; }
+};
+
+template <int D>
+__global__ void __launch_bounds__(kShortThreads) attention_short_kernel(AttnP p, uint32_t cap, int* error) {
+    pdl_enter();
+    using P = ShortPlan<D>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* ks = reinterpret_cast<float*>(smem);
+    float* vs = reinterpret_cast<float*>(smem + P::off_v(cap));
+    float* qs = reinterpret_cast<float*>(smem + P::off_q(cap));
+    float* ps = reinterpret_cast<float*>(smem + P::off_p(cap));
+    const float ninf = __int_as_float(0xff800000);
+    const uint64_t head = blockIdx.y, kvh = head / p.group;
+    const uint64_t q0 = (uint64_t)blockIdx.x * kShortQ;
+    const int nq = (int)min((uint64_t)kShortQ, p.seq_len - q0);
+    uint64_t span_lo, span_hi, tmp;
+    key_range(p, p.qpos0 + q0, span_lo, tmp);
+    key_range(p, p.qpos0 + q0 + nq - 1, tmp, span_hi);
+    if (span_lo > span_hi) span_lo = span_hi;
+    const uint64_t span = span_hi - span_lo;
+    if (span > cap) {  // the host sizes cap for the widest span; never taken
+        if (threadIdx.x == 0) atomicExch(error, 1);
+        return;
+    }
+    const int n = (int)span;
+    constexpr int C4 = D / 4;  // 16-byte chunks per row
+
+    for (int i = threadIdx.x; i < kShortQ * C4; i += kShortThreads) {
+        const int qi = i / C4, c = i % C4;
+        float* dst = qs + qi * D + c * 4;
+        if (qi < nq) cp_async16(dst, p.q + (q0 + qi) * p.q_model_dim + head * D + c * 4);
+        else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int i = threadIdx.x; i < n * C4; i += kShortThreads) {
+        const int j = i / C4, c = i % C4;
+        const uint64_t key = span_lo + j;
+        cp_async16(ks + j * P::kKStride + c * 4, p.k + key * p.kv_model_dim + kvh * D + c * 4);
+        cp_async16(vs + j * D + c * 4, p.v + key * p.v_model_dim + kvh * D + c * 4);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // 1. scores (masked keys -inf), one key per thread
+    uint64_t qlo[kShortQ], qhi[kShortQ];
+#pragma unroll
+    for (int qi = 0; qi < kShortQ; qi++) {
+        key_range(p, p.qpos0 + q0 + qi, qlo[qi], qhi[qi]);
+        if (qi >= nq) qlo[qi] = qhi[qi] = 0;
+    }
+    for (int j = threadIdx.x; j < n; j += kShortThreads) {
+        float acc[kShortQ];
+#pragma unroll
+        for (int qi = 0; qi < kShortQ; qi++) acc[qi] = 0.0f;
+        const float4* kr = reinterpret_cast<const float4*>(ks + j * P::kKStride);
+#pragma unroll 4
+        for (int c = 0; c < C4; c++) {
+            const float4 kk = kr[c];
+#pragma unroll
+            for (int qi = 0; qi < kShortQ; qi++) {
+                const float4 qq = reinterpret_cast<const float4*>(qs + qi * D)[c];
+                acc[qi] += qq.x * kk.x + qq.y * kk.y + qq.z * kk.z + qq.w * kk.w;
+            }
+        }
+        const uint64_t key = span_lo + j;
+#pragma unroll
+        for (int qi = 0; qi < kShortQ; qi++)
+            ps[qi * cap + j] = (key >= qlo[qi] && key < qhi[qi]) ? acc[qi] * p.scale : ninf;
+    }
+    __syncthreads();
+
+    // 2. softmax of row `warp`: weights e / sum, all zero for a row with no admitted key
+    {
+        const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+        float* row = ps + warp * cap;
+        float m = ninf;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, row[j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (m == ninf) {
+            for (int j = lane; j < n; j += 32) row[j] = 0.0f;
+        } else {
+            float l = 0.0f;
+            for (int j = lane; j < n; j += 32) {
+                const float e = expf(row[j] - m);
+                row[j] = e;
+                l += e;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            for (int j = lane; j < n; j += 32) row[j] = row[j] / l;
+        }
+    }
+    __syncthreads();
+
+    // 3. out = P.V, one output column per thread, QPT queries each
+    constexpr int QPT = kShortQ * D / kShortThreads;
+    static_assert(QPT >= 1 && kShortThreads % D == 0, "one column per thread");
+    const int d = threadIdx.x % D, qg = threadIdx.x / D;
+    float acc0[QPT], acc1[QPT];
+#pragma unroll
+    for (int i = 0; i < QPT; i++) acc0[i] = acc1[i] = 0.0f;
+    int j = 0;
+    for (; j + 1 < n; j += 2) {
+        const float v0 = vs[j * D + d], v1 = vs[(j + 1) * D + d];
+#pragma unroll
+        for (int i = 0; i < QPT; i++) {
+            const float* prow = ps + (qg * QPT + i) * cap;
+            acc0[i] += prow[j] * v0;
+            acc1[i] += prow[j + 1] * v1;
+        }
+    }
+    if (j < n) {
+        const float v0 = vs[j * D + d];
+#pragma unroll
+        for (int i = 0; i < QPT; i++) acc0[i] += ps[(qg * QPT + i) * cap + j] * v0;
+    }
+#pragma unroll
+    for (int i = 0; i < QPT; i++) {
+        const int qi = qg * QPT + i;
+        if (qi < nq) p.out[((q0 + qi) * p.head_count + head) * D + d] = acc0[i] + acc1[i];
+    }
+}
+
+// Largest key span any CTA of the short kernel sees: all keys, or a causal window plus the
+// CTA's extra queries (a window implies causal masking).
+uint64_t short_span_bound(const AttnP& p) {
+    uint64_t span = p.kv_seq_len;
+    if (p.window >= 0 && p.causal) span = std::min<uint64_t>(span, (uint64_t)p.window + kShortQ - 1);
+    return span;
+}
+
+template <int D>
+mg_status launch_short(Device* d, const AttnP& p, uint32_t cap) {
+    using P = ShortPlan<D>;
+    const uint32_t smem = P::bytes(cap);
+    static uint32_t configured[64] = {0};
+    if (configured[d->ordinal & 63] < smem) {
+        MG_CUDA(cudaFuncSetAttribute(attention_short_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)ShortPlan<D>::bytes(short_cap_limit<D>())),
+                "configuring the short attention kernel");
+        configured[d->ordinal & 63] = ShortPlan<D>::bytes(short_cap_limit<D>());
+    }
+    dim3 grid((unsigned)((p.seq_len + kShortQ - 1) / kShortQ), (unsigned)p.head_count);
+    enqueue(d, attention_short_kernel<D>, grid, kShortThreads, smem, p, cap, d->flags + 2);
+    return launched(d, "short attention launch");
+}
+
 }  // namespace
 
 namespace k {
@@ -196,7 +381,6 @@ mg_status attention_tc(Device* d, const AttentionArgs& a);
 
 mg_status attention(Device* d, const AttentionArgs& a) {
     if (a.seq_len == 0 || a.head_count == 0) return MG_OK;
-    if (attention_tc_eligible(a)) return attention_tc(d, a);
     AttnP p;
     p.q = a.q;
     p.k = a.k;
@@ -215,27 +399,46 @@ mg_status attention(Device* d, const AttentionArgs& a) {
     p.window = a.window;
     p.qpos0 = a.query_position_offset;
     p.scale = a.scale;
-    if (a.seq_len == 0 || a.head_count == 0) return MG_OK;
     const bool aligned = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
                            reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out)) & 15) == 0 &&
                          a.q_model_dim % 4 == 0 && a.kv_model_dim % 4 == 0 && a.v_model_dim % 4 == 0;
+    if (a.head_count > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention head_count exceeds the launch grid");
+    // Short spans: one short kernel when every CTA's keys fit in shared memory and the grid is
+    // at most two waves; otherwise the tensor-core pipeline.
+    if (aligned && a.value_dim == a.head_dim && (a.head_dim == 32 || a.head_dim == 64 || a.head_dim == 128)) {
+        const uint64_t span = short_span_bound(p);
+        const uint32_t limit = a.head_dim == 32 ? short_cap_limit<32>() : a.head_dim == 64 ? short_cap_limit<64>()
+                                                                                            : short_cap_limit<128>();
+        if (span <= limit) {
+            const uint32_t cap = (uint32_t)std::min<uint64_t>(((span + 31) / 32) * 32, limit);
+            const uint32_t smem = a.head_dim == 32 ? ShortPlan<32>::bytes(cap) : a.head_dim == 64 ? ShortPlan<64>::bytes(cap)
+                                                                                                : ShortPlan<128>::bytes(cap);
+            const uint64_t per_sm = std::max<uint64_t>(1, std::min<uint64_t>(8, (228ull * 1024) / (smem + 1024)));
+            const uint64_t ctas = (a.seq_len + kShortQ - 1) / kShortQ * a.head_count;
+            if (ctas <= 2 * per_sm * (uint64_t)d->sm_count) {
+                if (a.head_dim == 32) return launch_short<32>(d, p, cap);
+                if (a.head_dim == 64) return launch_short<64>(d, p, cap);
+                return launch_short<128>(d, p, cap);
+            }
+        }
+    }
+    if (attention_tc_eligible(a)) return attention_tc(d, a);
     const bool tiled = aligned && a.value_dim == a.head_dim && (a.head_dim == 64 || a.head_dim == 128 ||
                                                                  a.head_dim == 32 || a.head_dim == 16);
     if (tiled) {
         dim3 grid((unsigned)((a.seq_len + BQ - 1) / BQ), (unsigned)a.head_count);
-        if (a.head_count > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention head_count exceeds the launch grid");
         switch (a.head_dim) {
-            case 16: attention_tile_kernel<1><<<grid, kAttnThreads, 0, d->stream>>>(p); break;
-            case 32: attention_tile_kernel<2><<<grid, kAttnThreads, 0, d->stream>>>(p); break;
-            case 64: attention_tile_kernel<4><<<grid, kAttnThreads, 0, d->stream>>>(p); break;
-            default: attention_tile_kernel<8><<<grid, kAttnThreads, 0, d->stream>>>(p); break;
+            case 16: enqueue(d, attention_tile_kernel<1>, grid, kAttnThreads, 0, p); break;
+            case 32: enqueue(d, attention_tile_kernel<2>, grid, kAttnThreads, 0, p); break;
+            case 64: enqueue(d, attention_tile_kernel<4>, grid, kAttnThreads, 0, p); break;
+            default: enqueue(d, attention_tile_kernel<8>, grid, kAttnThreads, 0, p); break;
         }
         return launched(d, "attention kernel launch");
     }
     const uint64_t warps = a.head_count * a.seq_len;
     const uint64_t blocks = (warps + 7) / 8;
     if (blocks > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "attention launch size overflows");
-    attention_generic_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(p);
+    enqueue(d, attention_generic_kernel, (unsigned)blocks, 256, 0, p);
     return launched(d, "attention kernel launch");
 }
 

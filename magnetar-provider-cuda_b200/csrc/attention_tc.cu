@@ -50,6 +50,7 @@ __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) 
 // [rows, cols] f32 -> bf16 hi / lo in the same layout.
 __global__ void __launch_bounds__(256) split_bf16_rows_kernel(const float* __restrict__ src, uint16_t* __restrict__ hi,
                                                               uint16_t* __restrict__ lo, uint64_t n) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += stride) {
         const float4 v = reinterpret_cast<const float4*>(src)[i];
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(256) split_bf16_rows_kernel(const float* __res
 __global__ void __launch_bounds__(256) split_bf16_transpose_kernel(const float* __restrict__ v, uint64_t keys,
                                                                    uint64_t width, uint16_t* __restrict__ hi,
                                                                    uint16_t* __restrict__ lo, uint64_t keys_p) {
+    pdl_enter();
     __shared__ float tile[32][33];
     const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
     const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
                         AttnTcParams p) {
+    pdl_enter();
     using S = AttnShape<D>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bars[9];
@@ -447,7 +450,7 @@ mg_status launch_attention_tc(Device* d, const k::AttentionArgs& a, const CUtens
     p.q_tiles = q_tiles;
     p.error = d->flags + 2;
     dim3 grid((unsigned)q_tiles, (unsigned)a.head_count);
-    attention_tc_kernel<D><<<grid, kAttnTcThreads, S::kSmem, d->stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
+    enqueue(d, attention_tc_kernel<D>, grid, kAttnTcThreads, S::kSmem, maps[0], maps[1], maps[2], maps[3], maps[4],
                                                                           maps[5], p);
     return launched(d, "tensor-core attention launch");
 }
@@ -477,13 +480,13 @@ mg_status attention_tc(Device* d, const AttentionArgs& a) {
     uint16_t* klo = khi + k_elems;
     uint16_t* vhi = klo + k_elems;
     uint16_t* vlo = vhi + vt_elems;
-    split_bf16_rows_kernel<<<grid_for_n(d, q_elems / 4), 256, 0, d->stream>>>(a.q, qhi, qlo, q_elems);
+    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, q_elems / 4), 256, 0, a.q, qhi, qlo, q_elems);
     MG_TRY(launched(d, "attention split launch"));
-    split_bf16_rows_kernel<<<grid_for_n(d, k_elems / 4), 256, 0, d->stream>>>(a.k, khi, klo, k_elems);
+    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, k_elems / 4), 256, 0, a.k, khi, klo, k_elems);
     MG_TRY(launched(d, "attention split launch"));
     dim3 tg((unsigned)((kvd + 31) / 32), (unsigned)((skv_p + 31) / 32));
     if (tg.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the split pass");
-    split_bf16_transpose_kernel<<<tg, 256, 0, d->stream>>>(a.v, Skv, kvd, vhi, vlo, skv_p);
+    enqueue(d, split_bf16_transpose_kernel, tg, 256, 0, a.v, Skv, kvd, vhi, vlo, skv_p);
     MG_TRY(launched(d, "attention split launch"));
     const int D = (int)a.head_dim;
     CUtensorMap maps[6];

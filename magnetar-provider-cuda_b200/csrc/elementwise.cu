@@ -59,6 +59,7 @@ __device__ inline float4 apply1(Op op, float4 a) {
 template <class Op>
 __global__ void __launch_bounds__(kThreads) binary_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                                           float* __restrict__ out, uint64_t n, int vec, Op op) {
+    pdl_enter();
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t tail = 0;
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kThreads) binary_kernel(const float* __restric
 template <class Op>
 __global__ void __launch_bounds__(kThreads) unary_kernel(const float* __restrict__ a, float* __restrict__ out,
                                                          uint64_t n, int vec, Op op) {
+    pdl_enter();
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t tail = 0;
@@ -114,6 +116,7 @@ __global__ void __launch_bounds__(kThreads) bias_add_kernel(const float* __restr
                                                             const float* __restrict__ bias,
                                                             float* __restrict__ out, uint64_t cols,
                                                             uint64_t rows, int vec) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (vec) {
@@ -134,6 +137,7 @@ __global__ void __launch_bounds__(kThreads) bias_add_kernel(const float* __restr
 // src/kernels.cu:112-117: out[i] = a[i] * b[0]
 __global__ void __launch_bounds__(kThreads) mul_scalar_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                                               float* __restrict__ out, uint64_t n, int vec) {
+    pdl_enter();
     const float s = b[0];
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -235,6 +239,7 @@ template <int DT, int OP>
 __global__ void __launch_bounds__(kThreads) half_binary_kernel(const uint16_t* __restrict__ a,
                                                                const uint16_t* __restrict__ b,
                                                                uint16_t* __restrict__ out, uint64_t n, int vec) {
+    pdl_enter();
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t tail = 0;
@@ -292,6 +297,7 @@ struct HalfRoundTripOp {
 template <int DT>
 __global__ void __launch_bounds__(kThreads) encode_kernel(const float* __restrict__ in, uint16_t* __restrict__ out,
                                                           uint64_t n) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
         out[i] = (uint16_t)hencode<DT>(in[i]);
@@ -300,12 +306,14 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const float* __restric
 template <int DT>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const uint16_t* __restrict__ in, float* __restrict__ out,
                                                           uint64_t n) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
         out[i] = hdecode<DT>(in[i]);
 }
 
 __global__ void __launch_bounds__(kThreads) zero_kernel(uint4* __restrict__ p, uint64_t n16) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride)
         p[i] = make_uint4(0, 0, 0, 0);
@@ -321,44 +329,44 @@ static inline unsigned vec_grid(const Device* d, uint64_t n, int vec, int lanes)
 
 mg_status add(Device* d, const float* a, const float* b, float* out, uint64_t n) {
     int vec = aligned16(a) && aligned16(b) && aligned16(out);
-    binary_kernel<<<vec_grid(d, n, vec, 4), kThreads, 0, d->stream>>>(a, b, out, n, vec, AddOp{});
+    enqueue(d, binary_kernel<AddOp>, vec_grid(d, n, vec, 4), kThreads, 0, a, b, out, n, vec, AddOp{});
     return launched(d, "add kernel launch");
 }
 
 mg_status mul(Device* d, const float* a, const float* b, float* out, uint64_t n) {
     int vec = aligned16(a) && aligned16(b) && aligned16(out);
-    binary_kernel<<<vec_grid(d, n, vec, 4), kThreads, 0, d->stream>>>(a, b, out, n, vec, MulOp{});
+    enqueue(d, binary_kernel<MulOp>, vec_grid(d, n, vec, 4), kThreads, 0, a, b, out, n, vec, MulOp{});
     return launched(d, "mul kernel launch");
 }
 
 mg_status silu_mul(Device* d, const float* g, const float* u, float* out, uint64_t n) {
     int vec = aligned16(g) && aligned16(u) && aligned16(out);
-    binary_kernel<<<vec_grid(d, n, vec, 4), kThreads, 0, d->stream>>>(g, u, out, n, vec, SiluMulOp{});
+    enqueue(d, binary_kernel<SiluMulOp>, vec_grid(d, n, vec, 4), kThreads, 0, g, u, out, n, vec, SiluMulOp{});
     return launched(d, "silu-mul kernel launch");
 }
 
 mg_status silu(Device* d, const float* x, float* out, uint64_t n) {
     int vec = aligned16(x) && aligned16(out);
-    unary_kernel<<<vec_grid(d, n, vec, 4), kThreads, 0, d->stream>>>(x, out, n, vec, SiluOp{});
+    enqueue(d, unary_kernel<SiluOp>, vec_grid(d, n, vec, 4), kThreads, 0, x, out, n, vec, SiluOp{});
     return launched(d, "silu kernel launch");
 }
 
 mg_status scale(Device* d, const float* x, float* out, float factor, uint64_t n) {
     int vec = aligned16(x) && aligned16(out);
-    unary_kernel<<<vec_grid(d, n, vec, 4), kThreads, 0, d->stream>>>(x, out, n, vec, ScaleOp{factor});
+    enqueue(d, unary_kernel<ScaleOp>, vec_grid(d, n, vec, 4), kThreads, 0, x, out, n, vec, ScaleOp{factor});
     return launched(d, "scale kernel launch");
 }
 
 mg_status bias_add(Device* d, const float* a, const float* bias, float* out, uint64_t cols, uint64_t n) {
     const uint64_t rows = cols ? n / cols : 0;
     int vec = (cols % 4 == 0) && aligned16(a) && aligned16(bias) && aligned16(out);
-    bias_add_kernel<<<grid_for(d, vec ? n / 4 : n), kThreads, 0, d->stream>>>(a, bias, out, cols, rows, vec);
+    enqueue(d, bias_add_kernel, grid_for(d, vec ? n / 4 : n), kThreads, 0, a, bias, out, cols, rows, vec);
     return launched(d, "bias-add kernel launch");
 }
 
 mg_status mul_scalar(Device* d, const float* a, const float* b, float* out, uint64_t n) {
     int vec = aligned16(a) && aligned16(out);
-    mul_scalar_kernel<<<grid_for(d, vec ? n / 4 : n), kThreads, 0, d->stream>>>(a, b, out, n, vec);
+    enqueue(d, mul_scalar_kernel, grid_for(d, vec ? n / 4 : n), kThreads, 0, a, b, out, n, vec);
     return launched(d, "mul-scalar kernel launch");
 }
 
@@ -367,11 +375,11 @@ mg_status half_binary(Device* d, const uint16_t* a, const uint16_t* b, uint16_t*
     int vec = aligned16(a) && aligned16(b) && aligned16(out);
     unsigned grid = vec_grid(d, n, vec, 8);
     if (dtype == MG_F16) {
-        if (op == 0) half_binary_kernel<MG_F16, 0><<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec);
-        else half_binary_kernel<MG_F16, 1><<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec);
+        if (op == 0) enqueue(d, half_binary_kernel<MG_F16, 0>, grid, kThreads, 0, a, b, out, n, vec);
+        else enqueue(d, half_binary_kernel<MG_F16, 1>, grid, kThreads, 0, a, b, out, n, vec);
     } else {
-        if (op == 0) half_binary_kernel<MG_BF16, 0><<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec);
-        else half_binary_kernel<MG_BF16, 1><<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec);
+        if (op == 0) enqueue(d, half_binary_kernel<MG_BF16, 0>, grid, kThreads, 0, a, b, out, n, vec);
+        else enqueue(d, half_binary_kernel<MG_BF16, 1>, grid, kThreads, 0, a, b, out, n, vec);
     }
     return launched(d, "half kernel launch");
 }
@@ -380,30 +388,30 @@ mg_status half_binary_f32(Device* d, const float* a, const float* b, float* out,
     int vec = aligned16(a) && aligned16(b) && aligned16(out);
     unsigned grid = vec_grid(d, n, vec, 4);
     if (dtype == MG_F16) {
-        if (op == 0) binary_kernel<<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec, HalfRoundTripOp<MG_F16, 0>{});
-        else binary_kernel<<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec, HalfRoundTripOp<MG_F16, 1>{});
+        if (op == 0) enqueue(d, binary_kernel<HalfRoundTripOp<MG_F16, 0>>, grid, kThreads, 0, a, b, out, n, vec, HalfRoundTripOp<MG_F16, 0>{});
+        else enqueue(d, binary_kernel<HalfRoundTripOp<MG_F16, 1>>, grid, kThreads, 0, a, b, out, n, vec, HalfRoundTripOp<MG_F16, 1>{});
     } else {
-        if (op == 0) binary_kernel<<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec, HalfRoundTripOp<MG_BF16, 0>{});
-        else binary_kernel<<<grid, kThreads, 0, d->stream>>>(a, b, out, n, vec, HalfRoundTripOp<MG_BF16, 1>{});
+        if (op == 0) enqueue(d, binary_kernel<HalfRoundTripOp<MG_BF16, 0>>, grid, kThreads, 0, a, b, out, n, vec, HalfRoundTripOp<MG_BF16, 0>{});
+        else enqueue(d, binary_kernel<HalfRoundTripOp<MG_BF16, 1>>, grid, kThreads, 0, a, b, out, n, vec, HalfRoundTripOp<MG_BF16, 1>{});
     }
     return launched(d, "half round-trip kernel launch");
 }
 
 mg_status encode_half(Device* d, const float* in, uint16_t* out, uint64_t n, mg_dtype dtype) {
-    if (dtype == MG_F16) encode_kernel<MG_F16><<<grid_for(d, n), kThreads, 0, d->stream>>>(in, out, n);
-    else encode_kernel<MG_BF16><<<grid_for(d, n), kThreads, 0, d->stream>>>(in, out, n);
+    if (dtype == MG_F16) enqueue(d, encode_kernel<MG_F16>, grid_for(d, n), kThreads, 0, in, out, n);
+    else enqueue(d, encode_kernel<MG_BF16>, grid_for(d, n), kThreads, 0, in, out, n);
     return launched(d, "half encode kernel launch");
 }
 
 mg_status decode_half(Device* d, const uint16_t* in, float* out, uint64_t n, mg_dtype dtype) {
-    if (dtype == MG_F16) decode_kernel<MG_F16><<<grid_for(d, n), kThreads, 0, d->stream>>>(in, out, n);
-    else decode_kernel<MG_BF16><<<grid_for(d, n), kThreads, 0, d->stream>>>(in, out, n);
+    if (dtype == MG_F16) enqueue(d, decode_kernel<MG_F16>, grid_for(d, n), kThreads, 0, in, out, n);
+    else enqueue(d, decode_kernel<MG_BF16>, grid_for(d, n), kThreads, 0, in, out, n);
     return launched(d, "half decode kernel launch");
 }
 
 mg_status fill_zero(Device* d, void* ptr, uint64_t bytes) {
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && bytes % 16 == 0) {
-        if (bytes) zero_kernel<<<grid_for(d, bytes / 16), kThreads, 0, d->stream>>>((uint4*)ptr, bytes / 16);
+        if (bytes) enqueue(d, zero_kernel, grid_for(d, bytes / 16), kThreads, 0, (uint4*)ptr, bytes / 16);
         return launched(d, "zero kernel launch");
     }
     MG_CUDA(cudaMemsetAsync(ptr, 0, bytes, d->stream), "zeroing a buffer");

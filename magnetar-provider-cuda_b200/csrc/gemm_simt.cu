@@ -11,6 +11,7 @@ namespace {
 constexpr int BM = 64, BN = 64, BK = 16;
 
 __global__ void __launch_bounds__(256) gemm_simt_kernel(k::GemmArgs g) {
+    pdl_enter();
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[2][BK][BN + 4];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -80,7 +81,7 @@ namespace k {
 mg_status gemm_simt(Device* d, const GemmArgs& g) {
     dim3 grid((unsigned)((g.n + BN - 1) / BN), (unsigned)((g.m + BM - 1) / BM));
     if (grid.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "matmul with %llu rows exceeds the launch grid", (unsigned long long)g.m);
-    gemm_simt_kernel<<<grid, 256, 0, d->stream>>>(g);
+    enqueue(d, gemm_simt_kernel, grid, 256, 0, g);
     return launched(d, "matmul kernel launch");
 }
 

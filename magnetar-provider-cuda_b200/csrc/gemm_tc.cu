@@ -13,12 +13,12 @@
 //   warp 0      TMA producer: 32-column k-blocks (one 128-byte swizzle row per tile row) of
 //               A and B into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM and issues the MMAs (one thread), committing each stage back;
-//   warps 2-5   stage the accumulator (tcgen05.ld) in the drained shared-memory ring;
+//   warps 2-5   read the accumulator (tcgen05.ld) into the drained shared-memory ring;
 //   warps 6-9   (when A arrives as raw f32) split each A tile into its hi/lo terms in shared
 //               memory, in place, so no separate pass over A is needed.
 // When the output grid alone would leave SMs idle, k is split across the CTAs of a thread-block
-// cluster; the cluster then reduces its staged partial tiles through distributed shared memory
-// and every thread writes finished rows (bias / residual / SwiGLU applied) with coalesced stores.
+// cluster; the partial tiles are then summed through distributed shared memory and every
+// thread writes finished rows (bias / residual / SwiGLU applied) with coalesced stores.
 // B comes either from a weight's prepared hi/lo form (built once, kept with the weight) or
 // from a per-call split pass that also transposes it to K-major.
 #include <cooperative_groups.h>
@@ -74,6 +74,7 @@ __device__ __forceinline__ void split4(float4 v, float4& hi, float4& lo) {
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, uint64_t ld, uint64_t rows,
                                                          uint64_t k, float* __restrict__ hi, float* __restrict__ lo,
                                                          uint64_t kp, int vec) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (vec) {  // k == kp, k % 4 == 0, 16-byte aligned
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ src, uint64_t r_count,
                                                               uint64_t c_count, float* __restrict__ hi,
                                                               float* __restrict__ lo, uint64_t rp) {
+    pdl_enter();
     __shared__ float tile[64][65];
     const uint64_t c0 = (uint64_t)blockIdx.x * 64, r0 = (uint64_t)blockIdx.y * 64;
     const int tx = threadIdx.x % 64, ty = threadIdx.x / 64;  // 64 x 4
@@ -130,50 +132,63 @@ struct TcParams {
     int tiles_m, tiles_n;
     int kb_per_split;  // k-blocks each CTA of a split handles
     int splits;        // CTAs per cluster (blockIdx.y), each over its own range of k
+    int b_early;       // B is a stable prepared weight: its first loads may precede pdl_enter()
     int* error;        // device word set when a wait times out
 };
 
-template <int BN, int NB, int STAGES, bool A_RAW>
+template <int BN, int NB, int STAGES, bool A_RAW, bool SPLIT>
 struct TcShape {
     static constexpr int kATile = BM * BK * 4;  // bytes of one A term tile
     static constexpr int kBTile = BN * BK * 4;  // bytes of one B term tile
     static constexpr int kStage = 2 * kATile + NB * 2 * kBTile;
     static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + NB * 2 * kBTile;  // TMA bytes per stage
-    static constexpr int kLd = BN + 4;                                            // staged tile row stride
-    static constexpr int kStageTile = BM * kLd * 4;                               // bytes of one staged tile
-    static_assert(NB * kStageTile <= STAGES * kStage, "the staged output fits the drained ring");
-    static constexpr int kSmem = STAGES * kStage + 1024 /* align */ + 512 /* barriers */;
+    static constexpr int kRing = STAGES * kStage;
+    static constexpr int kLd = BN + 4;  // row stride (floats) of a staged tile and of the receive slots
+    static_assert(NB * BM * kLd * 4 <= kRing, "the staged tile fits the drained ring");
+    static constexpr int kBars = 512;
+    // Split k: receive slots [NB][splits][band][kLd] for the other CTAs' partial rows of this
+    // CTA's band, in a region of their own (free from the start, so no CTA has to wait for a
+    // peer's ring to drain before sending).
+    static constexpr int kRecv = SPLIT ? NB * (BM + kMaxSplits - 1) * kLd * 4 : 0;
+    static constexpr int kSmem = kRing + kBars + kRecv + 1024 /* align */;
     static constexpr uint32_t kTmemCols =
         NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
     static constexpr int kThreads = A_RAW ? 320 : 192;
 };
 
 // The CTAs of one output tile form a cluster along blockIdx.y, each multiplying its own range
-// of k.  After the main loop every CTA stages its f32 accumulator in its own (drained) shared
-// memory; then each CTA sums one band of rows across the cluster's staged tiles through
-// distributed shared memory, in cluster-rank order, and writes the finished band with
-// coalesced stores (bias / residual / SwiGLU applied).  One kernel, deterministic, and the
-// partial sums never leave the chip.
-template <int BN, int NB, int STAGES, bool A_RAW>
-__global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
+// of k.  After the main loop each CTA pushes the rows of its f32 accumulator into the shared
+// memory of the CTA that owns their band; each CTA then sums its band's partials in
+// cluster-rank order and writes the finished band with coalesced stores (bias / residual /
+// SwiGLU applied).  One kernel, deterministic, and the partial sums never leave the chip.
+template <int BN, int NB, int STAGES, bool A_RAW, bool SPLIT>
+__global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                    const __grid_constant__ CUtensorMap map_b2hi, const __grid_constant__ CUtensorMap map_b2lo,
                    TcParams p) {
-    using S = TcShape<BN, NB, STAGES, A_RAW>;
+    using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* base_ptr = smem_raw + (base - raw);
-    const uint32_t bar_base = base + STAGES * S::kStage;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + STAGES * S::kStage);
-    // bars: [0, S) full (TMA), [S, 2S) empty (MMA done), [2S, 3S) converted, [3S] accumulator
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * STAGES + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 2);
+    const uint32_t bar_base = base + S::kRing;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + S::kRing);
+    // bars: [0, S) full (TMA), [S, 2S) empty (MMA done), [2S, 3S) converted, [3S] accumulator,
+    // [3S + 1] split-k partials received
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * STAGES + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 3);
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
     auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
     auto conv_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + s); };
     const uint32_t accum_bar = bar_base + 8u * (3 * STAGES);
+    const uint32_t recv_bar = bar_base + 8u * (3 * STAGES + 1);
+    const uint32_t recv_base = bar_base + S::kBars;
+    // Split k: the CTAs of a tile's cluster each own one band of the tile's rows.
+    const int splits = SPLIT ? p.splits : 1;
+    const int rank = SPLIT ? (int)cooperative_groups::this_cluster().block_rank() : 0;
+    const int band = (BM + splits - 1) / splits;
+    const int r_begin = rank * band, r_end = min(BM, r_begin + band);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -190,20 +205,30 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
     const int kb0 = blockIdx.y * p.kb_per_split;
     const int num_kb = max(0, min(num_kb_total, kb0 + p.kb_per_split) - kb0);
 
-    // TMA loads of one stage (the producer's job).
-    auto issue = [&](int i) {
+    // TMA loads of one stage (the producer's job): issue_b arms the stage's barrier for all
+    // of the stage's bytes and loads B, issue_a loads A.
+    auto issue_a = [&](int i) {
+        const int s = i % STAGES;
+        const uint32_t st = base + s * S::kStage;
+        const int kx = (kb0 + i) * BK;
+        tma_load_2d(st, &map_a0, full_bar(s), kx, m0);
+        if (!A_RAW) tma_load_2d(st + S::kATile, &map_a1, full_bar(s), kx, m0);
+    };
+    auto issue_b = [&](int i) {
         const int s = i % STAGES;
         const uint32_t st = base + s * S::kStage;
         mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
         const int kx = (kb0 + i) * BK;
-        tma_load_2d(st, &map_a0, full_bar(s), kx, m0);
-        if (!A_RAW) tma_load_2d(st + S::kATile, &map_a1, full_bar(s), kx, m0);
         tma_load_2d(st + 2 * S::kATile, &map_bhi, full_bar(s), kx, n0);
         tma_load_2d(st + 2 * S::kATile + S::kBTile, &map_blo, full_bar(s), kx, n0);
         if (NB == 2) {
             tma_load_2d(st + 2 * S::kATile + 2 * S::kBTile, &map_b2hi, full_bar(s), kx, n0);
             tma_load_2d(st + 2 * S::kATile + 3 * S::kBTile, &map_b2lo, full_bar(s), kx, n0);
         }
+    };
+    auto issue = [&](int i) {
+        issue_b(i);
+        issue_a(i);
     };
 
     if (threadIdx.x == 0) {
@@ -213,21 +238,37 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
             mbar_init(conv_bar(s), 128);
         }
         mbar_init(accum_bar, 1);
+        if (SPLIT) mbar_init(recv_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
-        // The first stages are free: start their loads before the set-up barrier so that the
-        // memory latency overlaps TMEM allocation.
-        for (int i = 0; i < min(STAGES, num_kb); i++) issue(i);
+        // Arm the receive barrier for the other CTAs' partial rows of this CTA's band.
+        if (SPLIT) mbar_arrive_expect_tx(recv_bar, (uint32_t)(NB * (splits - 1) * (r_end - r_begin) * S::kLd * 4));
+        // A stable prepared weight is read by no earlier kernel's writes: its first stages
+        // load while the previous kernel of the stream is still finishing.
+        if (p.b_early)
+            for (int i = 0; i < min(STAGES, num_kb); i++) issue_b(i);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32((const void*)tmem_slot), S::kTmemCols);
         tmem_relinquish();
     }
+    // Cluster barrier, phase 1 (arrive now, wait in the epilogue): every CTA's receive
+    // barrier is initialised and armed before any CTA sends to it.
+    if (SPLIT) cluster_arrive();
+    pdl_enter();
+    if (threadIdx.x == 0) {
+        // The first stages are free: start their loads before the set-up barrier so that the
+        // memory latency overlaps the rest of the set-up.
+        for (int i = 0; i < min(STAGES, num_kb); i++) {
+            if (!p.b_early) issue_b(i);
+            issue_a(i);
+        }
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    float* staged = reinterpret_cast<float*>(base_ptr);  // [NB][BM][kLd] once the ring has drained
+    bool acc_ready = false;  // warps 2-5: the accumulator is complete and valid
 
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------------
@@ -314,67 +355,104 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
             }
         }
     } else {
-        // ---- epilogue, part 1: warps 2..5 stage their TMEM lane quarter (warp % 4) ------
-        const int q = warp % 4;
+        // ---- warps 2..5: wait for the accumulator ------------------------------------------
         const bool waited = mbar_wait(accum_bar, 0);
         if (!waited) atomicExch(p.error, 1);
-        tc_fence_after();
         // tcgen05.ld is warp-collective: the whole warp reads the accumulator or none of it.
-        const bool ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_kb > 0);
+        acc_ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_kb > 0);
+    }
+
+    // ---- epilogue ------------------------------------------------------------------------
+    // Warps 2-5 read their TMEM lane quarter and stage the tile in the drained ring
+    // ([NB][BM][kLd]).  With split k, one thread then sends each band of the staged rows to the
+    // CTA that owns it with one bulk copy into that CTA's receive slot for this split
+    // (completing on the owner's receive barrier); each CTA sums its band's partials in split
+    // order 0, 1, ... (deterministic) and writes the finished rows with coalesced stores, bias /
+    // residual / SwiGLU applied.  The partial sums never leave the chip.
+    if (warp >= 2 && warp < 6) {
+        tc_fence_after();
+        const int q = warp % 4;
         const int r = q * 32 + lane;  // this thread's row of the tile
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
 #pragma unroll
             for (int z = 0; z < NB; z++) {
                 float v[32];
-                if (ready) {
+                if (acc_ready) {
                     tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(z * BN + c0), v);
                     tc_wait_ld();
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] = 0.0f;
                 }
-                float* dst = staged + (size_t)z * BM * S::kLd + (size_t)r * S::kLd + c0;
+                const uint32_t dst = base + (uint32_t)(((z * BM + r) * S::kLd + c0) * 4);
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int j = 0; j < 32; j += 4) sts4(dst + 4 * j, v[j], v[j + 1], v[j + 2], v[j + 3]);
             }
         }
+        if (SPLIT) fence_proxy_async();  // the staged rows are read by bulk copies next
     }
-
-    // ---- epilogue, part 2: every thread of the cluster reduces one band of rows ----------
-    cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
     tc_fence_before();
     __syncthreads();
-    cluster.sync();  // every CTA of the tile has staged its partial tile
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::kTmemCols);
+    }
+    if (SPLIT) {
+        cluster_wait();  // phase 1: every receive barrier of the cluster is armed
+        if (threadIdx.x == 64) {
+            for (int b = 0; b < splits; b++) {
+                if (b == rank) continue;
+                const int b_begin = b * band, b_rows = min(BM, b_begin + band) - b_begin;
+#pragma unroll
+                for (int z = 0; z < NB; z++) {
+                    const uint32_t src = base + (uint32_t)((z * BM + b_begin) * S::kLd * 4);
+                    const uint32_t dst = recv_base + (uint32_t)(((z * splits + rank) * band) * S::kLd * 4);
+                    bulk_copy_to_cluster(mapa(dst, (uint32_t)b), src, (uint32_t)(b_rows * S::kLd * 4),
+                                         mapa(recv_bar, (uint32_t)b));
+                }
+            }
+        }
+        if (!mbar_wait(recv_bar, 0)) atomicExch(p.error, 1);
+        cluster_arrive();  // phase 2: every copy into this CTA has landed
+    }
+    // Address of row lr of this CTA's band, column c, term z, in split s's partial.
+    auto part_at = [&](int z, int s, int lr, int c) -> uint32_t {
+        return s == rank ? base + (uint32_t)(((z * BM + r_begin + lr) * S::kLd + c) * 4)
+                         : recv_base + (uint32_t)((((z * splits + s) * band + lr) * S::kLd + c) * 4);
+    };
     {
-        const int splits = (int)cluster.num_blocks();
-        const int rank = (int)cluster.block_rank();
-        const float* src[8][NB];
-#pragma unroll
-        for (int s = 0; s < 8; s++)
-#pragma unroll
-            for (int z = 0; z < NB; z++)
-                src[s][z] = s < splits ? cluster.map_shared_rank(staged + (size_t)z * BM * S::kLd, (unsigned)s) : nullptr;
-        const int band = (BM + splits - 1) / splits;
-        const int r_begin = rank * band, r_end = min(BM, r_begin + band);
         constexpr int kVec = BN / 4;  // float4 per row
         const bool vec = (p.n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
                          (p.addend_mode == 0 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0);
         for (int e = threadIdx.x; e < (r_end - r_begin) * kVec; e += blockDim.x) {
-            const int lr = r_begin + e / kVec, c4 = (e % kVec) * 4;
-            const uint64_t row = (uint64_t)m0 + lr, col = (uint64_t)n0 + c4;
+            const int lr = e / kVec, c4 = (e % kVec) * 4;
+            const uint64_t row = (uint64_t)m0 + r_begin + lr, col = (uint64_t)n0 + c4;
             if (row >= p.m || col >= p.n) continue;
+            const bool full4 = vec && col + 4 <= p.n;
+            // The addend's global load goes out first, so that its latency overlaps the
+            // shared-memory loads below.
+            float4 add4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (full4 && p.addend_mode == 1) add4 = *reinterpret_cast<const float4*>(p.addend + col);
+            else if (full4 && p.addend_mode == 2) add4 = *reinterpret_cast<const float4*>(p.addend + row * p.n + col);
+            float4 t[NB][kMaxSplits];
+#pragma unroll
+            for (int z = 0; z < NB; z++)
+#pragma unroll
+                for (int s = 0; s < kMaxSplits; s++)
+                    if (s < splits) t[z][s] = lds4(part_at(z, s, lr, c4));
             float4 acc[NB];
 #pragma unroll
             for (int z = 0; z < NB; z++) {
-                acc[z] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int s = 0; s < splits; s++) {
-                    const float4 t = *reinterpret_cast<const float4*>(src[s][z] + (size_t)lr * S::kLd + c4);
-                    acc[z].x += t.x;
-                    acc[z].y += t.y;
-                    acc[z].z += t.z;
-                    acc[z].w += t.w;
+                acc[z] = t[z][0];
+#pragma unroll
+                for (int s = 1; s < kMaxSplits; s++) {
+                    if (s < splits) {
+                        acc[z].x += t[z][s].x;
+                        acc[z].y += t[z][s].y;
+                        acc[z].z += t[z][s].z;
+                        acc[z].w += t[z][s].w;
+                    }
                 }
             }
             float o[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
@@ -384,32 +462,23 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW>::kThreads, 1)
                 for (int j = 0; j < 4; j++) o[j] = (o[j] * (1.0f / (1.0f + expf(-o[j])))) * u[j];
             }
             float* orow = p.out + row * p.n;
-            if (vec && col + 4 <= p.n) {
-                if (p.addend_mode == 1) {
-                    const float4 b = *reinterpret_cast<const float4*>(p.addend + col);
-                    o[0] += b.x, o[1] += b.y, o[2] += b.z, o[3] += b.w;
-                } else if (p.addend_mode == 2) {
-                    const float4 b = *reinterpret_cast<const float4*>(p.addend + row * p.n + col);
-                    o[0] += b.x, o[1] += b.y, o[2] += b.z, o[3] += b.w;
-                }
+            if (full4) {
+                if (p.addend_mode != 0) o[0] += add4.x, o[1] += add4.y, o[2] += add4.z, o[3] += add4.w;
                 *reinterpret_cast<float4*>(orow + col) = make_float4(o[0], o[1], o[2], o[3]);
             } else {
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     if (col + j >= p.n) break;
-                    float s = o[j];
-                    if (p.addend_mode == 1) s += p.addend[col + j];
-                    else if (p.addend_mode == 2) s += p.addend[row * p.n + col + j];
-                    orow[col + j] = s;
+                    float sum = o[j];
+                    if (p.addend_mode == 1) sum += p.addend[col + j];
+                    else if (p.addend_mode == 2) sum += p.addend[row * p.n + col + j];
+                    orow[col + j] = sum;
                 }
             }
         }
     }
-    cluster.sync();  // the peers have finished reading this CTA's staged tile
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, S::kTmemCols);
-    }
+    // Phase 2: every copy out of this CTA's shared memory has landed before the CTA exits.
+    if (SPLIT) cluster_wait();
 }
 
 // ---- host side ---------------------------------------------------------------------------------
@@ -453,57 +522,84 @@ mg_status split_operand(Device* d, const float* src, uint64_t rows, uint64_t k, 
                         uint64_t kp) {
     if (kmajor) {
         const int vec = k == kp && k % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
-        split_rows_kernel<<<grid_cap(d, vec ? rows * kp / 4 : rows * kp), 256, 0, d->stream>>>(src, k, rows, k, hi, lo,
+        enqueue(d, split_rows_kernel, grid_cap(d, vec ? rows * kp / 4 : rows * kp), 256, 0, src, k, rows, k, hi, lo,
                                                                                               kp, vec);
     } else {
         dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((kp + 63) / 64));
         if (grid.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "matmul inner dimension %llu is too large", (unsigned long long)k);
-        split_transpose_kernel<<<grid, 256, 0, d->stream>>>(src, k, rows, hi, lo, kp);
+        enqueue(d, split_transpose_kernel, grid, 256, 0, src, k, rows, hi, lo, kp);
     }
     return launched(d, "operand split kernel launch");
 }
 
-template <int BN, int NB, int STAGES, bool A_RAW>
-mg_status launch_tc(Device* d, const TcParams& p, const CUtensorMap* maps) {
-    using S = TcShape<BN, NB, STAGES, A_RAW>;
+template <int BN, int NB, int STAGES, bool A_RAW, bool SPLIT>
+mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
+    using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT>;
     static_assert(S::kSmem <= 227 * 1024, "shared memory budget");
+    auto kernel = gemm_tc_kernel<BN, NB, STAGES, A_RAW, SPLIT>;
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
-        MG_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, NB, STAGES, A_RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     S::kSmem),
+        MG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
                 "configuring the tensor-core matmul");
         configured[d->ordinal & 63] = true;
     }
     const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
     if (tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "matmul has too many output tiles");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits, 1);
     cfg.blockDim = dim3(S::kThreads, 1, 1);
     cfg.dynamicSmemBytes = S::kSmem;
     cfg.stream = d->stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = (unsigned)p.splits;  // the k splits of one tile share a cluster
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    MG_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, NB, STAGES, A_RAW>, maps[0], maps[1], maps[2], maps[3], maps[4],
-                               maps[5], p),
+    if (SPLIT) {
+        // Keep the clusters to one wave: fewer splits when the GPCs cannot hold `tiles`
+        // clusters of this size at once (queried once per cluster size).
+        static int max_clusters[kMaxSplits + 1] = {0};
+        const int num_kb = (int)((p.k + BK - 1) / BK);
+        while (p.splits > 2) {
+            int& mc = max_clusters[p.splits];
+            if (mc == 0) {
+                attr[0].val.clusterDim.y = (unsigned)p.splits;
+                cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits, 1);
+                cfg.numAttrs = 1;
+                if (cudaOccupancyMaxActiveClusters(&mc, kernel, &cfg) != cudaSuccess || mc <= 0) {
+                    (void)cudaGetLastError();
+                    mc = 1 << 30;  // unknown: assume it fits
+                }
+            }
+            if ((uint64_t)mc >= tiles) break;
+            p.splits--;
+            p.kb_per_split = (num_kb + p.splits - 1) / p.splits;
+            p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
+        }
+    }
+    attr[0].val.clusterDim.y = (unsigned)p.splits;  // the k splits of one tile share a cluster
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits, 1);
+    cfg.numAttrs = d->pdl ? 2 : 1;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p),
             "tensor-core matmul launch");
     return launched(d, "tensor-core matmul launch");
 }
 
+// Ring depth per tile width: as deep as the shared memory allows, with the split-k receive
+// slots taking their share when k is split.
 template <int NB, bool A_RAW>
 mg_status launch_bn(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
+    const bool split = p.splits > 1;
     if constexpr (NB == 2) {
-        if (bn == 128) return launch_tc<128, NB, 2, A_RAW>(d, p, maps);
-        if (bn == 64) return launch_tc<64, NB, 3, A_RAW>(d, p, maps);
-        return launch_tc<32, NB, 4, A_RAW>(d, p, maps);
+        if (bn == 128 && !split) return launch_tc<128, NB, 2, A_RAW, false>(d, p, maps);
+        if (bn == 64) return split ? launch_tc<64, NB, 2, A_RAW, true>(d, p, maps) : launch_tc<64, NB, 3, A_RAW, false>(d, p, maps);
+        if (bn == 32) return split ? launch_tc<32, NB, 3, A_RAW, true>(d, p, maps) : launch_tc<32, NB, 4, A_RAW, false>(d, p, maps);
+        return fail(MG_EXECUTION_FAILED, "gated matmul tile width %d with split k", bn);
     } else {
-        if (bn == 128) return launch_tc<128, NB, 3, A_RAW>(d, p, maps);
-        if (bn == 64) return launch_tc<64, NB, 4, A_RAW>(d, p, maps);
-        return launch_tc<32, NB, 5, A_RAW>(d, p, maps);
+        if (bn == 128) return split ? launch_tc<128, NB, 2, A_RAW, true>(d, p, maps) : launch_tc<128, NB, 3, A_RAW, false>(d, p, maps);
+        if (bn == 64) return split ? launch_tc<64, NB, 3, A_RAW, true>(d, p, maps) : launch_tc<64, NB, 4, A_RAW, false>(d, p, maps);
+        return split ? launch_tc<32, NB, 4, A_RAW, true>(d, p, maps) : launch_tc<32, NB, 5, A_RAW, false>(d, p, maps);
     }
 }
 
@@ -565,7 +661,7 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
             blo[z] = lo;
         }
     }
-    const int bn = pick_bn(d, g.m, g.n);
+    int bn = pick_bn(d, g.m, g.n);
     TcParams p;
     p.out = g.out;
     p.addend = g.addend;
@@ -573,21 +669,31 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
     p.m = g.m;
     p.n = g.n;
     p.k = g.k;
-    p.tiles_m = (int)((g.m + BM - 1) / BM);
-    p.tiles_n = (int)((g.n + bn - 1) / bn);
     p.error = d->flags + 2;
-    // Split k when the output grid leaves SMs idle, keeping at least 2 k-blocks per split.
+    p.b_early = g.b_stable && g.b_prep[0] && (nb == 1 || g.b_prep[1]) ? 1 : 0;
+    // Split k when the output grid leaves SMs idle: as many splits as fit in one wave, at
+    // least 2 k-blocks each.  A gated split-k tile is at most 64 wide (its receive slots
+    // share the shared memory with the ring).
     const int num_kb = (int)((g.k + BK - 1) / BK);
-    const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
-    int splits = 1;
-    if (tiles < (uint64_t)d->sm_count && num_kb >= 4) {
-        splits = (int)((d->sm_count + tiles - 1) / tiles);
-        if (splits > num_kb / 2) splits = num_kb / 2;
-        if (splits > kMaxSplits) splits = kMaxSplits;  // a portable cluster holds 8 CTAs
-        if (splits < 1) splits = 1;
+    auto plan_splits = [&](int width) {
+        p.tiles_m = (int)((g.m + BM - 1) / BM);
+        p.tiles_n = (int)((g.n + width - 1) / width);
+        const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
+        int splits = 1;
+        if (tiles * 2 <= (uint64_t)d->sm_count && num_kb >= 4) {
+            splits = (int)((uint64_t)d->sm_count / tiles);
+            if (splits > num_kb / 2) splits = num_kb / 2;
+            if (splits > kMaxSplits) splits = kMaxSplits;  // a portable cluster holds 8 CTAs
+            if (splits < 1) splits = 1;
+        }
+        p.kb_per_split = (num_kb + splits - 1) / splits;
+        p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
+    };
+    plan_splits(bn);
+    if (nb == 2 && bn == 128 && p.splits > 1) {
+        bn = 64;
+        plan_splits(bn);
     }
-    p.kb_per_split = (num_kb + splits - 1) / splits;
-    p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
     CUtensorMap maps[6];
     if (a_raw) {
         MG_TRY(make_map(&maps[0], ahi, g.m, g.k, g.k, BM));

@@ -40,6 +40,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_partial_kernel(const float* 
                                                                     float* __restrict__ partial, uint64_t m,
                                                                     uint64_t n, uint64_t k, uint64_t slice_len,
                                                                     int transpose_a) {
+    pdl_enter();
     extern __shared__ float smem[];
     float* a_s = smem;                      // [M][slice_len]
     float* red = smem + M * slice_len;      // [kWarps][kCols]
@@ -137,6 +138,7 @@ __global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restric
                                                           uint64_t m, uint64_t n, uint64_t slices,
                                                           const float* __restrict__ addend, int addend_mode,
                                                           int gated) {
+    pdl_enter();
     const uint64_t total = m * n;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         float s = 0.0f;
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restric
 
 template <int M>
 void launch_partial(Device* d, dim3 grid, size_t smem, const k::GemmArgs& g, float* partial, uint64_t slice_len) {
-    gemv_partial_kernel<M><<<grid, kWarps * 32, smem, d->stream>>>(g.a, g.b, g.b2, partial, g.m, g.n, g.k, slice_len,
+    enqueue(d, gemv_partial_kernel<M>, grid, kWarps * 32, smem, g.a, g.b, g.b2, partial, g.m, g.n, g.k, slice_len,
                                                                    g.transpose_a);
 }
 
@@ -190,6 +192,7 @@ template <int M>
 __global__ void __launch_bounds__((kWarps + 1) * 32) gemv_tma_kernel(const __grid_constant__ CUtensorMap map_b,
                                                                       const __grid_constant__ CUtensorMap map_b2,
                                                                       GemvTmaArgs p) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     using namespace sm100;
     __shared__ unsigned int s_last;
@@ -388,7 +391,7 @@ mg_status launch_tma(Device* d, dim3 grid, size_t smem, const CUtensorMap* maps,
     p.transpose_a = g.transpose_a;
     p.error = d->flags + 2;
     p.counters = d->counters;
-    gemv_tma_kernel<M><<<grid, (kWarps + 1) * 32, smem, d->stream>>>(maps[0], maps[1], p);
+    enqueue(d, gemv_tma_kernel<M>, grid, (kWarps + 1) * 32, smem, maps[0], maps[1], p);
     return launched(d, "gemv kernel launch");
 }
 
@@ -458,7 +461,7 @@ mg_status gemv(Device* d, const GemmArgs& g) {
     uint64_t total = g.m * g.n;
     uint64_t blocks = (total + 255) / 256;
     if (blocks > (uint64_t)d->sm_count * 8) blocks = (uint64_t)d->sm_count * 8;
-    gemv_reduce_kernel<<<(unsigned)(blocks ? blocks : 1), 256, 0, d->stream>>>(partial, g.out, g.m, g.n, slices,
+    enqueue(d, gemv_reduce_kernel, (unsigned)(blocks ? blocks : 1), 256, 0, partial, g.out, g.m, g.n, slices,
                                                                               g.addend, g.addend_mode, g.gated);
     return launched(d, "gemv reduce kernel launch");
 }

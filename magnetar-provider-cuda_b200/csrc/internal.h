@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <set>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/magnetar_cuda.h"
@@ -52,6 +53,9 @@ struct Device {
     // between kernels: the finishing CTA resets its entry).
     unsigned int* counters = nullptr;
     bool capturing = false;
+    // Programmatic dependent launch between the provider's kernels (on unless the environment
+    // sets MAGNETAR_CUDA_PDL=0).
+    bool pdl = true;
     // Workspaces grown on demand (see scratch()); freed in stream order.
     void* scratch_ptr[8] = {nullptr};
     size_t scratch_bytes[8] = {0};
@@ -152,6 +156,9 @@ struct GemmArgs {
     int gated;
     // Prepared tensor-core forms of b / b2 (K-major tf32 hi, lo: [n, kp]); null = split per call.
     const float* b_prep[2];
+    // The prepared forms existed before this call: no kernel earlier in the stream writes
+    // them, so the GEMM may start loading them before it waits on its predecessor.
+    int b_stable;
 };
 mg_status gemm(Device* d, const GemmArgs& g);
 // Round-up of k the tensor-core path stores operands with.
@@ -182,6 +189,41 @@ inline mg_status launched(Device* d, const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return from_cuda(e, what);
     return MG_OK;
+}
+
+// ---- programmatic dependent launch --------------------------------------------------------
+// A chain of small kernels (a decoder layer) spends much of its time between kernels: the
+// next grid is scheduled only after the previous one has drained.  Kernels launched through
+// enqueue() may instead be scheduled while the previous kernel of the stream still runs; each
+// of them starts with pdl_enter(), which waits until the kernels it depends on have completed
+// and their memory is visible, and only then lets the next kernel of the stream be scheduled.
+// Before pdl_enter() a kernel reads no global memory that an earlier kernel may write (a
+// prepared weight is the one exception taken), writes none, and may allocate tensor memory
+// only if every kernel using tensor memory does so before its own pdl_enter(): the next grid
+// is scheduled only after every CTA of this one has passed pdl_enter(), so each CTA that
+// waits for tensor memory waits on a grid that is already running and never on its successor.
+// Kernels launched without the attribute pass pdl_enter() at once.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#endif
+
+// Enqueues `kernel` on the device stream (a launch failure is left for launched() to read).
+template <typename... KArgs, typename... Args>
+inline void enqueue(Device* d, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = d->pdl ? 1 : 0;
+    (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace mg

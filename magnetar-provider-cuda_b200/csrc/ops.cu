@@ -115,7 +115,8 @@ mg_status half_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_b
 enum AddendMode { kNone = 0, kRow = 1, kFull = 2 };
 
 // The prepared tensor-core operand form of a weight read as matmul B, built on first use.
-mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int transposed, const float** out) {
+mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int transposed, const float** out,
+                      bool* built) {
     *out = nullptr;
     if (!cb || !cb->is_weight) return MG_OK;
     Buffer* b = const_cast<Buffer*>(cb);  // the prepared form is a cache of the buffer's contents
@@ -123,6 +124,7 @@ mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int t
         *out = b->prep;
         return MG_OK;
     }
+    *built = true;
     buffer_drop_prep(b);
     const uint64_t kp = k::gemm_kp(k);
     void* mem = nullptr;
@@ -186,7 +188,7 @@ mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
     const uint64_t shape[2] = {m, n};
     Buffer* o;
     MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
-    k::GemmArgs g;
+    k::GemmArgs g{};
     g.a = (const float*)a->ptr;
     g.b = (const float*)b->ptr;
     g.b2 = b2 ? (const float*)b2->ptr : nullptr;
@@ -201,8 +203,10 @@ mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
     g.gated = b2 ? 1 : 0;
     g.b_prep[0] = g.b_prep[1] = nullptr;
     if (k::gemm_uses_tensor_cores(m, n, kk, tb, g.b)) {
-        MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0]));
-        if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1]));
+        bool built = false;
+        MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0], &built));
+        if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1], &built));
+        g.b_stable = !built && g.b_prep[0] && (!b2 || g.b_prep[1]);
     }
     return k::gemm(d, g);
 }

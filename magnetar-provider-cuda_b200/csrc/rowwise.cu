@@ -58,6 +58,7 @@ template <int TPR, int VPT>
 __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                           float* __restrict__ out, uint64_t rows, uint64_t cols,
                                                           uint64_t w_stride, float eps) {
+    pdl_enter();
     __shared__ float red[8];
     const int rows_per_cta = 256 / TPR;
     const int sub = threadIdx.x / TPR, t = threadIdx.x % TPR;
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const float* __restric
 __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                              float* __restrict__ out, uint64_t rows, uint64_t cols,
                                                              uint64_t w_stride, float eps) {
+    pdl_enter();
     __shared__ float red[8];
     for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const float* in = x + row * cols;
@@ -172,6 +174,7 @@ __device__ __forceinline__ float2 rope_cs(const RopeK& p, uint64_t row, uint64_t
 }
 
 __global__ void __launch_bounds__(256) rope_kernel(const float* __restrict__ x, float* __restrict__ out, RopeK p) {
+    pdl_enter();
     extern __shared__ float2 cs[];  // [half]
     for (uint64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         __syncthreads();
@@ -247,6 +250,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const float* __restrict__ x, 
 // every head, evaluates the rotation of that float4's pairs once for the row, and applies it
 // to the same float4 of all heads -- each head's 32 float4 form one coalesced 512-byte access.
 __global__ void __launch_bounds__(256) rope_warp_kernel(const float* __restrict__ x, float* __restrict__ out, RopeK p) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * 8;
     const uint64_t hw4 = p.head_width >> 2;
@@ -301,6 +305,7 @@ __global__ void __launch_bounds__(256) rope_warp_kernel(const float* __restrict_
 template <int VPL>
 __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ x, float* __restrict__ out,
                                                            uint64_t rows, uint64_t cols, int* flag) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * 8;
     const uint64_t c4 = cols >> 2;
@@ -346,6 +351,7 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
 
 __global__ void __launch_bounds__(256) softmax_block_kernel(const float* __restrict__ x, float* __restrict__ out,
                                                             uint64_t rows, uint64_t cols, int* flag) {
+    pdl_enter();
     __shared__ float red[8];
     for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const float* in = x + row * cols;
@@ -374,6 +380,7 @@ __global__ void __launch_bounds__(256) embedding_kernel(const float* __restrict_
                                                         float* __restrict__ out, uint64_t dim, uint64_t num_ids,
                                                         uint64_t vocab, int* flag, int has_scale, float scale,
                                                         int vec) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * 8;
     for (uint64_t row = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < num_ids; row += warps) {
@@ -415,14 +422,14 @@ mg_status rmsnorm(Device* d, const float* x, const float* w, float* out, uint64_
                   uint64_t w_stride, float eps) {
     const bool vec = cols % 4 == 0 && a16(x) && a16(out) && (!w || (a16(w) && w_stride % 4 == 0));
     if (!vec) {
-        rmsnorm_scalar_kernel<<<cap_grid(d, rows, 8), 256, 0, d->stream>>>(x, w, out, rows, cols, w_stride, eps);
+        enqueue(d, rmsnorm_scalar_kernel, cap_grid(d, rows, 8), 256, 0, x, w, out, rows, cols, w_stride, eps);
     } else if (cols <= 1024) {
         // a warp per row, up to 8 float4 per lane
-        rmsnorm_vec_kernel<32, 8><<<cap_grid(d, (rows + 7) / 8, 8), 256, 0, d->stream>>>(x, w, out, rows, cols,
+        enqueue(d, rmsnorm_vec_kernel<32, 8>, cap_grid(d, (rows + 7) / 8, 8), 256, 0, x, w, out, rows, cols,
                                                                                           w_stride, eps);
     } else {
         // a CTA per row, up to 8 float4 per thread (rows of up to 8192 read once)
-        rmsnorm_vec_kernel<256, 8><<<cap_grid(d, rows, 8), 256, 0, d->stream>>>(x, w, out, rows, cols, w_stride, eps);
+        enqueue(d, rmsnorm_vec_kernel<256, 8>, cap_grid(d, rows, 8), 256, 0, x, w, out, rows, cols, w_stride, eps);
     }
     return launched(d, "rmsnorm kernel launch");
 }
@@ -453,7 +460,7 @@ mg_status rope(Device* d, const float* x, float* out, const RopeArgs& a) {
     else vec = vec && p.dimension % 4 == 0;
     p.vec = vec ? 1 : 0;
     if (p.vec) {
-        rope_warp_kernel<<<cap_grid(d, (a.rows + 7) / 8, 8), 256, 0, d->stream>>>(x, out, p);
+        enqueue(d, rope_warp_kernel, cap_grid(d, (a.rows + 7) / 8, 8), 256, 0, x, out, p);
         return launched(d, "rope kernel launch");
     }
     size_t smem = p.half * sizeof(float2);
@@ -461,26 +468,26 @@ mg_status rope(Device* d, const float* x, float* out, const RopeArgs& a) {
         MG_CUDA(cudaFuncSetAttribute(rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "configuring rope shared memory");
     }
-    rope_kernel<<<cap_grid(d, a.rows, 8), 256, smem, d->stream>>>(x, out, p);
+    enqueue(d, rope_kernel, cap_grid(d, a.rows, 8), 256, smem, x, out, p);
     return launched(d, "rope kernel launch");
 }
 
 mg_status softmax(Device* d, const float* x, float* out, uint64_t rows, uint64_t cols, int* flag) {
     const bool vec = cols % 4 == 0 && a16(x) && a16(out);
     const unsigned grid = cap_grid(d, (rows + 7) / 8, 8);
-    if (vec && cols <= 128) softmax_warp_kernel<1><<<grid, 256, 0, d->stream>>>(x, out, rows, cols, flag);
-    else if (vec && cols <= 256) softmax_warp_kernel<2><<<grid, 256, 0, d->stream>>>(x, out, rows, cols, flag);
-    else if (vec && cols <= 512) softmax_warp_kernel<4><<<grid, 256, 0, d->stream>>>(x, out, rows, cols, flag);
-    else if (vec && cols <= 1024) softmax_warp_kernel<8><<<grid, 256, 0, d->stream>>>(x, out, rows, cols, flag);
-    else if (vec && cols <= 2048) softmax_warp_kernel<16><<<grid, 256, 0, d->stream>>>(x, out, rows, cols, flag);
-    else softmax_block_kernel<<<cap_grid(d, rows, 8), 256, 0, d->stream>>>(x, out, rows, cols, flag);
+    if (vec && cols <= 128) enqueue(d, softmax_warp_kernel<1>, grid, 256, 0, x, out, rows, cols, flag);
+    else if (vec && cols <= 256) enqueue(d, softmax_warp_kernel<2>, grid, 256, 0, x, out, rows, cols, flag);
+    else if (vec && cols <= 512) enqueue(d, softmax_warp_kernel<4>, grid, 256, 0, x, out, rows, cols, flag);
+    else if (vec && cols <= 1024) enqueue(d, softmax_warp_kernel<8>, grid, 256, 0, x, out, rows, cols, flag);
+    else if (vec && cols <= 2048) enqueue(d, softmax_warp_kernel<16>, grid, 256, 0, x, out, rows, cols, flag);
+    else enqueue(d, softmax_block_kernel, cap_grid(d, rows, 8), 256, 0, x, out, rows, cols, flag);
     return launched(d, "softmax kernel launch");
 }
 
 mg_status embedding(Device* d, const float* table, const float* ids, float* out, uint64_t dim, uint64_t num_ids,
                     uint64_t vocab, int* flag, int has_scale, float scale) {
     int vec = dim % 4 == 0 && a16(table) && a16(out);
-    embedding_kernel<<<cap_grid(d, (num_ids + 7) / 8, 8), 256, 0, d->stream>>>(table, ids, out, dim, num_ids, vocab,
+    enqueue(d, embedding_kernel, cap_grid(d, (num_ids + 7) / 8, 8), 256, 0, table, ids, out, dim, num_ids, vocab,
                                                                                 flag, has_scale, scale, vec);
     return launched(d, "embedding kernel launch");
 }

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -273,6 +274,8 @@ mg_status mg_device_open(int ordinal, mg_device** out) {
     d->sm_count = prop.multiProcessorCount;
     d->sm_major = prop.major;
     d->sm_minor = prop.minor;
+    const char* pdl = getenv("MAGNETAR_CUDA_PDL");
+    d->pdl = !(pdl && pdl[0] == '0');
     cudaError_t e = cudaStreamCreateWithFlags(&d->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         delete d;

@@ -66,6 +66,12 @@ class DeviceBuffer:
         check(N.lib().mg_buffer_reshape(self._h, len(shape), N.shape_array(shape)))
         return self
 
+    def set_weight(self, is_weight: bool = True) -> "DeviceBuffer":
+        """Marks the buffer as a weight (``write_weight_tensor``): a matmul that reads it as B
+        keeps B's tensor-core operand form with it instead of re-deriving it per call."""
+        check(N.lib().mg_buffer_set_weight(self._h, 1 if is_weight else 0))
+        return self
+
     def release(self) -> None:
         if self._h and self._h.value:
             N.lib().mg_buffer_release(self._h)

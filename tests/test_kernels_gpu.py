@@ -329,6 +329,16 @@ ATTN_CASES = [
     dict(seq=384, kv=512, heads=4, kvh=2, d=64, causal=False),
     dict(seq=300, kv=300, heads=2, kvh=1, d=128, causal=True, window=100),
     dict(seq=129, kv=1000, heads=2, kvh=2, d=64, causal=True, key_count=777),
+    # spans too long for the short (span-resident) kernel: tensor-core path with a window,
+    # GQA with a query offset, non-causal
+    dict(seq=300, kv=300, heads=2, kvh=1, d=128, causal=True, window=250),
+    dict(seq=70, kv=420, heads=4, kvh=2, d=64, causal=True),
+    dict(seq=33, kv=400, heads=2, kvh=2, d=64, causal=False),
+    # short kernel: a window over a long sequence, the 384-key capacity, D = 32, D = 128
+    dict(seq=50, kv=300, heads=3, kvh=1, d=64, causal=True, window=40),
+    dict(seq=16, kv=384, heads=2, kvh=2, d=64, causal=True),
+    dict(seq=100, kv=100, heads=2, kvh=2, d=32, causal=True),
+    dict(seq=129, kv=129, heads=2, kvh=2, d=128, causal=False),
 ]
 
 
