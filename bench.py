@@ -52,57 +52,95 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) of the GPU's clocks during the timed region."""
+    """SM clock and clock-event (throttle) reasons of one GPU, polled through NVML every
+    ~2 ms on a background thread while the timed region runs (read-only queries).  Falls back
+    to ``nvidia-smi -lms 200`` when NVML is unavailable."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
+        self.sm, self.reasons, self.max_mhz = [], set(), None
+        self.stop = threading.Event()
+        self.thread = None
         self.proc = None
         self.lines = []
 
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            bus = torch.cuda.get_device_properties(self.gpu).pci_bus_id
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _poll(self, nv, h):
+        flags = [(name, getattr(nv, attr, 0)) for name, attr in self.REASONS]
+        while not self.stop.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                active = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, bit in flags:
+                    if bit and active & bit:
+                        self.reasons.add(name)
+            except Exception:
+                return
+            self.stop.wait(0.002)
+
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
             self.thread.start()
         except Exception:
-            self.proc = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.thread = threading.Thread(target=self._read_smi, daemon=True)
+                self.thread.start()
+            except Exception:
+                self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                self.sm.append(float(parts[1]))
+                self.max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for (name, _), val in zip(self.REASONS, parts[5:9]):
+                if val.lower() == "active":
+                    self.reasons.add(name)
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
-                                 parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.sm),
+                "source": "nvml" if self.proc is None else "nvidia-smi"}
 
 
 def dist_setup():
@@ -382,11 +420,12 @@ def tp_mlp_bench(torch, mpc, kernels, world, rank, steps, warmup, tf32_tflops):
             dist.barrier()
         st = torch.cuda.Event(enable_timing=True)
         en = torch.cuda.Event(enable_timing=True)
-        st.record()
-        for _ in range(steps):
-            group.mlp(dx, dg, du, dd, chunks=4, out=dy)
-        en.record()
-        en.synchronize()
+        with ClockSampler(torch.cuda.current_device()) as clocks:
+            st.record()
+            for _ in range(steps):
+                group.mlp(dx, dg, du, dd, chunks=4, out=dy)
+            en.record()
+            en.synchronize()
         ms = st.elapsed_time(en) / steps
         t = torch.tensor([ms], device="cuda")
         if world > 1:
@@ -399,7 +438,8 @@ def tp_mlp_bench(torch, mpc, kernels, world, rank, steps, warmup, tf32_tflops):
                         "down row-split, one NCCL all-reduce chunked x4 over the down projection",
             "n_gpus": world, "ms_per_step": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
             "tflops": round(flops / (ms * 1e-3) / 1e12, 2),
-            "frac_of_3xtf32_effective_x_n": round(flops / (ms * 1e-3) / 1e12 / (world * tf32_tflops / 3), 4)}
+            "frac_of_3xtf32_effective_x_n": round(flops / (ms * 1e-3) / 1e12 / (world * tf32_tflops / 3), 4),
+            "clocks": clocks.summary()}
 
 
 def run_ours(args, world, rank, local):
@@ -514,7 +554,7 @@ def run_ours(args, world, rank, local):
         node_times.append((inv, ms))
     tf32 = measure_tf32_peak(torch) if rank == 0 else 0.0
     dom_inv, dom_ms = max(node_times, key=lambda x: x[1])
-    roofline = dominant_roofline(cfg, dom_inv, dom_ms, peaks, tf32)
+    roofline = dominant_roofline(cfg, dom_inv, dom_ms, peaks, tf32) if rank == 0 else None
 
     tp_line = None
     if not args.no_tp:

@@ -82,6 +82,7 @@ mg_status mg_comm_init(mg_device* h, int rank, int world, const unsigned char id
         delete c;
         return from_cuda(e, "creating the all-reduce stream");
     }
+    device_ref(c->device);
     *out = c;
     return MG_OK;
 }
@@ -93,7 +94,9 @@ mg_status mg_comm_destroy(mg_comm* c) {
     for (cudaEvent_t ev : c->events) cudaEventDestroy(ev);
     cudaStreamDestroy(c->side);
     if (c->nccl) ncclCommDestroy(c->nccl);
+    Device* d = c->device;
     delete c;
+    device_unref(d);
     return MG_OK;
 }
 

@@ -45,6 +45,11 @@ struct Device {
     int sm_count = 148;
     int sm_major = 10, sm_minor = 0;
     std::atomic<uint64_t> uploads{0}, downloads{0}, launches{0};
+    // The open handle, every live buffer and every communicator hold a reference; the device's
+    // stream, pool and status words go when the last is dropped, so a buffer released after
+    // mg_device_close still frees into a live pool.  A closed device refuses new work.
+    std::atomic<int> refs{1};
+    std::atomic<bool> closed{false};
     // Device-side status words of the data-dependent checks: [0] invalid embedding id,
     // [1] non-finite softmax row.  Pinned host mirror for the read back.
     int* flags = nullptr;
@@ -68,6 +73,10 @@ struct Device {
 
 // Frees the allocations deferred while a capture was recording.
 void flush_deferred_frees(Device* d);
+
+void device_ref(Device* d);
+// Drops one reference; the last one destroys the device.
+void device_unref(Device* d);
 
 mg_status device_check(mg_device* d);
 inline Device* dev(mg_device* d) { return reinterpret_cast<Device*>(d); }

@@ -71,6 +71,7 @@ bool same_shape(const Buffer* a, const Buffer* b) {
 
 mg_status device_check(mg_device* d) {
     if (!d) return fail(MG_INVALID_ARGUMENT, "null device handle");
+    if (dev(d)->closed.load()) return fail(MG_DEVICE_UNAVAILABLE, "the device handle was closed");
     cudaError_t e = cudaSetDevice(dev(d)->ordinal);
     if (e != cudaSuccess) return from_cuda(e, "selecting the device");
     return MG_OK;
@@ -170,6 +171,7 @@ mg_status buffer_new(Device* d, mg_dtype dtype, int rank, const uint64_t* shape,
         delete b;
         return s;
     }
+    device_ref(d);
     *out = b;
     return MG_OK;
 }
@@ -183,9 +185,11 @@ void buffer_drop_prep(Buffer* b) {
 
 void buffer_free(Buffer* b) {
     if (!b) return;
+    Device* d = b->device;
     buffer_drop_prep(b);
-    if (b->owned && b->ptr) device_free(b->device, b->ptr);
+    if (b->owned && b->ptr) device_free(d, b->ptr);
     delete b;
+    device_unref(d);
 }
 
 mg_status output_for(Device* d, mg_dtype dtype, int rank, const uint64_t* shape, mg_buffer** out,
@@ -207,6 +211,21 @@ mg_status output_for(Device* d, mg_dtype dtype, int rank, const uint64_t* shape,
     *out = reinterpret_cast<mg_buffer*>(n);
     *result = n;
     return MG_OK;
+}
+
+void device_ref(Device* d) { d->refs.fetch_add(1); }
+
+void device_unref(Device* d) {
+    if (d->refs.fetch_sub(1) != 1) return;
+    cudaSetDevice(d->ordinal);
+    cudaStreamSynchronize(d->stream);
+    cudaStreamSynchronize(d->own_stream);
+    cudaFree(d->flags);
+    cudaFree(d->counters);
+    cudaFreeHost(d->host_flags);
+    cudaMemPoolDestroy(d->pool);
+    cudaStreamDestroy(d->own_stream);
+    delete d;
 }
 
 }  // namespace mg
@@ -315,18 +334,13 @@ mg_status mg_device_open(int ordinal, mg_device** out) {
 mg_status mg_device_close(mg_device* h) {
     if (!h) return MG_OK;
     Device* d = dev(h);
+    if (d->closed.exchange(true)) return MG_OK;
     cudaSetDevice(d->ordinal);
     d->capturing = false;
     flush_deferred_frees(d);
     scratch_release(d);
     cudaStreamSynchronize(d->stream);
-    cudaStreamSynchronize(d->own_stream);
-    cudaFree(d->flags);
-    cudaFree(d->counters);
-    cudaFreeHost(d->host_flags);
-    cudaMemPoolDestroy(d->pool);
-    cudaStreamDestroy(d->own_stream);
-    delete d;
+    device_unref(d);  // the handle's reference: the device goes with its last buffer
     return MG_OK;
 }
 
@@ -395,6 +409,7 @@ mg_status mg_buffer_zeros(mg_device* h, mg_dtype dtype, int rank, const uint64_t
 
 mg_status mg_buffer_wrap(mg_device* h, mg_dtype dtype, int rank, const uint64_t* shape, void* ptr, mg_buffer** out) {
     if (!h || !out || (rank > 0 && !shape)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    MG_TRY(device_check(h));
     if (rank < 0 || rank > MG_MAX_RANK) return fail(MG_SHAPE_UNSUPPORTED, "rank %d is outside 0..%d", rank, MG_MAX_RANK);
     uint64_t count;
     if (!shape_count(rank, shape, &count)) return fail(MG_SHAPE_UNSUPPORTED, "element count overflows");
@@ -407,6 +422,7 @@ mg_status mg_buffer_wrap(mg_device* h, mg_dtype dtype, int rank, const uint64_t*
     b->count = count;
     b->ptr = ptr;
     b->owned = false;
+    device_ref(b->device);
     *out = reinterpret_cast<mg_buffer*>(b);
     return MG_OK;
 }

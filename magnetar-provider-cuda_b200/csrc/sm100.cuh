@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the tensor-core kernels use: mbarriers,
-// TMA tiled loads (no multicast anywhere in this library), tcgen05 TMEM allocation, MMA,
+// TMA tiled loads (each to this CTA alone), tcgen05 TMEM allocation, MMA,
 // commit and loads.  Every wait is bounded: it gives up after kWaitNs of global time and
 // reports the timeout so that a kernel can record an error and leave instead of hanging.
 #pragma once
@@ -96,11 +96,6 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
-}
-// Store into another CTA's shared memory (an address from mapa).
-__device__ __forceinline__ void st_cluster4(uint32_t addr, float a, float b, float c, float d) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
 }
 
 // ---- thread-block cluster ---------------------------------------------------------------------

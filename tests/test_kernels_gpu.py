@@ -409,3 +409,21 @@ def test_gemm_sweep_full_size_linearity(kernels):
     # and a row sample against float64
     exp = a[:8].astype(np.float64) @ (b1 + b2).astype(np.float64)
     assert rel(lhs[:8], exp) <= TOL_MATMUL
+
+
+def test_buffers_outlive_a_closed_device(mpc):
+    # A buffer released after its device handle was closed frees into the still-live pool,
+    # and the closed handle refuses new work with DeviceUnavailable instead of crashing.
+    import ctypes
+    import importlib
+    N = importlib.import_module("magnetar-provider-cuda_b200._native")
+    unavailable = [c for c, name in N.STATUS_NAMES.items() if name == "DeviceUnavailable"][0]
+    k = mpc.CudaKernels(0)
+    a = k.upload(np.ones((4, 4), np.float32))
+    b = k.add(a, a)
+    stale = ctypes.c_void_p(k.handle.value)
+    k.close()
+    out = ctypes.c_void_p()
+    assert N.lib().mg_add(stale, a.handle, b.handle, ctypes.byref(out)) == unavailable
+    a.release()
+    b.release()  # the last reference: the device goes now
