@@ -18,6 +18,7 @@ host cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import importlib
 import json
 import math
@@ -73,14 +74,26 @@ class ClockSampler:
         self.lines = []
 
     def _nvml_handle(self):
+        """The NVML handle of CUDA device ``self.gpu``, matched by PCI bus id (the CUDA and
+        NVML orders can differ); by index when the id is unavailable."""
         import pynvml
         import torch
         pynvml.nvmlInit()
-        try:
-            bus = torch.cuda.get_device_properties(self.gpu).pci_bus_id
-            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-        except Exception:
-            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
+        def norm(bus):  # "0000:1B:00.0" / "00000000:1b:00.0" -> "1b:00.0"
+            if isinstance(bus, bytes):
+                bus = bus.decode()
+            return str(bus).lower().split(":", 1)[-1] if str(bus).count(":") == 2 else str(bus).lower()
+
+        props = torch.cuda.get_device_properties(self.gpu)
+        bus, dev = getattr(props, "pci_bus_id", None), getattr(props, "pci_device_id", None)
+        want = f"{bus:02x}:{dev:02x}.0" if isinstance(bus, int) and isinstance(dev, int) else norm(bus or "")
+        if want:
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                if norm(pynvml.nvmlDeviceGetPciInfo(h).busId) == want:
+                    return pynvml, h
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def _poll(self, nv, h):
         flags = [(name, getattr(nv, attr, 0)) for name, attr in self.REASONS]
@@ -603,6 +616,13 @@ def run_ours(args, world, rank, local):
         torch.distributed.destroy_process_group()
 
 
+# DRAM bytes (read + write) per launch of each layer node, from one ncu capture of this bench
+# command (dram__bytes_read.sum + dram__bytes_write.sum; the decoder-layer summary in profiles/),
+# keyed by the node's output id.  Writes stay in the L2 at this size.
+LAYER_NODE_TRAFFIC = {"x": 275712, "h": 285184, "q": 2393344, "k": 2393344, "v": 2393088, "qr": 318208,
+                      "kr": 318208, "a": 821248, "x2": 2655488, "h2": 285184, "g": 11577344, "out": 6636544}
+
+
 def dominant_roofline(cfg, inv, ms, peaks, tf32):
     """Roofline object of the layer's slowest node (algorithmic work per launch / time)."""
     s, h, f, d, H = cfg.seq, cfg.hidden, cfg.ffn, cfg.head_dim, cfg.heads
@@ -614,16 +634,19 @@ def dominant_roofline(cfg, inv, ms, peaks, tf32):
         eff = tf32 / 3.0
         ach = flops[inv.kernel] / (ms * 1e-3) / 1e12
         return {"kernel": inv.kernel, "bound": "tensor", "achieved": round(ach, 3), "peak": round(eff, 1),
-                "unit": "TFLOP/s", "frac": round(ach / eff, 5), "traffic": None,
-                "peak_basis": "3xTF32-effective = measured cuBLAS TF32 / 3 (of measured)"}
+                "unit": "TFLOP/s", "frac": round(ach / eff, 5), "traffic": LAYER_NODE_TRAFFIC.get(inv.output),
+                "peak_basis": "3xTF32-effective = measured cuBLAS TF32 / 3 (of measured)",
+                "node": inv.output, "ms": round(ms, 5)}
     bytes_ = {"embedding": s * h * 4 * 2 + s * 4, "rmsnorm": 2 * s * h * 4 + h * 4, "rope": 2 * s * h * 4}
     b = bytes_.get(inv.kernel, 2 * s * h * 4)
     ach = b / (ms * 1e-3) / 1e9
     return {"kernel": inv.kernel, "bound": "hbm", "achieved": round(ach, 2), "peak": peaks["hbm_gbs"],
-            "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 5), "traffic": None}
+            "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 5), "traffic": LAYER_NODE_TRAFFIC.get(inv.output),
+            "node": inv.output, "ms": round(ms, 5)}
 
 
 def main():
+    faulthandler.enable()  # a native crash prints every thread's Python stack
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

@@ -5,7 +5,7 @@
  * `CudaExecutor` (src/executor.rs:2244-2565) over launch wrappers `CudaKernels::<op>`
  * (src/kernels.rs:794-7132) that JIT-compile src/kernels.cu with NVRTC.  Here the kernels
  * are precompiled sm_100a code and every entry point below is a plain C function a Rust
- * `extern "C"` block binds directly (see INTEGRATION.md).
+ * `extern "C"` block binds directly.
  *
  * Conventions
  *  - Every function returns an mg_status; MG_OK is 0.  On failure the calling thread's

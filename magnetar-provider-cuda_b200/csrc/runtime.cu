@@ -218,8 +218,7 @@ void device_ref(Device* d) { d->refs.fetch_add(1); }
 void device_unref(Device* d) {
     if (d->refs.fetch_sub(1) != 1) return;
     cudaSetDevice(d->ordinal);
-    cudaStreamSynchronize(d->stream);
-    cudaStreamSynchronize(d->own_stream);
+    cudaStreamSynchronize(d->own_stream);  // the device's stream since mg_device_close
     cudaFree(d->flags);
     cudaFree(d->counters);
     cudaFreeHost(d->host_flags);
@@ -340,6 +339,9 @@ mg_status mg_device_close(mg_device* h) {
     flush_deferred_frees(d);
     scratch_release(d);
     cudaStreamSynchronize(d->stream);
+    // A stream the caller bound (mg_device_set_stream) may be destroyed once the handle is
+    // closed: buffers released later free on the device's own stream.
+    d->stream = d->own_stream;
     device_unref(d);  // the handle's reference: the device goes with its last buffer
     return MG_OK;
 }
