@@ -136,7 +136,13 @@ struct TcParams {
     int* error;        // device word set when a wait times out
 };
 
-template <int BN, int NB, int STAGES, bool A_RAW, bool SPLIT>
+// Split-k modes: kNoSplit; kSplitOwnRecv -- the receive slots have a region of their own (free
+// from the start: no CTA waits for a peer's ring to drain before sending; costs ring depth);
+// kSplitRingRecv -- the receive slots sit in the drained ring behind the staged tile (a cluster
+// barrier after staging tells the senders every ring is drained; keeps the ring deep for long k).
+constexpr int kNoSplit = 0, kSplitOwnRecv = 1, kSplitRingRecv = 2;
+
+template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT>
 struct TcShape {
     static constexpr int kATile = BM * BK * 4;  // bytes of one A term tile
     static constexpr int kBTile = BN * BK * 4;  // bytes of one B term tile
@@ -147,9 +153,11 @@ struct TcShape {
     static_assert(NB * BM * kLd * 4 <= kRing, "the staged tile fits the drained ring");
     static constexpr int kBars = 512;
     // Split k: receive slots [NB][splits][band][kLd] for the other CTAs' partial rows of this
-    // CTA's band, in a region of their own (free from the start, so no CTA has to wait for a
-    // peer's ring to drain before sending).
-    static constexpr int kRecv = SPLIT ? NB * (BM + kMaxSplits - 1) * kLd * 4 : 0;
+    // CTA's band.
+    static constexpr int kStaged = NB * BM * kLd * 4;
+    static constexpr int kRecvBytes = NB * (BM + kMaxSplits - 1) * kLd * 4;
+    static_assert(SPLIT != kSplitRingRecv || kStaged + kRecvBytes <= kRing, "receive slots fit the drained ring");
+    static constexpr int kRecv = SPLIT == kSplitOwnRecv ? kRecvBytes : 0;
     static constexpr int kSmem = kRing + kBars + kRecv + 1024 /* align */;
     static constexpr uint32_t kTmemCols =
         NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
@@ -161,7 +169,7 @@ struct TcShape {
 // memory of the CTA that owns their band; each CTA then sums its band's partials in
 // cluster-rank order and writes the finished band with coalesced stores (bias / residual /
 // SwiGLU applied).  One kernel, deterministic, and the partial sums never leave the chip.
-template <int BN, int NB, int STAGES, bool A_RAW, bool SPLIT>
+template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT>
 __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
@@ -183,7 +191,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
     auto conv_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + s); };
     const uint32_t accum_bar = bar_base + 8u * (3 * STAGES);
     const uint32_t recv_bar = bar_base + 8u * (3 * STAGES + 1);
-    const uint32_t recv_base = bar_base + S::kBars;
+    const uint32_t recv_base = SPLIT == kSplitOwnRecv ? bar_base + S::kBars : base + S::kStaged;
     // Split k: the CTAs of a tile's cluster each own one band of the tile's rows.
     const int splits = SPLIT ? p.splits : 1;
     const int rank = SPLIT ? (int)cooperative_groups::this_cluster().block_rank() : 0;
@@ -252,9 +260,9 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
         tmem_alloc(smem_u32((const void*)tmem_slot), S::kTmemCols);
         tmem_relinquish();
     }
-    // Cluster barrier, phase 1 (arrive now, wait in the epilogue): every CTA's receive
-    // barrier is initialised and armed before any CTA sends to it.
-    if (SPLIT) cluster_arrive();
+    // Cluster barrier, phase 1 (own receive region: arrive now, wait in the epilogue): every
+    // CTA's receive barrier is initialised and armed before any CTA sends to it.
+    if (SPLIT == kSplitOwnRecv) cluster_arrive();
     pdl_enter();
     if (threadIdx.x == 0) {
         // The first stages are free: start their loads before the set-up barrier so that the
@@ -399,7 +407,10 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
         tmem_dealloc(tmem, S::kTmemCols);
     }
     if (SPLIT) {
-        cluster_wait();  // phase 1: every receive barrier of the cluster is armed
+        // Phase 1: every receive barrier of the cluster is armed (and, receiving in the ring,
+        // every CTA has staged its tile: its ring is drained).
+        if (SPLIT == kSplitRingRecv) cluster_arrive();
+        cluster_wait();
         if (threadIdx.x == 64) {
             for (int b = 0; b < splits; b++) {
                 if (b == rank) continue;
@@ -532,7 +543,7 @@ mg_status split_operand(Device* d, const float* src, uint64_t rows, uint64_t k, 
     return launched(d, "operand split kernel launch");
 }
 
-template <int BN, int NB, int STAGES, bool A_RAW, bool SPLIT>
+template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT>
 mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
     using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT>;
     static_assert(S::kSmem <= 227 * 1024, "shared memory budget");
@@ -586,20 +597,40 @@ mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
     return launched(d, "tensor-core matmul launch");
 }
 
-// Ring depth per tile width: as deep as the shared memory allows, with the split-k receive
-// slots taking their share when k is split.
+// Ring depth per tile width: as deep as the shared memory allows.  Split k with few k-blocks
+// per CTA (the decoder layer's GEMMs) takes its own receive region and a shallower ring, so no
+// CTA waits for its peers before sending; with many k-blocks per CTA the ring depth matters more
+// and the partials are received in the drained ring.
 template <int NB, bool A_RAW>
 mg_status launch_bn(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
-    const bool split = p.splits > 1;
+    const int mode = p.splits <= 1 ? kNoSplit : p.kb_per_split < 8 ? kSplitOwnRecv : kSplitRingRecv;
     if constexpr (NB == 2) {
-        if (bn == 128 && !split) return launch_tc<128, NB, 2, A_RAW, false>(d, p, maps);
-        if (bn == 64) return split ? launch_tc<64, NB, 2, A_RAW, true>(d, p, maps) : launch_tc<64, NB, 3, A_RAW, false>(d, p, maps);
-        if (bn == 32) return split ? launch_tc<32, NB, 3, A_RAW, true>(d, p, maps) : launch_tc<32, NB, 4, A_RAW, false>(d, p, maps);
+        if (bn == 128 && mode == kNoSplit) return launch_tc<128, NB, 2, A_RAW, kNoSplit>(d, p, maps);
+        if (bn == 64) {
+            if (mode == kNoSplit) return launch_tc<64, NB, 3, A_RAW, kNoSplit>(d, p, maps);
+            if (mode == kSplitOwnRecv) return launch_tc<64, NB, 2, A_RAW, kSplitOwnRecv>(d, p, maps);
+            return launch_tc<64, NB, 3, A_RAW, kSplitRingRecv>(d, p, maps);
+        }
+        if (bn == 32) {
+            if (mode == kNoSplit) return launch_tc<32, NB, 4, A_RAW, kNoSplit>(d, p, maps);
+            if (mode == kSplitOwnRecv) return launch_tc<32, NB, 3, A_RAW, kSplitOwnRecv>(d, p, maps);
+            return launch_tc<32, NB, 4, A_RAW, kSplitRingRecv>(d, p, maps);
+        }
         return fail(MG_EXECUTION_FAILED, "gated matmul tile width %d with split k", bn);
     } else {
-        if (bn == 128) return split ? launch_tc<128, NB, 2, A_RAW, true>(d, p, maps) : launch_tc<128, NB, 3, A_RAW, false>(d, p, maps);
-        if (bn == 64) return split ? launch_tc<64, NB, 3, A_RAW, true>(d, p, maps) : launch_tc<64, NB, 4, A_RAW, false>(d, p, maps);
-        return split ? launch_tc<32, NB, 4, A_RAW, true>(d, p, maps) : launch_tc<32, NB, 5, A_RAW, false>(d, p, maps);
+        if (bn == 128) {
+            if (mode == kNoSplit) return launch_tc<128, NB, 3, A_RAW, kNoSplit>(d, p, maps);
+            if (mode == kSplitOwnRecv) return launch_tc<128, NB, 2, A_RAW, kSplitOwnRecv>(d, p, maps);
+            return launch_tc<128, NB, 3, A_RAW, kSplitRingRecv>(d, p, maps);
+        }
+        if (bn == 64) {
+            if (mode == kNoSplit) return launch_tc<64, NB, 4, A_RAW, kNoSplit>(d, p, maps);
+            if (mode == kSplitOwnRecv) return launch_tc<64, NB, 3, A_RAW, kSplitOwnRecv>(d, p, maps);
+            return launch_tc<64, NB, 4, A_RAW, kSplitRingRecv>(d, p, maps);
+        }
+        if (mode == kNoSplit) return launch_tc<32, NB, 5, A_RAW, kNoSplit>(d, p, maps);
+        if (mode == kSplitOwnRecv) return launch_tc<32, NB, 4, A_RAW, kSplitOwnRecv>(d, p, maps);
+        return launch_tc<32, NB, 5, A_RAW, kSplitRingRecv>(d, p, maps);
     }
 }
 

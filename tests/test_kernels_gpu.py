@@ -230,6 +230,9 @@ MATMUL_SHAPES = [
     (1, 4096, 512), (1, 1000, 70), (3, 129, 64), (16, 4096, 4096), (4, 50, 40),
     (17, 64, 96), (128, 512, 512), (128, 512, 1376), (128, 1376, 512), (200, 904, 136),
     (256, 1024, 768), (300, 129, 65), (513, 257, 130),
+    # split k with many k-blocks per CTA (partials received in the drained ring): 128- and
+    # 32-wide tiles; and the 32-wide tile with its own receive region
+    (128, 4096, 512), (128, 2048, 2048), (64, 4096, 32), (64, 512, 32),
 ]
 
 
@@ -252,10 +255,10 @@ def test_matmul_transposed(kernels, oracle, m, k, n, ta, tb):
     assert rel(got, oracle.matmul(a, b, ta, tb)) <= TOL_MATMUL
 
 
-@pytest.mark.parametrize("m", [1, 16, 128, 300])
-def test_matmul_bias_and_residual(kernels, oracle, m):
+@pytest.mark.parametrize("m,k", [(1, 256), (16, 256), (128, 256), (300, 256), (128, 4096)])
+def test_matmul_bias_and_residual(kernels, oracle, m, k):
     r = rng(12)
-    k, n = 256, 192
+    n = 192
     a = r.standard_normal((m, k)).astype(np.float32)
     b = r.standard_normal((k, n)).astype(np.float32)
     bias = r.standard_normal(n).astype(np.float32)
@@ -267,7 +270,8 @@ def test_matmul_bias_and_residual(kernels, oracle, m):
     assert rel(got, oracle.matmul(a, b, addend=res, addend_mode=2)) <= TOL_MATMUL
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 512, 1376), (16, 512, 256), (128, 512, 1376), (200, 300, 136)])
+@pytest.mark.parametrize("m,k,n", [(1, 512, 1376), (16, 512, 256), (128, 512, 1376), (200, 300, 136),
+                                   (128, 4096, 256)])
 def test_gated_matmul(kernels, oracle, m, k, n):
     r = rng(13)
     a = r.standard_normal((m, k)).astype(np.float32)
