@@ -8,6 +8,7 @@
 // one partial per (slice, row, column) to a workspace, and a second kernel sums the slices
 // in slice order and applies the addend (bias row / residual) or the SwiGLU gate -- so the
 // result is deterministic, and B (the 64 MB weight at K = N = 4096) is read exactly once.
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -168,7 +169,8 @@ void launch_partial(Device* d, dim3 grid, size_t smem, const k::GemmArgs& g, flo
 // matching 4 columns of A (one 16-byte shared load per row of A), so ~96 KB of B is in flight
 // per CTA regardless of the warps' arithmetic.
 constexpr int kChunkRows = 32;
-constexpr int kStages = 6;
+constexpr int kStages = 4;      // 64 KB of B in flight per CTA; two CTAs fit an SM
+constexpr int kMaxSlices = 32;  // k slices per column tile (the last CTA's sum loads them at once)
 constexpr int kChunkBytes = kChunkRows * kCols * 4;
 constexpr uint64_t kMaxCounterTiles = 1u << 16;  // Device::counters entries
 
@@ -189,7 +191,7 @@ struct GemvTmaArgs {
 // that tile's partials over the slices (in slice order) and writes the output, so no second
 // kernel is needed.
 template <int M>
-__global__ void __launch_bounds__((kWarps + 1) * 32) gemv_tma_kernel(const __grid_constant__ CUtensorMap map_b,
+__global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_tma_kernel(const __grid_constant__ CUtensorMap map_b,
                                                                       const __grid_constant__ CUtensorMap map_b2,
                                                                       GemvTmaArgs p) {
     pdl_enter();
@@ -222,12 +224,42 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) gemv_tma_kernel(const __gri
         }
         fence_barrier_init();
     }
-    // Stage A[:, k0:k1] (zero past k1 so a partial last tile multiplies zero rows of B).
-    for (uint64_t i = threadIdx.x; i < (uint64_t)M * slice_len; i += blockDim.x) {
-        const uint64_t r = i / slice_len, kk = k0 + i % slice_len;
-        float v = 0.0f;
-        if (r < m && kk < k1) v = p.transpose_a ? p.a[kk * m + r] : p.a[r * k + kk];
-        a_s[i] = v;
+    // Stage A[:, k0:k1] (zero past k1 so a partial last tile multiplies zero rows of B), with
+    // several loads in flight per thread: 16-byte loads when A's rows allow them.
+    if (!p.transpose_a && k % 4 == 0 && k0 % 4 == 0 && (reinterpret_cast<uintptr_t>(p.a) & 15) == 0) {
+        const uint64_t q = slice_len / 4;  // float4 per staged row (slice_len is a multiple of 32)
+        const uint64_t total = (uint64_t)M * q;
+        for (uint64_t i0 = threadIdx.x; i0 < total; i0 += 4 * blockDim.x) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint64_t i = i0 + (uint64_t)u * blockDim.x;
+                const uint64_t r = i / q, kk = k0 + 4 * (i % q);
+                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i < total && r < m && kk < k1) v[u] = *reinterpret_cast<const float4*>(p.a + r * k + kk);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint64_t i = i0 + (uint64_t)u * blockDim.x;
+                if (i < total) reinterpret_cast<float4*>(a_s)[i] = v[u];
+            }
+        }
+    } else {
+        for (uint64_t i0 = threadIdx.x; i0 < (uint64_t)M * slice_len; i0 += 4 * blockDim.x) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint64_t i = i0 + (uint64_t)u * blockDim.x;
+                const uint64_t r = i / slice_len, kk = k0 + i % slice_len;
+                v[u] = 0.0f;
+                if (i < (uint64_t)M * slice_len && r < m && kk < k1) v[u] = p.transpose_a ? p.a[kk * m + r] : p.a[r * k + kk];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint64_t i = i0 + (uint64_t)u * blockDim.x;
+                if (i < (uint64_t)M * slice_len) a_s[i] = v[u];
+            }
+        }
     }
     __syncthreads();
 
@@ -308,17 +340,30 @@ __global__ void __launch_bounds__((kWarps + 1) * 32) gemv_tma_kernel(const __gri
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    const uint64_t slices = gridDim.y;
+    const int slices = (int)gridDim.y;  // <= kMaxSlices
     const uint64_t mn = m * n;
+    // Sum over the slices in slice order, eight slices' partials loaded before they are added
+    // (eight loads in flight at once).
+    auto sum_slices = [&](int zs, uint64_t off) {
+        float acc = 0.0f;
+        for (int sl0 = 0; sl0 < slices; sl0 += 8) {
+            float t[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (sl0 + u < slices) t[u] = __ldcg(p.partial + ((uint64_t)zs * slices + sl0 + u) * mn + off);
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (sl0 + u < slices) acc += t[u];
+        }
+        return acc;
+    };
     for (uint64_t i = threadIdx.x; i < m * kCols; i += blockDim.x) {
         const uint64_t r = i / kCols, cidx = col0 + i % kCols;
         if (cidx >= n) continue;
         const uint64_t off = r * n + cidx;
-        float s = 0.0f;
-        for (uint64_t sl = 0; sl < slices; sl++) s += __ldcg(p.partial + sl * mn + off);
+        float s = sum_slices(0, off);
         if (p.gated) {
-            float u = 0.0f;
-            for (uint64_t sl = 0; sl < slices; sl++) u += __ldcg(p.partial + (slices + sl) * mn + off);
+            const float u = sum_slices(1, off);
             s = (s * (1.0f / (1.0f + expf(-s)))) * u;
         } else if (p.addend_mode == 1) {
             s += p.addend[cidx];
@@ -358,6 +403,230 @@ mg_status gemv_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n) {
     return MG_OK;
 }
 
+// ---- cluster GEMV: A and B streamed together, k split across a thread-block cluster -----------
+// A producer lane streams, per stage, a [32 x 128] tile of B and the matching [M x 32] columns
+// of A with TMA (no prologue staging A); 8 compute warps take 4 rows of B each per stage and
+// multiply them by A from shared memory.  The k slices of one column tile (and, gated, the
+// gate and up terms) form one cluster: each CTA sums its warps once through the drained ring,
+// then sends each band of its [M x 128] partial to the CTA that owns the band with one bulk
+// copy into that CTA's receive slot; owners add the partials in split order (deterministic),
+// apply bias / residual / SwiGLU and write.  B is read exactly once; nothing goes through
+// global memory but the operands and the result.
+constexpr int kCStages = 4;
+
+struct GemvClusterArgs {
+    float* out;
+    const float* addend;
+    int addend_mode;
+    uint64_t m, n, k;
+    uint64_t slice_len;  // k rows per split (multiple of kChunkRows)
+    int splits;          // S; the cluster is (1, S, terms)
+    int terms;           // 1, or 2 for gated (gate: z = 0, up: z = 1)
+    int band;            // floats of the flattened [m][128] tile each cluster CTA finishes (multiple of 4)
+    int* error;
+};
+
+template <int M>
+struct GemvCShape {
+    static constexpr int kB = kChunkRows * kCols * 4;  // 16 KB of B per stage
+    static constexpr int kA = M * kChunkRows * 4;      // [M][32] of A per stage
+    static constexpr int kStage = kB + kA;
+    static constexpr int kRing = kCStages * kStage;
+    static constexpr int kPart = M * kCols * 4;         // this CTA's partial [M][128]
+    static constexpr int kRecv = (M * kCols + 4 * 8) * 4;  // the other CTAs' partials of this CTA's band
+    static_assert(kWarps * kPart <= kRing, "the warp partials fit the drained ring");
+    static constexpr int kSmem = 128 + kRing + kPart + kRecv + 8 * (2 * kCStages + 1);
+};
+
+template <int M>
+__global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                          const __grid_constant__ CUtensorMap map_b,
+                                                                          const __grid_constant__ CUtensorMap map_b2,
+                                                                          GemvClusterArgs p) {
+    using namespace sm100;
+    using S = GemvCShape<M>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 127u) & ~127u;
+    uint8_t* base_ptr = smem_raw + (base - raw);
+    const uint32_t part = base + S::kRing;
+    const uint32_t recv = part + S::kPart;
+    const uint32_t bar0 = recv + S::kRecv;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kCStages + s); };
+    const uint32_t recv_bar = bar0 + 8u * (2 * kCStages);
+    float* partf = reinterpret_cast<float*>(base_ptr + S::kRing);
+    float* recvf = reinterpret_cast<float*>(base_ptr + S::kRing + S::kPart);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t col0 = (uint64_t)blockIdx.x * kCols;
+    const int nc = p.splits * p.terms;
+    const int rank = (int)cooperative_groups::this_cluster().block_rank();
+    const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
+    const uint64_t k1 = min(p.k, k0 + p.slice_len);
+    const int chunks = k1 > k0 ? (int)((k1 - k0 + kChunkRows - 1) / kChunkRows) : 0;
+    const int F = (int)p.m * kCols;
+    const int my_lo = min(F, rank * p.band), my_hi = min(F, my_lo + p.band);
+    const CUtensorMap* mb = blockIdx.z ? &map_b2 : &map_b;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kCStages; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), kWarps);
+        }
+        mbar_init(recv_bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(recv_bar, (uint32_t)((nc - 1) * (my_hi - my_lo) * 4));
+    }
+    cluster_arrive();  // phase 1: every CTA's receive barrier is armed before anyone sends
+    pdl_enter();
+    __syncthreads();
+
+    float acc[M][4];
+#pragma unroll
+    for (int r = 0; r < M; r++) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    if (warp == kWarps) {
+        // ---- producer: keep the ring full -----------------------------------------------
+        if (lane == 0) {
+            for (int c = 0; c < chunks; c++) {
+                const int s = c % kCStages;
+                if (c >= kCStages && !mbar_wait(empty_bar(s), (uint32_t)(c / kCStages - 1) & 1u)) {
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                const uint32_t st = base + (uint32_t)(s * S::kStage);
+                const int kr = (int)(k0 + (uint64_t)c * kChunkRows);
+                mbar_arrive_expect_tx(full_bar(s), (uint32_t)S::kStage);
+                tma_load_2d(st, mb, full_bar(s), (int)col0, kr);
+                tma_load_2d(st + S::kB, &map_a, full_bar(s), kr, 0);
+            }
+        }
+        __syncwarp();
+    } else {
+        for (int c = 0; c < chunks; c++) {
+            const int s = c % kCStages;
+            if (!mbar_wait(full_bar(s), (uint32_t)(c / kCStages) & 1u)) {
+                atomicExch(p.error, 1);
+                break;
+            }
+            const float* tile = reinterpret_cast<const float*>(base_ptr + s * S::kStage);
+            const float* at = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kB);  // [M][32]
+            const int rr = warp * 4;  // this warp's 4 rows of the stage
+            float4 bv[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) bv[u] = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+#pragma unroll
+            for (int r = 0; r < M; r++) {
+                const float4 av = *reinterpret_cast<const float4*>(at + r * kChunkRows + rr);
+                const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    acc[r][0] += aa[u] * bv[u].x;
+                    acc[r][1] += aa[u] * bv[u].y;
+                    acc[r][2] += aa[u] * bv[u].z;
+                    acc[r][3] += aa[u] * bv[u].w;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));  // this warp is done with the stage
+        }
+    }
+    // ---- this CTA's partial: the warps' sums in warp order, through the drained ring ----------
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(base_ptr);  // [kWarps][M][128]
+    if (warp < kWarps) {
+#pragma unroll
+        for (int r = 0; r < M; r++)
+            *reinterpret_cast<float4*>(red + (warp * M + r) * kCols + 4 * lane) =
+                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < F; i += blockDim.x) {
+        const int r = i / kCols, c = i % kCols;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) sum += red[(w * M + r) * kCols + c];
+        partf[i] = sum;
+    }
+    fence_proxy_async();  // the partial is read by bulk copies next
+    __syncthreads();
+    // ---- exchange: each band of the partial to the CTA that owns it ---------------------------
+    cluster_wait();  // phase 1
+    if (threadIdx.x == 0) {
+        for (int o = 0; o < nc; o++) {
+            if (o == rank) continue;
+            const int lo = min(F, o * p.band), hi = min(F, lo + p.band);
+            if (hi > lo)
+                bulk_copy_to_cluster(mapa(recv + (uint32_t)(rank * p.band * 4), (uint32_t)o), part + (uint32_t)(lo * 4),
+                                     (uint32_t)((hi - lo) * 4), mapa(recv_bar, (uint32_t)o));
+        }
+    }
+    if (!mbar_wait(recv_bar, 0)) atomicExch(p.error, 1);
+    cluster_arrive();  // phase 2: every copy into this CTA has landed
+    // ---- finish this CTA's band: splits in order, per term -----------------------------------
+    for (int e = my_lo + (int)threadIdx.x; e < my_hi; e += blockDim.x) {
+        const int r = e / kCols, c = e % kCols;
+        const uint64_t col = col0 + c;
+        if (col >= p.n) continue;
+        auto from = [&](int src) { return src == rank ? partf[e] : recvf[src * p.band + (e - my_lo)]; };
+        float g = 0.0f;
+        for (int s = 0; s < p.splits; s++) g += from(s);
+        float v;
+        if (p.terms == 2) {
+            float u = 0.0f;
+            for (int s = 0; s < p.splits; s++) u += from(p.splits + s);
+            v = (g * (1.0f / (1.0f + expf(-g)))) * u;
+        } else {
+            v = g;
+            if (p.addend_mode == 1) v += p.addend[col];
+            else if (p.addend_mode == 2) v += p.addend[(uint64_t)r * p.n + col];
+        }
+        p.out[(uint64_t)r * p.n + col] = v;
+    }
+    cluster_wait();  // phase 2: every copy out of this CTA's shared memory has landed
+}
+
+// Row-major [m, k] f32 A, box [32 x mp] (rows past m read as zero).
+mg_status gemv_a_map(CUtensorMap* map, const float* a, uint64_t m, uint64_t k, uint32_t mp) {
+    auto fn = gemv_encode_fn();
+    if (!fn) return mg::fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {k, m};
+    cuuint64_t strides[1] = {k * sizeof(float)};
+    cuuint32_t box[2] = {kChunkRows, mp};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return mg::fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
+template <int M>
+mg_status launch_cluster(Device* d, const GemvClusterArgs& p, uint64_t col_tiles, const CUtensorMap* maps) {
+    using S = GemvCShape<M>;
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+                "configuring the cluster gemv kernel");
+        configured[d->ordinal & 63] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
+    cfg.blockDim = dim3((kWarps + 1) * 32, 1, 1);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)p.splits;
+    attr[0].val.clusterDim.z = (unsigned)p.terms;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = d->pdl ? 2 : 1;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<M>, maps[0], maps[1], maps[2], p), "cluster gemv launch");
+    return launched(d, "cluster gemv launch");
+}
+
 }  // namespace
 
 namespace k {
@@ -395,22 +664,32 @@ mg_status launch_tma(Device* d, dim3 grid, size_t smem, const CUtensorMap* maps,
     return launched(d, "gemv kernel launch");
 }
 
-// The TMA-staged path: about two CTAs per SM, each streaming one k-slice of one 128-column
-// tile of B.
-mg_status gemv_tma(Device* d, const GemmArgs& g) {
+// The TMA-staged path: one wave of CTAs (two per SM), each streaming one k-slice of one
+// 128-column tile of B; eligible when the k slices needed for that fit kMaxSlices with A's
+// slice in shared memory.
+bool gemv_tma_plan(const Device* d, const GemmArgs& g, uint64_t* slices_out, uint64_t* slice_len_out) {
     const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
     const int zs = g.gated ? 2 : 1;
     const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
     const uint64_t max_slice = (uint64_t)(8192 / mp) / kChunkRows * kChunkRows;  // A's slice <= 32 KB
-    if (col_tiles > kMaxCounterTiles) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
-    // One wave: at most two CTAs per SM over all column tiles and slices.
+    if (col_tiles > kMaxCounterTiles) return false;
     uint64_t slices = (uint64_t)d->sm_count * 2 / zs / col_tiles;
     if (slices < 1) slices = 1;
+    if (slices > (uint64_t)kMaxSlices) slices = kMaxSlices;
     uint64_t slice_len = (g.k + slices - 1) / slices;
     slice_len = ((slice_len + kChunkRows - 1) / kChunkRows) * kChunkRows;
     if (slice_len > max_slice) slice_len = max_slice;
     slices = (g.k + slice_len - 1) / slice_len;
-    if (slices > 65535) return fail(MG_SHAPE_UNSUPPORTED, "gemv inner dimension %llu is too large", (unsigned long long)g.k);
+    if (slices > (uint64_t)kMaxSlices) return false;
+    *slices_out = slices;
+    *slice_len_out = slice_len;
+    return true;
+}
+
+mg_status gemv_tma(Device* d, const GemmArgs& g, uint64_t slices, uint64_t slice_len) {
+    const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
+    const int zs = g.gated ? 2 : 1;
+    const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
     const size_t smem = 128 + (size_t)kStages * kChunkBytes + ((size_t)mp * slice_len + kWarps * kCols) * sizeof(float) +
                         2 * kStages * sizeof(uint64_t);
     float* partial = nullptr;
@@ -430,8 +709,61 @@ mg_status gemv_tma(Device* d, const GemmArgs& g) {
     return MG_OK;
 }
 
+// The cluster path: A K-major with 16-byte rows, B with 16-byte rows; k split so that the
+// clusters fill the GPU about twice over (two CTAs per SM), at most 8 CTAs per cluster.
+bool gemv_cluster_eligible(const GemmArgs& g) {
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    return !g.transpose_a && !g.transpose_b && g.k % 4 == 0 && g.n % 4 == 0 && al(g.a) && al(g.b) &&
+           (!g.b2 || al(g.b2)) && g.k < (1ull << 31) && g.n < (1ull << 31);
+}
+
+mg_status gemv_cluster(Device* d, const GemmArgs& g) {
+    const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
+    if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
+    const int terms = g.gated ? 2 : 1;
+    const uint64_t kb = (g.k + kChunkRows - 1) / kChunkRows;
+    uint64_t splits = (uint64_t)d->sm_count * 2 / (col_tiles * terms);
+    const uint64_t max_splits = 8 / terms;
+    if (splits > max_splits) splits = max_splits;
+    if (splits > kb) splits = kb;
+    if (splits < 1) splits = 1;
+    uint64_t slice_len = ((kb + splits - 1) / splits) * kChunkRows;
+    splits = (g.k + slice_len - 1) / slice_len;
+    if (splits < 1) splits = 1;
+    const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
+    const int nc = (int)splits * terms;
+    const int F = (int)g.m * kCols;
+    GemvClusterArgs p;
+    p.out = g.out;
+    p.addend = g.addend;
+    p.addend_mode = g.addend_mode;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.slice_len = slice_len;
+    p.splits = (int)splits;
+    p.terms = terms;
+    p.band = ((F + nc - 1) / nc + 3) / 4 * 4;
+    p.error = d->flags + 2;
+    CUtensorMap maps[3];
+    MG_TRY(gemv_a_map(&maps[0], g.a, g.m, g.k, (uint32_t)mp));
+    MG_TRY(gemv_map(&maps[1], g.b, g.k, g.n));
+    if (g.gated) MG_TRY(gemv_map(&maps[2], g.b2, g.k, g.n));
+    else maps[2] = maps[1];
+    switch (mp) {
+        case 1: return launch_cluster<1>(d, p, col_tiles, maps);
+        case 2: return launch_cluster<2>(d, p, col_tiles, maps);
+        case 4: return launch_cluster<4>(d, p, col_tiles, maps);
+        case 8: return launch_cluster<8>(d, p, col_tiles, maps);
+        default: return launch_cluster<16>(d, p, col_tiles, maps);
+    }
+}
+
 mg_status gemv(Device* d, const GemmArgs& g) {
-    if (g.n <= (1ull << 31) && g.k <= (1ull << 31)) return gemv_tma(d, g);
+    if (gemv_cluster_eligible(g)) return gemv_cluster(d, g);
+    uint64_t tma_slices = 0, tma_slice_len = 0;
+    if (g.n <= (1ull << 31) && g.k <= (1ull << 31) && gemv_tma_plan(d, g, &tma_slices, &tma_slice_len))
+        return gemv_tma(d, g, tma_slices, tma_slice_len);
     const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
     // Enough slices of k for about four CTAs per SM, each slice a multiple of the rows the
     // warps consume per step and at most 512 rows (A's slice fits shared memory).

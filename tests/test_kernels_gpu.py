@@ -233,6 +233,9 @@ MATMUL_SHAPES = [
     # split k with many k-blocks per CTA (partials received in the drained ring): 128- and
     # 32-wide tiles; and the 32-wide tile with its own receive region
     (128, 4096, 512), (128, 2048, 2048), (64, 4096, 32), (64, 512, 32),
+    # GEMV: the most k splits of one cluster, a long k, and k not a multiple of 4 (TMA-staged
+    # path); transposed A with a long k takes the two-kernel path (test_matmul_transposed)
+    (8, 16384, 256), (16, 40000, 128), (5, 4098, 260),
 ]
 
 
@@ -245,7 +248,7 @@ def test_matmul(kernels, oracle, m, k, n):
     assert rel(got, oracle.matmul(a, b)) <= TOL_MATMUL
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 300, 70), (16, 256, 128), (130, 200, 96)])
+@pytest.mark.parametrize("m,k,n", [(1, 300, 70), (16, 256, 128), (130, 200, 96), (16, 40000, 128)])
 @pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
 def test_matmul_transposed(kernels, oracle, m, k, n, ta, tb):
     r = rng(11)
