@@ -127,7 +127,6 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
                         AttnTcParams p) {
-    pdl_enter();
     using S = AttnShape<D>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bars[9];
@@ -176,6 +175,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         tmem_alloc(smem_u32(&tmem_slot), S::kTmemCols);
         tmem_relinquish();
     }
+    pdl_enter();  // after the TMEM allocation, as every tensor-memory kernel here does
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
