@@ -411,17 +411,16 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
         // every CTA has staged its tile: its ring is drained).
         if (SPLIT == kSplitRingRecv) cluster_arrive();
         cluster_wait();
-        if (threadIdx.x == 64) {
-            for (int b = 0; b < splits; b++) {
-                if (b == rank) continue;
-                const int b_begin = b * band, b_rows = min(BM, b_begin + band) - b_begin;
+        // Thread 64 + b sends band b (one issuing thread per destination).
+        const int b = (int)threadIdx.x - 64;
+        if (b >= 0 && b < splits && b != rank) {
+            const int b_begin = b * band, b_rows = min(BM, b_begin + band) - b_begin;
 #pragma unroll
-                for (int z = 0; z < NB; z++) {
-                    const uint32_t src = base + (uint32_t)((z * BM + b_begin) * S::kLd * 4);
-                    const uint32_t dst = recv_base + (uint32_t)(((z * splits + rank) * band) * S::kLd * 4);
-                    bulk_copy_to_cluster(mapa(dst, (uint32_t)b), src, (uint32_t)(b_rows * S::kLd * 4),
-                                         mapa(recv_bar, (uint32_t)b));
-                }
+            for (int z = 0; z < NB; z++) {
+                const uint32_t src = base + (uint32_t)((z * BM + b_begin) * S::kLd * 4);
+                const uint32_t dst = recv_base + (uint32_t)(((z * splits + rank) * band) * S::kLd * 4);
+                bulk_copy_to_cluster(mapa(dst, (uint32_t)b), src, (uint32_t)(b_rows * S::kLd * 4),
+                                     mapa(recv_bar, (uint32_t)b));
             }
         }
         if (!mbar_wait(recv_bar, 0)) atomicExch(p.error, 1);
@@ -643,14 +642,14 @@ bool tensor_cores_enabled() {
     return enabled == 1;
 }
 
-// Output tile width.  Narrow MMAs cost about as much issue time as wide ones (measured: a
-// 128 x 32 tile spends ~1.5 us per k-block, a 128 x 128 tile ~0.6 us), so tiles stay 128 wide
-// and small output grids get their parallelism from splitting k; only a narrow n narrows them.
+// Output tile width: 128, except that a single row of tiles narrow enough to need deep k
+// splits (128 x 512 x 512 in the decoder layer: 8 splits of 4 tiles) uses 64-wide tiles -- the
+// same MMA work over twice the CTAs with half the split-k exchange per CTA (measured per call:
+// 4.7 vs 6.5 us at k = 512, 8.5 vs 14.1 us at k = 1376; at n = 4096, 128 wide stays faster).
 int pick_bn(const Device* d, uint64_t m, uint64_t n) {
-    (void)d;
-    (void)m;
     if (n <= 32) return 32;
     if (n <= 64) return 64;
+    if (m <= 128 && ((n + 127) / 128) * 8 <= (uint64_t)d->sm_count) return 64;
     return 128;
 }
 

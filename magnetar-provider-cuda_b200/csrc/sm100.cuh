@@ -100,7 +100,10 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
 
 // ---- thread-block cluster ---------------------------------------------------------------------
 // Split-phase cluster barrier: every thread of every CTA of the cluster arrives, then waits.
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+// The arrive is relaxed: what it publishes is ordered by other means (mbarrier initialisation
+// by fence.mbarrier_init; data by the mbarrier transactions that carried it), and a release
+// arrive costs a cluster-wide fence (~0.6 us measured in the GEMM epilogue).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
 // Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's
