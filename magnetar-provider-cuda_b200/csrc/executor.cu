@@ -42,6 +42,19 @@ struct mg_executor {
     cudaGraphExec_t graph_exec = nullptr;
     bool step_has_embedding = false;
     uint64_t launches_at_capture = 0, graph_kernels = 0;  // kernels one replay launches
+    // Step capture only: plain matmuls of one input (weights as B) waiting to launch as one
+    // grouped projection, with the ropes of their outputs folded into its epilogue.  Nothing
+    // runs during a capture, so deferring a launch changes only the recorded order, and every
+    // invocation that is not folded in launches the group first.
+    struct Deferred {
+        k::GemmArgs g;
+        Buffer* a;
+        Buffer* out;
+        Buffer* rope_out;
+    };
+    std::vector<Deferred> deferred;
+    bool deferred_rope = false;
+    k::RopeArgs rope{};
     // tensor parallel
     mg_comm* comm = nullptr;
     std::map<std::string, int> plan;            // weight id -> 0 columns, 1 rows
@@ -133,6 +146,65 @@ void yarn_correction_range(double beta_fast, double beta_slow, uint64_t dimensio
 
 inline mg_buffer* H(Buffer* b) { return reinterpret_cast<mg_buffer*>(b); }
 
+// The rope attributes the reference parses (src/executor.rs:1563-1666), with its defaults and
+// refusals.
+mg_status parse_rope(const Attrs& at, mg_rope_params* p) {
+    memset(p, 0, sizeof *p);
+    p->base = at.flt("base", 10000.0f);
+    p->scale = at.flt("scale", 1.0f);
+    if (!at.integer("dimension", &p->dimension)) return fail(MG_ATTRIBUTE_UNSUPPORTED, "dimension");
+    const char* mode = at.string("position_mode");
+    if (mode && strcmp(mode, "sequential") != 0)
+        return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_mode '%s' is not implemented", mode);
+    const mg_attribute* po = at.find("position_offset");
+    if (po) {
+        if (po->kind != MG_ATTR_INT) return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_offset must be an integer");
+        if (po->int_value < 0)
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_offset %lld must not be negative", (long long)po->int_value);
+        p->position_offset = (uint64_t)po->int_value;
+    }
+    if (!at.integer("head_count", &p->head_count)) p->head_count = 1;
+    const mg_attribute* pr = at.find("rotation_pairing");
+    p->pairing = 0;
+    if (pr) {
+        if (pr->kind != MG_ATTR_STRING) return fail(MG_ATTRIBUTE_UNSUPPORTED, "rotation_pairing must be a string");
+        if (!strcmp(pr->string_value, "interleaved")) p->pairing = 0;
+        else if (!strcmp(pr->string_value, "half_split")) p->pairing = 1;
+        else return fail(MG_ATTRIBUTE_UNSUPPORTED, "rotation_pairing '%s' is not implemented", pr->string_value);
+    }
+    const char* fs = at.string("frequency_scaling");
+    p->amplitude = 1.0f;
+    if (fs && !strcmp(fs, "yarn")) {
+        const float factor = at.flt("factor", 0.0f);
+        const float original = at.flt("original_context_length", 0.0f);
+        if (!(factor > 0.0f) || !(original > 0.0f))
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "yarn needs a positive factor and original_context_length");
+        p->yarn_factor = factor;
+        yarn_correction_range(at.flt("beta_fast", 32.0f), at.flt("beta_slow", 1.0f), p->dimension, p->base, original,
+                              &p->yarn_low, &p->yarn_high);
+        p->amplitude = at.flt("attention_factor", 1.0f);
+    } else if (fs && !strcmp(fs, "banded")) {
+        p->banded_factor = at.flt("factor", 0.0f);
+        p->low_freq_factor = at.flt("low_freq_factor", 0.0f);
+        p->high_freq_factor = at.flt("high_freq_factor", 0.0f);
+        p->original_context_length = at.flt("original_context_length", 0.0f);
+        if (!(p->banded_factor > 0.0f) || !(p->low_freq_factor > 0.0f) || !(p->high_freq_factor > p->low_freq_factor) ||
+            !(p->original_context_length > 0.0f))
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "banded frequency scaling needs factor > 0, 0 < low < high and a context length");
+    } else if (fs) {
+        return fail(MG_ATTRIBUTE_UNSUPPORTED, "frequency_scaling '%s' is not implemented", fs);
+    }
+    p->rotated_pairs = UINT64_MAX;
+    const mg_attribute* prf = at.find("partial_rotary_factor");
+    if (prf) {
+        if (prf->kind != MG_ATTR_FLOAT || !(prf->float_value > 0.0) || prf->float_value > 1.0)
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "partial_rotary_factor must be a float in (0, 1]");
+        p->rotated_pairs = (uint64_t)std::floor(prf->float_value * (double)p->dimension / 2.0);
+    }
+    return MG_OK;
+}
+
+
 // The body of run_invocation_with_offer (src/executor.rs:1422-2027).  `out` holds the
 // offered previous output buffer (or null) and receives the result.
 mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
@@ -191,58 +263,7 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
     if (!strcmp(name, "rope")) {
         MG_TRY(get_input(ex, inv, 0, &a));
         mg_rope_params p;
-        memset(&p, 0, sizeof p);
-        p.base = at.flt("base", 10000.0f);
-        p.scale = at.flt("scale", 1.0f);
-        if (!at.integer("dimension", &p.dimension)) return fail(MG_ATTRIBUTE_UNSUPPORTED, "dimension");
-        const char* mode = at.string("position_mode");
-        if (mode && strcmp(mode, "sequential") != 0)
-            return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_mode '%s' is not implemented", mode);
-        const mg_attribute* po = at.find("position_offset");
-        if (po) {
-            if (po->kind != MG_ATTR_INT) return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_offset must be an integer");
-            if (po->int_value < 0)
-                return fail(MG_ATTRIBUTE_UNSUPPORTED, "position_offset %lld must not be negative", (long long)po->int_value);
-            p.position_offset = (uint64_t)po->int_value;
-        }
-        if (!at.integer("head_count", &p.head_count)) p.head_count = 1;
-        const mg_attribute* pr = at.find("rotation_pairing");
-        p.pairing = 0;
-        if (pr) {
-            if (pr->kind != MG_ATTR_STRING) return fail(MG_ATTRIBUTE_UNSUPPORTED, "rotation_pairing must be a string");
-            if (!strcmp(pr->string_value, "interleaved")) p.pairing = 0;
-            else if (!strcmp(pr->string_value, "half_split")) p.pairing = 1;
-            else return fail(MG_ATTRIBUTE_UNSUPPORTED, "rotation_pairing '%s' is not implemented", pr->string_value);
-        }
-        const char* fs = at.string("frequency_scaling");
-        p.amplitude = 1.0f;
-        if (fs && !strcmp(fs, "yarn")) {
-            const float factor = at.flt("factor", 0.0f);
-            const float original = at.flt("original_context_length", 0.0f);
-            if (!(factor > 0.0f) || !(original > 0.0f))
-                return fail(MG_ATTRIBUTE_UNSUPPORTED, "yarn needs a positive factor and original_context_length");
-            p.yarn_factor = factor;
-            yarn_correction_range(at.flt("beta_fast", 32.0f), at.flt("beta_slow", 1.0f), p.dimension, p.base, original,
-                                  &p.yarn_low, &p.yarn_high);
-            p.amplitude = at.flt("attention_factor", 1.0f);
-        } else if (fs && !strcmp(fs, "banded")) {
-            p.banded_factor = at.flt("factor", 0.0f);
-            p.low_freq_factor = at.flt("low_freq_factor", 0.0f);
-            p.high_freq_factor = at.flt("high_freq_factor", 0.0f);
-            p.original_context_length = at.flt("original_context_length", 0.0f);
-            if (!(p.banded_factor > 0.0f) || !(p.low_freq_factor > 0.0f) || !(p.high_freq_factor > p.low_freq_factor) ||
-                !(p.original_context_length > 0.0f))
-                return fail(MG_ATTRIBUTE_UNSUPPORTED, "banded frequency scaling needs factor > 0, 0 < low < high and a context length");
-        } else if (fs) {
-            return fail(MG_ATTRIBUTE_UNSUPPORTED, "frequency_scaling '%s' is not implemented", fs);
-        }
-        p.rotated_pairs = UINT64_MAX;
-        const mg_attribute* prf = at.find("partial_rotary_factor");
-        if (prf) {
-            if (prf->kind != MG_ATTR_FLOAT || !(prf->float_value > 0.0) || prf->float_value > 1.0)
-                return fail(MG_ATTRIBUTE_UNSUPPORTED, "partial_rotary_factor must be a float in (0, 1]");
-            p.rotated_pairs = (uint64_t)std::floor(prf->float_value * (double)p.dimension / 2.0);
-        }
+        MG_TRY(parse_rope(at, &p));
         return mg_rope(dh, H(a), &p, out);
     }
     if (!strcmp(name, "attention")) {
@@ -331,6 +352,141 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
         return op ? mg_mul_half(dh, H(a), H(b), out) : mg_add_half(dh, H(a), H(b), out);
     }
     return fail(MG_KERNEL_NOT_FOUND, "kernel '%s' is not provided", name);
+}
+
+// ---- step-capture fusion ---------------------------------------------------------------------
+// Launches the deferred group: one grouped projection (with its ropes), or a lone matmul.
+mg_status flush_deferred(mg_executor* ex) {
+    if (ex->deferred.empty()) return MG_OK;
+    k::GemmArgs gs[3];
+    float* ro[3] = {nullptr, nullptr, nullptr};
+    const int n = (int)ex->deferred.size();
+    for (int i = 0; i < n; i++) {
+        gs[i] = ex->deferred[i].g;
+        ro[i] = ex->deferred[i].rope_out ? (float*)ex->deferred[i].rope_out->ptr : nullptr;
+    }
+    const bool rope = ex->deferred_rope;
+    ex->deferred.clear();
+    ex->deferred_rope = false;
+    if (n == 1 && !rope) return k::gemm(ex->device, gs[0]);
+    return k::gemm_group(ex->device, gs, n, rope ? &ex->rope : nullptr, ro);
+}
+
+bool deferred_uses(const mg_executor* ex, const Buffer* b) {
+    for (const auto& d : ex->deferred)
+        if (d.a == b || d.out == b || d.rope_out == b) return true;
+    return false;
+}
+
+bool deferred_writes(const mg_executor* ex, const Buffer* b) {
+    for (const auto& d : ex->deferred)
+        if (d.out == b || d.rope_out == b) return true;
+    return false;
+}
+
+bool same_rope(const k::RopeArgs& x, const k::RopeArgs& y) {
+    return x.rows == y.rows && x.cols == y.cols && x.half == y.half && x.dimension == y.dimension &&
+           x.position_offset == y.position_offset && x.head_count == y.head_count && x.rotated_pairs == y.rotated_pairs &&
+           x.base == y.base && x.scale == y.scale && x.banded_factor == y.banded_factor &&
+           x.low_freq_factor == y.low_freq_factor && x.high_freq_factor == y.high_freq_factor &&
+           x.original_context_length == y.original_context_length && x.yarn_factor == y.yarn_factor &&
+           x.yarn_low == y.yarn_low && x.yarn_high == y.yarn_high && x.amplitude == y.amplitude &&
+           x.half_split == y.half_split;
+}
+
+// During a step capture: takes a plain matmul whose B is a weight into the deferred group (or
+// starts a new group), or folds a rope of a deferred matmul's output into the group's
+// epilogue.  Returns false when the invocation runs the ordinary way (the caller launches the
+// group first); true when it was handled here, with its output in *result and its status in
+// *status.  Validation and the output follow the ordinary call exactly (matmul_plan,
+// rope_plan), so errors and the output-offer rule are unchanged.
+bool capture_defer(mg_executor* ex, const mg_invocation* inv, mg_buffer* offered, mg_buffer** result,
+                   mg_status* status) {
+    Attrs at{inv};
+    const bool is_mm = !strcmp(inv->kernel, "matmul"), is_rope = !strcmp(inv->kernel, "rope");
+    if (!is_mm && !is_rope) return false;
+    if (offered && deferred_uses(ex, buf(offered))) return false;
+    Device* d = ex->device;
+    if (is_mm) {
+        Buffer *a = nullptr, *b = nullptr;
+        if (get_input(ex, inv, 0, &a) != MG_OK || get_input(ex, inv, 1, &b) != MG_OK) return false;
+        if (at.boolean("transpose_a", false) || at.boolean("transpose_b", false)) return false;
+        if (require_f32_accumulation(at) != MG_OK || !b->is_weight) return false;
+        if (deferred_writes(ex, a) || deferred_writes(ex, b)) return false;
+        k::GemmArgs g;
+        mg_buffer* res = offered;
+        mg_status s = matmul_plan(ex->handle, H(a), H(b), nullptr, nullptr, 0, 0, 0, &res, &g);
+        *result = res;
+        if (s != MG_OK) {
+            *status = s;
+            return true;
+        }
+        const size_t n = ex->deferred.size();
+        bool joined = false;
+        if (n > 0 && n < 3 && ex->deferred[0].a == a && g.b_prep[0]) {
+            k::GemmArgs gs[3];
+            float* ro[3] = {nullptr, nullptr, nullptr};
+            for (size_t i = 0; i < n; i++) {
+                gs[i] = ex->deferred[i].g;
+                ro[i] = ex->deferred[i].rope_out ? (float*)ex->deferred[i].rope_out->ptr : nullptr;
+            }
+            gs[n] = g;
+            joined = k::gemm_group_eligible(gs, (int)n + 1, ex->deferred_rope ? &ex->rope : nullptr, ro);
+        }
+        if (!joined) {
+            s = flush_deferred(ex);
+            if (s == MG_OK && !(g.b_prep[0] && k::gemm_group_eligible(&g, 1, nullptr, nullptr))) {
+                *status = k::gemm(d, g);  // not groupable: launched now
+                return true;
+            }
+            if (s != MG_OK) {
+                *status = s;
+                return true;
+            }
+        }
+        ex->deferred.push_back({g, a, buf(res), nullptr});
+        *status = MG_OK;
+        return true;
+    }
+    // a rope of a deferred matmul's output
+    Buffer* x = nullptr;
+    if (get_input(ex, inv, 0, &x) != MG_OK) return false;
+    int member = -1;
+    for (size_t i = 0; i < ex->deferred.size(); i++)
+        if (ex->deferred[i].out == x && !ex->deferred[i].rope_out) member = (int)i;
+    if (member < 0) return false;
+    mg_rope_params rp;
+    if (parse_rope(at, &rp) != MG_OK) return false;  // the ordinary call reports it
+    k::RopeArgs ra;
+    mg_buffer* res = offered;
+    mg_status s = rope_plan(ex->handle, H(x), &rp, &res, &ra);
+    *result = res;
+    if (s != MG_OK) {
+        *status = s;
+        return true;
+    }
+    bool attach = !deferred_uses(ex, buf(res)) && (!ex->deferred_rope || same_rope(ex->rope, ra));
+    if (attach) {
+        const size_t n = ex->deferred.size();
+        k::GemmArgs gs[3];
+        float* ro[3] = {nullptr, nullptr, nullptr};
+        for (size_t i = 0; i < n; i++) {
+            gs[i] = ex->deferred[i].g;
+            ro[i] = ex->deferred[i].rope_out ? (float*)ex->deferred[i].rope_out->ptr : nullptr;
+        }
+        ro[member] = (float*)buf(res)->ptr;
+        attach = k::gemm_group_eligible(gs, (int)n, &ra, ro);
+    }
+    if (!attach) {  // the group launches, then this rope on its own
+        s = flush_deferred(ex);
+        *status = s == MG_OK ? k::rope(d, (const float*)x->ptr, (float*)buf(res)->ptr, ra) : s;
+        return true;
+    }
+    ex->deferred[member].rope_out = buf(res);
+    ex->rope = ra;
+    ex->deferred_rope = true;
+    *status = MG_OK;
+    return true;
 }
 
 // Role of an invocation's output under the tensor-parallel plan
@@ -599,8 +755,13 @@ mg_status mg_executor_submit_kernel(mg_executor* ex, const mg_invocation* inv) {
     if (prev != ex->storage.end() && !reads_output && !data_checked && prev->second->owned) offered = H(prev->second);
     mg_buffer* result = offered;
     const int role = ex->comm ? tp_role(ex, inv) : 0;
-    s = dispatch(ex, inv, &result);
-    if (s == MG_OK && role == 2) s = comm_all_reduce_buffer(ex->comm, buf(result));
+    // During a step capture (one rank), projections of one input are grouped into one launch.
+    const bool taken = ex->capturing && !ex->comm && capture_defer(ex, inv, offered, &result, &s);
+    if (!taken) {
+        s = flush_deferred(ex);
+        if (s == MG_OK) s = dispatch(ex, inv, &result);
+        if (s == MG_OK && role == 2) s = comm_all_reduce_buffer(ex->comm, buf(result));
+    }
     if (s != MG_OK) {
         // The previous value stays; a fresh buffer made for this call is dropped.
         if (result && result != offered) buffer_free(buf(result));
@@ -638,13 +799,14 @@ mg_status mg_executor_end_step_capture(mg_executor* ex) {
     std::lock_guard<std::mutex> g(ex->lock);
     if (!ex->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "no step capture is in progress");
     Device* d = ex->device;
+    const mg_status fs = flush_deferred(ex);  // the last deferred group
     cudaGraph_t gph = nullptr;
     cudaError_t e = cudaStreamEndCapture(d->stream, &gph);
     ex->capturing = d->capturing = false;
     flush_deferred_frees(d);
-    if (e != cudaSuccess) {
+    if (e != cudaSuccess || fs != MG_OK) {
         if (gph) cudaGraphDestroy(gph);
-        return from_cuda(e, "ending the step capture");
+        return fs != MG_OK ? fs : from_cuda(e, "ending the step capture");
     }
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, gph, 0);
@@ -668,6 +830,8 @@ mg_status mg_executor_abort_step_capture(mg_executor* ex) {
     std::lock_guard<std::mutex> g(ex->lock);
     if (!ex->capturing) return MG_OK;
     cudaGraph_t gph = nullptr;
+    ex->deferred.clear();
+    ex->deferred_rope = false;
     cudaStreamEndCapture(ex->device->stream, &gph);
     cudaGetLastError();
     if (gph) cudaGraphDestroy(gph);

@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "internal.h"
+#include "rope.cuh"
 #include "sm100.cuh"
 
 namespace mg {
@@ -134,6 +135,13 @@ struct TcParams {
     int splits;        // CTAs per cluster (blockIdx.y), each over its own range of k
     int b_early;       // B is a stable prepared weight: its first loads may precede pdl_enter()
     int* error;        // device word set when a wait times out
+    // Grouped projection: `groups` (1-3) weights multiply the same A side by side (tiles_n is
+    // per weight); weight g writes outs[g] and, when rope_out[g] is set, also the rows of
+    // outs[g] rotated by `rope` (interleaved pairs) into rope_out[g].
+    int groups;
+    float* outs[3];
+    float* rope_out[3];
+    RopeK rope;
 };
 
 // Split-k modes: kNoSplit; kSplitOwnRecv -- the receive slots have a region of their own (free
@@ -174,6 +182,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                    const __grid_constant__ CUtensorMap map_b2hi, const __grid_constant__ CUtensorMap map_b2lo,
+                   const __grid_constant__ CUtensorMap map_b3hi, const __grid_constant__ CUtensorMap map_b3lo,
                    TcParams p) {
     using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
@@ -202,13 +211,19 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
 
     // Grouped rasterisation of the output tiles (blockIdx.x); blockIdx.y is the k split.
     const int tile = blockIdx.x;
-    const int group_size = kGroupM * p.tiles_n;
+    const int group_size = kGroupM * p.tiles_n * p.groups;
     const int group = tile / group_size;
     const int first_m = group * kGroupM;
     const int rows_in_group = min(p.tiles_m - first_m, kGroupM);
     const int tm = first_m + (tile % group_size) % rows_in_group;
-    const int tn = (tile % group_size) / rows_in_group;
+    const int tn_all = (tile % group_size) / rows_in_group;
+    const int wsel = tn_all / p.tiles_n;  // the weight of a grouped projection (0 otherwise)
+    const int tn = tn_all - wsel * p.tiles_n;
     const int m0 = tm * BM, n0 = tn * BN;
+    const CUtensorMap* map_whi = wsel == 0 ? &map_bhi : wsel == 1 ? &map_b2hi : &map_b3hi;
+    const CUtensorMap* map_wlo = wsel == 0 ? &map_blo : wsel == 1 ? &map_b2lo : &map_b3lo;
+    float* const outp = wsel == 0 ? p.outs[0] : wsel == 1 ? p.outs[1] : p.outs[2];
+    float* const ropep = wsel == 0 ? p.rope_out[0] : wsel == 1 ? p.rope_out[1] : p.rope_out[2];
     const int num_kb_total = (int)((p.k + BK - 1) / BK);
     const int kb0 = blockIdx.y * p.kb_per_split;
     const int num_kb = max(0, min(num_kb_total, kb0 + p.kb_per_split) - kb0);
@@ -227,8 +242,8 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
         const uint32_t st = base + s * S::kStage;
         mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
         const int kx = (kb0 + i) * BK;
-        tma_load_2d(st + 2 * S::kATile, &map_bhi, full_bar(s), kx, n0);
-        tma_load_2d(st + 2 * S::kATile + S::kBTile, &map_blo, full_bar(s), kx, n0);
+        tma_load_2d(st + 2 * S::kATile, map_whi, full_bar(s), kx, n0);
+        tma_load_2d(st + 2 * S::kATile + S::kBTile, map_wlo, full_bar(s), kx, n0);
         if (NB == 2) {
             tma_load_2d(st + 2 * S::kATile + 2 * S::kBTile, &map_b2hi, full_bar(s), kx, n0);
             tma_load_2d(st + 2 * S::kATile + 3 * S::kBTile, &map_b2lo, full_bar(s), kx, n0);
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
     };
     {
         constexpr int kVec = BN / 4;  // float4 per row
-        const bool vec = (p.n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
+        const bool vec = (p.n % 4 == 0) && ((reinterpret_cast<uintptr_t>(outp) & 15) == 0) &&
                          (p.addend_mode == 0 || (reinterpret_cast<uintptr_t>(p.addend) & 15) == 0);
         for (int e = threadIdx.x; e < (r_end - r_begin) * kVec; e += blockDim.x) {
             const int lr = e / kVec, c4 = (e % kVec) * 4;
@@ -471,10 +486,24 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
 #pragma unroll
                 for (int j = 0; j < 4; j++) o[j] = (o[j] * (1.0f / (1.0f + expf(-o[j])))) * u[j];
             }
-            float* orow = p.out + row * p.n;
+            float* orow = outp + row * p.n;
             if (full4) {
                 if (p.addend_mode != 0) o[0] += add4.x, o[1] += add4.y, o[2] += add4.z, o[3] += add4.w;
                 *reinterpret_cast<float4*>(orow + col) = make_float4(o[0], o[1], o[2], o[3]);
+                if (ropep) {
+                    // RoPE of this float4 (two interleaved pairs of one head), the rope kernel's
+                    // arithmetic on the same values.
+                    const uint64_t ch = col % p.rope.head_width;
+                    float4 y = make_float4(o[0], o[1], o[2], o[3]);
+                    if (ch < p.rope.dimension) {
+                        const float2 r0 = rope_cs(p.rope, row, ch >> 1), r1 = rope_cs(p.rope, row, (ch >> 1) + 1);
+                        y.x = o[0] * r0.x - o[1] * r0.y;
+                        y.y = o[0] * r0.y + o[1] * r0.x;
+                        y.z = o[2] * r1.x - o[3] * r1.y;
+                        y.w = o[2] * r1.y + o[3] * r1.x;
+                    }
+                    *reinterpret_cast<float4*>(ropep + row * p.n + col) = y;
+                }
             } else {
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
@@ -553,7 +582,7 @@ mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
                 "configuring the tensor-core matmul");
         configured[d->ordinal & 63] = true;
     }
-    const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
+    const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n * p.groups;
     if (tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "matmul has too many output tiles");
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(S::kThreads, 1, 1);
@@ -591,7 +620,7 @@ mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
     attr[0].val.clusterDim.y = (unsigned)p.splits;  // the k splits of one tile share a cluster
     cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits, 1);
     cfg.numAttrs = d->pdl ? 2 : 1;
-    MG_CUDA(cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p),
+    MG_CUDA(cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], maps[7], p),
             "tensor-core matmul launch");
     return launched(d, "tensor-core matmul launch");
 }
@@ -657,7 +686,12 @@ int pick_bn(const Device* d, uint64_t m, uint64_t n) {
 
 namespace k {
 
-mg_status gemm_tc(Device* d, const GemmArgs& g) {
+// One launch for `count` (1-3) matmuls that share A and their shape: a grouped projection
+// (the decoder layer's q, k and v), each optionally also written rotated by `rope`
+// (rope_outs[i], or null).  count > 1 or a rope needs plain matmuls: no gate, no addend, no
+// transposes, f32 rows with 16-byte alignment; the caller checks (gemm_group_eligible).
+mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* rope, float* const* rope_outs) {
+    const GemmArgs& g = gs[0];
     const uint64_t kp = gemm_kp(g.k);  // TMA row strides are multiples of 16 bytes
     const int nb = g.gated ? 2 : 1;
     // A: raw through TMA (split inside the kernel) when it is K-major with 16-byte rows and
@@ -673,25 +707,31 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
         ahi = a_split;
         alo = a_split + g.m * kp;
     }
-    const float* bhi[2];
-    const float* blo[2];
-    bool need_split = false;
-    for (int z = 0; z < nb; z++) need_split |= g.b_prep[z] == nullptr;
+    // B terms: [term or weight] -> hi, lo ([n, kp] each)
+    const int nw = nb == 2 ? 2 : count;
+    const float* bhi[3];
+    const float* blo[3];
+    int need_split = 0;
+    for (int w = 0; w < nw; w++) need_split += (nb == 2 ? g.b_prep[w] : gs[w].b_prep[0]) == nullptr;
     float* b_split = nullptr;
-    if (need_split) MG_TRY(scratch(d, 2, (size_t)nb * 2 * g.n * kp * sizeof(float), (void**)&b_split));
-    for (int z = 0; z < nb; z++) {
-        if (g.b_prep[z]) {
-            bhi[z] = g.b_prep[z];
-            blo[z] = g.b_prep[z] + g.n * kp;
+    if (need_split) MG_TRY(scratch(d, 2, (size_t)nw * 2 * g.n * kp * sizeof(float), (void**)&b_split));
+    bool stable = true;
+    for (int w = 0; w < nw; w++) {
+        const float* prep = nb == 2 ? g.b_prep[w] : gs[w].b_prep[0];
+        stable = stable && prep && (nb == 2 ? g.b_stable : gs[w].b_stable);
+        if (prep) {
+            bhi[w] = prep;
+            blo[w] = prep + g.n * kp;
         } else {
-            float* hi = b_split + (size_t)z * 2 * g.n * kp;
+            float* hi = b_split + (size_t)w * 2 * g.n * kp;
             float* lo = hi + g.n * kp;
-            MG_TRY(split_operand(d, z ? g.b2 : g.b, g.n, g.k, g.transpose_b != 0, hi, lo, kp));
-            bhi[z] = hi;
-            blo[z] = lo;
+            const float* src = nb == 2 ? (w ? g.b2 : g.b) : gs[w].b;
+            MG_TRY(split_operand(d, src, g.n, g.k, g.transpose_b != 0, hi, lo, kp));
+            bhi[w] = hi;
+            blo[w] = lo;
         }
     }
-    int bn = pick_bn(d, g.m, g.n);
+    int bn = pick_bn(d, g.m, g.n * (uint64_t)count);
     TcParams p;
     p.out = g.out;
     p.addend = g.addend;
@@ -700,7 +740,14 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
     p.n = g.n;
     p.k = g.k;
     p.error = d->flags + 2;
-    p.b_early = g.b_stable && g.b_prep[0] && (nb == 1 || g.b_prep[1]) ? 1 : 0;
+    p.b_early = stable ? 1 : 0;
+    p.groups = count;
+    for (int i = 0; i < 3; i++) {
+        p.outs[i] = i < count ? gs[i].out : nullptr;
+        p.rope_out[i] = i < count && rope_outs ? rope_outs[i] : nullptr;
+    }
+    if (rope) p.rope = *rope;
+    else memset(&p.rope, 0, sizeof p.rope);
     // Split k when the output grid leaves SMs idle: as many splits as fit in one wave, at
     // least 2 k-blocks each.  A gated split-k tile is at most 64 wide (its receive slots
     // share the shared memory with the ring).
@@ -708,7 +755,7 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
     auto plan_splits = [&](int width) {
         p.tiles_m = (int)((g.m + BM - 1) / BM);
         p.tiles_n = (int)((g.n + width - 1) / width);
-        const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n;
+        const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n * count;
         int splits = 1;
         if (tiles * 2 <= (uint64_t)d->sm_count && num_kb >= 4) {
             splits = (int)((uint64_t)d->sm_count / tiles);
@@ -724,7 +771,7 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
         bn = 64;
         plan_splits(bn);
     }
-    CUtensorMap maps[6];
+    CUtensorMap maps[8];
     if (a_raw) {
         MG_TRY(make_map(&maps[0], ahi, g.m, g.k, g.k, BM));
         maps[1] = maps[0];
@@ -732,20 +779,72 @@ mg_status gemm_tc(Device* d, const GemmArgs& g) {
         MG_TRY(make_map(&maps[0], ahi, g.m, kp, kp, BM));
         MG_TRY(make_map(&maps[1], alo, g.m, kp, kp, BM));
     }
-    MG_TRY(make_map(&maps[2], bhi[0], g.n, kp, kp, bn));
-    MG_TRY(make_map(&maps[3], blo[0], g.n, kp, kp, bn));
-    if (nb == 2) {
-        MG_TRY(make_map(&maps[4], bhi[1], g.n, kp, kp, bn));
-        MG_TRY(make_map(&maps[5], blo[1], g.n, kp, kp, bn));
-    } else {
-        maps[4] = maps[2];
-        maps[5] = maps[3];
+    for (int w = 0; w < 3; w++) {
+        if (w < nw) {
+            MG_TRY(make_map(&maps[2 + 2 * w], bhi[w], g.n, kp, kp, bn));
+            MG_TRY(make_map(&maps[3 + 2 * w], blo[w], g.n, kp, kp, bn));
+        } else {
+            maps[2 + 2 * w] = maps[2];
+            maps[3 + 2 * w] = maps[3];
+        }
     }
     mg_status s;
     if (nb == 2) s = a_raw ? launch_bn<2, true>(d, bn, p, maps) : launch_bn<2, false>(d, bn, p, maps);
     else s = a_raw ? launch_bn<1, true>(d, bn, p, maps) : launch_bn<1, false>(d, bn, p, maps);
     MG_TRY(s);
     return MG_OK;
+}
+
+mg_status gemm_tc(Device* d, const GemmArgs& g) { return gemm_tc_group(d, &g, 1, nullptr, nullptr); }
+
+bool gemm_group_eligible(const GemmArgs* gs, int count, const RopeArgs* rope, float* const* rope_outs) {
+    if (count < 1 || count > 3) return false;
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const GemmArgs& g = gs[0];
+    if (!gemm_uses_tensor_cores(g.m, g.n, g.k, 0, g.b) || g.n % 4 != 0) return false;
+    for (int i = 0; i < count; i++) {
+        const GemmArgs& x = gs[i];
+        if (x.gated || x.addend_mode != 0 || x.transpose_a || x.transpose_b || x.a != g.a || x.m != g.m ||
+            x.n != g.n || x.k != g.k || !al(x.out))
+            return false;
+        if (rope_outs && rope_outs[i] && !al(rope_outs[i])) return false;
+    }
+    if (rope) {  // interleaved pairs whose float4 groups never straddle a head or the rotary part
+        const uint64_t hw = rope->cols / rope->head_count;
+        if (rope->half_split || rope->cols != g.n || rope->rows != g.m || hw % 4 != 0 || rope->dimension % 4 != 0)
+            return false;
+    }
+    return true;
+}
+
+mg_status gemm_group(Device* d, const GemmArgs* gs, int count, const RopeArgs* rope, float* const* rope_outs) {
+    if (!gemm_group_eligible(gs, count, rope, rope_outs))
+        return fail(MG_EXECUTION_FAILED, "matmul group is not eligible for one launch");
+    RopeK rk;
+    memset(&rk, 0, sizeof rk);
+    if (rope) {
+        rk.rows = rope->rows;
+        rk.cols = rope->cols;
+        rk.half = rope->half;
+        rk.dimension = rope->dimension;
+        rk.position_offset = rope->position_offset;
+        rk.head_count = rope->head_count;
+        rk.head_width = rope->cols / rope->head_count;
+        rk.rotated_pairs = rope->rotated_pairs;
+        rk.base = rope->base;
+        rk.scale = rope->scale;
+        rk.banded_factor = rope->banded_factor;
+        rk.low_freq_factor = rope->low_freq_factor;
+        rk.high_freq_factor = rope->high_freq_factor;
+        rk.original_context_length = rope->original_context_length;
+        rk.yarn_factor = rope->yarn_factor;
+        rk.yarn_low = rope->yarn_low;
+        rk.yarn_high = rope->yarn_high;
+        rk.amplitude = rope->amplitude;
+        rk.half_split = 0;
+        rk.vec = 1;
+    }
+    return gemm_tc_group(d, gs, count, rope ? &rk : nullptr, rope_outs);
 }
 
 bool gemm_uses_tensor_cores(uint64_t m, uint64_t n, uint64_t k, int transpose_b, const float* b) {

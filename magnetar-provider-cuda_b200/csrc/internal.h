@@ -191,7 +191,19 @@ struct AttentionArgs {
     float scale;
 };
 mg_status attention(Device* d, const AttentionArgs& a);
+
+// One launch for `count` (1-3) plain matmuls that share A and their shape (a grouped
+// projection), each optionally also written rotated by `rope` into rope_outs[i] (null: none).
+bool gemm_group_eligible(const GemmArgs* gs, int count, const RopeArgs* rope, float* const* rope_outs);
+mg_status gemm_group(Device* d, const GemmArgs* gs, int count, const RopeArgs* rope, float* const* rope_outs);
 }  // namespace k
+
+// Everything a matmul / rope call does but the launch: validation, the output (offer rule) and
+// the weights' operand forms.  The executor's step capture defers launches to fuse them; the
+// launch is then k::gemm / k::gemm_group / k::rope with the result.
+mg_status matmul_plan(mg_device* h, const mg_buffer* a, const mg_buffer* b, const mg_buffer* b2, const mg_buffer* addend,
+                      int addend_mode, int ta, int tb, mg_buffer** out, k::GemmArgs* g);
+mg_status rope_plan(mg_device* h, const mg_buffer* x, const mg_rope_params* p, mg_buffer** out, k::RopeArgs* a);
 
 inline mg_status launched(Device* d, const char* what) {
     d->launches.fetch_add(1, std::memory_order_relaxed);

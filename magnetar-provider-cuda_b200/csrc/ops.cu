@@ -143,9 +143,13 @@ mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int t
     return MG_OK;
 }
 
-// src/kernels.rs:5518-5580: shapes, transposes and the addend's shape.
-mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, const mg_buffer* b2h,
-                      const mg_buffer* addh, int addend_mode, int ta, int tb, mg_buffer** out) {
+}  // namespace
+
+namespace mg {
+// src/kernels.rs:5518-5580: shapes, transposes and the addend's shape; the output and the
+// weights' operand forms -- everything a matmul does but the launch.
+mg_status matmul_plan(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, const mg_buffer* b2h,
+                      const mg_buffer* addh, int addend_mode, int ta, int tb, mg_buffer** out, k::GemmArgs* gp) {
     MG_TRY(device_check(h));
     MG_TRY(need(ah, "a"));
     MG_TRY(need(bh, "b"));
@@ -208,7 +212,18 @@ mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
         if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1], &built));
         g.b_stable = !built && g.b_prep[0] && (!b2 || g.b_prep[1]);
     }
-    return k::gemm(d, g);
+    *gp = g;
+    return MG_OK;
+}
+}  // namespace mg
+
+namespace {
+
+mg_status matmul_impl(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, const mg_buffer* b2h,
+                      const mg_buffer* addh, int addend_mode, int ta, int tb, mg_buffer** out) {
+    k::GemmArgs g;
+    MG_TRY(matmul_plan(h, ah, bh, b2h, addh, addend_mode, ta, tb, out, &g));
+    return k::gemm(dev(h), g);
 }
 
 }  // namespace
@@ -390,6 +405,16 @@ mg_status mg_rmsnorm(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, flo
 
 // src/kernels.rs:4224-4355
 mg_status mg_rope(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp, mg_buffer** out) {
+    k::RopeArgs a;
+    MG_TRY(mg::rope_plan(h, xh, pp, out, &a));
+    return k::rope(dev(h), (const float*)buf(xh)->ptr, (float*)buf(*out)->ptr, a);
+}
+
+}  // extern "C"
+
+namespace mg {
+// src/kernels.rs:4224-4355: everything a rope does but the launch.
+mg_status rope_plan(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp, mg_buffer** out, k::RopeArgs* ap) {
     MG_TRY(device_check(h));
     MG_TRY(need(xh, "input"));
     if (!pp) return fail(MG_INVALID_ARGUMENT, "null rope parameters");
@@ -443,8 +468,12 @@ mg_status mg_rope(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp, m
     a.yarn_high = p.yarn_high;
     a.amplitude = p.yarn_factor > 0.0f ? p.amplitude : 1.0f;
     a.half_split = p.pairing;
-    return k::rope(d, (const float*)x->ptr, (float*)o->ptr, a);
+    *ap = a;
+    return MG_OK;
 }
+}  // namespace mg
+
+extern "C" {
 
 // src/kernels.rs:4357-4386
 mg_status mg_softmax(mg_device* h, const mg_buffer* xh, mg_buffer** out) {

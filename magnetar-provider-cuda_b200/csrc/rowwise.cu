@@ -10,6 +10,7 @@
 // each (row, pair) rotation once for all heads.  The per-element f32 expressions are the
 // reference's; only the order of the row reductions differs (a tree instead of a serial sum).
 #include "internal.h"
+#include "rope.cuh"
 
 namespace mg {
 namespace {
@@ -139,40 +140,6 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const float* __rest
 // the rotation (cos, sin) of each of the row's `half` pairs -- the reference's exact
 // per-pair expression -- into shared memory, then rotates every head's pairs with it.
 // =====================================================================================
-struct RopeK {
-    uint64_t rows, cols, half, dimension, position_offset, head_count, head_width, rotated_pairs;
-    float base, scale, banded_factor, low_freq_factor, high_freq_factor, original_context_length;
-    float yarn_factor, yarn_low, yarn_high, amplitude;
-    int half_split;
-    int vec;  // 1: 16-byte path (alignment and divisibility checked on the host)
-};
-
-__device__ __forceinline__ float2 rope_cs(const RopeK& p, uint64_t row, uint64_t pair) {
-    float position = (float)(p.position_offset + row) * p.scale;
-    float frequency = powf(p.base, -2.0f * (float)pair / (float)p.dimension);
-    if (p.banded_factor > 0.0f) {
-        float wavelength = 6.283185307179586f / frequency;
-        if (wavelength < p.original_context_length / p.high_freq_factor) {
-        } else if (wavelength > p.original_context_length / p.low_freq_factor) {
-            frequency = frequency / p.banded_factor;
-        } else {
-            float smooth = (p.original_context_length / wavelength - p.low_freq_factor) /
-                           (p.high_freq_factor - p.low_freq_factor);
-            frequency = (1.0f - smooth) * frequency / p.banded_factor + smooth * frequency;
-        }
-    }
-    if (p.yarn_factor > 0.0f) {
-        float high = p.yarn_low == p.yarn_high ? p.yarn_high + 0.001f : p.yarn_high;
-        float ramp = ((float)pair - p.yarn_low) / (high - p.yarn_low);
-        ramp = fminf(fmaxf(ramp, 0.0f), 1.0f);
-        float interpolated = frequency / p.yarn_factor;
-        frequency = interpolated * ramp + frequency * (1.0f - ramp);
-    }
-    float angle = pair < p.rotated_pairs ? position * frequency : 0.0f;
-    float amp = pair < p.rotated_pairs ? p.amplitude : 1.0f;
-    return make_float2(cosf(angle) * amp, sinf(angle) * amp);
-}
-
 __global__ void __launch_bounds__(256) rope_kernel(const float* __restrict__ x, float* __restrict__ out, RopeK p) {
     pdl_enter();
     extern __shared__ float2 cs[];  // [half]
