@@ -150,12 +150,16 @@ struct TcParams {
 // barrier after staging tells the senders every ring is drained; keeps the ring deep for long k).
 constexpr int kNoSplit = 0, kSplitOwnRecv = 1, kSplitRingRecv = 2;
 
-template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT>
+template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT, bool B_RAW = false>
 struct TcShape {
     static constexpr int kATile = BM * BK * 4;  // bytes of one A term tile
     static constexpr int kBTile = BN * BK * 4;  // bytes of one B term tile
-    static constexpr int kStage = 2 * kATile + NB * 2 * kBTile;
-    static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + NB * 2 * kBTile;  // TMA bytes per stage
+    // B_RAW: TMA brings B's raw f32 [BK][BN] tile (N-major, as B lies in memory) behind the B
+    // terms, and the converter warps split and transpose it into the K-major hi / lo terms.
+    static constexpr int kOffBRaw = 2 * kATile + NB * 2 * kBTile;
+    static constexpr int kStage = kOffBRaw + (B_RAW ? kBTile : 0);
+    static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + (B_RAW ? kBTile : NB * 2 * kBTile);  // TMA bytes per stage
+    static_assert(!B_RAW || NB == 1, "raw B is for plain matmuls");
     static constexpr int kRing = STAGES * kStage;
     static constexpr int kLd = BN + 4;  // row stride (floats) of a staged tile and of the receive slots
     static_assert(NB * BM * kLd * 4 <= kRing, "the staged tile fits the drained ring");
@@ -169,7 +173,7 @@ struct TcShape {
     static constexpr int kSmem = kRing + kBars + kRecv + 1024 /* align */;
     static constexpr uint32_t kTmemCols =
         NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
-    static constexpr int kThreads = A_RAW ? 320 : 192;
+    static constexpr int kThreads = (A_RAW || B_RAW) ? 320 : 192;
 };
 
 // The CTAs of one output tile form a cluster along blockIdx.y, each multiplying its own range
@@ -177,14 +181,15 @@ struct TcShape {
 // memory of the CTA that owns their band; each CTA then sums its band's partials in
 // cluster-rank order and writes the finished band with coalesced stores (bias / residual /
 // SwiGLU applied).  One kernel, deterministic, and the partial sums never leave the chip.
-template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT>
-__global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThreads, 1)
+template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT, bool B_RAW>
+__global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                    const __grid_constant__ CUtensorMap map_b2hi, const __grid_constant__ CUtensorMap map_b2lo,
                    const __grid_constant__ CUtensorMap map_b3hi, const __grid_constant__ CUtensorMap map_b3lo,
                    TcParams p) {
-    using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT>;
+    using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>;
+    constexpr bool kConvert = A_RAW || B_RAW;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -242,6 +247,10 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
         const uint32_t st = base + s * S::kStage;
         mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
         const int kx = (kb0 + i) * BK;
+        if (B_RAW) {
+            tma_load_2d(st + S::kOffBRaw, map_whi, full_bar(s), n0, kx);  // [BK rows of k][BN columns]
+            return;
+        }
         tma_load_2d(st + 2 * S::kATile, map_whi, full_bar(s), kx, n0);
         tma_load_2d(st + 2 * S::kATile + S::kBTile, map_wlo, full_bar(s), kx, n0);
         if (NB == 2) {
@@ -317,7 +326,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
             for (int i = 0; i < num_kb; i++) {
                 const int s = i % STAGES;
                 const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
-                if (!mbar_wait(full_bar(s), phase) || (A_RAW && !mbar_wait(conv_bar(s), phase))) {
+                if (!mbar_wait(full_bar(s), phase) || (kConvert && !mbar_wait(conv_bar(s), phase))) {
                     *abort_flag = 1;
                     atomicExch(p.error, 1);
                     ok = false;
@@ -351,8 +360,8 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
         }
         __syncwarp();
     } else if (warp >= 6) {
-        // ---- A converter: raw f32 tile -> hi (in place) + lo ------------------------------
-        if (A_RAW) {
+        // ---- converters: raw f32 A tile -> hi (in place) + lo; raw B tile -> K-major hi / lo
+        if (kConvert) {
             const int t = threadIdx.x - 192;  // 0..127
             for (int i = 0; i < num_kb; i++) {
                 const int s = i % STAGES;
@@ -362,15 +371,37 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT>::kThread
                     atomicExch(p.error, 1);
                     // still arrive so that the MMA warp does not wait for us
                 }
-                float4* a_hi = reinterpret_cast<float4*>(base_ptr + s * S::kStage);
-                float4* a_lo = reinterpret_cast<float4*>(base_ptr + s * S::kStage + S::kATile);
+                if (A_RAW) {
+                    float4* a_hi = reinterpret_cast<float4*>(base_ptr + s * S::kStage);
+                    float4* a_lo = reinterpret_cast<float4*>(base_ptr + s * S::kStage + S::kATile);
 #pragma unroll
-                for (int j = 0; j < S::kATile / 16 / 128; j++) {
-                    const int idx = t + j * 128;
-                    float4 h, l;
-                    split4(a_hi[idx], h, l);
-                    a_hi[idx] = h;
-                    a_lo[idx] = l;
+                    for (int j = 0; j < S::kATile / 16 / 128; j++) {
+                        const int idx = t + j * 128;
+                        float4 h, l;
+                        split4(a_hi[idx], h, l);
+                        a_hi[idx] = h;
+                        a_lo[idx] = l;
+                    }
+                }
+                if (B_RAW) {
+                    // Column n of the raw tile (BK values of k, BN floats apart) becomes row n of
+                    // the K-major terms: 16-byte chunk c (k = 4c .. 4c+3) at byte
+                    // n * 128 + (c ^ (n % 8)) * 16, the layout TMA's 128-byte swizzle gives.
+                    const float* raw = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kOffBRaw);
+                    uint8_t* b_hi = base_ptr + s * S::kStage + 2 * S::kATile;
+                    uint8_t* b_lo = b_hi + S::kBTile;
+#pragma unroll
+                    for (int j = 0; j < BN * (BK / 4) / 128; j++) {
+                        const int task = t + j * 128;
+                        const int n = task % BN, c = task / BN;
+                        const float4 x = make_float4(raw[(4 * c) * BN + n], raw[(4 * c + 1) * BN + n],
+                                                     raw[(4 * c + 2) * BN + n], raw[(4 * c + 3) * BN + n]);
+                        float4 h, l;
+                        split4(x, h, l);
+                        const int off = n * 128 + ((c ^ (n & 7)) * 16);
+                        *reinterpret_cast<float4*>(b_hi + off) = h;
+                        *reinterpret_cast<float4*>(b_lo + off) = l;
+                    }
                 }
                 fence_proxy_async();  // make the generic-proxy writes visible to tcgen05.mma
                 mbar_arrive(conv_bar(s));
@@ -550,6 +581,22 @@ mg_status make_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t c
     return MG_OK;
 }
 
+// B as it lies in memory, row-major [k, n] f32: box [BK rows x box_cols], no swizzle; rows and
+// columns past the end read as zero.
+mg_status make_raw_b_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n, uint32_t box_cols) {
+    auto fn = encode_fn();
+    if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {n, k};
+    cuuint64_t strides[1] = {n * sizeof(float)};
+    cuuint32_t box[2] = {box_cols, BK};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(b), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
 inline unsigned grid_cap(const Device* d, uint64_t items) {
     uint64_t want = (items + 255) / 256, cap = (uint64_t)d->sm_count * 8;
     return (unsigned)(want < 1 ? 1 : want > cap ? cap : want);
@@ -571,11 +618,11 @@ mg_status split_operand(Device* d, const float* src, uint64_t rows, uint64_t k, 
     return launched(d, "operand split kernel launch");
 }
 
-template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT>
+template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT, bool B_RAW = false>
 mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
-    using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT>;
+    using S = TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>;
     static_assert(S::kSmem <= 227 * 1024, "shared memory budget");
-    auto kernel = gemm_tc_kernel<BN, NB, STAGES, A_RAW, SPLIT>;
+    auto kernel = gemm_tc_kernel<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>;
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
         MG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
@@ -662,6 +709,21 @@ mg_status launch_bn(Device* d, int bn, const TcParams& p, const CUtensorMap* map
     }
 }
 
+// Raw B: the ring holds B's raw tile as well, so it is shallower; with split k the partials
+// are received in the drained ring.
+template <bool A_RAW>
+mg_status launch_bn_raw_b(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
+    const bool split = p.splits > 1;
+    if (bn == 128)
+        return split ? launch_tc<128, 1, 2, A_RAW, kSplitRingRecv, true>(d, p, maps)
+                     : launch_tc<128, 1, 2, A_RAW, kNoSplit, true>(d, p, maps);
+    if (bn == 64)
+        return split ? launch_tc<64, 1, 3, A_RAW, kSplitRingRecv, true>(d, p, maps)
+                     : launch_tc<64, 1, 3, A_RAW, kNoSplit, true>(d, p, maps);
+    return split ? launch_tc<32, 1, 4, A_RAW, kSplitRingRecv, true>(d, p, maps)
+                 : launch_tc<32, 1, 4, A_RAW, kNoSplit, true>(d, p, maps);
+}
+
 bool tensor_cores_enabled() {
     static int enabled = -1;
     if (enabled < 0) {
@@ -707,16 +769,24 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
         ahi = a_split;
         alo = a_split + g.m * kp;
     }
+    // B raw (split and transposed in the kernel, no separate pass over B): for a plain matmul
+    // with one row of tiles (M <= 128) whose B has no prepared form.  Measured at K = N = 4096:
+    // M = 128 takes 64 us against 97 us with the split pass; with more rows of tiles, or a
+    // prepared weight, the shallower ring it needs costs more than it saves (M = 2048: 0.62 vs
+    // 0.39 ms; a prepared weight at M = 128: 64 vs 43 us).
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const bool b_raw = count == 1 && nb == 1 && !g.transpose_b && g.n % 4 == 0 && al16(g.b) &&
+                       g.b_prep[0] == nullptr && g.m <= 128;
     // B terms: [term or weight] -> hi, lo ([n, kp] each)
     const int nw = nb == 2 ? 2 : count;
     const float* bhi[3];
     const float* blo[3];
     int need_split = 0;
-    for (int w = 0; w < nw; w++) need_split += (nb == 2 ? g.b_prep[w] : gs[w].b_prep[0]) == nullptr;
+    for (int w = 0; w < nw && !b_raw; w++) need_split += (nb == 2 ? g.b_prep[w] : gs[w].b_prep[0]) == nullptr;
     float* b_split = nullptr;
     if (need_split) MG_TRY(scratch(d, 2, (size_t)nw * 2 * g.n * kp * sizeof(float), (void**)&b_split));
     bool stable = true;
-    for (int w = 0; w < nw; w++) {
+    for (int w = 0; w < nw && !b_raw; w++) {
         const float* prep = nb == 2 ? g.b_prep[w] : gs[w].b_prep[0];
         stable = stable && prep && (nb == 2 ? g.b_stable : gs[w].b_stable);
         if (prep) {
@@ -740,7 +810,8 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
     p.n = g.n;
     p.k = g.k;
     p.error = d->flags + 2;
-    p.b_early = stable ? 1 : 0;
+    // raw B may load early when it is a weight (nothing earlier in the stream writes it)
+    p.b_early = (b_raw ? g.b_stable != 0 : stable) ? 1 : 0;
     p.groups = count;
     for (int i = 0; i < 3; i++) {
         p.outs[i] = i < count ? gs[i].out : nullptr;
@@ -780,7 +851,11 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
         MG_TRY(make_map(&maps[1], alo, g.m, kp, kp, BM));
     }
     for (int w = 0; w < 3; w++) {
-        if (w < nw) {
+        if (b_raw) {
+            if (w == 0) MG_TRY(make_raw_b_map(&maps[2], g.b, g.k, g.n, (uint32_t)bn));
+            else maps[2 + 2 * w] = maps[2];
+            maps[3 + 2 * w] = maps[2];
+        } else if (w < nw) {
             MG_TRY(make_map(&maps[2 + 2 * w], bhi[w], g.n, kp, kp, bn));
             MG_TRY(make_map(&maps[3 + 2 * w], blo[w], g.n, kp, kp, bn));
         } else {
@@ -788,6 +863,7 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
             maps[3 + 2 * w] = maps[3];
         }
     }
+    if (b_raw) return a_raw ? launch_bn_raw_b<true>(d, bn, p, maps) : launch_bn_raw_b<false>(d, bn, p, maps);
     mg_status s;
     if (nb == 2) s = a_raw ? launch_bn<2, true>(d, bn, p, maps) : launch_bn<2, false>(d, bn, p, maps);
     else s = a_raw ? launch_bn<1, true>(d, bn, p, maps) : launch_bn<1, false>(d, bn, p, maps);

@@ -413,6 +413,7 @@ mg_status gemv_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n) {
 // apply bias / residual / SwiGLU and write.  B is read exactly once; nothing goes through
 // global memory but the operands and the result.
 constexpr int kCStages = 4;
+constexpr int kMaxClusterCtas = 16;  // non-portable cluster size (checked against the GPU at launch)
 
 struct GemvClusterArgs {
     float* out;
@@ -433,7 +434,7 @@ struct GemvCShape {
     static constexpr int kStage = kB + kA;
     static constexpr int kRing = kCStages * kStage;
     static constexpr int kPart = M * kCols * 4;         // this CTA's partial [M][128]
-    static constexpr int kRecv = (M * kCols + 4 * 8) * 4;  // the other CTAs' partials of this CTA's band
+    static constexpr int kRecv = (M * kCols + 4 * kMaxClusterCtas) * 4;  // the other CTAs' partials of this CTA's band
     static_assert(kWarps * kPart <= kRing, "the warp partials fit the drained ring");
     static constexpr int kSmem = 128 + kRing + kPart + kRecv + 8 * (2 * kCStages + 1);
 };
@@ -600,14 +601,55 @@ mg_status gemv_a_map(CUtensorMap* map, const float* a, uint64_t m, uint64_t k, u
     return MG_OK;
 }
 
+// k slices of `splits` CTAs each, and the band of the output tile each cluster CTA finishes.
+void gemv_slices(GemvClusterArgs& p, uint64_t splits) {
+    const uint64_t kb = (p.k + kChunkRows - 1) / kChunkRows;
+    if (splits > kb) splits = kb;
+    if (splits < 1) splits = 1;
+    p.slice_len = ((kb + splits - 1) / splits) * kChunkRows;
+    p.splits = (int)((p.k + p.slice_len - 1) / p.slice_len);
+    if (p.splits < 1) p.splits = 1;
+    const int nc = p.splits * p.terms, F = (int)p.m * kCols;
+    p.band = ((F + nc - 1) / nc + 3) / 4 * 4;
+}
+
 template <int M>
-mg_status launch_cluster(Device* d, const GemvClusterArgs& p, uint64_t col_tiles, const CUtensorMap* maps) {
+mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const CUtensorMap* maps) {
     using S = GemvCShape<M>;
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
         MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
                 "configuring the cluster gemv kernel");
+        MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "allowing the cluster gemv kernel clusters of up to 16");
         configured[d->ordinal & 63] = true;
+    }
+    // Clusters larger than 8 only where the GPU holds them all in one wave (queried once per
+    // size); otherwise fewer k splits.
+    static int fits[kMaxClusterCtas + 1] = {0};  // 1 fits, -1 does not
+    while (p.splits * p.terms > 8) {
+        const int nc = p.splits * p.terms;
+        if (fits[nc] == 0) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
+            q.blockDim = dim3((kWarps + 1) * 32, 1, 1);
+            q.dynamicSmemBytes = S::kSmem;
+            cudaLaunchAttribute ca;
+            ca.id = cudaLaunchAttributeClusterDimension;
+            ca.val.clusterDim.x = 1;
+            ca.val.clusterDim.y = (unsigned)p.splits;
+            ca.val.clusterDim.z = (unsigned)p.terms;
+            q.attrs = &ca;
+            q.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_cluster_kernel<M>, &q) != cudaSuccess) {
+                (void)cudaGetLastError();
+                clusters = 0;
+            }
+            fits[nc] = (uint64_t)clusters >= col_tiles ? 1 : -1;
+        }
+        if (fits[nc] > 0) break;
+        gemv_slices(p, (uint64_t)p.splits - 1);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
@@ -721,18 +763,10 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
     if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
     const int terms = g.gated ? 2 : 1;
-    const uint64_t kb = (g.k + kChunkRows - 1) / kChunkRows;
     uint64_t splits = (uint64_t)d->sm_count * 2 / (col_tiles * terms);
-    const uint64_t max_splits = 8 / terms;
+    const uint64_t max_splits = kMaxClusterCtas / terms;
     if (splits > max_splits) splits = max_splits;
-    if (splits > kb) splits = kb;
-    if (splits < 1) splits = 1;
-    uint64_t slice_len = ((kb + splits - 1) / splits) * kChunkRows;
-    splits = (g.k + slice_len - 1) / slice_len;
-    if (splits < 1) splits = 1;
     const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
-    const int nc = (int)splits * terms;
-    const int F = (int)g.m * kCols;
     GemvClusterArgs p;
     p.out = g.out;
     p.addend = g.addend;
@@ -740,10 +774,8 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     p.m = g.m;
     p.n = g.n;
     p.k = g.k;
-    p.slice_len = slice_len;
-    p.splits = (int)splits;
     p.terms = terms;
-    p.band = ((F + nc - 1) / nc + 3) / 4 * 4;
+    gemv_slices(p, splits);
     p.error = d->flags + 2;
     CUtensorMap maps[3];
     MG_TRY(gemv_a_map(&maps[0], g.a, g.m, g.k, (uint32_t)mp));

@@ -248,6 +248,22 @@ def test_matmul(kernels, oracle, m, k, n):
     assert rel(got, oracle.matmul(a, b)) <= TOL_MATMUL
 
 
+@pytest.mark.parametrize("m,k,n", [(128, 512, 512), (200, 904, 136), (128, 2048, 2048), (513, 257, 132),
+                                   (64, 4096, 32), (300, 129, 65)])
+def test_matmul_with_weight_b(kernels, oracle, m, k, n):
+    # B marked as a weight: its tensor-core operand form is built by the first call and kept;
+    # both calls match the oracle and each other.  (Plain B at M <= 128 is split inside the
+    # kernel: the other matmul tests.)
+    r = rng(15)
+    a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
+    b = r.standard_normal((k, n)).astype(np.float32)
+    da, db = kernels.upload(a), kernels.upload(b).set_weight()
+    first = kernels.download(kernels.matmul(da, db))
+    second = kernels.download(kernels.matmul(da, db))
+    assert rel(first, oracle.matmul(a, b)) <= TOL_MATMUL
+    np.testing.assert_array_equal(first, second)
+
+
 @pytest.mark.parametrize("m,k,n", [(1, 300, 70), (16, 256, 128), (130, 200, 96), (16, 40000, 128)])
 @pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
 def test_matmul_transposed(kernels, oracle, m, k, n, ta, tb):
