@@ -13,9 +13,10 @@
 //   warp 0      TMA producer: 32-column k-blocks (one 128-byte swizzle row per tile row) of
 //               A and B into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM and issues the MMAs (one thread), committing each stage back;
-//   warps 2-5   read the accumulator (tcgen05.ld) into the drained shared-memory ring;
-//   warps 6-9   (when A arrives as raw f32) split each A tile into its hi/lo terms in shared
-//               memory, in place, so no separate pass over A is needed.
+//   warps 2-9   (when A or B arrives as raw f32) split each raw tile into its hi/lo terms in
+//               shared memory during the main loop, so no separate pass over the operand is
+//               needed; afterwards warps 2-5 read the accumulator (tcgen05.ld) into the drained
+//               shared-memory ring.
 // When the output grid alone would leave SMs idle, k is split across the CTAs of a thread-block
 // cluster; the partial tiles are then summed through distributed shared memory and every
 // thread writes finished rows (bias / residual / SwiGLU applied) with coalesced stores.
@@ -48,6 +49,7 @@ constexpr int BM = 128;
 constexpr int BK = 32;       // f32 k-columns per stage: one 128-byte swizzle row
 constexpr int kGroupM = 16;  // rasterisation: M-tiles walked together for L2 reuse
 constexpr int kMaxSplits = 8;  // k splits of one tile: the CTAs of one portable cluster
+constexpr int kConvThreads = 256;  // warps 2-9 split raw operand tiles during the main loop
 
 // ---- operand split ----------------------------------------------------------------------------
 __device__ __forceinline__ float tf32_round(float x) {
@@ -68,6 +70,20 @@ __device__ __forceinline__ void split4(float4 v, float4& hi, float4& lo) {
     split_tf32(v.y, hi.y, lo.y);
     split_tf32(v.z, hi.z, lo.z);
     split_tf32(v.w, hi.w, lo.w);
+}
+
+// The in-kernel split of raw operand tiles (on the MMA's critical path): hi = x truncated to
+// tf32 (no rounding, so nothing overflows), lo = tf32_rna(x - hi), which is exact to 2^-21 of
+// x -- inside the f32 contract with room to spare, and three instructions per value.
+__device__ __forceinline__ float4 trunc_tf32x4(float4 v) {
+    return make_float4(__uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                       __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                       __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                       __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+}
+__device__ __forceinline__ void split4_fast(float4 v, float4& hi, float4& lo) {
+    hi = trunc_tf32x4(v);
+    lo = make_float4(tf32_round(v.x - hi.x), tf32_round(v.y - hi.y), tf32_round(v.z - hi.z), tf32_round(v.w - hi.w));
 }
 
 // src [rows, k] (row stride ld) -> hi/lo [rows, kp], zero past k.  16-byte vectors when the
@@ -267,7 +283,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
-            mbar_init(conv_bar(s), 128);
+            mbar_init(conv_bar(s), kConvThreads);
         }
         mbar_init(accum_bar, 1);
         if (SPLIT) mbar_init(recv_bar, 1);
@@ -359,10 +375,11 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
             else mbar_arrive(accum_bar);  // release the epilogue
         }
         __syncwarp();
-    } else if (warp >= 6) {
-        // ---- converters: raw f32 A tile -> hi (in place) + lo; raw B tile -> K-major hi / lo
+    } else {
+        // ---- warps 2..9 (raw operands): split each raw f32 A tile into hi (in place) + lo and
+        //      each raw B tile into its K-major hi / lo terms, stage by stage ----------------
         if (kConvert) {
-            const int t = threadIdx.x - 192;  // 0..127
+            const int t = threadIdx.x - 64;  // 0 .. kConvThreads - 1
             for (int i = 0; i < num_kb; i++) {
                 const int s = i % STAGES;
                 const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
@@ -371,16 +388,15 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                     atomicExch(p.error, 1);
                     // still arrive so that the MMA warp does not wait for us
                 }
+                const uint32_t st = base + s * S::kStage;
                 if (A_RAW) {
-                    float4* a_hi = reinterpret_cast<float4*>(base_ptr + s * S::kStage);
-                    float4* a_lo = reinterpret_cast<float4*>(base_ptr + s * S::kStage + S::kATile);
 #pragma unroll
-                    for (int j = 0; j < S::kATile / 16 / 128; j++) {
-                        const int idx = t + j * 128;
+                    for (int j = 0; j < S::kATile / 16 / kConvThreads; j++) {
+                        const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
                         float4 h, l;
-                        split4(a_hi[idx], h, l);
-                        a_hi[idx] = h;
-                        a_lo[idx] = l;
+                        split4_fast(lds4(st + off), h, l);
+                        sts4(st + off, h.x, h.y, h.z, h.w);
+                        sts4(st + S::kATile + off, l.x, l.y, l.z, l.w);
                     }
                 }
                 if (B_RAW) {
@@ -388,19 +404,18 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                     // the K-major terms: 16-byte chunk c (k = 4c .. 4c+3) at byte
                     // n * 128 + (c ^ (n % 8)) * 16, the layout TMA's 128-byte swizzle gives.
                     const float* raw = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kOffBRaw);
-                    uint8_t* b_hi = base_ptr + s * S::kStage + 2 * S::kATile;
-                    uint8_t* b_lo = b_hi + S::kBTile;
+                    const uint32_t b_hi = st + 2 * S::kATile, b_lo = b_hi + S::kBTile;
 #pragma unroll
-                    for (int j = 0; j < BN * (BK / 4) / 128; j++) {
-                        const int task = t + j * 128;
+                    for (int j = 0; j < BN * (BK / 4) / kConvThreads; j++) {
+                        const int task = t + j * kConvThreads;
                         const int n = task % BN, c = task / BN;
                         const float4 x = make_float4(raw[(4 * c) * BN + n], raw[(4 * c + 1) * BN + n],
                                                      raw[(4 * c + 2) * BN + n], raw[(4 * c + 3) * BN + n]);
                         float4 h, l;
-                        split4(x, h, l);
-                        const int off = n * 128 + ((c ^ (n & 7)) * 16);
-                        *reinterpret_cast<float4*>(b_hi + off) = h;
-                        *reinterpret_cast<float4*>(b_lo + off) = l;
+                        split4_fast(x, h, l);
+                        const uint32_t off = (uint32_t)(n * 128 + ((c ^ (n & 7)) * 16));
+                        sts4(b_hi + off, h.x, h.y, h.z, h.w);
+                        sts4(b_lo + off, l.x, l.y, l.z, l.w);
                     }
                 }
                 fence_proxy_async();  // make the generic-proxy writes visible to tcgen05.mma
@@ -408,7 +423,8 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                 if (*abort_flag) break;
             }
         }
-    } else {
+    }
+    if (warp >= 2 && warp < 6) {
         // ---- warps 2..5: wait for the accumulator ------------------------------------------
         const bool waited = mbar_wait(accum_bar, 0);
         if (!waited) atomicExch(p.error, 1);
