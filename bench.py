@@ -247,10 +247,12 @@ def make_l2_flush(torch):
     return flush
 
 
-def time_events(torch, fn, iters, flush=None, warmup=2, reps=1):
+def time_events(torch, fn, iters, flush=None, warmup=2, reps=1, busy_us=200.0):
     """Device time (ms) of one call of ``fn`` on the current stream, per iteration: the L2 is
     flushed before each iteration, which then runs ``fn`` ``reps`` times back to back between
-    two events (``reps`` > 1 only for inputs larger than the L2)."""
+    two events (``reps`` > 1 only for inputs larger than the L2).  An event pair with nothing
+    between it reads ~2.7 us on a B200 (the clock itself ticks in 32 ns), so a single short
+    call reads long by about that much; ``reps`` spreads it."""
     for _ in range(warmup):
         fn()
     times = []
@@ -259,7 +261,7 @@ def time_events(torch, fn, iters, flush=None, warmup=2, reps=1):
             flush()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
-        gpu_busy(torch)
+        gpu_busy(torch, busy_us)
         s.record()
         for _ in range(reps):
             fn()
@@ -270,8 +272,7 @@ def time_events(torch, fn, iters, flush=None, warmup=2, reps=1):
 
 
 def robust_mean(xs):
-    """Mean of the middle 60% of the samples: robust to an outlier, and (unlike the median)
-    not stuck on the event timer's ~2 us tick for short kernels."""
+    """Mean of the middle 60% of the samples: robust to an outlier iteration."""
     xs = sorted(xs)
     cut = int(len(xs) * 0.2)
     mid = xs[cut:len(xs) - cut] or xs
@@ -291,12 +292,16 @@ def measure_tf32_peak(torch):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+GEMV_COPIES = 6  # copies of the 64 MB B the GEMV lines rotate through (384 MB > the 126 MB L2)
+NODE_COPIES = 8  # instances of a layer node per timed step (per-node times)
+
+
 def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
     """Configs 2-4: each kernel timed alone with CUDA events, as % of its roofline.  The L2 is
     flushed before every timed iteration; the memory-bound cases, whose inputs are larger than
-    the L2, time 10 (softmax: 3) back-to-back launches per iteration, the rest one.  Times are
-    the mean of the middle 60% of the iterations.  ``filt`` keeps only the cases whose name
-    contains it."""
+    the L2, time 10 (softmax: 3) back-to-back launches per iteration, the GEMV lines one call on
+    each of GEMV_COPIES copies of B, the rest one launch.  Times are the mean of the middle 60%
+    of at least 10 iterations.  ``filt`` keeps only the cases whose name contains it."""
     results = []
     flush = make_l2_flush(torch)
 
@@ -306,7 +311,7 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
     hbm = peaks["hbm_gbs"]
     eff = tf32_tflops / 3.0 if tf32_tflops > 0 else float("nan")
 
-    def add(name, config, ms, bound, work):
+    def add(name, config, ms, bound, work, bf16x3=False):
         if bound == "hbm":
             achieved = work / (ms * 1e-3) / 1e9
             results.append({"kernel": name, "config": config, "ms": round(ms, 4), "bound": "hbm",
@@ -318,9 +323,14 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
                             "achieved": round(achieved, 2), "unit": "TFLOP/s", "peak": round(eff, 1),
                             "peak_basis": "3xTF32-effective = measured cuBLAS TF32 / 3",
                             "frac": round(achieved / eff, 4)})
+            if bf16x3:  # the kernel issues three bf16 MMAs per product: its own ceiling
+                bf = peaks["bf16_tflops"] / 3.0
+                results[-1]["frac_of_bf16x3_effective"] = round(achieved / bf, 4)
+                results[-1]["bf16x3_effective_peak"] = round(bf, 1)
 
     def timed(fn, n=iters, warmup=2, reps=1):
-        return robust_mean(time_events(torch, fn, n, flush, warmup=warmup, reps=reps))
+        # the spin covers the host's enqueueing of all `reps` calls
+        return robust_mean(time_events(torch, fn, max(n, 10), flush, warmup=warmup, reps=reps, busy_us=200.0 * reps))
 
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
@@ -334,6 +344,13 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
         b = torch.randn(K, N, device="cuda", generator=g) / math.sqrt(K)
         bw = b.clone()
         db, dbw = W(b), W(bw).set_weight()
+        # The GEMV lines (M <= 16) run kGemvCopies back-to-back calls per event pair, each on
+        # its own copy of B, so that every call streams B from HBM (the copies together are
+        # larger than the L2) and a ~15 us call is not measured against the event clock alone.
+        gemv_bs = []
+        if want("matmul M=1") or want("matmul M=16"):
+            gemv_bs = [bw] + [bw.clone() for _ in range(GEMV_COPIES - 1)]
+            gemv_dbs = [W(x).set_weight() for x in gemv_bs]
         for M in (1, 16, 128, 2048, 8192):
             if not want(f"matmul M={M}"):
                 continue
@@ -343,13 +360,25 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
             for label, bb in (("", dbw), (" (B per-call)", db)):
                 if M <= 16 and label:
                     continue  # the GEMV path reads B as it is either way
-                ms = timed(lambda: kernels.matmul(da, bb, out=dc), n=max(iters, 15) if M <= 16 else iters)
                 if M <= 16:
+                    rot = iter(())
+
+                    def call():
+                        nonlocal rot
+                        try:
+                            nb = next(rot)
+                        except StopIteration:
+                            rot = iter(gemv_dbs)
+                            nb = next(rot)
+                        kernels.matmul(da, nb, out=dc)
+
+                    ms = timed(call, n=max(iters, 15), reps=GEMV_COPIES)
                     add(f"matmul M={M}{label}", "configs[1]", ms, "hbm", 4.0 * (M * K + K * N + M * N))
                 else:
+                    ms = timed(lambda: kernels.matmul(da, bb, out=dc), n=iters)
                     add(f"matmul M={M}{label}", "configs[1]", ms, "tensor", 2.0 * M * N * K)
             del a, c
-        del b, bw, db, dbw
+        del b, bw, db, dbw, gemv_bs
     # config 3: causal attention b4 h32 d128 s2048 (batch folded into 128 heads)
     S, H, D = 2048, 4 * 32, 128
     name = "attention causal b4 h32 d128 s2048"
@@ -360,7 +389,7 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
         o = torch.empty(S, H * D, device="cuda")
         dq, dk, dv, do = W(q), W(k_), W(v), W(o)
         ms = timed(lambda: kernels.attention(dq, dk, dv, H, D, causal=True, out=do), max(3, iters // 2), 1)
-        add(name, "configs[2]", ms, "tensor", 4.0 * H * S * S * D / 2)
+        add(name, "configs[2]", ms, "tensor", 4.0 * H * S * S * D / 2, bf16x3=True)
         del q, k_, v, o
     # config 3': softmax rows [262144, 2048]
     name = "softmax [262144,2048]"
@@ -550,19 +579,29 @@ def run_ours(args, world, rank, local):
     e2e_value = world * cfg.seq * args.steps / (float(t.item()) * 1e-3)
 
     # ---- per-node times of the layer: the dominant kernel's roofline --------------------------
-    # Each node is captured alone as a one-node step and replayed between CUDA events (L2
-    # flushed first), so a node's time is its kernels' device time plus one graph launch --
-    # no host work, and no flag read-back, inside the events.
+    # Each node is timed as NODE_COPIES instances of itself captured into one step, each on its
+    # own copy of the layer's tensors (id prefixes), chained by programmatic dependent launch as
+    # in the layer's step.  The L2 is flushed before every replay, so each instance reads its
+    # weights from HBM; a node's time is the replay's over NODE_COPIES (the event pair's fixed
+    # cost and the graph launch spread over the copies).  No host work and no flag read-back
+    # inside the events.
+    prefixes = [f"node{i}/" for i in range(NODE_COPIES)]
+    for pfx in prefixes:
+        layer.load(ex, w, pfx)
+        layer.forward(ex, cfg, pfx)  # allocates the copy's intermediates
+    ex.synchronize()
+    copies = [layer.invocations(cfg, pfx) for pfx in prefixes]
     node_times = []
-    for inv in layer.invocations(cfg):
+    for j, inv in enumerate(layer.invocations(cfg)):
         ex.begin_step_capture()
         try:
-            ex.run(inv)
+            for c in copies:
+                ex.run(c[j])
         except Exception:
             ex.abort_step_capture()
             raise
         ex.end_step_capture()
-        ms = robust_mean(time_events(torch, ex.launch_step, 15, flush, warmup=3))
+        ms = robust_mean(time_events(torch, ex.launch_step, 15, flush, warmup=3)) / NODE_COPIES
         ex.check_steps()
         node_times.append((inv, ms))
     tf32 = measure_tf32_peak(torch) if rank == 0 else 0.0

@@ -108,7 +108,9 @@ struct AttnShape {
     static constexpr int kK = (D / 64) * kKAtom;     // one term of a K tile
     static constexpr int kV = D * 128;               // one term of a V^T tile: [D][64 keys]
     static constexpr int kP = AQ * 128;              // one term of P: [128][64 keys]
-    static constexpr int kOffQ = 0, kOffK = 2 * kQ, kOffV = kOffK + 2 * kK, kOffP = kOffV + 2 * kV;
+    // K is double-buffered (slot b: hi at kOffK + 2 * b * kK, lo right after): the next tile's K
+    // loads while this tile's scores are computed.
+    static constexpr int kOffQ = 0, kOffK = 2 * kQ, kOffV = kOffK + 4 * kK, kOffP = kOffV + 2 * kV;
     static constexpr int kBytes = kOffP + 2 * kP;
     static constexpr int kSmem = kBytes + 1024 + 256;
     static constexpr uint32_t kTmemCols = 256;       // S: [0, 64) and [64, 128), P.V: [128, 128 + D)
@@ -119,8 +121,9 @@ struct AttnShape {
 // Warp roles: 0 TMA producer; 1 MMA issuer; 4..11 softmax, two threads per query row (warp w
 // reads TMEM lane quarter w % 4; warps 4-7 take key columns [0, 32) of each tile and output
 // columns [0, D/2), warps 8-11 the other halves), exchanging row max and sum through shared
-// memory.  The MMA runs one S tile ahead (S is double-buffered in TMEM), so the next tile's
-// Q.K^T overlaps this tile's softmax.
+// memory (each pair of warps that shares a lane quarter on its own named barrier).  S is
+// double-buffered in TMEM and K in shared memory: Q.K^T runs up to two tiles ahead, and the P.V
+// of tile j runs on the tensor cores while the softmax of tile j + 1 is computed.
 template <int D>
 __global__ void __launch_bounds__(kAttnTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                         AttnTcParams p) {
     using S = AttnShape<D>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bars[9];
+    __shared__ uint64_t bars[11];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     __shared__ float red_max[2][AQ], red_sum[2][AQ];
@@ -137,7 +140,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* base_ptr = smem_raw + (base - raw);
     const uint32_t b0 = smem_u32(bars);
-    const uint32_t q_full = b0, k_full = b0 + 8, k_empty = b0 + 16, v_full = b0 + 24, v_empty = b0 + 32,
+    // k_full / k_empty of K slot b: b0 + 8 / b0 + 16 for slot 0, b0 + 72 / b0 + 80 for slot 1
+    auto k_full = [&](int b) { return b ? b0 + 72 : b0 + 8; };
+    auto k_empty = [&](int b) { return b ? b0 + 80 : b0 + 16; };
+    const uint32_t q_full = b0, v_full = b0 + 24, v_empty = b0 + 32,
                    p_full = b0 + 40, pv_full = b0 + 48, s_full0 = b0 + 56;  // s_full[2] at 56, 64
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -160,8 +166,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(k_full, 1);
-        mbar_init(k_empty, 1);
+        mbar_init(k_full(0), 1);
+        mbar_init(k_empty(0), 1);
+        mbar_init(k_full(1), 1);
+        mbar_init(k_empty(1), 1);
         mbar_init(v_full, 1);
         mbar_init(v_empty, 1);
         mbar_init(p_full, 256);
@@ -189,18 +197,27 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 tma_load_2d(base + S::kOffQ + a * S::kQAtom, &map_qhi, q_full, (int)(head * D + a * 64), (int)q0);
                 tma_load_2d(base + S::kOffQ + S::kQ + a * S::kQAtom, &map_qlo, q_full, (int)(head * D + a * 64), (int)q0);
             }
-            for (int j = 0; j < n_kv; j++) {
+            // K of tile t into slot t % 2, once the scores of tile t - 2 (the slot's last user)
+            // are done: K runs one tile ahead of V.
+            auto load_k = [&](int t) -> bool {
+                const int b = t & 1;
+                if (t >= 2 && !mbar_wait(k_empty(b), (uint32_t)((t - 2) >> 1) & 1u)) return false;
+                const int key = (int)(kv0 + (uint64_t)t * AKV);
+                const uint32_t slot = base + S::kOffK + (uint32_t)(b * 2 * S::kK);
+                mbar_arrive_expect_tx(k_full(b), 2 * S::kK);
+                for (int a = 0; a < D / 64; a++) {
+                    tma_load_2d(slot + a * S::kKAtom, &map_khi, k_full(b), (int)(kvh * D + a * 64), key);
+                    tma_load_2d(slot + S::kK + a * S::kKAtom, &map_klo, k_full(b), (int)(kvh * D + a * 64), key);
+                }
+                return true;
+            };
+            bool ok = load_k(0);
+            for (int j = 0; j < n_kv && ok; j++) {
                 const int key0 = (int)(kv0 + (uint64_t)j * AKV);
                 const uint32_t ph = (uint32_t)(j - 1) & 1u;
-                if (j > 0 && !mbar_wait(k_empty, ph)) {
-                    abort_flag = 1;
-                    atomicExch(p.error, 1);
+                if (j + 1 < n_kv && !load_k(j + 1)) {
+                    ok = false;
                     break;
-                }
-                mbar_arrive_expect_tx(k_full, 2 * S::kK);
-                for (int a = 0; a < D / 64; a++) {
-                    tma_load_2d(base + S::kOffK + a * S::kKAtom, &map_khi, k_full, (int)(kvh * D + a * 64), key0);
-                    tma_load_2d(base + S::kOffK + S::kK + a * S::kKAtom, &map_klo, k_full, (int)(kvh * D + a * 64), key0);
                 }
                 if (j > 0 && !mbar_wait(v_empty, ph)) {
                     abort_flag = 1;
@@ -210,6 +227,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 mbar_arrive_expect_tx(v_full, 2 * S::kV);
                 tma_load_2d(base + S::kOffV, &map_vhi, v_full, key0, (int)(kvh * D));
                 tma_load_2d(base + S::kOffV + S::kV, &map_vlo, v_full, key0, (int)(kvh * D));
+            }
+            if (!ok) {
+                abort_flag = 1;
+                atomicExch(p.error, 1);
             }
         }
         __syncwarp();
@@ -221,30 +242,29 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
             const uint32_t tO = tmem + S::kColPV;
             // S(j) = Q K(j)^T into TMEM columns [64 * (j % 2), +64), then frees K's buffer.
             auto issue_s = [&](int j) -> bool {
-                if (!mbar_wait(k_full, (uint32_t)j & 1u)) return false;
+                if (!mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u)) return false;
                 tc_fence_after();
                 const uint32_t tS = tmem + (uint32_t)(j & 1) * AKV;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
                     const uint32_t off = (uint32_t)(kk % 4) * 32;
                     const uint32_t qa = base + S::kOffQ + (kk / 4) * S::kQAtom + off;
-                    const uint32_t kb = base + S::kOffK + (kk / 4) * S::kKAtom + off;
+                    const uint32_t kb = base + S::kOffK + (uint32_t)((j & 1) * 2 * S::kK) + (kk / 4) * S::kKAtom + off;
                     const uint64_t qhi = desc_k_sw128(qa), qlo = desc_k_sw128(qa + S::kQ);
                     const uint64_t khi = desc_k_sw128(kb), klo = desc_k_sw128(kb + S::kK);
                     mma_bf16(tS, qlo, khi, idesc_s, kk > 0 ? 1u : 0u);
                     mma_bf16(tS, qhi, klo, idesc_s, 1u);
                     mma_bf16(tS, qhi, khi, idesc_s, 1u);
                 }
-                tc_commit(k_empty);
+                tc_commit(k_empty(j & 1));
                 tc_commit(s_full0 + 8u * (uint32_t)(j & 1));
                 return true;
             };
-            bool ok = mbar_wait(q_full, 0) && issue_s(0);
+            // S runs two tiles ahead: S(j + 2) reuses S(j)'s TMEM columns, which are free once
+            // P(j) is written; P.V(j) is issued first so the softmax of tile j + 1 (whose S is
+            // ready) overlaps it.
+            bool ok = mbar_wait(q_full, 0) && issue_s(0) && (n_kv < 2 || issue_s(1));
             for (int j = 0; j < n_kv && ok; j++) {
-                if (j + 1 < n_kv && !issue_s(j + 1)) {
-                    ok = false;
-                    break;
-                }
                 const uint32_t ph = (uint32_t)j & 1u;
                 if (!mbar_wait(p_full, ph) || !mbar_wait(v_full, ph)) {
                     ok = false;
@@ -265,6 +285,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 }
                 tc_commit(v_empty);
                 tc_commit(pv_full);
+                if (j + 2 < n_kv && !issue_s(j + 2)) {
+                    ok = false;
+                    break;
+                }
             }
             if (!ok) {
                 abort_flag = 1;
@@ -289,6 +313,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
             if (row_lo > row_hi) row_lo = row_hi;
         }
         const float scale2 = p.scale * kLog2e;  // scores in log2 units
+        // The two threads of a row are in warps qq + 4 and qq + 8: those two warps meet on
+        // named barrier 1 + qq (64 threads) to exchange the row's max and sum.
+        auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + qq) : "memory"); };
         const uint32_t lane_base = tmem + ((uint32_t)(qq * 32) << 16);
         float o[S::kHalfD];
 #pragma unroll
@@ -299,8 +326,24 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         // Every softmax warp runs every iteration (the named barriers below need all 256
         // threads); a wait that times out marks the CTA failed and later waits are skipped.
         bool failed = false;
+        // O <- O * keep + P.V(t): tile t's P.V, read from TMEM once its MMA has completed.
+        auto fold_pv = [&](int t, float keep) {
+            if (!failed && !mbar_wait(pv_full, (uint32_t)t & 1u)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < S::kHalfD; c += 32) {
+                float pv[32];
+                tmem_ld32(lane_base + S::kColPV + (uint32_t)(hf * S::kHalfD + c), pv);
+                tc_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; e++) o[c + e] = o[c + e] * keep + pv[e];
+            }
+        };
+        // The softmax of tile j runs while tile j - 1's P.V is on the tensor cores; that P.V is
+        // folded in only then (with its own keep factor), before P(j) replaces P(j - 1).
+        float keep_prev = 0.0f;
         for (int j = 0; j < n_kv; j++) {
-            const uint32_t ph = (uint32_t)j & 1u;
             if (!failed && !mbar_wait(s_full0 + 8u * (uint32_t)(j & 1), (uint32_t)(j >> 1) & 1u)) failed = true;
             failed = __any_sync(0xffffffffu, failed);
             tc_fence_after();
@@ -324,7 +367,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 }
             }
             red_max[hf][r] = tmax;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            pair_sync();
             const float m_new = fmaxf(m, fmaxf(red_max[0][r], red_max[1][r]));
             float alpha = 0.0f, psum = 0.0f;
             if (m_new != __int_as_float(0xff800000)) {
@@ -339,11 +382,13 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 for (int c = 0; c < 32; c++) s[c] = 0.0f;
             }
             red_sum[hf][r] = psum;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            pair_sync();
             const float l_new = l * alpha + (red_sum[0][r] + red_sum[1][r]);
             const float inv = l_new > 0.0f ? 1.0f / l_new : 0.0f;
             const float keep = l_new > 0.0f ? (l * alpha) * inv : 0.0f;
+            if (j > 0) fold_pv(j - 1, keep_prev);
             // P / l_new as bf16 hi / lo: 16-byte chunk c of row r lives at chunk (c ^ (r % 8)).
+            // P(j) overwrites P(j - 1), whose P.V has completed (fold_pv waited for it).
 #pragma unroll
             for (int cc = 0; cc < 4; cc++) {
                 const int c = hf * 4 + cc;
@@ -362,21 +407,13 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 *reinterpret_cast<uint4*>(p_lo + sw) = make_uint4(lo4[0], lo4[1], lo4[2], lo4[3]);
             }
             fence_proxy_async();  // the P writes are read by tcgen05.mma
+            tc_fence_before();    // ... and the P.V read above precedes the next P.V's write
             mbar_arrive(p_full);
-            if (!failed && !mbar_wait(pv_full, ph)) failed = true;
-            failed = __any_sync(0xffffffffu, failed);
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < S::kHalfD; c += 32) {
-                float pv[32];
-                tmem_ld32(lane_base + S::kColPV + (uint32_t)(hf * S::kHalfD + c), pv);
-                tc_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; e++) o[c + e] = o[c + e] * keep + pv[e];
-            }
+            keep_prev = keep;
             m = m_new;
             l = l_new;
         }
+        if (n_kv > 0) fold_pv(n_kv - 1, keep_prev);
         if (failed) atomicExch(p.error, 1);
         if (live) {
             float* orow = p.out + qi * p.out_dim + head * D + hf * S::kHalfD;

@@ -406,7 +406,9 @@ mg_status gemv_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n) {
 // ---- cluster GEMV: A and B streamed together, k split across a thread-block cluster -----------
 // A producer lane streams, per stage, a [32 x 128] tile of B and the matching [M x 32] columns
 // of A with TMA (no prologue staging A); 8 compute warps take 4 rows of B each per stage and
-// multiply them by A from shared memory.  The k slices of one column tile (and, gated, the
+// multiply them by A from shared memory, two columns per packed FMA.  When B is a settled
+// weight, the first stages' B loads are issued before the dependency wait, so a chain of
+// GEMVs streams the next weight while the previous call finishes.  The k slices of one column tile (and, gated, the
 // gate and up terms) form one cluster: each CTA sums its warps once through the drained ring,
 // then sends each band of its [M x 128] partial to the CTA that owns the band with one bulk
 // copy into that CTA's receive slot; owners add the partials in split order (deterministic),
@@ -424,23 +426,51 @@ struct GemvClusterArgs {
     int splits;          // S; the cluster is (1, S, terms)
     int terms;           // 1, or 2 for gated (gate: z = 0, up: z = 1)
     int band;            // floats of the flattened [m][128] tile each cluster CTA finishes (multiple of 4)
+    int b_early;         // B does not depend on the preceding kernel: the first stages' B loads
+                         // are issued before the dependency wait
     int* error;
 };
 
+// Two f32 lanes at once (Blackwell's packed FMA): d.lo += a * b.lo, d.hi += a * b.hi, each
+// lane one fused multiply-add with round-to-nearest, as the scalar form.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void fma2(uint64_t& d, float a, uint64_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(pack2(a, a)), "l"(b));
+}
+__device__ __forceinline__ void fma2(uint64_t& d, uint64_t a, uint64_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float4 unpack4(uint64_t lo, uint64_t hi) {
+    float4 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(lo));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.z), "=f"(v.w) : "l"(hi));
+    return v;
+}
+
+// From 8 rows up, a transposer warp rewrites each stage's A tile as [32 k][M] so that the
+// compute warps read A in pairs of rows (one packed FMA per pair and column, B duplicated
+// once per column) instead of duplicating every A value.
 template <int M>
 struct GemvCShape {
+    static constexpr bool kTrans = M >= 8;
+    static constexpr int kThreads = (kWarps + 1 + (kTrans ? 1 : 0)) * 32;
     static constexpr int kB = kChunkRows * kCols * 4;  // 16 KB of B per stage
     static constexpr int kA = M * kChunkRows * 4;      // [M][32] of A per stage
     static constexpr int kStage = kB + kA;
     static constexpr int kRing = kCStages * kStage;
+    static constexpr int kAT = kTrans ? kCStages * kA : 0;  // the transposed A tiles, [32][M] per stage
     static constexpr int kPart = M * kCols * 4;         // this CTA's partial [M][128]
     static constexpr int kRecv = (M * kCols + 4 * kMaxClusterCtas) * 4;  // the other CTAs' partials of this CTA's band
     static_assert(kWarps * kPart <= kRing, "the warp partials fit the drained ring");
-    static constexpr int kSmem = 128 + kRing + kPart + kRecv + 8 * (2 * kCStages + 1);
+    static constexpr int kSmem = 128 + kRing + kAT + kPart + kRecv + 8 * (3 * kCStages + 1);
 };
 
 template <int M>
-__global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
+__global__ void __launch_bounds__(GemvCShape<M>::kThreads, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                           const __grid_constant__ CUtensorMap map_b,
                                                                           const __grid_constant__ CUtensorMap map_b2,
                                                                           GemvClusterArgs p) {
@@ -450,14 +480,16 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_cluster_kernel(cons
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 127u) & ~127u;
     uint8_t* base_ptr = smem_raw + (base - raw);
-    const uint32_t part = base + S::kRing;
+    const uint32_t part = base + S::kRing + S::kAT;
     const uint32_t recv = part + S::kPart;
     const uint32_t bar0 = recv + S::kRecv;
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kCStages + s); };
     const uint32_t recv_bar = bar0 + 8u * (2 * kCStages);
-    float* partf = reinterpret_cast<float*>(base_ptr + S::kRing);
-    float* recvf = reinterpret_cast<float*>(base_ptr + S::kRing + S::kPart);
+    auto at_bar = [&](int s) { return bar0 + 8u * (2 * kCStages + 1 + s); };  // transposed A ready
+    float* atf = reinterpret_cast<float*>(base_ptr + S::kRing);  // [kCStages][32][M]
+    float* partf = reinterpret_cast<float*>(base_ptr + S::kRing + S::kAT);
+    float* recvf = reinterpret_cast<float*>(base_ptr + S::kRing + S::kAT + S::kPart);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t col0 = (uint64_t)blockIdx.x * kCols;
     const int nc = p.splits * p.terms;
@@ -473,19 +505,45 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_cluster_kernel(cons
         for (int s = 0; s < kCStages; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), kWarps);
+            if (S::kTrans) mbar_init(at_bar(s), 1);
         }
         mbar_init(recv_bar, 1);
         fence_barrier_init();
         mbar_arrive_expect_tx(recv_bar, (uint32_t)((nc - 1) * (my_hi - my_lo) * 4));
+        if (p.b_early) {
+            for (int c = 0; c < min(chunks, kCStages); c++) {
+                mbar_arrive_expect_tx(full_bar(c), (uint32_t)S::kStage);
+                tma_load_2d(base + (uint32_t)(c * S::kStage), mb, full_bar(c), (int)col0, (int)(k0 + (uint64_t)c * kChunkRows));
+            }
+        }
     }
     cluster_arrive();  // phase 1: every CTA's receive barrier is armed before anyone sends
     pdl_enter();
     __syncthreads();
 
-    float acc[M][4];
+    // Packed f32 accumulators of this thread's 4 columns: [row][column pair] below 8 rows,
+    // [row pair][column] from 8 rows up.
+    uint64_t acc2[2 * M];
 #pragma unroll
-    for (int r = 0; r < M; r++) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
-    if (warp == kWarps) {
+    for (int i = 0; i < 2 * M; i++) acc2[i] = 0ull;
+    if (S::kTrans && warp == kWarps + 1) {
+        // ---- transposer: A [M][32] -> [32][M] per stage (lane = k) ---------------------------
+        for (int c = 0; c < chunks; c++) {
+            const int s = c % kCStages;
+            if (!mbar_wait(full_bar(s), (uint32_t)(c / kCStages) & 1u)) {
+                atomicExch(p.error, 1);
+                break;
+            }
+            const float* at = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kB);
+            float* dst = atf + (s * kChunkRows + lane) * M;
+#pragma unroll
+            for (int q = 0; q < M / 4; q++)
+                *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(at[(4 * q) * kChunkRows + lane], at[(4 * q + 1) * kChunkRows + lane],
+                                                                      at[(4 * q + 2) * kChunkRows + lane], at[(4 * q + 3) * kChunkRows + lane]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(at_bar(s));
+        }
+    } else if (warp == kWarps) {
         // ---- producer: keep the ring full -----------------------------------------------
         if (lane == 0) {
             for (int c = 0; c < chunks; c++) {
@@ -496,35 +554,59 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_cluster_kernel(cons
                 }
                 const uint32_t st = base + (uint32_t)(s * S::kStage);
                 const int kr = (int)(k0 + (uint64_t)c * kChunkRows);
-                mbar_arrive_expect_tx(full_bar(s), (uint32_t)S::kStage);
-                tma_load_2d(st, mb, full_bar(s), (int)col0, kr);
+                if (!p.b_early || c >= kCStages) {
+                    mbar_arrive_expect_tx(full_bar(s), (uint32_t)S::kStage);
+                    tma_load_2d(st, mb, full_bar(s), (int)col0, kr);
+                }
                 tma_load_2d(st + S::kB, &map_a, full_bar(s), kr, 0);
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < kWarps) {
         for (int c = 0; c < chunks; c++) {
             const int s = c % kCStages;
-            if (!mbar_wait(full_bar(s), (uint32_t)(c / kCStages) & 1u)) {
+            const uint32_t ph = (uint32_t)(c / kCStages) & 1u;
+            if (!mbar_wait(full_bar(s), ph) || (S::kTrans && !mbar_wait(at_bar(s), ph))) {
                 atomicExch(p.error, 1);
                 break;
             }
             const float* tile = reinterpret_cast<const float*>(base_ptr + s * S::kStage);
-            const float* at = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kB);  // [M][32]
             const int rr = warp * 4;  // this warp's 4 rows of the stage
-            float4 bv[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) bv[u] = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
-#pragma unroll
-            for (int r = 0; r < M; r++) {
-                const float4 av = *reinterpret_cast<const float4*>(at + r * kChunkRows + rr);
-                const float aa[4] = {av.x, av.y, av.z, av.w};
+            if constexpr (S::kTrans) {
+                const float* att = atf + s * kChunkRows * M;  // [32][M]
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    acc[r][0] += aa[u] * bv[u].x;
-                    acc[r][1] += aa[u] * bv[u].y;
-                    acc[r][2] += aa[u] * bv[u].z;
-                    acc[r][3] += aa[u] * bv[u].w;
+                    const float4 bv = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+                    const uint64_t bd[4] = {pack2(bv.x, bv.x), pack2(bv.y, bv.y), pack2(bv.z, bv.z), pack2(bv.w, bv.w)};
+#pragma unroll
+                    for (int q = 0; q < M / 4; q++) {
+                        const float4 a4 = *reinterpret_cast<const float4*>(att + (rr + u) * M + 4 * q);
+                        const uint64_t a01 = pack2(a4.x, a4.y), a23 = pack2(a4.z, a4.w);
+#pragma unroll
+                        for (int cc = 0; cc < 4; cc++) {
+                            fma2(acc2[(2 * q) * 4 + cc], a01, bd[cc]);
+                            fma2(acc2[(2 * q + 1) * 4 + cc], a23, bd[cc]);
+                        }
+                    }
+                }
+            } else {
+                const float* at = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kB);  // [M][32]
+                uint64_t b01[4], b23[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float4 bv = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+                    b01[u] = pack2(bv.x, bv.y);
+                    b23[u] = pack2(bv.z, bv.w);
+                }
+#pragma unroll
+                for (int r = 0; r < M; r++) {
+                    const float4 av = *reinterpret_cast<const float4*>(at + r * kChunkRows + rr);
+                    const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        fma2(acc2[r * 2], aa[u], b01[u]);
+                        fma2(acc2[r * 2 + 1], aa[u], b23[u]);
+                    }
                 }
             }
             __syncwarp();
@@ -535,10 +617,21 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 2) gemv_cluster_kernel(cons
     __syncthreads();
     float* red = reinterpret_cast<float*>(base_ptr);  // [kWarps][M][128]
     if (warp < kWarps) {
+        if constexpr (S::kTrans) {
 #pragma unroll
-        for (int r = 0; r < M; r++)
-            *reinterpret_cast<float4*>(red + (warp * M + r) * kCols + 4 * lane) =
-                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+            for (int q = 0; q < M / 2; q++) {
+                float lo[4], hi[4];
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++)
+                    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo[cc]), "=f"(hi[cc]) : "l"(acc2[q * 4 + cc]));
+                *reinterpret_cast<float4*>(red + (warp * M + 2 * q) * kCols + 4 * lane) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<float4*>(red + (warp * M + 2 * q + 1) * kCols + 4 * lane) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < M; r++)
+                *reinterpret_cast<float4*>(red + (warp * M + r) * kCols + 4 * lane) = unpack4(acc2[r * 2], acc2[r * 2 + 1]);
+        }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < F; i += blockDim.x) {
@@ -632,7 +725,7 @@ mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const
         if (fits[nc] == 0) {
             cudaLaunchConfig_t q = {};
             q.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
-            q.blockDim = dim3((kWarps + 1) * 32, 1, 1);
+            q.blockDim = dim3(S::kThreads, 1, 1);
             q.dynamicSmemBytes = S::kSmem;
             cudaLaunchAttribute ca;
             ca.id = cudaLaunchAttributeClusterDimension;
@@ -653,7 +746,7 @@ mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
-    cfg.blockDim = dim3((kWarps + 1) * 32, 1, 1);
+    cfg.blockDim = dim3(S::kThreads, 1, 1);
     cfg.dynamicSmemBytes = S::kSmem;
     cfg.stream = d->stream;
     cudaLaunchAttribute attr[2];
@@ -776,6 +869,7 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     p.k = g.k;
     p.terms = terms;
     gemv_slices(p, splits);
+    p.b_early = g.b_stable ? 1 : 0;
     p.error = d->flags + 2;
     CUtensorMap maps[3];
     MG_TRY(gemv_a_map(&maps[0], g.a, g.m, g.k, (uint32_t)mp));

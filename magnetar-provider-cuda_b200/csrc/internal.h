@@ -101,6 +101,10 @@ struct Buffer {
     // it: the K-major tf32 hi/lo terms ([n, kp] each, hi first), built on first use with the
     // transpose flag it was read with, and dropped whenever the buffer's contents change.
     bool is_weight = false;
+    // Set when the buffer becomes a weight: the kernel just before the next matmul may have
+    // written it, so that matmul reads it only after its dependency wait.  Cleared by that
+    // matmul; later ones may start loading the weight before the wait.
+    bool weight_fresh = false;
     float* prep = nullptr;
     uint64_t prep_n = 0, prep_k = 0, prep_kp = 0;
     int prep_transposed = -1;

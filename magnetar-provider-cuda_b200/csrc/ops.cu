@@ -211,6 +211,13 @@ mg_status matmul_plan(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
         MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0], &built));
         if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1], &built));
         g.b_stable = !built && g.b_prep[0] && (!b2 || g.b_prep[1]);
+    } else {
+        // The GEMV path reads B as it is: before its dependency wait when B is a weight that
+        // the preceding kernel cannot have written.
+        auto settled = [](const Buffer* w) { return w->is_weight && !w->weight_fresh; };
+        g.b_stable = settled(b) && (!b2 || settled(b2));
+        const_cast<Buffer*>(b)->weight_fresh = false;
+        if (b2) const_cast<Buffer*>(b2)->weight_fresh = false;
     }
     *gp = g;
     return MG_OK;

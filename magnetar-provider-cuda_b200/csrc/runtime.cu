@@ -562,6 +562,7 @@ mg_status mg_buffer_set_weight(mg_buffer* h, int is_weight) {
         cudaSetDevice(b->device->ordinal);
         buffer_drop_prep(b);
     }
+    if (is_weight && !b->is_weight) b->weight_fresh = true;
     b->is_weight = is_weight != 0;
     return MG_OK;
 }

@@ -236,6 +236,9 @@ MATMUL_SHAPES = [
     # GEMV: the most k splits of one cluster, a long k, and k not a multiple of 4 (TMA-staged
     # path); transposed A with a long k takes the two-kernel path (test_matmul_transposed)
     (8, 16384, 256), (16, 40000, 128), (5, 4098, 260),
+    # GEMV item path (m <= 4): two and three rows, a ragged last column tile, k shorter than one
+    # item, and a long k (many items per column tile summed by the last one)
+    (2, 4096, 4096), (3, 8192, 200), (4, 1024, 1000), (1, 36, 64), (1, 65536, 96),
 ]
 
 
@@ -249,7 +252,8 @@ def test_matmul(kernels, oracle, m, k, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(128, 512, 512), (200, 904, 136), (128, 2048, 2048), (513, 257, 132),
-                                   (64, 4096, 32), (300, 129, 65)])
+                                   (64, 4096, 32), (300, 129, 65), (1, 4096, 512), (3, 2048, 1000),
+                                   (16, 4096, 256)])
 def test_matmul_with_weight_b(kernels, oracle, m, k, n):
     # B marked as a weight: its tensor-core operand form is built by the first call and kept;
     # both calls match the oracle and each other.  (Plain B at M <= 128 is split inside the
@@ -264,6 +268,23 @@ def test_matmul_with_weight_b(kernels, oracle, m, k, n):
     np.testing.assert_array_equal(first, second)
 
 
+def test_gemv_weight_written_by_the_preceding_kernel(kernels, oracle):
+    # A buffer that a kernel has just written and that then becomes a weight: the next matmul
+    # must wait for that kernel before reading it; later matmuls may read it early.
+    r = rng(16)
+    a = (r.standard_normal((2, 2048)) / math.sqrt(2048)).astype(np.float32)
+    x = r.standard_normal((2048, 768)).astype(np.float32)
+    y = r.standard_normal((2048, 768)).astype(np.float32)
+    da = kernels.upload(a)
+    for _ in range(3):
+        w = kernels.add(kernels.upload(x), kernels.upload(y)).set_weight()
+        first = kernels.download(kernels.matmul(da, w))
+        second = kernels.download(kernels.matmul(da, w))
+        exp = oracle.matmul(a, x + y)
+        assert rel(first, exp) <= TOL_MATMUL
+        np.testing.assert_array_equal(first, second)
+
+
 @pytest.mark.parametrize("m,k,n", [(1, 300, 70), (16, 256, 128), (130, 200, 96), (16, 40000, 128)])
 @pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
 def test_matmul_transposed(kernels, oracle, m, k, n, ta, tb):
@@ -274,7 +295,7 @@ def test_matmul_transposed(kernels, oracle, m, k, n, ta, tb):
     assert rel(got, oracle.matmul(a, b, ta, tb)) <= TOL_MATMUL
 
 
-@pytest.mark.parametrize("m,k", [(1, 256), (16, 256), (128, 256), (300, 256), (128, 4096)])
+@pytest.mark.parametrize("m,k", [(1, 256), (16, 256), (128, 256), (300, 256), (128, 4096), (3, 4096)])
 def test_matmul_bias_and_residual(kernels, oracle, m, k):
     r = rng(12)
     n = 192
@@ -290,7 +311,7 @@ def test_matmul_bias_and_residual(kernels, oracle, m, k):
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 512, 1376), (16, 512, 256), (128, 512, 1376), (200, 300, 136),
-                                   (128, 4096, 256)])
+                                   (128, 4096, 256), (4, 4096, 1000)])
 def test_gated_matmul(kernels, oracle, m, k, n):
     r = rng(13)
     a = r.standard_normal((m, k)).astype(np.float32)
