@@ -292,16 +292,16 @@ def measure_tf32_peak(torch):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-GEMV_COPIES = 6  # copies of the 64 MB B the GEMV lines rotate through (384 MB > the 126 MB L2)
+ROT_COPIES = 6  # copies of the 64 MB B the M <= 128 lines rotate through (384 MB > the 126 MB L2)
 NODE_COPIES = 8  # instances of a layer node per timed step (per-node times)
 
 
 def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
     """Configs 2-4: each kernel timed alone with CUDA events, as % of its roofline.  The L2 is
     flushed before every timed iteration; the memory-bound cases, whose inputs are larger than
-    the L2, time 10 (softmax: 3) back-to-back launches per iteration, the GEMV lines one call on
-    each of GEMV_COPIES copies of B, the rest one launch.  Times are the mean of the middle 60%
-    of at least 10 iterations.  ``filt`` keeps only the cases whose name contains it."""
+    the L2, time 10 (softmax: 3) back-to-back launches per iteration, the matmul lines with
+    M <= 128 one call on each of ROT_COPIES copies of B, the rest one launch.  Times are the
+    mean of the middle 60% of at least 10 iterations.  ``filt`` keeps only the cases whose name contains it."""
     results = []
     flush = make_l2_flush(torch)
 
@@ -342,43 +342,41 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
     # built once and kept with it), and B as a plain tensor (operand form derived per call).
     if any(want(f"matmul M={M}") for M in (1, 16, 128, 2048, 8192)):
         b = torch.randn(K, N, device="cuda", generator=g) / math.sqrt(K)
-        bw = b.clone()
-        db, dbw = W(b), W(bw).set_weight()
-        # The GEMV lines (M <= 16) run kGemvCopies back-to-back calls per event pair, each on
-        # its own copy of B, so that every call streams B from HBM (the copies together are
-        # larger than the L2) and a ~15 us call is not measured against the event clock alone.
-        gemv_bs = []
-        if want("matmul M=1") or want("matmul M=16"):
-            gemv_bs = [bw] + [bw.clone() for _ in range(GEMV_COPIES - 1)]
-            gemv_dbs = [W(x).set_weight() for x in gemv_bs]
+        # Lines with M <= 128 (a call of a few tens of microseconds, B read once) run
+        # ROT_COPIES back-to-back calls per event pair, each on its own copy of B, as the
+        # layers of a model follow one another: every call streams its B from HBM (the copies
+        # together are larger than the L2) and the event pair's fixed cost is spread.  Larger
+        # M times one call on one B.
+        copies = [b] + [b.clone() for _ in range(ROT_COPIES - 1)]
+        rot = {"": [W(x).set_weight() for x in copies], " (B per-call)": [W(x) for x in copies]}
         for M in (1, 16, 128, 2048, 8192):
             if not want(f"matmul M={M}"):
                 continue
             a = torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)
             c = torch.empty(M, N, device="cuda")
             da, dc = W(a), W(c)
-            for label, bb in (("", dbw), (" (B per-call)", db)):
+            for label in ("", " (B per-call)"):
                 if M <= 16 and label:
                     continue  # the GEMV path reads B as it is either way
-                if M <= 16:
-                    rot = iter(())
+                bufs = rot[label]
+                if M <= 128:
+                    turn = [0]
 
                     def call():
-                        nonlocal rot
-                        try:
-                            nb = next(rot)
-                        except StopIteration:
-                            rot = iter(gemv_dbs)
-                            nb = next(rot)
-                        kernels.matmul(da, nb, out=dc)
+                        kernels.matmul(da, bufs[turn[0] % ROT_COPIES], out=dc)
+                        turn[0] += 1
 
-                    ms = timed(call, n=max(iters, 15), reps=GEMV_COPIES)
+                    for _ in range(ROT_COPIES):  # builds each copy's prepared form (weights)
+                        call()
+                    ms = timed(call, n=max(iters, 15), reps=ROT_COPIES)
+                else:
+                    ms = timed(lambda: kernels.matmul(da, bufs[0], out=dc), n=iters)
+                if M <= 16:
                     add(f"matmul M={M}{label}", "configs[1]", ms, "hbm", 4.0 * (M * K + K * N + M * N))
                 else:
-                    ms = timed(lambda: kernels.matmul(da, bb, out=dc), n=iters)
                     add(f"matmul M={M}{label}", "configs[1]", ms, "tensor", 2.0 * M * N * K)
             del a, c
-        del b, bw, db, dbw, gemv_bs
+        del b, copies, rot
     # config 3: causal attention b4 h32 d128 s2048 (batch folded into 128 heads)
     S, H, D = 2048, 4 * 32, 128
     name = "attention causal b4 h32 d128 s2048"

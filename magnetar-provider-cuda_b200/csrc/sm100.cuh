@@ -78,6 +78,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// 2-D tiled TMA prefetch of one box into the L2 (no shared memory, no completion): a later
+// load of the same box then finds it there.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 // ---- shared memory with explicit state spaces -----------------------------------------------
 __device__ __forceinline__ float4 lds4(uint32_t addr) {
     float4 v;
