@@ -47,43 +47,85 @@ __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) 
     lo = __bfloat16_as_ushort(__float2bfloat16_rn(x - hf));
 }
 
-// [rows, cols] f32 -> bf16 hi / lo in the same layout.
+__device__ __forceinline__ uint32_t pack_bf16(uint16_t a, uint16_t b) { return a | ((uint32_t)b << 16); }
+
+// [rows, cols] f32 -> bf16 hi / lo in the same layout; four 16-byte loads in flight per thread.
 __global__ void __launch_bounds__(256) split_bf16_rows_kernel(const float* __restrict__ src, uint16_t* __restrict__ hi,
                                                               uint16_t* __restrict__ lo, uint64_t n) {
     pdl_enter();
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += stride) {
-        const float4 v = reinterpret_cast<const float4*>(src)[i];
-        uint16_t h[4], l[4];
-        split_bf16(v.x, h[0], l[0]);
-        split_bf16(v.y, h[1], l[1]);
-        split_bf16(v.z, h[2], l[2]);
-        split_bf16(v.w, h[3], l[3]);
-        reinterpret_cast<uint2*>(hi)[i] = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
-        reinterpret_cast<uint2*>(lo)[i] = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+    const uint64_t n4 = n / 4, stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n4; i0 += 4 * stride) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint64_t i = i0 + u * stride;
+            if (i < n4) v[u] = reinterpret_cast<const float4*>(src)[i];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint64_t i = i0 + u * stride;
+            if (i >= n4) break;
+            uint16_t h[4], l[4];
+            split_bf16(v[u].x, h[0], l[0]);
+            split_bf16(v[u].y, h[1], l[1]);
+            split_bf16(v[u].z, h[2], l[2]);
+            split_bf16(v[u].w, h[3], l[3]);
+            reinterpret_cast<uint2*>(hi)[i] = make_uint2(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]));
+            reinterpret_cast<uint2*>(lo)[i] = make_uint2(pack_bf16(l[0], l[1]), pack_bf16(l[2], l[3]));
+        }
     }
 }
 
 // v [keys, width] f32 -> hi / lo [width, keys_p] bf16 (dst[c][r] = v[r][c]), zero past keys.
+// One CTA per 64 x 64 tile: 16-byte loads along v's rows, and each output row segment (64
+// keys, 128 bytes) written by eight lanes with 16-byte stores.
 __global__ void __launch_bounds__(256) split_bf16_transpose_kernel(const float* __restrict__ v, uint64_t keys,
                                                                    uint64_t width, uint16_t* __restrict__ hi,
                                                                    uint16_t* __restrict__ lo, uint64_t keys_p) {
     pdl_enter();
-    __shared__ float tile[32][33];
-    const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
-    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
-    for (int j = ty; j < 32; j += 8) {
-        const uint64_t r = r0 + j, c = c0 + tx;
-        tile[j][tx] = (r < keys && c < width) ? v[r * width + c] : 0.0f;
+    __shared__ float tile[64][65];  // [key][column]
+    const uint64_t c0 = (uint64_t)blockIdx.x * 64, r0 = (uint64_t)blockIdx.y * 64;
+    const bool vec = width % 4 == 0 && c0 + 64 <= width;
+    for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+        const int r = e / 16, q = e % 16;
+        const uint64_t row = r0 + r, col = c0 + 4 * q;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < keys) {
+            if (vec) {
+                x = *reinterpret_cast<const float4*>(v + row * width + col);
+            } else {
+                const float* p = v + row * width;
+                if (col < width) x.x = p[col];
+                if (col + 1 < width) x.y = p[col + 1];
+                if (col + 2 < width) x.z = p[col + 2];
+                if (col + 3 < width) x.w = p[col + 3];
+            }
+        }
+        tile[r][4 * q] = x.x;
+        tile[r][4 * q + 1] = x.y;
+        tile[r][4 * q + 2] = x.z;
+        tile[r][4 * q + 3] = x.w;
     }
     __syncthreads();
-    for (int j = ty; j < 32; j += 8) {
-        const uint64_t c = c0 + j, r = r0 + tx;
-        if (c < width && r < keys_p) {
-            uint16_t h, l;
-            split_bf16(tile[tx][j], h, l);
-            hi[c * keys_p + r] = h;
-            lo[c * keys_p + r] = l;
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    for (int cc = warp * 4 + lane / 8; cc < 64; cc += 32) {  // 4 columns per warp and turn
+        const uint64_t col = c0 + cc;
+        const int k8 = (lane % 8) * 8;  // this lane's 8 keys of the column
+        const uint64_t key = r0 + k8;
+        if (col >= width || key >= keys_p) continue;
+        uint16_t h[8], l[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) split_bf16(tile[k8 + j][cc], h[j], l[j]);
+        uint16_t* dh = hi + col * keys_p + key;
+        uint16_t* dl = lo + col * keys_p + key;
+        if (key + 8 <= keys_p && (keys_p % 8) == 0) {
+            *reinterpret_cast<uint4*>(dh) = make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
+            *reinterpret_cast<uint4*>(dl) = make_uint4(pack_bf16(l[0], l[1]), pack_bf16(l[2], l[3]), pack_bf16(l[4], l[5]), pack_bf16(l[6], l[7]));
+        } else {
+            for (int j = 0; j < 8 && key + j < keys_p; j++) {
+                dh[j] = h[j];
+                dl[j] = l[j];
+            }
         }
     }
 }
@@ -521,7 +563,7 @@ mg_status attention_tc(Device* d, const AttentionArgs& a) {
     MG_TRY(launched(d, "attention split launch"));
     enqueue(d, split_bf16_rows_kernel, grid_for_n(d, k_elems / 4), 256, 0, a.k, khi, klo, k_elems);
     MG_TRY(launched(d, "attention split launch"));
-    dim3 tg((unsigned)((kvd + 31) / 32), (unsigned)((skv_p + 31) / 32));
+    dim3 tg((unsigned)((kvd + 63) / 64), (unsigned)((skv_p + 63) / 64));
     if (tg.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the split pass");
     enqueue(d, split_bf16_transpose_kernel, tg, 256, 0, a.v, Skv, kvd, vhi, vlo, skv_p);
     MG_TRY(launched(d, "attention split launch"));
