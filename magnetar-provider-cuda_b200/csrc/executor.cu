@@ -55,6 +55,11 @@ struct mg_executor {
     std::vector<Deferred> deferred;
     bool deferred_rope = false;
     k::RopeArgs rope{};
+    // Step capture only: an embedding lookup waiting to see whether the next invocation is an
+    // rmsnorm of its rows (then both launch as one kernel).  At most one of the two kinds of
+    // deferred launch is pending at a time.
+    bool embed_pending = false;
+    k::EmbedArgs embed{};
     // tensor parallel
     mg_comm* comm = nullptr;
     std::map<std::string, int> plan;            // weight id -> 0 columns, 1 rows
@@ -207,6 +212,41 @@ mg_status parse_rope(const Attrs& at, mg_rope_params* p) {
 
 // The body of run_invocation_with_offer (src/executor.rs:1422-2027).  `out` holds the
 // offered previous output buffer (or null) and receives the result.
+// An rmsnorm invocation's inputs and attributes (src/executor.rs:1586-1640).
+struct RmsInv {
+    Buffer* x = nullptr;
+    Buffer* w = nullptr;
+    float eps = 1e-6f;
+    uint64_t hc = 0, hd = 0;
+};
+
+mg_status parse_rmsnorm(mg_executor* ex, const mg_invocation* inv, RmsInv* r) {
+    Attrs at{inv};
+    MG_TRY(get_input(ex, inv, 0, &r->x));
+    if (inv->input_count > 1) MG_TRY(get_input(ex, inv, 1, &r->w));
+    const mg_attribute* ws = at.find("with_scale");
+    if (ws && ws->kind == MG_ATTR_BOOL && (ws->int_value != 0) != (r->w != nullptr))
+        return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm with_scale %s contradicts its %d input(s)",
+                    ws->int_value ? "true" : "false", inv->input_count);
+    bool have_hc = false, have_hd = false;
+    for (const char* key : {"head_count", "head_dimension"}) {
+        const mg_attribute* h = at.find(key);
+        if (!h) continue;
+        if (h->kind != MG_ATTR_INT || h->int_value <= 0)
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm %s must be a positive integer", key);
+        if (!strcmp(key, "head_count")) {
+            r->hc = (uint64_t)h->int_value;
+            have_hc = true;
+        } else {
+            r->hd = (uint64_t)h->int_value;
+            have_hd = true;
+        }
+    }
+    if (have_hc != have_hd) return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm head_count and head_dimension go together");
+    r->eps = at.flt("epsilon", 1e-6f);
+    return MG_OK;
+}
+
 mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
     const char* name = inv->kernel;
     Attrs at{inv};
@@ -239,26 +279,9 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
         return mg_embedding(dh, H(a), H(b), has_scale ? 1 : 0, scale, out);
     }
     if (!strcmp(name, "rmsnorm")) {
-        MG_TRY(get_input(ex, inv, 0, &a));
-        if (inv->input_count > 1) MG_TRY(get_input(ex, inv, 1, &b));
-        const mg_attribute* ws = at.find("with_scale");
-        if (ws && ws->kind == MG_ATTR_BOOL && (ws->int_value != 0) != (b != nullptr))
-            return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm with_scale %s contradicts its %d input(s)",
-                        ws->int_value ? "true" : "false", inv->input_count);
-        uint64_t hc = 0, hd = 0;
-        bool have_hc = false, have_hd = false;
-        for (const char* key : {"head_count", "head_dimension"}) {
-            const mg_attribute* h = at.find(key);
-            if (!h) continue;
-            if (h->kind != MG_ATTR_INT || h->int_value <= 0)
-                return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm %s must be a positive integer", key);
-            if (!strcmp(key, "head_count")) { hc = (uint64_t)h->int_value; have_hc = true; }
-            else { hd = (uint64_t)h->int_value; have_hd = true; }
-        }
-        if (have_hc != have_hd)
-            return fail(MG_ATTRIBUTE_UNSUPPORTED, "rmsnorm head_count and head_dimension go together");
-        const float eps = at.flt("epsilon", 1e-6f);
-        return mg_rmsnorm(dh, H(a), b ? H(b) : nullptr, eps, hc, hd, out);
+        RmsInv r;
+        MG_TRY(parse_rmsnorm(ex, inv, &r));
+        return mg_rmsnorm(dh, H(r.x), r.w ? H(r.w) : nullptr, r.eps, r.hc, r.hd, out);
     }
     if (!strcmp(name, "rope")) {
         MG_TRY(get_input(ex, inv, 0, &a));
@@ -355,8 +378,15 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
 }
 
 // ---- step-capture fusion ---------------------------------------------------------------------
-// Launches the deferred group: one grouped projection (with its ropes), or a lone matmul.
+// Launches what is deferred: the pending embedding lookup, or the deferred group -- one grouped
+// projection (with its ropes), or a lone matmul.
 mg_status flush_deferred(mg_executor* ex) {
+    if (ex->embed_pending) {
+        ex->embed_pending = false;
+        const k::EmbedArgs& e = ex->embed;
+        return k::embedding(ex->device, e.table, e.ids, e.out, e.dim, e.num_ids, e.vocab, ex->device->flags,
+                            e.has_scale, e.scale);
+    }
     if (ex->deferred.empty()) return MG_OK;
     k::GemmArgs gs[3];
     float* ro[3] = {nullptr, nullptr, nullptr};
@@ -403,8 +433,50 @@ bool same_rope(const k::RopeArgs& x, const k::RopeArgs& y) {
 bool capture_defer(mg_executor* ex, const mg_invocation* inv, mg_buffer* offered, mg_buffer** result,
                    mg_status* status) {
     Attrs at{inv};
+    if (!strcmp(inv->kernel, "embedding")) {
+        // Deferred until the next invocation shows whether an rmsnorm of its rows follows.
+        Buffer *table = nullptr, *ids = nullptr;
+        if (get_input(ex, inv, 0, &table) != MG_OK || get_input(ex, inv, 1, &ids) != MG_OK) return false;
+        bool has_scale = false;
+        float scale = 1.0f;
+        if (at.flt_opt("scale", &has_scale, &scale) != MG_OK) return false;  // the ordinary call reports it
+        *status = flush_deferred(ex);
+        if (*status != MG_OK) return true;
+        mg_buffer* res = offered;
+        *status = embedding_plan(ex->handle, H(table), H(ids), has_scale ? 1 : 0, scale, &res, &ex->embed);
+        *result = res;
+        if (*status != MG_OK) return true;
+        ex->embed_pending = true;
+        ex->capture_has_embedding = true;
+        return true;
+    }
+    if (ex->embed_pending && !strcmp(inv->kernel, "rmsnorm")) {
+        RmsInv r;
+        if (parse_rmsnorm(ex, inv, &r) != MG_OK || (float*)r.x->ptr != ex->embed.out) return false;
+        if (offered && (float*)buf(offered)->ptr == ex->embed.out) return false;  // in place
+        k::RmsArgs ra;
+        mg_buffer* res = offered;
+        *status = rmsnorm_plan(ex->handle, H(r.x), r.w ? H(r.w) : nullptr, r.eps, r.hc, r.hd, &res, &ra);
+        *result = res;
+        if (*status != MG_OK) return true;
+        if (!k::embedding_rmsnorm_eligible(ex->embed, ra)) {
+            *status = flush_deferred(ex);
+            if (*status == MG_OK) *status = k::rmsnorm(ex->device, ra.x, ra.w, ra.out, ra.rows, ra.cols, ra.w_stride, ra.eps);
+            return true;
+        }
+        ex->embed_pending = false;
+        *status = k::embedding_rmsnorm(ex->device, ex->embed, ra, ex->device->flags);
+        return true;
+    }
     const bool is_mm = !strcmp(inv->kernel, "matmul"), is_rope = !strcmp(inv->kernel, "rope");
     if (!is_mm && !is_rope) return false;
+    if (ex->embed_pending) {  // a matmul or rope after an embedding: the lookup launches first
+        *status = flush_deferred(ex);
+        if (*status != MG_OK) {
+            *result = offered;
+            return true;
+        }
+    }
     if (offered && deferred_uses(ex, buf(offered))) return false;
     Device* d = ex->device;
     if (is_mm) {
@@ -832,6 +904,7 @@ mg_status mg_executor_abort_step_capture(mg_executor* ex) {
     cudaGraph_t gph = nullptr;
     ex->deferred.clear();
     ex->deferred_rope = false;
+    ex->embed_pending = false;
     cudaStreamEndCapture(ex->device->stream, &gph);
     cudaGetLastError();
     if (gph) cudaGraphDestroy(gph);

@@ -147,6 +147,25 @@ mg_status embedding(Device* d, const float* table, const float* ids, float* out,
                     uint64_t num_ids, uint64_t vocab, int* flag, int has_scale, float scale);
 mg_status rmsnorm(Device* d, const float* x, const float* w, float* out, uint64_t rows,
                   uint64_t cols, uint64_t w_stride, float eps);
+struct EmbedArgs {
+    const float* table;
+    const float* ids;
+    float* out;
+    uint64_t dim, num_ids, vocab;
+    int has_scale;
+    float scale;
+};
+struct RmsArgs {
+    const float* x;
+    const float* w;  // null: no gain
+    float* out;
+    uint64_t rows, cols, w_stride;
+    float eps;
+};
+// An embedding followed by an rmsnorm of its rows in one launch (the step capture's fusion):
+// x = the gathered rows, out = rmsnorm(x), each exactly as the two kernels compute them.
+bool embedding_rmsnorm_eligible(const EmbedArgs& e, const RmsArgs& r);
+mg_status embedding_rmsnorm(Device* d, const EmbedArgs& e, const RmsArgs& r, int* flag);
 struct RopeArgs {
     uint64_t rows, cols, half, dimension, position_offset, head_count, rotated_pairs;
     float base, scale, banded_factor, low_freq_factor, high_freq_factor, original_context_length;
@@ -208,6 +227,12 @@ mg_status gemm_group(Device* d, const GemmArgs* gs, int count, const RopeArgs* r
 mg_status matmul_plan(mg_device* h, const mg_buffer* a, const mg_buffer* b, const mg_buffer* b2, const mg_buffer* addend,
                       int addend_mode, int ta, int tb, mg_buffer** out, k::GemmArgs* g);
 mg_status rope_plan(mg_device* h, const mg_buffer* x, const mg_rope_params* p, mg_buffer** out, k::RopeArgs* a);
+// The same for an embedding lookup and an rmsnorm (launch: k::embedding / k::rmsnorm, or the
+// two fused by k::embedding_rmsnorm).
+mg_status embedding_plan(mg_device* h, const mg_buffer* table, const mg_buffer* ids, int has_scale, float scale,
+                         mg_buffer** out, k::EmbedArgs* e);
+mg_status rmsnorm_plan(mg_device* h, const mg_buffer* x, const mg_buffer* w, float epsilon, uint64_t head_count,
+                       uint64_t head_dimension, mg_buffer** out, k::RmsArgs* r);
 
 inline mg_status launched(Device* d, const char* what) {
     d->launches.fetch_add(1, std::memory_order_relaxed);

@@ -332,9 +332,12 @@ mg_status mg_half_binary_f32(mg_device* h, const mg_buffer* ah, const mg_buffer*
     return k::half_binary_f32(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, a->count, dtype, op ? 1 : 0);
 }
 
+}  // extern "C"
+
+namespace mg {
 // src/kernels.rs:3833-3997 (f32 table path) and the executor's `scale` (src/executor.rs:1502-1518)
-mg_status mg_embedding(mg_device* h, const mg_buffer* th, const mg_buffer* ih, int has_scale, float scale,
-                       mg_buffer** out) {
+mg_status embedding_plan(mg_device* h, const mg_buffer* th, const mg_buffer* ih, int has_scale, float scale,
+                         mg_buffer** out, k::EmbedArgs* e) {
     MG_TRY(device_check(h));
     MG_TRY(need(th, "table"));
     MG_TRY(need(ih, "ids"));
@@ -350,9 +353,27 @@ mg_status mg_embedding(mg_device* h, const mg_buffer* th, const mg_buffer* ih, i
     const uint64_t shape[2] = {ids->count, dim};
     Buffer* o;
     MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
+    e->table = (const float*)t->ptr;
+    e->ids = (const float*)ids->ptr;
+    e->out = (float*)o->ptr;
+    e->dim = dim;
+    e->num_ids = ids->count;
+    e->vocab = vocab;
+    e->has_scale = has_scale;
+    e->scale = scale;
+    return MG_OK;
+}
+}  // namespace mg
+
+extern "C" {
+
+mg_status mg_embedding(mg_device* h, const mg_buffer* th, const mg_buffer* ih, int has_scale, float scale,
+                       mg_buffer** out) {
+    k::EmbedArgs e;
+    MG_TRY(embedding_plan(h, th, ih, has_scale, scale, out, &e));
+    Device* d = dev(h);
     if (!d->capturing) MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
-    MG_TRY(k::embedding(d, (const float*)t->ptr, (const float*)ids->ptr, (float*)o->ptr, dim, ids->count, vocab,
-                        d->flags, has_scale, scale));
+    MG_TRY(k::embedding(d, e.table, e.ids, e.out, e.dim, e.num_ids, e.vocab, d->flags, e.has_scale, e.scale));
     if (d->capturing) return MG_OK;  // checked once the captured step has run
     int flags[4];
     MG_TRY(read_flags(d, flags));
@@ -361,9 +382,12 @@ mg_status mg_embedding(mg_device* h, const mg_buffer* th, const mg_buffer* ih, i
     return MG_OK;
 }
 
+}  // extern "C"
+
+namespace mg {
 // src/kernels.rs:4013-4104
-mg_status mg_rmsnorm(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, float epsilon, uint64_t head_count,
-                     uint64_t head_dimension, mg_buffer** out) {
+mg_status rmsnorm_plan(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, float epsilon, uint64_t head_count,
+                       uint64_t head_dimension, mg_buffer** out, k::RmsArgs* r) {
     MG_TRY(device_check(h));
     MG_TRY(need(xh, "input"));
     Device* d = dev(h);
@@ -406,8 +430,24 @@ mg_status mg_rmsnorm(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, flo
     if (!(epsilon > 0.0f)) return fail(MG_SHAPE_UNSUPPORTED, "RMSNorm epsilon must be positive");
     Buffer* o;
     MG_TRY(output_for(d, MG_F32, x->rank, x->shape, out, &o));
-    return k::rmsnorm(d, (const float*)x->ptr, w ? (const float*)w->ptr : nullptr, (float*)o->ptr, rows, cols, w_stride,
-                      epsilon);
+    r->x = (const float*)x->ptr;
+    r->w = w ? (const float*)w->ptr : nullptr;
+    r->out = (float*)o->ptr;
+    r->rows = rows;
+    r->cols = cols;
+    r->w_stride = w_stride;
+    r->eps = epsilon;
+    return MG_OK;
+}
+}  // namespace mg
+
+extern "C" {
+
+mg_status mg_rmsnorm(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, float epsilon, uint64_t head_count,
+                     uint64_t head_dimension, mg_buffer** out) {
+    k::RmsArgs r;
+    MG_TRY(rmsnorm_plan(h, xh, wh, epsilon, head_count, head_dimension, out, &r));
+    return k::rmsnorm(dev(h), r.x, r.w, r.out, r.rows, r.cols, r.w_stride, r.eps);
 }
 
 // src/kernels.rs:4224-4355

@@ -373,6 +373,63 @@ __global__ void __launch_bounds__(256) embedding_kernel(const float* __restrict_
     }
 }
 
+// An embedding then an rmsnorm of its rows, fused (the step capture's fusion of the two nodes):
+// a warp per id copies the table row to x and writes rmsnorm(x) to h.  The row is the
+// embedding kernel's (scaled the same way) and the normalisation is rmsnorm_vec_kernel<32, 8>'s
+// -- the same sums in the same order -- so both outputs equal the two separate launches'.
+// dim % 4 == 0, dim <= 1024, 16-byte aligned rows.
+__global__ void __launch_bounds__(256) embedding_rmsnorm_kernel(const float* __restrict__ table,
+                                                                const float* __restrict__ ids, float* __restrict__ x,
+                                                                uint64_t dim, uint64_t num_ids, uint64_t vocab,
+                                                                int* flag, int has_scale, float scale,
+                                                                const float* __restrict__ w, uint64_t w_stride,
+                                                                float* __restrict__ h, float eps) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * 8, c4 = dim >> 2;
+    for (uint64_t row = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < num_ids; row += warps) {
+        const float raw = ids[row];
+        if (raw < 0.0f || raw != floorf(raw) || !(raw < (float)vocab && (uint64_t)raw < vocab)) {
+            if (lane == 0) atomicExch(flag, 1);
+            continue;
+        }
+        const float4* src = reinterpret_cast<const float4*>(table + (uint64_t)raw * dim);
+        float4* xo = reinterpret_cast<float4*>(x + row * dim);
+        float4 cache[8];
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint64_t idx = (uint64_t)lane + (uint64_t)j * 32;
+            if (idx < c4) {
+                float4 v = src[idx];
+                if (has_scale) v = make_float4(v.x * scale, v.y * scale, v.z * scale, v.w * scale);
+                xo[idx] = v;
+                cache[j] = v;
+                sum += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+        }
+        const float total = warp_sum(sum);
+        const float inv = 1.0f / sqrtf(total / (float)dim + eps);
+        float4* ho = reinterpret_cast<float4*>(h + row * dim);
+        const float4* wr = w ? reinterpret_cast<const float4*>(w + row * w_stride) : nullptr;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint64_t idx = (uint64_t)lane + (uint64_t)j * 32;
+            if (idx < c4) {
+                const float4 v = cache[j];
+                float4 r;
+                if (wr) {
+                    const float4 g = wr[idx];
+                    r = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+                } else {
+                    r = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+                }
+                ho[idx] = r;
+            }
+        }
+    }
+}
+
 inline unsigned cap_grid(const Device* d, uint64_t want, unsigned per_sm) {
     uint64_t cap = (uint64_t)d->sm_count * per_sm;
     if (want > cap) want = cap;
@@ -457,6 +514,18 @@ mg_status embedding(Device* d, const float* table, const float* ids, float* out,
     enqueue(d, embedding_kernel, cap_grid(d, (num_ids + 7) / 8, 8), 256, 0, table, ids, out, dim, num_ids, vocab,
                                                                                 flag, has_scale, scale, vec);
     return launched(d, "embedding kernel launch");
+}
+
+bool embedding_rmsnorm_eligible(const EmbedArgs& e, const RmsArgs& r) {
+    return r.x == e.out && r.out != e.out && r.rows == e.num_ids && r.cols == e.dim && e.dim % 4 == 0 &&
+           e.dim <= 1024 && a16(e.table) && a16(e.out) && a16(r.out) &&
+           (!r.w || (a16(r.w) && (r.w_stride == 0 || r.w_stride == e.dim)));
+}
+
+mg_status embedding_rmsnorm(Device* d, const EmbedArgs& e, const RmsArgs& r, int* flag) {
+    enqueue(d, embedding_rmsnorm_kernel, cap_grid(d, (e.num_ids + 7) / 8, 8), 256, 0, e.table, e.ids, e.out, e.dim,
+            e.num_ids, e.vocab, flag, e.has_scale, e.scale, r.w, r.w_stride, r.out, r.eps);
+    return launched(d, "embedding + rmsnorm kernel launch");
 }
 
 }  // namespace k

@@ -257,3 +257,78 @@ def test_capture_does_not_fuse_what_it_must_not(executor, oracle):
     executor.replay_steps(1)
     for n in names:  # nothing was grouped: bit-identical to the eager launches
         np.testing.assert_array_equal(executor.read_tensor(n), eager[n], err_msg=n)
+
+
+@pytest.mark.parametrize("scaled", [False, True])
+def test_capture_fuses_an_embedding_and_the_rmsnorm_of_its_rows(executor, oracle, scaled):
+    # embedding -> x, rmsnorm(x, gain) -> h: captured, one launch writing both, each equal bit
+    # for bit to the two separate launches; an invalid id is still reported after the replay.
+    mpc = importlib.import_module("magnetar-provider-cuda_b200")
+    native = importlib.import_module("magnetar-provider-cuda_b200._native")
+    r = np.random.default_rng(5)
+    vocab, dim, n = 1000, 512, 96
+    table = r.standard_normal((vocab, dim)).astype(np.float32)
+    gain = (1.0 + 0.1 * r.standard_normal(dim)).astype(np.float32)
+    ids = r.integers(0, vocab, n).astype(np.float32)
+    executor.write_weight_tensor("table", table)
+    executor.write_weight_tensor("gain", gain)
+    executor.write_tensor("ids", ids)
+    attrs = {"scale": 0.5} if scaled else {}
+    invs = [inv("embedding", ["table", "ids"], "x", attrs), inv("rmsnorm", ["x", "gain"], "h", {"epsilon": 1e-5})]
+    for i in invs:
+        executor.run(i)
+    eager = {k: executor.read_tensor(k) for k in ("x", "h")}
+    x_exp = table[ids.astype(np.int64)] * (0.5 if scaled else 1.0)
+    np.testing.assert_array_equal(eager["x"], x_exp)
+    assert rel(eager["h"], oracle.rmsnorm(x_exp, gain, 1e-5)) <= 1e-5
+    executor.begin_step_capture()
+    for i in invs:
+        executor.run(i)
+    executor.end_step_capture()
+    _zero(executor, ("x", "h"))
+    before = executor.kernels.launch_count()
+    executor.replay_steps(1)
+    assert executor.kernels.launch_count() - before == 1  # one fused launch
+    for k in ("x", "h"):
+        np.testing.assert_array_equal(executor.read_tensor(k), eager[k], err_msg=k)
+    bad = ids.copy()
+    bad[7] = vocab + 1
+    native.check(native.lib().mg_buffer_upload(executor.buffer("ids").handle, bad.ctypes.data, bad.nbytes))
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_step()
+    assert e.value.code == "ShapeUnsupported"
+
+
+def test_capture_keeps_an_embedding_apart_when_it_must(executor, oracle):
+    # An rmsnorm of another tensor, an rmsnorm over head slices (its rows are not the
+    # embedding's), and an embedding followed by a matmul of its rows: each launches on its
+    # own, with the eager results.
+    r = np.random.default_rng(6)
+    vocab, dim, n = 500, 256, 64
+    table = r.standard_normal((vocab, dim)).astype(np.float32)
+    gain = (1.0 + 0.1 * r.standard_normal(dim)).astype(np.float32)
+    w = (r.standard_normal((dim, dim)) * 0.05).astype(np.float32)
+    y = r.standard_normal((n, dim)).astype(np.float32)
+    executor.write_weight_tensor("table", table)
+    executor.write_weight_tensor("gain", gain)
+    executor.write_weight_tensor("w", w)
+    executor.write_tensor("ids", r.integers(0, vocab, n).astype(np.float32))
+    executor.write_tensor("y", y)
+    invs = [inv("embedding", ["table", "ids"], "x"), inv("rmsnorm", ["y", "gain"], "hy", {"epsilon": 1e-5}),
+            inv("embedding", ["table", "ids"], "x2"),
+            inv("rmsnorm", ["x2"], "hx", {"epsilon": 1e-5, "head_count": 4, "head_dimension": 64}),
+            inv("embedding", ["table", "ids"], "x3"), inv("matmul", ["x3", "w"], "m")]
+    for i in invs:
+        executor.run(i)
+    names = ("x", "hy", "x2", "hx", "x3", "m")
+    eager = {k: executor.read_tensor(k) for k in names}
+    executor.begin_step_capture()
+    for i in invs:
+        executor.run(i)
+    executor.end_step_capture()
+    _zero(executor, names)
+    before = executor.kernels.launch_count()
+    executor.replay_steps(1)
+    assert executor.kernels.launch_count() - before == 6
+    for k in names:
+        np.testing.assert_array_equal(executor.read_tensor(k), eager[k], err_msg=k)
