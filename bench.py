@@ -389,6 +389,19 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
         ms = timed(lambda: kernels.attention(dq, dk, dv, H, D, causal=True, out=do), max(3, iters // 2), 1)
         add(name, "configs[2]", ms, "tensor", 4.0 * H * S * S * D / 2, bf16x3=True)
         del q, k_, v, o
+    # decode (the "next" row): one query row over a 32768-key history, GQA 32 / 8 heads of 128;
+    # bound by reading K and V once (268 MB, larger than the L2)
+    S, H, KVH, D = 32768, 32, 8, 128
+    name = "attention decode q1 h32 kvh8 d128 kv32768"
+    if want(name):
+        q = torch.randn(1, H * D, device="cuda", generator=g)
+        k_ = torch.randn(S, KVH * D, device="cuda", generator=g)
+        v = torch.randn(S, KVH * D, device="cuda", generator=g)
+        o = torch.empty(1, H * D, device="cuda")
+        dq, dk, dv, do = W(q), W(k_), W(v), W(o)
+        ms = timed(lambda: kernels.attention(dq, dk, dv, H, D, kv_head_count=KVH, causal=True, out=do), reps=3)
+        add(name, "decode", ms, "hbm", 4.0 * (2 * S * KVH * D + 2 * H * D))
+        del q, k_, v, o
     # config 3': softmax rows [262144, 2048]
     name = "softmax [262144,2048]"
     if want(name):

@@ -197,6 +197,12 @@ typedef struct mg_rope_params {
 } mg_rope_params;
 mg_status mg_rope(mg_device* d, const mg_buffer* x, const mg_rope_params* params, mg_buffer** out);
 
+/* kv-write (src/kernels.rs:2278-2325, `append-kv-history-in-place`): writes the rows of the
+ * rank-2 `rows` [count, width] over `store`'s rows row_offset .. row_offset + count, in place;
+ * the store's other rows are unchanged.  Both f32 of the same width; a range past the store's
+ * rows is MG_SHAPE_UNSUPPORTED. */
+mg_status mg_kv_write(mg_device* d, mg_buffer* store, const mg_buffer* rows, uint64_t row_offset);
+
 /* softmax over the rows of a rank-2 buffer; MG_EXECUTION_FAILED when a row has no finite
  * maximum (src/kernels.rs:4357-4386). */
 mg_status mg_softmax(mg_device* d, const mg_buffer* x, mg_buffer** out);
@@ -322,6 +328,17 @@ mg_status mg_executor_replay_steps(mg_executor* ex, int count);
 mg_status mg_executor_launch_step(mg_executor* ex);
 /* ... and the check of every replay since the last check (waits for the device). */
 mg_status mg_executor_check_steps(mg_executor* ex);
+/* Step capture with advancing attributes (src/kernels.rs:1019-1062, StepCaptureRequest's
+ * advancing_attributes): while recording, a launch whose attribute is named here --
+ * "position_offset" (rope), "key_count" (attention with a key count: one query row),
+ * "row_offset" (kv-write) -- adds the replay's offset to that attribute at run time, and
+ * records the largest offset it stays in bounds for.  mg_executor_replay_step_at replays at
+ * an offset (above the captured bound: MG_CAPTURE_UNSUPPORTED, nothing runs); the other
+ * replays use offset 0.  A decode loop captures one step and replays it at 0, 1, 2, ... */
+mg_status mg_executor_begin_step_capture_advancing(mg_executor* ex, const char* const* attributes, int count);
+mg_status mg_executor_replay_step_at(mg_executor* ex, uint64_t offset);
+/* The largest offset the captured step accepts (UINT64_MAX: unbounded). */
+mg_status mg_executor_step_max_offset(mg_executor* ex, uint64_t* out);
 /* Observation log (src/executor.rs:1082-1100): counts of Started/Completed/Failed. */
 mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t* completed,
                                    uint64_t* failed);

@@ -133,6 +133,7 @@ SIGNATURES = {
     "mg_rmsnorm": [_P, _P, _P, _F, _U64, _U64, _PP],
     "mg_rope": [_P, _P, ctypes.POINTER(RopeParams), _PP],
     "mg_softmax": [_P, _P, _PP],
+    "mg_kv_write": [_P, _P, _P, _U64],
     "mg_matmul": [_P, _P, _P, _I, _I, _PP],
     "mg_matmul_bias": [_P, _P, _P, _P, _I, _I, _PP],
     "mg_matmul_residual": [_P, _P, _P, _P, _I, _I, _PP],
@@ -154,6 +155,9 @@ SIGNATURES = {
     "mg_executor_submit_kernel": [_P, ctypes.POINTER(Invocation)],
     "mg_executor_synchronize": [_P],
     "mg_executor_begin_step_capture": [_P],
+    "mg_executor_begin_step_capture_advancing": [_P, ctypes.POINTER(ctypes.c_char_p), _I],
+    "mg_executor_replay_step_at": [_P, _U64],
+    "mg_executor_step_max_offset": [_P, _U64P],
     "mg_executor_end_step_capture": [_P],
     "mg_executor_abort_step_capture": [_P],
     "mg_executor_replay_step": [_P],

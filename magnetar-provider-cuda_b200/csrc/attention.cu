@@ -372,6 +372,208 @@ mg_status launch_short(Device* d, const AttnP& p, uint32_t cap) {
     return launched(d, "short attention launch");
 }
 
+// ---- decode: one query row against a key history, keys split across CTAs -------------------
+// The reference's attention_split / attention_combine (src/kernels.rs:6939-7078): chunks of
+// keys scored by separate CTAs, merged in chunk order.  Here a CTA of 128 threads takes one
+// head and 128 keys (a thread per key for the scores; a thread per output column for P.V, so
+// V's rows are read coalesced) and writes its partial (max, sum, unnormalised output); the
+// combine kernel rescales the partials to the common max and adds them in chunk order.  Bound
+// by reading K and V once.  With a captured step's advancing key count the grid covers every
+// row K and V hold and the admitted count is read at run time.
+constexpr int kDecodeKeys = 128;
+constexpr int kDecodeMaxDim = 256;
+
+struct DecodeP {
+    const float* q;
+    const float* k;
+    const float* v;
+    float* partial;  // [head][chunk][value_dim + 2]: max, sum, output
+    float* out;
+    uint64_t kv_seq_len, head_count, group, head_dim, value_dim, q_model_dim, kv_model_dim, v_model_dim, chunks;
+    int causal;
+    int64_t window;
+    float scale;
+    const uint64_t* step;
+    int vec;  // K rows 16-byte aligned: float4 loads
+};
+
+// Max (or sum) over the CTA's 128 threads of each of G values, one pair of barriers for all.
+template <int G>
+__device__ __forceinline__ void block_reduce_g(float (&v)[G], float (*red)[4], bool is_max) {
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        for (int o = 16; o > 0; o >>= 1) {
+            const float w = __shfl_xor_sync(0xffffffffu, v[g], o);
+            v[g] = is_max ? fmaxf(v[g], w) : v[g] + w;
+        }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0)
+#pragma unroll
+        for (int g = 0; g < G; g++) red[g][warp] = v[g];
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        v[g] = is_max ? fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]))
+                      : (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
+}
+
+// G > 1: a CTA takes the G query heads of one KV head (blockIdx.y = KV head), so K and V are
+// read once for the group (the reference's grouped decode kernel); G == 1: blockIdx.y = the
+// query head.  blockIdx.x = the chunk of keys.
+template <int G>
+__global__ void __launch_bounds__(kDecodeKeys) attention_decode_kernel(DecodeP p) {
+    pdl_enter();
+    __shared__ float qs[G][kDecodeMaxDim];
+    __shared__ float ps[G][kDecodeKeys];
+    __shared__ float red[G][4];
+    const uint64_t h0 = G == 1 ? blockIdx.y : (uint64_t)blockIdx.y * G;
+    const uint64_t kvh = G == 1 ? blockIdx.y / p.group : blockIdx.y;
+    const uint64_t c = blockIdx.x;
+    const uint64_t n_keys = p.kv_seq_len + (p.step ? *p.step : 0);
+    const uint64_t qpos = n_keys - 1;  // the row's position: the last admitted key
+    uint64_t lo = 0;
+    if (p.window >= 0) {
+        const uint64_t back = (uint64_t)p.window - 1;
+        lo = qpos > back ? qpos - back : 0;
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        for (uint64_t d = threadIdx.x; d < p.head_dim; d += kDecodeKeys) qs[g][d] = p.q[(h0 + g) * p.head_dim + d];
+    __syncthreads();
+    const uint64_t key = c * kDecodeKeys + threadIdx.x;
+    const bool live = key >= lo && key < n_keys;
+    float s[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) s[g] = __int_as_float(0xff800000);
+    if (live) {
+        const float* kr = p.k + key * p.kv_model_dim + kvh * p.head_dim;
+        float dot[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) dot[g] = 0.0f;
+        if (p.vec) {  // the same sums, in the same order, from 16-byte loads
+            for (uint64_t d = 0; d < p.head_dim; d += 4) {
+                const float4 kv = *reinterpret_cast<const float4*>(kr + d);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    dot[g] += qs[g][d] * kv.x;
+                    dot[g] += qs[g][d + 1] * kv.y;
+                    dot[g] += qs[g][d + 2] * kv.z;
+                    dot[g] += qs[g][d + 3] * kv.w;
+                }
+            }
+        } else {
+            for (uint64_t d = 0; d < p.head_dim; d++) {
+                const float kv = kr[d];
+#pragma unroll
+                for (int g = 0; g < G; g++) dot[g] += qs[g][d] * kv;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) s[g] = dot[g] * p.scale;
+    }
+    float m[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) m[g] = s[g];
+    block_reduce_g<G>(m, red, true);
+    if (m[0] == __int_as_float(0xff800000)) {  // no admitted key in this chunk (for any head)
+        if (threadIdx.x == 0)
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float* part = p.partial + ((h0 + g) * p.chunks + c) * (p.value_dim + 2);
+                part[0] = __int_as_float(0xff800000);
+                part[1] = 0.0f;
+            }
+        return;
+    }
+    float l[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        l[g] = live ? expf(s[g] - m[g]) : 0.0f;
+        ps[g][threadIdx.x] = l[g];
+    }
+    block_reduce_g<G>(l, red, false);  // its barriers also publish ps
+    const uint64_t k0 = c * kDecodeKeys;
+    const int nk = (int)min((uint64_t)kDecodeKeys, n_keys - k0);
+    for (uint64_t d = threadIdx.x; d < p.value_dim; d += kDecodeKeys) {
+        const float* vc = p.v + k0 * p.v_model_dim + kvh * p.value_dim + d;
+        float acc[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) acc[g] = 0.0f;
+        for (int j = 0; j < nk; j++) {
+            const float vv = vc[(uint64_t)j * p.v_model_dim];
+#pragma unroll
+            for (int g = 0; g < G; g++) acc[g] += ps[g][j] * vv;
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) p.partial[((h0 + g) * p.chunks + c) * (p.value_dim + 2) + 2 + d] = acc[g];
+    }
+    if (threadIdx.x == 0)
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float* part = p.partial + ((h0 + g) * p.chunks + c) * (p.value_dim + 2);
+            part[0] = m[g];
+            part[1] = l[g];
+        }
+}
+
+__global__ void __launch_bounds__(kDecodeKeys) attention_combine_kernel(DecodeP p) {
+    pdl_enter();
+    const uint64_t h = blockIdx.x;
+    const float* base = p.partial + h * p.chunks * (p.value_dim + 2);
+    float mx = __int_as_float(0xff800000);
+    for (uint64_t c = 0; c < p.chunks; c++) mx = fmaxf(mx, base[c * (p.value_dim + 2)]);
+    float l = 0.0f;
+    for (uint64_t c = 0; c < p.chunks; c++) {
+        const float mc = base[c * (p.value_dim + 2)];
+        if (mc != __int_as_float(0xff800000)) l += base[c * (p.value_dim + 2) + 1] * expf(mc - mx);
+    }
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    for (uint64_t d = threadIdx.x; d < p.value_dim; d += kDecodeKeys) {
+        float o = 0.0f;
+        for (uint64_t c = 0; c < p.chunks; c++) {
+            const float mc = base[c * (p.value_dim + 2)];
+            if (mc != __int_as_float(0xff800000)) o += base[c * (p.value_dim + 2) + 2 + d] * expf(mc - mx);
+        }
+        p.out[h * p.value_dim + d] = o * inv;
+    }
+}
+
+mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
+    DecodeP p;
+    p.q = a.q;
+    p.k = a.k;
+    p.v = a.v;
+    p.out = a.out;
+    p.kv_seq_len = a.kv_seq_len;
+    p.head_count = a.head_count;
+    p.group = a.head_count / a.kv_head_count;
+    p.head_dim = a.head_dim;
+    p.value_dim = a.value_dim;
+    p.q_model_dim = a.q_model_dim;
+    p.kv_model_dim = a.kv_model_dim;
+    p.v_model_dim = a.v_model_dim;
+    p.causal = a.causal;
+    p.window = a.window;
+    p.scale = a.scale;
+    p.step = a.step;
+    p.vec = (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 && a.kv_model_dim % 4 == 0 && a.head_dim % 4 == 0;
+    const uint64_t keys = a.step ? a.kv_rows : a.kv_seq_len;  // the grid covers what may be admitted
+    p.chunks = std::max<uint64_t>(1, (keys + kDecodeKeys - 1) / kDecodeKeys);
+    if (p.chunks > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the decode grid");
+    MG_TRY(scratch(d, 6, a.head_count * p.chunks * (a.value_dim + 2) * sizeof(float), (void**)&p.partial));
+    const dim3 by_kv((unsigned)p.chunks, (unsigned)a.kv_head_count), by_q((unsigned)p.chunks, (unsigned)a.head_count);
+    switch (p.group) {
+        case 2: enqueue(d, attention_decode_kernel<2>, by_kv, kDecodeKeys, 0, p); break;
+        case 4: enqueue(d, attention_decode_kernel<4>, by_kv, kDecodeKeys, 0, p); break;
+        case 8: enqueue(d, attention_decode_kernel<8>, by_kv, kDecodeKeys, 0, p); break;
+        default: enqueue(d, attention_decode_kernel<1>, by_q, kDecodeKeys, 0, p); break;
+    }
+    MG_TRY(launched(d, "decode attention launch"));
+    enqueue(d, attention_combine_kernel, dim3((unsigned)a.head_count), kDecodeKeys, 0, p);
+    return launched(d, "decode attention combine launch");
+}
+
 }  // namespace
 
 namespace k {
@@ -403,6 +605,13 @@ mg_status attention(Device* d, const AttentionArgs& a) {
                            reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out)) & 15) == 0 &&
                          a.q_model_dim % 4 == 0 && a.kv_model_dim % 4 == 0 && a.v_model_dim % 4 == 0;
     if (a.head_count > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention head_count exceeds the launch grid");
+    // One query row (a decode step): keys split across CTAs.
+    const bool decode = a.seq_len == 1 && a.head_dim <= kDecodeMaxDim && a.value_dim <= kDecodeMaxDim;
+    if (decode) return attention_decode(d, a);
+    if (a.step)
+        return fail(MG_CAPTURE_UNSUPPORTED,
+                    "an advancing key_count needs a single query row with head and value dimensions of at most %d",
+                    kDecodeMaxDim);
     // Short spans: one short kernel when every CTA's keys fit in shared memory and the grid is
     // at most two waves; otherwise the tensor-core pipeline.
     if (aligned && a.value_dim == a.head_dim && (a.head_dim == 32 || a.head_dim == 64 || a.head_dim == 128)) {

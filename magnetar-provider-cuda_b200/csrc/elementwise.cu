@@ -312,6 +312,29 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const uint16_t* __rest
         out[i] = hdecode<DT>(in[i]);
 }
 
+// kv-write (src/kernels.rs:2278-2325): store rows row_offset + step .. + count <- rows, where
+// `step` is a captured step's advancing offset read at run time (null: none).
+__global__ void __launch_bounds__(kThreads) kv_write_kernel(const float* __restrict__ rows, float* __restrict__ store,
+                                                            uint64_t n, uint64_t width, uint64_t row_offset,
+                                                            const uint64_t* __restrict__ step, int vec) {
+    pdl_enter();
+    float* dst = store + (row_offset + (step ? *step : 0)) * width;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {
+        const float4* s4 = reinterpret_cast<const float4*>(rows);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (uint64_t i = t0; i < n / 4; i += stride) d4[i] = s4[i];
+        return;
+    }
+    for (uint64_t i = t0; i < n; i += stride) dst[i] = rows[i];
+}
+
+__global__ void set_u64_kernel(uint64_t* dst, uint64_t value) {
+    pdl_enter();
+    *dst = value;
+}
+
 __global__ void __launch_bounds__(kThreads) zero_kernel(uint4* __restrict__ p, uint64_t n16) {
     pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -407,6 +430,21 @@ mg_status decode_half(Device* d, const uint16_t* in, float* out, uint64_t n, mg_
     if (dtype == MG_F16) enqueue(d, decode_kernel<MG_F16>, grid_for(d, n), kThreads, 0, in, out, n);
     else enqueue(d, decode_kernel<MG_BF16>, grid_for(d, n), kThreads, 0, in, out, n);
     return launched(d, "half decode kernel launch");
+}
+
+mg_status kv_write(Device* d, const KvWriteArgs& a) {
+    const uint64_t n = a.count * a.width;
+    if (n == 0) return MG_OK;
+    const int vec = a.width % 4 == 0 && (reinterpret_cast<uintptr_t>(a.rows) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(a.store) & 15) == 0;
+    enqueue(d, kv_write_kernel, grid_for(d, vec ? n / 4 : n), kThreads, 0, a.rows, a.store, n, a.width, a.row_offset,
+            a.step, vec);
+    return launched(d, "kv-write kernel launch");
+}
+
+mg_status set_step_offset(Device* d, uint64_t* dst, uint64_t value) {
+    enqueue(d, set_u64_kernel, 1, 1, 0, dst, value);
+    return launched(d, "step offset launch");
 }
 
 mg_status fill_zero(Device* d, void* ptr, uint64_t bytes) {

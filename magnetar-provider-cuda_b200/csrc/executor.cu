@@ -60,6 +60,13 @@ struct mg_executor {
     // deferred launch is pending at a time.
     bool embed_pending = false;
     k::EmbedArgs embed{};
+    // Advancing attributes of the step being captured (src/kernels.rs:1019-1062): launches
+    // whose attribute is named here read the replay's offset from the device and record the
+    // largest offset they stay in bounds for; the captured step keeps the least of those.
+    std::set<std::string> advancing;
+    uint64_t capture_max_offset = UINT64_MAX;
+    uint64_t step_max_offset = UINT64_MAX;
+    bool step_advancing = false;
     // tensor parallel
     mg_comm* comm = nullptr;
     std::map<std::string, int> plan;            // weight id -> 0 columns, 1 rows
@@ -125,6 +132,16 @@ mg_status get_input(mg_executor* ex, const mg_invocation* inv, int index, Buffer
         return fail(MG_EXECUTION_FAILED, "no materialized data for input resource %s", inv->inputs[index]);
     *out = it->second;
     return MG_OK;
+}
+
+// While a step capture records: the device address of the replay offset for a launch whose
+// `attribute` advances, after recording that the launch stays within bounds for offsets up to
+// `max_offset` (src/kernels.rs:1425-1435).  Null outside a capture or for an attribute that
+// does not advance.
+const uint64_t* advancing_offset(mg_executor* ex, const char* attribute, uint64_t max_offset) {
+    if (!ex->capturing || !ex->advancing.count(attribute)) return nullptr;
+    ex->capture_max_offset = std::min(ex->capture_max_offset, max_offset);
+    return ex->device->step_offset;
 }
 
 // src/executor.rs:1238-1249: accumulation_dtype, when given, must be f32.
@@ -269,6 +286,41 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
         MG_TRY(get_input(ex, inv, 1, &b));
         return mg_silu_mul(dh, H(a), H(b), out);
     }
+    if (!strcmp(name, "kv-write")) {
+        // src/executor.rs:1366-1420: in place when the output is the store (a KV history), else
+        // into a copy of the store kept under the output; a failed write leaves the rows as
+        // they were.
+        uint64_t row_offset = 0;
+        if (!at.integer("row_offset", &row_offset))
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "kv-write needs a non-negative integer row_offset");
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        k::KvWriteArgs kw;
+        MG_TRY(kv_write_plan(dh, H(a), H(b), row_offset, &kw));
+        // An advancing row_offset writes at row_offset + offset (src/kernels.rs:2306-2310).
+        kw.step = advancing_offset(ex, "row_offset", kw.capacity - (kw.row_offset + kw.count));
+        const bool in_place = !strcmp(inv->inputs[0], inv->output);
+        Buffer* target = a;
+        if (!in_place) {
+            MG_TRY(buffer_new(ex->device, a->dtype, a->rank, a->shape, &target));
+            cudaError_t e = cudaMemcpyAsync(target->ptr, a->ptr, a->count * dtype_size(a->dtype),
+                                            cudaMemcpyDeviceToDevice, ex->device->stream);
+            if (e != cudaSuccess) {
+                buffer_free(target);
+                return from_cuda(e, "copying the kv-write store");
+            }
+            kw.store = (float*)target->ptr;
+        } else {
+            buffer_drop_prep(a);
+        }
+        const mg_status s = k::kv_write(ex->device, kw);
+        if (s != MG_OK) {
+            if (!in_place) buffer_free(target);
+            return s;
+        }
+        *out = H(target);
+        return MG_OK;
+    }
     if (!strcmp(name, "embedding")) {
         MG_TRY(get_input(ex, inv, 0, &a));
         MG_TRY(get_input(ex, inv, 1, &b));
@@ -287,7 +339,10 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
         MG_TRY(get_input(ex, inv, 0, &a));
         mg_rope_params p;
         MG_TRY(parse_rope(at, &p));
-        return mg_rope(dh, H(a), &p, out);
+        k::RopeArgs ra;
+        MG_TRY(rope_plan(dh, H(a), &p, out, &ra));
+        ra.step = advancing_offset(ex, "position_offset", UINT64_MAX);
+        return k::rope(ex->device, (const float*)a->ptr, (float*)buf(*out)->ptr, ra);
     }
     if (!strcmp(name, "attention")) {
         MG_TRY(get_input(ex, inv, 0, &a));
@@ -325,7 +380,11 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
         }
         if (at.find("value_head_stride") || at.find("latent_kv_width"))
             return fail(MG_ATTRIBUTE_UNSUPPORTED, "latent and strided-value attention forms are not implemented");
-        return mg_attention(dh, H(a), H(b), H(c), &p, out);
+        k::AttentionArgs aa;
+        MG_TRY(attention_plan(dh, H(a), H(b), H(c), &p, out, &aa));
+        // An advancing key_count admits key_count + offset keys (src/kernels.rs:6630-6640).
+        if (p.key_count >= 0) aa.step = advancing_offset(ex, "key_count", aa.kv_rows - aa.kv_seq_len);
+        return k::attention(ex->device, aa);
     }
     if (!strcmp(name, "softmax")) {
         MG_TRY(get_input(ex, inv, 0, &a));
@@ -421,7 +480,7 @@ bool same_rope(const k::RopeArgs& x, const k::RopeArgs& y) {
            x.low_freq_factor == y.low_freq_factor && x.high_freq_factor == y.high_freq_factor &&
            x.original_context_length == y.original_context_length && x.yarn_factor == y.yarn_factor &&
            x.yarn_low == y.yarn_low && x.yarn_high == y.yarn_high && x.amplitude == y.amplitude &&
-           x.half_split == y.half_split;
+           x.half_split == y.half_split && x.step == y.step;
 }
 
 // During a step capture: takes a plain matmul whose B is a weight into the deferred group (or
@@ -537,6 +596,7 @@ bool capture_defer(mg_executor* ex, const mg_invocation* inv, mg_buffer* offered
         *status = s;
         return true;
     }
+    ra.step = advancing_offset(ex, "position_offset", UINT64_MAX);
     bool attach = !deferred_uses(ex, buf(res)) && (!ex->deferred_rope || same_rope(ex->rope, ra));
     if (attach) {
         const size_t n = ex->deferred.size();
@@ -853,7 +913,11 @@ mg_status mg_executor_synchronize(mg_executor* ex) {
 }
 
 mg_status mg_executor_begin_step_capture(mg_executor* ex) {
-    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    return mg_executor_begin_step_capture_advancing(ex, nullptr, 0);
+}
+
+mg_status mg_executor_begin_step_capture_advancing(mg_executor* ex, const char* const* attributes, int count) {
+    if (!ex || (count > 0 && !attributes)) return fail(MG_INVALID_ARGUMENT, "null argument");
     std::lock_guard<std::mutex> g(ex->lock);
     if (ex->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "a step capture is already in progress");
     MG_TRY(device_check(ex->handle));
@@ -861,6 +925,10 @@ mg_status mg_executor_begin_step_capture(mg_executor* ex) {
     MG_CUDA(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed), "beginning a step capture");
     ex->capturing = true;
     d->capturing = true;
+    ex->advancing.clear();
+    for (int i = 0; i < count; i++)
+        if (attributes[i]) ex->advancing.insert(attributes[i]);
+    ex->capture_max_offset = UINT64_MAX;
     ex->capture_has_embedding = false;
     ex->launches_at_capture = d->launches.load();
     return MG_OK;
@@ -890,6 +958,9 @@ mg_status mg_executor_end_step_capture(mg_executor* ex) {
     if (ex->graph) cudaGraphDestroy(ex->graph);
     ex->graph = gph;
     ex->graph_exec = exec;
+    ex->step_advancing = !ex->advancing.empty();
+    ex->step_max_offset = ex->capture_max_offset;
+    ex->advancing.clear();
     ex->step_has_embedding = ex->capture_has_embedding;
     // Captured launches did not run; count them when a replay runs them.
     ex->graph_kernels = d->launches.load() - ex->launches_at_capture;
@@ -905,6 +976,7 @@ mg_status mg_executor_abort_step_capture(mg_executor* ex) {
     ex->deferred.clear();
     ex->deferred_rope = false;
     ex->embed_pending = false;
+    ex->advancing.clear();
     cudaStreamEndCapture(ex->device->stream, &gph);
     cudaGetLastError();
     if (gph) cudaGraphDestroy(gph);
@@ -913,14 +985,20 @@ mg_status mg_executor_abort_step_capture(mg_executor* ex) {
     return MG_OK;
 }
 
-mg_status mg_executor_replay_steps(mg_executor* ex, int count) {
+namespace {
+// Replays the captured step `count` times at `offset` (count < 0: one launch and no check; 0:
+// the check only).
+mg_status replay_at(mg_executor* ex, int count, uint64_t offset) {
     if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
     std::lock_guard<std::mutex> g(ex->lock);
     if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
     MG_TRY(device_check(ex->handle));
     Device* d = ex->device;
-    // count < 0: one launch and no check; 0: the check only.
+    if (offset > ex->step_max_offset)
+        return fail(MG_CAPTURE_UNSUPPORTED, "offset %llu leaves the captured bounds (at most %llu)",
+                    (unsigned long long)offset, (unsigned long long)ex->step_max_offset);
     const int launches = count < 0 ? 1 : count;
+    if (ex->step_advancing && launches > 0) MG_TRY(k::set_step_offset(d, d->step_offset, offset));
     for (int i = 0; i < launches; i++) {
         MG_CUDA(cudaGraphLaunch(ex->graph_exec, d->stream), "replaying the captured step");
         d->launches.fetch_add(ex->graph_kernels);
@@ -934,6 +1012,20 @@ mg_status mg_executor_replay_steps(mg_executor* ex, int count) {
         if (d->host_flags[0])
             return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
     }
+    return MG_OK;
+}
+
+}  // namespace
+
+mg_status mg_executor_replay_steps(mg_executor* ex, int count) { return replay_at(ex, count, 0); }
+
+mg_status mg_executor_replay_step_at(mg_executor* ex, uint64_t offset) { return replay_at(ex, 1, offset); }
+
+mg_status mg_executor_step_max_offset(mg_executor* ex, uint64_t* out) {
+    if (!ex || !out) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step");
+    *out = ex->step_max_offset;
     return MG_OK;
 }
 

@@ -944,6 +944,7 @@ mg_status gemm_group(Device* d, const GemmArgs* gs, int count, const RopeArgs* r
         rk.half = rope->half;
         rk.dimension = rope->dimension;
         rk.position_offset = rope->position_offset;
+        rk.step = rope->step;
         rk.head_count = rope->head_count;
         rk.head_width = rope->cols / rope->head_count;
         rk.rotated_pairs = rope->rotated_pairs;

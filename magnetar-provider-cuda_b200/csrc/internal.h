@@ -54,6 +54,9 @@ struct Device {
     // [1] non-finite softmax row.  Pinned host mirror for the read back.
     int* flags = nullptr;
     int* host_flags = nullptr;
+    // The offset a captured step's advancing attributes add, read by its kernels at run time
+    // (written before each replay).
+    uint64_t* step_offset = nullptr;
     // Arrival counters of kernels whose last CTA finishes a tile (65,536 entries, zero
     // between kernels: the finishing CTA resets its entry).
     unsigned int* counters = nullptr;
@@ -142,6 +145,15 @@ mg_status half_binary_f32(Device* d, const float* a, const float* b, float* out,
 mg_status encode_half(Device* d, const float* in, uint16_t* out, uint64_t n, mg_dtype dtype);
 mg_status decode_half(Device* d, const uint16_t* in, float* out, uint64_t n, mg_dtype dtype);
 mg_status fill_zero(Device* d, void* ptr, uint64_t bytes);
+struct KvWriteArgs {
+    const float* rows;
+    float* store;
+    uint64_t count, width, row_offset, capacity;
+    const uint64_t* step;  // a captured step's advancing row offset (null: none)
+};
+mg_status kv_write(Device* d, const KvWriteArgs& a);
+// *dst = value, in stream order (a captured step's offset before its replay).
+mg_status set_step_offset(Device* d, uint64_t* dst, uint64_t value);
 
 mg_status embedding(Device* d, const float* table, const float* ids, float* out, uint64_t dim,
                     uint64_t num_ids, uint64_t vocab, int* flag, int has_scale, float scale);
@@ -171,6 +183,7 @@ struct RopeArgs {
     float base, scale, banded_factor, low_freq_factor, high_freq_factor, original_context_length;
     float yarn_factor, yarn_low, yarn_high, amplitude;
     int half_split;
+    const uint64_t* step = nullptr;  // a captured step's advancing position offset (null: none)
 };
 mg_status rope(Device* d, const float* x, float* out, const RopeArgs& a);
 mg_status softmax(Device* d, const float* x, float* out, uint64_t rows, uint64_t cols, int* flag);
@@ -212,6 +225,10 @@ struct AttentionArgs {
     int64_t window;  // -1 none
     uint64_t query_position_offset;
     float scale;
+    // A captured step's advancing key count (null: none): kv_seq_len + *step keys are admitted
+    // at run time, at most kv_rows (the rows K and V hold).  Single query rows only.
+    const uint64_t* step = nullptr;
+    uint64_t kv_rows = 0;
 };
 mg_status attention(Device* d, const AttentionArgs& a);
 
@@ -233,6 +250,11 @@ mg_status embedding_plan(mg_device* h, const mg_buffer* table, const mg_buffer* 
                          mg_buffer** out, k::EmbedArgs* e);
 mg_status rmsnorm_plan(mg_device* h, const mg_buffer* x, const mg_buffer* w, float epsilon, uint64_t head_count,
                        uint64_t head_dimension, mg_buffer** out, k::RmsArgs* r);
+// kv-write's validation (the write lands in `store` itself).
+mg_status kv_write_plan(mg_device* h, mg_buffer* store, const mg_buffer* rows, uint64_t row_offset, k::KvWriteArgs* a);
+// attention's validation and output (launch: k::attention).
+mg_status attention_plan(mg_device* h, const mg_buffer* q, const mg_buffer* k, const mg_buffer* v,
+                         const mg_attention_params* p, mg_buffer** out, k::AttentionArgs* a);
 
 inline mg_status launched(Device* d, const char* what) {
     d->launches.fetch_add(1, std::memory_order_relaxed);

@@ -450,6 +450,50 @@ mg_status mg_rmsnorm(mg_device* h, const mg_buffer* xh, const mg_buffer* wh, flo
     return k::rmsnorm(dev(h), r.x, r.w, r.out, r.rows, r.cols, r.w_stride, r.eps);
 }
 
+}  // extern "C"
+
+namespace mg {
+// src/kernels.rs:2278-2325
+mg_status kv_write_plan(mg_device* h, mg_buffer* sh, const mg_buffer* rh, uint64_t row_offset, k::KvWriteArgs* a) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(sh, "store"));
+    MG_TRY(need(rh, "rows"));
+    Device* d = dev(h);
+    Buffer* store = buf(sh);
+    const Buffer* rows = buf(rh);
+    MG_TRY(same_device(d, store));
+    MG_TRY(same_device(d, rows));
+    MG_TRY(require_f32(store, "kv-write"));
+    MG_TRY(require_f32(rows, "kv-write"));
+    uint64_t capacity, width, count, row_width;
+    MG_TRY(rows_cols(store, &capacity, &width));
+    MG_TRY(rows_cols(rows, &count, &row_width));
+    if (row_width != width)
+        return fail(MG_SHAPE_UNSUPPORTED, "kv-write rows have width %llu, the store %llu", (unsigned long long)row_width,
+                    (unsigned long long)width);
+    if (row_offset > capacity || count > capacity - row_offset)
+        return fail(MG_SHAPE_UNSUPPORTED, "kv-write of %llu rows at %llu exceeds the store's %llu rows",
+                    (unsigned long long)count, (unsigned long long)row_offset, (unsigned long long)capacity);
+    a->rows = (const float*)rows->ptr;
+    a->store = (float*)store->ptr;
+    a->count = count;
+    a->width = width;
+    a->row_offset = row_offset;
+    a->capacity = capacity;
+    a->step = nullptr;
+    return MG_OK;
+}
+}  // namespace mg
+
+extern "C" {
+
+mg_status mg_kv_write(mg_device* h, mg_buffer* store, const mg_buffer* rows, uint64_t row_offset) {
+    k::KvWriteArgs a;
+    MG_TRY(kv_write_plan(h, store, rows, row_offset, &a));
+    buffer_drop_prep(buf(store));  // its contents change
+    return k::kv_write(dev(h), a);
+}
+
 // src/kernels.rs:4224-4355
 mg_status mg_rope(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp, mg_buffer** out) {
     k::RopeArgs a;
@@ -566,8 +610,11 @@ mg_status mg_gated_matmul(mg_device* h, const mg_buffer* a, const mg_buffer* gat
 }
 
 // src/kernels.rs:6505-6629
-mg_status mg_attention(mg_device* h, const mg_buffer* qh, const mg_buffer* kh, const mg_buffer* vh,
-                       const mg_attention_params* pp, mg_buffer** out) {
+}  // extern "C"
+
+namespace mg {
+mg_status attention_plan(mg_device* h, const mg_buffer* qh, const mg_buffer* kh, const mg_buffer* vh,
+                         const mg_attention_params* pp, mg_buffer** out, k::AttentionArgs* ap) {
     MG_TRY(device_check(h));
     MG_TRY(need(qh, "q"));
     MG_TRY(need(kh, "k"));
@@ -649,7 +696,20 @@ mg_status mg_attention(mg_device* h, const mg_buffer* qh, const mg_buffer* kh, c
     a.window = p.window_size > 0 ? p.window_size : -1;
     a.query_position_offset = kv_seq_len - seq_len;
     a.scale = scale;
-    return k::attention(d, a);
+    a.step = nullptr;
+    a.kv_rows = kv_rows;
+    *ap = a;
+    return MG_OK;
+}
+}  // namespace mg
+
+extern "C" {
+
+mg_status mg_attention(mg_device* h, const mg_buffer* qh, const mg_buffer* kh, const mg_buffer* vh,
+                       const mg_attention_params* pp, mg_buffer** out) {
+    k::AttentionArgs a;
+    MG_TRY(attention_plan(h, qh, kh, vh, pp, out, &a));
+    return k::attention(dev(h), a);
 }
 
 }  // extern "C"

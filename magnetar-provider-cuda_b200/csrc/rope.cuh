@@ -15,10 +15,12 @@ struct RopeK {
     float yarn_factor, yarn_low, yarn_high, amplitude;
     int half_split;
     int vec;  // 1: 16-byte path (alignment and divisibility checked on the host)
+    const uint64_t* step;  // a captured step's advancing position offset (null: none)
 };
 
 __device__ __forceinline__ float2 rope_cs(const RopeK& p, uint64_t row, uint64_t pair) {
-    float position = (float)(p.position_offset + row) * p.scale;
+    const uint64_t offset = p.position_offset + (p.step ? *p.step : 0);
+    float position = (float)(offset + row) * p.scale;
     float frequency = powf(p.base, -2.0f * (float)pair / (float)p.dimension);
     if (p.banded_factor > 0.0f) {
         float wavelength = 6.283185307179586f / frequency;

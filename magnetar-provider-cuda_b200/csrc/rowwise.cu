@@ -465,6 +465,7 @@ mg_status rope(Device* d, const float* x, float* out, const RopeArgs& a) {
     p.half = a.half;
     p.dimension = a.dimension;
     p.position_offset = a.position_offset;
+    p.step = a.step;
     p.head_count = a.head_count;
     p.head_width = a.cols / a.head_count;
     p.rotated_pairs = a.rotated_pairs;

@@ -318,6 +318,8 @@ mg_status mg_device_open(int ordinal, mg_device** out) {
     if (e == cudaSuccess) e = cudaMalloc(&d->counters, (1u << 16) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(d->counters, 0, (1u << 16) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMallocHost(&d->host_flags, 64);
+    // The step offset shares the status words' allocation (bytes 32..39; the words use 0..15).
+    d->step_offset = reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(d->flags) + 32);
     if (e != cudaSuccess) {
         if (d->flags) cudaFree(d->flags);
         if (d->counters) cudaFree(d->counters);

@@ -187,8 +187,15 @@ class CudaExecutor:
         check(N.lib().mg_executor_synchronize(self._h))
 
     # ---- step capture ---------------------------------------------------------------------
-    def begin_step_capture(self) -> None:
-        check(N.lib().mg_executor_begin_step_capture(self._h))
+    def begin_step_capture(self, advancing: Sequence[str] = ()) -> None:
+        """Records the following invocations into one replayable step.  ``advancing`` names
+        the attributes a replay's offset is added to ("position_offset", "key_count",
+        "row_offset"; the reference's StepCaptureRequest advancing_attributes)."""
+        if not advancing:
+            check(N.lib().mg_executor_begin_step_capture(self._h))
+            return
+        names = (ctypes.c_char_p * len(advancing))(*[a.encode() for a in advancing])
+        check(N.lib().mg_executor_begin_step_capture_advancing(self._h, names, len(advancing)))
 
     def end_step_capture(self) -> None:
         check(N.lib().mg_executor_end_step_capture(self._h))
@@ -196,8 +203,18 @@ class CudaExecutor:
     def abort_step_capture(self) -> None:
         check(N.lib().mg_executor_abort_step_capture(self._h))
 
-    def replay_step(self) -> None:
-        check(N.lib().mg_executor_replay_step(self._h))
+    def replay_step(self, offset: int = 0) -> None:
+        """One replay (with the embedding-id check) at ``offset`` for the advancing attributes."""
+        if offset:
+            check(N.lib().mg_executor_replay_step_at(self._h, int(offset)))
+        else:
+            check(N.lib().mg_executor_replay_step(self._h))
+
+    def step_max_offset(self) -> int:
+        """The largest offset the captured step accepts (2**64 - 1: unbounded)."""
+        v = ctypes.c_uint64()
+        check(N.lib().mg_executor_step_max_offset(self._h, ctypes.byref(v)))
+        return v.value
 
     def replay_steps(self, count: int) -> None:
         """``count`` replays back to back with one embedding-id check for all of them."""

@@ -265,6 +265,11 @@ class CudaKernels:
     def softmax_rows(self, x, out=None):
         return self._run(N.lib().mg_softmax, x.handle, out=out)
 
+    def kv_write(self, store, rows, row_offset):
+        """``kv_write``: ``rows`` over ``store``'s rows ``row_offset..`` in place."""
+        check(N.lib().mg_kv_write(self._h, store.handle, rows.handle, int(row_offset)))
+        return store
+
     def matmul(self, a, b, transpose_a=False, transpose_b=False, out=None):
         return self._run(N.lib().mg_matmul, a.handle, b.handle, int(transpose_a), int(transpose_b), out=out)
 

@@ -332,3 +332,87 @@ def test_capture_keeps_an_embedding_apart_when_it_must(executor, oracle):
     assert executor.kernels.launch_count() - before == 6
     for k in names:
         np.testing.assert_array_equal(executor.read_tensor(k), eager[k], err_msg=k)
+
+
+def test_kv_write_in_place_and_into_a_copy(executor):
+    # src/executor.rs:1366-1420: output == store writes the store in place; another output
+    # id gets a copy of the store with the rows written, the store unchanged.
+    r = np.random.default_rng(7)
+    cache = r.standard_normal((16, 8)).astype(np.float32)
+    new = r.standard_normal((2, 8)).astype(np.float32)
+    executor.write_tensor("cache", cache)
+    executor.write_tensor("new", new)
+    before = executor.buffer("cache").handle.value
+    executor.run(inv("kv-write", ["cache", "new"], "cache", {"row_offset": 5}))
+    exp = cache.copy()
+    exp[5:7] = new
+    np.testing.assert_array_equal(executor.read_tensor("cache"), exp)
+    assert executor.buffer("cache").handle.value == before  # the same device buffer
+    executor.run(inv("kv-write", ["cache", "new"], "copy", {"row_offset": 14}))
+    exp2 = exp.copy()
+    exp2[14:16] = new
+    np.testing.assert_array_equal(executor.read_tensor("copy"), exp2)
+    np.testing.assert_array_equal(executor.read_tensor("cache"), exp)
+    r1 = executor.submit_kernel(inv("kv-write", ["cache", "new"], "cache"))
+    assert not r1.success and r1.error_code == "KernelAttributeUnsupported"
+    r2 = executor.submit_kernel(inv("kv-write", ["cache", "new"], "cache", {"row_offset": 15}))
+    assert not r2.success and r2.error_code == "ShapeUnsupported"
+    np.testing.assert_array_equal(executor.read_tensor("cache"), exp)
+
+
+def test_captured_decode_step_replays_at_advancing_offsets(executor, oracle):
+    # A decode step -- RoPE of the new query and key at the step's position, the new key and
+    # value written into the KV history in place, attention of the one query row over the
+    # history -- captured once with position_offset, row_offset and key_count advancing
+    # (src/kernels.rs:1019-1062, 1343-1349) and replayed at offsets 0, 1, 2, ... with the
+    # step's inputs written into the captured buffers each time.
+    mpc = importlib.import_module("magnetar-provider-cuda_b200")
+    native = importlib.import_module("magnetar-provider-cuda_b200._native")
+    r = np.random.default_rng(8)
+    cap, prefix, heads, kvh, d = 300, 40, 4, 2, 64
+    kc = np.zeros((cap, kvh * d), np.float32)
+    vc = np.zeros((cap, kvh * d), np.float32)
+    kc[:prefix] = r.standard_normal((prefix, kvh * d))
+    vc[:prefix] = r.standard_normal((prefix, kvh * d))
+    executor.write_tensor("kc", kc)
+    executor.write_tensor("vc", vc)
+
+    def step_inputs(t):
+        g = np.random.default_rng(100 + t)
+        return (g.standard_normal((1, heads * d)).astype(np.float32),
+                g.standard_normal((1, kvh * d)).astype(np.float32),
+                g.standard_normal((1, kvh * d)).astype(np.float32))
+
+    q0, k0, v0 = step_inputs(0)
+    for n, x in (("q", q0), ("k", k0), ("v", v0)):
+        executor.write_tensor(n, x)
+    invs = [inv("rope", ["q"], "qr", {"dimension": d, "head_count": heads, "position_offset": prefix}),
+            inv("rope", ["k"], "kr", {"dimension": d, "head_count": kvh, "position_offset": prefix}),
+            inv("kv-write", ["kc", "kr"], "kc", {"row_offset": prefix}),
+            inv("kv-write", ["vc", "v"], "vc", {"row_offset": prefix}),
+            inv("attention", ["qr", "kc", "vc"], "o",
+                {"head_count": heads, "head_dimension": d, "kv_head_count": kvh, "causal": True,
+                 "key_count": prefix + 1})]
+    executor.begin_step_capture(advancing=("position_offset", "row_offset", "key_count"))
+    for i in invs:
+        executor.run(i)
+    executor.end_step_capture()
+    assert executor.step_max_offset() == cap - prefix - 1
+    kc_exp, vc_exp = kc.copy(), vc.copy()
+    for t in range(6):
+        q, k, v = step_inputs(t)
+        for n, x in (("q", q), ("k", k), ("v", v)):
+            native.check(native.lib().mg_buffer_upload(executor.buffer(n).handle, x.ctypes.data, x.nbytes))
+        executor.replay_step(offset=t)
+        pos = prefix + t
+        qr = oracle.rope(q, base=10000.0, dimension=d, head_count=heads, position_offset=pos)
+        kr = oracle.rope(k, base=10000.0, dimension=d, head_count=kvh, position_offset=pos)
+        kc_exp[pos] = kr[0]
+        vc_exp[pos] = v[0]
+        exp = oracle.attention(qr, kc_exp[:pos + 1], vc_exp[:pos + 1], heads, d, kv_head_count=kvh, causal=True)
+        assert rel(executor.read_tensor("o"), exp) <= 1e-4, t
+    assert rel(executor.read_tensor("kc"), kc_exp) <= 1e-5
+    np.testing.assert_array_equal(executor.read_tensor("vc"), vc_exp)
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_step(offset=cap - prefix)  # would write past the history
+    assert e.value.code == "CaptureUnsupported"

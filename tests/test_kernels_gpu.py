@@ -383,6 +383,18 @@ ATTN_CASES = [
     dict(seq=16, kv=384, heads=2, kvh=2, d=64, causal=True),
     dict(seq=100, kv=100, heads=2, kvh=2, d=32, causal=True),
     dict(seq=129, kv=129, heads=2, kvh=2, d=128, causal=False),
+    # one query row (decode): keys split across CTAs in chunks of 128 -- one chunk, a ragged
+    # last chunk, many chunks with GQA, a window, a key count, non-causal, D = 256, Dv != D,
+    # a head dimension that is no multiple of 4
+    dict(seq=1, kv=1, heads=2, kvh=2, d=64, causal=True),
+    dict(seq=1, kv=129, heads=4, kvh=4, d=128, causal=True),
+    dict(seq=1, kv=4096, heads=32, kvh=8, d=128, causal=True),
+    dict(seq=1, kv=1000, heads=4, kvh=2, d=64, causal=True, window=300),
+    dict(seq=1, kv=1000, heads=4, kvh=2, d=64, causal=True, key_count=513),
+    dict(seq=1, kv=700, heads=2, kvh=2, d=64, causal=False),
+    dict(seq=1, kv=300, heads=2, kvh=1, d=256, causal=True),
+    dict(seq=1, kv=300, heads=2, kvh=2, d=64, causal=True, vd=96),
+    dict(seq=1, kv=200, heads=3, kvh=3, d=30, causal=True),
 ]
 
 
@@ -399,6 +411,32 @@ def test_attention(kernels, oracle, c):
                                              c["heads"], c["d"], **kw))
     exp = oracle.attention(q, k, v, c["heads"], c["d"], **kw)
     assert rel(got, exp) <= TOL_MATMUL
+
+
+def test_kv_write(kernels, mpc):
+    # src/kernels.rs:2278-2325: rows over the store's rows row_offset.. in place, the rest kept
+    r = rng(17)
+    store = r.standard_normal((64, 96)).astype(np.float32)
+    rows = r.standard_normal((5, 96)).astype(np.float32)
+    ds = kernels.upload(store)
+    kernels.kv_write(ds, kernels.upload(rows), 40)
+    exp = store.copy()
+    exp[40:45] = rows
+    np.testing.assert_array_equal(kernels.download(ds), exp)
+    kernels.kv_write(ds, kernels.upload(rows[:1]), 63)  # the last row
+    exp[63] = rows[0]
+    np.testing.assert_array_equal(kernels.download(ds), exp)
+    odd = r.standard_normal((3, 7)).astype(np.float32)  # unvectorised width
+    do = kernels.upload(np.zeros((9, 7), np.float32))
+    kernels.kv_write(do, kernels.upload(odd), 2)
+    np.testing.assert_array_equal(kernels.download(do)[2:5], odd)
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.kv_write(ds, kernels.upload(rows), 60)  # past the store's rows
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.kv_write(ds, kernels.upload(np.zeros((2, 95), np.float32)), 0)
+    assert e.value.code == "ShapeUnsupported"
+    np.testing.assert_array_equal(kernels.download(ds), exp)  # failed writes changed nothing
 
 
 def test_attention_large_values_stay_finite(kernels):
