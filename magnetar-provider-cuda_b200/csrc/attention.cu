@@ -14,7 +14,13 @@
 // merge rescales by l_old * alpha / l_new and adds p_j / l_new times v_j), so it never
 // exceeds the largest |v| -- the reference's overflow-safety invariant for large finite V
 // (src/tests_conformance.rs:884-914).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace mg {
 namespace {
@@ -395,6 +401,7 @@ struct DecodeP {
     float scale;
     const uint64_t* step;
     int vec;  // K rows 16-byte aligned: float4 loads
+    int* error;
 };
 
 // Max (or sum) over the CTA's 128 threads of each of G values, one pair of barriers for all.
@@ -517,6 +524,279 @@ __global__ void __launch_bounds__(kDecodeKeys) attention_decode_kernel(DecodeP p
         }
 }
 
+// The TMA form (16-byte aligned rows, head dimensions multiples of 4): a CTA of 256 threads
+// takes a span of keys of one KV head (about three CTAs per SM over the grid) and its G query
+// heads, and streams the span in tiles of 32 keys through a 2-stage ring of TMA copies ([32][D]
+// of K and [32][Dv] of V per stage).  Each warp takes 4 keys of every tile and keeps its own
+// online softmax (running max, sum and unnormalised output) over them: scores with 8 lanes per
+// key (16-byte column chunks, a 3-level butterfly per head), max and sum by shuffles inside the
+// warp, P.V with each lane owning output columns 4 lane .. 4 lane + 3 (and + 128) read as
+// 16-byte loads of the V rows -- no CTA-wide barrier per tile but the one that frees a stage.
+// The warps' states are merged once, in warp order, into the span's partial (max, sum,
+// output) for the combine kernel.
+constexpr int kDecodeThreads = 256;
+constexpr int kDecodeStages = 2;
+constexpr int kDecodeTileKeys = 32;  // 4 keys per warp
+constexpr int kDecodeStageBytes = kDecodeTileKeys * 2 * kDecodeMaxDim * 4;  // 64 KB at D = Dv = 256
+
+template <int G, int C>  // C: 128-column chunks of the output (Dv <= 128 * C)
+__global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(const __grid_constant__ CUtensorMap map_k,
+                                                                             const __grid_constant__ CUtensorMap map_v,
+                                                                             DecodeP p, uint64_t span) {
+    using namespace sm100;
+    constexpr int kc = kDecodeTileKeys;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(16) float qs[G][kDecodeMaxDim];
+    __shared__ float wm[8][G], wl[8][G];
+    __shared__ uint64_t bars[kDecodeStages];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 127u) & ~127u;
+    float* smem_f = reinterpret_cast<float*>(smem_raw + (base - raw));
+    const uint64_t h0 = G == 1 ? blockIdx.y : (uint64_t)blockIdx.y * G;
+    const uint64_t kvh = G == 1 ? blockIdx.y / p.group : blockIdx.y;
+    const uint64_t c = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t D = p.head_dim, DV = p.value_dim;
+    const uint32_t k_bytes = (uint32_t)(4 * kc * D);
+    const uint32_t stage_bytes = (uint32_t)(4 * kc * (D + DV));
+    pdl_enter();  // K and V may have just been written (kv-write)
+    const uint64_t n_keys = p.kv_seq_len + (p.step ? *p.step : 0);
+    const uint64_t qpos = n_keys - 1;
+    uint64_t lo = 0;
+    if (p.window >= 0) {
+        const uint64_t back = (uint64_t)p.window - 1;
+        lo = qpos > back ? qpos - back : 0;
+    }
+    // This CTA's tiles: from the span's start (or the first tile holding `lo`) to its admitted end.
+    const uint64_t k_begin = c * span, k_end = min(k_begin + span, n_keys);
+    const uint64_t first = lo > k_begin ? k_begin + (lo - k_begin) / kc * kc : k_begin;
+    const int tiles = k_end > first ? (int)((k_end - first + kc - 1) / kc) : 0;
+    const uint64_t pstride = p.chunks * (DV + 2);
+    float* part0 = p.partial + (h0 * p.chunks + c) * (DV + 2);
+    const float kNegInf = __int_as_float(0xff800000);
+    if (tiles == 0) {  // no admitted key here: an empty partial, no copies
+        if (threadIdx.x == 0)
+            for (int g = 0; g < G; g++) {
+                part0[g * pstride] = kNegInf;
+                part0[g * pstride + 1] = 0.0f;
+            }
+        return;
+    }
+    auto issue = [&](int t) {
+        const int st = t % kDecodeStages;
+        const uint32_t dst = base + (uint32_t)st * stage_bytes;
+        const int key = (int)(first + (uint64_t)t * kc);
+        mbar_arrive_expect_tx(smem_u32(&bars[st]), stage_bytes);
+        tma_load_2d(dst, &map_k, smem_u32(&bars[st]), (int)(kvh * D), key);
+        tma_load_2d(dst + k_bytes, &map_v, smem_u32(&bars[st]), (int)(kvh * DV), key);
+    };
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kDecodeStages; st++) mbar_init(smem_u32(&bars[st]), 1);
+        fence_barrier_init();
+        for (int t = 0; t < min(tiles, kDecodeStages); t++) issue(t);
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        for (uint64_t d = threadIdx.x; d < D; d += kDecodeThreads) qs[g][d] = p.q[(h0 + g) * D + d];
+    __syncthreads();  // the barriers' initialisation and q are visible
+    const int sk = lane >> 3, sc4 = (lane & 7) * 4;  // scores: key sk of the warp's 4, columns sc4 + 32 i
+    // P.V: this lane's output columns 4 lane + 128 i + e, slot i * 4 + e
+    float m[G], l[G], acc[G][4 * C];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = kNegInf;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4 * C; e++) acc[g][e] = 0.0f;
+    }
+    bool ok = true;
+    for (int t = 0; t < tiles; t++) {
+        const int st = t % kDecodeStages;
+        if (!mbar_wait(smem_u32(&bars[st]), (uint32_t)(t / kDecodeStages) & 1u)) ok = false;
+        if (__syncthreads_or(!ok)) {
+            ok = false;
+            if (threadIdx.x == 0) atomicExch(p.error, 1);
+            break;
+        }
+        const float* ks = smem_f + (uint64_t)st * (stage_bytes / 4);
+        const float* vs = ks + (uint64_t)kc * D;
+        const int jb = warp * 4, j = jb + sk;
+        float sc[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) sc[g] = 0.0f;
+        for (uint64_t d = sc4; d < D; d += 32) {
+            const float4 kv = *reinterpret_cast<const float4*>(ks + (uint64_t)j * D + d);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float4 qv = *reinterpret_cast<const float4*>(&qs[g][d]);
+                sc[g] += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+            }
+        }
+        const uint64_t key = first + (uint64_t)t * kc + j;
+        const bool live = key >= lo && key < k_end;
+        float pk[G][4];  // the weights of the warp's 4 keys, the same in every lane
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            for (int o = 4; o > 0; o >>= 1) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+            sc[g] = live ? sc[g] * p.scale : kNegInf;
+            float tmx = fmaxf(sc[g], __shfl_xor_sync(0xffffffffu, sc[g], 8));
+            tmx = fmaxf(tmx, __shfl_xor_sync(0xffffffffu, tmx, 16));
+            const float m_new = fmaxf(m[g], tmx);
+            float ex = 0.0f, alpha = 1.0f;
+            if (m_new != kNegInf) {  // some key admitted so far
+                alpha = m[g] == kNegInf ? 0.0f : expf(m[g] - m_new);
+                m[g] = m_new;
+                ex = sc[g] != kNegInf ? expf(sc[g] - m_new) : 0.0f;
+            }
+            float es = ex + __shfl_xor_sync(0xffffffffu, ex, 8);
+            es += __shfl_xor_sync(0xffffffffu, es, 16);
+            l[g] = l[g] * alpha + es;
+#pragma unroll
+            for (int k = 0; k < 4; k++) pk[g][k] = __shfl_sync(0xffffffffu, ex, k * 8);
+#pragma unroll
+            for (int e = 0; e < 4 * C; e++) acc[g][e] *= alpha;
+        }
+#pragma unroll
+        for (int i = 0; i < C; i++) {
+            const uint64_t d = 4 * (uint64_t)lane + 128 * (uint64_t)i;
+            if (d >= DV) break;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float4 vv = *reinterpret_cast<const float4*>(vs + (uint64_t)(jb + k) * DV + d);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    acc[g][i * 4 + 0] += pk[g][k] * vv.x;
+                    acc[g][i * 4 + 1] += pk[g][k] * vv.y;
+                    acc[g][i * 4 + 2] += pk[g][k] * vv.z;
+                    acc[g][i * 4 + 3] += pk[g][k] * vv.w;
+                }
+            }
+        }
+        __syncthreads();  // every warp is done with this stage
+        if (threadIdx.x == 0 && t + kDecodeStages < tiles) issue(t + kDecodeStages);
+    }
+    if (!ok) {  // give the copies in flight a second bound before the CTA exits
+        if (threadIdx.x == 0)
+            for (int st = 0; st < min(tiles, kDecodeStages); st++) (void)mbar_wait(smem_u32(&bars[st]), 0);
+        __syncthreads();
+        return;
+    }
+    // ---- merge the 8 warps' states (in warp order) into the span's partial -------------------
+    if (lane == 0)
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+    __syncthreads();
+    float* wo = smem_f;  // [8][G][DV], the drained ring
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        float mx = kNegInf;
+        for (int w = 0; w < 8; w++) mx = fmaxf(mx, wm[w][g]);
+        const float sc = m[g] == kNegInf ? 0.0f : expf(m[g] - mx);
+#pragma unroll
+        for (int i = 0; i < C; i++) {
+            const uint64_t d = 4 * (uint64_t)lane + 128 * (uint64_t)i;
+            if (d >= DV) break;
+            *reinterpret_cast<float4*>(wo + ((uint64_t)warp * G + g) * DV + d) =
+                make_float4(acc[g][i * 4] * sc, acc[g][i * 4 + 1] * sc, acc[g][i * 4 + 2] * sc, acc[g][i * 4 + 3] * sc);
+        }
+    }
+    __syncthreads();
+    for (uint64_t e = threadIdx.x; e < (uint64_t)G * DV; e += kDecodeThreads) {
+        const uint64_t g = e / DV, d = e % DV;
+        float o = 0.0f;
+        for (int w = 0; w < 8; w++) o += wo[((uint64_t)w * G + g) * DV + d];
+        part0[g * pstride + 2 + d] = o;
+    }
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float mx = kNegInf;
+        for (int w = 0; w < 8; w++) mx = fmaxf(mx, wm[w][g]);
+        float ls = 0.0f;
+        for (int w = 0; w < 8; w++)
+            if (wm[w][g] != kNegInf) ls += wl[w][g] * expf(wm[w][g] - mx);
+        part0[g * pstride] = mx;
+        part0[g * pstride + 1] = ls;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 decode_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// Row-major [rows, cols] f32, box [box_rows, box_cols], no swizzle; rows past the end read as zero.
+mg_status decode_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                     uint32_t box_rows) {
+    auto fn = decode_encode_fn();
+    if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * sizeof(float)};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
+inline int decode_tma_smem(int g, uint64_t d, uint64_t dv) {
+    const uint64_t ring = (uint64_t)kDecodeStages * kDecodeTileKeys * 4 * (d + dv);
+    const uint64_t merge = 8ull * g * 4 * dv;  // the warps' outputs, in the drained ring
+    return 128 + (int)(ring > merge ? ring : merge);
+}
+
+// Resident CTAs per SM of the G-head form at this shared-memory size (queried once per size).
+template <int G, int C>
+int decode_tma_occupancy(Device* d, int smem) {
+    static int cached[64][4] = {{0}};
+    static int cached_smem[64][4] = {{0}};
+    const int slot = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+    int& c = cached[d->ordinal & 63][slot];
+    if (c == 0 || cached_smem[d->ordinal & 63][slot] != smem) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attention_decode_tma_kernel<G, C>, kDecodeThreads, smem) !=
+                cudaSuccess ||
+            n < 1) {
+            (void)cudaGetLastError();
+            n = 1;
+        }
+        c = n;
+        cached_smem[d->ordinal & 63][slot] = smem;
+    }
+    return c;
+}
+
+template <int G, int C>
+mg_status launch_decode_tma(Device* d, const DecodeP& p, const CUtensorMap* maps, uint64_t span, dim3 grid) {
+    const int smem = decode_tma_smem(G, p.head_dim, p.value_dim);
+    enqueue(d, attention_decode_tma_kernel<G, C>, grid, kDecodeThreads, (size_t)smem, maps[0], maps[1], p, span);
+    return launched(d, "decode attention launch");
+}
+
+template <int G, int C>
+mg_status configure_decode_tma(Device* d) {
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(attention_decode_tma_kernel<G, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     128 + kDecodeStages * kDecodeStageBytes),
+                "configuring the decode attention kernel");
+        configured[d->ordinal & 63] = true;
+    }
+    return MG_OK;
+}
+
 __global__ void __launch_bounds__(kDecodeKeys) attention_combine_kernel(DecodeP p) {
     pdl_enter();
     const uint64_t h = blockIdx.x;
@@ -558,11 +838,60 @@ mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
     p.scale = a.scale;
     p.step = a.step;
     p.vec = (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 && a.kv_model_dim % 4 == 0 && a.head_dim % 4 == 0;
+    p.error = d->flags + 2;
     const uint64_t keys = a.step ? a.kv_rows : a.kv_seq_len;  // the grid covers what may be admitted
-    p.chunks = std::max<uint64_t>(1, (keys + kDecodeKeys - 1) / kDecodeKeys);
+    auto al16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
+    const bool tma = al16(a.k) && al16(a.v) && a.head_dim % 4 == 0 && a.value_dim % 4 == 0 &&
+                     a.kv_model_dim % 4 == 0 && a.v_model_dim % 4 == 0 && a.kv_rows < (1ull << 31) &&
+                     a.kv_model_dim < (1ull << 31) && a.v_model_dim < (1ull << 31);
+    const int kc = tma ? kDecodeTileKeys : kDecodeKeys;
+    // TMA form: spans of whole tiles, one wave of CTAs (as many per SM as fit).
+    uint64_t span = (uint64_t)kc;
+    if (tma) {
+        const int G = (p.group == 2 || p.group == 4 || p.group == 8) ? (int)p.group : 1;
+        const int smem = decode_tma_smem(G, a.head_dim, a.value_dim);
+        int per_sm = 1;
+        const bool wide = a.value_dim > 128;
+#define MG_DECODE_OCC(GG)                                                              \
+    if (wide) {                                                                        \
+        MG_TRY((configure_decode_tma<GG, 2>(d)));                                      \
+        per_sm = decode_tma_occupancy<GG, 2>(d, smem);                                 \
+    } else {                                                                           \
+        MG_TRY((configure_decode_tma<GG, 1>(d)));                                      \
+        per_sm = decode_tma_occupancy<GG, 1>(d, smem);                                 \
+    }
+        switch (G) {
+            case 2: MG_DECODE_OCC(2) break;
+            case 4: MG_DECODE_OCC(4) break;
+            case 8: MG_DECODE_OCC(8) break;
+            default: MG_DECODE_OCC(1) break;
+        }
+#undef MG_DECODE_OCC
+        const uint64_t sets = G == 1 ? a.head_count : a.kv_head_count;  // CTAs per span of keys
+        const uint64_t want = std::max<uint64_t>(1, (uint64_t)per_sm * d->sm_count / std::max<uint64_t>(1, sets));
+        span = std::max<uint64_t>(1, (keys + want - 1) / want);
+        span = (span + kc - 1) / kc * kc;
+    }
+    p.chunks = std::max<uint64_t>(1, (keys + span - 1) / span);
     if (p.chunks > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the decode grid");
     MG_TRY(scratch(d, 6, a.head_count * p.chunks * (a.value_dim + 2) * sizeof(float), (void**)&p.partial));
     const dim3 by_kv((unsigned)p.chunks, (unsigned)a.kv_head_count), by_q((unsigned)p.chunks, (unsigned)a.head_count);
+    if (tma) {
+        CUtensorMap maps[2];
+        MG_TRY(decode_map(&maps[0], a.k, a.kv_rows, a.kv_model_dim, (uint32_t)a.head_dim, (uint32_t)kc));
+        MG_TRY(decode_map(&maps[1], a.v, a.kv_rows, a.v_model_dim, (uint32_t)a.value_dim, (uint32_t)kc));
+        const bool wide = a.value_dim > 128;
+        mg_status ls = MG_OK;
+        switch (p.group) {
+            case 2: ls = wide ? launch_decode_tma<2, 2>(d, p, maps, span, by_kv) : launch_decode_tma<2, 1>(d, p, maps, span, by_kv); break;
+            case 4: ls = wide ? launch_decode_tma<4, 2>(d, p, maps, span, by_kv) : launch_decode_tma<4, 1>(d, p, maps, span, by_kv); break;
+            case 8: ls = wide ? launch_decode_tma<8, 2>(d, p, maps, span, by_kv) : launch_decode_tma<8, 1>(d, p, maps, span, by_kv); break;
+            default: ls = wide ? launch_decode_tma<1, 2>(d, p, maps, span, by_q) : launch_decode_tma<1, 1>(d, p, maps, span, by_q); break;
+        }
+        MG_TRY(ls);
+        enqueue(d, attention_combine_kernel, dim3((unsigned)a.head_count), kDecodeKeys, 0, p);
+        return launched(d, "decode attention combine launch");
+    }
     switch (p.group) {
         case 2: enqueue(d, attention_decode_kernel<2>, by_kv, kDecodeKeys, 0, p); break;
         case 4: enqueue(d, attention_decode_kernel<4>, by_kv, kDecodeKeys, 0, p); break;
