@@ -156,6 +156,25 @@ mg_status mg_scale(mg_device* d, const mg_buffer* x, float factor, mg_buffer** o
 mg_status mg_silu(mg_device* d, const mg_buffer* x, mg_buffer** out);
 /* silu(gate) * up (src/kernels.rs:4492-4523) */
 mg_status mg_silu_mul(mg_device* d, const mg_buffer* gate, const mg_buffer* up, mg_buffer** out);
+/* gelu, tanh approximation (src/kernels.rs:3167-3170, kernels.cu:80-92) */
+mg_status mg_gelu_tanh(mg_device* d, const mg_buffer* x, mg_buffer** out);
+/* activation kind sigmoid: 1 / (1 + exp(-x)) (src/kernels.rs:3121-3125) */
+mg_status mg_sigmoid(mg_device* d, const mg_buffer* x, mg_buffer** out);
+/* activation kind softcap: cap * tanh(x / cap); cap finite and positive (src/kernels.rs:3211-3224) */
+mg_status mg_softcap(mg_device* d, const mg_buffer* x, float cap, mg_buffer** out);
+/* row-scale: out[t, :] = x[t, :] * scale[t], x rank-2, scale [T] or [T, 1] (src/kernels.rs:3255-3290) */
+mg_status mg_row_scale(mg_device* d, const mg_buffer* x, const mg_buffer* scale, mg_buffer** out);
+/* concat along the first dimension; trailing dimensions must agree (src/kernels.rs:3058-3100) */
+mg_status mg_concat(mg_device* d, const mg_buffer* a, const mg_buffer* b, mg_buffer** out);
+/* concat across heads: row r = for each head h, a's head h then b's head h (second_head_count ==
+ * head_count) or b's only head (second_head_count == 1) (src/kernels.rs:7084-7130) */
+mg_status mg_concat_heads(mg_device* d, const mg_buffer* a, const mg_buffer* b, uint64_t head_count,
+                          uint64_t second_head_count, mg_buffer** out);
+/* batched-matmul: out [rows, groups * n], group g of row r = a[r, g k .. (g + 1) k] times
+ * b[g k .. (g + 1) k, :] or, with transpose_b, times b[g n .. (g + 1) n, :] transposed
+ * (src/kernels.rs:5882-5950) */
+mg_status mg_batched_matmul(mg_device* d, const mg_buffer* a, const mg_buffer* b, uint64_t groups, int transpose_b,
+                            mg_buffer** out);
 /* Half-precision add/mul on f16 or bf16 buffers, bit-exact with the reference's integer
  * decode -> f32 op -> RNE encode (src/kernels.rs:2227-2266, src/kernels.cu:2806-2939).
  * Both inputs must share shape and dtype. */

@@ -134,6 +134,13 @@ SIGNATURES = {
     "mg_rope": [_P, _P, ctypes.POINTER(RopeParams), _PP],
     "mg_softmax": [_P, _P, _PP],
     "mg_kv_write": [_P, _P, _P, _U64],
+    "mg_gelu_tanh": [_P, _P, _PP],
+    "mg_sigmoid": [_P, _P, _PP],
+    "mg_softcap": [_P, _P, _F, _PP],
+    "mg_row_scale": [_P, _P, _P, _PP],
+    "mg_concat": [_P, _P, _P, _PP],
+    "mg_concat_heads": [_P, _P, _P, _U64, _U64, _PP],
+    "mg_batched_matmul": [_P, _P, _P, _U64, _I, _PP],
     "mg_matmul": [_P, _P, _P, _I, _I, _PP],
     "mg_matmul_bias": [_P, _P, _P, _P, _I, _I, _PP],
     "mg_matmul_residual": [_P, _P, _P, _P, _I, _I, _PP],

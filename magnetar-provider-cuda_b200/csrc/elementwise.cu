@@ -45,6 +45,22 @@ struct ScaleOp {
     float f;
     __device__ float operator()(float v) const { return v * f; }
 };
+// The tanh form of GELU in the reference's order of operations (src/kernels.cu:80-86):
+// 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), sqrt(2 / pi) as the f32 0.7978846.
+struct GeluTanhOp {
+    __device__ float operator()(float x) const {
+        return 0.5f * x * (1.0f + tanhf(0.7978846f * (x + 0.044715f * x * x * x)));
+    }
+};
+// src/kernels.cu:1079-1084: 1 / (1 + exp(-x))
+struct SigmoidOp {
+    __device__ float operator()(float x) const { return 1.0f / (1.0f + expf(-x)); }
+};
+// src/kernels.cu:103-109: cap * tanh(x / cap)
+struct SoftcapOp {
+    float cap;
+    __device__ float operator()(float x) const { return cap * tanhf(x / cap); }
+};
 
 template <class Op>
 __device__ inline float4 apply2(Op op, float4 a, float4 b) {
@@ -330,6 +346,93 @@ __global__ void __launch_bounds__(kThreads) kv_write_kernel(const float* __restr
     for (uint64_t i = t0; i < n; i += stride) dst[i] = rows[i];
 }
 
+// row-scale (src/kernels.cu:1066-1077): out[r][c] = x[r][c] * scale[r].
+__global__ void __launch_bounds__(kThreads) row_scale_kernel(const float* __restrict__ x, const float* __restrict__ scale,
+                                                             float* __restrict__ out, uint64_t rows, uint64_t cols,
+                                                             int vec) {
+    pdl_enter();
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {  // cols % 4 == 0
+        const uint64_t c4 = cols >> 2, n4 = rows * c4;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        float4* o4 = reinterpret_cast<float4*>(out);
+        for (uint64_t i = tid; i < n4; i += stride) {
+            const float s = scale[i / c4];
+            const float4 v = x4[i];
+            o4[i] = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+        }
+        return;
+    }
+    for (uint64_t i = tid; i < rows * cols; i += stride) out[i] = x[i] * scale[i / cols];
+}
+
+// concat across heads (src/kernels.cu:5786-5812): output row r holds `heads` heads, head h being
+// a's head h (a_width values) then b's head h -- or b's only head when b_heads == 1.  `vec`:
+// both widths multiples of 4 and the buffers 16-byte aligned (16-byte copies).
+__global__ void __launch_bounds__(kThreads) concat_heads_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                                                float* __restrict__ out, uint64_t rows, uint64_t heads,
+                                                                uint64_t a_width, uint64_t b_width, uint64_t b_heads,
+                                                                int vec) {
+    pdl_enter();
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t q = vec ? 4 : 1;  // elements per item
+    const uint64_t width = (a_width + b_width) / q, aw = a_width / q, bw = b_width / q;
+    const uint64_t items = rows * heads * width;
+    for (uint64_t i = tid; i < items; i += stride) {
+        const uint64_t rh = i / width, j = i % width;  // rh = row * heads + head
+        const uint64_t row = rh / heads, head = rh % heads;
+        if (vec) {
+            reinterpret_cast<float4*>(out)[i] =
+                j < aw ? reinterpret_cast<const float4*>(a)[rh * aw + j]
+                       : reinterpret_cast<const float4*>(b)[(row * b_heads + (b_heads == 1 ? 0 : head)) * bw + (j - aw)];
+        } else {
+            out[i] = j < aw ? a[rh * aw + j] : b[(row * b_heads + (b_heads == 1 ? 0 : head)) * bw + (j - aw)];
+        }
+    }
+}
+
+// batched-matmul (src/kernels.cu:6296-6365): out [rows, groups * n], group g of row r being
+// a[r, g k .. (g + 1) k] times b[g k .. (g + 1) k, :], or with transpose_b times
+// b[g n .. (g + 1) n, :] transposed.  Sums in index order: a thread per output (consecutive
+// threads read consecutive columns of b) without the transpose; with it, a warp per output
+// whose lanes take every 32nd index and add their sums with a butterfly.
+__global__ void __launch_bounds__(kThreads) batched_matmul_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                                                  float* __restrict__ out, uint64_t rows,
+                                                                  uint64_t groups, uint64_t k, uint64_t n) {
+    pdl_enter();
+    const uint64_t width = groups * n, total = rows * width;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        const uint64_t r = idx / width, col = idx % width, g = col / n, j = col % n;
+        const float* in = a + r * groups * k + g * k;
+        const float* w = b + g * k * n + j;
+        float sum = 0.0f;
+        for (uint64_t i = 0; i < k; i++) sum += in[i] * w[i * n];
+        out[idx] = sum;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) batched_matmul_t_kernel(const float* __restrict__ a,
+                                                                    const float* __restrict__ b,
+                                                                    float* __restrict__ out, uint64_t rows,
+                                                                    uint64_t groups, uint64_t k, uint64_t n) {
+    pdl_enter();
+    const uint64_t width = groups * n, total = rows * width;
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (kThreads / 32);
+    for (uint64_t idx = (uint64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); idx < total; idx += warps) {
+        const uint64_t r = idx / width, col = idx % width, g = col / n, j = col % n;
+        const float* in = a + r * groups * k + g * k;
+        const float* w = b + (g * n + j) * k;
+        float sum = 0.0f;
+        for (uint64_t i = lane; i < k; i += 32) sum += in[i] * w[i];
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) out[idx] = sum;
+    }
+}
+
 __global__ void set_u64_kernel(uint64_t* dst, uint64_t value) {
     pdl_enter();
     *dst = value;
@@ -378,6 +481,51 @@ mg_status scale(Device* d, const float* x, float* out, float factor, uint64_t n)
     int vec = aligned16(x) && aligned16(out);
     enqueue(d, unary_kernel<ScaleOp>, vec_grid(d, n, vec, 4), kThreads, 0, x, out, n, vec, ScaleOp{factor});
     return launched(d, "scale kernel launch");
+}
+
+mg_status gelu_tanh(Device* d, const float* x, float* out, uint64_t n) {
+    int vec = aligned16(x) && aligned16(out);
+    enqueue(d, unary_kernel<GeluTanhOp>, vec_grid(d, n, vec, 4), kThreads, 0, x, out, n, vec, GeluTanhOp{});
+    return launched(d, "gelu kernel launch");
+}
+
+mg_status sigmoid(Device* d, const float* x, float* out, uint64_t n) {
+    int vec = aligned16(x) && aligned16(out);
+    enqueue(d, unary_kernel<SigmoidOp>, vec_grid(d, n, vec, 4), kThreads, 0, x, out, n, vec, SigmoidOp{});
+    return launched(d, "sigmoid kernel launch");
+}
+
+mg_status softcap(Device* d, const float* x, float* out, float cap, uint64_t n) {
+    int vec = aligned16(x) && aligned16(out);
+    enqueue(d, unary_kernel<SoftcapOp>, vec_grid(d, n, vec, 4), kThreads, 0, x, out, n, vec, SoftcapOp{cap});
+    return launched(d, "softcap kernel launch");
+}
+
+mg_status row_scale(Device* d, const float* x, const float* scale, float* out, uint64_t rows, uint64_t cols) {
+    const int vec = cols % 4 == 0 && aligned16(x) && aligned16(out);
+    enqueue(d, row_scale_kernel, grid_for(d, vec ? rows * cols / 4 : rows * cols), kThreads, 0, x, scale, out, rows, cols,
+            vec);
+    return launched(d, "row-scale kernel launch");
+}
+
+mg_status concat_heads(Device* d, const float* a, const float* b, float* out, uint64_t rows, uint64_t heads,
+                       uint64_t a_width, uint64_t b_width, uint64_t b_heads) {
+    const int vec = a_width % 4 == 0 && b_width % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out);
+    const uint64_t items = rows * heads * (a_width + b_width) / (vec ? 4 : 1);
+    enqueue(d, concat_heads_kernel, grid_for(d, items), kThreads, 0, a, b, out, rows, heads, a_width, b_width, b_heads,
+            vec);
+    return launched(d, "concat kernel launch");
+}
+
+mg_status batched_matmul(Device* d, const float* a, const float* b, float* out, uint64_t rows, uint64_t groups,
+                         uint64_t k, uint64_t n, int transpose_b) {
+    const uint64_t total = rows * groups * n;
+    if (total == 0) return MG_OK;
+    if (transpose_b)
+        enqueue(d, batched_matmul_t_kernel, grid_for(d, total * 32), kThreads, 0, a, b, out, rows, groups, k, n);
+    else
+        enqueue(d, batched_matmul_kernel, grid_for(d, total), kThreads, 0, a, b, out, rows, groups, k, n);
+    return launched(d, "batched-matmul kernel launch");
 }
 
 mg_status bias_add(Device* d, const float* a, const float* bias, float* out, uint64_t cols, uint64_t n) {

@@ -394,6 +394,44 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
         MG_TRY(get_input(ex, inv, 0, &a));
         return mg_silu(dh, H(a), out);
     }
+    if (!strcmp(name, "gelu")) {
+        // src/executor.rs:1817-1828: the tanh approximation, the only one implemented
+        MG_TRY(get_input(ex, inv, 0, &a));
+        const mg_attribute* ap = at.find("approximate");
+        if (ap && !(ap->kind == MG_ATTR_STRING && ap->string_value && !strcmp(ap->string_value, "tanh")))
+            return fail(MG_ATTRIBUTE_UNSUPPORTED, "gelu approximate %s is not implemented",
+                        ap->kind == MG_ATTR_STRING && ap->string_value ? ap->string_value : "(not a string)");
+        return mg_gelu_tanh(dh, H(a), out);
+    }
+    if (!strcmp(name, "row-scale")) {
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        return mg_row_scale(dh, H(a), H(b), out);
+    }
+    if (!strcmp(name, "concat")) {
+        // src/executor.rs:1933-1965: along the rows, or head by head (axis "heads"); a missing
+        // axis concatenates rows
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        const mg_attribute* ax = at.find("axis");
+        const char* axis = ax && ax->kind == MG_ATTR_STRING ? ax->string_value : nullptr;
+        if (!ax || (axis && !strcmp(axis, "rows"))) return mg_concat(dh, H(a), H(b), out);
+        if (axis && !strcmp(axis, "heads")) {
+            uint64_t hc = 0, shc = 0;
+            if (!at.integer("head_count", &hc)) return fail(MG_ATTRIBUTE_UNSUPPORTED, "head_count");
+            if (!at.integer("second_head_count", &shc)) shc = hc;
+            return mg_concat_heads(dh, H(a), H(b), hc, shc, out);
+        }
+        return fail(MG_ATTRIBUTE_UNSUPPORTED, "concat axis must be 'rows' or 'heads'");
+    }
+    if (!strcmp(name, "batched-matmul")) {
+        // src/executor.rs:1798-1808
+        MG_TRY(get_input(ex, inv, 0, &a));
+        MG_TRY(get_input(ex, inv, 1, &b));
+        uint64_t groups = 0;
+        if (!at.integer("group_count", &groups) || groups == 0) return fail(MG_ATTRIBUTE_UNSUPPORTED, "group_count");
+        return mg_batched_matmul(dh, H(a), H(b), groups, at.boolean("transpose_b", false), out);
+    }
     if (!strcmp(name, "activation")) {
         MG_TRY(get_input(ex, inv, 0, &a));
         const char* kind = at.string("kind");
@@ -404,6 +442,15 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
             MG_TRY(at.flt_opt("factor", &present, &f));
             if (!present) return fail(MG_ATTRIBUTE_UNSUPPORTED, "scale needs a factor");
             return mg_scale(dh, H(a), f, out);
+        }
+        // src/executor.rs:1829-1860
+        if (kind && !strcmp(kind, "sigmoid")) return mg_sigmoid(dh, H(a), out);
+        if (kind && !strcmp(kind, "softcap")) {
+            bool present;
+            float cap = 0.0f;
+            MG_TRY(at.flt_opt("cap", &present, &cap));
+            if (!present) return fail(MG_ATTRIBUTE_UNSUPPORTED, "softcap needs a cap");
+            return mg_softcap(dh, H(a), cap, out);
         }
         return fail(MG_ATTRIBUTE_UNSUPPORTED, "activation kind %s is not implemented", kind ? kind : "(none)");
     }

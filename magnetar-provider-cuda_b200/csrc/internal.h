@@ -137,6 +137,14 @@ mg_status mul(Device* d, const float* a, const float* b, float* out, uint64_t n)
 mg_status mul_scalar(Device* d, const float* a, const float* b, float* out, uint64_t n);
 mg_status scale(Device* d, const float* x, float* out, float factor, uint64_t n);
 mg_status silu(Device* d, const float* x, float* out, uint64_t n);
+mg_status gelu_tanh(Device* d, const float* x, float* out, uint64_t n);
+mg_status sigmoid(Device* d, const float* x, float* out, uint64_t n);
+mg_status softcap(Device* d, const float* x, float* out, float cap, uint64_t n);
+mg_status row_scale(Device* d, const float* x, const float* scale, float* out, uint64_t rows, uint64_t cols);
+mg_status concat_heads(Device* d, const float* a, const float* b, float* out, uint64_t rows, uint64_t heads,
+                       uint64_t a_width, uint64_t b_width, uint64_t b_heads);
+mg_status batched_matmul(Device* d, const float* a, const float* b, float* out, uint64_t rows, uint64_t groups,
+                         uint64_t k, uint64_t n, int transpose_b);
 mg_status silu_mul(Device* d, const float* g, const float* u, float* out, uint64_t n);
 mg_status half_binary(Device* d, const uint16_t* a, const uint16_t* b, uint16_t* out, uint64_t n,
                       mg_dtype dtype, int op);

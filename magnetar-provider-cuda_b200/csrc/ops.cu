@@ -283,6 +283,154 @@ mg_status mg_silu(mg_device* h, const mg_buffer* xh, mg_buffer** out) {
     return k::silu(d, (const float*)x->ptr, (float*)o->ptr, x->count);
 }
 
+// src/kernels.rs:3167-3170 (the tanh approximation)
+mg_status mg_gelu_tanh(mg_device* h, const mg_buffer* xh, mg_buffer** out) {
+    Device* d;
+    const Buffer* x;
+    Buffer* o;
+    MG_TRY(unary_prep(h, xh, out, "gelu", &d, &x, &o));
+    return k::gelu_tanh(d, (const float*)x->ptr, (float*)o->ptr, x->count);
+}
+
+// src/kernels.rs:3121-3125
+mg_status mg_sigmoid(mg_device* h, const mg_buffer* xh, mg_buffer** out) {
+    Device* d;
+    const Buffer* x;
+    Buffer* o;
+    MG_TRY(unary_prep(h, xh, out, "sigmoid", &d, &x, &o));
+    return k::sigmoid(d, (const float*)x->ptr, (float*)o->ptr, x->count);
+}
+
+// src/kernels.rs:3211-3224
+mg_status mg_softcap(mg_device* h, const mg_buffer* xh, float cap, mg_buffer** out) {
+    if (!std::isfinite(cap) || !(cap > 0.0f))
+        return fail(MG_SHAPE_UNSUPPORTED, "softcap cap %g must be finite and positive", (double)cap);
+    Device* d;
+    const Buffer* x;
+    Buffer* o;
+    MG_TRY(unary_prep(h, xh, out, "softcap", &d, &x, &o));
+    return k::softcap(d, (const float*)x->ptr, (float*)o->ptr, cap, x->count);
+}
+
+// src/kernels.rs:3255-3290: out[t, :] = x[t, :] * scale[t], scale of [T, 1] or [T]
+mg_status mg_row_scale(mg_device* h, const mg_buffer* xh, const mg_buffer* sh, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(xh, "input"));
+    MG_TRY(need(sh, "scale"));
+    Device* d = dev(h);
+    const Buffer* x = buf(xh);
+    const Buffer* sc = buf(sh);
+    MG_TRY(same_device(d, x));
+    MG_TRY(same_device(d, sc));
+    MG_TRY(require_f32(x, "row-scale"));
+    MG_TRY(require_f32(sc, "row-scale"));
+    uint64_t rows, cols;
+    MG_TRY(rows_cols(x, &rows, &cols));
+    if (sc->count != rows)
+        return fail(MG_SHAPE_UNSUPPORTED, "row-scale expects one scale per row of %s, got %s", shape_str(x).c_str(),
+                    shape_str(sc).c_str());
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, x->rank, x->shape, out, &o));
+    return k::row_scale(d, (const float*)x->ptr, (const float*)sc->ptr, (float*)o->ptr, rows, cols);
+}
+
+// src/kernels.rs:3058-3100: along the first dimension (the trailing ones must agree)
+mg_status mg_concat(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    MG_TRY(require_f32(a, "concat"));
+    MG_TRY(require_f32(b, "concat"));
+    if (a->rank == 0) return fail(MG_SHAPE_UNSUPPORTED, "concat expects a to have at least one dimension");
+    if (b->rank == 0) return fail(MG_SHAPE_UNSUPPORTED, "concat expects b to have at least one dimension");
+    bool same_rest = a->rank == b->rank;
+    for (int i = 1; same_rest && i < a->rank; i++) same_rest = a->shape[i] == b->shape[i];
+    if (!same_rest)
+        return fail(MG_SHAPE_UNSUPPORTED, "concat expects a and b to share trailing dimensions, got %s and %s",
+                    shape_str(a).c_str(), shape_str(b).c_str());
+    uint64_t shape[MG_MAX_RANK];
+    for (int i = 0; i < a->rank; i++) shape[i] = a->shape[i];
+    shape[0] = a->shape[0] + b->shape[0];
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, a->rank, shape, out, &o));
+    if (a->count)
+        MG_CUDA(cudaMemcpyAsync(o->ptr, a->ptr, a->count * 4, cudaMemcpyDeviceToDevice, d->stream), "concat copy");
+    if (b->count)
+        MG_CUDA(cudaMemcpyAsync((float*)o->ptr + a->count, b->ptr, b->count * 4, cudaMemcpyDeviceToDevice, d->stream),
+                "concat copy");
+    return MG_OK;
+}
+
+// src/kernels.rs:7084-7130: each output row holds head_count heads, head h being a's head h
+// then b's head h (second_head_count == head_count) or b's only head (second_head_count == 1).
+mg_status mg_concat_heads(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, uint64_t head_count,
+                          uint64_t second_head_count, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    MG_TRY(require_f32(a, "concat"));
+    MG_TRY(require_f32(b, "concat"));
+    uint64_t rows, a_cols, b_rows, b_cols;
+    MG_TRY(rows_cols(a, &rows, &a_cols));
+    MG_TRY(rows_cols(b, &b_rows, &b_cols));
+    if (rows != b_rows)
+        return fail(MG_SHAPE_UNSUPPORTED, "concat across heads needs inputs with the same rows, got %s and %s",
+                    shape_str(a).c_str(), shape_str(b).c_str());
+    if (head_count == 0 || a_cols % head_count != 0 || second_head_count == 0 ||
+        (second_head_count != 1 && second_head_count != head_count) || b_cols % second_head_count != 0)
+        return fail(MG_SHAPE_UNSUPPORTED,
+                    "concat across heads cannot split %s into %llu heads and %s into %llu (the second input has "
+                    "one head or as many as the first)",
+                    shape_str(a).c_str(), (unsigned long long)head_count, shape_str(b).c_str(),
+                    (unsigned long long)second_head_count);
+    const uint64_t a_width = a_cols / head_count, b_width = b_cols / second_head_count;
+    const uint64_t shape[2] = {rows, head_count * (a_width + b_width)};
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
+    return k::concat_heads(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, rows, head_count, a_width,
+                           b_width, second_head_count);
+}
+
+// src/kernels.rs:5882-5950
+mg_status mg_batched_matmul(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, uint64_t groups, int transpose_b,
+                            mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ah, "a"));
+    MG_TRY(need(bh, "b"));
+    Device* d = dev(h);
+    const Buffer* a = buf(ah);
+    const Buffer* b = buf(bh);
+    MG_TRY(same_device(d, a));
+    MG_TRY(same_device(d, b));
+    MG_TRY(require_f32(a, "batched-matmul"));
+    MG_TRY(require_f32(b, "batched-matmul"));
+    uint64_t rows, a_cols, b_rows, b_cols;
+    MG_TRY(rows_cols(a, &rows, &a_cols));
+    MG_TRY(rows_cols(b, &b_rows, &b_cols));
+    const bool fits = groups > 0 && a_cols % groups == 0 && b_rows % groups == 0 &&
+                      (transpose_b ? b_cols == a_cols / groups : b_rows == a_cols);
+    if (!fits)
+        return fail(MG_SHAPE_UNSUPPORTED, "batched-matmul of %llu groups (transpose_b %s) cannot take %s and %s",
+                    (unsigned long long)groups, transpose_b ? "true" : "false", shape_str(a).c_str(),
+                    shape_str(b).c_str());
+    const uint64_t k = a_cols / groups, n = transpose_b ? b_rows / groups : b_cols;
+    const uint64_t shape[2] = {rows, groups * n};
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
+    return k::batched_matmul(d, (const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, rows, groups, k, n,
+                             transpose_b);
+}
+
 // src/kernels.rs:4492-4523
 mg_status mg_silu_mul(mg_device* h, const mg_buffer* gh, const mg_buffer* uh, mg_buffer** out) {
     MG_TRY(device_check(h));

@@ -265,6 +265,32 @@ class CudaKernels:
     def softmax_rows(self, x, out=None):
         return self._run(N.lib().mg_softmax, x.handle, out=out)
 
+    def gelu_tanh(self, x, out=None):
+        """``gelu_tanh`` (the tanh approximation)."""
+        return self._run(N.lib().mg_gelu_tanh, x.handle, out=out)
+
+    def sigmoid(self, x, out=None):
+        return self._run(N.lib().mg_sigmoid, x.handle, out=out)
+
+    def softcap(self, x, cap, out=None):
+        """``cap * tanh(x / cap)``."""
+        return self._run(N.lib().mg_softcap, x.handle, float(cap), out=out)
+
+    def row_scale(self, x, scale, out=None):
+        """``out[t, :] = x[t, :] * scale[t]``."""
+        return self._run(N.lib().mg_row_scale, x.handle, scale.handle, out=out)
+
+    def concat(self, a, b, out=None):
+        """Along the first dimension."""
+        return self._run(N.lib().mg_concat, a.handle, b.handle, out=out)
+
+    def concat_heads(self, a, b, head_count, second_head_count=None, out=None):
+        shc = head_count if second_head_count is None else second_head_count
+        return self._run(N.lib().mg_concat_heads, a.handle, b.handle, int(head_count), int(shc), out=out)
+
+    def batched_matmul(self, a, b, groups, transpose_b=False, out=None):
+        return self._run(N.lib().mg_batched_matmul, a.handle, b.handle, int(groups), int(bool(transpose_b)), out=out)
+
     def kv_write(self, store, rows, row_offset):
         """``kv_write``: ``rows`` over ``store``'s rows ``row_offset..`` in place."""
         check(N.lib().mg_kv_write(self._h, store.handle, rows.handle, int(row_offset)))

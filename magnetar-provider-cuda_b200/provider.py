@@ -67,12 +67,17 @@ def cuda_kernel_advertisements(device: str, provider: str = CUDA_PROVIDER_NAME) 
         _baseline("rope", "PositionEncoding", device, provider,
                   ["rope-banded-frequency-scaling", "rope-partial-rotary", "rope-yarn-frequency-scaling"]),
         _baseline("attention", "Attention", device, provider,
-                  ["attention-key-count", "attention-scale", "attention-value-head-dimension"]),
+                  ["attention-key-count", "attention-scale", "attention-value-head-dimension", "key-count"]),
         _baseline("softmax", "Activation", device, provider),
         _baseline("silu", "Activation", device, provider),
+        _baseline("gelu", "Activation", device, provider),  # the tanh approximation
         _baseline("add", "Tensor", device, provider),
         _baseline("mul", "Tensor", device, provider),
         _baseline("residual-add", "Tensor", device, provider),
+        _baseline("row-scale", "Tensor", device, provider),
+        _baseline("concat", "Tensor", device, provider, ["heads"]),  # rows, or heads (axis = "heads")
+        _baseline("batched-matmul", "LinearAlgebra", device, provider),
+        _baseline("kv-write", "Tensor", device, provider),  # f32 stores, in place
         _half("add", "Tensor", device, provider),
         _half("mul", "Tensor", device, provider),
     ]

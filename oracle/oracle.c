@@ -201,6 +201,68 @@ void orc_silu(const float* x, float* out, uint64_t n) {
     }
 }
 
+/* src/kernels.cu:80-92: the tanh form of GELU, in the reference's order of operations */
+void orc_gelu_tanh(const float* x, float* out, uint64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; i++) {
+        float v = x[i];
+        out[i] = 0.5f * v * (1.0f + tanhf(0.7978846f * (v + 0.044715f * v * v * v)));
+    }
+}
+
+/* src/kernels.cu:1079-1084 */
+void orc_sigmoid(const float* x, float* out, uint64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; i++) out[i] = 1.0f / (1.0f + expf(-x[i]));
+}
+
+/* src/kernels.cu:103-109 */
+void orc_softcap(const float* x, float* out, float cap, uint64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; i++) out[i] = cap * tanhf(x[i] / cap);
+}
+
+/* src/kernels.cu:1066-1077: out[i] = x[i] * scale[i / cols] */
+void orc_row_scale(const float* x, const float* scale, float* out, uint64_t rows, uint64_t cols) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)(rows * cols); i++) out[i] = x[i] * scale[(uint64_t)i / cols];
+}
+
+/* src/kernels.cu:5786-5812: head h of output row r = a's head h, then b's head h (or b's only
+ * head when b_heads == 1) */
+void orc_concat_heads(const float* a, const float* b, float* out, uint64_t rows, uint64_t heads, uint64_t a_width,
+                      uint64_t b_width, uint64_t b_heads) {
+    const uint64_t width = a_width + b_width;
+#pragma omp parallel for schedule(static)
+    for (int64_t idx = 0; idx < (int64_t)(rows * heads * width); idx++) {
+        const uint64_t row = (uint64_t)idx / (heads * width), rem = (uint64_t)idx % (heads * width);
+        const uint64_t head = rem / width, j = rem % width;
+        out[idx] = j < a_width ? a[(row * heads + head) * a_width + j]
+                               : b[(row * b_heads + (b_heads == 1 ? 0 : head)) * b_width + (j - a_width)];
+    }
+}
+
+/* src/kernels.cu:6296-6336: out[r][g n + j] = sum over i in order of a[r][g k + i] times
+ * b[g k + i][j] (or b[g n + j][i] with transpose_b) */
+void orc_batched_matmul(const float* a, const float* b, float* out, uint64_t rows, uint64_t groups, uint64_t k,
+                        uint64_t n, int transpose_b) {
+    const uint64_t width = groups * n;
+#pragma omp parallel for schedule(static)
+    for (int64_t idx = 0; idx < (int64_t)(rows * width); idx++) {
+        const uint64_t r = (uint64_t)idx / width, col = (uint64_t)idx % width, g = col / n, j = col % n;
+        const float* in = a + r * groups * k + g * k;
+        float sum = 0.0f;
+        if (transpose_b) {
+            const float* w = b + (g * n + j) * k;
+            for (uint64_t i = 0; i < k; i++) sum += in[i] * w[i];
+        } else {
+            const float* w = b + g * k * n + j;
+            for (uint64_t i = 0; i < k; i++) sum += in[i] * w[i * n];
+        }
+        out[idx] = sum;
+    }
+}
+
 /* src/kernels.cu:64-71 */
 void orc_silu_mul(const float* gate, const float* up, float* out, uint64_t n) {
 #pragma omp parallel for schedule(static)

@@ -48,6 +48,14 @@ void orc_mul(const float* a, const float* b, float* out, uint64_t n);
 void orc_mul_scalar(const float* a, const float* b, float* out, uint64_t n);
 void orc_scale(const float* x, float* out, float factor, uint64_t n);
 void orc_silu(const float* x, float* out, uint64_t n);
+void orc_gelu_tanh(const float* x, float* out, uint64_t n);
+void orc_sigmoid(const float* x, float* out, uint64_t n);
+void orc_softcap(const float* x, float* out, float cap, uint64_t n);
+void orc_row_scale(const float* x, const float* scale, float* out, uint64_t rows, uint64_t cols);
+void orc_concat_heads(const float* a, const float* b, float* out, uint64_t rows, uint64_t heads, uint64_t a_width,
+                      uint64_t b_width, uint64_t b_heads);
+void orc_batched_matmul(const float* a, const float* b, float* out, uint64_t rows, uint64_t groups, uint64_t k,
+                        uint64_t n, int transpose_b);
 void orc_silu_mul(const float* gate, const float* up, float* out, uint64_t n);
 
 /* ---- embedding (src/kernels.cu:127-176); returns 1 when an id was invalid ---- */

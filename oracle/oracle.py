@@ -198,6 +198,68 @@ def silu(x):
     return o
 
 
+def gelu_tanh(x):
+    """src/kernels.cu:80-92"""
+    x, xp = _f(x)
+    o, op = _out(x.shape)
+    lib().orc_gelu_tanh(xp, op, _u64(x.size))
+    return o
+
+
+def sigmoid(x):
+    """src/kernels.cu:1079-1084"""
+    x, xp = _f(x)
+    o, op = _out(x.shape)
+    lib().orc_sigmoid(xp, op, _u64(x.size))
+    return o
+
+
+def softcap(x, cap):
+    """src/kernels.cu:103-109"""
+    x, xp = _f(x)
+    o, op = _out(x.shape)
+    lib().orc_softcap(xp, op, ctypes.c_float(cap), _u64(x.size))
+    return o
+
+
+def row_scale(x, scale):
+    """src/kernels.cu:1066-1077"""
+    x, xp = _f(x)
+    s, sp = _f(scale)
+    o, op = _out(x.shape)
+    lib().orc_row_scale(xp, sp, op, _u64(x.shape[0]), _u64(x.shape[1]))
+    return o
+
+
+def concat(a, b):
+    """src/kernels.rs:3058-3100: along the first dimension"""
+    return np.concatenate([np.asarray(a, np.float32), np.asarray(b, np.float32)], axis=0)
+
+
+def concat_heads(a, b, head_count, second_head_count=None):
+    """src/kernels.cu:5786-5812"""
+    a, ap = _f(a)
+    b, bp = _f(b)
+    second = head_count if second_head_count is None else second_head_count
+    rows = a.shape[0]
+    aw, bw = a.shape[1] // head_count, b.shape[1] // second
+    o, op = _out((rows, head_count * (aw + bw)))
+    lib().orc_concat_heads(ap, bp, op, _u64(rows), _u64(head_count), _u64(aw), _u64(bw), _u64(second))
+    return o
+
+
+def batched_matmul(a, b, groups, transpose_b=False):
+    """src/kernels.cu:6296-6336"""
+    a, ap = _f(a)
+    b, bp = _f(b)
+    rows, acols = a.shape
+    k = acols // groups
+    n = b.shape[0] // groups if transpose_b else b.shape[1]
+    o, op = _out((rows, groups * n))
+    lib().orc_batched_matmul(ap, bp, op, _u64(rows), _u64(groups), _u64(k), _u64(n), ctypes.c_int(int(transpose_b)))
+    return o
+
+
 def silu_mul(g, u):
     g, gp = _f(g)
     u, up = _f(u)

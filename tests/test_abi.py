@@ -67,8 +67,10 @@ def test_device_discovery_without_gpu_is_graceful(mpc):
 def test_advertisements_mirror_the_reference(mpc):
     ads = mpc.cuda_kernel_advertisements("cuda:0")
     names = [a.name for a in ads]
+    # src/tests.rs:130-153 lists the reference's set; all but moe-experts (out of scope) here
     for n in ["matmul", "matmul-bias", "matmul-residual", "gated-matmul", "silu-mul", "embedding", "rmsnorm",
-              "rope", "attention", "softmax", "silu", "add", "mul", "residual-add", "add-half", "mul-half"]:
+              "rope", "attention", "softmax", "silu", "add", "mul", "residual-add", "add-half", "mul-half",
+              "batched-matmul", "row-scale", "activation", "kv-write", "gelu", "concat"]:
         assert n in names
     by = {a.name: a for a in ads}
     assert all(by[n].rank == 2 for n in ("matmul", "rope", "attention", "softmax"))

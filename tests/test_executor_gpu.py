@@ -416,3 +416,39 @@ def test_captured_decode_step_replays_at_advancing_offsets(executor, oracle):
     with pytest.raises(mpc.CudaError) as e:
         executor.replay_step(offset=cap - prefix)  # would write past the history
     assert e.value.code == "CaptureUnsupported"
+
+
+def test_layered_forms_through_the_executor(executor, oracle):
+    # src/executor.rs:1798-1965: gelu's approximate, activation sigmoid / softcap, row-scale,
+    # concat rows / heads and batched-matmul with their attribute rules
+    r = np.random.default_rng(9)
+    x = r.standard_normal((6, 16)).astype(np.float32)
+    s = r.standard_normal((6, 1)).astype(np.float32)
+    y = r.standard_normal((6, 8)).astype(np.float32)
+    w = r.standard_normal((2 * 8, 3)).astype(np.float32)
+    for n, t in (("x", x), ("s", s), ("y", y), ("w", w)):
+        executor.write_tensor(n, t)
+    executor.run(inv("gelu", ["x"], "g", {"approximate": "tanh"}))
+    assert rel(executor.read_tensor("g"), oracle.gelu_tanh(x)) <= 1e-5
+    executor.run(inv("gelu", ["x"], "g2"))
+    np.testing.assert_array_equal(executor.read_tensor("g2"), executor.read_tensor("g"))
+    r1 = executor.submit_kernel(inv("gelu", ["x"], "g3", {"approximate": "none"}))
+    assert not r1.success and r1.error_code == "KernelAttributeUnsupported"
+    executor.run(inv("activation", ["x"], "sg", {"kind": "sigmoid"}))
+    assert rel(executor.read_tensor("sg"), oracle.sigmoid(x)) <= 1e-5
+    executor.run(inv("activation", ["x"], "sc", {"kind": "softcap", "cap": 2.0}))
+    assert rel(executor.read_tensor("sc"), oracle.softcap(x, 2.0)) <= 1e-5
+    r2 = executor.submit_kernel(inv("activation", ["x"], "sc2", {"kind": "softcap"}))
+    assert not r2.success and r2.error_code == "KernelAttributeUnsupported"
+    executor.run(inv("row-scale", ["x", "s"], "rs"))
+    np.testing.assert_array_equal(executor.read_tensor("rs"), oracle.row_scale(x, s.reshape(-1)))
+    executor.run(inv("concat", ["x", "x"], "cr"))
+    np.testing.assert_array_equal(executor.read_tensor("cr"), np.concatenate([x, x]))
+    executor.run(inv("concat", ["x", "y"], "ch", {"axis": "heads", "head_count": 2}))
+    np.testing.assert_array_equal(executor.read_tensor("ch"), oracle.concat_heads(x, y, 2))
+    r3 = executor.submit_kernel(inv("concat", ["x", "y"], "cb", {"axis": "columns"}))
+    assert not r3.success and r3.error_code == "KernelAttributeUnsupported"
+    executor.run(inv("batched-matmul", ["x", "w"], "bm", {"group_count": 2}))
+    assert rel(executor.read_tensor("bm"), oracle.batched_matmul(x, w, 2)) <= 1e-4
+    r4 = executor.submit_kernel(inv("batched-matmul", ["x", "w"], "bm2"))
+    assert not r4.success and r4.error_code == "KernelAttributeUnsupported"

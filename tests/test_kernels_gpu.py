@@ -509,3 +509,66 @@ def test_buffers_outlive_a_closed_device(mpc):
     assert N.lib().mg_add(stale, a.handle, b.handle, ctypes.byref(out)) == unavailable
     a.release()
     b.release()  # the last reference: the device goes now
+
+
+def test_layered_elementwise_forms(kernels, oracle, mpc):
+    # gelu (tanh), sigmoid, softcap and row-scale against the oracle (src/tests_conformance.rs:
+    # 4717-4732, 4945-4990); vectorised and ragged sizes
+    r = rng(18)
+    for shape in ((3, 70), (64, 1024), (5, 7)):
+        x = (r.standard_normal(shape) * 4).astype(np.float32)
+        dx = kernels.upload(x)
+        assert rel(kernels.download(kernels.gelu_tanh(dx)), oracle.gelu_tanh(x)) <= TOL_ELEMENTWISE
+        assert rel(kernels.download(kernels.sigmoid(dx)), oracle.sigmoid(x)) <= TOL_ELEMENTWISE
+        assert rel(kernels.download(kernels.softcap(dx, 1.5)), oracle.softcap(x, 1.5)) <= TOL_ELEMENTWISE
+        s = r.standard_normal(shape[0]).astype(np.float32)
+        for sd in (kernels.upload(s), kernels.upload(s.reshape(-1, 1))):
+            np.testing.assert_array_equal(kernels.download(kernels.row_scale(dx, sd)), oracle.row_scale(x, s))
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.softcap(dx, 0.0)
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.row_scale(dx, kernels.upload(np.ones(6, np.float32)))
+    assert e.value.code == "ShapeUnsupported"
+
+
+def test_concat_rows_and_heads(kernels, oracle, mpc):
+    # src/kernels.rs:3058-3100, 7084-7130; src/tests_conformance.rs:5606-5640
+    r = rng(19)
+    a = r.standard_normal((3, 4, 5)).astype(np.float32)
+    b = r.standard_normal((2, 4, 5)).astype(np.float32)
+    got = kernels.concat(kernels.upload(a), kernels.upload(b))
+    assert got.shape == (5, 4, 5)
+    np.testing.assert_array_equal(kernels.download(got), oracle.concat(a, b))
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.concat(kernels.upload(a), kernels.upload(np.zeros((2, 4, 6), np.float32)))
+    assert e.value.code == "ShapeUnsupported"
+    for heads, aw, second, bw in ((4, 6, 4, 2), (16, 128, 1, 64), (3, 5, 3, 3), (2, 8, 1, 4)):
+        x = r.standard_normal((5, heads * aw)).astype(np.float32)
+        y = r.standard_normal((5, second * bw)).astype(np.float32)
+        got = kernels.concat_heads(kernels.upload(x), kernels.upload(y), heads, second)
+        np.testing.assert_array_equal(kernels.download(got), oracle.concat_heads(x, y, heads, second))
+    x = kernels.upload(r.standard_normal((5, 12)).astype(np.float32))
+    for y, second in ((np.zeros((4, 3), np.float32), 1), (np.zeros((5, 6), np.float32), 2)):
+        with pytest.raises(mpc.CudaError) as e:
+            kernels.concat_heads(x, kernels.upload(y), 4, second)
+        assert e.value.code == "ShapeUnsupported"
+
+
+@pytest.mark.parametrize("rows,groups,k,n", [(3, 2, 8, 5), (16, 4, 64, 32), (1, 8, 128, 96), (7, 3, 33, 17)])
+@pytest.mark.parametrize("tb", [False, True])
+def test_batched_matmul(kernels, oracle, rows, groups, k, n, tb):
+    r = rng(20)
+    a = r.standard_normal((rows, groups * k)).astype(np.float32)
+    b = r.standard_normal((groups * n, k) if tb else (groups * k, n)).astype(np.float32)
+    got = kernels.download(kernels.batched_matmul(kernels.upload(a), kernels.upload(b), groups, tb))
+    assert rel(got, oracle.batched_matmul(a, b, groups, tb)) <= TOL_MATMUL
+
+
+def test_batched_matmul_shape_errors(kernels, mpc):
+    a = kernels.upload(np.zeros((2, 12), np.float32))
+    for b, groups, tb in ((np.zeros((12, 4), np.float32), 5, False), (np.zeros((10, 4), np.float32), 2, False),
+                          (np.zeros((6, 5), np.float32), 2, True)):
+        with pytest.raises(mpc.CudaError) as e:
+            kernels.batched_matmul(a, kernels.upload(b), groups, tb)
+        assert e.value.code == "ShapeUnsupported"

@@ -137,3 +137,32 @@ def test_rmsnorm_matches_definition(oracle):
     out = oracle.rmsnorm(x, w, 1e-5)
     ref = x / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + 1e-5) * w
     np.testing.assert_allclose(out, ref, rtol=2e-6, atol=1e-6)
+
+
+def test_oracle_layered_forms_against_numpy(oracle):
+    # gelu (tanh), sigmoid, softcap, row-scale, concat across heads and batched-matmul: the C
+    # restatements against independent float64 numpy computations of the same definitions.
+    r = np.random.default_rng(31)
+    x = (r.standard_normal((7, 40)) * 4).astype(np.float32)
+    x64 = x.astype(np.float64)
+    gelu = 0.5 * x64 * (1 + np.tanh(0.7978846 * (x64 + 0.044715 * x64 ** 3)))
+    np.testing.assert_allclose(oracle.gelu_tanh(x), gelu, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(oracle.sigmoid(x), 1 / (1 + np.exp(-x64)), rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(oracle.softcap(x, 1.5), 1.5 * np.tanh(x64 / 1.5), rtol=1e-6, atol=1e-6)
+    s = r.standard_normal(7).astype(np.float32)
+    np.testing.assert_array_equal(oracle.row_scale(x, s), x * s[:, None])
+    a = r.standard_normal((5, 4 * 6)).astype(np.float32)
+    b = r.standard_normal((5, 4 * 2)).astype(np.float32)
+    exp = np.concatenate([a.reshape(5, 4, 6), b.reshape(5, 4, 2)], axis=2).reshape(5, 32)
+    np.testing.assert_array_equal(oracle.concat_heads(a, b, 4), exp)
+    b1 = r.standard_normal((5, 3)).astype(np.float32)
+    exp1 = np.concatenate([a.reshape(5, 4, 6), np.repeat(b1[:, None, :], 4, axis=1)], axis=2).reshape(5, 36)
+    np.testing.assert_array_equal(oracle.concat_heads(a, b1, 4, 1), exp1)
+    ga = r.standard_normal((3, 2 * 8)).astype(np.float32)
+    gb = r.standard_normal((2 * 8, 5)).astype(np.float32)
+    exp = np.concatenate([ga[:, g * 8:(g + 1) * 8].astype(np.float64) @ gb[g * 8:(g + 1) * 8] for g in range(2)], axis=1)
+    np.testing.assert_allclose(oracle.batched_matmul(ga, gb, 2), exp, rtol=1e-5, atol=1e-5)
+    gbt = r.standard_normal((2 * 5, 8)).astype(np.float32)
+    exp = np.concatenate([ga[:, g * 8:(g + 1) * 8].astype(np.float64) @ gbt[g * 5:(g + 1) * 5].T for g in range(2)],
+                         axis=1)
+    np.testing.assert_allclose(oracle.batched_matmul(ga, gbt, 2, transpose_b=True), exp, rtol=1e-5, atol=1e-5)
