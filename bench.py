@@ -413,13 +413,14 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
         del x, y
     # config 4: memory-bound suite on [8192, 4096]
     R, C = 8192, 4096
-    names = ["rmsnorm", "rope h32x128 theta5e5", "silu", "add", "mul", "residual-add"]
+    names = ["rmsnorm", "rope h32x128 theta5e5", "silu", "add", "mul", "residual-add", "gelu", "row-scale"]
     if any(want(f"{n} [8192,4096]") for n in names):
         x = torch.randn(R, C, device="cuda", generator=g)
         y = torch.randn(R, C, device="cuda", generator=g)
         o = torch.empty(R, C, device="cuda")
         gain = 1 + 0.1 * torch.randn(C, device="cuda", generator=g)
-        dx, dy, do, dg = W(x), W(y), W(o), W(gain)
+        rs = torch.randn(R, device="cuda", generator=g)
+        dx, dy, do, dg, drs = W(x), W(y), W(o), W(gain), W(rs)
         nb = R * C * 4
         suite = [
             ("rmsnorm", lambda: kernels.rmsnorm(dx, dg, 1e-5, out=do), 2 * nb + C * 4),
@@ -429,10 +430,14 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
             ("add", lambda: kernels.add(dx, dy, out=do), 3 * nb),
             ("mul", lambda: kernels.mul(dx, dy, out=do), 3 * nb),
             ("residual-add", lambda: kernels.residual_add(dx, dy, out=do), 3 * nb),
+            # the remaining advertised elementwise forms (not in the configs: same shape)
+            ("gelu", lambda: kernels.gelu_tanh(dx, out=do), 2 * nb),
+            ("row-scale", lambda: kernels.row_scale(dx, drs, out=do), 2 * nb + R * 4),
         ]
         for nm, fn, work in suite:
             if want(f"{nm} [8192,4096]"):
-                add(f"{nm} [8192,4096]", "configs[3]", timed(fn, reps=10), "hbm", work)
+                add(f"{nm} [8192,4096]", "configs[3]" if nm not in ("gelu", "row-scale") else "advertised ops",
+                    timed(fn, reps=10), "hbm", work)
         del x, y, o
     for dt, tdt in (("f16", torch.float16), ("bf16", torch.bfloat16)):
         if not any(want(f"{op} {dt} [8192,4096]") for op in ("add-half", "mul-half")):
