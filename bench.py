@@ -292,6 +292,7 @@ def measure_tf32_peak(torch):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+EXACT_MS = (1, 16, 128, 2048)  # the matmul lines also timed with bfloat16-exact weights
 ROT_COPIES = 6  # copies of the 64 MB B the M <= 128 lines rotate through (384 MB > the 126 MB L2)
 NODE_COPIES = 8  # instances of a layer node per timed step (per-node times)
 
@@ -349,15 +350,24 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
         # M times one call on one B.
         copies = [b] + [b.clone() for _ in range(ROT_COPIES - 1)]
         rot = {"": [W(x).set_weight() for x in copies], " (B per-call)": [W(x) for x in copies]}
+        if any(want(f"matmul M={M} (bf16-exact weight)") for M in EXACT_MS):
+            # the same weights rounded to bfloat16 values (a bfloat16 checkpoint's): the GEMV
+            # streams their compact bfloat16 form, and their prepared lo term is zero, so the
+            # GEMM reads hi alone
+            exact = [(x.view(torch.int32) & -65536).view(torch.float32) for x in copies]
+            rot[" (bf16-exact weight)"] = [W(x).set_weight() for x in exact]
         for M in (1, 16, 128, 2048, 8192):
             if not want(f"matmul M={M}"):
                 continue
             a = torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)
             c = torch.empty(M, N, device="cuda")
             da, dc = W(a), W(c)
-            for label in ("", " (B per-call)"):
-                if M <= 16 and label:
+            for label in ("", " (B per-call)", " (bf16-exact weight)"):
+                exact = label == " (bf16-exact weight)"
+                if M <= 16 and label and not exact:
                     continue  # the GEMV path reads B as it is either way
+                if label not in rot or (exact and M not in EXACT_MS):
+                    continue
                 bufs = rot[label]
                 if M <= 128:
                     turn = [0]
@@ -371,8 +381,9 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
                     ms = timed(call, n=max(iters, 15), reps=ROT_COPIES)
                 else:
                     ms = timed(lambda: kernels.matmul(da, bufs[0], out=dc), n=iters)
-                if M <= 16:
-                    add(f"matmul M={M}{label}", "configs[1]", ms, "hbm", 4.0 * (M * K + K * N + M * N))
+                if M <= 16:  # B's bytes: 4 per value, 2 in the compact form
+                    add(f"matmul M={M}{label}", "configs[1]", ms, "hbm",
+                        4.0 * (M * K + M * N) + (2.0 if exact else 4.0) * K * N)
                 else:
                     add(f"matmul M={M}{label}", "configs[1]", ms, "tensor", 2.0 * M * N * K)
             del a, c

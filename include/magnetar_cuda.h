@@ -136,6 +136,12 @@ void* mg_buffer_device_ptr(const mg_buffer* buffer);
  * call, as the reference prepares compact weights at upload (src/kernels.rs:1667-1723).  Any
  * write to the buffer drops the prepared form. */
 mg_status mg_buffer_set_weight(mg_buffer* buffer, int is_weight);
+/* 1 when a weight holds its compact form: a matrix of at least 65536 values, all exactly
+ * bfloat16, kept also as its bfloat16 bits, which the few-row (M <= 16) matmul streams instead
+ * of the f32 values -- half the bytes, bit-identical results (the reference's compact weight,
+ * `CudaDeviceBuffer::is_compact`, src/kernels.rs:257-268, 1668-1712).  Built and checked on the
+ * first such matmul that reads the weight; 0 before that, for other buffers, and for null. */
+int mg_buffer_is_compact(const mg_buffer* buffer);
 
 /* ---------------------------------------------------------------------------------- */
 /* Kernels -- one entry per advertised hot-path operator, with the validation of the    */

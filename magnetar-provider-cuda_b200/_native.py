@@ -120,6 +120,7 @@ SIGNATURES = {
     "mg_buffer_reshape": [_P, _I, _U64P],
     "mg_buffer_device_ptr": [_P],
     "mg_buffer_set_weight": [_P, _I],
+    "mg_buffer_is_compact": [_P],
     "mg_add": [_P, _P, _P, _PP],
     "mg_mul": [_P, _P, _P, _PP],
     "mg_residual_add": [_P, _P, _P, _PP],

@@ -86,14 +86,22 @@ __device__ __forceinline__ void split4_fast(float4 v, float4& hi, float4& lo) {
     lo = make_float4(tf32_round(v.x - hi.x), tf32_round(v.y - hi.y), tf32_round(v.z - hi.z), tf32_round(v.w - hi.w));
 }
 
+// Sets *flag (when not null) if any lane of the warp saw a nonzero lo term.  Every lane of
+// the warp calls it once, after its loop.
+__device__ __forceinline__ void note_lo(int* flag, bool nonzero) {
+    if (!flag) return;
+    if (__any_sync(0xffffffffu, nonzero) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
+}
+
 // src [rows, k] (row stride ld) -> hi/lo [rows, kp], zero past k.  16-byte vectors when the
-// rows allow it.
+// rows allow it.  `lo_nonzero` (optional): set when any lo term is nonzero.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, uint64_t ld, uint64_t rows,
                                                          uint64_t k, float* __restrict__ hi, float* __restrict__ lo,
-                                                         uint64_t kp, int vec) {
+                                                         uint64_t kp, int vec, int* lo_nonzero) {
     pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    bool nz = false;
     if (vec) {  // k == kp, k % 4 == 0, 16-byte aligned
         const uint64_t n4 = rows * kp / 4;
         const float4* s4 = reinterpret_cast<const float4*>(src);
@@ -102,24 +110,27 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
             split4(s4[i], h, l);
             reinterpret_cast<float4*>(hi)[i] = h;
             reinterpret_cast<float4*>(lo)[i] = l;
+            nz = nz || l.x != 0.0f || l.y != 0.0f || l.z != 0.0f || l.w != 0.0f;
         }
-        return;
+    } else {
+        const uint64_t total = rows * kp;
+        for (uint64_t i = t0; i < total; i += stride) {
+            const uint64_t r = i / kp, c = i % kp;
+            float h = 0.0f, l = 0.0f;
+            if (c < k) split_tf32(src[r * ld + c], h, l);
+            hi[i] = h;
+            lo[i] = l;
+            nz = nz || l != 0.0f;
+        }
     }
-    const uint64_t total = rows * kp;
-    for (uint64_t i = t0; i < total; i += stride) {
-        const uint64_t r = i / kp, c = i % kp;
-        float h = 0.0f, l = 0.0f;
-        if (c < k) split_tf32(src[r * ld + c], h, l);
-        hi[i] = h;
-        lo[i] = l;
-    }
+    note_lo(lo_nonzero, nz);
 }
 
 // src [r_count, c_count] row-major -> hi/lo [c_count, rp] with dst[c][r] = src[r][c], through
 // 64 x 64 shared-memory tiles.
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ src, uint64_t r_count,
                                                               uint64_t c_count, float* __restrict__ hi,
-                                                              float* __restrict__ lo, uint64_t rp) {
+                                                              float* __restrict__ lo, uint64_t rp, int* lo_nonzero) {
     pdl_enter();
     __shared__ float tile[64][65];
     const uint64_t c0 = (uint64_t)blockIdx.x * 64, r0 = (uint64_t)blockIdx.y * 64;
@@ -129,6 +140,7 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
         tile[j][tx] = (r < r_count && c < c_count) ? src[r * c_count + c] : 0.0f;
     }
     __syncthreads();
+    bool nz = false;
     for (int j = ty; j < 64; j += 4) {
         const uint64_t c = c0 + j, r = r0 + tx;
         if (c < c_count && r < rp) {
@@ -136,8 +148,10 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
             split_tf32(tile[tx][j], h, l);
             hi[c * rp + r] = h;
             lo[c * rp + r] = l;
+            nz = nz || l != 0.0f;
         }
     }
+    note_lo(lo_nonzero, nz);
 }
 
 // ---- the tensor-core GEMM ---------------------------------------------------------------------
@@ -151,6 +165,8 @@ struct TcParams {
     int splits;        // CTAs per cluster (blockIdx.y), each over its own range of k
     int b_early;       // B is a stable prepared weight: its first loads may precede pdl_enter()
     int prefetch;      // prefetch tiles into the L2 one ring's depth ahead (one row of M tiles)
+    int b_terms;       // 2; 1 when every B's lo term is zero (its values are exactly tf32): lo is
+                       // neither loaded nor multiplied -- the products it would add are exact zeros
     int* error;        // device word set when a wait times out
     // Grouped projection: `groups` (1-3) weights multiply the same A side by side (tiles_n is
     // per weight); weight g writes outs[g] and, when rope_out[g] is set, also the rows of
@@ -262,17 +278,17 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
     auto issue_b = [&](int i) {
         const int s = i % STAGES;
         const uint32_t st = base + s * S::kStage;
-        mbar_arrive_expect_tx(full_bar(s), S::kTxBytes);
+        mbar_arrive_expect_tx(full_bar(s), S::kTxBytes - (B_RAW || p.b_terms == 2 ? 0 : NB * S::kBTile));
         const int kx = (kb0 + i) * BK;
         if (B_RAW) {
             tma_load_2d(st + S::kOffBRaw, map_whi, full_bar(s), n0, kx);  // [BK rows of k][BN columns]
             return;
         }
         tma_load_2d(st + 2 * S::kATile, map_whi, full_bar(s), kx, n0);
-        tma_load_2d(st + 2 * S::kATile + S::kBTile, map_wlo, full_bar(s), kx, n0);
+        if (p.b_terms == 2) tma_load_2d(st + 2 * S::kATile + S::kBTile, map_wlo, full_bar(s), kx, n0);
         if (NB == 2) {
             tma_load_2d(st + 2 * S::kATile + 2 * S::kBTile, &map_b2hi, full_bar(s), kx, n0);
-            tma_load_2d(st + 2 * S::kATile + 3 * S::kBTile, &map_b2lo, full_bar(s), kx, n0);
+            if (p.b_terms == 2) tma_load_2d(st + 2 * S::kATile + 3 * S::kBTile, &map_b2lo, full_bar(s), kx, n0);
         }
     };
     auto issue = [&](int i) {
@@ -290,10 +306,10 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
             tma_prefetch_2d(map_whi, n0, kx);
         } else {
             tma_prefetch_2d(map_whi, kx, n0);
-            tma_prefetch_2d(map_wlo, kx, n0);
+            if (p.b_terms == 2) tma_prefetch_2d(map_wlo, kx, n0);
             if (NB == 2) {
                 tma_prefetch_2d(&map_b2hi, kx, n0);
-                tma_prefetch_2d(&map_b2lo, kx, n0);
+                if (p.b_terms == 2) tma_prefetch_2d(&map_b2lo, kx, n0);
             }
         }
         tma_prefetch_2d(&map_a0, kx, m0);
@@ -361,6 +377,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         // ---- MMA issuer ----------------------------------------------------------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
+            const bool two_b = B_RAW || p.b_terms == 2;
             bool ok = true;
             for (int i = 0; i < num_kb; i++) {
                 const int s = i % STAGES;
@@ -388,7 +405,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                         const uint32_t d = tmem + (uint32_t)(z * BN);
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                         mma_tf32(d, alo + koff, bhi + koff, idesc, acc);
-                        mma_tf32(d, ahi + koff, blo + koff, idesc, 1u);
+                        if (two_b) mma_tf32(d, ahi + koff, blo + koff, idesc, 1u);
                         mma_tf32(d, ahi + koff, bhi + koff, idesc, 1u);
                     }
                 }
@@ -644,15 +661,15 @@ inline unsigned grid_cap(const Device* d, uint64_t items) {
 // Writes the K-major hi/lo terms of an operand; `kmajor` says whether the stored matrix
 // already has k contiguous ([rows, k]) or is [k, rows] and must be transposed.
 mg_status split_operand(Device* d, const float* src, uint64_t rows, uint64_t k, bool kmajor, float* hi, float* lo,
-                        uint64_t kp) {
+                        uint64_t kp, int* lo_nonzero = nullptr) {
     if (kmajor) {
         const int vec = k == kp && k % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
         enqueue(d, split_rows_kernel, grid_cap(d, vec ? rows * kp / 4 : rows * kp), 256, 0, src, k, rows, k, hi, lo,
-                                                                                              kp, vec);
+                                                                                              kp, vec, lo_nonzero);
     } else {
         dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((kp + 63) / 64));
         if (grid.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "matmul inner dimension %llu is too large", (unsigned long long)k);
-        enqueue(d, split_transpose_kernel, grid, 256, 0, src, k, rows, hi, lo, kp);
+        enqueue(d, split_transpose_kernel, grid, 256, 0, src, k, rows, hi, lo, kp, lo_nonzero);
     }
     return launched(d, "operand split kernel launch");
 }
@@ -852,6 +869,11 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
     // raw B may load early when it is a weight (nothing earlier in the stream writes it)
     p.b_early = (b_raw ? g.b_stable != 0 : stable) ? 1 : 0;
     p.prefetch = g.m <= 128 ? 1 : 0;
+    // One B term when every weight read is a prepared form whose lo term is all zero.
+    bool one_term = !b_raw;
+    for (int w = 0; w < nw && one_term; w++)
+        one_term = (nb == 2 ? g.b_prep[w] && g.b_one_term[w] : gs[w].b_prep[0] && gs[w].b_one_term[0]) != 0;
+    p.b_terms = one_term ? 1 : 2;
     p.groups = count;
     for (int i = 0; i < 3; i++) {
         p.outs[i] = i < count ? gs[i].out : nullptr;
@@ -976,9 +998,10 @@ bool gemm_uses_tensor_cores(uint64_t m, uint64_t n, uint64_t k, int transpose_b,
     return tensor_cores_enabled() && m > 16;
 }
 
-mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int transposed, float* dst) {
+mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int transposed, float* dst,
+                         int* lo_nonzero) {
     const uint64_t kp = gemm_kp(k);
-    return split_operand(d, b, n, k, transposed != 0, dst, dst + n * kp, kp);
+    return split_operand(d, b, n, k, transposed != 0, dst, dst + n * kp, kp, lo_nonzero);
 }
 
 mg_status gemm(Device* d, const GemmArgs& g) {

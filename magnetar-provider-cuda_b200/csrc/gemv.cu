@@ -454,28 +454,47 @@ __device__ __forceinline__ float4 unpack4(uint64_t lo, uint64_t hi) {
 // From 8 rows up, a transposer warp rewrites each stage's A tile as [32 k][M] so that the
 // compute warps read A in pairs of rows (one packed FMA per pair and column, B duplicated
 // once per column) instead of duplicating every A value.
-template <int M>
+//
+// H: B is a compact weight, its values stored as bfloat16 bits (each exactly its f32 value);
+// a stage carries half the bytes of B, the ring holds more stages, and each value is widened
+// back to the same f32 in registers -- the arithmetic and its order are those of the f32 form,
+// so the results are bit-identical.
+template <int M, bool H = false>
 struct GemvCShape {
     static constexpr bool kTrans = M >= 8;
     static constexpr int kThreads = (kWarps + 1 + (kTrans ? 1 : 0)) * 32;
-    static constexpr int kB = kChunkRows * kCols * 4;  // 16 KB of B per stage
+    static constexpr int kStages = H ? (M >= 16 ? 7 : 8) : kCStages;
+    static constexpr int kB = kChunkRows * kCols * (H ? 2 : 4);  // 16 KB (8 KB compact) of B per stage
     static constexpr int kA = M * kChunkRows * 4;      // [M][32] of A per stage
     static constexpr int kStage = kB + kA;
-    static constexpr int kRing = kCStages * kStage;
-    static constexpr int kAT = kTrans ? kCStages * kA : 0;  // the transposed A tiles, [32][M] per stage
+    static constexpr int kRing = kStages * kStage;
+    static constexpr int kAT = kTrans ? kStages * kA : 0;  // the transposed A tiles, [32][M] per stage
     static constexpr int kPart = M * kCols * 4;         // this CTA's partial [M][128]
     static constexpr int kRecv = (M * kCols + 4 * kMaxClusterCtas) * 4;  // the other CTAs' partials of this CTA's band
     static_assert(kWarps * kPart <= kRing, "the warp partials fit the drained ring");
-    static constexpr int kSmem = 128 + kRing + kAT + kPart + kRecv + 8 * (3 * kCStages + 1);
+    static constexpr int kSmem = 128 + kRing + kAT + kPart + kRecv + 8 * (3 * kStages + 1);
 };
 
-template <int M>
-__global__ void __launch_bounds__(GemvCShape<M>::kThreads, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
+// Four consecutive columns of row `row` of a B stage, as f32.
+template <bool H>
+__device__ __forceinline__ float4 gemv_b4(const uint8_t* tile, int row, int lane) {
+    if constexpr (H) {
+        const uint2 u = *reinterpret_cast<const uint2*>(tile + (row * kCols + 4 * lane) * 2);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                           __uint_as_float(u.y & 0xFFFF0000u));
+    } else {
+        return *reinterpret_cast<const float4*>(tile + (row * kCols + 4 * lane) * 4);
+    }
+}
+
+template <int M, bool H>
+__global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                           const __grid_constant__ CUtensorMap map_b,
                                                                           const __grid_constant__ CUtensorMap map_b2,
                                                                           GemvClusterArgs p) {
     using namespace sm100;
-    using S = GemvCShape<M>;
+    using S = GemvCShape<M, H>;
+    constexpr int kCStages = S::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 127u) & ~127u;
@@ -570,13 +589,13 @@ __global__ void __launch_bounds__(GemvCShape<M>::kThreads, 2) gemv_cluster_kerne
                 atomicExch(p.error, 1);
                 break;
             }
-            const float* tile = reinterpret_cast<const float*>(base_ptr + s * S::kStage);
+            const uint8_t* tile = base_ptr + s * S::kStage;
             const int rr = warp * 4;  // this warp's 4 rows of the stage
             if constexpr (S::kTrans) {
                 const float* att = atf + s * kChunkRows * M;  // [32][M]
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const float4 bv = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+                    const float4 bv = gemv_b4<H>(tile, rr + u, lane);
                     const uint64_t bd[4] = {pack2(bv.x, bv.x), pack2(bv.y, bv.y), pack2(bv.z, bv.z), pack2(bv.w, bv.w)};
 #pragma unroll
                     for (int q = 0; q < M / 4; q++) {
@@ -594,7 +613,7 @@ __global__ void __launch_bounds__(GemvCShape<M>::kThreads, 2) gemv_cluster_kerne
                 uint64_t b01[4], b23[4];
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const float4 bv = *reinterpret_cast<const float4*>(tile + (rr + u) * kCols + 4 * lane);
+                    const float4 bv = gemv_b4<H>(tile, rr + u, lane);
                     b01[u] = pack2(bv.x, bv.y);
                     b23[u] = pack2(bv.z, bv.w);
                 }
@@ -679,6 +698,21 @@ __global__ void __launch_bounds__(GemvCShape<M>::kThreads, 2) gemv_cluster_kerne
     cluster_wait();  // phase 2: every copy out of this CTA's shared memory has landed
 }
 
+// Row-major [k, n] bfloat16 bits of a compact B, box [kChunkRows x kCols], no swizzle.
+mg_status gemv_map_compact(CUtensorMap* map, const uint16_t* b, uint64_t k, uint64_t n) {
+    auto fn = gemv_encode_fn();
+    if (!fn) return mg::fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {n, k};
+    cuuint64_t strides[1] = {n * sizeof(uint16_t)};
+    cuuint32_t box[2] = {kCols, kChunkRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(b), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return mg::fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
 // Row-major [m, k] f32 A, box [32 x mp] (rows past m read as zero).
 mg_status gemv_a_map(CUtensorMap* map, const float* a, uint64_t m, uint64_t k, uint32_t mp) {
     auto fn = gemv_encode_fn();
@@ -706,14 +740,14 @@ void gemv_slices(GemvClusterArgs& p, uint64_t splits) {
     p.band = ((F + nc - 1) / nc + 3) / 4 * 4;
 }
 
-template <int M>
+template <int M, bool H>
 mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const CUtensorMap* maps) {
-    using S = GemvCShape<M>;
+    using S = GemvCShape<M, H>;
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
-        MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+        MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M, H>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
                 "configuring the cluster gemv kernel");
-        MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+        MG_CUDA(cudaFuncSetAttribute(gemv_cluster_kernel<M, H>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
                 "allowing the cluster gemv kernel clusters of up to 16");
         configured[d->ordinal & 63] = true;
     }
@@ -735,7 +769,7 @@ mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const
             q.attrs = &ca;
             q.numAttrs = 1;
             int clusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_cluster_kernel<M>, &q) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_cluster_kernel<M, H>, &q) != cudaSuccess) {
                 (void)cudaGetLastError();
                 clusters = 0;
             }
@@ -758,13 +792,38 @@ mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = d->pdl ? 2 : 1;
-    MG_CUDA(cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<M>, maps[0], maps[1], maps[2], p), "cluster gemv launch");
+    MG_CUDA(cudaLaunchKernelEx(&cfg, gemv_cluster_kernel<M, H>, maps[0], maps[1], maps[2], p), "cluster gemv launch");
     return launched(d, "cluster gemv launch");
+}
+
+// dst[i] = the bfloat16 bits of src[i]; *not_exact is set when some value is not exactly a
+// bfloat16 value (nonzero low 16 bits), and dst is then not used.
+__global__ void __launch_bounds__(256) compact_bf16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst,
+                                                           uint64_t quads, int* not_exact) {
+    uint32_t low = 0;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float4 v = src[i];
+        const uint32_t x = __float_as_uint(v.x), y = __float_as_uint(v.y), z = __float_as_uint(v.z), w = __float_as_uint(v.w);
+        low |= (x | y | z | w) & 0xFFFFu;
+        dst[i] = make_uint2((x >> 16) | (y & 0xFFFF0000u), (z >> 16) | (w & 0xFFFF0000u));
+    }
+    if (__syncthreads_or(low != 0) && threadIdx.x == 0) atomicExch(not_exact, 1);
 }
 
 }  // namespace
 
 namespace k {
+
+mg_status gemv_compact_b(Device* d, const float* b, uint16_t* dst, uint64_t count, int* not_exact) {
+    if (count % 4 != 0 || (reinterpret_cast<uintptr_t>(b) & 15) != 0)
+        return fail(MG_LAYOUT_UNSUPPORTED, "a compact weight needs a multiple of 4 values, 16-byte aligned");
+    const uint64_t quads = count / 4;
+    uint64_t blocks = (quads + 255) / 256;
+    if (blocks > (uint64_t)d->sm_count * 8) blocks = (uint64_t)d->sm_count * 8;
+    enqueue(d, compact_bf16_kernel, (unsigned)(blocks ? blocks : 1), 256, 0, reinterpret_cast<const float4*>(b),
+            reinterpret_cast<uint2*>(dst), quads, not_exact);
+    return launched(d, "weight compaction launch");
+}
 
 // Eligible when M <= 16, B is not transposed and its rows are 16-byte aligned.
 bool gemv_eligible(const GemmArgs& g) {
@@ -871,17 +930,32 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     gemv_slices(p, splits);
     p.b_early = g.b_stable ? 1 : 0;
     p.error = d->flags + 2;
+    // Compact weights (every value exactly bfloat16) stream as their bfloat16 bits: B and, gated,
+    // the up weight both, or neither.
+    const bool h = g.b16[0] && (!g.gated || g.b16[1]);
     CUtensorMap maps[3];
     MG_TRY(gemv_a_map(&maps[0], g.a, g.m, g.k, (uint32_t)mp));
+    if (h) {
+        MG_TRY(gemv_map_compact(&maps[1], g.b16[0], g.k, g.n));
+        if (g.gated) MG_TRY(gemv_map_compact(&maps[2], g.b16[1], g.k, g.n));
+        else maps[2] = maps[1];
+        switch (mp) {
+            case 1: return launch_cluster<1, true>(d, p, col_tiles, maps);
+            case 2: return launch_cluster<2, true>(d, p, col_tiles, maps);
+            case 4: return launch_cluster<4, true>(d, p, col_tiles, maps);
+            case 8: return launch_cluster<8, true>(d, p, col_tiles, maps);
+            default: return launch_cluster<16, true>(d, p, col_tiles, maps);
+        }
+    }
     MG_TRY(gemv_map(&maps[1], g.b, g.k, g.n));
     if (g.gated) MG_TRY(gemv_map(&maps[2], g.b2, g.k, g.n));
     else maps[2] = maps[1];
     switch (mp) {
-        case 1: return launch_cluster<1>(d, p, col_tiles, maps);
-        case 2: return launch_cluster<2>(d, p, col_tiles, maps);
-        case 4: return launch_cluster<4>(d, p, col_tiles, maps);
-        case 8: return launch_cluster<8>(d, p, col_tiles, maps);
-        default: return launch_cluster<16>(d, p, col_tiles, maps);
+        case 1: return launch_cluster<1, false>(d, p, col_tiles, maps);
+        case 2: return launch_cluster<2, false>(d, p, col_tiles, maps);
+        case 4: return launch_cluster<4, false>(d, p, col_tiles, maps);
+        case 8: return launch_cluster<8, false>(d, p, col_tiles, maps);
+        default: return launch_cluster<16, false>(d, p, col_tiles, maps);
     }
 }
 

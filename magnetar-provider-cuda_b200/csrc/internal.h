@@ -111,7 +111,20 @@ struct Buffer {
     float* prep = nullptr;
     uint64_t prep_n = 0, prep_k = 0, prep_kp = 0;
     int prep_transposed = -1;
+    // Every lo term of the prepared form is zero: the weight's values are exactly tf32 (as every
+    // bfloat16 checkpoint's are), and the tensor-core matmul reads and multiplies hi alone.
+    bool prep_one_term = false;
+    // A compact weight: a matrix of at least kCompactMinElements values, every one exactly a
+    // bfloat16 value, also kept as its bfloat16 bits ([k, n] as stored), which the few-row matmul
+    // streams instead of the f32 values -- half the bytes, the same results.  Built on the first
+    // such matmul that reads the weight, dropped with the prepared form.  compact_state: 0 not yet
+    // checked, 1 built, -1 some value is not exactly bfloat16.
+    uint16_t* compact = nullptr;
+    int compact_state = 0;
 };
+
+// Weights smaller than this stay f32 only (src/kernels.rs:506-510).
+constexpr uint64_t kCompactMinElements = 1ull << 16;
 
 // Drops a weight's prepared operand form (its contents are about to change).
 void buffer_drop_prep(Buffer* b);
@@ -212,13 +225,24 @@ struct GemmArgs {
     // The prepared forms existed before this call: no kernel earlier in the stream writes
     // them, so the GEMM may start loading them before it waits on its predecessor.
     int b_stable;
+    // The prepared form's lo term is all zero (b / b2's values are exactly tf32).
+    int b_one_term[2];
+    // Compact (bfloat16-bit) forms of b / b2 for the few-row path; null = read the f32 values.
+    const uint16_t* b16[2];
 };
 mg_status gemm(Device* d, const GemmArgs& g);
+// Writes the bfloat16 bits of b's `count` values to dst; sets *not_exact (a device word) when
+// some value is not exactly a bfloat16 value.
+mg_status gemv_compact_b(Device* d, const float* b, uint16_t* dst, uint64_t count, int* not_exact);
 // Round-up of k the tensor-core path stores operands with.
 inline uint64_t gemm_kp(uint64_t k) { return (k + 3) & ~3ull; }
 // Fills dst ([n, kp] hi then [n, kp] lo) with the K-major tf32 terms of B ([k, n] row-major,
 // or [n, k] when transposed).
-mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int transposed, float* dst);
+// `lo_nonzero` (optional device word): set when any lo term is nonzero.
+mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int transposed, float* dst,
+                         int* lo_nonzero = nullptr);
+// Whether the few-row (M <= 16) path takes a matmul.
+bool gemv_eligible(const GemmArgs& g);
 // Whether a matmul of these dimensions takes the tensor-core path (and so reads a prepared B).
 bool gemm_uses_tensor_cores(uint64_t m, uint64_t n, uint64_t k, int transpose_b, const float* b);
 

@@ -116,12 +116,14 @@ enum AddendMode { kNone = 0, kRow = 1, kFull = 2 };
 
 // The prepared tensor-core operand form of a weight read as matmul B, built on first use.
 mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int transposed, const float** out,
-                      bool* built) {
+                      bool* built, int* one_term) {
     *out = nullptr;
+    *one_term = 0;
     if (!cb || !cb->is_weight) return MG_OK;
     Buffer* b = const_cast<Buffer*>(cb);  // the prepared form is a cache of the buffer's contents
     if (b->prep && b->prep_n == n && b->prep_k == k && b->prep_transposed == transposed) {
         *out = b->prep;
+        *one_term = b->prep_one_term ? 1 : 0;
         return MG_OK;
     }
     *built = true;
@@ -129,17 +131,57 @@ mg_status weight_prep(Device* d, const Buffer* cb, uint64_t k, uint64_t n, int t
     const uint64_t kp = k::gemm_kp(k);
     void* mem = nullptr;
     MG_TRY(device_alloc(d, 2 * n * kp * sizeof(float), &mem));
-    mg_status s = k::gemm_prepare_b(d, (const float*)b->ptr, k, n, transposed, (float*)mem);
+    // Whether the lo term is all zero is read back once, here (never while a capture records:
+    // such a weight keeps both terms).
+    int* lo_flag = d->capturing ? nullptr : d->flags + 3;
+    if (lo_flag) MG_CUDA(cudaMemsetAsync(lo_flag, 0, sizeof(int), d->stream), "resetting the lo flag");
+    mg_status s = k::gemm_prepare_b(d, (const float*)b->ptr, k, n, transposed, (float*)mem, lo_flag);
+    int flags[4] = {0, 0, 0, 1};
+    if (s == MG_OK && lo_flag) s = read_flags(d, flags);
     if (s != MG_OK) {
         device_free(d, mem);
         return s;
     }
+    b->prep_one_term = flags[3] == 0;
     b->prep = (float*)mem;
     b->prep_n = n;
     b->prep_k = k;
     b->prep_kp = kp;
     b->prep_transposed = transposed;
     *out = b->prep;
+    *one_term = b->prep_one_term ? 1 : 0;
+    return MG_OK;
+}
+
+// The compact form of a weight read as the few-row matmul's B (src/kernels.rs:1668-1712: a
+// matrix of at least 65536 values, all exactly bfloat16, is kept as bfloat16 bits): built and
+// checked on first use -- one read-back, never while a capture records -- then reused until
+// the weight's contents change.  Null when the weight is not compact.
+mg_status weight_compact(Device* d, const Buffer* cb, uint64_t k, uint64_t n, const uint16_t** out) {
+    *out = nullptr;
+    Buffer* b = const_cast<Buffer*>(cb);  // the compact form is a cache of the buffer's contents
+    if (!b->is_weight || b->rank != 2 || b->count < kCompactMinElements || b->count != k * n || n % 8 != 0) return MG_OK;
+    if (b->compact_state == 1) {
+        *out = b->compact;
+        return MG_OK;
+    }
+    if (b->compact_state < 0 || d->capturing) return MG_OK;
+    void* mem = nullptr;
+    MG_TRY(device_alloc(d, b->count * sizeof(uint16_t), &mem));
+    int* flag = d->flags + 3;
+    const cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), d->stream);
+    mg_status s = e == cudaSuccess ? MG_OK : from_cuda(e, "resetting the compact flag");
+    if (s == MG_OK) s = k::gemv_compact_b(d, (const float*)b->ptr, (uint16_t*)mem, b->count, flag);
+    int flags[4] = {0, 0, 0, 1};
+    if (s == MG_OK) s = read_flags(d, flags);
+    if (s != MG_OK || flags[3] != 0) {
+        device_free(d, mem);
+        if (s == MG_OK) b->compact_state = -1;
+        return s;
+    }
+    b->compact = (uint16_t*)mem;
+    b->compact_state = 1;
+    *out = b->compact;
     return MG_OK;
 }
 
@@ -206,16 +248,21 @@ mg_status matmul_plan(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
     g.transpose_b = tb;
     g.gated = b2 ? 1 : 0;
     g.b_prep[0] = g.b_prep[1] = nullptr;
+    g.b16[0] = g.b16[1] = nullptr;
     if (k::gemm_uses_tensor_cores(m, n, kk, tb, g.b)) {
         bool built = false;
-        MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0], &built));
-        if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1], &built));
+        MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0], &built, &g.b_one_term[0]));
+        if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1], &built, &g.b_one_term[1]));
         g.b_stable = !built && g.b_prep[0] && (!b2 || g.b_prep[1]);
     } else {
         // The GEMV path reads B as it is: before its dependency wait when B is a weight that
         // the preceding kernel cannot have written.
         auto settled = [](const Buffer* w) { return w->is_weight && !w->weight_fresh; };
         g.b_stable = settled(b) && (!b2 || settled(b2));
+        if (k::gemv_eligible(g)) {
+            MG_TRY(weight_compact(d, b, kk, n, &g.b16[0]));
+            if (b2) MG_TRY(weight_compact(d, b2, kk, n, &g.b16[1]));
+        }
         const_cast<Buffer*>(b)->weight_fresh = false;
         if (b2) const_cast<Buffer*>(b2)->weight_fresh = false;
     }

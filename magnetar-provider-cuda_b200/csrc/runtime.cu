@@ -181,6 +181,10 @@ void buffer_drop_prep(Buffer* b) {
     b->prep = nullptr;
     b->prep_n = b->prep_k = b->prep_kp = 0;
     b->prep_transposed = -1;
+    b->prep_one_term = false;
+    if (b->compact) device_free(b->device, b->compact);
+    b->compact = nullptr;
+    b->compact_state = 0;
 }
 
 void buffer_free(Buffer* b) {
@@ -556,6 +560,8 @@ mg_status mg_buffer_reshape(mg_buffer* h, int rank, const uint64_t* shape) {
 }
 
 void* mg_buffer_device_ptr(const mg_buffer* h) { return h ? buf(h)->ptr : nullptr; }
+
+int mg_buffer_is_compact(const mg_buffer* h) { return h && buf(h)->compact_state == 1 ? 1 : 0; }
 
 mg_status mg_buffer_set_weight(mg_buffer* h, int is_weight) {
     if (!h) return fail(MG_INVALID_ARGUMENT, "null buffer");

@@ -72,6 +72,18 @@ class DeviceBuffer:
         check(N.lib().mg_buffer_set_weight(self._h, 1 if is_weight else 0))
         return self
 
+    def write(self, array) -> "DeviceBuffer":
+        """Overwrites the buffer with host f32 values of the same element count (a weight
+        drops its prepared and compact forms)."""
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        check(N.lib().mg_buffer_upload_f32(self._h, a.ctypes.data, a.size))
+        return self
+
+    def is_compact(self) -> bool:
+        """Whether this weight holds its compact (bfloat16-bit) form, which the few-row matmul
+        streams in place of the f32 values (``CudaDeviceBuffer::is_compact``)."""
+        return bool(N.lib().mg_buffer_is_compact(self._h))
+
     def release(self) -> None:
         if self._h and self._h.value:
             N.lib().mg_buffer_release(self._h)

@@ -572,3 +572,122 @@ def test_batched_matmul_shape_errors(kernels, mpc):
         with pytest.raises(mpc.CudaError) as e:
             kernels.batched_matmul(a, kernels.upload(b), groups, tb)
         assert e.value.code == "ShapeUnsupported"
+
+
+def _bf16_exact(x):
+    return (np.asarray(x, np.float32).view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 512, 384), (200, 904, 136), (2048, 256, 256), (128, 1024, 512)])
+def test_matmul_with_an_exact_weight_drops_its_lo_term(kernels, oracle, m, k, n):
+    # A weight whose values are exactly bfloat16 (so tf32): its prepared lo term is zero and the
+    # matmul reads and multiplies hi alone -- bit-identical to multiplying the zero term as well
+    # (the per-call split of the same values, which keeps all three products), and to the oracle
+    # within the matmul tolerance.
+    r = rng(22)
+    a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
+    b = _bf16_exact(r.standard_normal((k, n)))
+    da = kernels.upload(a)
+    db = kernels.upload(b).set_weight()
+    first = kernels.download(kernels.matmul(da, db))
+    second = kernels.download(kernels.matmul(da, db))
+    assert rel(first, oracle.matmul(a, b)) <= TOL_MATMUL
+    np.testing.assert_array_equal(first, second)
+    if m > 128:  # the per-call form goes through the same kernel (B split into a scratch form)
+        np.testing.assert_array_equal(second, kernels.download(kernels.matmul(da, kernels.upload(b))))
+
+
+@pytest.mark.parametrize("exact_up", [True, False])
+def test_gated_matmul_with_exact_weights(kernels, oracle, exact_up):
+    r = rng(23)
+    m, k, n = 256, 512, 320
+    a = r.standard_normal((m, k)).astype(np.float32)
+    g = _bf16_exact(r.standard_normal((k, n)) * 0.05)
+    u = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    if exact_up:
+        u = _bf16_exact(u)
+    da, dg, du = kernels.upload(a), kernels.upload(g).set_weight(), kernels.upload(u).set_weight()
+    got = kernels.download(kernels.gated_matmul(da, dg, du))
+    got2 = kernels.download(kernels.gated_matmul(da, dg, du))
+    assert rel(got, oracle.gated_matmul(a, g, u)) <= TOL_MATMUL
+    np.testing.assert_array_equal(got, got2)
+    np.testing.assert_array_equal(got2, kernels.download(kernels.gated_matmul(da, kernels.upload(g), kernels.upload(u))))
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 512, 256), (3, 1024, 1000), (8, 256, 512), (16, 640, 384), (1, 4096, 4096)])
+def test_compact_weight_gemv_is_bit_identical(kernels, oracle, m, k, n):
+    # src/tests_conformance.rs:2564-2640: a weight whose values are all exactly bfloat16 is kept
+    # compact and gives bit-identical matmul / bias / residual results to the same values
+    # stored as f32 (here: the same values in a plain, non-weight buffer).
+    r = rng(24)
+    a = r.standard_normal((m, k)).astype(np.float32)
+    b = _bf16_exact(r.standard_normal((k, n)) / math.sqrt(k))
+    bias = r.standard_normal(n).astype(np.float32)
+    res = r.standard_normal((m, n)).astype(np.float32)
+    da, dbias, dres = kernels.upload(a), kernels.upload(bias), kernels.upload(res)
+    w = kernels.upload(b).set_weight()
+    full = kernels.upload(b)
+    assert not w.is_compact()
+    got = kernels.download(kernels.matmul(da, w))
+    assert w.is_compact() and not full.is_compact()
+    np.testing.assert_array_equal(got, kernels.download(kernels.matmul(da, full)))
+    assert rel(got, oracle.matmul(a, b)) <= TOL_MATMUL
+    np.testing.assert_array_equal(kernels.download(kernels.matmul_bias(da, w, dbias)),
+                                  kernels.download(kernels.matmul_bias(da, full, dbias)))
+    np.testing.assert_array_equal(kernels.download(kernels.matmul_residual(da, w, dres)),
+                                  kernels.download(kernels.matmul_residual(da, full, dres)))
+    np.testing.assert_array_equal(kernels.download(w), b)  # the f32 values stay readable
+
+
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_compact_gated_gemv_is_bit_identical(kernels, oracle, m):
+    r = rng(25)
+    k, n = 768, 512
+    a = r.standard_normal((m, k)).astype(np.float32)
+    g = _bf16_exact(r.standard_normal((k, n)) * 0.05)
+    u = _bf16_exact(r.standard_normal((k, n)) * 0.05)
+    da = kernels.upload(a)
+    dg, du = kernels.upload(g).set_weight(), kernels.upload(u).set_weight()
+    got = kernels.download(kernels.gated_matmul(da, dg, du))
+    assert dg.is_compact() and du.is_compact()
+    np.testing.assert_array_equal(got, kernels.download(kernels.gated_matmul(da, kernels.upload(g), kernels.upload(u))))
+    assert rel(got, oracle.gated_matmul(a, g, u)) <= TOL_MATMUL
+    # one compact and one f32 weight: both stream as f32
+    u2 = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    du2 = kernels.upload(u2).set_weight()
+    got2 = kernels.download(kernels.gated_matmul(da, dg, du2))
+    assert not du2.is_compact()
+    np.testing.assert_array_equal(got2, kernels.download(kernels.gated_matmul(da, kernels.upload(g), kernels.upload(u2))))
+
+
+def test_non_exact_or_small_weights_stay_f32(kernels):
+    r = rng(26)
+    a = r.standard_normal((2, 256)).astype(np.float32)
+    da = kernels.upload(a)
+    small = kernels.upload(_bf16_exact(r.standard_normal((256, 128)))).set_weight()  # 32768 values
+    inexact = kernels.upload(r.standard_normal((256, 512)).astype(np.float32)).set_weight()
+    kernels.matmul(da, small)
+    kernels.matmul(da, inexact)
+    kernels.synchronize()
+    assert not small.is_compact() and not inexact.is_compact()
+
+
+def test_rewriting_a_compact_weight_drops_its_compact_form(kernels, oracle):
+    r = rng(27)
+    a = r.standard_normal((1, 512)).astype(np.float32)
+    da = kernels.upload(a)
+    b = _bf16_exact(r.standard_normal((512, 256)))
+    w = kernels.upload(b).set_weight()
+    kernels.matmul(da, w)
+    assert w.is_compact()
+    b2 = r.standard_normal((512, 256)).astype(np.float32)  # not exact: stays f32 after the write
+    w.write(b2)
+    assert not w.is_compact()
+    got = kernels.download(kernels.matmul(da, w))
+    assert not w.is_compact()
+    np.testing.assert_array_equal(got, kernels.download(kernels.matmul(da, kernels.upload(b2))))
+    b3 = _bf16_exact(r.standard_normal((512, 256)))
+    w.write(b3)
+    got3 = kernels.download(kernels.matmul(da, w))
+    assert w.is_compact()
+    np.testing.assert_array_equal(got3, kernels.download(kernels.matmul(da, kernels.upload(b3))))
