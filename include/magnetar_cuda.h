@@ -228,6 +228,15 @@ mg_status mg_rope(mg_device* d, const mg_buffer* x, const mg_rope_params* params
  * rows is MG_SHAPE_UNSUPPORTED. */
 mg_status mg_kv_write(mg_device* d, mg_buffer* store, const mg_buffer* rows, uint64_t row_offset);
 
+/* Greedy selection (src/kernels.rs:4441-4488, `keep-sampling-on-device`): the column of row `row`
+ * of the logits (the last dimension's columns) with the highest score / temperature (the score as
+ * is when temperature is 0), among columns whose raw score is finite and which lie outside each
+ * of the `excluded_count` [start, end) pairs in `excluded` ([2 * count] uint64); ties, -0 against
+ * +0 included, go to the lowest column.  *found = 0 when no column is eligible.  A row past the
+ * logits is MG_SHAPE_UNSUPPORTED; it reads its result back (not capturable). */
+mg_status mg_greedy_select(mg_device* d, const mg_buffer* logits, uint64_t row, const uint64_t* excluded,
+                           uint32_t excluded_count, float temperature, int* found, uint64_t* column);
+
 /* softmax over the rows of a rank-2 buffer; MG_EXECUTION_FAILED when a row has no finite
  * maximum (src/kernels.rs:4357-4386). */
 mg_status mg_softmax(mg_device* d, const mg_buffer* x, mg_buffer** out);
@@ -329,6 +338,10 @@ mg_status mg_executor_read_tensor(mg_executor* ex, const char* id, float* data, 
                                   int* rank, uint64_t* shape);
 mg_status mg_executor_read_tensor_rows(mg_executor* ex, const char* id, uint64_t first_row,
                                        uint64_t rows, float* data, uint64_t capacity);
+/* select_greedy_column (src/executor.rs:2549-2563): mg_greedy_select over a resident tensor. */
+mg_status mg_executor_select_greedy_column(mg_executor* ex, const char* id, uint64_t row, const uint64_t* excluded,
+                                           uint32_t excluded_count, float temperature, int* found,
+                                           uint64_t* column);
 /* *released = 1 when a resource was dropped (src/executor.rs release_tensor). */
 mg_status mg_executor_release_tensor(mg_executor* ex, const char* id, int* released);
 /* *present = 0 when the id is not resident. */

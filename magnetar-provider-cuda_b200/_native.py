@@ -134,6 +134,7 @@ SIGNATURES = {
     "mg_rmsnorm": [_P, _P, _P, _F, _U64, _U64, _PP],
     "mg_rope": [_P, _P, ctypes.POINTER(RopeParams), _PP],
     "mg_softmax": [_P, _P, _PP],
+    "mg_greedy_select": [_P, _P, _U64, _U64P, ctypes.c_uint32, _F, _IP, _U64P],
     "mg_kv_write": [_P, _P, _P, _U64],
     "mg_gelu_tanh": [_P, _P, _PP],
     "mg_sigmoid": [_P, _P, _PP],
@@ -157,6 +158,7 @@ SIGNATURES = {
     "mg_executor_buffer": [_P, _S, _PP],
     "mg_executor_read_tensor": [_P, _S, _P, _U64, _IP, _U64P],
     "mg_executor_read_tensor_rows": [_P, _S, _U64, _U64, _P, _U64],
+    "mg_executor_select_greedy_column": [_P, _S, _U64, _U64P, ctypes.c_uint32, _F, _IP, _U64P],
     "mg_executor_release_tensor": [_P, _S, _IP],
     "mg_executor_resident_shape": [_P, _S, _IP, _IP, _U64P],
     "mg_executor_copy_tensor": [_P, _S, _S],
@@ -202,6 +204,13 @@ def build(force: bool = False) -> str:
         subprocess.run(["make", "-C", CSRC, "clean"], check=True, stdout=subprocess.DEVNULL)
     subprocess.run(["make", "-C", CSRC, "-j", jobs], check=True, stdout=subprocess.DEVNULL)
     return LIB_PATH
+
+
+def range_pairs(ranges):
+    """(start, end) ranges as a [2 * count] uint64 array for the C ABI, and the count."""
+    flat = [int(v) for r in ranges for v in (r[0], r[1])]
+    arr = (ctypes.c_uint64 * max(1, len(flat)))(*flat)
+    return arr, len(flat) // 2
 
 
 def lib():

@@ -840,6 +840,21 @@ mg_status mg_executor_read_tensor(mg_executor* ex, const char* id, float* data, 
     return mg_buffer_download_f32(H(b), data, b->count);
 }
 
+// src/executor.rs:2549-2563: greedy selection over a resident logits tensor.
+mg_status mg_executor_select_greedy_column(mg_executor* ex, const char* id, uint64_t row, const uint64_t* excluded,
+                                           uint32_t excluded_count, float temperature, int* found, uint64_t* column) {
+    if (!ex || !id || !found || !column) return fail(MG_INVALID_ARGUMENT, "null argument");
+    *found = 0;
+    Buffer* b;
+    {
+        std::lock_guard<std::mutex> g(ex->lock);
+        auto it = ex->storage.find(id);
+        if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", id);
+        b = it->second;
+    }
+    return mg_greedy_select(ex->handle, H(b), row, excluded, excluded_count, temperature, found, column);
+}
+
 mg_status mg_executor_read_tensor_rows(mg_executor* ex, const char* id, uint64_t first_row, uint64_t rows, float* data,
                                        uint64_t capacity) {
     if (!ex || !id) return fail(MG_INVALID_ARGUMENT, "null argument");

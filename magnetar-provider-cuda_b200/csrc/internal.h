@@ -50,8 +50,10 @@ struct Device {
     // mg_device_close still frees into a live pool.  A closed device refuses new work.
     std::atomic<int> refs{1};
     std::atomic<bool> closed{false};
-    // Device-side status words of the data-dependent checks: [0] invalid embedding id,
-    // [1] non-finite softmax row.  Pinned host mirror for the read back.
+    // Device-side words (128 bytes): ints [0] invalid embedding id, [1] non-finite softmax row,
+    // [2] kernel wait timeout, [3] a weight's lo term / compact check; bytes 32..39 the step
+    // offset; 64..87 greedy selection's running max, ticket and result.  Pinned host mirror
+    // (64 bytes) for the read backs.
     int* flags = nullptr;
     int* host_flags = nullptr;
     // The offset a captured step's advancing attributes add, read by its kernels at run time
@@ -176,6 +178,10 @@ mg_status kv_write(Device* d, const KvWriteArgs& a);
 // *dst = value, in stream order (a captured step's offset before its replay).
 mg_status set_step_offset(Device* d, uint64_t* dst, uint64_t value);
 
+// The largest greedy-selection key of a logits row (0: no column eligible); `excluded` holds
+// `count` host [start, end) pairs.  Reads the key back (synchronises the stream).
+mg_status greedy_select(Device* d, const float* row, uint64_t cols, const uint64_t* excluded, uint32_t count,
+                        float temperature, uint64_t* key);
 mg_status embedding(Device* d, const float* table, const float* ids, float* out, uint64_t dim,
                     uint64_t num_ids, uint64_t vocab, int* flag, int has_scale, float scale);
 mg_status rmsnorm(Device* d, const float* x, const float* w, float* out, uint64_t rows,

@@ -762,6 +762,35 @@ mg_status rope_plan(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp,
 extern "C" {
 
 // src/kernels.rs:4357-4386
+// src/kernels.rs:4441-4488: the column of one logits row with the highest score over the
+// temperature, among finite scores outside the excluded ranges; *found = 0 when none is eligible.
+mg_status mg_greedy_select(mg_device* h, const mg_buffer* lh, uint64_t row, const uint64_t* excluded,
+                           uint32_t excluded_count, float temperature, int* found, uint64_t* column) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(lh, "logits"));
+    if (!found || !column || (excluded_count && !excluded)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    *found = 0;
+    *column = 0;
+    Device* d = dev(h);
+    const Buffer* l = buf(lh);
+    MG_TRY(same_device(d, l));
+    MG_TRY(require_f32(l, "greedy selection's logits"));
+    if (l->rank < 1) return fail(MG_SHAPE_UNSUPPORTED, "logits have no columns");
+    const uint64_t cols = l->shape[l->rank - 1];
+    const uint64_t rows = l->count / (cols ? cols : 1);
+    if (cols == 0 || row >= rows || cols > 0xFFFFFFFFull)
+        return fail(MG_SHAPE_UNSUPPORTED, "no logits row %llu of %llu rows of %llu columns", (unsigned long long)row,
+                    (unsigned long long)rows, (unsigned long long)cols);
+    if (d->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "greedy selection reads its result on the host and cannot be captured");
+    uint64_t key = 0;
+    MG_TRY(k::greedy_select(d, (const float*)l->ptr + row * cols, cols, excluded, excluded_count, temperature, &key));
+    if (key) {
+        *found = 1;
+        *column = 0xFFFFFFFFull - (key & 0xFFFFFFFFull);
+    }
+    return MG_OK;
+}
+
 mg_status mg_softmax(mg_device* h, const mg_buffer* xh, mg_buffer** out) {
     MG_TRY(device_check(h));
     MG_TRY(need(xh, "input"));

@@ -438,6 +438,72 @@ inline unsigned cap_grid(const Device* d, uint64_t want, unsigned per_sm) {
 
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+
+// ---- greedy selection (src/kernels.cu:1808-1866, src/kernels.rs:4441-4488) ----------------------
+// Each eligible column of the logits row (raw score finite, outside every excluded [start, end)
+// range) is one 64-bit key: the score after the temperature division (as is when the temperature
+// is 0; -0 taken as +0) mapped so unsigned order is float order, above the complement of the
+// column -- the largest key is the highest score, ties going to the lowest column, whatever order
+// threads and CTAs run in.  CTAs fold their largest key into words[0] with atomicMax; the last CTA
+// to finish (a ticket in words[1]) moves the result to words[2] and leaves words[0..1] zero for
+// the next call, so one launch does the whole reduction.
+constexpr int kInlineRanges = 16;
+struct GreedyArgs {
+    const float* row;
+    uint64_t cols;
+    const uint64_t* ranges;  // [2 * count] when count > kInlineRanges
+    uint64_t inline_ranges[2 * kInlineRanges];
+    uint32_t count;
+    float temperature;
+    unsigned long long* words;  // [0] running max, [1] ticket (low 32 bits), [2] result
+};
+
+__device__ __forceinline__ unsigned long long greedy_key(const GreedyArgs& p, uint64_t i, float raw) {
+    if (!isfinite(raw)) return 0ull;
+    for (uint32_t r = 0; r < p.count; r++) {
+        const uint64_t lo = p.count <= kInlineRanges ? p.inline_ranges[2 * r] : p.ranges[2 * r];
+        const uint64_t hi = p.count <= kInlineRanges ? p.inline_ranges[2 * r + 1] : p.ranges[2 * r + 1];
+        if (i >= lo && i < hi) return 0ull;
+    }
+    float v = p.temperature != 0.0f ? raw / p.temperature : raw;
+    if (v == 0.0f) v = 0.0f;
+    const uint32_t bits = __float_as_uint(v);
+    const uint32_t ordered = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+    return ((unsigned long long)ordered << 32) | (0xFFFFFFFFull - (i & 0xFFFFFFFFull));
+}
+
+__global__ void __launch_bounds__(256) greedy_select_kernel(const __grid_constant__ GreedyArgs p) {
+    pdl_enter();
+    unsigned long long key = 0ull;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < p.cols; i += 4 * stride) {  // four loads in flight
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = __ldg(p.row + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < 4; u++) key = max(key, greedy_key(p, i + u * stride, v[u]));
+    }
+    for (; i < p.cols; i += stride) key = max(key, greedy_key(p, i, __ldg(p.row + i)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, o));
+    __shared__ unsigned long long warp_keys[8];
+    __shared__ bool last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) warp_keys[warp] = key;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) key = max(key, warp_keys[w]);
+        if (key) atomicMax(&p.words[0], key);
+        __threadfence();
+        last = atomicAdd(&p.words[1], 1ull) == gridDim.x - 1;
+        if (last) {
+            p.words[2] = atomicExch(&p.words[0], 0ull);
+            p.words[1] = 0ull;
+        }
+    }
+}
+
 }  // namespace
 
 namespace k {
@@ -527,6 +593,41 @@ mg_status embedding_rmsnorm(Device* d, const EmbedArgs& e, const RmsArgs& r, int
     enqueue(d, embedding_rmsnorm_kernel, cap_grid(d, (e.num_ids + 7) / 8, 8), 256, 0, e.table, e.ids, e.out, e.dim,
             e.num_ids, e.vocab, flag, e.has_scale, e.scale, r.w, r.w_stride, r.out, r.eps);
     return launched(d, "embedding + rmsnorm kernel launch");
+}
+
+mg_status greedy_select(Device* d, const float* row, uint64_t cols, const uint64_t* excluded, uint32_t count,
+                        float temperature, uint64_t* key) {
+    GreedyArgs p{};
+    p.row = row;
+    p.cols = cols;
+    p.count = count;
+    p.temperature = temperature;
+    p.words = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(d->flags) + 64);
+    void* staged = nullptr;
+    if (count <= (uint32_t)kInlineRanges) {
+        for (uint32_t r = 0; r < 2 * count; r++) p.inline_ranges[r] = excluded[r];
+    } else {
+        MG_TRY(device_alloc(d, 2 * (size_t)count * sizeof(uint64_t), &staged));
+        cudaError_t e = cudaMemcpyAsync(staged, excluded, 2 * (size_t)count * sizeof(uint64_t), cudaMemcpyHostToDevice, d->stream);
+        if (e != cudaSuccess) {
+            device_free(d, staged);
+            return from_cuda(e, "uploading the excluded ranges");
+        }
+        p.ranges = static_cast<const uint64_t*>(staged);
+    }
+    uint64_t blocks = (cols + 1023) / 1024;
+    if (blocks > (uint64_t)d->sm_count) blocks = (uint64_t)d->sm_count;
+    enqueue(d, greedy_select_kernel, (unsigned)(blocks ? blocks : 1), 256, 0, p);
+    mg_status s = launched(d, "greedy selection launch");
+    if (staged) device_free(d, staged);
+    MG_TRY(s);
+    uint64_t* host = reinterpret_cast<uint64_t*>(d->host_flags) + 4;  // bytes 32..39 of the pinned words
+    MG_CUDA(cudaMemcpyAsync(host, reinterpret_cast<char*>(d->flags) + 80, sizeof(uint64_t), cudaMemcpyDeviceToHost, d->stream),
+            "reading the selected key");
+    MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the device");
+    *key = *host;
+    d->downloads.fetch_add(1);
+    return MG_OK;
 }
 
 }  // namespace k

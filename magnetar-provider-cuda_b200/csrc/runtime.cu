@@ -317,8 +317,8 @@ mg_status mg_device_open(int ordinal, mg_device** out) {
     }
     uint64_t keep = UINT64_MAX;
     cudaMemPoolSetAttribute(d->pool, cudaMemPoolAttrReleaseThreshold, &keep);
-    e = cudaMalloc(&d->flags, 64);
-    if (e == cudaSuccess) e = cudaMemset(d->flags, 0, 64);
+    e = cudaMalloc(&d->flags, 128);
+    if (e == cudaSuccess) e = cudaMemset(d->flags, 0, 128);
     if (e == cudaSuccess) e = cudaMalloc(&d->counters, (1u << 16) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(d->counters, 0, (1u << 16) * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMallocHost(&d->host_flags, 64);

@@ -142,6 +142,16 @@ class CudaExecutor:
                                                    out.size))
         return out
 
+    def select_greedy_column(self, logits: str, row: int, excluded=(), temperature: float = 0.0) -> Optional[int]:
+        """``select_greedy_column``: greedy selection over a resident logits tensor; None when
+        no column is eligible or the selection fails (the reference's ``ok().flatten()``)."""
+        found, column = ctypes.c_int(), ctypes.c_uint64()
+        pairs, count = N.range_pairs(excluded)
+        status = N.lib().mg_executor_select_greedy_column(self._h, logits.encode(), row, pairs, count,
+                                                          ctypes.c_float(temperature), ctypes.byref(found),
+                                                          ctypes.byref(column))
+        return int(column.value) if status == 0 and found.value else None
+
     def release_tensor(self, id: str) -> bool:
         r = ctypes.c_int()
         check(N.lib().mg_executor_release_tensor(self._h, id.encode(), ctypes.byref(r)))

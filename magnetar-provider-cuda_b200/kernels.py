@@ -277,6 +277,16 @@ class CudaKernels:
     def softmax_rows(self, x, out=None):
         return self._run(N.lib().mg_softmax, x.handle, out=out)
 
+    def greedy_select(self, logits, row: int, excluded=(), temperature: float = 0.0) -> Optional[int]:
+        """``greedy_select``: the column of logits row ``row`` with the highest finite score /
+        temperature outside the ``excluded`` ``(start, end)`` ranges, ties to the lowest column;
+        None when no column is eligible."""
+        found, column = ctypes.c_int(), ctypes.c_uint64()
+        pairs, count = N.range_pairs(excluded)
+        check(N.lib().mg_greedy_select(self.handle, logits.handle, row, pairs, count, ctypes.c_float(temperature),
+                                       ctypes.byref(found), ctypes.byref(column)))
+        return int(column.value) if found.value else None
+
     def gelu_tanh(self, x, out=None):
         """``gelu_tanh`` (the tanh approximation)."""
         return self._run(N.lib().mg_gelu_tanh, x.handle, out=out)

@@ -222,6 +222,28 @@ void orc_softcap(const float* x, float* out, float cap, uint64_t n) {
     for (int64_t i = 0; i < (int64_t)n; i++) out[i] = cap * tanhf(x[i] / cap);
 }
 
+/* Host greedy selection (src/tests_conformance.rs:571-587, the Runtime's rule the device kernel
+ * src/kernels.cu:1808-1866 matches): the first column, in column order, whose finite raw score,
+ * outside every excluded [start, end) pair, divided by the temperature (as is when 0), is
+ * strictly greater than every earlier one.  Returns -1 when no column is eligible. */
+int64_t orc_greedy_select(const float* row, uint64_t cols, const uint64_t* ranges, uint32_t count, float temperature) {
+    int64_t best = -1;
+    float best_value = 0.0f;
+    for (uint64_t c = 0; c < cols; c++) {
+        const float raw = row[c];
+        if (!isfinite(raw)) continue;
+        int excluded = 0;
+        for (uint32_t r = 0; r < count && !excluded; r++) excluded = c >= ranges[2 * r] && c < ranges[2 * r + 1];
+        if (excluded) continue;
+        const float score = temperature == 0.0f ? raw : raw / temperature;
+        if (best < 0 || score > best_value) {
+            best = (int64_t)c;
+            best_value = score;
+        }
+    }
+    return best;
+}
+
 /* src/kernels.cu:1066-1077: out[i] = x[i] * scale[i / cols] */
 void orc_row_scale(const float* x, const float* scale, float* out, uint64_t rows, uint64_t cols) {
 #pragma omp parallel for schedule(static)

@@ -72,6 +72,8 @@ def lib():
         L.orc_f32_to_bf16.restype = ctypes.c_uint16
         L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
         L.orc_get_threads.restype = ctypes.c_int
+        L.orc_greedy_select.restype = ctypes.c_int64
+        L.orc_greedy_select.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float]
         L.orc_embedding.restype = ctypes.c_int
         L.orc_softmax_rows.restype = ctypes.c_int
         _lib = L
@@ -229,6 +231,16 @@ def row_scale(x, scale):
     o, op = _out(x.shape)
     lib().orc_row_scale(xp, sp, op, _u64(x.shape[0]), _u64(x.shape[1]))
     return o
+
+
+def greedy_select(logits, row, excluded=(), temperature=0.0):
+    """src/tests_conformance.rs:571-587 (host greedy selection); None when nothing is eligible"""
+    x = np.ascontiguousarray(logits, np.float32)
+    cols = x.shape[-1]
+    r = np.ascontiguousarray(x.reshape(-1, cols)[row])
+    pairs = np.ascontiguousarray(np.array([v for p in excluded for v in p] or [0, 0], np.uint64))
+    c = lib().orc_greedy_select(r.ctypes.data, cols, pairs.ctypes.data, len(excluded), float(temperature))
+    return None if c < 0 else int(c)
 
 
 def concat(a, b):

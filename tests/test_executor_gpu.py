@@ -452,3 +452,18 @@ def test_layered_forms_through_the_executor(executor, oracle):
     assert rel(executor.read_tensor("bm"), oracle.batched_matmul(x, w, 2)) <= 1e-4
     r4 = executor.submit_kernel(inv("batched-matmul", ["x", "w"], "bm2"))
     assert not r4.success and r4.error_code == "KernelAttributeUnsupported"
+
+
+def test_select_greedy_column_over_a_resident_tensor(executor, oracle):
+    # src/executor.rs:2549-2563: one reduction and an 8-byte read instead of the row
+    r = np.random.default_rng(29)
+    logits = r.standard_normal((3, 32000)).astype(np.float32)
+    executor.write_tensor("logits", logits)
+    k = executor.kernels
+    down = k.download_count()
+    for row in range(3):
+        assert executor.select_greedy_column("logits", row) == oracle.greedy_select(logits, row)
+    assert k.download_count() == down + 3
+    assert executor.select_greedy_column("logits", 1, [(0, 16000)], 0.8) == oracle.greedy_select(logits, 1, [(0, 16000)], 0.8)
+    assert executor.select_greedy_column("logits", 3) is None  # a row past the logits
+    assert executor.select_greedy_column("missing", 0) is None

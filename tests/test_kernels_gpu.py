@@ -691,3 +691,37 @@ def test_rewriting_a_compact_weight_drops_its_compact_form(kernels, oracle):
     got3 = kernels.download(kernels.matmul(da, w))
     assert w.is_compact()
     np.testing.assert_array_equal(got3, kernels.download(kernels.matmul(da, kernels.upload(b3))))
+
+
+def test_greedy_select_matches_host_greedy_selection(kernels, oracle, mpc):
+    # src/tests_conformance.rs:563-658: 40 seeded rounds (vocab 151936 / 1000 / 33 / 7, common
+    # ties, planted NaN / inf / -inf / -0, excluded ranges, temperatures 0 / 1 / 0.7 / 1.3)
+    from greedy_cases import cases
+    for rnd, (logits, row, excluded, temperature) in enumerate(cases()):
+        got = kernels.greedy_select(kernels.upload(logits), row, excluded, temperature)
+        assert got == oracle.greedy_select(logits, row, excluded, temperature), (rnd, logits.shape, row, temperature)
+    assert kernels.greedy_select(kernels.upload(np.array([[-1.0, 0.0, -0.0]], np.float32)), 0) == 1
+    assert kernels.greedy_select(kernels.upload(np.array([[-1.0, -0.0, 0.0]], np.float32)), 0) == 1
+    logits = kernels.upload(np.array([[1.0, np.nan, 2.0]], np.float32))
+    assert kernels.greedy_select(logits, 0, [(0, 1), (2, 3)]) is None
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.greedy_select(logits, 1)
+    assert e.value.code == "ShapeUnsupported"
+
+
+def test_greedy_select_many_ranges_and_wide_rows(kernels, oracle):
+    r = rng(28)
+    cols = 262_144
+    logits = r.standard_normal((2, cols)).astype(np.float32)
+    logits[1, cols - 1] = 100.0  # the last column of the last row
+    d = kernels.upload(logits)
+    assert kernels.greedy_select(d, 1) == cols - 1
+    # more ranges than travel in the launch's parameters
+    excluded = [(int(s), int(s) + 3) for s in np.argsort(-logits[0])[:40]]
+    for temperature in (0.0, 0.5, 2.0):
+        assert kernels.greedy_select(d, 0, excluded, temperature) == oracle.greedy_select(logits, 0, excluded, temperature)
+    # every column excluded
+    assert kernels.greedy_select(d, 0, [(0, cols)]) is None
+    # rank-3 logits: rows are the leading dimensions flattened
+    x = r.standard_normal((2, 3, 50)).astype(np.float32)
+    assert kernels.greedy_select(kernels.upload(x), 4) == oracle.greedy_select(x.reshape(6, 50), 4)

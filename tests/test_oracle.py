@@ -166,3 +166,14 @@ def test_oracle_layered_forms_against_numpy(oracle):
     exp = np.concatenate([ga[:, g * 8:(g + 1) * 8].astype(np.float64) @ gbt[g * 5:(g + 1) * 5].T for g in range(2)],
                          axis=1)
     np.testing.assert_allclose(oracle.batched_matmul(ga, gbt, 2, transpose_b=True), exp, rtol=1e-5, atol=1e-5)
+
+
+def test_greedy_select_oracle_matches_the_host_rule(oracle):
+    from greedy_cases import cases, host_greedy
+    for logits, row, excluded, temperature in cases(rounds=24, widths=(2000, 1000, 33, 7)):
+        assert oracle.greedy_select(logits, row, excluded, temperature) == host_greedy(logits[row], excluded, temperature)
+    # -0 and +0 compare equal: the lower column wins (src/tests_conformance.rs:630-645)
+    assert oracle.greedy_select(np.array([[-1.0, 0.0, -0.0]], np.float32), 0) == 1
+    assert oracle.greedy_select(np.array([[-1.0, -0.0, 0.0]], np.float32), 0) == 1
+    # nothing eligible
+    assert oracle.greedy_select(np.array([[1.0, np.nan, 2.0]], np.float32), 0, [(0, 1), (2, 3)]) is None
