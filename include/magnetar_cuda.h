@@ -54,7 +54,9 @@ typedef enum mg_status {
 
 /* Element types: f32 everywhere, f16/bf16 for add-half/mul-half
  * (CudaHalfDType, src/kernels.rs:211-215). */
-typedef enum mg_dtype { MG_F32 = 0, MG_F16 = 1, MG_BF16 = 2 } mg_dtype;
+/* MG_Q8_0: a packed weight (mg_buffer_upload_q8_0); only matmul's b, embedding's table,
+ * mg_dequantize_q8 and downloads accept it. */
+typedef enum mg_dtype { MG_F32 = 0, MG_F16 = 1, MG_BF16 = 2, MG_Q8_0 = 3 } mg_dtype;
 
 typedef struct mg_device mg_device;     /* CudaKernels + its stream (src/kernels.rs:538-616) */
 typedef struct mg_buffer mg_buffer;     /* CudaDeviceBuffer / CudaHalfBuffer (src/kernels.rs:211-276) */
@@ -141,7 +143,24 @@ mg_status mg_buffer_set_weight(mg_buffer* buffer, int is_weight);
  * of the f32 values -- half the bytes, bit-identical results (the reference's compact weight,
  * `CudaDeviceBuffer::is_compact`, src/kernels.rs:257-268, 1668-1712).  Built and checked on the
  * first such matmul that reads the weight; 0 before that, for other buffers, and for null. */
-int mg_buffer_is_compact(const mg_buffer* buffer);
+int mg_buffer_is_compact(const mg_buffer* buffer); /* 1 for packed weights too, as the reference's */
+
+/* Packed weights (`execute-direct-quantized-weights`).  Q8_0 only: 34-byte blocks of a
+ * little-endian f16 scale and 32 signed 8-bit quants, `stored_rows` x `stored_cols` values in
+ * stored row-major order (stored_cols a multiple of 32); the logical matrix is the stored one, or
+ * its transpose when `transposed` (a checkpoint's [out, in] weight read as matmul B [in, out]).
+ * Replaces CudaKernels::upload_packed_weight's Q8_0 branch (src/kernels.rs:1725-1838): the blocks
+ * are split on the device into quants and f32 scales (the f16 widened exactly).  A matmul with a
+ * transposed-storage Q8_0 b and at most 16 rows of a streams the quants (k a multiple of 128);
+ * other matmuls dequantize b for the call; an embedding lookup reads the rows of a packed table
+ * stored untransposed. */
+#define MG_PACKED_Q8_0 0
+mg_status mg_buffer_upload_q8_0(mg_device* d, const void* blocks, uint64_t bytes, uint64_t stored_rows,
+                                uint64_t stored_cols, int transposed, mg_buffer** out);
+/* 1 for a packed buffer (the reference's `is_q8()`, src/kernels.rs:376-378). */
+int mg_buffer_is_q8(const mg_buffer* buffer);
+/* A packed weight's logical matrix as f32 (src/kernels.rs:1964-1967). */
+mg_status mg_dequantize_q8(mg_device* d, const mg_buffer* packed, mg_buffer** out);
 
 /* ---------------------------------------------------------------------------------- */
 /* Kernels -- one entry per advertised hot-path operator, with the validation of the    */
@@ -338,6 +357,11 @@ mg_status mg_executor_read_tensor(mg_executor* ex, const char* id, float* data, 
                                   int* rank, uint64_t* shape);
 mg_status mg_executor_read_tensor_rows(mg_executor* ex, const char* id, uint64_t first_row,
                                        uint64_t rows, float* data, uint64_t capacity);
+/* write_packed_weight_tensor (src/executor.rs:404-420): `format` MG_PACKED_Q8_0; arguments as
+ * mg_buffer_upload_q8_0.  MG_DTYPE_UNSUPPORTED for other formats. */
+mg_status mg_executor_write_packed_weight_tensor(mg_executor* ex, const char* id, int format, const void* blocks,
+                                                 uint64_t bytes, uint64_t stored_rows, uint64_t stored_cols,
+                                                 int transposed);
 /* select_greedy_column (src/executor.rs:2549-2563): mg_greedy_select over a resident tensor. */
 mg_status mg_executor_select_greedy_column(mg_executor* ex, const char* id, uint64_t row, const uint64_t* excluded,
                                            uint32_t excluded_count, float temperature, int* found,

@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(_HERE, "lib", "libmagnetar_cuda.so")
 CSRC = os.path.join(_HERE, "csrc")
 
 MG_MAX_RANK = 8
-F32, F16, BF16 = 0, 1, 2
+F32, F16, BF16, Q8_0 = 0, 1, 2, 3
+PACKED_Q8_0 = 0
 ATTR_INT, ATTR_FLOAT, ATTR_BOOL, ATTR_STRING = 0, 1, 2, 3
 
 # mg_status -> the reference's CudaErrorCode / KernelError names (src/error.rs:14-42).
@@ -121,6 +122,9 @@ SIGNATURES = {
     "mg_buffer_device_ptr": [_P],
     "mg_buffer_set_weight": [_P, _I],
     "mg_buffer_is_compact": [_P],
+    "mg_buffer_upload_q8_0": [_P, _P, _U64, _U64, _U64, _I, _PP],
+    "mg_buffer_is_q8": [_P],
+    "mg_dequantize_q8": [_P, _P, _PP],
     "mg_add": [_P, _P, _P, _PP],
     "mg_mul": [_P, _P, _P, _PP],
     "mg_residual_add": [_P, _P, _P, _PP],
@@ -158,6 +162,7 @@ SIGNATURES = {
     "mg_executor_buffer": [_P, _S, _PP],
     "mg_executor_read_tensor": [_P, _S, _P, _U64, _IP, _U64P],
     "mg_executor_read_tensor_rows": [_P, _S, _U64, _U64, _P, _U64],
+    "mg_executor_write_packed_weight_tensor": [_P, _S, _I, _P, _U64, _U64, _U64, _I],
     "mg_executor_select_greedy_column": [_P, _S, _U64, _U64P, ctypes.c_uint32, _F, _IP, _U64P],
     "mg_executor_release_tensor": [_P, _S, _IP],
     "mg_executor_resident_shape": [_P, _S, _IP, _IP, _U64P],

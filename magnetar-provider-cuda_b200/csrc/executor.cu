@@ -490,8 +490,7 @@ mg_status flush_deferred(mg_executor* ex) {
     if (ex->embed_pending) {
         ex->embed_pending = false;
         const k::EmbedArgs& e = ex->embed;
-        return k::embedding(ex->device, e.table, e.ids, e.out, e.dim, e.num_ids, e.vocab, ex->device->flags,
-                            e.has_scale, e.scale);
+        return k::embedding_run(ex->device, e, ex->device->flags);
     }
     if (ex->deferred.empty()) return MG_OK;
     k::GemmArgs gs[3];
@@ -754,6 +753,23 @@ mg_status mg_executor_write_tensor(mg_executor* ex, const char* id, int rank, co
     return upload_tensor(ex, id, rank, shape, data);
 }
 
+// src/executor.rs:404-420: a packed weight stored as the checkpoint stored it.
+mg_status mg_executor_write_packed_weight_tensor(mg_executor* ex, const char* id, int format, const void* blocks,
+                                                 uint64_t bytes, uint64_t stored_rows, uint64_t stored_cols,
+                                                 int transposed) {
+    if (!ex || !id) return fail(MG_INVALID_ARGUMENT, "null argument");
+    if (format != MG_PACKED_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "packed weight format %d is not supported", format);
+    std::lock_guard<std::mutex> g(ex->lock);
+    MG_TRY(device_check(ex->handle));
+    if (ex->comm && ex->plan.count(id))
+        return fail(MG_LAYOUT_UNSUPPORTED, "a packed weight cannot be split for tensor parallelism");
+    mg_buffer* b = nullptr;
+    MG_TRY(mg_buffer_upload_q8_0(ex->handle, blocks, bytes, stored_rows, stored_cols, transposed, &b));
+    store_replace(ex, id, buf(b));
+    ex->sharded.erase(id);
+    return MG_OK;
+}
+
 mg_status mg_executor_write_weight_tensor(mg_executor* ex, const char* id, int rank, const uint64_t* shape,
                                           const float* data) {
     if (!ex || !id || (rank > 0 && !shape)) return fail(MG_INVALID_ARGUMENT, "null argument");
@@ -912,6 +928,18 @@ mg_status mg_executor_copy_tensor(mg_executor* ex, const char* from, const char*
     MG_TRY(buffer_new(ex->device, src->dtype, src->rank, src->shape, &nb));
     cudaError_t e = cudaMemcpyAsync(nb->ptr, src->ptr, src->count * dtype_size(src->dtype), cudaMemcpyDeviceToDevice,
                                     ex->device->stream);
+    if (e == cudaSuccess && src->dtype == MG_Q8_0) {  // a packed weight: its scales too
+        nb->q8_rows = src->q8_rows;
+        nb->q8_cols = src->q8_cols;
+        nb->q8_transposed = src->q8_transposed;
+        const size_t sb = src->q8_rows * src->q8_cols / 32 * sizeof(float);
+        mg_status s = device_alloc(ex->device, sb, (void**)&nb->q8_scales);
+        if (s != MG_OK) {
+            buffer_free(nb);
+            return s;
+        }
+        e = cudaMemcpyAsync(nb->q8_scales, src->q8_scales, sb, cudaMemcpyDeviceToDevice, ex->device->stream);
+    }
     if (e != cudaSuccess) {
         buffer_free(nb);
         return from_cuda(e, "copying a resource");

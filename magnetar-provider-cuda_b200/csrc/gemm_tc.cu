@@ -1006,6 +1006,7 @@ mg_status gemm_prepare_b(Device* d, const float* b, uint64_t k, uint64_t n, int 
 
 mg_status gemm(Device* d, const GemmArgs& g) {
     if (g.m == 0 || g.n == 0) return MG_OK;
+    if (g.packed[0] || g.packed[1]) return q8_matmul(d, g);
     if (g.k == 0) {
         // An empty inner dimension: every sum is 0 before the addend / gate.
         return gemm_simt(d, g);

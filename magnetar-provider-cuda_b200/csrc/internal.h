@@ -123,6 +123,12 @@ struct Buffer {
     // checked, 1 built, -1 some value is not exactly bfloat16.
     uint16_t* compact = nullptr;
     int compact_state = 0;
+    // A packed Q8_0 weight (dtype MG_Q8_0): ptr holds the int8 quants in stored row-major order
+    // ([q8_rows, q8_cols]), q8_scales one f32 per 32 of them; the logical matrix (shape, count) is
+    // the stored one, or its transpose when q8_transposed.
+    float* q8_scales = nullptr;
+    uint64_t q8_rows = 0, q8_cols = 0;
+    int q8_transposed = 0;
 };
 
 // Weights smaller than this stay f32 only (src/kernels.rs:506-510).
@@ -133,7 +139,7 @@ void buffer_drop_prep(Buffer* b);
 
 inline Buffer* buf(mg_buffer* b) { return reinterpret_cast<Buffer*>(b); }
 inline const Buffer* buf(const mg_buffer* b) { return reinterpret_cast<const Buffer*>(b); }
-inline size_t dtype_size(mg_dtype t) { return t == MG_F32 ? 4 : 2; }
+inline size_t dtype_size(mg_dtype t) { return t == MG_F32 ? 4 : t == MG_Q8_0 ? 1 : 2; }
 const char* dtype_name(mg_dtype t);
 std::string shape_str(const Buffer* b);
 bool same_shape(const Buffer* a, const Buffer* b);
@@ -187,6 +193,7 @@ mg_status embedding(Device* d, const float* table, const float* ids, float* out,
 mg_status rmsnorm(Device* d, const float* x, const float* w, float* out, uint64_t rows,
                   uint64_t cols, uint64_t w_stride, float eps);
 struct EmbedArgs {
+    const Buffer* packed = nullptr;  // a packed Q8_0 table (table then unused)
     const float* table;
     const float* ids;
     float* out;
@@ -203,6 +210,8 @@ struct RmsArgs {
 };
 // An embedding followed by an rmsnorm of its rows in one launch (the step capture's fusion):
 // x = the gathered rows, out = rmsnorm(x), each exactly as the two kernels compute them.
+// The lookup of a planned embedding: the f32 table's kernel or the packed table's.
+mg_status embedding_run(Device* d, const EmbedArgs& e, int* flag);
 bool embedding_rmsnorm_eligible(const EmbedArgs& e, const RmsArgs& r);
 mg_status embedding_rmsnorm(Device* d, const EmbedArgs& e, const RmsArgs& r, int* flag);
 struct RopeArgs {
@@ -235,8 +244,18 @@ struct GemmArgs {
     int b_one_term[2];
     // Compact (bfloat16-bit) forms of b / b2 for the few-row path; null = read the f32 values.
     const uint16_t* b16[2];
+    // Packed Q8_0 b / b2 (b / b2 then unused); null for f32 operands.
+    const Buffer* packed[2];
 };
 mg_status gemm(Device* d, const GemmArgs& g);
+// Q8_0 packed weights: the 34-byte blocks split into quants and f32 scales; the logical matrix
+// (or, stored_order, the stored one) dequantized; embedding rows of a packed table; the matmul
+// with packed B (the few-row kernel, else dequantized for the call).
+mg_status q8_unpack(Device* d, const uint8_t* blocks, int8_t* quants, float* scales, uint64_t nblocks);
+mg_status q8_dequantize(Device* d, const Buffer* b, float* out, bool stored_order);
+mg_status q8_embedding(Device* d, const Buffer* table, const float* ids, float* out, uint64_t num_ids, int* flag,
+                       int has_scale, float scale);
+mg_status q8_matmul(Device* d, const GemmArgs& g);
 // Writes the bfloat16 bits of b's `count` values to dst; sets *not_exact (a device word) when
 // some value is not exactly a bfloat16 value.
 mg_status gemv_compact_b(Device* d, const float* b, uint16_t* dst, uint64_t count, int* not_exact);

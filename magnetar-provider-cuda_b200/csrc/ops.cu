@@ -215,7 +215,7 @@ mg_status matmul_plan(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
         if (!same_shape(b, b2))
             return fail(MG_SHAPE_UNSUPPORTED, "gated-matmul expects gate and up to share a shape, got %s and %s",
                         shape_str(b).c_str(), shape_str(b2).c_str());
-        MG_TRY(require_f32(b2, "gated-matmul's up"));
+        if (b2->dtype != MG_Q8_0) MG_TRY(require_f32(b2, "gated-matmul's up"));
     }
     const Buffer* add = nullptr;
     if (addh) {
@@ -229,7 +229,7 @@ mg_status matmul_plan(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
                         (unsigned long long)m, (unsigned long long)n, shape_str(add).c_str());
     }
     MG_TRY(require_f32(a, "matmul's a"));
-    MG_TRY(require_f32(b, "matmul's b"));
+    if (b->dtype != MG_Q8_0) MG_TRY(require_f32(b, "matmul's b"));
     if (add) MG_TRY(require_f32(add, "a fused matmul's addend"));
     const uint64_t shape[2] = {m, n};
     Buffer* o;
@@ -249,7 +249,12 @@ mg_status matmul_plan(mg_device* h, const mg_buffer* ah, const mg_buffer* bh, co
     g.gated = b2 ? 1 : 0;
     g.b_prep[0] = g.b_prep[1] = nullptr;
     g.b16[0] = g.b16[1] = nullptr;
-    if (k::gemm_uses_tensor_cores(m, n, kk, tb, g.b)) {
+    g.packed[0] = b->dtype == MG_Q8_0 ? b : nullptr;
+    g.packed[1] = b2 && b2->dtype == MG_Q8_0 ? b2 : nullptr;
+    if (g.packed[0] || g.packed[1]) {
+        // packed weights: read by the packed paths (src/kernels.rs:5581-5600)
+        g.b_stable = 0;
+    } else if (k::gemm_uses_tensor_cores(m, n, kk, tb, g.b)) {
         bool built = false;
         MG_TRY(weight_prep(d, b, kk, n, tb, &g.b_prep[0], &built, &g.b_one_term[0]));
         if (b2) MG_TRY(weight_prep(d, b2, kk, n, tb, &g.b_prep[1], &built, &g.b_one_term[1]));
@@ -544,11 +549,15 @@ mg_status embedding_plan(mg_device* h, const mg_buffer* th, const mg_buffer* ih,
     uint64_t vocab, dim;
     MG_TRY(rows_cols(t, &vocab, &dim));
     MG_TRY(require_f32(ids, "the embedding lookup's ids"));
-    MG_TRY(require_f32(t, "the embedding lookup's table"));
+    // a packed table is read row by row when stored untransposed (src/kernels.rs:1970-1982)
+    if (t->dtype == MG_Q8_0 && t->q8_transposed)
+        return fail(MG_DTYPE_UNSUPPORTED, "rows of a packed weight stored transposed");
+    if (t->dtype != MG_Q8_0) MG_TRY(require_f32(t, "the embedding lookup's table"));
     const uint64_t shape[2] = {ids->count, dim};
     Buffer* o;
     MG_TRY(output_for(d, MG_F32, 2, shape, out, &o));
-    e->table = (const float*)t->ptr;
+    e->packed = t->dtype == MG_Q8_0 ? t : nullptr;
+    e->table = e->packed ? nullptr : (const float*)t->ptr;
     e->ids = (const float*)ids->ptr;
     e->out = (float*)o->ptr;
     e->dim = dim;
@@ -568,7 +577,7 @@ mg_status mg_embedding(mg_device* h, const mg_buffer* th, const mg_buffer* ih, i
     MG_TRY(embedding_plan(h, th, ih, has_scale, scale, out, &e));
     Device* d = dev(h);
     if (!d->capturing) MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
-    MG_TRY(k::embedding(d, e.table, e.ids, e.out, e.dim, e.num_ids, e.vocab, d->flags, e.has_scale, e.scale));
+    MG_TRY(k::embedding_run(d, e, d->flags));
     if (d->capturing) return MG_OK;  // checked once the captured step has run
     int flags[4];
     MG_TRY(read_flags(d, flags));
@@ -762,6 +771,19 @@ mg_status rope_plan(mg_device* h, const mg_buffer* xh, const mg_rope_params* pp,
 extern "C" {
 
 // src/kernels.rs:4357-4386
+// src/kernels.rs:1964-1967: a packed weight's logical matrix as f32.
+mg_status mg_dequantize_q8(mg_device* h, const mg_buffer* ph, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    MG_TRY(need(ph, "packed weight"));
+    Device* d = dev(h);
+    const Buffer* p = buf(ph);
+    MG_TRY(same_device(d, p));
+    if (p->dtype != MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "not a packed weight");
+    Buffer* o;
+    MG_TRY(output_for(d, MG_F32, 2, p->shape, out, &o));
+    return k::q8_dequantize(d, p, (float*)o->ptr, false);
+}
+
 // src/kernels.rs:4441-4488: the column of one logits row with the highest score over the
 // temperature, among finite scores outside the excluded ranges; *found = 0 when none is eligible.
 mg_status mg_greedy_select(mg_device* h, const mg_buffer* lh, uint64_t row, const uint64_t* excluded,

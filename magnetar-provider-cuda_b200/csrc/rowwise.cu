@@ -583,8 +583,13 @@ mg_status embedding(Device* d, const float* table, const float* ids, float* out,
     return launched(d, "embedding kernel launch");
 }
 
+mg_status embedding_run(Device* d, const EmbedArgs& e, int* flag) {
+    if (e.packed) return q8_embedding(d, e.packed, e.ids, e.out, e.num_ids, flag, e.has_scale, e.scale);
+    return embedding(d, e.table, e.ids, e.out, e.dim, e.num_ids, e.vocab, flag, e.has_scale, e.scale);
+}
+
 bool embedding_rmsnorm_eligible(const EmbedArgs& e, const RmsArgs& r) {
-    return r.x == e.out && r.out != e.out && r.rows == e.num_ids && r.cols == e.dim && e.dim % 4 == 0 &&
+    return !e.packed && r.x == e.out && r.out != e.out && r.rows == e.num_ids && r.cols == e.dim && e.dim % 4 == 0 &&
            e.dim <= 1024 && a16(e.table) && a16(e.out) && a16(r.out) &&
            (!r.w || (a16(r.w) && (r.w_stride == 0 || r.w_stride == e.dim)));
 }

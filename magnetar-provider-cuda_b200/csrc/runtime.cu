@@ -49,6 +49,7 @@ const char* dtype_name(mg_dtype t) {
         case MG_F32: return "f32";
         case MG_F16: return "f16";
         case MG_BF16: return "bf16";
+        case MG_Q8_0: return "q8_0";
     }
     return "?";
 }
@@ -192,6 +193,7 @@ void buffer_free(Buffer* b) {
     Device* d = b->device;
     buffer_drop_prep(b);
     if (b->owned && b->ptr) device_free(d, b->ptr);
+    if (b->q8_scales) device_free(d, b->q8_scales);
     delete b;
     device_unref(d);
 }
@@ -446,6 +448,7 @@ mg_status mg_buffer_release(mg_buffer* h) {
 mg_status mg_buffer_upload(mg_buffer* h, const void* host, uint64_t bytes) {
     if (!h || (!host && bytes)) return fail(MG_INVALID_ARGUMENT, "null argument");
     Buffer* b = buf(h);
+    if (b->dtype == MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "a packed weight is written by mg_buffer_upload_q8_0 only");
     if (bytes != b->count * dtype_size(b->dtype))
         return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes cannot fill a %s buffer of shape %s",
                     (unsigned long long)bytes, dtype_name(b->dtype), shape_str(b).c_str());
@@ -459,6 +462,7 @@ mg_status mg_buffer_upload(mg_buffer* h, const void* host, uint64_t bytes) {
 mg_status mg_buffer_download(const mg_buffer* h, void* host, uint64_t bytes) {
     if (!h || (!host && bytes)) return fail(MG_INVALID_ARGUMENT, "null argument");
     const Buffer* b = buf(h);
+    if (b->dtype == MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "a packed weight downloads as f32 values only");
     if (bytes != b->count * dtype_size(b->dtype))
         return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes cannot hold a %s buffer of shape %s",
                     (unsigned long long)bytes, dtype_name(b->dtype), shape_str(b).c_str());
@@ -472,6 +476,7 @@ mg_status mg_buffer_download(const mg_buffer* h, void* host, uint64_t bytes) {
 mg_status mg_buffer_upload_f32(mg_buffer* h, const float* host, uint64_t count) {
     if (!h || (!host && count)) return fail(MG_INVALID_ARGUMENT, "null argument");
     Buffer* b = buf(h);
+    if (b->dtype == MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "a packed weight is written by mg_buffer_upload_q8_0 only");
     if (count != b->count)
         return fail(MG_SHAPE_UNSUPPORTED, "%llu values cannot fill a buffer of shape %s",
                     (unsigned long long)count, shape_str(b).c_str());
@@ -499,7 +504,8 @@ mg_status mg_buffer_download_f32(const mg_buffer* h, float* host, uint64_t count
     MG_CUDA(cudaSetDevice(d->ordinal), "selecting the device");
     void* staging = nullptr;
     MG_TRY(device_alloc(d, count * 4, &staging));
-    mg_status s = k::decode_half(d, (const uint16_t*)b->ptr, (float*)staging, count, b->dtype);
+    mg_status s = b->dtype == MG_Q8_0 ? k::q8_dequantize(d, b, (float*)staging, false)
+                                      : k::decode_half(d, (const uint16_t*)b->ptr, (float*)staging, count, b->dtype);
     if (s == MG_OK) {
         cudaError_t e = cudaMemcpyAsync(host, staging, count * 4, cudaMemcpyDeviceToHost, d->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
@@ -551,6 +557,7 @@ mg_status mg_buffer_reshape(mg_buffer* h, int rank, const uint64_t* shape) {
     if (!h || (rank > 0 && !shape)) return fail(MG_INVALID_ARGUMENT, "null argument");
     if (rank < 0 || rank > MG_MAX_RANK) return fail(MG_SHAPE_UNSUPPORTED, "rank %d is outside 0..%d", rank, MG_MAX_RANK);
     Buffer* b = buf(h);
+    if (b->dtype == MG_Q8_0) return fail(MG_LAYOUT_UNSUPPORTED, "a packed weight keeps its logical shape");
     uint64_t count;
     if (!shape_count(rank, shape, &count) || count != b->count)
         return fail(MG_SHAPE_UNSUPPORTED, "cannot reshape %s to a different element count", shape_str(b).c_str());
@@ -561,7 +568,61 @@ mg_status mg_buffer_reshape(mg_buffer* h, int rank, const uint64_t* shape) {
 
 void* mg_buffer_device_ptr(const mg_buffer* h) { return h ? buf(h)->ptr : nullptr; }
 
-int mg_buffer_is_compact(const mg_buffer* h) { return h && buf(h)->compact_state == 1 ? 1 : 0; }
+int mg_buffer_is_compact(const mg_buffer* h) {
+    return h && (buf(h)->compact_state == 1 || buf(h)->dtype == MG_Q8_0) ? 1 : 0;
+}
+
+int mg_buffer_is_q8(const mg_buffer* h) { return h && buf(h)->dtype == MG_Q8_0 ? 1 : 0; }
+
+// src/kernels.rs:1725-1838 (the Q8_0 branch): the blocks uploaded as they are and split on the
+// device into quants and f32 scales.
+mg_status mg_buffer_upload_q8_0(mg_device* h, const void* blocks, uint64_t bytes, uint64_t stored_rows,
+                                uint64_t stored_cols, int transposed, mg_buffer** out) {
+    MG_TRY(device_check(h));
+    if (!out || (!blocks && bytes)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    Device* d = dev(h);
+    if (stored_rows == 0 || stored_cols == 0 || stored_cols % 32 != 0)
+        return fail(MG_SHAPE_UNSUPPORTED, "a Q8_0 weight needs rows and a multiple of 32 columns, got [%llu, %llu]",
+                    (unsigned long long)stored_rows, (unsigned long long)stored_cols);
+    if (stored_rows > (UINT64_MAX >> 8) / stored_cols)
+        return fail(MG_SHAPE_UNSUPPORTED, "Q8_0 weight element count overflows");
+    const uint64_t nblocks = stored_rows * stored_cols / 32;
+    if (bytes != nblocks * 34)
+        return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes are not the %llu blocks of a [%llu, %llu] Q8_0 weight",
+                    (unsigned long long)bytes, (unsigned long long)nblocks, (unsigned long long)stored_rows,
+                    (unsigned long long)stored_cols);
+    if (d->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "a host-to-device upload cannot be captured");
+    MG_CUDA(cudaSetDevice(d->ordinal), "selecting the device");
+    const uint64_t shape[2] = {transposed ? stored_cols : stored_rows, transposed ? stored_rows : stored_cols};
+    Buffer* b = nullptr;
+    MG_TRY(buffer_new(d, MG_Q8_0, 2, shape, &b));
+    b->q8_rows = stored_rows;
+    b->q8_cols = stored_cols;
+    b->q8_transposed = transposed ? 1 : 0;
+    void* staging = nullptr;
+    mg_status s = device_alloc(d, nblocks * sizeof(float), (void**)&b->q8_scales);
+    if (s == MG_OK) s = device_alloc(d, bytes, &staging);
+    if (s == MG_OK) {
+        cudaError_t e = cudaMemcpyAsync(staging, blocks, bytes, cudaMemcpyHostToDevice, d->stream);
+        s = e == cudaSuccess ? MG_OK : from_cuda(e, "uploading");
+    }
+    if (s == MG_OK) s = k::q8_unpack(d, (const uint8_t*)staging, (int8_t*)b->ptr, b->q8_scales, nblocks);
+    if (staging) device_free(d, staging);
+    // Settled before it returns: the packed few-row matmul starts loading a packed weight before
+    // its dependency wait, so no kernel that writes one may still be running then.
+    if (s == MG_OK) {
+        cudaError_t e = cudaStreamSynchronize(d->stream);
+        if (e != cudaSuccess) s = from_cuda(e, "waiting for the packed weight");
+    }
+    if (s != MG_OK) {
+        buffer_free(b);
+        return s;
+    }
+    d->uploads.fetch_add(1);
+    *out = reinterpret_cast<mg_buffer*>(b);
+    return MG_OK;
+}
 
 mg_status mg_buffer_set_weight(mg_buffer* h, int is_weight) {
     if (!h) return fail(MG_INVALID_ARGUMENT, "null buffer");

@@ -101,6 +101,15 @@ class CudaExecutor:
         check(N.lib().mg_executor_write_weight_tensor(self._h, id.encode(), len(shape),
                                                       N.shape_array(shape), a.ctypes.data))
 
+    def write_packed_weight_tensor(self, id: str, blocks, stored_rows: int, stored_cols: int,
+                                   transposed: bool = True, format: str = "q8_0") -> None:
+        """``write_packed_weight_tensor``: a Q8_0 weight kept as its 34-byte blocks' quants and scales."""
+        if format != "q8_0":
+            raise CudaError(2, f"packed weight format {format} is not supported")
+        raw = np.ascontiguousarray(np.asarray(blocks, np.uint8).ravel())
+        check(N.lib().mg_executor_write_packed_weight_tensor(self._h, id.encode(), N.PACKED_Q8_0, raw.ctypes.data,
+                                                             raw.nbytes, stored_rows, stored_cols, 1 if transposed else 0))
+
     def write_zeroed_tensor(self, id: str, shape: Sequence[int]) -> None:
         check(N.lib().mg_executor_write_zeroed_tensor(self._h, id.encode(), len(shape), N.shape_array(shape)))
 

@@ -15,7 +15,7 @@ import numpy as np
 from . import _native as N
 from ._native import CudaError, check
 
-_DTYPES = {"f32": N.F32, "f16": N.F16, "bf16": N.BF16}
+_DTYPES = {"f32": N.F32, "f16": N.F16, "bf16": N.BF16, "q8_0": N.Q8_0}
 _DTYPE_NAMES = {v: k for k, v in _DTYPES.items()}
 
 
@@ -78,6 +78,10 @@ class DeviceBuffer:
         a = np.ascontiguousarray(array, dtype=np.float32)
         check(N.lib().mg_buffer_upload_f32(self._h, a.ctypes.data, a.size))
         return self
+
+    def is_q8(self) -> bool:
+        """Whether this is a packed Q8_0 weight (``CudaDeviceBuffer::is_q8``)."""
+        return bool(N.lib().mg_buffer_is_q8(self._h))
 
     def is_compact(self) -> bool:
         """Whether this weight holds its compact (bfloat16-bit) form, which the few-row matmul
@@ -175,8 +179,22 @@ class CudaKernels:
         check(N.lib().mg_buffer_upload(buf.handle, a.ctypes.data, a.nbytes))
         return buf
 
+    def upload_q8_0(self, blocks, stored_rows: int, stored_cols: int, transposed: bool = True) -> DeviceBuffer:
+        """``upload_packed_weight`` for ``Q8_0``: 34-byte blocks (f16 scale, 32 int8 quants) of a
+        [stored_rows, stored_cols] matrix; the logical matrix is its transpose when ``transposed``."""
+        raw = np.ascontiguousarray(np.frombuffer(bytes(blocks), np.uint8) if isinstance(blocks, (bytes, bytearray))
+                                   else np.asarray(blocks, np.uint8).ravel())
+        out = ctypes.c_void_p()
+        check(N.lib().mg_buffer_upload_q8_0(self._h, raw.ctypes.data, raw.nbytes, stored_rows, stored_cols,
+                                            1 if transposed else 0, ctypes.byref(out)))
+        return DeviceBuffer(out.value, self)
+
+    def dequantize_q8(self, packed, out=None):
+        """``dequantize_q8``: a packed weight's logical matrix as f32."""
+        return self._run(N.lib().mg_dequantize_q8, packed.handle, out=out)
+
     def download(self, buf: DeviceBuffer) -> np.ndarray:
-        """Values as f32 (half buffers decoded exactly)."""
+        """Values as f32 (half buffers decoded exactly, packed weights dequantized)."""
         out = np.empty(buf.shape, dtype=np.float32)
         check(N.lib().mg_buffer_download_f32(buf.handle, out.ctypes.data, out.size))
         return out

@@ -222,6 +222,23 @@ void orc_softcap(const float* x, float* out, float cap, uint64_t n) {
     for (int64_t i = 0; i < (int64_t)n; i++) out[i] = cap * tanhf(x[i] / cap);
 }
 
+/* Q8_0 blocks (src/kernels.rs:309-330, 1800-1838; src/kernels.cu:230-246): 34 bytes each, a
+ * little-endian f16 scale d then 32 signed 8-bit quants q; value = q * d with d widened exactly.
+ * out is the logical matrix: the stored [rows, cols] one, or its transpose when transposed. */
+void orc_q8_0_dequantize(const uint8_t* blocks, uint64_t rows, uint64_t cols, int transposed, float* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < (int64_t)rows; r++) {
+        for (uint64_t c = 0; c < cols; c++) {
+            const uint64_t index = (uint64_t)r * cols + c, block = index / 32;
+            const uint8_t* b = blocks + block * 34;
+            const float d = orc_f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+            const float v = (float)(int8_t)b[2 + index % 32] * d;
+            if (transposed) out[c * rows + (uint64_t)r] = v;
+            else out[index] = v;
+        }
+    }
+}
+
 /* Host greedy selection (src/tests_conformance.rs:571-587, the Runtime's rule the device kernel
  * src/kernels.cu:1808-1866 matches): the first column, in column order, whose finite raw score,
  * outside every excluded [start, end) pair, divided by the temperature (as is when 0), is

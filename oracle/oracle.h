@@ -52,6 +52,7 @@ void orc_gelu_tanh(const float* x, float* out, uint64_t n);
 void orc_sigmoid(const float* x, float* out, uint64_t n);
 void orc_softcap(const float* x, float* out, float cap, uint64_t n);
 void orc_row_scale(const float* x, const float* scale, float* out, uint64_t rows, uint64_t cols);
+void orc_q8_0_dequantize(const uint8_t* blocks, uint64_t rows, uint64_t cols, int transposed, float* out);
 int64_t orc_greedy_select(const float* row, uint64_t cols, const uint64_t* ranges, uint32_t count, float temperature);
 void orc_concat_heads(const float* a, const float* b, float* out, uint64_t rows, uint64_t heads, uint64_t a_width,
                       uint64_t b_width, uint64_t b_heads);

@@ -233,6 +233,17 @@ def row_scale(x, scale):
     return o
 
 
+def q8_0_dequantize(blocks, stored_rows, stored_cols, transposed=True):
+    """src/kernels.rs:1800-1838 + src/kernels.cu:230-246: the logical f32 matrix of Q8_0 blocks"""
+    raw = np.ascontiguousarray(np.asarray(blocks, np.uint8).ravel())
+    assert raw.size == stored_rows * stored_cols // 32 * 34
+    shape = (stored_cols, stored_rows) if transposed else (stored_rows, stored_cols)
+    o, op = _out(shape)
+    lib().orc_q8_0_dequantize(raw.ctypes.data_as(ctypes.c_void_p), _u64(stored_rows), _u64(stored_cols),
+                              int(bool(transposed)), op)
+    return o
+
+
 def greedy_select(logits, row, excluded=(), temperature=0.0):
     """src/tests_conformance.rs:571-587 (host greedy selection); None when nothing is eligible"""
     x = np.ascontiguousarray(logits, np.float32)

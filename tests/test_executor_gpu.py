@@ -467,3 +467,28 @@ def test_select_greedy_column_over_a_resident_tensor(executor, oracle):
     assert executor.select_greedy_column("logits", 1, [(0, 16000)], 0.8) == oracle.greedy_select(logits, 1, [(0, 16000)], 0.8)
     assert executor.select_greedy_column("logits", 3) is None  # a row past the logits
     assert executor.select_greedy_column("missing", 0) is None
+
+
+def test_packed_weight_through_the_executor(executor, oracle):
+    # src/executor.rs:404-420: write_packed_weight_tensor, then matmul / gated-matmul invocations
+    # read it packed; a captured decode step over packed weights replays to the same result
+    from q8_cases import activations, packed_q8
+    k, n = 128, 64
+    gate, up = packed_q8(n, k, 21), packed_q8(n, k, 22)
+    executor.write_packed_weight_tensor("gate", gate, n, k)
+    executor.write_packed_weight_tensor("up", up, n, k)
+    a = activations(1, k, 9)
+    executor.write_tensor("x", a)
+    executor.run(inv("gated-matmul", ["x", "gate", "up"], "h"))
+    expected = oracle.gated_matmul(a, oracle.q8_0_dequantize(gate, n, k), oracle.q8_0_dequantize(up, n, k))
+    got = executor.read_tensor("h")
+    assert np.all(np.abs(got - expected) <= 1e-5 + 1e-5 * k)
+    assert executor.resident_shape("gate") == (k, n)
+    np.testing.assert_array_equal(executor.read_tensor("gate"), oracle.q8_0_dequantize(gate, n, k))
+    executor.begin_step_capture()
+    executor.run(inv("gated-matmul", ["x", "gate", "up"], "h2"))
+    executor.end_step_capture()
+    executor.replay_step()
+    np.testing.assert_array_equal(executor.read_tensor("h2"), got)
+    executor.copy_tensor("gate", "gate_copy")
+    np.testing.assert_array_equal(executor.read_tensor("gate_copy"), oracle.q8_0_dequantize(gate, n, k))

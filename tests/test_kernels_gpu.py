@@ -725,3 +725,103 @@ def test_greedy_select_many_ranges_and_wide_rows(kernels, oracle):
     # rank-3 logits: rows are the leading dimensions flattened
     x = r.standard_normal((2, 3, 50)).astype(np.float32)
     assert kernels.greedy_select(kernels.upload(x), 4) == oracle.greedy_select(x.reshape(6, 50), 4)
+
+
+def _close_scaled(actual, expected, scale):
+    # src/tests_conformance.rs:3370-3379: the packed kernels sum in another order than the
+    # reference CPU; |actual - expected| <= 1e-5 + 1e-5 * scale
+    assert actual.shape == expected.shape
+    assert np.all(np.abs(actual - expected) <= 1e-5 + 1e-5 * scale), np.max(np.abs(actual - expected))
+
+
+def test_q8_packed_matmul_matches_reference_cpu(kernels, oracle):
+    # src/tests_conformance.rs:3381-3438
+    from q8_cases import activations, packed_q8
+    k, n = 256, 96
+    blocks = packed_q8(n, k, 7)  # stored as n rows of k quants: the graph sees [k, n]
+    dense = oracle.q8_0_dequantize(blocks, n, k, transposed=True)
+    w = kernels.upload_q8_0(blocks, n, k, transposed=True)
+    assert w.is_q8() and w.is_compact() and w.shape == (k, n) and w.dtype == "q8_0"
+    np.testing.assert_array_equal(kernels.download(w), dense)
+    np.testing.assert_array_equal(kernels.download(kernels.dequantize_q8(w)), dense)
+    bias = (np.arange(n) * 0.01).astype(np.float32)
+    dbias = kernels.upload(bias)
+    for m in (1, 3, 8, 16, 64, 65):
+        a = activations(m, k, m)
+        expected = oracle.matmul(a, dense)
+        da = kernels.upload(a)
+        _close_scaled(kernels.download(kernels.matmul(da, w)), expected, k)
+        _close_scaled(kernels.download(kernels.matmul_bias(da, w, dbias)), expected + bias, k)
+        res = activations(m, n, 99)
+        _close_scaled(kernels.download(kernels.matmul_residual(da, w, kernels.upload(res))), expected + res, k)
+
+
+def test_q8_packed_gated_matmul_and_embedding_match_reference_cpu(kernels, oracle):
+    # src/tests_conformance.rs:4000-4040
+    from q8_cases import activations, packed_q8
+    k, n = 128, 64
+    gate, up = packed_q8(n, k, 11), packed_q8(n, k, 12)
+    dg, du = kernels.upload_q8_0(gate, n, k), kernels.upload_q8_0(up, n, k)
+    g_dense = oracle.q8_0_dequantize(gate, n, k)
+    u_dense = oracle.q8_0_dequantize(up, n, k)
+    for m in (1, 5, 70):
+        a = activations(m, k, 5)
+        expected = oracle.gated_matmul(a, g_dense, u_dense)
+        _close_scaled(kernels.download(kernels.gated_matmul(kernels.upload(a), dg, du)), expected, k)
+    # a [vocab = 6, hidden = 64] table stored untransposed, rows read packed
+    table = packed_q8(6, 64, 13)
+    dt = kernels.upload_q8_0(table, 6, 64, transposed=False)
+    ids = np.array([5.0, 0.0, 3.0, 5.0], np.float32)
+    np.testing.assert_array_equal(kernels.download(kernels.embedding_lookup(dt, kernels.upload(ids))),
+                                  oracle.embedding(oracle.q8_0_dequantize(table, 6, 64, transposed=False), ids)[0])
+
+
+def test_q8_packed_weights_at_real_checkpoint_sizes(kernels):
+    # src/tests_conformance.rs:4128-4205: a [151936, 896] table and the same blocks as an lm head
+    from q8_cases import activations, checkpoint_blocks
+    vocab, hidden = 151_936, 896
+    blocks, values = checkpoint_blocks(vocab, hidden)
+    table = kernels.upload_q8_0(blocks, vocab, hidden, transposed=False)
+    ids = [0, 1, 77_777, vocab - 1, 4242]
+    rows = kernels.download(kernels.embedding_lookup(table, kernels.upload(np.array(ids, np.float32))))
+    np.testing.assert_array_equal(rows, values[ids])
+    lm_head = kernels.upload_q8_0(blocks, vocab, hidden, transposed=True)
+    a = activations(5, hidden, 3)
+    logits = kernels.download(kernels.matmul(kernels.upload(a), lm_head))
+    assert logits.shape == (5, vocab)
+    cols = [0, 1, 31, 32, 99_999, vocab - 1]
+    expected = a.astype(np.float64) @ values[cols].T.astype(np.float64)
+    assert np.all(np.abs(logits[:, cols] - expected) <= 1e-3)
+
+
+def test_q8_packed_fallbacks_and_refusals(kernels, oracle, mpc):
+    from q8_cases import activations, packed_q8
+    # k not a multiple of 128, and untransposed storage: dequantized for the call
+    for stored_rows, stored_cols, transposed, m in ((40, 96, True, 2), (96, 64, False, 3), (64, 256, False, 1)):
+        blocks = packed_q8(stored_rows, stored_cols, 31)
+        w = kernels.upload_q8_0(blocks, stored_rows, stored_cols, transposed=transposed)
+        dense = oracle.q8_0_dequantize(blocks, stored_rows, stored_cols, transposed=transposed)
+        a = activations(m, dense.shape[0], 4)
+        _close_scaled(kernels.download(kernels.matmul(kernels.upload(a), w)), oracle.matmul(a, dense), dense.shape[0])
+        # B transposed by the caller reads the logical matrix transposed
+        at = activations(m, dense.shape[1], 6)
+        _close_scaled(kernels.download(kernels.matmul(kernels.upload(at), w, transpose_b=True)),
+                      oracle.matmul(at, dense.T.copy()), dense.shape[1])
+    w = kernels.upload_q8_0(packed_q8(64, 128, 3), 64, 128)
+    x = kernels.upload(np.ones((128, 64), np.float32))
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.add(w, x)
+    assert e.value.code == "DTypeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:  # rows of a transposed-storage table
+        kernels.embedding_lookup(w, kernels.upload(np.array([0.0], np.float32)))
+    assert e.value.code == "DTypeUnsupported"
+    t = kernels.upload_q8_0(packed_q8(6, 64, 13), 6, 64, transposed=False)
+    with pytest.raises(mpc.CudaError) as e:  # an id past the table
+        kernels.embedding_lookup(t, kernels.upload(np.array([6.0], np.float32)))
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:  # not whole blocks
+        kernels.upload_q8_0(np.zeros(33, np.uint8), 1, 32)
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        kernels.upload_q8_0(np.zeros(34, np.uint8), 2, 16)
+    assert e.value.code == "ShapeUnsupported"

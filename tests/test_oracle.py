@@ -177,3 +177,16 @@ def test_greedy_select_oracle_matches_the_host_rule(oracle):
     assert oracle.greedy_select(np.array([[-1.0, -0.0, 0.0]], np.float32), 0) == 1
     # nothing eligible
     assert oracle.greedy_select(np.array([[1.0, np.nan, 2.0]], np.float32), 0, [(0, 1), (2, 3)]) is None
+
+
+def test_q8_0_dequantize_known_answers(oracle):
+    from q8_cases import checkpoint_blocks, packed_q8
+    blocks, values = checkpoint_blocks(6, 64)
+    np.testing.assert_array_equal(oracle.q8_0_dequantize(blocks, 6, 64, transposed=False), values)
+    np.testing.assert_array_equal(oracle.q8_0_dequantize(blocks, 6, 64, transposed=True), values.T)
+    # against numpy's own f16 widening of the scales
+    raw = packed_q8(8, 96, 7).reshape(-1, 34)
+    d = raw[:, :2].copy().view(np.float16).astype(np.float32).ravel()
+    q = raw[:, 2:].view(np.int8).astype(np.float32)
+    np.testing.assert_array_equal(oracle.q8_0_dequantize(raw, 8, 96, transposed=False), (q * d[:, None]).reshape(8, 96))
+    assert q.min() >= -127 and q.max() <= 127 and (q.min(), q.max()) != (0, 0)
