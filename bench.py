@@ -293,6 +293,7 @@ def measure_tf32_peak(torch):
 
 
 EXACT_MS = (1, 16, 128, 2048)  # the matmul lines also timed with bfloat16-exact weights
+Q8_MS = (1, 16)  # and with packed Q8_0 weights (the few-row path reads them packed)
 ROT_COPIES = 6  # copies of the 64 MB B the M <= 128 lines rotate through (384 MB > the 126 MB L2)
 NODE_COPIES = 8  # instances of a layer node per timed step (per-node times)
 
@@ -356,17 +357,30 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
             # GEMM reads hi alone
             exact = [(x.view(torch.int32) & -65536).view(torch.float32) for x in copies]
             rot[" (bf16-exact weight)"] = [W(x).set_weight() for x in exact]
+        if any(want(f"matmul M={M} (Q8_0 weight)") for M in Q8_MS):
+            # packed Q8_0 weights (a checkpoint's [N, K] storage read as B [K, N]): seeded f16
+            # scales between 2^-9 and 2^-5 and quants over -127..127
+            rq = np.random.default_rng(5)
+            nb = N * K // 32
+            q8 = []
+            for _ in range(ROT_COPIES):
+                blk = np.empty((nb, 34), np.uint8)
+                blk[:, :2] = rq.uniform(2.0 ** -9, 2.0 ** -5, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+                blk[:, 2:] = rq.integers(-127, 128, (nb, 32), dtype=np.int8).view(np.uint8)
+                q8.append(kernels.upload_q8_0(blk, N, K, transposed=True))
+            rot[" (Q8_0 weight)"] = q8
         for M in (1, 16, 128, 2048, 8192):
             if not want(f"matmul M={M}"):
                 continue
             a = torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)
             c = torch.empty(M, N, device="cuda")
             da, dc = W(a), W(c)
-            for label in ("", " (B per-call)", " (bf16-exact weight)"):
+            for label in ("", " (B per-call)", " (bf16-exact weight)", " (Q8_0 weight)"):
                 exact = label == " (bf16-exact weight)"
-                if M <= 16 and label and not exact:
+                packed = label == " (Q8_0 weight)"
+                if M <= 16 and label == " (B per-call)":
                     continue  # the GEMV path reads B as it is either way
-                if label not in rot or (exact and M not in EXACT_MS):
+                if label not in rot or (exact and M not in EXACT_MS) or (packed and M not in Q8_MS):
                     continue
                 bufs = rot[label]
                 if M <= 128:
@@ -381,9 +395,9 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
                     ms = timed(call, n=max(iters, 15), reps=ROT_COPIES)
                 else:
                     ms = timed(lambda: kernels.matmul(da, bufs[0], out=dc), n=iters)
-                if M <= 16:  # B's bytes: 4 per value, 2 in the compact form
+                if M <= 16:  # B's bytes: 4 per value, 2 in the compact form, 1.125 packed (quant + f32 scale / 32)
                     add(f"matmul M={M}{label}", "configs[1]", ms, "hbm",
-                        4.0 * (M * K + M * N) + (2.0 if exact else 4.0) * K * N)
+                        4.0 * (M * K + M * N) + (2.0 if exact else 1.125 if packed else 4.0) * K * N)
                 else:
                     add(f"matmul M={M}{label}", "configs[1]", ms, "tensor", 2.0 * M * N * K)
             del a, c

@@ -926,19 +926,27 @@ mg_status mg_executor_copy_tensor(mg_executor* ex, const char* from, const char*
     Buffer* src = it->second;
     Buffer* nb = nullptr;
     MG_TRY(buffer_new(ex->device, src->dtype, src->rank, src->shape, &nb));
-    cudaError_t e = cudaMemcpyAsync(nb->ptr, src->ptr, src->count * dtype_size(src->dtype), cudaMemcpyDeviceToDevice,
-                                    ex->device->stream);
-    if (e == cudaSuccess && src->dtype == MG_Q8_0) {  // a packed weight: its scales too
+    cudaError_t e = cudaSuccess;
+    if (src->dtype == MG_Q8_0) {  // a packed weight: its layout, quants and scales
         nb->q8_rows = src->q8_rows;
         nb->q8_cols = src->q8_cols;
         nb->q8_transposed = src->q8_transposed;
-        const size_t sb = src->q8_rows * src->q8_cols / 32 * sizeof(float);
-        mg_status s = device_alloc(ex->device, sb, (void**)&nb->q8_scales);
+        nb->q8_tiled = src->q8_tiled;
+        device_free(ex->device, nb->ptr);
+        nb->ptr = nullptr;
+        mg_status s = device_alloc(ex->device, q8_quant_bytes(src), &nb->ptr);
+        if (s == MG_OK) s = device_alloc(ex->device, q8_scale_bytes(src), (void**)&nb->q8_scales);
         if (s != MG_OK) {
             buffer_free(nb);
             return s;
         }
-        e = cudaMemcpyAsync(nb->q8_scales, src->q8_scales, sb, cudaMemcpyDeviceToDevice, ex->device->stream);
+        e = cudaMemcpyAsync(nb->ptr, src->ptr, q8_quant_bytes(src), cudaMemcpyDeviceToDevice, ex->device->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(nb->q8_scales, src->q8_scales, q8_scale_bytes(src), cudaMemcpyDeviceToDevice,
+                                ex->device->stream);
+    } else {
+        e = cudaMemcpyAsync(nb->ptr, src->ptr, src->count * dtype_size(src->dtype), cudaMemcpyDeviceToDevice,
+                            ex->device->stream);
     }
     if (e != cudaSuccess) {
         buffer_free(nb);

@@ -129,7 +129,18 @@ struct Buffer {
     float* q8_scales = nullptr;
     uint64_t q8_rows = 0, q8_cols = 0;
     int q8_transposed = 0;
+    // Tiled layout (transposed storage with q8_cols a multiple of 128, the few-row matmul's
+    // operand): per 256 stored rows and 128 stored columns one contiguous 32 KB record of quants
+    // (each row's 128 quants in eight 16-byte pieces, piece j at position j ^ (row % 8)) and one
+    // 4 KB record of scales ([256][4]), records ordered tile-major; stored rows padded to a
+    // multiple of 256 with zeros.  Otherwise quants [q8_rows][q8_cols] and scales one per 32.
+    int q8_tiled = 0;
 };
+
+// Rows a packed weight's arrays hold (padded when tiled), and the arrays' bytes.
+inline uint64_t q8_rows_held(const Buffer* b) { return b->q8_tiled ? (b->q8_rows + 255) / 256 * 256 : b->q8_rows; }
+inline uint64_t q8_quant_bytes(const Buffer* b) { return q8_rows_held(b) * b->q8_cols; }
+inline uint64_t q8_scale_bytes(const Buffer* b) { return q8_rows_held(b) * b->q8_cols / 32 * sizeof(float); }
 
 // Weights smaller than this stay f32 only (src/kernels.rs:506-510).
 constexpr uint64_t kCompactMinElements = 1ull << 16;
@@ -251,7 +262,7 @@ mg_status gemm(Device* d, const GemmArgs& g);
 // Q8_0 packed weights: the 34-byte blocks split into quants and f32 scales; the logical matrix
 // (or, stored_order, the stored one) dequantized; embedding rows of a packed table; the matmul
 // with packed B (the few-row kernel, else dequantized for the call).
-mg_status q8_unpack(Device* d, const uint8_t* blocks, int8_t* quants, float* scales, uint64_t nblocks);
+mg_status q8_unpack(Device* d, const uint8_t* blocks, const Buffer* b);
 mg_status q8_dequantize(Device* d, const Buffer* b, float* out, bool stored_order);
 mg_status q8_embedding(Device* d, const Buffer* table, const float* ids, float* out, uint64_t num_ids, int* flag,
                        int has_scale, float scale);

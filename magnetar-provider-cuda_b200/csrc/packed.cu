@@ -5,15 +5,18 @@
 // exactly).  The few-row matmul streams the quants -- 1.125 bytes per weight value with the
 // scales -- against f32 activations; everything else reads the dequantized values q * d.
 //
-// The few-row kernel: a CTA owns 256 output columns (one per thread: a transposed-storage weight
-// keeps each output column's k quants contiguous) and one slice of k.  A producer lane streams
-// per stage, with TMA, the [256 columns x 128 k] quants (one 128-byte row per column, 128-byte
-// swizzle so that 32 threads reading their own rows hit distinct banks), the matching [256 x 4]
-// scales and [M x 128] of A; each thread widens its 128 quants to f32 exactly (byte permute into
-// the mantissa of 2^23 and one subtraction), multiplies them by every row of A (A read from shared
-// memory as a broadcast) and adds each 32-value block's sum times the block's scale.  The slices'
-// partials go to a workspace; the last CTA of a column tile adds them in slice order and applies
-// bias / residual / SwiGLU (deterministic).
+// A transposed-storage weight (each output column's k quants contiguous) whose k is a multiple of
+// 128 is unpacked into the tiled layout the few-row kernel streams: per 256 output columns and
+// 128 k one 32 KB record of quants, column after column (128 bytes each, its eight 16-byte pieces
+// permuted so that 32 threads reading their own columns' piece hit distinct banks), and one 4 KB
+// record of the matching [256][4] scales, records in column-tile-major order.  A CTA owns one
+// tile of 256 columns (one per thread) and one slice of k, i.e. one contiguous run of records: a
+// producer lane moves per stage the two records with two bulk copies and [M x 128] of A with TMA;
+// each thread widens its 128 quants to f32 exactly (byte permute into the mantissa of 2^23 and
+// one subtraction), multiplies them by every row of A (a broadcast read of shared memory) and
+// adds each 32-value block's sum times the block's scale.  The slices' partials go to a
+// workspace; the last CTA of a column tile adds them in slice order and applies bias / residual /
+// SwiGLU (deterministic).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -30,33 +33,54 @@ constexpr int kQ8Block = 32;       // quants per block
 constexpr int kQ8BlockBytes = 34;  // f16 scale + 32 quants
 constexpr int kQCols = 256;        // output columns per CTA, one per compute thread
 constexpr int kQChunk = 128;       // k per stage: four blocks, one 128-byte swizzled row per column
-constexpr int kQStages = 3;
-constexpr int kQMaxSplits = 64;
-constexpr uint64_t kQMaxTiles = 1u << 16;  // Device::counters entries
 
-// One thread per block: the scale widened to f32 (exact) and the 32 quants stored contiguous.
-__global__ void __launch_bounds__(256) q8_unpack_kernel(const uint8_t* __restrict__ blocks, int8_t* __restrict__ quants,
-                                                        float* __restrict__ scales, uint64_t nblocks) {
+// Where stored element (r, c) of a packed weight lives: its quant's byte offset and its scale's
+// index, in the plain or the tiled layout (c a multiple of 16 addresses 16 contiguous quants).
+struct Q8View {
+    const int8_t* q;
+    const float* s;
+    uint64_t rows, cols, chunks;  // chunks = cols / 128 (tiled)
+    int tiled;
+};
+__device__ __forceinline__ uint64_t q8_qoff(const Q8View& v, uint64_t r, uint64_t c) {
+    if (!v.tiled) return r * v.cols + c;
+    const uint64_t rec = (r >> 8) * v.chunks + (c >> 7);
+    const uint32_t piece = (uint32_t)((c & 127) >> 4) ^ (uint32_t)(r & 7);
+    return ((rec << 8) + (r & 255)) * kQChunk + (piece << 4) + (c & 15);
+}
+__device__ __forceinline__ uint64_t q8_soff(const Q8View& v, uint64_t r, uint64_t c) {
+    if (!v.tiled) return (r * v.cols + c) >> 5;
+    const uint64_t rec = (r >> 8) * v.chunks + (c >> 7);
+    return ((rec << 8) + (r & 255)) * 4 + ((c & 127) >> 5);
+}
+
+// One thread per block: the scale widened to f32 (exact) and the 32 quants stored as the layout
+// places them.
+__global__ void __launch_bounds__(256) q8_unpack_kernel(const uint8_t* __restrict__ blocks, Q8View v, uint64_t nblocks) {
     pdl_enter();
+    int8_t* quants = const_cast<int8_t*>(v.q);
+    float* scales = const_cast<float*>(v.s);
+    const uint64_t per_row = v.cols / kQ8Block;
     for (uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += (uint64_t)gridDim.x * blockDim.x) {
         const uint16_t* src = reinterpret_cast<const uint16_t*>(blocks + b * kQ8BlockBytes);  // 2-byte aligned
-        scales[b] = __half2float(__ushort_as_half(src[0]));
+        const uint64_t r = b / per_row, c = (b % per_row) * kQ8Block;
+        scales[q8_soff(v, r, c)] = __half2float(__ushort_as_half(src[0]));
         uint32_t w[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) w[i] = (uint32_t)src[1 + 2 * i] | ((uint32_t)src[2 + 2 * i] << 16);
-        uint4* dst = reinterpret_cast<uint4*>(quants + b * kQ8Block);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        *reinterpret_cast<uint4*>(quants + q8_qoff(v, r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(quants + q8_qoff(v, r, c + 16)) = make_uint4(w[4], w[5], w[6], w[7]);
     }
 }
 
 // out = q * d in stored order, 16 values per thread and step (src/kernels.cu:230-246).
-__global__ void __launch_bounds__(256) q8_dequantize_kernel(const int8_t* __restrict__ quants, const float* __restrict__ scales,
-                                                            float* __restrict__ out, uint64_t groups) {
+__global__ void __launch_bounds__(256) q8_dequantize_kernel(Q8View v, float* __restrict__ out, uint64_t groups) {
     pdl_enter();
+    const uint64_t per_row = v.cols / 16;
     for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (uint64_t)gridDim.x * blockDim.x) {
-        const uint4 q = reinterpret_cast<const uint4*>(quants)[g];
-        const float d = scales[g >> 1];  // two 16-value groups per block
+        const uint64_t r = g / per_row, c = (g % per_row) * 16;
+        const uint4 q = *reinterpret_cast<const uint4*>(v.q + q8_qoff(v, r, c));
+        const float d = v.s[q8_soff(v, r, c)];
         const int8_t* b = reinterpret_cast<const int8_t*>(&q);
         float4* o = reinterpret_cast<float4*>(out) + 4 * g;
 #pragma unroll
@@ -67,24 +91,19 @@ __global__ void __launch_bounds__(256) q8_dequantize_kernel(const int8_t* __rest
 
 // The logical matrix of a transposed-storage weight: out[c, r] = q[r, c] * d, through 32 x 32
 // tiles so that both the quants and the output are read and written along rows.
-__global__ void __launch_bounds__(256) q8_dequantize_transpose_kernel(const int8_t* __restrict__ quants,
-                                                                      const float* __restrict__ scales, float* __restrict__ out,
-                                                                      uint64_t stored_rows, uint64_t stored_cols) {
+__global__ void __launch_bounds__(256) q8_dequantize_transpose_kernel(Q8View v, float* __restrict__ out) {
     pdl_enter();
     __shared__ float tile[32][33];
-    const uint64_t r0 = (uint64_t)blockIdx.y * 32, c0 = (uint64_t)blockIdx.x * 32;  // stored_cols % 32 == 0
+    const uint64_t r0 = (uint64_t)blockIdx.y * 32, c0 = (uint64_t)blockIdx.x * 32;  // cols % 32 == 0
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     for (int i = ty; i < 32; i += 8) {
         const uint64_t r = r0 + i;
-        if (r < stored_rows) {
-            const uint64_t idx = r * stored_cols + c0 + tx;
-            tile[i][tx] = (float)quants[idx] * scales[idx >> 5];
-        }
+        if (r < v.rows) tile[i][tx] = (float)v.q[q8_qoff(v, r, c0 + tx)] * v.s[q8_soff(v, r, c0 + tx)];
     }
     __syncthreads();
     for (int i = ty; i < 32; i += 8) {
         const uint64_t r = r0 + tx;
-        if (r < stored_rows) out[(c0 + i) * stored_rows + r] = tile[tx][i];
+        if (r < v.rows) out[(c0 + i) * v.rows + r] = tile[tx][i];
     }
 }
 
@@ -115,26 +134,58 @@ __global__ void __launch_bounds__(256) q8_embedding_kernel(const int8_t* __restr
     }
 }
 
-// Four quants (one 32-bit word) widened to f32 exactly: each byte, offset by 128 to unsigned,
-// becomes the low mantissa byte of 2^23 (byte permute) and the sum 2^23 + 128 is subtracted.
-__device__ __forceinline__ void q8_widen4(uint32_t w, float& a, float& b, float& c, float& d) {
-    const uint32_t u = w ^ 0x80808080u;
-    constexpr float kBias = 8388736.0f;  // 2^23 + 128
-    a = __uint_as_float(__byte_perm(u, 0x4B00u, 0x5440u)) - kBias;
-    b = __uint_as_float(__byte_perm(u, 0x4B00u, 0x5441u)) - kBias;
-    c = __uint_as_float(__byte_perm(u, 0x4B00u, 0x5442u)) - kBias;
-    d = __uint_as_float(__byte_perm(u, 0x4B00u, 0x5443u)) - kBias;
+// Packed pairs of f32 (Blackwell's two-lane f32 arithmetic): each lane rounds as the scalar form.
+__device__ __forceinline__ uint64_t q8_pack(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t q8_packf(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t q8_sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ void q8_fma2(uint64_t& d, uint64_t a, uint64_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float q8_sum2(uint64_t v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo + hi;
 }
 
+// Sixteen quants (one 16-byte piece) widened to f32 exactly, as eight packed pairs: each byte,
+// offset by 128 to unsigned, becomes the low mantissa byte of 2^23 (byte permute) and 2^23 + 128
+// is subtracted from both lanes of a pair at once.
+__device__ __forceinline__ void q8_widen16(uint4 q, uint64_t* f) {
+    const uint64_t bias = q8_packf(8388736.0f, 8388736.0f);  // 2^23 + 128
+    const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        f[2 * i] = q8_sub2(q8_pack(__byte_perm(w[i], 0x4B00u, 0x5440u), __byte_perm(w[i], 0x4B00u, 0x5441u)), bias);
+        f[2 * i + 1] = q8_sub2(q8_pack(__byte_perm(w[i], 0x4B00u, 0x5442u), __byte_perm(w[i], 0x4B00u, 0x5443u)), bias);
+    }
+}
+
+constexpr int kQMaxCluster = 16;  // k slices x terms of one column tile (above 8 only where one wave holds them)
+
 struct Q8GemvArgs {
-    float* partial;  // [terms][splits][m][n]
+    const int8_t* quants[2];  // tiled quants of the weight (z = 0) and, gated, the up weight (z = 1)
+    const float* scales[2];
+    uint64_t chunks;          // k / 128: records per column tile
     float* out;
     const float* addend;
     int addend_mode;  // 0 none, 1 row [n], 2 full [m, n]
     int terms;        // 1, or 2 for gated (gate: z = 0, up: z = 1)
+    int splits;       // k slices; the cluster is (1, splits, terms)
+    int band;         // floats of the flattened [m][256] partial each cluster CTA finishes (multiple of 4)
     uint64_t m, n, k, slice_len;  // slice_len a multiple of kQChunk
     int* error;
-    unsigned int* counters;  // per column tile; zero between calls (the last CTA resets it)
 };
 
 template <int M>
@@ -142,52 +193,69 @@ struct Q8Shape {
     static constexpr int kQ = kQCols * kQChunk;                      // 32 KB of quants
     static constexpr int kS = kQCols * (kQChunk / kQ8Block) * 4;     // 4 KB of scales, [256][4]
     static constexpr int kA = M * kQChunk * 4;                       // [M][128] of A
-    static constexpr int kStage = (kQ + kS + kA + 1023) / 1024 * 1024;  // quants stay 1024-aligned (swizzle atom)
+    static constexpr int kStage = (kQ + kS + kA + 127) / 128 * 128;
+    static constexpr int kStages = M == 1 ? 3 : 2;                   // two CTAs fit an SM
+    static constexpr int kPart = M * kQCols * 4;                     // this CTA's partial, in the drained ring
+    static constexpr int kRecv = (M * kQCols + 4 * kQMaxCluster) * 4;  // the other CTAs' partials of this CTA's band
     static constexpr int kThreads = kQCols + 32;                     // 8 compute warps + the producer
-    static constexpr int kSmem = 1024 + kQStages * kStage + 16 * kQStages;
+    static_assert(kPart <= kStages * kStage, "the partial fits the drained ring");
+    static constexpr int kSmem = 128 + kStages * kStage + kRecv + 8 * (2 * kStages + 1);
+    static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs fit an SM");
 };
 
+// The k slices of one column tile (and, gated, both terms) form a cluster: each CTA stages its
+// [m][256] partial in its drained ring and sends every band of it to the CTA that owns the band
+// (one bulk copy into that CTA's receive region); owners add the partials in slice order and
+// apply bias / residual / SwiGLU -- deterministic, and nothing goes through global memory.
 template <int M>
 __global__ void __launch_bounds__(Q8Shape<M>::kThreads) q8_gemv_kernel(const __grid_constant__ CUtensorMap map_a,
-                                                                      const __grid_constant__ CUtensorMap map_q,
-                                                                      const __grid_constant__ CUtensorMap map_s,
-                                                                      const __grid_constant__ CUtensorMap map_q2,
-                                                                      const __grid_constant__ CUtensorMap map_s2,
-                                                                      Q8GemvArgs p) {
+                                                                      const __grid_constant__ Q8GemvArgs p) {
     using namespace sm100;
     using S = Q8Shape<M>;
+    constexpr int kQStages = S::kStages;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ unsigned int s_last;
     const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t base = (raw + 127u) & ~127u;
     uint8_t* base_ptr = smem_raw + (base - raw);
-    const uint32_t bar0 = base + kQStages * S::kStage;
+    const uint32_t recv = base + kQStages * S::kStage;
+    const uint32_t bar0 = recv + S::kRecv;
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kQStages + s); };
+    const uint32_t recv_bar = bar0 + 8u * (2 * kQStages);
+    float* partf = reinterpret_cast<float*>(base_ptr);
+    const float* recvf = reinterpret_cast<const float*>(base_ptr + kQStages * S::kStage);
     const int tid = threadIdx.x, warp = tid >> 5;
     const uint64_t col0 = (uint64_t)blockIdx.x * kQCols;
     const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
     const uint64_t k1 = min(p.k, k0 + p.slice_len);
     const int chunks = k1 > k0 ? (int)((k1 - k0) / kQChunk) : 0;
-    const CUtensorMap* mq = blockIdx.z ? &map_q2 : &map_q;
-    const CUtensorMap* ms = blockIdx.z ? &map_s2 : &map_s;
+    const int nc = p.splits * p.terms;
+    const int rank = (int)blockIdx.y + p.splits * (int)blockIdx.z;  // the cluster spans y and z whole
+    const int F = (int)p.m * kQCols;
+    const int my_lo = min(F, rank * p.band), my_hi = min(F, my_lo + p.band);
+    // this CTA's records: column tile blockIdx.x, chunks from k0 / 128 on
+    const uint64_t rec0 = (uint64_t)blockIdx.x * p.chunks + k0 / kQChunk;
+    const int8_t* qrec = p.quants[blockIdx.z] + rec0 * S::kQ;
+    const float* srec = p.scales[blockIdx.z] + rec0 * (S::kS / 4);
 
     if (tid == 0) {
         for (int s = 0; s < kQStages; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), kQCols / 32);
         }
+        mbar_init(recv_bar, 1);
         fence_barrier_init();
-        // The packed weight is written only by an upload: its first stages load before the
-        // dependency wait.
+        mbar_arrive_expect_tx(recv_bar, (uint32_t)((nc - 1) * (my_hi - my_lo) * 4));
+        // The packed weight is written only by an upload (which completes before it returns):
+        // its first stages load before the dependency wait.
         for (int c = 0; c < min(chunks, kQStages); c++) {
             const uint32_t st = base + (uint32_t)(c * S::kStage);
-            const int kk = (int)(k0 + (uint64_t)c * kQChunk);
             mbar_arrive_expect_tx(full_bar(c), (uint32_t)(S::kQ + S::kS + S::kA));
-            tma_load_2d(st, mq, full_bar(c), kk, (int)col0);
-            tma_load_2d(st + S::kQ, ms, full_bar(c), kk / kQ8Block, (int)col0);
+            bulk_load(st, qrec + (uint64_t)c * S::kQ, S::kQ, full_bar(c));
+            bulk_load(st + S::kQ, srec + (uint64_t)c * (S::kS / 4), S::kS, full_bar(c));
         }
     }
+    cluster_arrive();  // phase 1: every CTA's receive barrier is armed before anyone sends
     pdl_enter();
     __syncthreads();
 
@@ -207,8 +275,8 @@ __global__ void __launch_bounds__(Q8Shape<M>::kThreads) q8_gemv_kernel(const __g
                         break;
                     }
                     mbar_arrive_expect_tx(full_bar(s), (uint32_t)(S::kQ + S::kS + S::kA));
-                    tma_load_2d(st, mq, full_bar(s), kk, (int)col0);
-                    tma_load_2d(st + S::kQ, ms, full_bar(s), kk / kQ8Block, (int)col0);
+                    bulk_load(st, qrec + (uint64_t)c * S::kQ, S::kQ, full_bar(s));
+                    bulk_load(st + S::kQ, srec + (uint64_t)c * (S::kS / 4), S::kS, full_bar(s));
                 }
                 tma_load_2d(st + S::kQ + S::kS, &map_a, full_bar(s), kk, 0);
             }
@@ -216,7 +284,7 @@ __global__ void __launch_bounds__(Q8Shape<M>::kThreads) q8_gemv_kernel(const __g
         __syncwarp();
     } else {
         // ---- compute: thread tid owns output column col0 + tid --------------------------------
-        const uint32_t sw = (uint32_t)(tid & 7);  // the 128-byte swizzle's chunk permutation for this row
+        const uint32_t sw = (uint32_t)(tid & 7);  // the piece permutation of this column's record row
         for (int c = 0; c < chunks; c++) {
             const int s = c % kQStages;
             if (!mbar_wait(full_bar(s), (uint32_t)(c / kQStages) & 1u)) {
@@ -230,80 +298,73 @@ __global__ void __launch_bounds__(Q8Shape<M>::kThreads) q8_gemv_kernel(const __g
             const float scl[4] = {sc.x, sc.y, sc.z, sc.w};
 #pragma unroll
             for (int blk = 0; blk < 4; blk++) {
-                const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + (((2u * blk) ^ sw) << 4));
-                const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + (((2u * blk + 1u) ^ sw) << 4));
-                float f[32];
-                q8_widen4(q0.x, f[0], f[1], f[2], f[3]);
-                q8_widen4(q0.y, f[4], f[5], f[6], f[7]);
-                q8_widen4(q0.z, f[8], f[9], f[10], f[11]);
-                q8_widen4(q0.w, f[12], f[13], f[14], f[15]);
-                q8_widen4(q1.x, f[16], f[17], f[18], f[19]);
-                q8_widen4(q1.y, f[20], f[21], f[22], f[23]);
-                q8_widen4(q1.z, f[24], f[25], f[26], f[27]);
-                q8_widen4(q1.w, f[28], f[29], f[30], f[31]);
+                uint64_t f[16];  // the block's 32 quants as f32 pairs
+                q8_widen16(*reinterpret_cast<const uint4*>(qrow + (((2u * blk) ^ sw) << 4)), f);
+                q8_widen16(*reinterpret_cast<const uint4*>(qrow + (((2u * blk + 1u) ^ sw) << 4)), f + 8);
 #pragma unroll
                 for (int r = 0; r < M; r++) {
                     const float* ar = a_s + r * kQChunk + blk * kQ8Block;
-                    float s0 = 0.0f, s1 = 0.0f;
+                    // even and odd k of the block in the two lanes, two chains per row
+                    uint64_t s2a = 0ull, s2b = 0ull;
 #pragma unroll
                     for (int j = 0; j < kQ8Block; j += 8) {
                         const float4 x0 = *reinterpret_cast<const float4*>(ar + j);
                         const float4 x1 = *reinterpret_cast<const float4*>(ar + j + 4);
-                        s0 = fmaf(x0.x, f[j], s0);
-                        s1 = fmaf(x0.y, f[j + 1], s1);
-                        s0 = fmaf(x0.z, f[j + 2], s0);
-                        s1 = fmaf(x0.w, f[j + 3], s1);
-                        s0 = fmaf(x1.x, f[j + 4], s0);
-                        s1 = fmaf(x1.y, f[j + 5], s1);
-                        s0 = fmaf(x1.z, f[j + 6], s0);
-                        s1 = fmaf(x1.w, f[j + 7], s1);
+                        q8_fma2(s2a, q8_packf(x0.x, x0.y), f[j / 2]);
+                        q8_fma2(s2b, q8_packf(x0.z, x0.w), f[j / 2 + 1]);
+                        q8_fma2(s2a, q8_packf(x1.x, x1.y), f[j / 2 + 2]);
+                        q8_fma2(s2b, q8_packf(x1.z, x1.w), f[j / 2 + 3]);
                     }
-                    acc[r] = fmaf(scl[blk], s0 + s1, acc[r]);
+                    acc[r] = fmaf(scl[blk], q8_sum2(s2a) + q8_sum2(s2b), acc[r]);
                 }
             }
             __syncwarp();
             if ((tid & 31) == 0) mbar_arrive(empty_bar(s));
         }
-        // this slice's partial, one coalesced row per output row
-        const uint64_t col = col0 + tid;
-        if (col < p.n) {
-            float* part = p.partial + ((uint64_t)blockIdx.z * gridDim.y + blockIdx.y) * p.m * p.n;
-#pragma unroll
-            for (int r = 0; r < M; r++)
-                if ((uint64_t)r < p.m) part[(uint64_t)r * p.n + col] = acc[r];
-        }
     }
-    // ---- the last CTA of this column tile (over slices and gate / up) finishes it --------------
-    __threadfence();
+    // ---- this CTA's partial, [m][256] in the drained ring ----------------------------------------
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&p.counters[blockIdx.x], 1u) == gridDim.y * gridDim.z - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
     if (tid < kQCols) {
-        const uint64_t col = col0 + tid;
-        const int splits = (int)gridDim.y;
-        const uint64_t mn = p.m * p.n;
-        if (col < p.n) {
-            for (uint64_t r = 0; r < p.m; r++) {
-                const uint64_t off = r * p.n + col;
-                float g = 0.0f;
-                for (int sl = 0; sl < splits; sl++) g += __ldcg(p.partial + (uint64_t)sl * mn + off);
-                float v;
-                if (p.terms == 2) {
-                    float u = 0.0f;
-                    for (int sl = 0; sl < splits; sl++) u += __ldcg(p.partial + ((uint64_t)splits + sl) * mn + off);
-                    v = (g * (1.0f / (1.0f + expf(-g)))) * u;
-                } else {
-                    v = g;
-                    if (p.addend_mode == 1) v += p.addend[col];
-                    else if (p.addend_mode == 2) v += p.addend[off];
-                }
-                p.out[off] = v;
-            }
+#pragma unroll
+        for (int r = 0; r < M; r++)
+            if ((uint64_t)r < p.m) partf[r * kQCols + tid] = acc[r];
+    }
+    fence_proxy_async();  // the partial is read by bulk copies next
+    __syncthreads();
+    // ---- exchange: each band of the partial to the CTA that owns it ---------------------------
+    cluster_wait();  // phase 1
+    if (tid == 0) {
+        for (int o = 0; o < nc; o++) {
+            if (o == rank) continue;
+            const int lo = min(F, o * p.band), hi = min(F, lo + p.band);
+            if (hi > lo)
+                bulk_copy_to_cluster(mapa(recv + (uint32_t)(rank * p.band * 4), (uint32_t)o), base + (uint32_t)(lo * 4),
+                                     (uint32_t)((hi - lo) * 4), mapa(recv_bar, (uint32_t)o));
         }
     }
-    if (tid == 0) p.counters[blockIdx.x] = 0u;
+    if (!mbar_wait(recv_bar, 0)) atomicExch(p.error, 1);
+    cluster_arrive();  // phase 2: every copy into this CTA has landed
+    // ---- finish this CTA's band: slices in order, per term -----------------------------------
+    for (int e = my_lo + tid; e < my_hi; e += blockDim.x) {
+        const int r = e / kQCols, c = e % kQCols;
+        const uint64_t col = col0 + c;
+        if (col >= p.n) continue;
+        auto from = [&](int src) { return src == rank ? partf[e] : recvf[src * p.band + (e - my_lo)]; };
+        float g = 0.0f;
+        for (int sl = 0; sl < p.splits; sl++) g += from(sl);
+        float v;
+        if (p.terms == 2) {
+            float u = 0.0f;
+            for (int sl = 0; sl < p.splits; sl++) u += from(p.splits + sl);
+            v = (g * (1.0f / (1.0f + expf(-g)))) * u;
+        } else {
+            v = g;
+            if (p.addend_mode == 1) v += p.addend[col];
+            else if (p.addend_mode == 2) v += p.addend[(uint64_t)r * p.n + col];
+        }
+        p.out[(uint64_t)r * p.n + col] = v;
+    }
+    cluster_wait();  // phase 2: every copy out of this CTA's shared memory has landed
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 q8_encode_fn() {
@@ -334,16 +395,64 @@ mg_status q8_map(CUtensorMap* map, CUtensorMapDataType type, void* ptr, uint64_t
 }
 
 template <int M>
-mg_status launch_q8_gemv(Device* d, dim3 grid, const CUtensorMap* maps, const Q8GemvArgs& p) {
+mg_status launch_q8_gemv(Device* d, dim3 grid, const CUtensorMap& map_a, const Q8GemvArgs& p) {
     using S = Q8Shape<M>;
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
         MG_CUDA(cudaFuncSetAttribute(q8_gemv_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
                 "configuring the packed gemv kernel");
+        MG_CUDA(cudaFuncSetAttribute(q8_gemv_kernel<M>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "allowing the packed gemv kernel clusters of up to 16");
         configured[d->ordinal & 63] = true;
     }
-    enqueue(d, q8_gemv_kernel<M>, grid, S::kThreads, S::kSmem, maps[0], maps[1], maps[2], maps[3], maps[4], p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(S::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = grid.y;
+    attr[0].val.clusterDim.z = grid.z;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = d->pdl ? 2 : 1;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, q8_gemv_kernel<M>, map_a, p), "packed gemv launch");
     return launched(d, "packed gemv launch");
+}
+
+// Whether all `tiles` clusters of `nc` CTAs of q8_gemv_kernel<M> fit the GPU at once (the
+// occupancy query, once per size and device); sizes up to 8 always launch.
+template <int M>
+bool q8_cluster_fits(Device* d, int nc, uint64_t tiles, int terms) {
+    using S = Q8Shape<M>;
+    if (nc <= 8) return true;
+    static int active[64][kQMaxCluster + 1];  // clusters the GPU holds at once, + 1 (0: not asked yet)
+    int& a = active[d->ordinal & 63][nc];
+    if (a == 0) {
+        int clusters = 0;
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(1, (unsigned)(nc / terms), (unsigned)terms);
+        q.blockDim = dim3(S::kThreads, 1, 1);
+        q.dynamicSmemBytes = S::kSmem;
+        cudaLaunchAttribute ca;
+        ca.id = cudaLaunchAttributeClusterDimension;
+        ca.val.clusterDim.x = 1;
+        ca.val.clusterDim.y = (unsigned)(nc / terms);
+        ca.val.clusterDim.z = (unsigned)terms;
+        q.attrs = &ca;
+        q.numAttrs = 1;
+        if (cudaFuncSetAttribute(q8_gemv_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(q8_gemv_kernel<M>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+            cudaOccupancyMaxActiveClusters(&clusters, q8_gemv_kernel<M>, &q) != cudaSuccess) {
+            (void)cudaGetLastError();
+            clusters = 0;
+        }
+        a = clusters + 1;
+    }
+    return (uint64_t)(a - 1) >= tiles;
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
@@ -352,25 +461,36 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15)
 
 namespace k {
 
-mg_status q8_unpack(Device* d, const uint8_t* blocks, int8_t* quants, float* scales, uint64_t nblocks) {
+Q8View view(const Buffer* b) {
+    Q8View v;
+    v.q = static_cast<const int8_t*>(b->ptr);
+    v.s = b->q8_scales;
+    v.rows = b->q8_rows;
+    v.cols = b->q8_cols;
+    v.chunks = b->q8_cols / kQChunk;
+    v.tiled = b->q8_tiled;
+    return v;
+}
+
+mg_status q8_unpack(Device* d, const uint8_t* blocks, const Buffer* b) {
+    const uint64_t nblocks = b->q8_rows * b->q8_cols / kQ8Block;
     uint64_t grid = (nblocks + 255) / 256;
     if (grid > (uint64_t)d->sm_count * 8) grid = (uint64_t)d->sm_count * 8;
-    enqueue(d, q8_unpack_kernel, (unsigned)(grid ? grid : 1), 256, 0, blocks, quants, scales, nblocks);
+    enqueue(d, q8_unpack_kernel, (unsigned)(grid ? grid : 1), 256, 0, blocks, view(b), nblocks);
     return launched(d, "packed weight unpack launch");
 }
 
 mg_status q8_dequantize(Device* d, const Buffer* b, float* out, bool stored_order) {
-    const int8_t* q = static_cast<const int8_t*>(b->ptr);
     if (stored_order || !b->q8_transposed) {
         const uint64_t groups = b->q8_rows * b->q8_cols / 16;
         uint64_t grid = (groups + 255) / 256;
         if (grid > (uint64_t)d->sm_count * 8) grid = (uint64_t)d->sm_count * 8;
-        enqueue(d, q8_dequantize_kernel, (unsigned)(grid ? grid : 1), 256, 0, q, (const float*)b->q8_scales, out, groups);
+        enqueue(d, q8_dequantize_kernel, (unsigned)(grid ? grid : 1), 256, 0, view(b), out, groups);
         return launched(d, "packed weight dequantize launch");
     }
     if ((b->q8_rows + 31) / 32 > 65535) return fail(MG_SHAPE_UNSUPPORTED, "packed weight has too many stored rows");
     dim3 grid((unsigned)(b->q8_cols / 32), (unsigned)((b->q8_rows + 31) / 32));
-    enqueue(d, q8_dequantize_transpose_kernel, grid, 256, 0, q, (const float*)b->q8_scales, out, b->q8_rows, b->q8_cols);
+    enqueue(d, q8_dequantize_transpose_kernel, grid, 256, 0, view(b), out);
     return launched(d, "packed weight dequantize launch");
 }
 
@@ -383,58 +503,68 @@ mg_status q8_embedding(Device* d, const Buffer* table, const float* ids, float* 
     return launched(d, "packed embedding launch");
 }
 
-// The few-row kernel takes a matmul when every B is a transposed-storage packed weight, A is
-// contiguous and 16-byte aligned, M <= 16 and k is a multiple of 128 (the scales' rows then
-// stay 16-byte multiples for TMA).
+// The few-row kernel takes a matmul when every B is a tiled packed weight (transposed storage,
+// k a multiple of 128), A is contiguous and 16-byte aligned and M <= 16.
 bool q8_gemv_eligible(const GemmArgs& g) {
     const int terms = g.gated ? 2 : 1;
     for (int t = 0; t < terms; t++)
-        if (!g.packed[t] || !g.packed[t]->q8_transposed) return false;
+        if (!g.packed[t] || !g.packed[t]->q8_tiled) return false;
     return g.m >= 1 && g.m <= 16 && !g.transpose_a && !g.transpose_b && g.k % kQChunk == 0 && aligned16(g.a) &&
-           (g.n + kQCols - 1) / kQCols <= kQMaxTiles && g.k < (1ull << 31) && g.n < (1ull << 31);
+           g.k < (1ull << 31) && g.n < (1ull << 31);
 }
 
 mg_status q8_gemv(Device* d, const GemmArgs& g) {
     const uint64_t tiles = (g.n + kQCols - 1) / kQCols;
     const int terms = g.gated ? 2 : 1;
     const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
-    // k slices for about two CTAs per SM (one at the larger row counts)
-    const uint64_t per_sm = mp <= 1 ? 2 : 1;
+    // k slices for about two CTAs per SM, at most a portable cluster of them per column tile
     const uint64_t chunks = g.k / kQChunk;
-    uint64_t splits = ((uint64_t)d->sm_count * per_sm + tiles * terms - 1) / (tiles * terms);
+    uint64_t splits = ((uint64_t)d->sm_count * 2 + tiles * terms - 1) / (tiles * terms);
+    if (splits > (uint64_t)(kQMaxCluster / terms)) splits = kQMaxCluster / terms;
     if (splits > chunks) splits = chunks;
-    if (splits > (uint64_t)kQMaxSplits) splits = kQMaxSplits;
     if (splits < 1) splits = 1;
+    // clusters above 8 CTAs only where the GPU holds them (non-portable sizes)
+    auto fits = [&](int nc) {
+        switch (mp) {
+            case 1: return q8_cluster_fits<1>(d, nc, tiles, terms);
+            case 2: return q8_cluster_fits<2>(d, nc, tiles, terms);
+            case 4: return q8_cluster_fits<4>(d, nc, tiles, terms);
+            case 8: return q8_cluster_fits<8>(d, nc, tiles, terms);
+            default: return q8_cluster_fits<16>(d, nc, tiles, terms);
+        }
+    };
+    while (splits * terms > 8 && !fits((int)(splits * terms))) splits--;
     Q8GemvArgs p;
     p.slice_len = (chunks + splits - 1) / splits * kQChunk;
     splits = (g.k + p.slice_len - 1) / p.slice_len;
+    p.splits = (int)splits;
+    p.terms = terms;
+    const int nc = p.splits * terms, F = (int)g.m * kQCols;
+    p.band = ((F + nc - 1) / nc + 3) / 4 * 4;
     p.out = g.out;
     p.addend = g.addend;
     p.addend_mode = g.addend_mode;
-    p.terms = terms;
     p.m = g.m;
     p.n = g.n;
     p.k = g.k;
     p.error = d->flags + 2;
-    p.counters = d->counters;
-    MG_TRY(scratch(d, 0, (size_t)terms * splits * g.m * g.n * sizeof(float), (void**)&p.partial));
-    CUtensorMap maps[5];
-    MG_TRY(q8_map(&maps[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, const_cast<float*>(g.a), g.k, g.m, g.k * 4, kQChunk,
-                  (uint32_t)mp, CU_TENSOR_MAP_SWIZZLE_NONE));
     for (int t = 0; t < 2; t++) {
         const Buffer* w = g.packed[t < terms ? t : 0];
-        MG_TRY(q8_map(&maps[1 + 2 * t], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->ptr, g.k, g.n, g.k, kQChunk, kQCols,
-                      CU_TENSOR_MAP_SWIZZLE_128B));
-        MG_TRY(q8_map(&maps[2 + 2 * t], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->q8_scales, g.k / kQ8Block, g.n,
-                      g.k / kQ8Block * 4, kQChunk / kQ8Block, kQCols, CU_TENSOR_MAP_SWIZZLE_NONE));
+        p.quants[t] = static_cast<const int8_t*>(w->ptr);
+        p.scales[t] = w->q8_scales;
     }
+    p.chunks = chunks;
+    CUtensorMap map_a;
+    MG_TRY(q8_map(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, const_cast<float*>(g.a), g.k, g.m, g.k * 4, kQChunk,
+                  (uint32_t)mp, CU_TENSOR_MAP_SWIZZLE_NONE));
+    if (tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "packed gemv n %llu is too wide", (unsigned long long)g.n);
     dim3 grid((unsigned)tiles, (unsigned)splits, (unsigned)terms);
     switch (mp) {
-        case 1: return launch_q8_gemv<1>(d, grid, maps, p);
-        case 2: return launch_q8_gemv<2>(d, grid, maps, p);
-        case 4: return launch_q8_gemv<4>(d, grid, maps, p);
-        case 8: return launch_q8_gemv<8>(d, grid, maps, p);
-        default: return launch_q8_gemv<16>(d, grid, maps, p);
+        case 1: return launch_q8_gemv<1>(d, grid, map_a, p);
+        case 2: return launch_q8_gemv<2>(d, grid, map_a, p);
+        case 4: return launch_q8_gemv<4>(d, grid, map_a, p);
+        case 8: return launch_q8_gemv<8>(d, grid, map_a, p);
+        default: return launch_q8_gemv<16>(d, grid, map_a, p);
     }
 }
 

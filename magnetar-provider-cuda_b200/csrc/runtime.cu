@@ -600,14 +600,23 @@ mg_status mg_buffer_upload_q8_0(mg_device* h, const void* blocks, uint64_t bytes
     b->q8_rows = stored_rows;
     b->q8_cols = stored_cols;
     b->q8_transposed = transposed ? 1 : 0;
+    b->q8_tiled = transposed && stored_cols % 128 == 0 ? 1 : 0;
     void* staging = nullptr;
-    mg_status s = device_alloc(d, nblocks * sizeof(float), (void**)&b->q8_scales);
+    mg_status s = MG_OK;
+    if (b->q8_tiled) {  // padded: the allocation buffer_new made is too small
+        device_free(d, b->ptr);
+        b->ptr = nullptr;
+        s = device_alloc(d, q8_quant_bytes(b), &b->ptr);
+        if (s == MG_OK) s = k::fill_zero(d, b->ptr, q8_quant_bytes(b));
+    }
+    if (s == MG_OK) s = device_alloc(d, q8_scale_bytes(b), (void**)&b->q8_scales);
+    if (s == MG_OK && b->q8_tiled) s = k::fill_zero(d, b->q8_scales, q8_scale_bytes(b));
     if (s == MG_OK) s = device_alloc(d, bytes, &staging);
     if (s == MG_OK) {
         cudaError_t e = cudaMemcpyAsync(staging, blocks, bytes, cudaMemcpyHostToDevice, d->stream);
         s = e == cudaSuccess ? MG_OK : from_cuda(e, "uploading");
     }
-    if (s == MG_OK) s = k::q8_unpack(d, (const uint8_t*)staging, (int8_t*)b->ptr, b->q8_scales, nblocks);
+    if (s == MG_OK) s = k::q8_unpack(d, (const uint8_t*)staging, b);
     if (staging) device_free(d, staging);
     // Settled before it returns: the packed few-row matmul starts loading a packed weight before
     // its dependency wait, so no kernel that writes one may still be running then.

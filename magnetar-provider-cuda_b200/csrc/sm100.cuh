@@ -124,6 +124,14 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src,
                  : "memory");
 }
 
+// Bulk copy of `bytes` contiguous global bytes into this CTA's shared memory (both 16-byte
+// aligned, bytes a multiple of 16), completing on `mbar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(mbar)
+                 : "memory");
+}
+
 // ---- tcgen05 -------------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols) : "memory");
