@@ -600,6 +600,24 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
         for (uint64_t d = threadIdx.x; d < D; d += kDecodeThreads) qs[g][d] = p.q[(h0 + g) * D + d];
     __syncthreads();  // the barriers' initialisation and q are visible
     const int sk = lane >> 3, sc4 = (lane & 7) * 4;  // scores: key sk of the warp's 4, columns sc4 + 32 i
+    // Up to 4 query heads with head dimensions up to 128 (C = 1 is launched only then): this
+    // lane's 16 query columns per head stay in registers for the whole span instead of being
+    // re-read from shared memory per key.
+    constexpr bool kQRegs = C == 1 && G <= 4;
+    float qr[kQRegs ? G : 1][kQRegs ? 16 : 1];
+    if constexpr (kQRegs) {
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint64_t d = sc4 + 32 * i;
+                const float4 qv = d < D ? *reinterpret_cast<const float4*>(&qs[g][d]) : make_float4(0.f, 0.f, 0.f, 0.f);
+                qr[g][4 * i] = qv.x;
+                qr[g][4 * i + 1] = qv.y;
+                qr[g][4 * i + 2] = qv.z;
+                qr[g][4 * i + 3] = qv.w;
+            }
+    }
     // P.V: this lane's output columns 4 lane + 128 i + e, slot i * 4 + e
     float m[G], l[G], acc[G][4 * C];
 #pragma unroll
@@ -624,12 +642,24 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
         float sc[G];
 #pragma unroll
         for (int g = 0; g < G; g++) sc[g] = 0.0f;
-        for (uint64_t d = sc4; d < D; d += 32) {
-            const float4 kv = *reinterpret_cast<const float4*>(ks + (uint64_t)j * D + d);
+        if constexpr (kQRegs) {
 #pragma unroll
-            for (int g = 0; g < G; g++) {
-                const float4 qv = *reinterpret_cast<const float4*>(&qs[g][d]);
-                sc[g] += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+            for (int i = 0; i < 4; i++) {
+                const uint64_t d = sc4 + 32 * i;
+                if (d >= D) break;
+                const float4 kv = *reinterpret_cast<const float4*>(ks + (uint64_t)j * D + d);
+#pragma unroll
+                for (int g = 0; g < G; g++)
+                    sc[g] += qr[g][4 * i] * kv.x + qr[g][4 * i + 1] * kv.y + qr[g][4 * i + 2] * kv.z + qr[g][4 * i + 3] * kv.w;
+            }
+        } else {
+            for (uint64_t d = sc4; d < D; d += 32) {
+                const float4 kv = *reinterpret_cast<const float4*>(ks + (uint64_t)j * D + d);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const float4 qv = *reinterpret_cast<const float4*>(&qs[g][d]);
+                    sc[g] += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+                }
             }
         }
         const uint64_t key = first + (uint64_t)t * kc + j;
@@ -851,7 +881,7 @@ mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
         const int G = (p.group == 2 || p.group == 4 || p.group == 8) ? (int)p.group : 1;
         const int smem = decode_tma_smem(G, a.head_dim, a.value_dim);
         int per_sm = 1;
-        const bool wide = a.value_dim > 128;
+        const bool wide = a.value_dim > 128 || a.head_dim > 128;  // C = 2 (C = 1 holds q in registers)
 #define MG_DECODE_OCC(GG)                                                              \
     if (wide) {                                                                        \
         MG_TRY((configure_decode_tma<GG, 2>(d)));                                      \
@@ -880,7 +910,7 @@ mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
         CUtensorMap maps[2];
         MG_TRY(decode_map(&maps[0], a.k, a.kv_rows, a.kv_model_dim, (uint32_t)a.head_dim, (uint32_t)kc));
         MG_TRY(decode_map(&maps[1], a.v, a.kv_rows, a.v_model_dim, (uint32_t)a.value_dim, (uint32_t)kc));
-        const bool wide = a.value_dim > 128;
+        const bool wide = a.value_dim > 128 || a.head_dim > 128;  // C = 2 (C = 1 holds q in registers)
         mg_status ls = MG_OK;
         switch (p.group) {
             case 2: ls = wide ? launch_decode_tma<2, 2>(d, p, maps, span, by_kv) : launch_decode_tma<2, 1>(d, p, maps, span, by_kv); break;
