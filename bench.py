@@ -593,14 +593,10 @@ def run_ours(args, world, rank, local):
     # ---- e2e through the public API with host buffers ---------------------------------------
     ids_host = torch.from_numpy(w["ids"]).pin_memory()
     out_host = torch.empty((cfg.seq, cfg.hidden), dtype=torch.float32).pin_memory()
-    native = importlib.import_module(PACKAGE + "._native")
-    ids_buf = ex.buffer("ids")
-    out_buf = ex.buffer("out")
 
-    def e2e_step():
-        native.check(native.lib().mg_buffer_upload(ids_buf.handle, ids_host.data_ptr(), ids_host.numel() * 4))
-        ex.replay_steps(1)  # includes the embedding-id check (a 4-byte read)
-        native.check(native.lib().mg_buffer_download(out_buf.handle, out_host.data_ptr(), out_host.numel() * 4))
+    # one public call per step: the ids copied in, the captured layer replayed, the output copied
+    # out, one synchronisation (which also covers the embedding-id check)
+    e2e_step = ex.step_io({"ids": ids_host}, {"out": out_host})
 
     for _ in range(max(3, args.warmup)):
         e2e_step()

@@ -399,6 +399,17 @@ mg_status mg_executor_check_steps(mg_executor* ex);
  * replays use offset 0.  A decode loop captures one step and replays it at 0, 1, 2, ... */
 mg_status mg_executor_begin_step_capture_advancing(mg_executor* ex, const char* const* attributes, int count);
 mg_status mg_executor_replay_step_at(mg_executor* ex, uint64_t offset);
+/* One replay with its host I/O (src/executor.rs replay_step(id, offset, inputs) followed by the
+ * step's reads): each to_device entry's `bytes` are copied into the captured buffer of `id`
+ * before the replay, each other entry's buffer is copied to `host` after it, and one
+ * synchronisation covers them and the embedding-id check.  `bytes` must equal the buffer's. */
+typedef struct mg_step_io {
+    const char* id;
+    void* host;
+    uint64_t bytes;
+    int to_device; /* 1: input written before the replay; 0: output read after it */
+} mg_step_io;
+mg_status mg_executor_replay_step_io(mg_executor* ex, uint64_t offset, const mg_step_io* io, int count);
 /* The largest offset the captured step accepts (UINT64_MAX: unbounded). */
 mg_status mg_executor_step_max_offset(mg_executor* ex, uint64_t* out);
 /* Observation log (src/executor.rs:1082-1100): counts of Started/Completed/Failed. */

@@ -172,6 +172,7 @@ SIGNATURES = {
     "mg_executor_begin_step_capture": [_P],
     "mg_executor_begin_step_capture_advancing": [_P, ctypes.POINTER(ctypes.c_char_p), _I],
     "mg_executor_replay_step_at": [_P, _U64],
+    "mg_executor_replay_step_io": [_P, _U64, _P, _I],
     "mg_executor_step_max_offset": [_P, _U64P],
     "mg_executor_end_step_capture": [_P],
     "mg_executor_abort_step_capture": [_P],
@@ -209,6 +210,12 @@ def build(force: bool = False) -> str:
         subprocess.run(["make", "-C", CSRC, "clean"], check=True, stdout=subprocess.DEVNULL)
     subprocess.run(["make", "-C", CSRC, "-j", jobs], check=True, stdout=subprocess.DEVNULL)
     return LIB_PATH
+
+
+class StepIO(ctypes.Structure):
+    """mg_step_io: one host input (to_device 1) or output (0) of a replay."""
+    _fields_ = [("id", ctypes.c_char_p), ("host", ctypes.c_void_p), ("bytes", ctypes.c_uint64),
+                ("to_device", ctypes.c_int)]
 
 
 def range_pairs(ranges):

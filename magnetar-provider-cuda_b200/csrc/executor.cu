@@ -1117,6 +1117,56 @@ mg_status replay_at(mg_executor* ex, int count, uint64_t offset) {
 
 mg_status mg_executor_replay_steps(mg_executor* ex, int count) { return replay_at(ex, count, 0); }
 
+// src/executor.rs replay_step(id, offset, inputs) with the step's outputs read in the same call:
+// the inputs' host bytes are copied into their captured buffers, the step replays at `offset`,
+// the outputs are copied out, and one synchronisation covers them and the embedding-id check.
+mg_status mg_executor_replay_step_io(mg_executor* ex, uint64_t offset, const mg_step_io* io, int count) {
+    if (!ex || (count > 0 && !io) || count < 0) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
+    MG_TRY(device_check(ex->handle));
+    Device* d = ex->device;
+    if (offset > ex->step_max_offset)
+        return fail(MG_CAPTURE_UNSUPPORTED, "offset %llu leaves the captured bounds (at most %llu)",
+                    (unsigned long long)offset, (unsigned long long)ex->step_max_offset);
+    std::vector<Buffer*> bufs((size_t)count);
+    for (int i = 0; i < count; i++) {
+        if (!io[i].id || (!io[i].host && io[i].bytes)) return fail(MG_INVALID_ARGUMENT, "null argument");
+        auto it = ex->storage.find(io[i].id);
+        if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", io[i].id);
+        Buffer* b = it->second;
+        if (b->dtype == MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "resource %s is a packed weight", io[i].id);
+        if (io[i].bytes != b->count * dtype_size(b->dtype))
+            return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes do not match resource %s of shape %s",
+                        (unsigned long long)io[i].bytes, io[i].id, shape_str(b).c_str());
+        bufs[(size_t)i] = b;
+    }
+    for (int i = 0; i < count; i++) {
+        if (!io[i].to_device || !io[i].bytes) continue;
+        buffer_drop_prep(bufs[(size_t)i]);
+        MG_CUDA(cudaMemcpyAsync(bufs[(size_t)i]->ptr, io[i].host, io[i].bytes, cudaMemcpyHostToDevice, d->stream),
+                "writing a step input");
+        d->uploads.fetch_add(1);
+    }
+    if (ex->step_advancing) MG_TRY(k::set_step_offset(d, d->step_offset, offset));
+    MG_CUDA(cudaGraphLaunch(ex->graph_exec, d->stream), "replaying the captured step");
+    d->launches.fetch_add(ex->graph_kernels);
+    for (int i = 0; i < count; i++) {
+        if (io[i].to_device || !io[i].bytes) continue;
+        MG_CUDA(cudaMemcpyAsync(io[i].host, bufs[(size_t)i]->ptr, io[i].bytes, cudaMemcpyDeviceToHost, d->stream),
+                "reading a step output");
+        d->downloads.fetch_add(1);
+    }
+    if (ex->step_has_embedding) {
+        MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading the id flag");
+        MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
+    }
+    MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
+    if (ex->step_has_embedding && d->host_flags[0])
+        return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
+    return MG_OK;
+}
+
 mg_status mg_executor_replay_step_at(mg_executor* ex, uint64_t offset) { return replay_at(ex, 1, offset); }
 
 mg_status mg_executor_step_max_offset(mg_executor* ex, uint64_t* out) {

@@ -229,6 +229,41 @@ class CudaExecutor:
         else:
             check(N.lib().mg_executor_replay_step(self._h))
 
+    def replay_step_io(self, inputs: Mapping[str, object] = None, outputs: Mapping[str, object] = None,
+                       offset: int = 0) -> None:
+        """One replay with its host I/O in one call (``replay_step(id, offset, inputs)`` plus the
+        step's reads): ``inputs`` / ``outputs`` map ids to contiguous host arrays (numpy arrays or
+        pinned torch tensors) of exactly the buffers' bytes; one synchronisation covers the
+        copies and the embedding-id check."""
+        self.step_io(inputs, outputs)(offset)
+
+    def step_io(self, inputs: Mapping[str, object] = None, outputs: Mapping[str, object] = None):
+        """The host I/O of ``replay_step_io`` described once: returns ``replay(offset=0)``, which
+        replays with those arrays (their contents may change between calls, not their storage)."""
+        entries = []
+        keep = []
+        for mapping, to_dev in ((inputs or {}, 1), (outputs or {}, 0)):
+            for id, arr in mapping.items():
+                if hasattr(arr, "data_ptr"):  # a torch tensor
+                    ptr, nbytes = arr.data_ptr(), arr.numel() * arr.element_size()
+                else:
+                    a = np.asarray(arr)
+                    if not a.flags["C_CONTIGUOUS"] or (not to_dev and not a.flags["WRITEABLE"]):
+                        raise ValueError(f"{id}: host arrays must be contiguous (and writable for outputs)")
+                    ptr, nbytes = a.ctypes.data, a.nbytes
+                key = id.encode()
+                keep.append(key)
+                entries.append(N.StepIO(key, ptr, nbytes, to_dev))
+        arr_t = (N.StepIO * max(1, len(entries)))(*entries)
+        ptr, count, fn, h = ctypes.cast(arr_t, ctypes.c_void_p), len(entries), N.lib().mg_executor_replay_step_io, self._h
+        refs = (arr_t, keep, inputs, outputs)  # kept alive with the closure
+
+        def replay(offset: int = 0) -> None:
+            check(fn(h, offset, ptr, count))
+
+        replay.refs = refs
+        return replay
+
     def step_max_offset(self) -> int:
         """The largest offset the captured step accepts (2**64 - 1: unbounded)."""
         v = ctypes.c_uint64()

@@ -492,3 +492,31 @@ def test_packed_weight_through_the_executor(executor, oracle):
     np.testing.assert_array_equal(executor.read_tensor("h2"), got)
     executor.copy_tensor("gate", "gate_copy")
     np.testing.assert_array_equal(executor.read_tensor("gate_copy"), oracle.q8_0_dequantize(gate, n, k))
+
+
+def test_replay_step_with_host_io(executor, oracle, mpc):
+    # replay_step(id, offset, inputs) with the outputs read in the same call: new ids flow in,
+    # the layer's output comes back, one synchronisation; a bad id is still reported
+    layer = importlib.import_module("magnetar-provider-cuda_b200.layer")
+    cfg = layer.DecoderLayerConfig()
+    w = layer.make_inputs(cfg, seed=0)
+    layer.load(executor, w)
+    layer.forward(executor, cfg)
+    layer.capture(executor, cfg)
+    out = np.empty((cfg.seq, cfg.hidden), np.float32)
+    for seed in (1, 2):
+        ids = np.random.default_rng(seed).integers(0, cfg.vocab, cfg.seq).astype(np.float32)
+        executor.replay_step_io({"ids": ids}, {"out": out})
+        assert rel(out, _oracle_layer(oracle, cfg, dict(w, ids=ids))) <= 1e-4
+        np.testing.assert_array_equal(out, executor.read_tensor("out"))
+    bad = ids.copy()
+    bad[0] = -1.0
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_step_io({"ids": bad}, {"out": out})
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:  # bytes must match the buffer
+        executor.replay_step_io({"ids": ids[:5].copy()})
+    assert e.value.code == "ShapeUnsupported"
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_step_io(outputs={"missing": out})
+    assert e.value.code == "ExecutionFailed"
