@@ -463,7 +463,10 @@ template <int M, bool H = false>
 struct GemvCShape {
     static constexpr bool kTrans = M >= 8;
     static constexpr int kThreads = (kWarps + 1 + (kTrans ? 1 : 0)) * 32;
-    static constexpr int kStages = H ? (M >= 16 ? 7 : 8) : kCStages;
+    // 16 rows hold 64 accumulator registers per thread: one CTA per SM (no spills) with a ring
+    // twice as deep; fewer rows, two CTAs per SM.
+    static constexpr int kMinBlocks = M >= 16 ? 1 : 2;
+    static constexpr int kStages = M >= 16 ? (H ? 14 : 8) : (H ? 8 : kCStages);
     static constexpr int kB = kChunkRows * kCols * (H ? 2 : 4);  // 16 KB (8 KB compact) of B per stage
     static constexpr int kA = M * kChunkRows * 4;      // [M][32] of A per stage
     static constexpr int kStage = kB + kA;
@@ -488,7 +491,7 @@ __device__ __forceinline__ float4 gemv_b4(const uint8_t* tile, int row, int lane
 }
 
 template <int M, bool H>
-__global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
+__global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::kMinBlocks) gemv_cluster_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                           const __grid_constant__ CUtensorMap map_b,
                                                                           const __grid_constant__ CUtensorMap map_b2,
                                                                           GemvClusterArgs p) {
@@ -915,10 +918,11 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     const uint64_t col_tiles = (g.n + kCols - 1) / kCols;
     if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
     const int terms = g.gated ? 2 : 1;
-    uint64_t splits = (uint64_t)d->sm_count * 2 / (col_tiles * terms);
+    const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
+    const uint64_t per_sm = mp >= 16 ? 1 : 2;  // GemvCShape<mp>::kMinBlocks
+    uint64_t splits = (uint64_t)d->sm_count * per_sm / (col_tiles * terms);
     const uint64_t max_splits = kMaxClusterCtas / terms;
     if (splits > max_splits) splits = max_splits;
-    const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
     GemvClusterArgs p;
     p.out = g.out;
     p.addend = g.addend;
