@@ -548,7 +548,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(16) float qs[G][kDecodeMaxDim];
     __shared__ float wm[8][G], wl[8][G];
-    __shared__ uint64_t bars[kDecodeStages];
+    __shared__ uint64_t bars[kDecodeStages], empty[kDecodeStages];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 127u) & ~127u;
     float* smem_f = reinterpret_cast<float*>(smem_raw + (base - raw));
@@ -591,7 +591,10 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
         tma_load_2d(dst + k_bytes, &map_v, smem_u32(&bars[st]), (int)(kvh * DV), key);
     };
     if (threadIdx.x == 0) {
-        for (int st = 0; st < kDecodeStages; st++) mbar_init(smem_u32(&bars[st]), 1);
+        for (int st = 0; st < kDecodeStages; st++) {
+            mbar_init(smem_u32(&bars[st]), 1);
+            mbar_init(smem_u32(&empty[st]), kDecodeThreads / 32);  // every warp leaves the stage
+        }
         fence_barrier_init();
         for (int t = 0; t < min(tiles, kDecodeStages); t++) issue(t);
     }
@@ -631,9 +634,9 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
     for (int t = 0; t < tiles; t++) {
         const int st = t % kDecodeStages;
         if (!mbar_wait(smem_u32(&bars[st]), (uint32_t)(t / kDecodeStages) & 1u)) ok = false;
-        if (__syncthreads_or(!ok)) {
+        if (!__all_sync(0xffffffffu, ok)) {  // warps run ahead of one another: no CTA barrier per tile
             ok = false;
-            if (threadIdx.x == 0) atomicExch(p.error, 1);
+            if (lane == 0) atomicExch(p.error, 1);
             break;
         }
         const float* ks = smem_f + (uint64_t)st * (stage_bytes / 4);
@@ -702,9 +705,19 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
                 }
             }
         }
-        __syncthreads();  // every warp is done with this stage
-        if (threadIdx.x == 0 && t + kDecodeStages < tiles) issue(t + kDecodeStages);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty[st]));  // this warp is done with the stage
+        if (threadIdx.x == 0 && t + kDecodeStages < tiles) {
+            // the stage refills once every warp has left it
+            if (mbar_wait(smem_u32(&empty[st]), (uint32_t)(t / kDecodeStages) & 1u)) {
+                issue(t + kDecodeStages);
+            } else {
+                ok = false;  // the other warps' waits for this tile run out in turn
+                atomicExch(p.error, 1);
+            }
+        }
     }
+    ok = __syncthreads_and(ok) != 0;
     if (!ok) {  // give the copies in flight a second bound before the CTA exits
         if (threadIdx.x == 0)
             for (int st = 0; st < min(tiles, kDecodeStages); st++) (void)mbar_wait(smem_u32(&bars[st]), 0);
@@ -827,23 +840,71 @@ mg_status configure_decode_tma(Device* d) {
     return MG_OK;
 }
 
+// The spans' partials of one query head merged (src/kernels.cu:2301-2800, attention_combine):
+// the common max over the spans, each span's weight exp(m - max) (kept in shared memory for up
+// to kCombineWeights spans), the weighted sum of the span sums, and the output columns as the
+// weighted sums of the span outputs in span order, eight spans' loads in flight per step.
+constexpr int kCombineWeights = 2048;
+
 __global__ void __launch_bounds__(kDecodeKeys) attention_combine_kernel(DecodeP p) {
     pdl_enter();
+    __shared__ float wts[kCombineWeights];
+    __shared__ float red[kDecodeKeys / 32];
     const uint64_t h = blockIdx.x;
-    const float* base = p.partial + h * p.chunks * (p.value_dim + 2);
-    float mx = __int_as_float(0xff800000);
-    for (uint64_t c = 0; c < p.chunks; c++) mx = fmaxf(mx, base[c * (p.value_dim + 2)]);
-    float l = 0.0f;
-    for (uint64_t c = 0; c < p.chunks; c++) {
-        const float mc = base[c * (p.value_dim + 2)];
-        if (mc != __int_as_float(0xff800000)) l += base[c * (p.value_dim + 2) + 1] * expf(mc - mx);
+    const uint64_t stride = p.value_dim + 2;
+    const float* base = p.partial + h * p.chunks * stride;
+    const float kNegInf = __int_as_float(0xff800000);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    auto block_max = [&](float v) {
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float r = red[0];
+        for (int w = 1; w < kDecodeKeys / 32; w++) r = fmaxf(r, red[w]);
+        __syncthreads();
+        return r;
+    };
+    auto block_sum = [&](float v) {  // a fixed order: lanes by butterfly, then warps in order
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float r = red[0];
+        for (int w = 1; w < kDecodeKeys / 32; w++) r += red[w];
+        __syncthreads();
+        return r;
+    };
+    float mx = kNegInf;
+    for (uint64_t c = threadIdx.x; c < p.chunks; c += kDecodeKeys) mx = fmaxf(mx, base[c * stride]);
+    mx = block_max(mx);
+    const bool cached = p.chunks <= (uint64_t)kCombineWeights;
+    float ls = 0.0f;
+    for (uint64_t c = threadIdx.x; c < p.chunks; c += kDecodeKeys) {
+        const float mc = base[c * stride];
+        const float w = mc != kNegInf ? expf(mc - mx) : 0.0f;
+        if (cached) wts[c] = w;
+        ls += base[c * stride + 1] * w;
     }
+    const float l = block_sum(ls);  // its barriers also publish wts
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     for (uint64_t d = threadIdx.x; d < p.value_dim; d += kDecodeKeys) {
+        const float* col = base + 2 + d;
         float o = 0.0f;
-        for (uint64_t c = 0; c < p.chunks; c++) {
-            const float mc = base[c * (p.value_dim + 2)];
-            if (mc != __int_as_float(0xff800000)) o += base[c * (p.value_dim + 2) + 2 + d] * expf(mc - mx);
+        for (uint64_t c0 = 0; c0 < p.chunks; c0 += 8) {
+            float v[8], w[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const uint64_t c = c0 + u;
+                v[u] = c < p.chunks ? col[c * stride] : 0.0f;
+                if (cached) {
+                    w[u] = c < p.chunks ? wts[c] : 0.0f;
+                } else {
+                    const float mc = c < p.chunks ? base[c * stride] : kNegInf;
+                    w[u] = mc != kNegInf ? expf(mc - mx) : 0.0f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (c0 + u < p.chunks) o += v[u] * w[u];
         }
         p.out[h * p.value_dim + d] = o * inv;
     }
