@@ -557,6 +557,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
     const uint64_t c = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t D = p.head_dim, DV = p.value_dim;
+    const uint32_t D32 = (uint32_t)D, DV32 = (uint32_t)DV;  // shared-memory offsets stay 32-bit
     const uint32_t k_bytes = (uint32_t)(4 * kc * D);
     const uint32_t stage_bytes = (uint32_t)(4 * kc * (D + DV));
     pdl_enter();  // K and V may have just been written (kv-write)
@@ -607,7 +608,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
     // lane's 16 query columns per head stay in registers for the whole span instead of being
     // re-read from shared memory per key.
     constexpr bool kQRegs = C == 1 && G <= 4;
-    float qr[kQRegs ? G : 1][kQRegs ? 16 : 1];
+    uint64_t q2[kQRegs ? G : 1][kQRegs ? 8 : 1];  // column pairs (sc4 + 32 i + 2 h, + 1), slot 2 i + h
     if constexpr (kQRegs) {
 #pragma unroll
         for (int g = 0; g < G; g++)
@@ -615,20 +616,19 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
             for (int i = 0; i < 4; i++) {
                 const uint64_t d = sc4 + 32 * i;
                 const float4 qv = d < D ? *reinterpret_cast<const float4*>(&qs[g][d]) : make_float4(0.f, 0.f, 0.f, 0.f);
-                qr[g][4 * i] = qv.x;
-                qr[g][4 * i + 1] = qv.y;
-                qr[g][4 * i + 2] = qv.z;
-                qr[g][4 * i + 3] = qv.w;
+                q2[g][2 * i] = f2(qv.x, qv.y);
+                q2[g][2 * i + 1] = f2(qv.z, qv.w);
             }
     }
-    // P.V: this lane's output columns 4 lane + 128 i + e, slot i * 4 + e
-    float m[G], l[G], acc[G][4 * C];
+    // P.V: this lane's output columns 4 lane + 128 i + e as packed pairs, slot 2 i + e / 2
+    float m[G], l[G];
+    uint64_t acc2[G][2 * C];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         m[g] = kNegInf;
         l[g] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4 * C; e++) acc[g][e] = 0.0f;
+        for (int e = 0; e < 2 * C; e++) acc2[g][e] = 0ull;
     }
     bool ok = true;
     for (int t = 0; t < tiles; t++) {
@@ -646,14 +646,25 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
 #pragma unroll
         for (int g = 0; g < G; g++) sc[g] = 0.0f;
         if constexpr (kQRegs) {
+            uint64_t s2[G];  // even and odd columns, one lane each
+#pragma unroll
+            for (int g = 0; g < G; g++) s2[g] = 0ull;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const uint64_t d = sc4 + 32 * i;
-                if (d >= D) break;
-                const float4 kv = *reinterpret_cast<const float4*>(ks + (uint64_t)j * D + d);
+                const uint32_t d = (uint32_t)sc4 + 32u * i;
+                if (d >= D32) break;
+                const float4 kv = *reinterpret_cast<const float4*>(ks + (uint32_t)j * D32 + d);
+                const uint64_t k01 = f2(kv.x, kv.y), k23 = f2(kv.z, kv.w);
 #pragma unroll
-                for (int g = 0; g < G; g++)
-                    sc[g] += qr[g][4 * i] * kv.x + qr[g][4 * i + 1] * kv.y + qr[g][4 * i + 2] * kv.z + qr[g][4 * i + 3] * kv.w;
+                for (int g = 0; g < G; g++) {
+                    f2fma(s2[g], q2[g][2 * i], k01);
+                    f2fma(s2[g], q2[g][2 * i + 1], k23);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float2 sv = f2split(s2[g]);
+                sc[g] = sv.x + sv.y;
             }
         } else {
             for (uint64_t d = sc4; d < D; d += 32) {
@@ -676,32 +687,33 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
             tmx = fmaxf(tmx, __shfl_xor_sync(0xffffffffu, tmx, 16));
             const float m_new = fmaxf(m[g], tmx);
             float ex = 0.0f, alpha = 1.0f;
-            if (m_new != kNegInf) {  // some key admitted so far
-                alpha = m[g] == kNegInf ? 0.0f : expf(m[g] - m_new);
+            if (m_new != kNegInf) {  // some key admitted so far (the fast exponential: arguments <= 0)
+                alpha = m[g] == kNegInf ? 0.0f : __expf(m[g] - m_new);
                 m[g] = m_new;
-                ex = sc[g] != kNegInf ? expf(sc[g] - m_new) : 0.0f;
+                ex = sc[g] != kNegInf ? __expf(sc[g] - m_new) : 0.0f;
             }
             float es = ex + __shfl_xor_sync(0xffffffffu, ex, 8);
             es += __shfl_xor_sync(0xffffffffu, es, 16);
             l[g] = l[g] * alpha + es;
 #pragma unroll
             for (int k = 0; k < 4; k++) pk[g][k] = __shfl_sync(0xffffffffu, ex, k * 8);
+            const uint64_t alpha2 = f2(alpha, alpha);
 #pragma unroll
-            for (int e = 0; e < 4 * C; e++) acc[g][e] *= alpha;
+            for (int e = 0; e < 2 * C; e++) acc2[g][e] = f2mul(acc2[g][e], alpha2);
         }
 #pragma unroll
         for (int i = 0; i < C; i++) {
-            const uint64_t d = 4 * (uint64_t)lane + 128 * (uint64_t)i;
-            if (d >= DV) break;
+            const uint32_t d = 4u * lane + 128u * i;
+            if (d >= DV32) break;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const float4 vv = *reinterpret_cast<const float4*>(vs + (uint64_t)(jb + k) * DV + d);
+                const float4 vv = *reinterpret_cast<const float4*>(vs + (uint32_t)(jb + k) * DV32 + d);
+                const uint64_t v01 = f2(vv.x, vv.y), v23 = f2(vv.z, vv.w);
 #pragma unroll
                 for (int g = 0; g < G; g++) {
-                    acc[g][i * 4 + 0] += pk[g][k] * vv.x;
-                    acc[g][i * 4 + 1] += pk[g][k] * vv.y;
-                    acc[g][i * 4 + 2] += pk[g][k] * vv.z;
-                    acc[g][i * 4 + 3] += pk[g][k] * vv.w;
+                    const uint64_t pp = f2(pk[g][k], pk[g][k]);
+                    f2fma(acc2[g][2 * i], pp, v01);
+                    f2fma(acc2[g][2 * i + 1], pp, v23);
                 }
             }
         }
@@ -742,8 +754,9 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
         for (int i = 0; i < C; i++) {
             const uint64_t d = 4 * (uint64_t)lane + 128 * (uint64_t)i;
             if (d >= DV) break;
+            const float2 a01 = f2split(acc2[g][2 * i]), a23 = f2split(acc2[g][2 * i + 1]);
             *reinterpret_cast<float4*>(wo + ((uint64_t)warp * G + g) * DV + d) =
-                make_float4(acc[g][i * 4] * sc, acc[g][i * 4 + 1] * sc, acc[g][i * 4 + 2] * sc, acc[g][i * 4 + 3] * sc);
+                make_float4(a01.x * sc, a01.y * sc, a23.x * sc, a23.y * sc);
         }
     }
     __syncthreads();
