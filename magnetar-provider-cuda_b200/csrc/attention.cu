@@ -685,21 +685,24 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
             sc[g] = live ? sc[g] * p.scale : kNegInf;
             float tmx = fmaxf(sc[g], __shfl_xor_sync(0xffffffffu, sc[g], 8));
             tmx = fmaxf(tmx, __shfl_xor_sync(0xffffffffu, tmx, 16));
-            const float m_new = fmaxf(m[g], tmx);
-            float ex = 0.0f, alpha = 1.0f;
-            if (m_new != kNegInf) {  // some key admitted so far (the fast exponential: arguments <= 0)
-                alpha = m[g] == kNegInf ? 0.0f : __expf(m[g] - m_new);
+            // The reference max moves only when a tile's max passes it by more than e^8 (the
+            // weights then stay <= e^8, safe in f32, and the sums and outputs are rescaled only
+            // then); tmx and m are the same in every lane, so the branch is warp-uniform.
+            if (m[g] == kNegInf || tmx > m[g] + 8.0f) {
+                const float m_new = fmaxf(m[g], tmx);
+                const float alpha = m[g] == kNegInf ? 0.0f : __expf(m[g] - m_new);
                 m[g] = m_new;
-                ex = sc[g] != kNegInf ? __expf(sc[g] - m_new) : 0.0f;
+                l[g] *= alpha;
+                const uint64_t alpha2 = f2(alpha, alpha);
+#pragma unroll
+                for (int e = 0; e < 2 * C; e++) acc2[g][e] = f2mul(acc2[g][e], alpha2);
             }
+            const float ex = (sc[g] != kNegInf && m[g] != kNegInf) ? __expf(sc[g] - m[g]) : 0.0f;
             float es = ex + __shfl_xor_sync(0xffffffffu, ex, 8);
             es += __shfl_xor_sync(0xffffffffu, es, 16);
-            l[g] = l[g] * alpha + es;
+            l[g] += es;
 #pragma unroll
             for (int k = 0; k < 4; k++) pk[g][k] = __shfl_sync(0xffffffffu, ex, k * 8);
-            const uint64_t alpha2 = f2(alpha, alpha);
-#pragma unroll
-            for (int e = 0; e < 2 * C; e++) acc2[g][e] = f2mul(acc2[g][e], alpha2);
         }
 #pragma unroll
         for (int i = 0; i < C; i++) {
