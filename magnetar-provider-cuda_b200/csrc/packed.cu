@@ -572,6 +572,10 @@ mg_status q8_gemv(Device* d, const GemmArgs& g) {
 // packed weight dequantized (stored order) for the duration of the call and the f32 matmul.
 mg_status q8_matmul(Device* d, const GemmArgs& g) {
     if (q8_gemv_eligible(g)) return q8_gemv(d, g);
+    // Few rows: the logical [k, n] matrix, which the f32 few-row matmul reads as it lies (it takes
+    // no transposed B); more rows: the stored matrix (a plain row-major pass) with the transpose
+    // folded into B's flag for the tensor-core matmul.
+    const bool logical = g.m <= 16;
     GemmArgs f = g;
     void* mem[2] = {nullptr, nullptr};
     mg_status s = MG_OK;
@@ -579,7 +583,7 @@ mg_status q8_matmul(Device* d, const GemmArgs& g) {
         const Buffer* w = g.packed[t];
         if (!w) continue;
         s = device_alloc(d, w->q8_rows * w->q8_cols * sizeof(float), &mem[t]);
-        if (s == MG_OK) s = q8_dequantize(d, w, static_cast<float*>(mem[t]), true);
+        if (s == MG_OK) s = q8_dequantize(d, w, static_cast<float*>(mem[t]), !logical);
         (t == 0 ? f.b : f.b2) = static_cast<const float*>(mem[t]);
         f.packed[t] = nullptr;
     }
@@ -587,7 +591,7 @@ mg_status q8_matmul(Device* d, const GemmArgs& g) {
         // the stored matrix is the logical B, or its transpose for a transposed-storage weight;
         // a gated pair with one packed and one f32 weight is dequantized only when both agree
         const Buffer* w = g.packed[0] ? g.packed[0] : g.packed[1];
-        const bool flip = w->q8_transposed != 0;
+        const bool flip = !logical && w->q8_transposed != 0;
         if (g.gated && g.packed[0] && g.packed[1] && g.packed[0]->q8_transposed != g.packed[1]->q8_transposed)
             s = fail(MG_LAYOUT_UNSUPPORTED, "gated-matmul's packed weights differ in storage order");
         else if (g.gated && flip && (!g.packed[0] || !g.packed[1]))
