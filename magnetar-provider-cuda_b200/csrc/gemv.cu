@@ -919,7 +919,7 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
     const int terms = g.gated ? 2 : 1;
     const int mp = g.m <= 1 ? 1 : g.m <= 2 ? 2 : g.m <= 4 ? 4 : g.m <= 8 ? 8 : 16;
-    const uint64_t per_sm = mp >= 16 ? 1 : 2;  // GemvCShape<mp>::kMinBlocks
+    const uint64_t per_sm = mp >= 16 ? 1 : mp == 1 ? 3 : 2;  // CTAs per SM the launch fills
     uint64_t splits = (uint64_t)d->sm_count * per_sm / (col_tiles * terms);
     const uint64_t max_splits = kMaxClusterCtas / terms;
     if (splits > max_splits) splits = max_splits;
