@@ -193,6 +193,14 @@ def cpu_layer_rate(cfg, w, budget_s: float, threads: int = 0):
     return cfg.seq * n / el, n, orc.threads()
 
 
+def bench_config(world: int) -> dict:
+    """The ``config`` object both arms print (the same workload on the same inputs)."""
+    return {"workload": "decoder-layer b1 s128 h512 8x64 ffn1376 causal, RoPE 1e4, RMSNorm 1e-5 (configs[0]); "
+                        "one step = one layer forward over 128 tokens (layer.make_inputs seed 0 on rank 0)",
+            "global_batch": world, "seq_len": 128, "parallelism": f"replicas x{world}",
+            "l2": "flushed before every timed GPU step: 252 MB write, then 252 MB read of another buffer"}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
@@ -213,8 +221,7 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decoder-layer b1 s128 h512 8x64 ffn1376 (configs[0]), one step = one layer forward",
-                   "global_batch": 1, "seq_len": cfg.seq, "parallelism": "cpu"},
+        "config": bench_config(world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": orc.threads(), "kind": "port",
                          "sample": f"{args.steps} full layer forwards on the host cores (C oracle, OpenMP); the "
                                    "reference CPU executor (Rust providers-cpu) is not buildable here"},
@@ -314,21 +321,17 @@ def kernel_suite(torch, mpc, kernels, peaks, tf32_tflops, filt=None, iters=5):
     eff = tf32_tflops / 3.0 if tf32_tflops > 0 else float("nan")
 
     def add(name, config, ms, bound, work, bf16x3=False):
+        # compact entries: [name, ms, achieved, frac] -- achieved in GB/s (bound hbm, peak = the
+        # measured copy bandwidth) or TFLOP/s (bound tensor, peak = 3xTF32-effective); the
+        # attention line adds its fraction of bf16x3-effective (measured bf16 / 3)
         if bound == "hbm":
             achieved = work / (ms * 1e-3) / 1e9
-            results.append({"kernel": name, "config": config, "ms": round(ms, 4), "bound": "hbm",
-                            "achieved": round(achieved, 1), "unit": "GB/s", "peak": hbm,
-                            "frac": round(achieved / hbm, 4)})
+            results.append([name, round(ms, 4), round(achieved, 1), round(achieved / hbm, 3)])
         else:
             achieved = work / (ms * 1e-3) / 1e12
-            results.append({"kernel": name, "config": config, "ms": round(ms, 4), "bound": "tensor",
-                            "achieved": round(achieved, 2), "unit": "TFLOP/s", "peak": round(eff, 1),
-                            "peak_basis": "3xTF32-effective = measured cuBLAS TF32 / 3",
-                            "frac": round(achieved / eff, 4)})
+            results.append([name, round(ms, 4), round(achieved, 1), round(achieved / eff, 3)])
             if bf16x3:  # the kernel issues three bf16 MMAs per product: its own ceiling
-                bf = peaks["bf16_tflops"] / 3.0
-                results[-1]["frac_of_bf16x3_effective"] = round(achieved / bf, 4)
-                results[-1]["bf16x3_effective_peak"] = round(bf, 1)
+                results[-1].append(round(achieved / (peaks["bf16_tflops"] / 3.0), 3))
 
     def timed(fn, n=iters, warmup=2, reps=1):
         # the spin covers the host's enqueueing of all `reps` calls
@@ -666,10 +669,7 @@ def run_ours(args, world, rank, local):
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "decoder-layer b1 s128 h512 8x64 ffn1376 causal, RoPE 1e4, RMSNorm 1e-5 "
-                                   "(configs[0]); one step = one layer forward replayed as a captured graph",
-                       "global_batch": world, "seq_len": cfg.seq, "parallelism": f"replicas x{world}",
-                       "l2": "flushed before every timed step: 252 MB write, then 252 MB read of another buffer"},
+            "config": bench_config(world),
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": cfg.seq * 4,
                     "d2h_bytes_per_step": cfg.seq * cfg.hidden * 4 + 4},
             "gpu_launches": int(launches),
@@ -684,8 +684,17 @@ def run_ours(args, world, rank, local):
         if tp_line is not None:
             line["tp_mlp"] = tp_line
         if suite is not None:
+            line["kernels_columns"] = ["kernel", "ms", "achieved", "frac", "frac_of_bf16x3_effective"]
+            line["kernels_peaks"] = {"hbm_gbs": peaks["hbm_gbs"], "tensor_3xtf32_tflops": round(tf32 / 3.0, 1),
+                                     "bf16x3_tflops": round(peaks["bf16_tflops"] / 3.0, 1),
+                                     "units": "GB/s for HBM-bound lines (matmul M<=16, attention decode, "
+                                              "softmax, [8192,4096] ops); TFLOP/s otherwise"}
             line["kernels"] = suite
-        print(json.dumps(line), flush=True)
+        # the nested objects last but the headline keys first; a long "kernels" list sits
+        # before tp_mlp so that a tail of the line still shows the multi-GPU numbers
+        if "tp_mlp" in line:
+            line["tp_mlp"] = line.pop("tp_mlp")
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     provider.close()
     if world > 1:
         torch.distributed.barrier()

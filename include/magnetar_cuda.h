@@ -412,9 +412,50 @@ typedef struct mg_step_io {
 mg_status mg_executor_replay_step_io(mg_executor* ex, uint64_t offset, const mg_step_io* io, int count);
 /* The largest offset the captured step accepts (UINT64_MAX: unbounded). */
 mg_status mg_executor_step_max_offset(mg_executor* ex, uint64_t* out);
+/* Several captured steps per executor (src/executor.rs:209-340, StepCaptureId):
+ * mg_executor_end_step_capture_id ends the capture in progress, keeps its graph under a new
+ * id and runs it once (so the captured step's results are available, as end_step_capture
+ * does there).  mg_executor_replay_capture is replay_step(id, offset, inputs) with the
+ * outputs read in the same call (entries as mg_executor_replay_step_io): it refuses, with
+ * MG_CAPTURE_UNSUPPORTED and nothing run, a step whose resources no longer have their
+ * captured storage ("resource '...' no longer has its captured storage"), an input the step
+ * never read, and an input the step reads through a weight's operand form; embedding ids
+ * written to the step are checked on the host first (MG_SHAPE_UNSUPPORTED).
+ * mg_executor_release_step_capture drops a step (src/executor.rs release_step_capture); an
+ * unknown id is not an error.  Device memory a live step addresses is never freed under it:
+ * a workspace that grows, a dropped operand form or a replaced tensor stays allocated until
+ * the last step addressing it is released.  The single-step calls above replay the step
+ * that mg_executor_end_step_capture made last. */
+mg_status mg_executor_end_step_capture_id(mg_executor* ex, uint64_t* id);
+mg_status mg_executor_replay_capture(mg_executor* ex, uint64_t id, uint64_t offset, const mg_step_io* io,
+                                     int count);
+mg_status mg_executor_release_step_capture(mg_executor* ex, uint64_t id);
+/* Number of captured steps the executor holds. */
+mg_status mg_executor_step_capture_count(mg_executor* ex, int* count);
 /* Observation log (src/executor.rs:1082-1100): counts of Started/Completed/Failed. */
 mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t* completed,
                                    uint64_t* failed);
+/* The observation log itself (src/executor.rs:1082-1100, KernelObservation): the most recent
+ * MG_OBSERVATION_LOG_CAPACITY events, oldest first.  Every submit records DispatchStarted,
+ * then DispatchCompleted, DispatchFailed (with the status), or Timeout (an expired deadline);
+ * an output the device cannot hold also records MemoryFeasibilityFailed before the failure.
+ * `invocation` numbers the executor's submits from 0.  With out == NULL only *count is set;
+ * a capacity below the count is MG_SHAPE_UNSUPPORTED. */
+#define MG_OBSERVATION_LOG_CAPACITY 4096
+typedef enum mg_observation_kind {
+    MG_OBSERVATION_DISPATCH_STARTED = 0,
+    MG_OBSERVATION_DISPATCH_COMPLETED = 1,
+    MG_OBSERVATION_DISPATCH_FAILED = 2,
+    MG_OBSERVATION_TIMEOUT = 3,
+    MG_OBSERVATION_MEMORY_FEASIBILITY_FAILED = 4
+} mg_observation_kind;
+typedef struct mg_observation {
+    int kind;          /* mg_observation_kind */
+    char kernel[48];   /* the invocation's kernel name (truncated) */
+    uint64_t invocation;
+    int status;        /* mg_status of a failure (MG_OK otherwise) */
+} mg_observation;
+mg_status mg_executor_observation_log(mg_executor* ex, mg_observation* out, uint32_t capacity, uint32_t* count);
 
 /* ---------------------------------------------------------------------------------- */
 /* Tensor parallel -- src/multi.rs, src/multi/tensor_parallel.rs                        */
@@ -428,6 +469,26 @@ mg_status mg_comm_destroy(mg_comm* comm);
 /* In-place sum of an f32 buffer across the group (replaces the serial reduce-to-root +
  * copy-back of src/multi/tensor_parallel.rs:697-734). */
 mg_status mg_comm_all_reduce(mg_comm* comm, mg_buffer* buffer);
+/* Failure handling.  The reference's peer copies have no failure path of their own; here
+ * the communicator runs in NCCL's non-blocking mode and every NCCL call is bounded: the host
+ * polls the call until it settles, and after the group's timeout (default 300 s, or
+ * MAGNETAR_CUDA_COMM_TIMEOUT_MS, or mg_comm_set_timeout) the communicator is aborted and the
+ * call fails with MG_DEVICE_UNAVAILABLE; an asynchronous NCCL error aborts it with
+ * MG_DRIVER_FAILED.  An aborted communicator refuses all further work.
+ * mg_comm_check polls once for an asynchronous error; mg_comm_wait waits, bounded, for the
+ * group's enqueued work on this device (the compute and all-reduce streams) to finish and
+ * aborts on timeout; mg_comm_abort aborts at once (a rank that learnt on the host that a peer
+ * is gone). */
+mg_status mg_comm_set_timeout(mg_comm* comm, int64_t timeout_ms);
+mg_status mg_comm_check(mg_comm* comm);
+mg_status mg_comm_wait(mg_comm* comm, int64_t timeout_ms);
+mg_status mg_comm_abort(mg_comm* comm);
+int mg_comm_is_aborted(const mg_comm* comm);
+/* Host-only test hook of the bounded settle: drives the poll loop with a scripted sequence of
+ * NCCL results (0 success, 7 in progress, anything else an error; the last repeats) instead of
+ * a communicator.  Returns the status the settle ends with; *aborted counts the aborts, *polls
+ * the polls.  No GPU or NCCL call is made. */
+mg_status mg_comm_settle_selftest(const int* states, int count, int64_t timeout_ms, int* aborted, int* polls);
 /* The [start, end) share of `extent` that `member` of `parts` holds, aligned to 32 when
  * every part can hold at least one 32-block (src/multi/tensor_parallel.rs:82-86, 300-307). */
 mg_status mg_tp_share(uint64_t extent, int parts, int member, uint64_t* start, uint64_t* end);

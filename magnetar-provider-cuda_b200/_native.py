@@ -181,10 +181,21 @@ SIGNATURES = {
     "mg_executor_launch_step": [_P],
     "mg_executor_check_steps": [_P],
     "mg_executor_observations": [_P, _U64P, _U64P, _U64P],
+    "mg_executor_observation_log": [_P, _P, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32)],
+    "mg_executor_end_step_capture_id": [_P, _U64P],
+    "mg_executor_replay_capture": [_P, _U64, _U64, _P, _I],
+    "mg_executor_release_step_capture": [_P, _U64],
+    "mg_executor_step_capture_count": [_P, _IP],
     "mg_comm_unique_id": [ctypes.c_char_p],
     "mg_comm_init": [_P, _I, _I, ctypes.c_char_p, _PP],
     "mg_comm_destroy": [_P],
     "mg_comm_all_reduce": [_P, _P],
+    "mg_comm_set_timeout": [_P, ctypes.c_int64],
+    "mg_comm_check": [_P],
+    "mg_comm_wait": [_P, ctypes.c_int64],
+    "mg_comm_abort": [_P],
+    "mg_comm_is_aborted": [_P],
+    "mg_comm_settle_selftest": [_IP, _I, ctypes.c_int64, _IP, _IP],
     "mg_tp_share": [_U64, _I, _I, _U64P, _U64P],
     "mg_tp_mlp": [_P, _P, _P, _P, _P, _I, _PP],
     "mg_executor_attach_comm": [_P, _P],
@@ -198,6 +209,7 @@ _RESTYPES = {
     "mg_device_stream": ctypes.c_void_p,
     "mg_device_launch_count": ctypes.c_uint64,
     "mg_buffer_device_ptr": ctypes.c_void_p,
+    "mg_comm_is_aborted": ctypes.c_int,
 }
 
 _lib = None
@@ -210,6 +222,17 @@ def build(force: bool = False) -> str:
         subprocess.run(["make", "-C", CSRC, "clean"], check=True, stdout=subprocess.DEVNULL)
     subprocess.run(["make", "-C", CSRC, "-j", jobs], check=True, stdout=subprocess.DEVNULL)
     return LIB_PATH
+
+
+OBSERVATION_KINDS = {0: "KernelDispatchStarted", 1: "KernelDispatchCompleted", 2: "KernelDispatchFailed",
+                     3: "KernelTimeout", 4: "KernelMemoryFeasibilityFailed"}
+OBSERVATION_LOG_CAPACITY = 4096
+
+
+class Observation(ctypes.Structure):
+    """mg_observation: one KernelObservation of the executor's log."""
+    _fields_ = [("kind", ctypes.c_int), ("kernel", ctypes.c_char * 48), ("invocation", ctypes.c_uint64),
+                ("status", ctypes.c_int)]
 
 
 class StepIO(ctypes.Structure):

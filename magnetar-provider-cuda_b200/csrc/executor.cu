@@ -29,19 +29,67 @@ int comm_world(mg_comm* comm);
 
 using namespace mg;
 
+// One captured step (src/executor.rs:177-376 `CapturedExecutorStep`): its graph, what a replay
+// needs to know, and what the capture recorded so that a replay can tell whether the step's
+// storage is still in place.
+struct CapturedStep {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool has_embedding = false;
+    bool advancing = false;
+    uint64_t max_offset = UINT64_MAX;
+    uint64_t kernels = 0;  // kernels one replay launches
+    // Device blocks the graph addresses: none of them is freed while the step lives.
+    std::vector<void*> blocks;
+    // Every resource an invocation of the step read or wrote, as it was at capture time
+    // (src/executor.rs record_captured_resources): the buffer and its device storage, and the
+    // operand forms of a weight that a captured matmul reads instead of its values.
+    struct Resource {
+        Buffer* b;
+        void* ptr;
+        uint64_t count;
+        void* prep;
+        void* compact;
+    };
+    std::map<std::string, Resource> resources;
+    // Embedding id resources and the vocabulary of their table (host-checked on replay writes).
+    std::map<std::string, uint64_t> embedding_ids;
+    uint64_t storage_gen = 0, prep_gen = 0;  // when the recorded state was last known current
+};
+
+// One entry of the executor's observation log (src/executor.rs:1082-1100, KernelObservation).
+struct Observation {
+    int kind;
+    std::string kernel;
+    uint64_t invocation;
+    mg_status status;
+};
+
 struct mg_executor {
     Device* device = nullptr;
     mg_device* handle = nullptr;
     std::map<std::string, Buffer*> storage;
+    // Bumped whenever an id's buffer is replaced or released (a captured step re-checks its
+    // resources only when this moved since it last checked).
+    uint64_t storage_gen = 0;
     std::mutex lock;
     uint64_t started = 0, completed = 0, failed = 0;
+    // Observation log: the most recent MG_OBSERVATION_LOG_CAPACITY entries, oldest first (the
+    // oldest half is dropped once twice the capacity is held, as the reference's log does).
+    std::vector<Observation> observations;
+    uint64_t next_invocation = 0;
     // step capture
     bool capturing = false;
     bool capture_has_embedding = false;
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t graph_exec = nullptr;
-    bool step_has_embedding = false;
-    uint64_t launches_at_capture = 0, graph_kernels = 0;  // kernels one replay launches
+    uint64_t launches_at_capture = 0;
+    std::map<std::string, CapturedStep::Resource> capture_resources;
+    std::map<std::string, uint64_t> capture_embedding_ids;
+    // Captured steps by id (src/executor.rs StepCaptureId); `current` is the one the
+    // single-step calls (mg_executor_replay_step, ...) replay: the last one
+    // mg_executor_end_step_capture made.
+    std::map<uint64_t, CapturedStep*> steps;
+    uint64_t next_step = 1;
+    uint64_t current = 0;
     // Step capture only: plain matmuls of one input (weights as B) waiting to launch as one
     // grouped projection, with the ropes of their outputs folded into its epilogue.  Nothing
     // runs during a capture, so deferring a launch changes only the recorded order, and every
@@ -65,8 +113,6 @@ struct mg_executor {
     // largest offset they stay in bounds for; the captured step keeps the least of those.
     std::set<std::string> advancing;
     uint64_t capture_max_offset = UINT64_MAX;
-    uint64_t step_max_offset = UINT64_MAX;
-    bool step_advancing = false;
     // tensor parallel
     mg_comm* comm = nullptr;
     std::map<std::string, int> plan;            // weight id -> 0 columns, 1 rows
@@ -120,8 +166,36 @@ struct Attrs {
 mg_status store_replace(mg_executor* ex, const std::string& id, Buffer* b) {
     auto it = ex->storage.find(id);
     if (it != ex->storage.end() && it->second != b) buffer_free(it->second);
+    if (it == ex->storage.end() || it->second != b) ex->storage_gen++;
     ex->storage[id] = b;
     return MG_OK;
+}
+
+void step_destroy(mg_executor* ex, CapturedStep* st) {
+    if (!st) return;
+    cudaSetDevice(ex->device->ordinal);
+    if (st->exec) cudaGraphExecDestroy(st->exec);
+    if (st->graph) cudaGraphDestroy(st->graph);
+    graph_release(ex->device, st->blocks);
+    delete st;
+}
+
+void observe(mg_executor* ex, int kind, const char* kernel, uint64_t invocation, mg_status status) {
+    if (ex->observations.size() >= 2 * MG_OBSERVATION_LOG_CAPACITY)
+        ex->observations.erase(ex->observations.begin(), ex->observations.begin() + MG_OBSERVATION_LOG_CAPACITY);
+    ex->observations.push_back({kind, kernel ? kernel : "", invocation, status});
+}
+
+// While capturing: records the device blocks and the storage of resource `id` (buffer `b`) for
+// the step being captured.
+void capture_record(mg_executor* ex, const std::string& id, Buffer* b) {
+    if (!b) return;
+    Device* d = ex->device;
+    graph_touch(d, b->ptr);
+    graph_touch(d, b->prep);
+    graph_touch(d, b->compact);
+    graph_touch(d, b->q8_scales);
+    ex->capture_resources[id] = {b, b->ptr, b->count, b->prep, b->compact};
 }
 
 mg_status get_input(mg_executor* ex, const mg_invocation* inv, int index, Buffer** out) {
@@ -311,6 +385,10 @@ mg_status dispatch(mg_executor* ex, const mg_invocation* inv, mg_buffer** out) {
             }
             kw.store = (float*)target->ptr;
         } else {
+            // A captured matmul may read the store through its operand form, which an in-place
+            // write inside the same step would leave stale.
+            if (ex->capturing && (a->prep || a->compact))
+                return fail(MG_CAPTURE_UNSUPPORTED, "an in-place kv-write into a weight read through its operand form cannot be captured");
             buffer_drop_prep(a);
         }
         const mg_status s = k::kv_write(ex->device, kw);
@@ -732,6 +810,7 @@ mg_status mg_executor_create(mg_device* h, mg_executor** out) {
     if (!ex) return fail(MG_EXECUTION_FAILED, "host allocation failed");
     ex->device = dev(h);
     ex->handle = h;
+    device_ref(ex->device);  // its captured steps release device memory when it goes
     *out = ex;
     return MG_OK;
 }
@@ -739,9 +818,11 @@ mg_status mg_executor_create(mg_device* h, mg_executor** out) {
 mg_status mg_executor_destroy(mg_executor* ex) {
     if (!ex) return MG_OK;
     cudaSetDevice(ex->device->ordinal);
-    if (ex->graph_exec) cudaGraphExecDestroy(ex->graph_exec);
-    if (ex->graph) cudaGraphDestroy(ex->graph);
+    if (ex->capturing) mg_executor_abort_step_capture(ex);
+    for (auto& kv : ex->steps) step_destroy(ex, kv.second);
+    ex->steps.clear();
     for (auto& kv : ex->storage) buffer_free(kv.second);
+    device_unref(ex->device);
     delete ex;
     return MG_OK;
 }
@@ -895,6 +976,7 @@ mg_status mg_executor_release_tensor(mg_executor* ex, const char* id, int* relea
         cudaSetDevice(ex->device->ordinal);
         buffer_free(it->second);
         ex->storage.erase(it);
+        ex->storage_gen++;
         r = 1;
     }
     ex->plan.erase(id);
@@ -962,14 +1044,18 @@ mg_status mg_executor_submit_kernel(mg_executor* ex, const mg_invocation* inv) {
     if (!ex || !inv || !inv->kernel || !inv->output) return fail(MG_INVALID_ARGUMENT, "null argument");
     std::lock_guard<std::mutex> g(ex->lock);
     ex->started++;
+    const uint64_t ordinal = ex->next_invocation++;
+    observe(ex, MG_OBSERVATION_DISPATCH_STARTED, inv->kernel, ordinal, MG_OK);
     // src/executor.rs:1202-1210: an already-expired deadline is a timeout.
     if (inv->deadline_millis == 0) {
         ex->failed++;
+        observe(ex, MG_OBSERVATION_TIMEOUT, inv->kernel, ordinal, MG_KERNEL_TIMEOUT);
         return fail(MG_KERNEL_TIMEOUT, "kernel '%s' deadline expired before dispatch", inv->kernel);
     }
     mg_status s = device_check(ex->handle);
     if (s != MG_OK) {
         ex->failed++;
+        observe(ex, MG_OBSERVATION_DISPATCH_FAILED, inv->kernel, ordinal, s);
         return s;
     }
     const std::string out_id = inv->output;
@@ -996,12 +1082,32 @@ mg_status mg_executor_submit_kernel(mg_executor* ex, const mg_invocation* inv) {
         // The previous value stays; a fresh buffer made for this call is dropped.
         if (result && result != offered) buffer_free(buf(result));
         ex->failed++;
+        // src/executor.rs:2095-2130: an output the device cannot hold is a memory-feasibility
+        // failure.
+        if (s == MG_OUT_OF_DEVICE_MEMORY) observe(ex, MG_OBSERVATION_MEMORY_FEASIBILITY_FAILED, inv->kernel, ordinal, s);
+        observe(ex, MG_OBSERVATION_DISPATCH_FAILED, inv->kernel, ordinal, s);
         return s;
     }
     store_replace(ex, out_id, buf(result));
+    if (ex->capturing) {
+        // The step records what the invocation read and wrote (src/executor.rs
+        // record_captured_resources); an embedding's ids are checked on the host when a replay
+        // writes them.
+        for (int i = 0; i < inv->input_count; i++) {
+            if (!inv->inputs || !inv->inputs[i]) continue;
+            auto it = ex->storage.find(inv->inputs[i]);
+            if (it != ex->storage.end()) capture_record(ex, inv->inputs[i], it->second);
+        }
+        capture_record(ex, out_id, buf(result));
+        if (!strcmp(inv->kernel, "embedding") && inv->input_count >= 2 && inv->inputs[0] && inv->inputs[1]) {
+            auto t = ex->storage.find(inv->inputs[0]);
+            if (t != ex->storage.end() && t->second->rank >= 1) ex->capture_embedding_ids[inv->inputs[1]] = t->second->shape[0];
+        }
+    }
     if (role == 1) ex->sharded.insert(out_id);
     else ex->sharded.erase(out_id);
     ex->completed++;
+    observe(ex, MG_OBSERVATION_DISPATCH_COMPLETED, inv->kernel, ordinal, MG_OK);
     return MG_OK;
 }
 
@@ -1020,49 +1126,246 @@ mg_status mg_executor_begin_step_capture_advancing(mg_executor* ex, const char* 
     if (ex->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "a step capture is already in progress");
     MG_TRY(device_check(ex->handle));
     Device* d = ex->device;
+    if (d->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "another executor of this device is capturing a step");
     MG_CUDA(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed), "beginning a step capture");
     ex->capturing = true;
     d->capturing = true;
+    graph_take(d);  // starts an empty record of the blocks the step addresses
     ex->advancing.clear();
     for (int i = 0; i < count; i++)
         if (attributes[i]) ex->advancing.insert(attributes[i]);
     ex->capture_max_offset = UINT64_MAX;
     ex->capture_has_embedding = false;
+    ex->capture_resources.clear();
+    ex->capture_embedding_ids.clear();
     ex->launches_at_capture = d->launches.load();
     return MG_OK;
 }
 
-mg_status mg_executor_end_step_capture(mg_executor* ex) {
-    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
-    std::lock_guard<std::mutex> g(ex->lock);
+namespace {
+
+// Ends the capture in progress and instantiates its graph (src/executor.rs end_step_capture).
+mg_status end_capture(mg_executor* ex, CapturedStep** out) {
+    *out = nullptr;
     if (!ex->capturing) return fail(MG_CAPTURE_UNSUPPORTED, "no step capture is in progress");
     Device* d = ex->device;
     const mg_status fs = flush_deferred(ex);  // the last deferred group
     cudaGraph_t gph = nullptr;
     cudaError_t e = cudaStreamEndCapture(d->stream, &gph);
     ex->capturing = d->capturing = false;
-    flush_deferred_frees(d);
-    if (e != cudaSuccess || fs != MG_OK) {
+    // The blocks the graph addresses are held before the frees deferred during the capture run,
+    // so a block the capture both used and released stays allocated for the graph.
+    CapturedStep* st = new (std::nothrow) CapturedStep();
+    if (!st) {
         if (gph) cudaGraphDestroy(gph);
+        graph_take(d);
+        flush_deferred_frees(d);
+        return fail(MG_EXECUTION_FAILED, "host allocation failed");
+    }
+    st->blocks = graph_take(d);
+    graph_hold(d, st->blocks);
+    flush_deferred_frees(d);
+    const uint64_t kernels = d->launches.load() - ex->launches_at_capture;
+    d->launches.fetch_sub(kernels);  // captured launches did not run; replays count them
+    if (e != cudaSuccess || fs != MG_OK) {
+        st->graph = gph;
+        step_destroy(ex, st);
         return fs != MG_OK ? fs : from_cuda(e, "ending the step capture");
     }
-    cudaGraphExec_t exec = nullptr;
-    e = cudaGraphInstantiate(&exec, gph, 0);
+    st->graph = gph;
+    e = cudaGraphInstantiate(&st->exec, gph, 0);
     if (e != cudaSuccess) {
-        cudaGraphDestroy(gph);
+        st->exec = nullptr;
+        step_destroy(ex, st);
         return from_cuda(e, "instantiating the step graph");
     }
-    if (ex->graph_exec) cudaGraphExecDestroy(ex->graph_exec);
-    if (ex->graph) cudaGraphDestroy(ex->graph);
-    ex->graph = gph;
-    ex->graph_exec = exec;
-    ex->step_advancing = !ex->advancing.empty();
-    ex->step_max_offset = ex->capture_max_offset;
+    st->kernels = kernels;
+    st->advancing = !ex->advancing.empty();
+    st->max_offset = ex->capture_max_offset;
+    st->has_embedding = ex->capture_has_embedding;
+    st->resources.swap(ex->capture_resources);
+    st->embedding_ids.swap(ex->capture_embedding_ids);
+    st->storage_gen = ex->storage_gen;
+    st->prep_gen = d->prep_gen.load();
     ex->advancing.clear();
-    ex->step_has_embedding = ex->capture_has_embedding;
-    // Captured launches did not run; count them when a replay runs them.
-    ex->graph_kernels = d->launches.load() - ex->launches_at_capture;
-    d->launches.fetch_sub(ex->graph_kernels);
+    *out = st;
+    return MG_OK;
+}
+
+// Whether every resource the step recorded still has its captured storage (src/executor.rs
+// replay_step: "resource '...' no longer has its captured storage"), including the operand
+// forms of weights its matmuls read.
+mg_status step_check_storage(mg_executor* ex, CapturedStep* st) {
+    const uint64_t pg = ex->device->prep_gen.load();
+    if (st->storage_gen == ex->storage_gen && st->prep_gen == pg) return MG_OK;
+    for (const auto& kv : st->resources) {
+        auto it = ex->storage.find(kv.first);
+        const CapturedStep::Resource& r = kv.second;
+        const Buffer* b = it == ex->storage.end() ? nullptr : it->second;
+        if (!b || b != r.b || b->ptr != r.ptr || b->count != r.count)
+            return fail(MG_CAPTURE_UNSUPPORTED, "resource '%s' no longer has its captured storage", kv.first.c_str());
+        if ((r.prep && b->prep != r.prep) || (r.compact && b->compact != r.compact))
+            return fail(MG_CAPTURE_UNSUPPORTED,
+                        "resource '%s' changed after the capture: the operand form the step reads is gone; capture the step again",
+                        kv.first.c_str());
+    }
+    st->storage_gen = ex->storage_gen;
+    st->prep_gen = pg;
+    return MG_OK;
+}
+
+CapturedStep* find_step(mg_executor* ex, uint64_t id) {
+    auto it = ex->steps.find(id);
+    return it == ex->steps.end() ? nullptr : it->second;
+}
+
+// Reads (and resets) the sticky embedding-id flag after replays; waits for the device.
+mg_status check_embedding_flag(Device* d) {
+    MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading the id flag");
+    MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
+    MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
+    if (d->host_flags[0])
+        return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
+    return MG_OK;
+}
+
+// Replays `st` `count` times at `offset` (count < 0: one launch and no check; 0: the check
+// only).
+mg_status replay_step_n(mg_executor* ex, CapturedStep* st, int count, uint64_t offset) {
+    Device* d = ex->device;
+    if (offset > st->max_offset)
+        return fail(MG_CAPTURE_UNSUPPORTED, "offset %llu leaves the captured bounds (at most %llu)",
+                    (unsigned long long)offset, (unsigned long long)st->max_offset);
+    const int launches = count < 0 ? 1 : count;
+    if (launches > 0) MG_TRY(step_check_storage(ex, st));
+    if (st->advancing && launches > 0) MG_TRY(k::set_step_offset(d, d->step_offset, offset));
+    for (int i = 0; i < launches; i++) {
+        MG_CUDA(cudaGraphLaunch(st->exec, d->stream), "replaying the captured step");
+        d->launches.fetch_add(st->kernels);
+    }
+    if (count < 0) return MG_OK;
+    // The id flag is sticky across the replays: one read covers them all, then resets.
+    if (st->has_embedding) return check_embedding_flag(d);
+    return MG_OK;
+}
+
+// One replay with host I/O (see mg_executor_replay_step_io).
+mg_status replay_io(mg_executor* ex, CapturedStep* st, uint64_t offset, const mg_step_io* io, int count) {
+    Device* d = ex->device;
+    if (offset > st->max_offset)
+        return fail(MG_CAPTURE_UNSUPPORTED, "offset %llu leaves the captured bounds (at most %llu)",
+                    (unsigned long long)offset, (unsigned long long)st->max_offset);
+    MG_TRY(step_check_storage(ex, st));
+    std::vector<Buffer*> bufs((size_t)count);
+    for (int i = 0; i < count; i++) {
+        if (!io[i].id || (!io[i].host && io[i].bytes)) return fail(MG_INVALID_ARGUMENT, "null argument");
+        auto it = ex->storage.find(io[i].id);
+        if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", io[i].id);
+        Buffer* b = it->second;
+        if (b->dtype == MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "resource %s is a packed weight", io[i].id);
+        if (io[i].bytes != b->count * dtype_size(b->dtype))
+            return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes do not match resource %s of shape %s",
+                        (unsigned long long)io[i].bytes, io[i].id, shape_str(b).c_str());
+        if (io[i].to_device) {
+            auto r = st->resources.find(io[i].id);
+            // src/executor.rs replay_step: an input the step never read is refused.
+            if (r == st->resources.end())
+                return fail(MG_CAPTURE_UNSUPPORTED, "input '%s' was not read by the captured step", io[i].id);
+            // The step reads this weight through an operand form derived from its values: new
+            // values would not reach it.
+            if (r->second.prep || r->second.compact)
+                return fail(MG_CAPTURE_UNSUPPORTED,
+                            "input '%s' is a weight the captured step reads through its operand form; write it with "
+                            "write_weight_tensor and capture the step again",
+                            io[i].id);
+            auto e = st->embedding_ids.find(io[i].id);
+            if (e != st->embedding_ids.end() && b->dtype == MG_F32) {  // src/executor.rs replay_step
+                const float* v = (const float*)io[i].host;
+                for (uint64_t j = 0; j < b->count; j++)
+                    if (!(v[j] >= 0.0f && v[j] == std::floor(v[j]) && (uint64_t)v[j] < e->second))
+                        return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
+            }
+        }
+        bufs[(size_t)i] = b;
+    }
+    for (int i = 0; i < count; i++) {
+        if (!io[i].to_device || !io[i].bytes) continue;
+        MG_CUDA(cudaMemcpyAsync(bufs[(size_t)i]->ptr, io[i].host, io[i].bytes, cudaMemcpyHostToDevice, d->stream),
+                "writing a step input");
+        d->uploads.fetch_add(1);
+    }
+    if (st->advancing) MG_TRY(k::set_step_offset(d, d->step_offset, offset));
+    MG_CUDA(cudaGraphLaunch(st->exec, d->stream), "replaying the captured step");
+    d->launches.fetch_add(st->kernels);
+    for (int i = 0; i < count; i++) {
+        if (io[i].to_device || !io[i].bytes) continue;
+        MG_CUDA(cudaMemcpyAsync(io[i].host, bufs[(size_t)i]->ptr, io[i].bytes, cudaMemcpyDeviceToHost, d->stream),
+                "reading a step output");
+        d->downloads.fetch_add(1);
+    }
+    if (st->has_embedding) return check_embedding_flag(d);
+    MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
+    return MG_OK;
+}
+
+}  // namespace
+
+mg_status mg_executor_end_step_capture(mg_executor* ex) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    CapturedStep* st = nullptr;
+    MG_TRY(end_capture(ex, &st));
+    // The single-step calls' step: replaces the previous one made by this call.
+    if (ex->current) {
+        step_destroy(ex, find_step(ex, ex->current));
+        ex->steps.erase(ex->current);
+    }
+    ex->current = ex->next_step++;
+    ex->steps[ex->current] = st;
+    return MG_OK;
+}
+
+mg_status mg_executor_end_step_capture_id(mg_executor* ex, uint64_t* id) {
+    if (!ex || !id) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    CapturedStep* st = nullptr;
+    MG_TRY(end_capture(ex, &st));
+    // src/executor.rs end_step_capture: the captured graph runs once as it ends, so the
+    // captured step's results are available.
+    const mg_status s = replay_step_n(ex, st, 1, 0);
+    if (s != MG_OK) {
+        step_destroy(ex, st);
+        return s;
+    }
+    *id = ex->next_step++;
+    ex->steps[*id] = st;
+    return MG_OK;
+}
+
+mg_status mg_executor_replay_capture(mg_executor* ex, uint64_t id, uint64_t offset, const mg_step_io* io, int count) {
+    if (!ex || (count > 0 && !io) || count < 0) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    CapturedStep* st = find_step(ex, id);
+    if (!st) return fail(MG_CAPTURE_UNSUPPORTED, "no step capture %llu", (unsigned long long)id);
+    MG_TRY(device_check(ex->handle));
+    return replay_io(ex, st, offset, io, count);
+}
+
+mg_status mg_executor_release_step_capture(mg_executor* ex, uint64_t id) {
+    if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    auto it = ex->steps.find(id);
+    if (it == ex->steps.end()) return MG_OK;
+    step_destroy(ex, it->second);
+    ex->steps.erase(it);
+    if (ex->current == id) ex->current = 0;
+    return MG_OK;
+}
+
+mg_status mg_executor_step_capture_count(mg_executor* ex, int* count) {
+    if (!ex || !count) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    *count = (int)ex->steps.size();
     return MG_OK;
 }
 
@@ -1075,42 +1378,27 @@ mg_status mg_executor_abort_step_capture(mg_executor* ex) {
     ex->deferred_rope = false;
     ex->embed_pending = false;
     ex->advancing.clear();
+    ex->capture_resources.clear();
+    ex->capture_embedding_ids.clear();
     cudaStreamEndCapture(ex->device->stream, &gph);
     cudaGetLastError();
     if (gph) cudaGraphDestroy(gph);
     ex->capturing = ex->device->capturing = false;
+    graph_take(ex->device);
     flush_deferred_frees(ex->device);
+    ex->device->launches.fetch_sub(ex->device->launches.load() - ex->launches_at_capture);
     return MG_OK;
 }
 
 namespace {
-// Replays the captured step `count` times at `offset` (count < 0: one launch and no check; 0:
-// the check only).
+// The single-step calls: the step mg_executor_end_step_capture made last.
 mg_status replay_at(mg_executor* ex, int count, uint64_t offset) {
     if (!ex) return fail(MG_INVALID_ARGUMENT, "null argument");
     std::lock_guard<std::mutex> g(ex->lock);
-    if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
+    CapturedStep* st = find_step(ex, ex->current);
+    if (!st) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
     MG_TRY(device_check(ex->handle));
-    Device* d = ex->device;
-    if (offset > ex->step_max_offset)
-        return fail(MG_CAPTURE_UNSUPPORTED, "offset %llu leaves the captured bounds (at most %llu)",
-                    (unsigned long long)offset, (unsigned long long)ex->step_max_offset);
-    const int launches = count < 0 ? 1 : count;
-    if (ex->step_advancing && launches > 0) MG_TRY(k::set_step_offset(d, d->step_offset, offset));
-    for (int i = 0; i < launches; i++) {
-        MG_CUDA(cudaGraphLaunch(ex->graph_exec, d->stream), "replaying the captured step");
-        d->launches.fetch_add(ex->graph_kernels);
-    }
-    if (count < 0) return MG_OK;
-    if (ex->step_has_embedding) {
-        // The id flag is sticky across the replays: one read covers them all, then resets.
-        MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading the id flag");
-        MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
-        MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
-        if (d->host_flags[0])
-            return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
-    }
-    return MG_OK;
+    return replay_step_n(ex, st, count, offset);
 }
 
 }  // namespace
@@ -1123,48 +1411,10 @@ mg_status mg_executor_replay_steps(mg_executor* ex, int count) { return replay_a
 mg_status mg_executor_replay_step_io(mg_executor* ex, uint64_t offset, const mg_step_io* io, int count) {
     if (!ex || (count > 0 && !io) || count < 0) return fail(MG_INVALID_ARGUMENT, "null argument");
     std::lock_guard<std::mutex> g(ex->lock);
-    if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
+    CapturedStep* st = find_step(ex, ex->current);
+    if (!st) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step to replay");
     MG_TRY(device_check(ex->handle));
-    Device* d = ex->device;
-    if (offset > ex->step_max_offset)
-        return fail(MG_CAPTURE_UNSUPPORTED, "offset %llu leaves the captured bounds (at most %llu)",
-                    (unsigned long long)offset, (unsigned long long)ex->step_max_offset);
-    std::vector<Buffer*> bufs((size_t)count);
-    for (int i = 0; i < count; i++) {
-        if (!io[i].id || (!io[i].host && io[i].bytes)) return fail(MG_INVALID_ARGUMENT, "null argument");
-        auto it = ex->storage.find(io[i].id);
-        if (it == ex->storage.end()) return fail(MG_EXECUTION_FAILED, "no materialized data for resource %s", io[i].id);
-        Buffer* b = it->second;
-        if (b->dtype == MG_Q8_0) return fail(MG_DTYPE_UNSUPPORTED, "resource %s is a packed weight", io[i].id);
-        if (io[i].bytes != b->count * dtype_size(b->dtype))
-            return fail(MG_SHAPE_UNSUPPORTED, "%llu bytes do not match resource %s of shape %s",
-                        (unsigned long long)io[i].bytes, io[i].id, shape_str(b).c_str());
-        bufs[(size_t)i] = b;
-    }
-    for (int i = 0; i < count; i++) {
-        if (!io[i].to_device || !io[i].bytes) continue;
-        buffer_drop_prep(bufs[(size_t)i]);
-        MG_CUDA(cudaMemcpyAsync(bufs[(size_t)i]->ptr, io[i].host, io[i].bytes, cudaMemcpyHostToDevice, d->stream),
-                "writing a step input");
-        d->uploads.fetch_add(1);
-    }
-    if (ex->step_advancing) MG_TRY(k::set_step_offset(d, d->step_offset, offset));
-    MG_CUDA(cudaGraphLaunch(ex->graph_exec, d->stream), "replaying the captured step");
-    d->launches.fetch_add(ex->graph_kernels);
-    for (int i = 0; i < count; i++) {
-        if (io[i].to_device || !io[i].bytes) continue;
-        MG_CUDA(cudaMemcpyAsync(io[i].host, bufs[(size_t)i]->ptr, io[i].bytes, cudaMemcpyDeviceToHost, d->stream),
-                "reading a step output");
-        d->downloads.fetch_add(1);
-    }
-    if (ex->step_has_embedding) {
-        MG_CUDA(cudaMemcpyAsync(d->host_flags, d->flags, sizeof(int), cudaMemcpyDeviceToHost, d->stream), "reading the id flag");
-        MG_CUDA(cudaMemsetAsync(d->flags, 0, sizeof(int), d->stream), "resetting the id flag");
-    }
-    MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
-    if (ex->step_has_embedding && d->host_flags[0])
-        return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
-    return MG_OK;
+    return replay_io(ex, st, offset, io, count);
 }
 
 mg_status mg_executor_replay_step_at(mg_executor* ex, uint64_t offset) { return replay_at(ex, 1, offset); }
@@ -1172,8 +1422,9 @@ mg_status mg_executor_replay_step_at(mg_executor* ex, uint64_t offset) { return 
 mg_status mg_executor_step_max_offset(mg_executor* ex, uint64_t* out) {
     if (!ex || !out) return fail(MG_INVALID_ARGUMENT, "null argument");
     std::lock_guard<std::mutex> g(ex->lock);
-    if (!ex->graph_exec) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step");
-    *out = ex->step_max_offset;
+    CapturedStep* st = find_step(ex, ex->current);
+    if (!st) return fail(MG_CAPTURE_UNSUPPORTED, "no captured step");
+    *out = st->max_offset;
     return MG_OK;
 }
 
@@ -1189,6 +1440,28 @@ mg_status mg_executor_observations(mg_executor* ex, uint64_t* started, uint64_t*
     if (started) *started = ex->started;
     if (completed) *completed = ex->completed;
     if (failed) *failed = ex->failed;
+    return MG_OK;
+}
+
+mg_status mg_executor_observation_log(mg_executor* ex, mg_observation* out, uint32_t capacity, uint32_t* count) {
+    if (!ex || !count || (capacity && !out)) return fail(MG_INVALID_ARGUMENT, "null argument");
+    std::lock_guard<std::mutex> g(ex->lock);
+    const size_t held = ex->observations.size();
+    const size_t first = held > MG_OBSERVATION_LOG_CAPACITY ? held - MG_OBSERVATION_LOG_CAPACITY : 0;
+    const size_t n = held - first;
+    *count = (uint32_t)n;
+    if (!out) return MG_OK;
+    if (capacity < n)
+        return fail(MG_SHAPE_UNSUPPORTED, "%u entries cannot hold the %zu observations", capacity, n);
+    for (size_t i = 0; i < n; i++) {
+        const Observation& o = ex->observations[first + i];
+        mg_observation& r = out[i];
+        memset(&r, 0, sizeof r);
+        r.kind = o.kind;
+        snprintf(r.kernel, sizeof r.kernel, "%s", o.kernel.c_str());
+        r.invocation = o.invocation;
+        r.status = o.status;
+    }
     return MG_OK;
 }
 

@@ -8,6 +8,8 @@
 
 #include <atomic>
 #include <cstdarg>
+#include <map>
+#include <mutex>
 #include <set>
 #include <string>
 #include <utility>
@@ -74,10 +76,32 @@ struct Device {
     // during a capture wait until the capture ends.
     std::set<void*> plain_allocs;
     std::vector<void*> deferred_frees;
+    // Device blocks that live captured steps address, each with the number of such steps.  A
+    // block freed while a step still addresses it (a scratch workspace that grew, a weight's
+    // dropped operand form, a replaced tensor) is only parked in held_frees; it is freed when
+    // the last step addressing it is released, so a replay never touches freed memory.
+    std::map<void*, int> graph_refs;
+    std::set<void*> held_frees;
+    // While a step capture records: every device block its launches address.
+    std::set<void*> capture_touched;
+    // Bumped whenever a buffer's prepared or compact operand form is dropped: a captured step
+    // re-checks the forms it reads only when this moved since the capture.
+    std::atomic<uint64_t> prep_gen{0};
+    // Guards the allocation bookkeeping above (several executors may share a device).
+    std::mutex mem_lock;
 };
 
 // Frees the allocations deferred while a capture was recording.
 void flush_deferred_frees(Device* d);
+
+// Captured-step bookkeeping: graph_touch records a block the capture in progress addresses
+// (no-op outside a capture); graph_take hands the recorded set to the step being made;
+// graph_hold / graph_release count a step's blocks in and out (the last release frees what
+// was freed meanwhile).
+void graph_touch(Device* d, const void* ptr);
+std::vector<void*> graph_take(Device* d);
+void graph_hold(Device* d, const std::vector<void*>& blocks);
+void graph_release(Device* d, const std::vector<void*>& blocks);
 
 void device_ref(Device* d);
 // Drops one reference; the last one destroys the device.

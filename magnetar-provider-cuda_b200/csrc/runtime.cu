@@ -84,7 +84,11 @@ mg_status device_alloc(Device* d, size_t bytes, void** ptr) {
     cudaError_t e;
     if (d->capturing) {
         e = cudaMalloc(ptr, bytes);
-        if (e == cudaSuccess) d->plain_allocs.insert(*ptr);
+        if (e == cudaSuccess) {
+            std::lock_guard<std::mutex> g(d->mem_lock);
+            d->plain_allocs.insert(*ptr);
+            d->capture_touched.insert(*ptr);
+        }
     } else {
         e = cudaMallocFromPoolAsync(ptr, bytes, d->pool, d->stream);
     }
@@ -97,12 +101,8 @@ mg_status device_alloc(Device* d, size_t bytes, void** ptr) {
     return MG_OK;
 }
 
-void device_free(Device* d, void* ptr) {
-    if (!ptr) return;
-    if (d->capturing) {
-        d->deferred_frees.push_back(ptr);
-        return;
-    }
+// Frees `ptr` now (in stream order for pool blocks).  Caller holds mem_lock.
+static void free_now(Device* d, void* ptr) {
     auto it = d->plain_allocs.find(ptr);
     if (it != d->plain_allocs.end()) {
         d->plain_allocs.erase(it);
@@ -112,15 +112,67 @@ void device_free(Device* d, void* ptr) {
     }
 }
 
+void device_free(Device* d, void* ptr) {
+    if (!ptr) return;
+    std::lock_guard<std::mutex> g(d->mem_lock);
+    if (d->capturing) {
+        d->deferred_frees.push_back(ptr);
+        return;
+    }
+    if (d->graph_refs.count(ptr)) {  // a live captured step still addresses it
+        d->held_frees.insert(ptr);
+        return;
+    }
+    free_now(d, ptr);
+}
+
 void flush_deferred_frees(Device* d) {
     std::vector<void*> pending;
-    pending.swap(d->deferred_frees);
+    {
+        std::lock_guard<std::mutex> g(d->mem_lock);
+        pending.swap(d->deferred_frees);
+    }
     for (void* p : pending) device_free(d, p);
+}
+
+void graph_touch(Device* d, const void* ptr) {
+    if (!ptr || !d->capturing) return;
+    std::lock_guard<std::mutex> g(d->mem_lock);
+    d->capture_touched.insert(const_cast<void*>(ptr));
+}
+
+std::vector<void*> graph_take(Device* d) {
+    std::lock_guard<std::mutex> g(d->mem_lock);
+    std::vector<void*> v(d->capture_touched.begin(), d->capture_touched.end());
+    d->capture_touched.clear();
+    return v;
+}
+
+void graph_hold(Device* d, const std::vector<void*>& blocks) {
+    std::lock_guard<std::mutex> g(d->mem_lock);
+    for (void* p : blocks) d->graph_refs[p]++;
+}
+
+void graph_release(Device* d, const std::vector<void*>& blocks) {
+    std::lock_guard<std::mutex> g(d->mem_lock);
+    for (void* p : blocks) {
+        auto it = d->graph_refs.find(p);
+        if (it == d->graph_refs.end()) continue;
+        if (--it->second > 0) continue;
+        d->graph_refs.erase(it);
+        auto h = d->held_frees.find(p);
+        if (h != d->held_frees.end()) {
+            d->held_frees.erase(h);
+            free_now(d, p);
+        }
+    }
 }
 
 // ---- scratch workspaces -------------------------------------------------------------------
 // Slots are grown on demand and freed in stream order, so a later kernel on the same stream
-// may reuse a workspace as soon as the previous user's kernels are ordered before it.
+// may reuse a workspace as soon as the previous user's kernels are ordered before it.  A
+// workspace a captured step addresses is recorded for that step: when the slot grows later,
+// the old block stays allocated until every step that addresses it is released.
 mg_status scratch(Device* d, int slot, size_t bytes, void** ptr) {
     if (d->scratch_bytes[slot] < bytes) {
         // The old workspace is released in stream order (or, during a capture, once the
@@ -133,6 +185,7 @@ mg_status scratch(Device* d, int slot, size_t bytes, void** ptr) {
         d->scratch_bytes[slot] = grow;
     }
     *ptr = d->scratch_ptr[slot];
+    graph_touch(d, *ptr);
     return MG_OK;
 }
 
@@ -178,6 +231,7 @@ mg_status buffer_new(Device* d, mg_dtype dtype, int rank, const uint64_t* shape,
 }
 
 void buffer_drop_prep(Buffer* b) {
+    if (b->prep || b->compact) b->device->prep_gen.fetch_add(1);
     if (b->prep) device_free(b->device, b->prep);
     b->prep = nullptr;
     b->prep_n = b->prep_k = b->prep_kp = 0;
@@ -225,6 +279,12 @@ void device_unref(Device* d) {
     if (d->refs.fetch_sub(1) != 1) return;
     cudaSetDevice(d->ordinal);
     cudaStreamSynchronize(d->own_stream);  // the device's stream since mg_device_close
+    for (void* p : d->held_frees) {  // parked for steps that are gone with their executors
+        if (d->plain_allocs.erase(p)) cudaFree(p);
+        else cudaFreeAsync(p, d->own_stream);
+    }
+    d->held_frees.clear();
+    cudaStreamSynchronize(d->own_stream);
     cudaFree(d->flags);
     cudaFree(d->counters);
     cudaFreeHost(d->host_flags);

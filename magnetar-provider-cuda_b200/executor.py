@@ -240,6 +240,34 @@ class CudaExecutor:
     def step_io(self, inputs: Mapping[str, object] = None, outputs: Mapping[str, object] = None):
         """The host I/O of ``replay_step_io`` described once: returns ``replay(offset=0)``, which
         replays with those arrays (their contents may change between calls, not their storage)."""
+        return self._step_io(N.lib().mg_executor_replay_step_io, (self._h,), inputs, outputs)
+
+    # ---- several captured steps (StepCaptureId) ----------------------------------------------
+    def end_step_capture_id(self) -> int:
+        """``end_step_capture``: ends the capture, keeps the step under a new id and runs it once
+        (its results are then available), as ``src/executor.rs`` end_step_capture does."""
+        v = ctypes.c_uint64()
+        check(N.lib().mg_executor_end_step_capture_id(self._h, ctypes.byref(v)))
+        return v.value
+
+    def replay_capture(self, step_id: int, offset: int = 0, inputs: Mapping[str, object] = None,
+                       outputs: Mapping[str, object] = None) -> None:
+        """``replay_step(id, offset, inputs)``, with ``outputs`` read back in the same call."""
+        self.capture_io(step_id, inputs, outputs)(offset)
+
+    def capture_io(self, step_id: int, inputs: Mapping[str, object] = None, outputs: Mapping[str, object] = None):
+        """``replay_capture``'s host I/O described once: returns ``replay(offset=0)``."""
+        return self._step_io(N.lib().mg_executor_replay_capture, (self._h, int(step_id)), inputs, outputs)
+
+    def release_step_capture(self, step_id: int) -> None:
+        check(N.lib().mg_executor_release_step_capture(self._h, int(step_id)))
+
+    def step_capture_count(self) -> int:
+        v = ctypes.c_int()
+        check(N.lib().mg_executor_step_capture_count(self._h, ctypes.byref(v)))
+        return v.value
+
+    def _step_io(self, fn, lead, inputs, outputs):
         entries = []
         keep = []
         for mapping, to_dev in ((inputs or {}, 1), (outputs or {}, 0)):
@@ -251,15 +279,16 @@ class CudaExecutor:
                     if not a.flags["C_CONTIGUOUS"] or (not to_dev and not a.flags["WRITEABLE"]):
                         raise ValueError(f"{id}: host arrays must be contiguous (and writable for outputs)")
                     ptr, nbytes = a.ctypes.data, a.nbytes
+                    keep.append(a)
                 key = id.encode()
                 keep.append(key)
                 entries.append(N.StepIO(key, ptr, nbytes, to_dev))
         arr_t = (N.StepIO * max(1, len(entries)))(*entries)
-        ptr, count, fn, h = ctypes.cast(arr_t, ctypes.c_void_p), len(entries), N.lib().mg_executor_replay_step_io, self._h
+        ptr, count = ctypes.cast(arr_t, ctypes.c_void_p), len(entries)
         refs = (arr_t, keep, inputs, outputs)  # kept alive with the closure
 
         def replay(offset: int = 0) -> None:
-            check(fn(h, offset, ptr, count))
+            check(fn(*lead, offset, ptr, count))
 
         replay.refs = refs
         return replay
@@ -288,6 +317,17 @@ class CudaExecutor:
         s, c, f = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
         check(N.lib().mg_executor_observations(self._h, ctypes.byref(s), ctypes.byref(c), ctypes.byref(f)))
         return {"started": s.value, "completed": c.value, "failed": f.value}
+
+    def observation_log(self) -> List[Dict[str, object]]:
+        """The most recent ``KernelObservation`` events, oldest first (at most 4096):
+        ``{"kind", "kernel", "invocation", "error"}`` (``error`` the failure's status name)."""
+        n = ctypes.c_uint32()
+        check(N.lib().mg_executor_observation_log(self._h, None, 0, ctypes.byref(n)))
+        arr = (N.Observation * max(1, n.value))()
+        check(N.lib().mg_executor_observation_log(self._h, ctypes.cast(arr, ctypes.c_void_p), n.value, ctypes.byref(n)))
+        return [{"kind": N.OBSERVATION_KINDS.get(o.kind, str(o.kind)), "kernel": o.kernel.decode(),
+                 "invocation": o.invocation, "error": N.STATUS_NAMES.get(o.status) if o.status else None}
+                for o in arr[:n.value]]
 
     # ---- tensor parallel -------------------------------------------------------------------
     def attach_comm(self, comm) -> None:

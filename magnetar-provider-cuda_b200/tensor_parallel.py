@@ -53,6 +53,48 @@ def split_rows(weight: np.ndarray, parts: int, member: int) -> np.ndarray:
     return np.ascontiguousarray(weight[s:e])
 
 
+class PeerLost(RuntimeError):
+    """A rank of the group did not reach a step in time (it exited, hung or was killed)."""
+
+    def __init__(self, step: int, missing):
+        self.step, self.missing = step, sorted(missing)
+        super().__init__(f"rank(s) {self.missing} did not reach step {step} in time")
+
+
+class StepMonitor:
+    """Host-side liveness of a group's ranks between steps, over a ``torch.distributed`` store.
+
+    Before each step every rank posts its arrival and waits, bounded, for every peer's; a rank
+    that exited or hung between steps is noticed there, on the host, before any kernel or
+    collective of the next step is enqueued -- so nothing waits on it on the device.  The
+    reference drives its members from one host thread and has no such failure path."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 30.0, prefix: str = "mg-step"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = float(timeout_s), prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def arrive(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), "1")
+
+    def check_peers(self, step: int) -> None:
+        """Raises ``PeerLost`` naming the ranks that have not arrived at ``step`` within the
+        timeout."""
+        import datetime
+        keys = [self._key(step, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, datetime.timedelta(seconds=self.timeout_s))
+        except Exception:
+            missing = [r for r, k in enumerate(keys) if not self.store.check([k])]
+            raise PeerLost(step, missing or list(range(self.world))) from None
+
+    def step(self, step: int) -> None:
+        self.arrive(step)
+        self.check_peers(step)
+
+
 class TpGroup:
     """This process's rank of a tensor-parallel group (an NCCL communicator)."""
 
@@ -92,6 +134,37 @@ class TpGroup:
 
     def all_reduce(self, buf: DeviceBuffer) -> None:
         check(N.lib().mg_comm_all_reduce(self._h, buf.handle))
+
+    # ---- failure handling: every NCCL call is bounded by the group's timeout -------------------
+    def set_timeout(self, timeout_ms: int) -> None:
+        """Host time after which a pending NCCL call aborts the communicator."""
+        check(N.lib().mg_comm_set_timeout(self._h, int(timeout_ms)))
+
+    def check(self) -> None:
+        """Raises (and aborts the communicator) if NCCL reported an asynchronous error."""
+        check(N.lib().mg_comm_check(self._h))
+
+    def wait(self, timeout_ms: int = 0) -> None:
+        """Waits for this rank's enqueued group work; aborts after ``timeout_ms`` (0: the
+        group's timeout) and raises ``DeviceUnavailable``."""
+        check(N.lib().mg_comm_wait(self._h, int(timeout_ms)))
+
+    def abort(self) -> None:
+        """Aborts the communicator at once (a peer is known to be gone)."""
+        check(N.lib().mg_comm_abort(self._h))
+
+    @property
+    def aborted(self) -> bool:
+        return bool(N.lib().mg_comm_is_aborted(self._h))
+
+    def begin_step(self, monitor: "StepMonitor", step: int) -> None:
+        """Checks on the host that every rank reached ``step`` before its work is enqueued; a
+        lost peer aborts the communicator and raises ``PeerLost``."""
+        try:
+            monitor.step(step)
+        except PeerLost:
+            self.abort()
+            raise
 
     def mlp(self, x: DeviceBuffer, gate_shard: DeviceBuffer, up_shard: DeviceBuffer, down_shard: DeviceBuffer,
             chunks: int = 4, out: DeviceBuffer = None) -> DeviceBuffer:

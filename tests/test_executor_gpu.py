@@ -520,3 +520,158 @@ def test_replay_step_with_host_io(executor, oracle, mpc):
     with pytest.raises(mpc.CudaError) as e:
         executor.replay_step_io(outputs={"missing": out})
     assert e.value.code == "ExecutionFailed"
+
+
+def _grow_scratch_and_allocate(mpc, kernels, oracle):
+    """Non-captured work that grows every scratch workspace the layer's step uses (a larger
+    matmul's A/B splits, attention partials and splits), then allocations that could land on
+    freed memory, filled with garbage."""
+    r = np.random.default_rng(11)
+    a = r.standard_normal((1024, 1024)).astype(np.float32)
+    b = r.standard_normal((1024, 1024)).astype(np.float32)
+    da, db = kernels.upload(a), kernels.upload(b)
+    kernels.matmul(da, db)  # per-call B split at M = 1024 (scratch slots for A and B)
+    q = r.standard_normal((1, 32 * 128)).astype(np.float32)
+    kv = r.standard_normal((8192, 8 * 128)).astype(np.float32)
+    kernels.attention(kernels.upload(q), kernels.upload(kv), kernels.upload(kv), 32, 128, kv_head_count=8,
+                      causal=True)  # decode partials
+    s = r.standard_normal((512, 16 * 64)).astype(np.float32)
+    kernels.attention(kernels.upload(s), kernels.upload(s), kernels.upload(s), 16, 64, causal=True)
+    junk = [kernels.upload(np.full((1 << 20,), np.nan, np.float32)) for _ in range(24)]
+    kernels.synchronize()
+    return junk
+
+
+def test_replay_after_scratch_growth_reads_live_memory(executor, oracle, mpc):
+    # A captured step keeps addressing the workspaces it was captured with: when later calls
+    # grow those workspaces, the old blocks must stay allocated for the step (not freed into
+    # the pool, where new allocations would reuse them).
+    layer = importlib.import_module("magnetar-provider-cuda_b200.layer")
+    cfg = layer.DecoderLayerConfig()
+    w = layer.make_inputs(cfg, seed=3)
+    layer.load(executor, w)
+    layer.capture(executor, cfg)
+    executor.replay_steps(1)
+    exp = _oracle_layer(oracle, cfg, w)
+    assert rel(executor.read_tensor("out"), exp) <= 1e-4
+    junk = _grow_scratch_and_allocate(mpc, executor.kernels, oracle)
+    for _ in range(3):
+        executor.replay_steps(1)
+        assert rel(executor.read_tensor("out"), exp) <= 1e-4
+    for j in junk:
+        j.release()
+
+
+def test_several_captured_steps_replay_and_release(executor, oracle, mpc):
+    # Several StepCaptureIds per executor (src/executor.rs:209-340): each step replays with its
+    # own inputs and outputs; a released step is gone; the others still replay.
+    layer = importlib.import_module("magnetar-provider-cuda_b200.layer")
+    cfg = layer.DecoderLayerConfig()
+    w = layer.make_inputs(cfg, seed=4)
+    layer.load(executor, w)
+    layer.forward(executor, cfg)
+    executor.synchronize()
+    executor.begin_step_capture()
+    layer.forward(executor, cfg)
+    whole = executor.end_step_capture_id()  # runs once as it ends
+    assert rel(executor.read_tensor("out"), _oracle_layer(oracle, cfg, w)) <= 1e-4
+    # a second step: the MLP half alone, on its own input
+    executor.write_tensor("x2b", executor.read_tensor("x2"))
+    executor.begin_step_capture()
+    executor.run(inv("rmsnorm", ["x2b", "mlp_norm"], "h2b", {"epsilon": float(cfg.eps)}))
+    executor.run(inv("gated-matmul", ["h2b", "wg", "wu"], "gb"))
+    executor.run(inv("matmul-residual", ["gb", "wd", "x2b"], "outb"))
+    mlp = executor.end_step_capture_id()
+    assert mlp != whole and executor.step_capture_count() == 2
+    out = np.empty((cfg.seq, cfg.hidden), np.float32)
+    for seed in (5, 6):
+        ids = np.random.default_rng(seed).integers(0, cfg.vocab, cfg.seq).astype(np.float32)
+        executor.replay_capture(whole, inputs={"ids": ids}, outputs={"out": out})
+        assert rel(out, _oracle_layer(oracle, cfg, dict(w, ids=ids))) <= 1e-4
+        x2 = np.random.default_rng(seed + 10).standard_normal((cfg.seq, cfg.hidden)).astype(np.float32)
+        outb = np.empty_like(out)
+        executor.replay_capture(mlp, inputs={"x2b": x2}, outputs={"outb": outb})
+        h2 = oracle.rmsnorm(x2, w["mlp_norm"], cfg.eps)
+        expb = oracle.matmul(oracle.gated_matmul(h2, w["wg"], w["wu"]), w["wd"], addend=x2, addend_mode=2)
+        assert rel(outb, expb) <= 1e-4
+    # an input the step never read is refused; so is an embedding id out of range (host check)
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_capture(mlp, inputs={"ids": ids})
+    assert e.value.code == "CaptureUnsupported" and "was not read" in e.value.detail
+    bad = ids.copy()
+    bad[3] = cfg.vocab
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_capture(whole, inputs={"ids": bad})
+    assert e.value.code == "ShapeUnsupported"
+    executor.release_step_capture(whole)
+    assert executor.step_capture_count() == 1
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_capture(whole)
+    assert e.value.code == "CaptureUnsupported"
+    executor.replay_capture(mlp, inputs={"x2b": x2}, outputs={"outb": outb})
+    assert rel(outb, expb) <= 1e-4
+    executor.release_step_capture(mlp)
+    executor.release_step_capture(mlp)  # unknown ids are not an error
+    assert executor.step_capture_count() == 0
+
+
+def test_replay_refuses_storage_that_changed_since_the_capture(executor, oracle, mpc):
+    # src/executor.rs replay_step: a resource rewritten into a new buffer after the capture
+    # ("no longer has its captured storage"), and a weight the step reads through its operand
+    # form, cannot feed a replay.
+    layer = importlib.import_module("magnetar-provider-cuda_b200.layer")
+    cfg = layer.DecoderLayerConfig()
+    w = layer.make_inputs(cfg, seed=5)
+    layer.load(executor, w)
+    layer.capture(executor, cfg)
+    with pytest.raises(mpc.CudaError) as e:  # a step-I/O write into a weight read as an operand form
+        executor.replay_step_io({"wq": w["wq"]})
+    assert e.value.code == "CaptureUnsupported" and "operand form" in e.value.detail
+    executor.replay_steps(1)
+    assert rel(executor.read_tensor("out"), _oracle_layer(oracle, cfg, w)) <= 1e-4
+    # the weight written in place: its operand form is rebuilt for eager calls, so the step's is gone
+    wq2 = (w["wq"] * 0.5).astype(np.float32)
+    mpc_native = importlib.import_module("magnetar-provider-cuda_b200._native")
+    mpc_native.check(mpc_native.lib().mg_buffer_upload(executor.buffer("wq").handle, wq2.ctypes.data, wq2.nbytes))
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_steps(1)
+    assert e.value.code == "CaptureUnsupported" and "wq" in e.value.detail
+    # a rewritten id (a new buffer) invalidates the step
+    layer.capture(executor, cfg)
+    executor.replay_steps(1)
+    executor.write_tensor("ids", w["ids"])
+    with pytest.raises(mpc.CudaError) as e:
+        executor.replay_steps(1)
+    assert e.value.code == "CaptureUnsupported" and "no longer has its captured storage" in e.value.detail
+    # capturing again makes a step over the current storage
+    layer.capture(executor, cfg)
+    executor.replay_steps(1)
+    assert rel(executor.read_tensor("out"), _oracle_layer(oracle, cfg, dict(w, wq=wq2))) <= 1e-4
+
+
+def test_observation_log_records_each_dispatch(executor, mpc):
+    # src/executor.rs:1082-1100, 1197-1232: Started, then Completed / Failed / Timeout.
+    executor.write_tensor("a", np.ones((2, 2), np.float32))
+    executor.run(inv("add", ["a", "a"], "b"))
+    r = executor.submit_kernel(inv("no-such-kernel", ["a"], "o"))
+    assert not r.success
+    r = executor.submit_kernel(inv("add", ["a", "a"], "c", deadline_millis=0))
+    assert not r.success and r.error_code == "KernelTimeout"
+    log = executor.observation_log()
+    assert [o["kind"] for o in log[-6:]] == [
+        "KernelDispatchStarted", "KernelDispatchCompleted", "KernelDispatchStarted", "KernelDispatchFailed",
+        "KernelDispatchStarted", "KernelTimeout"]
+    assert [o["kernel"] for o in log[-6:]] == ["add", "add", "no-such-kernel", "no-such-kernel", "add", "add"]
+    assert log[-3]["error"] == "KernelNotFound"
+    inv_ids = [o["invocation"] for o in log[-6:]]
+    assert inv_ids[0] == inv_ids[1] and inv_ids[2] == inv_ids[3] and inv_ids[4] == inv_ids[5]
+    assert inv_ids[0] < inv_ids[2] < inv_ids[4]
+
+
+def test_observation_log_is_bounded(executor):
+    executor.write_tensor("a", np.ones((4,), np.float32))
+    for _ in range(2100):
+        executor.run(inv("add", ["a", "a"], "b"))
+    log = executor.observation_log()
+    assert len(log) == 4096
+    assert log[-1]["kind"] == "KernelDispatchCompleted"

@@ -3,8 +3,8 @@
 It exists for callers that cannot allocate device memory at the moment they multiply (a
 runtime whose device memory is fully handed out under a fixed budget, or a latency-critical
 thread that must not enter the driver's allocator).  It keeps its partial sums in a workspace
-compiled into the library, so these tests check, through the C ABI, that two calls in a row
-match the ordinary allocating matmul within the matmul tolerance, and that a shape whose
+compiled into the library, so these tests check, through the C ABI, that calls in a row
+match the CPU oracle's matmul (and an f64 product) within the matmul tolerance, and that a shape whose
 partials would not fit the fixed workspace is refused with a clear error.  The file name
 sorts last so that a run stopping at the first failure has run every other test before it.
 """
@@ -33,8 +33,10 @@ def fixed_gemv(mpc, kernels, a_buf, b_buf, out_buf, m, k, n):
     return status
 
 
-@pytest.mark.parametrize("shapes", [[(16, 4096, 4096), (3, 1000, 256)], [(1, 512, 1376), (16, 512, 1376)]])
-def test_fixed_workspace_gemv_matches_the_allocating_matmul(mpc, kernels, shapes):
+@pytest.mark.parametrize("shapes", [[(16, 4096, 4096), (3, 1000, 256)], [(1, 512, 1376), (16, 512, 1376)],
+                                    [(5, 777, 260), (7, 4099, 1028)]])
+def test_fixed_workspace_gemv_matches_the_oracle(mpc, kernels, oracle, shapes):
+    # Odd row counts and k that is not a multiple of the kernel's k step (ragged slices) too.
     r = np.random.default_rng(42)
     for m, k, n in shapes:  # two calls in a row share the fixed workspace
         a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
@@ -43,8 +45,8 @@ def test_fixed_workspace_gemv_matches_the_allocating_matmul(mpc, kernels, shapes
         out = kernels.empty((m, n))
         assert fixed_gemv(mpc, kernels, da, db, out, m, k, n) == 0, mpc.lib().mg_last_error()
         got = kernels.download(out)
-        expected = kernels.download(kernels.matmul(da, db))
-        assert rel(got, expected) <= TOL_MATMUL
+        assert rel(got, oracle.matmul(a, b)) <= TOL_MATMUL
+        assert rel(got, a.astype(np.float64) @ b.astype(np.float64)) <= TOL_MATMUL
 
 
 def test_fixed_workspace_gemv_refuses_shapes_beyond_its_workspace(mpc, kernels):

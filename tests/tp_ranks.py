@@ -6,7 +6,8 @@ down by rows, the reference's ``WeightShard`` split, src/multi/tensor_parallel.r
 and runs
   1. the tensor-parallel SwiGLU MLP entry point (one NCCL all-reduce, chunked), and
   2. the executor with a tensor-parallel plan (``apply_tensor_parallel``: its row-split
-     matmul all-reduces the partial outputs, src/multi.rs:543-562),
+     matmul all-reduces the partial outputs, src/multi.rs:543-562), run directly and
+     captured as one step whose graph holds the all-reduce, replayed with new inputs,
 then compares its result with the CPU oracle of the unsplit computation (rel-L2 <= 1e-4).
 A rank that fails exits non-zero; the process group has a short timeout so that the others
 end with an error instead of waiting.
@@ -74,6 +75,20 @@ def main():
             ex.run(mpc.KernelInvocation("matmul", ["h", "down"], "y"))
             results["executor plan up=columns down=rows"] = rel(ex.read_tensor("y"),
                                                                 orc.matmul(orc.matmul(x, up), down))
+            # the same two matmuls captured as one step under the plan, the all-reduce of the
+            # row-split projection inside the graph (src/multi/tensor_parallel.rs:542-690), then
+            # replayed with new inputs written into the captured buffer
+            ex.begin_step_capture()
+            ex.run(mpc.KernelInvocation("matmul", ["x", "up"], "h"))
+            ex.run(mpc.KernelInvocation("matmul", ["h", "down"], "y"))
+            step = ex.end_step_capture_id()
+            results["captured plan, first run"] = rel(ex.read_tensor("y"), orc.matmul(orc.matmul(x, up), down))
+            for t in range(3):
+                xt = np.random.default_rng(77 + t).standard_normal((16, 128)).astype(np.float32)
+                yt = np.empty((16, 128), np.float32)
+                ex.replay_capture(step, inputs={"x": xt}, outputs={"y": yt})
+                results[f"captured plan, replay {t}"] = rel(yt, orc.matmul(orc.matmul(xt, up), down))
+            ex.release_step_capture(step)
             ex.attach_comm(None)
         finally:
             ex.close()
