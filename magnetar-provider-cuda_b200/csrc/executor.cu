@@ -55,6 +55,19 @@ struct CapturedStep {
     // Embedding id resources and the vocabulary of their table (host-checked on replay writes).
     std::map<std::string, uint64_t> embedding_ids;
     uint64_t storage_gen = 0, prep_gen = 0;  // when the recorded state was last known current
+    // Replays with host I/O whose host memory is pinned run as one graph launch: the input
+    // copies, the replay offset, the step itself (a child graph), the output copies and the
+    // embedding-flag read and reset, built once per distinct set of host buffers and kept here.
+    struct IoGraph {
+        std::vector<mg_step_io> io;  // the host side (ids point into `names`)
+        std::vector<std::string> names;
+        std::vector<void*> device;   // the device buffer each entry copies to or from
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        uint64_t* offset_word = nullptr;  // pinned host word holding the replay's offset
+    };
+    std::vector<IoGraph*> io_graphs;
+    bool io_graph_failed = false;  // building one failed once: use separate copies from then on
 };
 
 // One entry of the executor's observation log (src/executor.rs:1082-1100, KernelObservation).
@@ -171,9 +184,18 @@ mg_status store_replace(mg_executor* ex, const std::string& id, Buffer* b) {
     return MG_OK;
 }
 
+void io_graph_destroy(CapturedStep::IoGraph* g) {
+    if (!g) return;
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    if (g->offset_word) cudaFreeHost(g->offset_word);
+    delete g;
+}
+
 void step_destroy(mg_executor* ex, CapturedStep* st) {
     if (!st) return;
     cudaSetDevice(ex->device->ordinal);
+    for (CapturedStep::IoGraph* g : st->io_graphs) io_graph_destroy(g);
     if (st->exec) cudaGraphExecDestroy(st->exec);
     if (st->graph) cudaGraphDestroy(st->graph);
     graph_release(ex->device, st->blocks);
@@ -1249,6 +1271,90 @@ mg_status replay_step_n(mg_executor* ex, CapturedStep* st, int count, uint64_t o
     return MG_OK;
 }
 
+bool pinned_host(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// The one-launch graph of a replay with this host I/O (built on first use, kept with the step):
+// null when some host buffer is not pinned (graph copies need page-locked memory) or the graph
+// cannot be built, in which case the replay issues its copies separately.
+CapturedStep::IoGraph* io_graph_for(mg_executor* ex, CapturedStep* st, const mg_step_io* io, int count,
+                                    const std::vector<Buffer*>& bufs) {
+    for (CapturedStep::IoGraph* g : st->io_graphs) {
+        if ((int)g->io.size() != count) continue;
+        bool same = true;
+        for (int i = 0; i < count && same; i++)
+            same = g->io[i].host == io[i].host && g->io[i].bytes == io[i].bytes && g->io[i].to_device == io[i].to_device &&
+                   g->names[i] == io[i].id && g->device[i] == bufs[(size_t)i]->ptr;
+        if (same) return g;
+    }
+    for (int i = 0; i < count; i++)
+        if (io[i].bytes && !pinned_host(io[i].host)) return nullptr;
+    Device* d = ex->device;
+    CapturedStep::IoGraph* g = new (std::nothrow) CapturedStep::IoGraph();
+    if (!g) return nullptr;
+    bool ok = cudaGraphCreate(&g->graph, 0) == cudaSuccess;
+    std::vector<cudaGraphNode_t> before;
+    for (int i = 0; ok && i < count; i++) {
+        g->names.push_back(io[i].id);
+        g->io.push_back(io[i]);
+        g->device.push_back(bufs[(size_t)i]->ptr);
+        if (!io[i].to_device || !io[i].bytes) continue;
+        cudaGraphNode_t n;
+        ok = cudaGraphAddMemcpyNode1D(&n, g->graph, nullptr, 0, bufs[(size_t)i]->ptr, io[i].host, io[i].bytes,
+                                      cudaMemcpyHostToDevice) == cudaSuccess;
+        if (ok) before.push_back(n);
+    }
+    if (ok && st->advancing) {
+        ok = cudaMallocHost(&g->offset_word, sizeof(uint64_t)) == cudaSuccess;
+        cudaGraphNode_t n;
+        if (ok)
+            ok = cudaGraphAddMemcpyNode1D(&n, g->graph, nullptr, 0, d->step_offset, g->offset_word, sizeof(uint64_t),
+                                          cudaMemcpyHostToDevice) == cudaSuccess;
+        if (ok) before.push_back(n);
+    }
+    cudaGraphNode_t step_node = nullptr;
+    if (ok)
+        ok = cudaGraphAddChildGraphNode(&step_node, g->graph, before.data(), before.size(), st->graph) == cudaSuccess;
+    for (int i = 0; ok && i < count; i++) {
+        if (io[i].to_device || !io[i].bytes) continue;
+        cudaGraphNode_t n;
+        ok = cudaGraphAddMemcpyNode1D(&n, g->graph, &step_node, 1, io[i].host, bufs[(size_t)i]->ptr, io[i].bytes,
+                                      cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    if (ok && st->has_embedding) {
+        // the sticky id flag read back, then reset for the next replay
+        cudaGraphNode_t rd, rs;
+        ok = cudaGraphAddMemcpyNode1D(&rd, g->graph, &step_node, 1, d->host_flags, d->flags, sizeof(int),
+                                      cudaMemcpyDeviceToHost) == cudaSuccess;
+        cudaMemsetParams mp = {};
+        mp.dst = d->flags;
+        mp.value = 0;
+        mp.elementSize = sizeof(int);
+        mp.width = 1;
+        mp.height = 1;
+        if (ok) ok = cudaGraphAddMemsetNode(&rs, g->graph, &rd, 1, &mp) == cudaSuccess;
+    }
+    if (ok) ok = cudaGraphInstantiate(&g->exec, g->graph, 0) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        io_graph_destroy(g);
+        st->io_graph_failed = true;
+        return nullptr;
+    }
+    if (st->io_graphs.size() >= 4) {  // a few host-buffer sets per step; the oldest goes
+        io_graph_destroy(st->io_graphs.front());
+        st->io_graphs.erase(st->io_graphs.begin());
+    }
+    st->io_graphs.push_back(g);
+    return g;
+}
+
 // One replay with host I/O (see mg_executor_replay_step_io).
 mg_status replay_io(mg_executor* ex, CapturedStep* st, uint64_t offset, const mg_step_io* io, int count) {
     Device* d = ex->device;
@@ -1287,6 +1393,19 @@ mg_status replay_io(mg_executor* ex, CapturedStep* st, uint64_t offset, const mg
             }
         }
         bufs[(size_t)i] = b;
+    }
+    if (!st->io_graph_failed) {
+        CapturedStep::IoGraph* g = io_graph_for(ex, st, io, count, bufs);
+        if (g) {
+            if (g->offset_word) *g->offset_word = offset;  // read by the graph's first copy
+            MG_CUDA(cudaGraphLaunch(g->exec, d->stream), "replaying the captured step");
+            d->launches.fetch_add(st->kernels);
+            for (int i = 0; i < count; i++) (io[i].to_device ? d->uploads : d->downloads).fetch_add(io[i].bytes ? 1 : 0);
+            MG_CUDA(cudaStreamSynchronize(d->stream), "waiting for the replayed step");
+            if (st->has_embedding && d->host_flags[0])
+                return fail(MG_SHAPE_UNSUPPORTED, "embedding lookup id is not a valid in-range non-negative integer");
+            return MG_OK;
+        }
     }
     for (int i = 0; i < count; i++) {
         if (!io[i].to_device || !io[i].bytes) continue;

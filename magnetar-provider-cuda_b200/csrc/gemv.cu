@@ -963,7 +963,13 @@ mg_status gemv_cluster(Device* d, const GemmArgs& g) {
     }
 }
 
+bool gemv_tc_eligible(const GemmArgs& g);
+mg_status gemv_tc(Device* d, const GemmArgs& g);
+
 mg_status gemv(Device* d, const GemmArgs& g) {
+    // From about eight rows the CUDA-core kernels are bound by FMA issue: the tensor cores
+    // take those (gemv_tc.cu).
+    if (gemv_tc_eligible(g)) return gemv_tc(d, g);
     if (gemv_cluster_eligible(g)) return gemv_cluster(d, g);
     uint64_t tma_slices = 0, tma_slice_len = 0;
     if (g.n <= (1ull << 31) && g.k <= (1ull << 31) && gemv_tma_plan(d, g, &tma_slices, &tma_slice_len))

@@ -1,0 +1,465 @@
+// f32 matmul for a few rows (the decode side, 8 <= M <= 16) on the 5th-generation tensor cores,
+// with B streamed from HBM exactly once.
+//
+// The CUDA-core few-row path (gemv.cu) spends two FLOPs of FMA issue per weight value per row:
+// from about eight rows up it is bound by instruction issue, not by reading B.  Here the MMA is
+// turned around so that the weight is the 128-row operand and the activation rows are the
+// MMA's N = 16: D[n][m] = sum_k B[k][n] * A[m][k].  B's row-major [k, n] tile is exactly the
+// MN-major operand layout (n contiguous), so a stage is four TMA boxes of [32 k x 32 n] with
+// 128-byte swizzling, used as they land -- no transpose.  Each operand enters as two tf32
+// terms (3xTF32, the f32 contract): eight converter warps split every raw tile into hi
+// (truncated to tf32) and lo = tf32(x - hi), and one thread issues lo*hi + hi*lo + hi*hi into
+// one TMEM accumulator.  The raw ring (what HBM streams into) and the converted buffers (what
+// the MMAs read) are separate, so a raw stage is refilled as soon as the converters have read
+// it.  The k slices of one 128-column tile (and, gated, the gate and up terms) form one
+// thread-block cluster; each CTA stages its [16 x 128] partial, sends each band of rows to
+// the CTA that owns it with one bulk copy, and owners add the partials in split order
+// (deterministic), apply bias / residual / SwiGLU and write.
+//
+// Per weight value the converters spend about four instructions (the FMA path: sixteen FMAs
+// at 16 rows), and the tensor pipe does the multiply, so the kernel streams B at HBM speed.
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace mg {
+namespace {
+
+using namespace sm100;
+
+constexpr int kTcCols = 128;     // columns of B per CTA: the MMA's M
+constexpr int kTcK = 32;         // k rows per stage: one 128-byte swizzle row of A
+constexpr int kTcRows = 16;      // the MMA's N: activation rows (zero past M)
+constexpr int kRawStages = 7;    // raw B + A tiles in flight from HBM
+constexpr int kConvStages = 2;   // converted (hi / lo) tiles the MMAs read
+constexpr int kConvThreads = 256;
+constexpr int kMaxCluster = 16;  // non-portable cluster size (checked against the GPU at launch)
+
+struct TcGemvShape {
+    static constexpr int kWRaw = kTcK * kTcCols * 4;   // 16 KB: four [32 k][32 n] swizzled boxes
+    static constexpr int kARaw = kTcRows * kTcK * 4;   // 2 KB: [16 m][32 k] swizzled
+    static constexpr int kRawStage = kWRaw + kARaw;    // 18 KB
+    static constexpr int kConvStage = 2 * kWRaw + 2 * kARaw;  // W hi, W lo, A hi, A lo
+    static constexpr int kRing = kRawStages * kRawStage + kConvStages * kConvStage;
+    static constexpr int kRecv = 32 * kTcCols * 4;     // the other CTAs' rows of this CTA's band
+    static constexpr int kBars = 256;
+    static constexpr int kSmem = kRing + kRecv + kBars + 1024;
+    static constexpr int kThreads = 320;  // producer, MMA, 8 converter warps
+    static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+    static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
+};
+
+struct GemvTcArgs {
+    float* out;
+    const float* addend;
+    int addend_mode;  // 0 none, 1 row [n], 2 full [m, n]
+    uint64_t m, n, k;
+    uint64_t slice_len;  // k rows per split (a multiple of kTcK)
+    int splits;          // S; the cluster is (1, S, terms)
+    int terms;           // 1, or 2 for gated (gate: z = 0, up: z = 1)
+    int b_early;         // B does not depend on the preceding kernel: its first loads precede the wait
+    int* error;
+};
+
+// Shared-memory descriptor of an MN-major operand written by TMA with 128-byte swizzling: 32
+// consecutive tf32 of the M dimension per 128-byte row, eight k rows per 1024-byte atom (SBO
+// between atoms along k), the next 32 of M `lbo` bytes further.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// hi = x truncated to tf32 (nothing can overflow), lo = tf32(x - hi): exact to 2^-21 of x.
+__device__ __forceinline__ void split_fast(float4 v, float4& hi, float4& lo) {
+    hi = make_float4(__uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u), __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                     __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u), __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+    lo = make_float4(tf32_rna(v.x - hi.x), tf32_rna(v.y - hi.y), tf32_rna(v.z - hi.z), tf32_rna(v.w - hi.w));
+}
+
+__global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_b2, GemvTcArgs p) {
+    using S = TcGemvShape;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* base_ptr = smem_raw + (base - raw);
+    auto raw_stage = [&](int s) { return base + (uint32_t)(s * S::kRawStage); };
+    auto conv_stage = [&](int c) { return base + (uint32_t)(kRawStages * S::kRawStage + c * S::kConvStage); };
+    const uint32_t recv = base + S::kRing;
+    const uint32_t bar_base = recv + S::kRecv;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + S::kRing + S::kRecv);
+    auto raw_full = [&](int s) { return bar_base + 8u * s; };
+    auto raw_empty = [&](int s) { return bar_base + 8u * (kRawStages + s); };
+    auto conv_full = [&](int c) { return bar_base + 8u * (2 * kRawStages + c); };
+    auto conv_empty = [&](int c) { return bar_base + 8u * (2 * kRawStages + kConvStages + c); };
+    const uint32_t accum_bar = bar_base + 8u * (2 * kRawStages + 2 * kConvStages);
+    const uint32_t recv_bar = accum_bar + 8u;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 2 * kRawStages + 2 * kConvStages + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kRawStages + 2 * kConvStages + 3);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nc = p.splits * p.terms;
+    const int rank = (int)cooperative_groups::this_cluster().block_rank();
+    const int mb = ((int)p.m + nc - 1) / nc;  // activation rows each cluster CTA finishes
+    const int my_lo = min((int)p.m, rank * mb), my_hi = min((int)p.m, my_lo + mb);
+    const uint64_t n0 = (uint64_t)blockIdx.x * kTcCols;
+    const int term = blockIdx.z;
+    const CUtensorMap* map_w = term ? &map_b2 : &map_b;
+    const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
+    const uint64_t k1 = min(p.k, k0 + p.slice_len);
+    const int num_kb = k1 > k0 ? (int)((k1 - k0 + kTcK - 1) / kTcK) : 0;
+
+    auto issue_w = [&](int i) {
+        const int s = i % kRawStages;
+        const uint32_t st = raw_stage(s);
+        mbar_arrive_expect_tx(raw_full(s), (uint32_t)S::kRawStage);
+        const int ky = (int)(k0 + (uint64_t)i * kTcK);
+#pragma unroll
+        for (int j = 0; j < 4; j++) tma_load_2d(st + (uint32_t)(j * 4096), map_w, raw_full(s), (int)n0 + 32 * j, ky);
+    };
+    auto issue_a = [&](int i) {
+        const int s = i % kRawStages;
+        tma_load_2d(raw_stage(s) + S::kWRaw, &map_a, raw_full(s), (int)(k0 + (uint64_t)i * kTcK), 0);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRawStages; s++) {
+            mbar_init(raw_full(s), 1);
+            mbar_init(raw_empty(s), kConvThreads);
+        }
+        for (int c = 0; c < kConvStages; c++) {
+            mbar_init(conv_full(c), kConvThreads);
+            mbar_init(conv_empty(c), 1);
+        }
+        mbar_init(accum_bar, 1);
+        mbar_init(recv_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        // The other CTAs' rows of this CTA's band, one bulk copy from each.
+        mbar_arrive_expect_tx(recv_bar, (uint32_t)((nc - 1) * (my_hi - my_lo) * kTcCols * 4));
+        if (p.b_early)
+            for (int i = 0; i < min(kRawStages, num_kb); i++) issue_w(i);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32((const void*)tmem_slot), 32);
+        tmem_relinquish();
+    }
+    cluster_arrive();  // phase 1: every receive barrier of the cluster is armed
+    pdl_enter();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < min(kRawStages, num_kb); i++) {
+            if (!p.b_early) issue_w(i);
+            issue_a(i);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer: refills a raw stage once the converters have read it ------------
+        if (lane == 0) {
+            for (int i = kRawStages; i < num_kb; i++) {
+                const int s = i % kRawStages;
+                if (!mbar_wait(raw_empty(s), ((uint32_t)(i / kRawStages) & 1u) ^ 1u)) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                if (*abort_flag) break;
+                issue_w(i);
+                issue_a(i);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- MMA issuer: D[128 n][16 m] += W_lo A_hi + W_hi A_lo + W_hi A_hi --------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(kTcCols, kTcRows) | (1u << 15);  // A (the weight) MN-major
+            bool ok = true;
+            for (int i = 0; i < num_kb; i++) {
+                const int c = i % kConvStages;
+                if (!mbar_wait(conv_full(c), (uint32_t)(i / kConvStages) & 1u) || *abort_flag) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t cs = conv_stage(c);
+                const uint32_t whi = cs, wlo = cs + S::kWRaw, ahi = cs + 2 * S::kWRaw, alo = ahi + S::kARaw;
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 8; kk++) {
+                    const uint64_t dwhi = desc_mn_sw128(whi + (uint32_t)(kk * 1024), 4096);
+                    const uint64_t dwlo = desc_mn_sw128(wlo + (uint32_t)(kk * 1024), 4096);
+                    const uint64_t dahi = desc_k_sw128(ahi) + (uint64_t)((kk * 32) >> 4);
+                    const uint64_t dalo = desc_k_sw128(alo) + (uint64_t)((kk * 32) >> 4);
+                    mma_tf32(tmem, dwlo, dahi, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    mma_tf32(tmem, dwhi, dalo, idesc, 1u);
+                    mma_tf32(tmem, dwhi, dahi, idesc, 1u);
+                }
+                tc_commit(conv_empty(c));  // frees the conversion buffer once these MMAs have read it
+            }
+            if (ok && num_kb > 0) tc_commit(accum_bar);
+            else mbar_arrive(accum_bar);  // release the epilogue
+        }
+        __syncwarp();
+    } else {
+        // ---- warps 2..9: split each raw stage into hi / lo terms in a conversion buffer --------
+        const int t = threadIdx.x - 64;
+        for (int i = 0; i < num_kb; i++) {
+            const int s = i % kRawStages, c = i % kConvStages;
+            bool ok = mbar_wait(raw_full(s), (uint32_t)(i / kRawStages) & 1u);
+            ok = mbar_wait(conv_empty(c), ((uint32_t)(i / kConvStages) & 1u) ^ 1u) && ok;
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.error, 1);  // still arrive below so that no one waits for this thread
+            }
+            const uint32_t rs = raw_stage(s), cs = conv_stage(c);
+#pragma unroll
+            for (int j = 0; j < S::kWRaw / 16 / kConvThreads; j++) {
+                const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
+                float4 h, l;
+                split_fast(lds4(rs + off), h, l);
+                sts4(cs + off, h.x, h.y, h.z, h.w);
+                sts4(cs + S::kWRaw + off, l.x, l.y, l.z, l.w);
+            }
+            if (t < S::kARaw / 16) {
+                const uint32_t off = (uint32_t)t * 16;
+                float4 h, l;
+                split_fast(lds4(rs + S::kWRaw + off), h, l);
+                sts4(cs + 2 * S::kWRaw + off, h.x, h.y, h.z, h.w);
+                sts4(cs + 2 * S::kWRaw + S::kARaw + off, l.x, l.y, l.z, l.w);
+            }
+            fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
+            mbar_arrive(conv_full(c));
+            mbar_arrive(raw_empty(s));
+            if (*abort_flag) break;
+        }
+    }
+    bool acc_ready = false;
+    if (warp >= 2 && warp < 6) {
+        const bool waited = mbar_wait(accum_bar, 0);
+        if (!waited) atomicExch(p.error, 1);
+        // tcgen05.ld is warp-collective: the whole warp reads the accumulator or none of it.
+        acc_ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_kb > 0);
+    }
+    // ---- stage this CTA's partial as [16 m][128 n] in the drained first conversion buffer ------
+    float* staged = reinterpret_cast<float*>(base_ptr + (conv_stage(0) - base));
+    if (warp >= 2 && warp < 6) {
+        tc_fence_after();
+        const int q = warp % 4;
+        const int n = q * 32 + lane;
+        float v[16];
+        if (acc_ready) {
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16), v);
+            tc_wait_ld();
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kTcRows; j++) staged[j * kTcCols + n] = v[j];
+        fence_proxy_async();  // the staged rows are read by bulk copies next
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 32);
+    }
+    // ---- exchange: each band of rows to the CTA that owns it ------------------------------------
+    cluster_wait();  // phase 1
+    {
+        const int o = (int)threadIdx.x - 64;  // one issuing thread per destination
+        if (o >= 0 && o < nc && o != rank) {
+            const int lo = min((int)p.m, o * mb), hi = min((int)p.m, lo + mb);
+            if (hi > lo)
+                bulk_copy_to_cluster(mapa(recv + (uint32_t)(rank * mb * kTcCols * 4), (uint32_t)o),
+                                     conv_stage(0) + (uint32_t)(lo * kTcCols * 4), (uint32_t)((hi - lo) * kTcCols * 4),
+                                     mapa(recv_bar, (uint32_t)o));
+        }
+    }
+    if (!mbar_wait(recv_bar, 0)) atomicExch(p.error, 1);
+    cluster_arrive();  // phase 2: every copy into this CTA has landed
+    // ---- finish this CTA's rows: splits in order, per term ---------------------------------------
+    const float* recvf = reinterpret_cast<const float*>(base_ptr + S::kRing);
+    for (int e = (int)threadIdx.x; e < (my_hi - my_lo) * kTcCols; e += blockDim.x) {
+        const int r = my_lo + e / kTcCols, c = e % kTcCols;
+        const uint64_t col = n0 + (uint64_t)c;
+        if (col >= p.n) continue;
+        auto from = [&](int src) {
+            return src == rank ? staged[r * kTcCols + c] : recvf[(src * mb + (r - my_lo)) * kTcCols + c];
+        };
+        float g = 0.0f;
+        for (int s = 0; s < p.splits; s++) g += from(s);
+        float v;
+        if (p.terms == 2) {
+            float u = 0.0f;
+            for (int s = 0; s < p.splits; s++) u += from(p.splits + s);
+            v = (g * (1.0f / (1.0f + expf(-g)))) * u;
+        } else {
+            v = g;
+            if (p.addend_mode == 1) v += p.addend[col];
+            else if (p.addend_mode == 2) v += p.addend[(uint64_t)r * p.n + col];
+        }
+        p.out[(uint64_t)r * p.n + col] = v;
+    }
+    cluster_wait();  // phase 2: every copy out of this CTA's shared memory has landed
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tc_gemv_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// Row-major f32 [rows, cols], box [box_rows x 32 columns], 128-byte swizzle, zero past the edges.
+mg_status tc_gemv_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = tc_gemv_encode_fn();
+    if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * sizeof(float)};
+    cuuint32_t box[2] = {32, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
+// The fewest rows that take this path (MAGNETAR_CUDA_FEWROW_TC: a row count, or 0 to leave the
+// few-row matmul on the CUDA cores).
+int tc_min_rows() {
+    static int v = [] {
+        const char* e = getenv("MAGNETAR_CUDA_FEWROW_TC");
+        if (!e || !*e) return 8;
+        const int x = atoi(e);
+        return x <= 0 ? kTcRows + 1 : x;
+    }();
+    return v;
+}
+
+}  // namespace
+
+namespace k {
+
+bool gemv_tc_eligible(const GemmArgs& g) {
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    return g.m >= (uint64_t)tc_min_rows() && g.m <= (uint64_t)kTcRows && !g.transpose_a && !g.transpose_b &&
+           g.k % 4 == 0 && g.n % 4 == 0 && al(g.a) && al(g.b) && (!g.b2 || al(g.b2)) && !g.b16[0] && !g.packed[0] &&
+           g.k < (1ull << 31) && g.n < (1ull << 31);
+}
+
+mg_status gemv_tc(Device* d, const GemmArgs& g) {
+    using S = TcGemvShape;
+    const uint64_t col_tiles = (g.n + kTcCols - 1) / kTcCols;
+    if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
+    const int terms = g.gated ? 2 : 1;
+    const uint64_t kb = (g.k + kTcK - 1) / kTcK;
+    uint64_t splits = (uint64_t)d->sm_count / (col_tiles * terms);
+    if (splits > (uint64_t)(kMaxCluster / terms)) splits = kMaxCluster / terms;
+    if (splits > kb) splits = kb;
+    if (splits < 1) splits = 1;
+    GemvTcArgs p;
+    p.out = g.out;
+    p.addend = g.addend;
+    p.addend_mode = g.addend_mode;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.terms = terms;
+    p.b_early = g.b_stable ? 1 : 0;
+    p.error = d->flags + 2;
+    auto set_splits = [&](uint64_t sp) {
+        p.slice_len = ((kb + sp - 1) / sp) * kTcK;
+        p.splits = (int)((g.k + p.slice_len - 1) / p.slice_len);
+        if (p.splits < 1) p.splits = 1;
+    };
+    set_splits(splits);
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+                "configuring the tensor-core gemv kernel");
+        MG_CUDA(cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "allowing the tensor-core gemv kernel clusters of up to 16");
+        configured[d->ordinal & 63] = true;
+    }
+    // Clusters larger than 8 only where the GPU holds them all at once (queried once per size);
+    // otherwise fewer k splits.
+    static int fits[kMaxCluster + 1] = {0};  // 1 fits, -1 does not
+    while (p.splits * p.terms > 8) {
+        const int nc = p.splits * p.terms;
+        if (fits[nc] == 0) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
+            q.blockDim = dim3(S::kThreads, 1, 1);
+            q.dynamicSmemBytes = S::kSmem;
+            cudaLaunchAttribute ca;
+            ca.id = cudaLaunchAttributeClusterDimension;
+            ca.val.clusterDim.x = 1;
+            ca.val.clusterDim.y = (unsigned)p.splits;
+            ca.val.clusterDim.z = (unsigned)p.terms;
+            q.attrs = &ca;
+            q.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_tc_kernel, &q) != cudaSuccess) {
+                (void)cudaGetLastError();
+                clusters = 0;
+            }
+            fits[nc] = clusters > 0 ? 1 : -1;
+        }
+        if (fits[nc] > 0) break;
+        set_splits((uint64_t)p.splits - 1);
+    }
+    CUtensorMap maps[3];
+    MG_TRY(tc_gemv_map(&maps[0], g.a, g.m, g.k, kTcRows));
+    MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, kTcK));
+    if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, kTcK));
+    else maps[2] = maps[1];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
+    cfg.blockDim = dim3(S::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)p.splits;
+    attr[0].val.clusterDim.z = (unsigned)p.terms;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = d->pdl ? 2 : 1;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel, maps[0], maps[1], maps[2], p), "tensor-core gemv launch");
+    return launched(d, "tensor-core gemv launch");
+}
+
+}  // namespace k
+}  // namespace mg

@@ -321,6 +321,54 @@ def test_gated_matmul(kernels, oracle, m, k, n):
     assert rel(got, oracle.gated_matmul(a, g, u)) <= TOL_MATMUL
 
 
+# The few-row tensor-core path (8 <= M <= 16, k and n multiples of 4): the weight as the MMA's
+# 128-row operand, raw tiles split into tf32 hi / lo in the kernel, k split across a cluster.
+FEWROW_TC_SHAPES = [(8, 4096, 4096), (11, 4096, 4096), (16, 4096, 4096), (16, 4100, 260), (9, 64, 4),
+                    (16, 32, 128), (12, 12288, 136), (16, 1376, 512), (10, 512, 1376), (16, 256, 65536)]
+
+
+@pytest.mark.parametrize("m,k,n", FEWROW_TC_SHAPES)
+@pytest.mark.parametrize("weight", [False, True])
+def test_fewrow_tensor_core_matmul(kernels, oracle, m, k, n, weight):
+    r = rng(17)
+    a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
+    b = r.standard_normal((k, n)).astype(np.float32)
+    db = kernels.upload(b)
+    if weight:
+        db.set_weight()
+    da = kernels.upload(a)
+    first = kernels.download(kernels.matmul(da, db))
+    assert rel(first, oracle.matmul(a, b)) <= TOL_MATMUL
+    np.testing.assert_array_equal(first, kernels.download(kernels.matmul(da, db)))  # deterministic
+
+
+@pytest.mark.parametrize("m,k,n", [(16, 2048, 1000), (8, 512, 1376), (13, 4096, 128)])
+def test_fewrow_tensor_core_epilogues(kernels, oracle, m, k, n):
+    r = rng(18)
+    a = r.standard_normal((m, k)).astype(np.float32)
+    g = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    u = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    bias = r.standard_normal(n).astype(np.float32)
+    res = r.standard_normal((m, n)).astype(np.float32)
+    da, dg, du = kernels.upload(a), kernels.upload(g), kernels.upload(u)
+    assert rel(kernels.download(kernels.gated_matmul(da, dg, du)), oracle.gated_matmul(a, g, u)) <= TOL_MATMUL
+    got = kernels.download(kernels.matmul_bias(da, dg, kernels.upload(bias)))
+    assert rel(got, oracle.matmul(a, g, addend=bias, addend_mode=1)) <= TOL_MATMUL
+    got = kernels.download(kernels.matmul_residual(da, dg, kernels.upload(res)))
+    assert rel(got, oracle.matmul(a, g, addend=res, addend_mode=2)) <= TOL_MATMUL
+
+
+def test_fewrow_tensor_core_keeps_f32_activation_precision(kernels):
+    # src/tests_conformance.rs:807-846 at 16 rows: 1 + 2^-12 activations survive the tf32 split.
+    m, k, n = 16, 900, 132
+    a = np.full((m, k), 1.0 + 2.0 ** -12, np.float32)
+    w = np.abs(rng(21).standard_normal((k, n)).astype(np.float32))
+    w = (w.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    got = kernels.download(kernels.matmul(kernels.upload(a), kernels.upload(w))).astype(np.float64)
+    exp = a.astype(np.float64) @ w.astype(np.float64)
+    assert rel(got, exp) <= 1e-6
+
+
 @pytest.mark.parametrize("m,k,n", [(70, 900, 130), (200, 904, 136)])
 def test_matmul_keeps_f32_activation_precision(kernels, m, k, n):
     # src/tests_conformance.rs:807-846
