@@ -402,6 +402,9 @@ struct DecodeP {
     const uint64_t* step;
     int vec;  // K rows 16-byte aligned: float4 loads
     int* error;
+    // Arrival counters (one per KV head set, zero between launches): the last CTA of a set
+    // merges the set's span partials (the TMA form).
+    unsigned int* counters;
 };
 
 // Max (or sum) over the CTA's 128 threads of each of G values, one pair of barriers for all.
@@ -540,9 +543,8 @@ constexpr int kDecodeTileKeys = 32;  // 4 keys per warp
 constexpr int kDecodeStageBytes = kDecodeTileKeys * 2 * kDecodeMaxDim * 4;  // 64 KB at D = Dv = 256
 
 template <int G, int C>  // C: 128-column chunks of the output (Dv <= 128 * C)
-__global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(const __grid_constant__ CUtensorMap map_k,
-                                                                             const __grid_constant__ CUtensorMap map_v,
-                                                                             DecodeP p, uint64_t span) {
+__device__ __forceinline__ void decode_tma_span(const CUtensorMap& map_k, const CUtensorMap& map_v, const DecodeP& p,
+                                                uint64_t span) {
     using namespace sm100;
     constexpr int kc = kDecodeTileKeys;
     extern __shared__ uint8_t smem_raw[];
@@ -781,6 +783,101 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(co
     }
 }
 
+// The spans' partials of one query head merged (src/kernels.cu:2301-2800, attention_combine):
+// the common max over the spans, each span's weight exp(m - max) (kept in `wts` for up to
+// `cache` spans), the weighted sum of the span sums, and the output columns as the weighted
+// sums of the span outputs in span order, eight spans' loads in flight per step.  T threads;
+// `red` holds T / 32 floats.  Partials are read through the L2 (another CTA may have written
+// them in this launch).
+template <int T>
+__device__ void combine_head(const DecodeP& p, uint64_t h, float* wts, uint64_t cache, float* red) {
+    const uint64_t stride = p.value_dim + 2;
+    const float* base = p.partial + h * p.chunks * stride;
+    const float kNegInf = __int_as_float(0xff800000);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    auto block_max = [&](float v) {
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float r = red[0];
+        for (int w = 1; w < T / 32; w++) r = fmaxf(r, red[w]);
+        __syncthreads();
+        return r;
+    };
+    auto block_sum = [&](float v) {  // a fixed order: lanes by butterfly, then warps in order
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float r = red[0];
+        for (int w = 1; w < T / 32; w++) r += red[w];
+        __syncthreads();
+        return r;
+    };
+    float mx = kNegInf;
+    for (uint64_t c = threadIdx.x; c < p.chunks; c += T) mx = fmaxf(mx, __ldcg(base + c * stride));
+    mx = block_max(mx);
+    const bool cached = p.chunks <= cache;
+    float ls = 0.0f;
+    for (uint64_t c = threadIdx.x; c < p.chunks; c += T) {
+        const float mc = __ldcg(base + c * stride);
+        const float w = mc != kNegInf ? expf(mc - mx) : 0.0f;
+        if (cached) wts[c] = w;
+        ls += __ldcg(base + c * stride + 1) * w;
+    }
+    const float l = block_sum(ls);  // its barriers also publish wts
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    for (uint64_t d = threadIdx.x; d < p.value_dim; d += T) {
+        const float* col = base + 2 + d;
+        float o = 0.0f;
+        for (uint64_t c0 = 0; c0 < p.chunks; c0 += 8) {
+            float v[8], w[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const uint64_t c = c0 + u;
+                v[u] = c < p.chunks ? __ldcg(col + c * stride) : 0.0f;
+                if (cached) {
+                    w[u] = c < p.chunks ? wts[c] : 0.0f;
+                } else {
+                    const float mc = c < p.chunks ? __ldcg(base + c * stride) : kNegInf;
+                    w[u] = mc != kNegInf ? expf(mc - mx) : 0.0f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (c0 + u < p.chunks) o += v[u] * w[u];
+        }
+        p.out[h * p.value_dim + d] = o * inv;
+    }
+    __syncthreads();  // wts and red are reused by the next head
+}
+
+// One span of keys of one KV head set, then -- in the set's last CTA to finish (an arrival
+// ticket) -- the combine of the set's spans for its G query heads: one launch, no separate
+// combine kernel.  Every CTA arrives, also one with no admitted key or one whose waits ran out,
+// so the counter always completes and is reset by the last one.
+template <int G, int C>
+__global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(const __grid_constant__ CUtensorMap map_k,
+                                                                             const __grid_constant__ CUtensorMap map_v,
+                                                                             DecodeP p, uint64_t span) {
+    decode_tma_span<G, C>(map_k, map_v, p, span);
+    __shared__ unsigned int ticket;
+    __shared__ float red[kDecodeThreads / 32];
+    __syncthreads();  // every partial write of this CTA is issued
+    if (threadIdx.x == 0) {
+        __threadfence();
+        ticket = atomicAdd(p.counters + blockIdx.y, 1u);
+    }
+    __syncthreads();
+    if (ticket + 1 != (unsigned)p.chunks) return;
+    __threadfence();
+    extern __shared__ uint8_t smem_raw[];
+    float* wts = reinterpret_cast<float*>(smem_raw);  // the drained ring
+    const uint64_t cache = (uint64_t)kDecodeStages * kDecodeTileKeys * (p.head_dim + p.value_dim);
+    const uint64_t h0 = G == 1 ? blockIdx.y : (uint64_t)blockIdx.y * G;
+    for (int g = 0; g < G; g++) combine_head<kDecodeThreads>(p, h0 + g, wts, cache, red);
+    if (threadIdx.x == 0) p.counters[blockIdx.y] = 0;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 decode_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -866,64 +963,7 @@ __global__ void __launch_bounds__(kDecodeKeys) attention_combine_kernel(DecodeP 
     pdl_enter();
     __shared__ float wts[kCombineWeights];
     __shared__ float red[kDecodeKeys / 32];
-    const uint64_t h = blockIdx.x;
-    const uint64_t stride = p.value_dim + 2;
-    const float* base = p.partial + h * p.chunks * stride;
-    const float kNegInf = __int_as_float(0xff800000);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    auto block_max = [&](float v) {
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) red[warp] = v;
-        __syncthreads();
-        float r = red[0];
-        for (int w = 1; w < kDecodeKeys / 32; w++) r = fmaxf(r, red[w]);
-        __syncthreads();
-        return r;
-    };
-    auto block_sum = [&](float v) {  // a fixed order: lanes by butterfly, then warps in order
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) red[warp] = v;
-        __syncthreads();
-        float r = red[0];
-        for (int w = 1; w < kDecodeKeys / 32; w++) r += red[w];
-        __syncthreads();
-        return r;
-    };
-    float mx = kNegInf;
-    for (uint64_t c = threadIdx.x; c < p.chunks; c += kDecodeKeys) mx = fmaxf(mx, base[c * stride]);
-    mx = block_max(mx);
-    const bool cached = p.chunks <= (uint64_t)kCombineWeights;
-    float ls = 0.0f;
-    for (uint64_t c = threadIdx.x; c < p.chunks; c += kDecodeKeys) {
-        const float mc = base[c * stride];
-        const float w = mc != kNegInf ? expf(mc - mx) : 0.0f;
-        if (cached) wts[c] = w;
-        ls += base[c * stride + 1] * w;
-    }
-    const float l = block_sum(ls);  // its barriers also publish wts
-    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-    for (uint64_t d = threadIdx.x; d < p.value_dim; d += kDecodeKeys) {
-        const float* col = base + 2 + d;
-        float o = 0.0f;
-        for (uint64_t c0 = 0; c0 < p.chunks; c0 += 8) {
-            float v[8], w[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const uint64_t c = c0 + u;
-                v[u] = c < p.chunks ? col[c * stride] : 0.0f;
-                if (cached) {
-                    w[u] = c < p.chunks ? wts[c] : 0.0f;
-                } else {
-                    const float mc = c < p.chunks ? base[c * stride] : kNegInf;
-                    w[u] = mc != kNegInf ? expf(mc - mx) : 0.0f;
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-                if (c0 + u < p.chunks) o += v[u] * w[u];
-        }
-        p.out[h * p.value_dim + d] = o * inv;
-    }
+    combine_head<kDecodeKeys>(p, blockIdx.x, wts, kCombineWeights, red);
 }
 
 mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
@@ -946,6 +986,7 @@ mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
     p.step = a.step;
     p.vec = (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 && a.kv_model_dim % 4 == 0 && a.head_dim % 4 == 0;
     p.error = d->flags + 2;
+    p.counters = d->counters;
     const uint64_t keys = a.step ? a.kv_rows : a.kv_seq_len;  // the grid covers what may be admitted
     auto al16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
     const bool tma = al16(a.k) && al16(a.v) && a.head_dim % 4 == 0 && a.value_dim % 4 == 0 &&
@@ -995,9 +1036,7 @@ mg_status attention_decode(Device* d, const k::AttentionArgs& a) {
             case 8: ls = wide ? launch_decode_tma<8, 2>(d, p, maps, span, by_kv) : launch_decode_tma<8, 1>(d, p, maps, span, by_kv); break;
             default: ls = wide ? launch_decode_tma<1, 2>(d, p, maps, span, by_q) : launch_decode_tma<1, 1>(d, p, maps, span, by_q); break;
         }
-        MG_TRY(ls);
-        enqueue(d, attention_combine_kernel, dim3((unsigned)a.head_count), kDecodeKeys, 0, p);
-        return launched(d, "decode attention combine launch");
+        return ls;  // the last CTA of each KV head set combines its spans
     }
     switch (p.group) {
         case 2: enqueue(d, attention_decode_kernel<2>, by_kv, kDecodeKeys, 0, p); break;

@@ -732,19 +732,9 @@ mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
 // per CTA (the decoder layer's GEMMs) takes its own receive region and a shallower ring, so no
 // CTA waits for its peers before sending; with many k-blocks per CTA the ring depth matters more
 // and the partials are received in the drained ring.
-// k-blocks per CTA from which split k receives in the drained ring (MAGNETAR_CUDA_SPLIT_RING_KB,
-// default 8).
-int ring_recv_min_kb() {
-    static int v = [] {
-        const char* e = getenv("MAGNETAR_CUDA_SPLIT_RING_KB");
-        return e && atoi(e) > 0 ? atoi(e) : 8;
-    }();
-    return v;
-}
-
 template <int NB, bool A_RAW>
 mg_status launch_bn(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
-    const int mode = p.splits <= 1 ? kNoSplit : p.kb_per_split < ring_recv_min_kb() ? kSplitOwnRecv : kSplitRingRecv;
+    const int mode = p.splits <= 1 ? kNoSplit : p.kb_per_split < 8 ? kSplitOwnRecv : kSplitRingRecv;
     if constexpr (NB == 2) {
         if (bn == 128 && mode == kNoSplit) return launch_tc<128, NB, 2, A_RAW, kNoSplit>(d, p, maps);
         if (bn == 64) {

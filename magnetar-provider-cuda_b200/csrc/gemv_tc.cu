@@ -6,7 +6,7 @@
 // turned around so that the weight is the 128-row operand and the activation rows are the
 // MMA's N = 16: D[n][m] = sum_k B[k][n] * A[m][k].  B's row-major [k, n] tile is exactly the
 // MN-major operand layout (n contiguous), so a stage is four TMA boxes of [32 k x 32 n] with
-// 128-byte swizzling, used as they land -- no transpose.  Each operand enters as two tf32
+// 128-byte swizzling in 32-byte granules, used as they land -- no transpose.  Each operand enters as two tf32
 // terms (3xTF32, the f32 contract): eight converter warps split every raw tile into hi
 // (truncated to tf32) and lo = tf32(x - hi), and one thread issues lo*hi + hi*lo + hi*hi into
 // one TMEM accumulator.  The raw ring (what HBM streams into) and the converted buffers (what
@@ -18,11 +18,20 @@
 //
 // Per weight value the converters spend about four instructions (the FMA path: sixteen FMAs
 // at 16 rows), and the tensor pipe does the multiply, so the kernel streams B at HBM speed.
+//
+// Packed Q8_0 weights take the same kernel with a different producer and converter: a stage is
+// half of one tiled record (128 output columns x 128 k quants, each column's 128 bytes in eight
+// permuted 16-byte pieces, and their [128][4] scales), moved by two bulk copies; the converters
+// widen each quant exactly (byte permute into the mantissa of 2^23 and one subtraction), multiply
+// it by its block's scale (exact: 8 x 11 significant bits) and split the product into tf32 hi /
+// lo in the K-major swizzled layout, 32 k at a time -- so the product is the f32 matmul of the
+// dequantized weight, reading 1.125 bytes per weight value.
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "internal.h"
@@ -34,28 +43,44 @@ namespace {
 using namespace sm100;
 
 constexpr int kTcCols = 128;     // columns of B per CTA: the MMA's M
-constexpr int kTcK = 32;         // k rows per stage: one 128-byte swizzle row of A
+constexpr int kTcK = 32;         // k per conversion group: one 128-byte swizzle row
 constexpr int kTcRows = 16;      // the MMA's N: activation rows (zero past M)
-constexpr int kRawStages = 7;    // raw B + A tiles in flight from HBM
-constexpr int kConvStages = 2;   // converted (hi / lo) tiles the MMAs read
+constexpr int kConvStages = 2;   // converted (hi / lo) groups the MMAs read
 constexpr int kConvThreads = 256;
 constexpr int kMaxCluster = 16;  // non-portable cluster size (checked against the GPU at launch)
+constexpr int kQ8Chunk = 128;    // k per tiled Q8_0 record
 
+template <bool Q8>
 struct TcGemvShape {
-    static constexpr int kWRaw = kTcK * kTcCols * 4;   // 16 KB: four [32 k][32 n] swizzled boxes
-    static constexpr int kARaw = kTcRows * kTcK * 4;   // 2 KB: [16 m][32 k] swizzled
-    static constexpr int kRawStage = kWRaw + kARaw;    // 18 KB
-    static constexpr int kConvStage = 2 * kWRaw + 2 * kARaw;  // W hi, W lo, A hi, A lo
+    // f32: a raw stage is one group of k ([32 k][128 n] as four swizzled boxes, then A's [16][32]).
+    // Q8_0: a raw stage is four groups: the quants of 128 columns x 128 k (16 KB), their scales
+    // (2 KB), then A's [16][128] as four swizzled [16][32] boxes.
+    static constexpr int kGroups = Q8 ? kQ8Chunk / kTcK : 1;
+    static constexpr int kWRaw = Q8 ? kTcCols * kQ8Chunk : kTcK * kTcCols * 4;
+    static constexpr int kScales = Q8 ? kTcCols * 4 * 4 : 0;
+    static constexpr int kARaw = kTcRows * kTcK * 4 * kGroups;
+    static constexpr int kOffA = kWRaw + kScales;
+    static constexpr int kRawStage = kOffA + kARaw;
+    static constexpr int kRawStages = Q8 ? 5 : 7;  // raw bytes in flight from HBM
+    static constexpr int kWTile = kTcK * kTcCols * 4;     // one converted W term: 16 KB
+    static constexpr int kATile = kTcRows * kTcK * 4;     // one converted A term: 2 KB
+    static constexpr int kConvStage = 2 * kWTile + 2 * kATile;  // W hi, W lo, A hi, A lo
     static constexpr int kRing = kRawStages * kRawStage + kConvStages * kConvStage;
     static constexpr int kRecv = 32 * kTcCols * 4;     // the other CTAs' rows of this CTA's band
     static constexpr int kBars = 256;
     static constexpr int kSmem = kRing + kRecv + kBars + 1024;
     static constexpr int kThreads = 320;  // producer, MMA, 8 converter warps
-    static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+    static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0,
+                  "swizzle atoms stay 1024-byte aligned");
     static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
+    static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
 struct GemvTcArgs {
+    // Q8_0 B (tiled layout): quants / scales of B (and B2, gated), and k records per column tile
+    const int8_t* quants[2];
+    const float* scales[2];
+    uint64_t chunks;
     float* out;
     const float* addend;
     int addend_mode;  // 0 none, 1 row [n], 2 full [m, n]
@@ -67,15 +92,17 @@ struct GemvTcArgs {
     int* error;
 };
 
-// Shared-memory descriptor of an MN-major operand written by TMA with 128-byte swizzling: 32
-// consecutive tf32 of the M dimension per 128-byte row, eight k rows per 1024-byte atom (SBO
-// between atoms along k), the next 32 of M `lbo` bytes further.
-__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+// Shared-memory descriptor of an MN-major tf32 operand.  For 32-bit elements in MN-major order
+// the MMA takes one layout only: 128-byte rows (32 consecutive values of the M dimension, one row
+// per k) swizzled in 32-byte granules -- granule g of row r at position g ^ (r % 4), the pattern
+// of TMA's 128B_ATOM_32B mode -- four rows per 512-byte atom (SBO between atoms along k), the next
+// 32 of M `lbo` bytes further; layout type SWIZZLE_128B_BASE32B (1).
+__device__ __forceinline__ uint64_t desc_mn_sw128_32b(uint32_t saddr, uint32_t lbo) {
     uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
     d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)(512 >> 4) << 32;
     d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
+    d |= (uint64_t)1 << 61;
     return d;
 }
 
@@ -92,10 +119,25 @@ __device__ __forceinline__ void split_fast(float4 v, float4& hi, float4& lo) {
     lo = make_float4(tf32_rna(v.x - hi.x), tf32_rna(v.y - hi.y), tf32_rna(v.z - hi.z), tf32_rna(v.w - hi.w));
 }
 
-__global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
+// Four quants (one 32-bit word, little-endian) widened exactly to f32 and multiplied by the
+// block's scale: each biased byte becomes the low mantissa byte of 2^23 (byte permute), and
+// subtracting 2^23 + 128 leaves the signed value; q * scale is exact (8 x 11 significant bits).
+__device__ __forceinline__ float4 q8_widen4(uint32_t word, float scale) {
+    const uint32_t w = word ^ 0x80808080u;
+    const float bias = 8388736.0f;  // 2^23 + 128
+    return make_float4((__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540)) - bias) * scale,
+                       (__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541)) - bias) * scale,
+                       (__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542)) - bias) * scale,
+                       (__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543)) - bias) * scale);
+}
+
+template <bool Q8>
+__global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_b2, GemvTcArgs p) {
-    using S = TcGemvShape;
+    using S = TcGemvShape<Q8>;
+    constexpr int kRawStages = S::kRawStages;
+    constexpr int kG = S::kGroups;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -124,19 +166,36 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
     const CUtensorMap* map_w = term ? &map_b2 : &map_b;
     const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
     const uint64_t k1 = min(p.k, k0 + p.slice_len);
-    const int num_kb = k1 > k0 ? (int)((k1 - k0 + kTcK - 1) / kTcK) : 0;
+    constexpr int kStageK = kTcK * kG;  // k per raw stage
+    const int num_kb = k1 > k0 ? (int)((k1 - k0 + kStageK - 1) / kStageK) : 0;  // raw stages
+    const int num_groups = num_kb * kG;
 
+    // The producer's loads of raw stage i: B (the weight's tiles, or the Q8_0 record's half with
+    // its scales) arms the stage's barrier for all its bytes; A follows.
     auto issue_w = [&](int i) {
         const int s = i % kRawStages;
         const uint32_t st = raw_stage(s);
         mbar_arrive_expect_tx(raw_full(s), (uint32_t)S::kRawStage);
-        const int ky = (int)(k0 + (uint64_t)i * kTcK);
+        if constexpr (Q8) {
+            // record (column tile of 256, k chunk): this CTA's 128 columns are its first or second half
+            const uint64_t rec = (n0 >> 8) * p.chunks + (k0 / kQ8Chunk + (uint64_t)i);
+            const uint64_t row0 = rec * 256 + (n0 & 255);
+            const int8_t* quants = term ? p.quants[1] : p.quants[0];
+            const float* scales = term ? p.scales[1] : p.scales[0];
+            bulk_load(st, quants + row0 * kQ8Chunk, (uint32_t)S::kWRaw, raw_full(s));
+            bulk_load(st + S::kWRaw, scales + row0 * 4, (uint32_t)S::kScales, raw_full(s));
+        } else {
+            const int ky = (int)(k0 + (uint64_t)i * kTcK);
 #pragma unroll
-        for (int j = 0; j < 4; j++) tma_load_2d(st + (uint32_t)(j * 4096), map_w, raw_full(s), (int)n0 + 32 * j, ky);
+            for (int j = 0; j < 4; j++) tma_load_2d(st + (uint32_t)(j * 4096), map_w, raw_full(s), (int)n0 + 32 * j, ky);
+        }
     };
     auto issue_a = [&](int i) {
         const int s = i % kRawStages;
-        tma_load_2d(raw_stage(s) + S::kWRaw, &map_a, raw_full(s), (int)(k0 + (uint64_t)i * kTcK), 0);
+#pragma unroll
+        for (int j = 0; j < kG; j++)
+            tma_load_2d(raw_stage(s) + S::kOffA + (uint32_t)(j * S::kATile), &map_a, raw_full(s),
+                        (int)(k0 + (uint64_t)i * kStageK + (uint64_t)j * kTcK), 0);
     };
 
     if (threadIdx.x == 0) {
@@ -193,9 +252,10 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
     } else if (warp == 1) {
         // ---- MMA issuer: D[128 n][16 m] += W_lo A_hi + W_hi A_lo + W_hi A_hi --------------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(kTcCols, kTcRows) | (1u << 15);  // A (the weight) MN-major
+            // A (the weight) MN-major as it lies (f32), K-major as the converters write it (Q8_0)
+            constexpr uint32_t idesc = idesc_tf32(kTcCols, kTcRows) | (Q8 ? 0u : (1u << 15));
             bool ok = true;
-            for (int i = 0; i < num_kb; i++) {
+            for (int i = 0; i < num_groups; i++) {
                 const int c = i % kConvStages;
                 if (!mbar_wait(conv_full(c), (uint32_t)(i / kConvStages) & 1u) || *abort_flag) {
                     *abort_flag = 1;
@@ -205,11 +265,17 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t cs = conv_stage(c);
-                const uint32_t whi = cs, wlo = cs + S::kWRaw, ahi = cs + 2 * S::kWRaw, alo = ahi + S::kARaw;
+                const uint32_t whi = cs, wlo = cs + S::kWTile, ahi = cs + 2 * S::kWTile, alo = ahi + S::kATile;
 #pragma unroll
                 for (int kk = 0; kk < kTcK / 8; kk++) {
-                    const uint64_t dwhi = desc_mn_sw128(whi + (uint32_t)(kk * 1024), 4096);
-                    const uint64_t dwlo = desc_mn_sw128(wlo + (uint32_t)(kk * 1024), 4096);
+                    uint64_t dwhi, dwlo;
+                    if constexpr (Q8) {
+                        dwhi = desc_k_sw128(whi) + (uint64_t)((kk * 32) >> 4);
+                        dwlo = desc_k_sw128(wlo) + (uint64_t)((kk * 32) >> 4);
+                    } else {
+                        dwhi = desc_mn_sw128_32b(whi + (uint32_t)(kk * 1024), 4096);
+                        dwlo = desc_mn_sw128_32b(wlo + (uint32_t)(kk * 1024), 4096);
+                    }
                     const uint64_t dahi = desc_k_sw128(ahi) + (uint64_t)((kk * 32) >> 4);
                     const uint64_t dalo = desc_k_sw128(alo) + (uint64_t)((kk * 32) >> 4);
                     mma_tf32(tmem, dwlo, dahi, idesc, (i > 0 || kk > 0) ? 1u : 0u);
@@ -218,39 +284,62 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
                 }
                 tc_commit(conv_empty(c));  // frees the conversion buffer once these MMAs have read it
             }
-            if (ok && num_kb > 0) tc_commit(accum_bar);
+            if (ok && num_groups > 0) tc_commit(accum_bar);
             else mbar_arrive(accum_bar);  // release the epilogue
         }
         __syncwarp();
     } else {
-        // ---- warps 2..9: split each raw stage into hi / lo terms in a conversion buffer --------
+        // ---- warps 2..9: split each raw group into hi / lo terms in a conversion buffer --------
         const int t = threadIdx.x - 64;
         for (int i = 0; i < num_kb; i++) {
-            const int s = i % kRawStages, c = i % kConvStages;
+            const int s = i % kRawStages;
             bool ok = mbar_wait(raw_full(s), (uint32_t)(i / kRawStages) & 1u);
-            ok = mbar_wait(conv_empty(c), ((uint32_t)(i / kConvStages) & 1u) ^ 1u) && ok;
-            if (!ok) {
-                *abort_flag = 1;
-                atomicExch(p.error, 1);  // still arrive below so that no one waits for this thread
-            }
-            const uint32_t rs = raw_stage(s), cs = conv_stage(c);
+            const uint32_t rs = raw_stage(s);
+            for (int g = 0; g < kG; g++) {
+                const int gi = i * kG + g, c = gi % kConvStages;
+                ok = mbar_wait(conv_empty(c), ((uint32_t)(gi / kConvStages) & 1u) ^ 1u) && ok;
+                if (!ok) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);  // still arrive below so that no one waits for this thread
+                }
+                const uint32_t cs = conv_stage(c);
+                if constexpr (Q8) {
+                    // column n = t % 128 of the record half, 16 of the group's 32 k (piece 2g + t / 128)
+                    const int n = t & 127, half = t >> 7;
+                    const uint32_t piece = (uint32_t)((2 * g + half) ^ (n & 7));
+                    const uint4 q = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
+                    const float sc = *reinterpret_cast<const float*>(base_ptr + (rs - base) + S::kWRaw + (uint32_t)(n * 4 + g) * 4);
+                    auto put = [&](uint32_t word, int j) {
+                        float4 h, l;
+                        split_fast(q8_widen4(word, sc), h, l);
+                        const uint32_t off = (uint32_t)(n * 128 + (((4 * half + j) ^ (n & 7)) * 16));
+                        sts4(cs + off, h.x, h.y, h.z, h.w);
+                        sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
+                    };
+                    put(q.x, 0);
+                    put(q.y, 1);
+                    put(q.z, 2);
+                    put(q.w, 3);
+                } else {
 #pragma unroll
-            for (int j = 0; j < S::kWRaw / 16 / kConvThreads; j++) {
-                const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
-                float4 h, l;
-                split_fast(lds4(rs + off), h, l);
-                sts4(cs + off, h.x, h.y, h.z, h.w);
-                sts4(cs + S::kWRaw + off, l.x, l.y, l.z, l.w);
+                    for (int j = 0; j < S::kWRaw / 16 / kConvThreads; j++) {
+                        const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
+                        float4 h, l;
+                        split_fast(lds4(rs + off), h, l);
+                        sts4(cs + off, h.x, h.y, h.z, h.w);
+                        sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
+                    }
+                }
+                if (t < S::kATile / 16) {
+                    const uint32_t off = (uint32_t)t * 16;
+                    float4 h, l;
+                    split_fast(lds4(rs + S::kOffA + (uint32_t)(g * S::kATile) + off), h, l);
+                    sts4(cs + 2 * S::kWTile + off, h.x, h.y, h.z, h.w);
+                    sts4(cs + 2 * S::kWTile + S::kATile + off, l.x, l.y, l.z, l.w);
+                }
+                fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
+                mbar_arrive(conv_full(c));
             }
-            if (t < S::kARaw / 16) {
-                const uint32_t off = (uint32_t)t * 16;
-                float4 h, l;
-                split_fast(lds4(rs + S::kWRaw + off), h, l);
-                sts4(cs + 2 * S::kWRaw + off, h.x, h.y, h.z, h.w);
-                sts4(cs + 2 * S::kWRaw + S::kARaw + off, l.x, l.y, l.z, l.w);
-            }
-            fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
-            mbar_arrive(conv_full(c));
             mbar_arrive(raw_empty(s));
             if (*abort_flag) break;
         }
@@ -260,7 +349,7 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
         const bool waited = mbar_wait(accum_bar, 0);
         if (!waited) atomicExch(p.error, 1);
         // tcgen05.ld is warp-collective: the whole warp reads the accumulator or none of it.
-        acc_ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_kb > 0);
+        acc_ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_groups > 0);
     }
     // ---- stage this CTA's partial as [16 m][128 n] in the drained first conversion buffer ------
     float* staged = reinterpret_cast<float*>(base_ptr + (conv_stage(0) - base));
@@ -339,8 +428,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tc_gemv_encode_fn() {
     return fn;
 }
 
-// Row-major f32 [rows, cols], box [box_rows x 32 columns], 128-byte swizzle, zero past the edges.
-mg_status tc_gemv_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// Row-major f32 [rows, cols], box [box_rows x 32 columns], zero past the edges; 128-byte swizzle
+// (a K-major operand: 16-byte granules) or, `mn`, 128-byte swizzle in 32-byte granules (an
+// MN-major tf32 operand).
+mg_status tc_gemv_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                      bool mn = false) {
     auto fn = tc_gemv_encode_fn();
     if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
     cuuint64_t dims[2] = {cols, rows};
@@ -348,46 +440,48 @@ mg_status tc_gemv_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_
     cuuint32_t box[2] = {32, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
     return MG_OK;
 }
 
-// The fewest rows that take this path (MAGNETAR_CUDA_FEWROW_TC: a row count, or 0 to leave the
-// few-row matmul on the CUDA cores).
+// The fewest rows that take the f32 path (MAGNETAR_CUDA_FEWROW_TC: a row count, or 0 to leave
+// the few-row matmul on the CUDA cores), and the packed Q8_0 path (MAGNETAR_CUDA_FEWROW_TC_Q8).
+int env_min_rows(const char* name, int dflt) {
+    const char* e = getenv(name);
+    if (!e || !*e) return dflt;
+    const int x = atoi(e);
+    return x <= 0 ? kTcRows + 1 : x;
+}
+// Defaults from measurement at N = K = 4096: packed Q8_0 at 16 rows takes 29 us here against 61 us
+// on the CUDA cores, one row 28 us against 8 us; f32 at 16 rows 26 us against 21 us -- the f32 form
+// stays off until its per-group pipeline is shorter.
 int tc_min_rows() {
-    static int v = [] {
-        const char* e = getenv("MAGNETAR_CUDA_FEWROW_TC");
-        if (!e || !*e) return 8;
-        const int x = atoi(e);
-        return x <= 0 ? kTcRows + 1 : x;
-    }();
+    static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC", kTcRows + 1);
+    return v;
+}
+int tc_q8_min_rows() {
+    static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC_Q8", 8);
     return v;
 }
 
-}  // namespace
-
-namespace k {
-
-bool gemv_tc_eligible(const GemmArgs& g) {
-    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-    return g.m >= (uint64_t)tc_min_rows() && g.m <= (uint64_t)kTcRows && !g.transpose_a && !g.transpose_b &&
-           g.k % 4 == 0 && g.n % 4 == 0 && al(g.a) && al(g.b) && (!g.b2 || al(g.b2)) && !g.b16[0] && !g.packed[0] &&
-           g.k < (1ull << 31) && g.n < (1ull << 31);
-}
-
-mg_status gemv_tc(Device* d, const GemmArgs& g) {
-    using S = TcGemvShape;
+template <bool Q8>
+mg_status launch_gemv_tc(Device* d, const k::GemmArgs& g) {
+    using S = TcGemvShape<Q8>;
+    auto kernel = gemv_tc_kernel<Q8>;
     const uint64_t col_tiles = (g.n + kTcCols - 1) / kTcCols;
     if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
     const int terms = g.gated ? 2 : 1;
-    const uint64_t kb = (g.k + kTcK - 1) / kTcK;
+    constexpr uint64_t kStageK = (uint64_t)kTcK * S::kGroups;
+    const uint64_t kb = (g.k + kStageK - 1) / kStageK;
     uint64_t splits = (uint64_t)d->sm_count / (col_tiles * terms);
     if (splits > (uint64_t)(kMaxCluster / terms)) splits = kMaxCluster / terms;
     if (splits > kb) splits = kb;
     if (splits < 1) splits = 1;
     GemvTcArgs p;
+    memset(&p, 0, sizeof p);
     p.out = g.out;
     p.addend = g.addend;
     p.addend_mode = g.addend_mode;
@@ -395,24 +489,34 @@ mg_status gemv_tc(Device* d, const GemmArgs& g) {
     p.n = g.n;
     p.k = g.k;
     p.terms = terms;
-    p.b_early = g.b_stable ? 1 : 0;
+    // A packed weight changes only by an upload, which synchronises: its loads may always start
+    // before the dependency wait.
+    p.b_early = Q8 || g.b_stable ? 1 : 0;
     p.error = d->flags + 2;
+    if constexpr (Q8) {
+        for (int t = 0; t < 2; t++) {
+            const Buffer* w = g.packed[t < terms ? t : 0];
+            p.quants[t] = static_cast<const int8_t*>(w->ptr);
+            p.scales[t] = w->q8_scales;
+        }
+        p.chunks = g.k / kQ8Chunk;
+    }
     auto set_splits = [&](uint64_t sp) {
-        p.slice_len = ((kb + sp - 1) / sp) * kTcK;
+        p.slice_len = ((kb + sp - 1) / sp) * kStageK;
         p.splits = (int)((g.k + p.slice_len - 1) / p.slice_len);
         if (p.splits < 1) p.splits = 1;
     };
     set_splits(splits);
     static bool configured[64] = {false};
     if (!configured[d->ordinal & 63]) {
-        MG_CUDA(cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+        MG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
                 "configuring the tensor-core gemv kernel");
-        MG_CUDA(cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+        MG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
                 "allowing the tensor-core gemv kernel clusters of up to 16");
         configured[d->ordinal & 63] = true;
     }
-    // Clusters larger than 8 only where the GPU holds them all at once (queried once per size);
-    // otherwise fewer k splits.
+    // Clusters larger than 8 only where the GPU holds them (queried once per size); otherwise
+    // fewer k splits.
     static int fits[kMaxCluster + 1] = {0};  // 1 fits, -1 does not
     while (p.splits * p.terms > 8) {
         const int nc = p.splits * p.terms;
@@ -429,7 +533,7 @@ mg_status gemv_tc(Device* d, const GemmArgs& g) {
             q.attrs = &ca;
             q.numAttrs = 1;
             int clusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_tc_kernel, &q) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &q) != cudaSuccess) {
                 (void)cudaGetLastError();
                 clusters = 0;
             }
@@ -440,9 +544,13 @@ mg_status gemv_tc(Device* d, const GemmArgs& g) {
     }
     CUtensorMap maps[3];
     MG_TRY(tc_gemv_map(&maps[0], g.a, g.m, g.k, kTcRows));
-    MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, kTcK));
-    if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, kTcK));
-    else maps[2] = maps[1];
+    if constexpr (Q8) {
+        maps[1] = maps[2] = maps[0];  // B arrives by bulk copies
+    } else {
+        MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, kTcK, true));
+        if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, kTcK, true));
+        else maps[2] = maps[1];
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
     cfg.blockDim = dim3(S::kThreads, 1, 1);
@@ -457,9 +565,37 @@ mg_status gemv_tc(Device* d, const GemmArgs& g) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = d->pdl ? 2 : 1;
-    MG_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel, maps[0], maps[1], maps[2], p), "tensor-core gemv launch");
+    MG_CUDA(cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], p), "tensor-core gemv launch");
     return launched(d, "tensor-core gemv launch");
 }
+
+}  // namespace
+
+namespace k {
+
+bool gemv_tc_eligible(const GemmArgs& g) {
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    return g.m >= (uint64_t)tc_min_rows() && g.m <= (uint64_t)kTcRows && !g.transpose_a && !g.transpose_b &&
+           g.k % 4 == 0 && g.n % 4 == 0 && al(g.a) && al(g.b) && (!g.b2 || al(g.b2)) && !g.packed[0] &&
+           !g.packed[1] && g.k < (1ull << 31) && g.n < (1ull << 31);
+}
+// (A compact weight takes this path too, reading its f32 values: its results stay bit-identical to
+// the same values stored as f32, which take it as well.)
+
+mg_status gemv_tc(Device* d, const GemmArgs& g) { return launch_gemv_tc<false>(d, g); }
+
+// Every B a tiled packed Q8_0 weight (transposed storage, k a multiple of 128), A K-major with
+// 16-byte rows.
+bool gemv_tc_q8_eligible(const GemmArgs& g) {
+    const int terms = g.gated ? 2 : 1;
+    for (int t = 0; t < terms; t++)
+        if (!g.packed[t] || !g.packed[t]->q8_tiled) return false;
+    return g.m >= (uint64_t)tc_q8_min_rows() && g.m <= (uint64_t)kTcRows && !g.transpose_a && !g.transpose_b &&
+           g.k % kQ8Chunk == 0 && g.k % 4 == 0 && (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 && g.k < (1ull << 31) &&
+           g.n < (1ull << 31);
+}
+
+mg_status gemv_tc_q8(Device* d, const GemmArgs& g) { return launch_gemv_tc<true>(d, g); }
 
 }  // namespace k
 }  // namespace mg

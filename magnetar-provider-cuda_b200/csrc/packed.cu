@@ -570,7 +570,13 @@ mg_status q8_gemv(Device* d, const GemmArgs& g) {
 
 // A matmul with packed B (src/kernels.rs:5581-5600): the few-row kernel when eligible, else each
 // packed weight dequantized (stored order) for the duration of the call and the f32 matmul.
+bool gemv_tc_q8_eligible(const GemmArgs& g);
+mg_status gemv_tc_q8(Device* d, const GemmArgs& g);
+
 mg_status q8_matmul(Device* d, const GemmArgs& g) {
+    // The tensor-core form (gemv_tc.cu) widens, scales and splits the quants for the MMAs; the
+    // CUDA-core kernel below remains for what it does not take.
+    if (gemv_tc_q8_eligible(g)) return gemv_tc_q8(d, g);
     if (q8_gemv_eligible(g)) return q8_gemv(d, g);
     // Few rows: the logical [k, n] matrix, which the f32 few-row matmul reads as it lies (it takes
     // no transposed B); more rows: the stored matrix (a plain row-major pass) with the transpose

@@ -824,6 +824,23 @@ def test_q8_packed_gated_matmul_and_embedding_match_reference_cpu(kernels, oracl
                                   oracle.embedding(oracle.q8_0_dequantize(table, 6, 64, transposed=False), ids)[0])
 
 
+@pytest.mark.parametrize("m", [1, 2, 7, 16])
+def test_q8_packed_matmul_at_4096(kernels, oracle, m):
+    # the bench's packed lines: B [4096, 4096] stored transposed (tiled records), few rows through
+    # the tensor-core form (quants widened, scaled and split in shared memory)
+    r = np.random.default_rng(90 + m)
+    n = k = 4096
+    nb = n * k // 32
+    blk = np.empty((nb, 34), np.uint8)
+    blk[:, :2] = r.uniform(2.0 ** -9, 2.0 ** -5, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    blk[:, 2:] = r.integers(-127, 128, (nb, 32), dtype=np.int8).view(np.uint8)
+    w = kernels.upload_q8_0(blk.ravel(), n, k, transposed=True)
+    dense = oracle.q8_0_dequantize(blk.ravel(), n, k, transposed=True)
+    a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
+    got = kernels.download(kernels.matmul(kernels.upload(a), w))
+    assert rel(got, oracle.matmul(a, dense)) <= TOL_MATMUL
+
+
 def test_q8_packed_weights_at_real_checkpoint_sizes(kernels):
     # src/tests_conformance.rs:4128-4205: a [151936, 896] table and the same blocks as an lm head
     from q8_cases import activations, checkpoint_blocks
