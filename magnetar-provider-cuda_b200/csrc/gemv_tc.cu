@@ -45,7 +45,8 @@ using namespace sm100;
 constexpr int kTcCols = 128;     // columns of B per CTA: the MMA's M
 constexpr int kTcK = 32;         // k per conversion group: one 128-byte swizzle row
 constexpr int kTcRows = 16;      // the MMA's N: activation rows (zero past M)
-constexpr int kConvStages = 2;   // converted (hi / lo) groups the MMAs read
+constexpr int kConvStages = 3;   // converted (hi / lo) groups the MMAs read
+constexpr int kAccs = 4;         // TMEM accumulators: k-step s of a group adds into accumulator s
 constexpr int kConvThreads = 256;
 constexpr int kMaxCluster = 16;  // non-portable cluster size (checked against the GPU at launch)
 constexpr int kQ8Chunk = 128;    // k per tiled Q8_0 record
@@ -61,7 +62,7 @@ struct TcGemvShape {
     static constexpr int kARaw = kTcRows * kTcK * 4 * kGroups;
     static constexpr int kOffA = kWRaw + kScales;
     static constexpr int kRawStage = kOffA + kARaw;
-    static constexpr int kRawStages = Q8 ? 5 : 7;  // raw bytes in flight from HBM
+    static constexpr int kRawStages = Q8 ? 3 : 5;  // raw bytes in flight from HBM
     static constexpr int kWTile = kTcK * kTcCols * 4;     // one converted W term: 16 KB
     static constexpr int kATile = kTcRows * kTcK * 4;     // one converted A term: 2 KB
     static constexpr int kConvStage = 2 * kWTile + 2 * kATile;  // W hi, W lo, A hi, A lo
@@ -73,6 +74,7 @@ struct TcGemvShape {
     static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0,
                   "swizzle atoms stay 1024-byte aligned");
     static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
+    static_assert(kTcK / 8 == kAccs, "one accumulator per k-step of a group");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
             for (int i = 0; i < min(kRawStages, num_kb); i++) issue_w(i);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32((const void*)tmem_slot), 32);
+        tmem_alloc(smem_u32((const void*)tmem_slot), kAccs * kTcRows);
         tmem_relinquish();
     }
     cluster_arrive();  // phase 1: every receive barrier of the cluster is armed
@@ -278,9 +280,11 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
                     }
                     const uint64_t dahi = desc_k_sw128(ahi) + (uint64_t)((kk * 32) >> 4);
                     const uint64_t dalo = desc_k_sw128(alo) + (uint64_t)((kk * 32) >> 4);
-                    mma_tf32(tmem, dwlo, dahi, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                    mma_tf32(tmem, dwhi, dalo, idesc, 1u);
-                    mma_tf32(tmem, dwhi, dahi, idesc, 1u);
+                    // four accumulators, one per k-step: four independent chains of MMAs
+                    const uint32_t acc = tmem + (uint32_t)(kk * kTcRows);
+                    mma_tf32(acc, dwlo, dahi, idesc, i > 0 ? 1u : 0u);
+                    mma_tf32(acc, dwhi, dalo, idesc, 1u);
+                    mma_tf32(acc, dwhi, dahi, idesc, 1u);
                 }
                 tc_commit(conv_empty(c));  // frees the conversion buffer once these MMAs have read it
             }
@@ -321,11 +325,16 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
                     put(q.z, 2);
                     put(q.w, 3);
                 } else {
+                    // all of this thread's loads first, so that their latencies overlap
+                    constexpr int J = S::kWRaw / 16 / kConvThreads;
+                    float4 x[J];
 #pragma unroll
-                    for (int j = 0; j < S::kWRaw / 16 / kConvThreads; j++) {
+                    for (int j = 0; j < J; j++) x[j] = lds4(rs + (uint32_t)(t + j * kConvThreads) * 16);
+#pragma unroll
+                    for (int j = 0; j < J; j++) {
                         const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
                         float4 h, l;
-                        split_fast(lds4(rs + off), h, l);
+                        split_fast(x[j], h, l);
                         sts4(cs + off, h.x, h.y, h.z, h.w);
                         sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
                     }
@@ -359,8 +368,17 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
         const int n = q * 32 + lane;
         float v[16];
         if (acc_ready) {
+            // the accumulators added in order (deterministic)
             tmem_ld16(tmem + ((uint32_t)(q * 32) << 16), v);
             tc_wait_ld();
+#pragma unroll
+            for (int a = 1; a < kAccs; a++) {
+                float w[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kTcRows), w);
+                tc_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] += w[j];
+            }
         } else {
 #pragma unroll
             for (int j = 0; j < 16; j++) v[j] = 0.0f;
@@ -373,7 +391,7 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 32);
+        tmem_dealloc(tmem, kAccs * kTcRows);
     }
     // ---- exchange: each band of rows to the CTA that owns it ------------------------------------
     cluster_wait();  // phase 1
