@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         mbar_init(k_empty(1), 1);
         mbar_init(v_full, 1);
         mbar_init(v_empty, 1);
-        mbar_init(p_full, 256);
+        mbar_init(p_full, 8);  // the softmax warps
         mbar_init(pv_full, 1);
         mbar_init(s_full0, 1);
         mbar_init(s_full0 + 8, 1);
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
             }
             fence_proxy_async();  // the P writes are read by tcgen05.mma
             tc_fence_before();    // ... and the P.V read above precedes the next P.V's write
-            mbar_arrive(p_full);
+            mbar_arrive_warp(p_full);
             keep_prev = keep;
             m = m_new;
             l = l_new;

@@ -48,7 +48,7 @@ using namespace sm100;
 constexpr int BM = 128;
 constexpr int BK = 32;       // f32 k-columns per stage: one 128-byte swizzle row
 constexpr int kGroupM = 16;  // rasterisation: M-tiles walked together for L2 reuse
-constexpr int kMaxSplits = 8;  // k splits of one tile: the CTAs of one portable cluster
+constexpr int kMaxSplits = 16;  // k splits of one tile: the CTAs of one (non-portable) cluster
 constexpr int kConvThreads = 256;  // warps 2-9 split raw operand tiles during the main loop
 
 // ---- operand split ----------------------------------------------------------------------------
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
-            mbar_init(conv_bar(s), kConvThreads);
+            mbar_init(conv_bar(s), kConvThreads / 32);
         }
         mbar_init(accum_bar, 1);
         if (SPLIT) mbar_init(recv_bar, 1);
@@ -341,6 +341,16 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
     // CTA's receive barrier is initialised and armed before any CTA sends to it.
     if (SPLIT == kSplitOwnRecv) cluster_arrive();
     pdl_enter();
+    // A residual addend is written by an earlier kernel: bring this CTA's band of it into the L2
+    // now, so that the epilogue's loads of it do not wait on HBM.
+    if (warp == 2 && p.addend_mode == 2) {
+        constexpr int kLines = (BN * 4 + 127) / 128;  // 128-byte lines per band row
+        for (int e = lane; e < (r_end - r_begin) * kLines; e += 32) {
+            const uint64_t row = (uint64_t)m0 + r_begin + e / kLines, col = (uint64_t)n0 + (e % kLines) * 32;
+            if (row < p.m && col < p.n)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(p.addend + row * p.n + col) : "memory");
+        }
+    }
     if (threadIdx.x == 0) {
         // The first stages are free: start their loads before the set-up barrier so that the
         // memory latency overlaps the rest of the set-up.
@@ -459,8 +469,8 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                     }
                 }
                 fence_proxy_async();  // make the generic-proxy writes visible to tcgen05.mma
-                mbar_arrive(conv_bar(s));
-                if (*abort_flag) break;
+                mbar_arrive_warp(conv_bar(s));
+                if (__any_sync(0xffffffffu, *abort_flag)) break;
             }
         }
     }
@@ -547,23 +557,24 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
             float4 add4 = make_float4(0.f, 0.f, 0.f, 0.f);
             if (full4 && p.addend_mode == 1) add4 = *reinterpret_cast<const float4*>(p.addend + col);
             else if (full4 && p.addend_mode == 2) add4 = *reinterpret_cast<const float4*>(p.addend + row * p.n + col);
-            float4 t[NB][kMaxSplits];
-#pragma unroll
-            for (int z = 0; z < NB; z++)
-#pragma unroll
-                for (int s = 0; s < kMaxSplits; s++)
-                    if (s < splits) t[z][s] = lds4(part_at(z, s, lr, c4));
+            // the splits' partials in split order (deterministic), four loads in flight
             float4 acc[NB];
 #pragma unroll
             for (int z = 0; z < NB; z++) {
-                acc[z] = t[z][0];
+                acc[z] = lds4(part_at(z, 0, lr, c4));
+                for (int s0 = 1; s0 < splits; s0 += 4) {
+                    float4 t[4];
 #pragma unroll
-                for (int s = 1; s < kMaxSplits; s++) {
-                    if (s < splits) {
-                        acc[z].x += t[z][s].x;
-                        acc[z].y += t[z][s].y;
-                        acc[z].z += t[z][s].z;
-                        acc[z].w += t[z][s].w;
+                    for (int u = 0; u < 4; u++)
+                        if (s0 + u < splits) t[u] = lds4(part_at(z, s0 + u, lr, c4));
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        if (s0 + u < splits) {
+                            acc[z].x += t[u].x;
+                            acc[z].y += t[u].y;
+                            acc[z].z += t[u].z;
+                            acc[z].w += t[u].w;
+                        }
                     }
                 }
             }
@@ -683,6 +694,9 @@ mg_status launch_tc(Device* d, TcParams p, const CUtensorMap* maps) {
     if (!configured[d->ordinal & 63]) {
         MG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
                 "configuring the tensor-core matmul");
+        if (SPLIT)
+            MG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                    "allowing the tensor-core matmul clusters of up to 16");
         configured[d->ordinal & 63] = true;
     }
     const uint64_t tiles = (uint64_t)p.tiles_m * p.tiles_n * p.groups;
@@ -778,6 +792,17 @@ mg_status launch_bn_raw_b(Device* d, int bn, const TcParams& p, const CUtensorMa
                      : launch_tc<64, 1, 3, A_RAW, kNoSplit, true>(d, p, maps);
     return split ? launch_tc<32, 1, 4, A_RAW, kSplitRingRecv, true>(d, p, maps)
                  : launch_tc<32, 1, 4, A_RAW, kNoSplit, true>(d, p, maps);
+}
+
+// k splits per tile at most (MAGNETAR_CUDA_GEMM_MAX_SPLITS, 2..16): the CTAs of one cluster,
+// portable up to 8.
+int max_splits() {
+    static int v = [] {
+        const char* e = getenv("MAGNETAR_CUDA_GEMM_MAX_SPLITS");
+        const int x = e ? atoi(e) : 8;
+        return x < 2 ? 2 : x > kMaxSplits ? kMaxSplits : x;
+    }();
+    return v;
 }
 
 bool tensor_cores_enabled() {
@@ -893,7 +918,7 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
         if (tiles * 2 <= (uint64_t)d->sm_count && num_kb >= 4) {
             splits = (int)((uint64_t)d->sm_count / tiles);
             if (splits > num_kb / 2) splits = num_kb / 2;
-            if (splits > kMaxSplits) splits = kMaxSplits;  // a portable cluster holds 8 CTAs
+            if (splits > max_splits()) splits = max_splits();
             if (splits < 1) splits = 1;
         }
         p.kb_per_split = (num_kb + splits - 1) / splits;

@@ -29,6 +29,7 @@
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 
 #include <cstdlib>
 #include <cstring>
@@ -203,10 +204,10 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRawStages; s++) {
             mbar_init(raw_full(s), 1);
-            mbar_init(raw_empty(s), kConvThreads);
+            mbar_init(raw_empty(s), kConvThreads / 32);
         }
         for (int c = 0; c < kConvStages; c++) {
-            mbar_init(conv_full(c), kConvThreads);
+            mbar_init(conv_full(c), kConvThreads / 32);
             mbar_init(conv_empty(c), 1);
         }
         mbar_init(accum_bar, 1);
@@ -347,10 +348,10 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
                     sts4(cs + 2 * S::kWTile + S::kATile + off, l.x, l.y, l.z, l.w);
                 }
                 fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
-                mbar_arrive(conv_full(c));
+                mbar_arrive_warp(conv_full(c));
             }
-            mbar_arrive(raw_empty(s));
-            if (*abort_flag) break;
+            mbar_arrive_warp(raw_empty(s));
+            if (__any_sync(0xffffffffu, *abort_flag)) break;
         }
     }
     bool acc_ready = false;
@@ -433,6 +434,370 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
     cluster_wait();  // phase 2: every copy out of this CTA's shared memory has landed
 }
 
+// ---- packed Q8_0 with bf16 operands -------------------------------------------------------------
+// Every int8 quant is exactly a bfloat16 value, so the weight enters the MMA as it is stored -- one
+// bf16 term, no split -- and only the activations are split, into three bf16 terms h + m + l
+// (h the value truncated to bf16, m = bf16(x - h), l = bf16(x - h - m): within 2^-24 of x).  The
+// three terms are stacked as the MMA's N = 48 (rows 0-15, 16-31, 32-47), so one kind::f16 MMA per
+// 16 k reads the weight tile once for all of them.  A Q8_0 block's scale multiplies its 32 k only,
+// so each block accumulates into its own TMEM slot (48 columns, eight slots in rotation); four
+// scaler warps read a finished slot, add its three terms, and fold it into their registers as
+// sum += scale * block_sum -- the reference's per-block sum times the block's scale
+// (src/kernels.cu:283-348).  A group is 64 k (two blocks): a raw stage (half a tiled record) is two
+// groups.
+constexpr int kQbGroupK = 64;
+constexpr int kQbSlots = 8;          // TMEM block slots of 48 columns
+constexpr int kQbN = 3 * kTcRows;    // the MMA's N: three activation terms of 16 rows
+
+struct QbShape {
+    static constexpr int kWRaw = kTcCols * kQ8Chunk;   // quants of 128 columns x 128 k
+    static constexpr int kScales = kTcCols * 4 * 4;    // their [128][4] scales
+    static constexpr int kOffA = kWRaw + kScales;
+    static constexpr int kARaw = kTcRows * kTcK * 4 * 4;  // A's [16][128] as four [16][32] boxes
+    static constexpr int kRawStage = kOffA + kARaw;       // 26 KB
+    static constexpr int kRawStages = 4;
+    static constexpr int kWTile = kTcCols * kQbGroupK * 2;  // [128][64] bf16: 16 KB
+    static constexpr int kBTile = kQbN * kQbGroupK * 2;     // [48][64] bf16: 6 KB
+    static constexpr int kConvStage = kWTile + kBTile;      // 22 KB
+    static constexpr int kConvStages = 3;
+    static constexpr int kRing = kRawStages * kRawStage + kConvStages * kConvStage;
+    static constexpr int kRecv = 32 * kTcCols * 4;
+    static constexpr int kBars = 512;
+    static constexpr int kSmem = kRing + kRecv + kBars + 1024;
+    static constexpr int kThreads = 448;  // producer, MMA, 4 scaler warps, 8 converter warps
+    static constexpr uint32_t kTmemCols = 512;
+    static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0, "swizzle atoms aligned");
+    static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
+    static_assert(kQbSlots * kQbN <= (int)kTmemCols, "block slots fit the tensor memory");
+    static_assert(kSmem <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+__global__ void __launch_bounds__(QbShape::kThreads, 1)
+    gemv_tc_q8b_kernel(const __grid_constant__ CUtensorMap map_a, GemvTcArgs p) {
+    using S = QbShape;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* base_ptr = smem_raw + (base - raw);
+    auto raw_stage = [&](int s) { return base + (uint32_t)(s * S::kRawStage); };
+    auto conv_stage = [&](int c) { return base + (uint32_t)(S::kRawStages * S::kRawStage + c * S::kConvStage); };
+    const uint32_t recv = base + S::kRing;
+    const uint32_t bar_base = recv + S::kRecv;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + S::kRing + S::kRecv);
+    constexpr int R = S::kRawStages, C = S::kConvStages;
+    auto raw_full = [&](int s) { return bar_base + 8u * s; };
+    auto raw_empty = [&](int s) { return bar_base + 8u * (R + s); };
+    auto conv_full = [&](int c) { return bar_base + 8u * (2 * R + c); };
+    auto conv_empty = [&](int c) { return bar_base + 8u * (2 * R + C + c); };
+    auto acc_full = [&](int t) { return bar_base + 8u * (2 * R + 2 * C + t); };
+    auto acc_empty = [&](int t) { return bar_base + 8u * (2 * R + 2 * C + kQbSlots + t); };
+    const uint32_t recv_bar = bar_base + 8u * (2 * R + 2 * C + 2 * kQbSlots);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 2 * R + 2 * C + 2 * kQbSlots + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * R + 2 * C + 2 * kQbSlots + 2);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nc = p.splits * p.terms;
+    const int rank = (int)cooperative_groups::this_cluster().block_rank();
+    const int mb = ((int)p.m + nc - 1) / nc;
+    const int my_lo = min((int)p.m, rank * mb), my_hi = min((int)p.m, my_lo + mb);
+    const uint64_t n0 = (uint64_t)blockIdx.x * kTcCols;
+    const int term = blockIdx.z;
+    const int8_t* quants = term ? p.quants[1] : p.quants[0];
+    const float* scales = term ? p.scales[1] : p.scales[0];
+    const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
+    const uint64_t k1 = min(p.k, k0 + p.slice_len);
+    const int num_kb = k1 > k0 ? (int)((k1 - k0) / kQ8Chunk) : 0;  // raw stages (records)
+    const int num_groups = num_kb * (kQ8Chunk / kQbGroupK);
+    const int num_blocks = num_kb * (kQ8Chunk / 32);
+    const uint64_t rec0 = (n0 >> 8) * p.chunks + k0 / kQ8Chunk;  // this CTA's first record
+    const uint64_t half = n0 & 255;
+
+    auto issue_w = [&](int i) {
+        const int s = i % R;
+        const uint32_t st = raw_stage(s);
+        mbar_arrive_expect_tx(raw_full(s), (uint32_t)S::kRawStage);
+        const uint64_t row0 = (rec0 + (uint64_t)i) * 256 + half;
+        bulk_load(st, quants + row0 * kQ8Chunk, (uint32_t)S::kWRaw, raw_full(s));
+        bulk_load(st + S::kWRaw, scales + row0 * 4, (uint32_t)S::kScales, raw_full(s));
+    };
+    auto issue_a = [&](int i) {
+        const int s = i % R;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            tma_load_2d(raw_stage(s) + S::kOffA + (uint32_t)(j * kTcRows * kTcK * 4), &map_a, raw_full(s),
+                        (int)(k0 + (uint64_t)i * kQ8Chunk + (uint64_t)j * kTcK), 0);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < R; s++) {
+            mbar_init(raw_full(s), 1);
+            mbar_init(raw_empty(s), 8);  // the converter warps
+        }
+        for (int c = 0; c < C; c++) {
+            mbar_init(conv_full(c), 8);
+            mbar_init(conv_empty(c), 1);
+        }
+        for (int t = 0; t < kQbSlots; t++) {
+            mbar_init(acc_full(t), 1);
+            mbar_init(acc_empty(t), 4);  // the scaler warps
+        }
+        mbar_init(recv_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        mbar_arrive_expect_tx(recv_bar, (uint32_t)((nc - 1) * (my_hi - my_lo) * kTcCols * 4));
+        // a packed weight changes only by an upload, which synchronises: its loads may precede the wait
+        for (int i = 0; i < min(R, num_kb); i++) issue_w(i);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32((const void*)tmem_slot), S::kTmemCols);
+        tmem_relinquish();
+    }
+    cluster_arrive();  // phase 1: every receive barrier of the cluster is armed
+    pdl_enter();
+    if (threadIdx.x == 0)
+        for (int i = 0; i < min(R, num_kb); i++) issue_a(i);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    float acc[kTcRows];
+#pragma unroll
+    for (int j = 0; j < kTcRows; j++) acc[j] = 0.0f;
+
+    if (warp == 0) {
+        // ---- producer: refills a raw stage once the converters have read it ---------------------
+        if (lane == 0) {
+            for (int i = R; i < num_kb; i++) {
+                const int s = i % R;
+                if (!mbar_wait(raw_empty(s), ((uint32_t)(i / R) & 1u) ^ 1u) || *abort_flag) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                issue_w(i);
+                issue_a(i);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- MMA issuer: per 16 k, D[slot of the k's block] (+)= W (bf16) x [A_h; A_m; A_l]^T ----
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(kTcCols, kQbN);
+            for (int j = 0; j < num_groups; j++) {
+                const int c = j % C;
+                if (!mbar_wait(conv_full(c), (uint32_t)(j / C) & 1u) || *abort_flag) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t cs = conv_stage(c);
+                bool ok = true;
+#pragma unroll
+                for (int kk = 0; kk < kQbGroupK / 16; kk++) {
+                    const int b = j * 2 + kk / 2, slot = b % kQbSlots;
+                    if (kk % 2 == 0) {
+                        if (!mbar_wait(acc_empty(slot), ((uint32_t)(b / kQbSlots) & 1u) ^ 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+                    const uint64_t dw = desc_k_sw128(cs) + (uint64_t)((kk * 32) >> 4);
+                    const uint64_t da = desc_k_sw128(cs + S::kWTile) + (uint64_t)((kk * 32) >> 4);
+                    mma_bf16(tmem + (uint32_t)(slot * kQbN), dw, da, idesc, (uint32_t)(kk % 2));
+                    if (kk % 2 == 1) tc_commit(acc_full(slot));  // the block's sums are complete
+                }
+                if (!ok) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+                tc_commit(conv_empty(c));
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 6) {
+        // ---- converters (8 warps): quants -> bf16 weight tile, activations -> three bf16 terms ----
+        const int t = threadIdx.x - 192;  // 0..255
+        for (int i = 0; i < num_kb; i++) {
+            const int s = i % R;
+            bool ok = mbar_wait(raw_full(s), (uint32_t)(i / R) & 1u);
+            const uint32_t rs = raw_stage(s);
+            for (int g = 0; g < kQ8Chunk / kQbGroupK; g++) {
+                const int j = i * 2 + g, c = j % C;
+                ok = mbar_wait(conv_empty(c), ((uint32_t)(j / C) & 1u) ^ 1u) && ok;
+                if (!ok) {
+                    *abort_flag = 1;
+                    atomicExch(p.error, 1);
+                }
+                const uint32_t cs = conv_stage(c);
+                // weight row n = t % 128, half hp = t / 128 of the group: pieces 4g + 2hp, 4g + 2hp + 1
+                // of the record row (32 quants) -> bf16 chunks 4hp .. 4hp + 3
+                {
+                    const int n = t & 127, hp = t >> 7;
+                    uint4 q[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const uint32_t piece = (uint32_t)((4 * g + 2 * hp + u) ^ (n & 7));
+                        q[u] = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
+                    }
+                    // two quants -> two bf16 exactly: 0x43 | q & 0x7F is 128 + (q & 0x7F), 0x43 | q & 0x80
+                    // is 128 or 256 by the sign bit; their difference is q
+                    auto wid2 = [](uint32_t w, uint32_t sel) {
+                        const uint32_t y = __byte_perm(w, 0x43u, sel);
+                        uint32_t r;
+                        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(y & 0xFF7FFF7Fu), "r"(y & 0xFF80FF80u));
+                        return r;
+                    };
+                    auto put = [&](uint32_t w0, uint32_t w1, int chunk) {
+                        const uint32_t off = (uint32_t)(n * 128 + ((chunk ^ (n & 7)) * 16));
+                        asm volatile("st.shared::cta.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cs + off),
+                                     "r"(wid2(w0, 0x4140u)), "r"(wid2(w0, 0x4342u)), "r"(wid2(w1, 0x4140u)),
+                                     "r"(wid2(w1, 0x4342u))
+                                     : "memory");
+                    };
+                    // 16 quants = k 16u' .. 16u' + 15 of the group (u' = 2hp + u): chunks 2u', 2u' + 1
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        put(q[u].x, q[u].y, 4 * hp + 2 * u);
+                        put(q[u].z, q[u].w, 4 * hp + 2 * u + 1);
+                    }
+                }
+                // activations: row m = t / 16, 4 k (f = t % 16: k 4f .. 4f + 3) of the group, from the
+                // raw [16][32] f32 box 2g + f / 8 (128-byte swizzle)
+                {
+                    const int m = t >> 4, f = t & 15, fi = f & 7;
+                    const uint32_t box = rs + S::kOffA + (uint32_t)((2 * g + f / 8) * kTcRows * kTcK * 4);
+                    const float4 x = lds4(box + (uint32_t)(m * 128 + ((fi ^ (m & 7)) * 16)));
+                    uint32_t th[2], tm[2], tl[2];
+                    auto terms3 = [&](float xa, float xb, int e) {
+                        const float ha = __uint_as_float(__float_as_uint(xa) & 0xFFFF0000u);  // truncated: no overflow
+                        const float hb = __uint_as_float(__float_as_uint(xb) & 0xFFFF0000u);
+                        const float ra = xa - ha, rb = xb - hb;
+                        const float ma = __bfloat162float(__float2bfloat16_rn(ra));
+                        const float mb2 = __bfloat162float(__float2bfloat16_rn(rb));
+                        th[e] = (__float_as_uint(ha) >> 16) | (__float_as_uint(hb) & 0xFFFF0000u);
+                        tm[e] = bf16x2_rn(ma, mb2);
+                        tl[e] = bf16x2_rn(ra - ma, rb - mb2);
+                    };
+                    terms3(x.x, x.y, 0);
+                    terms3(x.z, x.w, 1);
+                    const uint32_t bt = cs + S::kWTile;
+                    const uint32_t cc = (uint32_t)(f >> 1), hoff = (uint32_t)(f & 1) * 8;
+                    auto put_row = [&](uint32_t row, const uint32_t (&w)[2]) {
+                        const uint32_t off = row * 128 + ((cc ^ (row & 7)) * 16) + hoff;
+                        asm volatile("st.shared::cta.v2.b32 [%0], {%1, %2};" ::"r"(bt + off), "r"(w[0]), "r"(w[1])
+                                     : "memory");
+                    };
+                    put_row((uint32_t)m, th);
+                    put_row((uint32_t)(kTcRows + m), tm);
+                    put_row((uint32_t)(2 * kTcRows + m), tl);
+                }
+                fence_proxy_async();
+                mbar_arrive_warp(conv_full(c));
+            }
+            mbar_arrive_warp(raw_empty(s));
+            if (__any_sync(0xffffffffu, *abort_flag)) break;
+        }
+    } else {
+        // ---- warps 2..5: fold each finished block slot into registers: sum += scale * block ------
+        // A record's four scales per column are fetched one record ahead, so their load latency
+        // stays off the chain of slot waits.
+        const int q = warp % 4, n = q * 32 + lane;
+        bool failed = false;
+        auto scale4 = [&](int r) {
+            return __ldg(reinterpret_cast<const float4*>(scales + ((rec0 + (uint64_t)r) * 256 + half + n) * 4));
+        };
+        float4 sc_cur = make_float4(0.f, 0.f, 0.f, 0.f), sc_nxt = num_kb > 0 ? scale4(0) : sc_cur;
+        for (int b = 0; b < num_blocks; b++) {
+            const int slot = b % kQbSlots;
+            if (b % 4 == 0) {
+                sc_cur = sc_nxt;
+                if (b / 4 + 1 < num_kb) sc_nxt = scale4(b / 4 + 1);
+            }
+            if (!failed && !mbar_wait(acc_full(slot), (uint32_t)(b / kQbSlots) & 1u)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
+            float v[kQbN];
+            if (!failed) {
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * kQbN);
+                tmem_ld16(ta, v);
+                tmem_ld16(ta + 16, v + 16);
+                tmem_ld16(ta + 32, v + 32);
+                tc_wait_ld();
+            }
+            tc_fence_before();
+            mbar_arrive_warp(acc_empty(slot));
+            if (failed) continue;
+            const float sc = (b & 3) == 0 ? sc_cur.x : (b & 3) == 1 ? sc_cur.y : (b & 3) == 2 ? sc_cur.z : sc_cur.w;
+#pragma unroll
+            for (int r = 0; r < kTcRows; r++) acc[r] = fmaf(sc, (v[r] + v[kTcRows + r]) + v[2 * kTcRows + r], acc[r]);
+        }
+        if (failed) {
+            *abort_flag = 1;
+            atomicExch(p.error, 1);
+        }
+    }
+    // ---- stage this CTA's partial as [16 m][128 n] in the drained first conversion buffer ------
+    tc_fence_before();
+    __syncthreads();
+    float* staged = reinterpret_cast<float*>(base_ptr + (conv_stage(0) - base));
+    if (warp >= 2 && warp < 6) {
+        const int n = (warp % 4) * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < kTcRows; j++) staged[j * kTcCols + n] = *abort_flag ? 0.0f : acc[j];
+        fence_proxy_async();  // the staged rows are read by bulk copies next
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::kTmemCols);
+    }
+    // ---- exchange: each band of rows to the CTA that owns it ------------------------------------
+    cluster_wait();  // phase 1
+    {
+        const int o = (int)threadIdx.x - 64;
+        if (o >= 0 && o < nc && o != rank) {
+            const int lo = min((int)p.m, o * mb), hi = min((int)p.m, lo + mb);
+            if (hi > lo)
+                bulk_copy_to_cluster(mapa(recv + (uint32_t)(rank * mb * kTcCols * 4), (uint32_t)o),
+                                     conv_stage(0) + (uint32_t)(lo * kTcCols * 4), (uint32_t)((hi - lo) * kTcCols * 4),
+                                     mapa(recv_bar, (uint32_t)o));
+        }
+    }
+    if (!mbar_wait(recv_bar, 0)) atomicExch(p.error, 1);
+    cluster_arrive();  // phase 2: every copy into this CTA has landed
+    const float* recvf = reinterpret_cast<const float*>(base_ptr + S::kRing);
+    for (int e = (int)threadIdx.x; e < (my_hi - my_lo) * kTcCols; e += blockDim.x) {
+        const int r = my_lo + e / kTcCols, c = e % kTcCols;
+        const uint64_t col = n0 + (uint64_t)c;
+        if (col >= p.n) continue;
+        auto from = [&](int src) {
+            return src == rank ? staged[r * kTcCols + c] : recvf[(src * mb + (r - my_lo)) * kTcCols + c];
+        };
+        float g = 0.0f;
+        for (int s2 = 0; s2 < p.splits; s2++) g += from(s2);
+        float v;
+        if (p.terms == 2) {
+            float u = 0.0f;
+            for (int s2 = 0; s2 < p.splits; s2++) u += from(p.splits + s2);
+            v = (g * (1.0f / (1.0f + expf(-g)))) * u;
+        } else {
+            v = g;
+            if (p.addend_mode == 1) v += p.addend[col];
+            else if (p.addend_mode == 2) v += p.addend[(uint64_t)r * p.n + col];
+        }
+        p.out[(uint64_t)r * p.n + col] = v;
+    }
+    cluster_wait();  // phase 2: every copy out of this CTA's shared memory has landed
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tc_gemv_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -473,9 +838,9 @@ int env_min_rows(const char* name, int dflt) {
     const int x = atoi(e);
     return x <= 0 ? kTcRows + 1 : x;
 }
-// Defaults from measurement at N = K = 4096: packed Q8_0 at 16 rows takes 29 us here against 61 us
-// on the CUDA cores, one row 28 us against 8 us; f32 at 16 rows 26 us against 21 us -- the f32 form
-// stays off until its per-group pipeline is shorter.
+// Defaults from measurement at N = K = 4096: packed Q8_0 at 16 rows takes 15 us here against 61 us
+// on the CUDA cores, at 8 rows 15 us against 19 us, one row 15 us against 8 us; f32 at 16 rows 26 us
+// against 21 us -- the f32 form stays off until its per-group pipeline is shorter.
 int tc_min_rows() {
     static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC", kTcRows + 1);
     return v;
@@ -613,7 +978,91 @@ bool gemv_tc_q8_eligible(const GemmArgs& g) {
            g.n < (1ull << 31);
 }
 
-mg_status gemv_tc_q8(Device* d, const GemmArgs& g) { return launch_gemv_tc<true>(d, g); }
+mg_status gemv_tc_q8(Device* d, const GemmArgs& g) {
+    using S = QbShape;
+    const uint64_t col_tiles = (g.n + kTcCols - 1) / kTcCols;
+    if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
+    const int terms = g.gated ? 2 : 1;
+    const uint64_t kb = g.k / kQ8Chunk;
+    uint64_t splits = (uint64_t)d->sm_count / (col_tiles * terms);
+    if (splits > (uint64_t)(kMaxCluster / terms)) splits = kMaxCluster / terms;
+    if (splits > kb) splits = kb;
+    if (splits < 1) splits = 1;
+    GemvTcArgs p;
+    memset(&p, 0, sizeof p);
+    p.out = g.out;
+    p.addend = g.addend;
+    p.addend_mode = g.addend_mode;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.terms = terms;
+    p.b_early = 1;
+    p.error = d->flags + 2;
+    for (int t = 0; t < 2; t++) {
+        const Buffer* w = g.packed[t < terms ? t : 0];
+        p.quants[t] = static_cast<const int8_t*>(w->ptr);
+        p.scales[t] = w->q8_scales;
+    }
+    p.chunks = kb;
+    auto set_splits = [&](uint64_t sp) {
+        p.slice_len = ((kb + sp - 1) / sp) * kQ8Chunk;
+        p.splits = (int)((g.k + p.slice_len - 1) / p.slice_len);
+        if (p.splits < 1) p.splits = 1;
+    };
+    set_splits(splits);
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(gemv_tc_q8b_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+                "configuring the packed tensor-core gemv kernel");
+        MG_CUDA(cudaFuncSetAttribute(gemv_tc_q8b_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "allowing the packed tensor-core gemv kernel clusters of up to 16");
+        configured[d->ordinal & 63] = true;
+    }
+    static int fits[kMaxCluster + 1] = {0};
+    while (p.splits * p.terms > 8) {
+        const int nc = p.splits * p.terms;
+        if (fits[nc] == 0) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
+            q.blockDim = dim3(S::kThreads, 1, 1);
+            q.dynamicSmemBytes = S::kSmem;
+            cudaLaunchAttribute ca;
+            ca.id = cudaLaunchAttributeClusterDimension;
+            ca.val.clusterDim.x = 1;
+            ca.val.clusterDim.y = (unsigned)p.splits;
+            ca.val.clusterDim.z = (unsigned)p.terms;
+            q.attrs = &ca;
+            q.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, gemv_tc_q8b_kernel, &q) != cudaSuccess) {
+                (void)cudaGetLastError();
+                clusters = 0;
+            }
+            fits[nc] = clusters > 0 ? 1 : -1;
+        }
+        if (fits[nc] > 0) break;
+        set_splits((uint64_t)p.splits - 1);
+    }
+    CUtensorMap map_a;
+    MG_TRY(tc_gemv_map(&map_a, g.a, g.m, g.k, kTcRows));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
+    cfg.blockDim = dim3(S::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::kSmem;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)p.splits;
+    attr[0].val.clusterDim.z = (unsigned)p.terms;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = d->pdl ? 2 : 1;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_q8b_kernel, map_a, p), "packed tensor-core gemv launch");
+    return launched(d, "packed tensor-core gemv launch");
+}
 
 }  // namespace k
 }  // namespace mg

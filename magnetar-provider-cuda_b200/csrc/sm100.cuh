@@ -43,6 +43,15 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// One arrival for the whole warp (the barrier counts warps): the lanes' earlier shared-memory
+// writes are ordered before lane 0's arrive.  Arrivals on one barrier serialise, so a stage
+// released by 256 threads one by one costs far more than by their 8 warps.  Every lane of the
+// warp must call it.
+__device__ __forceinline__ void mbar_arrive_warp(uint32_t bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
