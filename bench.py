@@ -513,16 +513,26 @@ def tp_mlp_bench(torch, mpc, kernels, world, rank, steps, warmup, tf32_tflops):
             en.record()
             en.synchronize()
         ms = st.elapsed_time(en) / steps
-        t = torch.tensor([ms], device="cuda")
+        # the split of a step (outside the timed loop, three calls): start -> last down chunk
+        # done (GEMMs, with the overlapped all-reduces beside them), then the all-reduce time
+        # left exposed after it; events on the compute stream, max over ranks
+        group.set_mlp_timing(True)
+        split = []
+        for _ in range(3):
+            group.mlp(dx, dg, du, dd, chunks=4, out=dy)
+            split.append(group.mlp_timing())
+        group.set_mlp_timing(False)
+        t = torch.tensor([ms, min(c for c, _ in split), min(e for _, e in split)], device="cuda")
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, compute_ms, exposed_ms = (float(v) for v in t.tolist())
     finally:
         group.close()
     flops = 3 * 2.0 * T * Hd * F
     return {"workload": "configs[4] SwiGLU MLP tokens 4096 hidden 8192 ffn 28672, gate/up column-split, "
                         "down row-split, one NCCL all-reduce chunked x4 over the down projection",
             "n_gpus": world, "ms_per_step": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
+            "compute_ms": round(compute_ms, 3), "exposed_allreduce_ms": round(exposed_ms, 3),
             "tflops": round(flops / (ms * 1e-3) / 1e12, 2),
             "frac_of_3xtf32_effective_x_n": round(flops / (ms * 1e-3) / 1e12 / (world * tf32_tflops / 3), 4),
             "clocks": clocks.summary()}

@@ -484,6 +484,16 @@ mg_status mg_comm_check(mg_comm* comm);
 mg_status mg_comm_wait(mg_comm* comm, int64_t timeout_ms);
 mg_status mg_comm_abort(mg_comm* comm);
 int mg_comm_is_aborted(const mg_comm* comm);
+
+/* Measurement of mg_tp_mlp (no reference interface: the split the reference's tensor-parallel
+ * MLP, src/multi/tensor_parallel.rs:697-734, leaves unmeasured).  With timing on, each
+ * mg_tp_mlp call records three events on the compute stream: its start, the end of its last
+ * down-projection chunk, and the join of the all-reduce stream.  mg_comm_mlp_timing waits for
+ * the last timed call and returns start -> compute end (the gated and down GEMMs, with the
+ * overlapped all-reduces running beside them) and compute end -> join (the all-reduce time
+ * left exposed after the last GEMM).  MG_INVALID_ARGUMENT when no call was timed. */
+mg_status mg_comm_set_mlp_timing(mg_comm* comm, int on);
+mg_status mg_comm_mlp_timing(mg_comm* comm, float* compute_ms, float* exposed_ms);
 /* Host-only test hook of the bounded settle: drives the poll loop with a scripted sequence of
  * NCCL results (0 success, 7 in progress, anything else an error; the last repeats) instead of
  * a communicator.  Returns the status the settle ends with; *aborted counts the aborts, *polls

@@ -195,6 +195,8 @@ SIGNATURES = {
     "mg_comm_wait": [_P, ctypes.c_int64],
     "mg_comm_abort": [_P],
     "mg_comm_is_aborted": [_P],
+    "mg_comm_set_mlp_timing": [_P, ctypes.c_int],
+    "mg_comm_mlp_timing": [_P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)],
     "mg_comm_settle_selftest": [_IP, _I, ctypes.c_int64, _IP, _IP],
     "mg_tp_share": [_U64, _I, _I, _U64P, _U64P],
     "mg_tp_mlp": [_P, _P, _P, _P, _P, _I, _PP],

@@ -33,6 +33,10 @@ struct mg_comm {
     std::vector<cudaEvent_t> events;
     int64_t timeout_ms = 300000;
     bool aborted = false;
+    // mg_tp_mlp's timing events (mg_comm_set_mlp_timing): start, last down-projection chunk
+    // done on the compute stream, the all-reduce stream joined.
+    cudaEvent_t timing[3] = {nullptr, nullptr, nullptr};
+    bool timed = false;
 };
 
 namespace mg {
@@ -186,6 +190,8 @@ mg_status mg_comm_destroy(mg_comm* c) {
     cudaSetDevice(c->device->ordinal);
     cudaStreamSynchronize(c->side);
     for (cudaEvent_t ev : c->events) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : c->timing)
+        if (ev) cudaEventDestroy(ev);
     cudaStreamDestroy(c->side);
     if (c->nccl && !c->aborted) {
         // Non-blocking: the destroy itself may be in progress; bounded like every other call.
@@ -277,6 +283,9 @@ mg_status mg_tp_mlp(mg_comm* c, const mg_buffer* xh, const mg_buffer* gh, const 
     const Buffer* x = buf(xh);
     const Buffer* dn = buf(dh);
     if (x->rank != 2 || dn->rank != 2) return fail(MG_SHAPE_UNSUPPORTED, "the MLP takes rank-2 activations and weights");
+    const bool timed = c->timing[0] != nullptr;
+    c->timed = false;
+    if (timed) MG_CUDA(cudaEventRecord(c->timing[0], d->stream), "recording the MLP's start");
     // h = silu(x G_s) * (x U_s): [tokens, ffn_share], from the rank's column shards.
     mg_buffer* hh = nullptr;
     MG_TRY(mg_gated_matmul(c->handle, xh, gh, uh, 0, 0, &hh));
@@ -330,13 +339,46 @@ mg_status mg_tp_mlp(mg_comm* c, const mg_buffer* xh, const mg_buffer* gh, const 
         s = comm_settle(c, ncclAllReduce(g.out, g.out, (r1 - r0) * hidden, ncclFloat32, ncclSum, c->nccl, c->side),
                         "all-reducing an MLP chunk");
     }
+    if (timed && s == MG_OK) {
+        cudaError_t e = cudaEventRecord(c->timing[1], d->stream);
+        if (e != cudaSuccess) s = from_cuda(e, "recording the MLP's compute end");
+    }
     if (c->world > 1) {
         cudaError_t e = cudaEventRecord(c->events[chunks], c->side);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(d->stream, c->events[chunks], 0);
         if (e != cudaSuccess && s == MG_OK) s = from_cuda(e, "joining the all-reduce stream");
     }
+    if (timed && s == MG_OK) {
+        cudaError_t e = cudaEventRecord(c->timing[2], d->stream);
+        if (e != cudaSuccess) s = from_cuda(e, "recording the MLP's end");
+        else c->timed = true;
+    }
     buffer_free(hb);
     return s;
+}
+
+mg_status mg_comm_set_mlp_timing(mg_comm* c, int on) {
+    if (!c) return fail(MG_INVALID_ARGUMENT, "null communicator");
+    MG_TRY(device_check(c->handle));
+    for (cudaEvent_t& ev : c->timing) {
+        if (on && !ev) MG_CUDA(cudaEventCreate(&ev), "creating a timing event");
+        if (!on && ev) {
+            cudaEventDestroy(ev);
+            ev = nullptr;
+        }
+    }
+    c->timed = false;
+    return MG_OK;
+}
+
+mg_status mg_comm_mlp_timing(mg_comm* c, float* compute_ms, float* exposed_ms) {
+    if (!c || !compute_ms || !exposed_ms) return fail(MG_INVALID_ARGUMENT, "null argument");
+    if (!c->timed) return fail(MG_INVALID_ARGUMENT, "no timed MLP call since timing was switched on");
+    MG_TRY(device_check(c->handle));
+    MG_CUDA(cudaEventSynchronize(c->timing[2]), "waiting for the timed MLP");
+    MG_CUDA(cudaEventElapsedTime(compute_ms, c->timing[0], c->timing[1]), "reading the MLP's compute time");
+    MG_CUDA(cudaEventElapsedTime(exposed_ms, c->timing[1], c->timing[2]), "reading the MLP's exposed all-reduce");
+    return MG_OK;
 }
 
 }  // extern "C"

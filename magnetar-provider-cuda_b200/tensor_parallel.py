@@ -176,6 +176,17 @@ class TpGroup:
             return out
         return DeviceBuffer(o.value, self.kernels)
 
+    def set_mlp_timing(self, on: bool = True) -> None:
+        """Record events around each ``mlp`` call (see ``mlp_timing``)."""
+        check(N.lib().mg_comm_set_mlp_timing(self._h, int(bool(on))))
+
+    def mlp_timing(self):
+        """(compute_ms, exposed_allreduce_ms) of the last timed ``mlp`` call: start to the end of
+        its last down-projection chunk, and from there to the all-reduce stream's join."""
+        c, e = ctypes.c_float(), ctypes.c_float()
+        check(N.lib().mg_comm_mlp_timing(self._h, ctypes.byref(c), ctypes.byref(e)))
+        return float(c.value), float(e.value)
+
     def close(self) -> None:
         if self._h and self._h.value:
             N.lib().mg_comm_destroy(self._h)

@@ -32,6 +32,34 @@ def test_tp_mlp_single_rank(kernels, oracle, chunks):
         g.close()
 
 
+def test_tp_mlp_timing_split(kernels, oracle, mpc):
+    # the measurement hook: start -> last down chunk, then the exposed all-reduce; results unchanged
+    tp = importlib.import_module("magnetar-provider-cuda_b200.tensor_parallel")
+    r = np.random.default_rng(5)
+    x = r.standard_normal((512, 256)).astype(np.float32)
+    wg = (r.standard_normal((256, 768)) * 0.05).astype(np.float32)
+    wu = (r.standard_normal((256, 768)) * 0.05).astype(np.float32)
+    wd = (r.standard_normal((768, 256)) * 0.05).astype(np.float32)
+    g = tp.TpGroup(kernels, 0, 1, tp.TpGroup.unique_id())
+    try:
+        args = [kernels.upload(v) for v in (x, wg, wu, wd)]
+        with pytest.raises(mpc.CudaError):
+            g.mlp_timing()  # timing is off
+        g.set_mlp_timing(True)
+        with pytest.raises(mpc.CudaError):
+            g.mlp_timing()  # on, but nothing timed yet
+        y = g.mlp(*args, chunks=4)
+        compute_ms, exposed_ms = g.mlp_timing()
+        assert compute_ms > 0.0 and 0.0 <= exposed_ms < compute_ms
+        assert rel(kernels.download(y), oracle.matmul(oracle.gated_matmul(x, wg, wu), wd)) <= 1e-4
+        g.set_mlp_timing(False)
+        g.mlp(*args, chunks=4)
+        with pytest.raises(mpc.CudaError):
+            g.mlp_timing()
+    finally:
+        g.close()
+
+
 def test_executor_plan_on_one_rank(executor, oracle):
     tp = importlib.import_module("magnetar-provider-cuda_b200.tensor_parallel")
     mpc = importlib.import_module("magnetar-provider-cuda_b200")
