@@ -19,13 +19,8 @@
 // Per weight value the converters spend about four instructions (the FMA path: sixteen FMAs
 // at 16 rows), and the tensor pipe does the multiply, so the kernel streams B at HBM speed.
 //
-// Packed Q8_0 weights take the same kernel with a different producer and converter: a stage is
-// half of one tiled record (128 output columns x 128 k quants, each column's 128 bytes in eight
-// permuted 16-byte pieces, and their [128][4] scales), moved by two bulk copies; the converters
-// widen each quant exactly (byte permute into the mantissa of 2^23 and one subtraction), multiply
-// it by its block's scale (exact: 8 x 11 significant bits) and split the product into tf32 hi /
-// lo in the K-major swizzled layout, 32 k at a time -- so the product is the f32 matmul of the
-// dequantized weight, reading 1.125 bytes per weight value.
+// Packed Q8_0 weights (tiled records) take a kernel of their own further down, on bf16 operands:
+// every quant is exactly a bfloat16 value, so only the activations are split.
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -52,18 +47,13 @@ constexpr int kConvThreads = 256;
 constexpr int kMaxCluster = 16;  // non-portable cluster size (checked against the GPU at launch)
 constexpr int kQ8Chunk = 128;    // k per tiled Q8_0 record
 
-template <bool Q8>
 struct TcGemvShape {
-    // f32: a raw stage is one group of k ([32 k][128 n] as four swizzled boxes, then A's [16][32]).
-    // Q8_0: a raw stage is four groups: the quants of 128 columns x 128 k (16 KB), their scales
-    // (2 KB), then A's [16][128] as four swizzled [16][32] boxes.
-    static constexpr int kGroups = Q8 ? kQ8Chunk / kTcK : 1;
-    static constexpr int kWRaw = Q8 ? kTcCols * kQ8Chunk : kTcK * kTcCols * 4;
-    static constexpr int kScales = Q8 ? kTcCols * 4 * 4 : 0;
-    static constexpr int kARaw = kTcRows * kTcK * 4 * kGroups;
-    static constexpr int kOffA = kWRaw + kScales;
+    // a raw stage is one group of k: [32 k][128 n] as four swizzled boxes, then A's [16][32]
+    static constexpr int kWRaw = kTcK * kTcCols * 4;
+    static constexpr int kARaw = kTcRows * kTcK * 4;
+    static constexpr int kOffA = kWRaw;
     static constexpr int kRawStage = kOffA + kARaw;
-    static constexpr int kRawStages = Q8 ? 3 : 5;  // raw bytes in flight from HBM
+    static constexpr int kRawStages = 5;                  // raw bytes in flight from HBM
     static constexpr int kWTile = kTcK * kTcCols * 4;     // one converted W term: 16 KB
     static constexpr int kATile = kTcRows * kTcK * 4;     // one converted A term: 2 KB
     static constexpr int kConvStage = 2 * kWTile + 2 * kATile;  // W hi, W lo, A hi, A lo
@@ -122,25 +112,11 @@ __device__ __forceinline__ void split_fast(float4 v, float4& hi, float4& lo) {
     lo = make_float4(tf32_rna(v.x - hi.x), tf32_rna(v.y - hi.y), tf32_rna(v.z - hi.z), tf32_rna(v.w - hi.w));
 }
 
-// Four quants (one 32-bit word, little-endian) widened exactly to f32 and multiplied by the
-// block's scale: each biased byte becomes the low mantissa byte of 2^23 (byte permute), and
-// subtracting 2^23 + 128 leaves the signed value; q * scale is exact (8 x 11 significant bits).
-__device__ __forceinline__ float4 q8_widen4(uint32_t word, float scale) {
-    const uint32_t w = word ^ 0x80808080u;
-    const float bias = 8388736.0f;  // 2^23 + 128
-    return make_float4((__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540)) - bias) * scale,
-                       (__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541)) - bias) * scale,
-                       (__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542)) - bias) * scale,
-                       (__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543)) - bias) * scale);
-}
-
-template <bool Q8>
-__global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
+__global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_b2, GemvTcArgs p) {
-    using S = TcGemvShape<Q8>;
+    using S = TcGemvShape;
     constexpr int kRawStages = S::kRawStages;
-    constexpr int kG = S::kGroups;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -169,36 +145,22 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
     const CUtensorMap* map_w = term ? &map_b2 : &map_b;
     const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
     const uint64_t k1 = min(p.k, k0 + p.slice_len);
-    constexpr int kStageK = kTcK * kG;  // k per raw stage
-    const int num_kb = k1 > k0 ? (int)((k1 - k0 + kStageK - 1) / kStageK) : 0;  // raw stages
-    const int num_groups = num_kb * kG;
+    const int num_kb = k1 > k0 ? (int)((k1 - k0 + kTcK - 1) / kTcK) : 0;  // raw stages, one group each
+    const int num_groups = num_kb;
 
-    // The producer's loads of raw stage i: B (the weight's tiles, or the Q8_0 record's half with
-    // its scales) arms the stage's barrier for all its bytes; A follows.
+    // The producer's loads of raw stage i: B (the weight's tiles) arms the stage's barrier for all
+    // its bytes; A follows.
     auto issue_w = [&](int i) {
         const int s = i % kRawStages;
         const uint32_t st = raw_stage(s);
         mbar_arrive_expect_tx(raw_full(s), (uint32_t)S::kRawStage);
-        if constexpr (Q8) {
-            // record (column tile of 256, k chunk): this CTA's 128 columns are its first or second half
-            const uint64_t rec = (n0 >> 8) * p.chunks + (k0 / kQ8Chunk + (uint64_t)i);
-            const uint64_t row0 = rec * 256 + (n0 & 255);
-            const int8_t* quants = term ? p.quants[1] : p.quants[0];
-            const float* scales = term ? p.scales[1] : p.scales[0];
-            bulk_load(st, quants + row0 * kQ8Chunk, (uint32_t)S::kWRaw, raw_full(s));
-            bulk_load(st + S::kWRaw, scales + row0 * 4, (uint32_t)S::kScales, raw_full(s));
-        } else {
-            const int ky = (int)(k0 + (uint64_t)i * kTcK);
+        const int ky = (int)(k0 + (uint64_t)i * kTcK);
 #pragma unroll
-            for (int j = 0; j < 4; j++) tma_load_2d(st + (uint32_t)(j * 4096), map_w, raw_full(s), (int)n0 + 32 * j, ky);
-        }
+        for (int j = 0; j < 4; j++) tma_load_2d(st + (uint32_t)(j * 4096), map_w, raw_full(s), (int)n0 + 32 * j, ky);
     };
     auto issue_a = [&](int i) {
         const int s = i % kRawStages;
-#pragma unroll
-        for (int j = 0; j < kG; j++)
-            tma_load_2d(raw_stage(s) + S::kOffA + (uint32_t)(j * S::kATile), &map_a, raw_full(s),
-                        (int)(k0 + (uint64_t)i * kStageK + (uint64_t)j * kTcK), 0);
+        tma_load_2d(raw_stage(s) + S::kOffA, &map_a, raw_full(s), (int)(k0 + (uint64_t)i * kTcK), 0);
     };
 
     if (threadIdx.x == 0) {
@@ -255,8 +217,8 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
     } else if (warp == 1) {
         // ---- MMA issuer: D[128 n][16 m] += W_lo A_hi + W_hi A_lo + W_hi A_hi --------------------
         if (lane == 0) {
-            // A (the weight) MN-major as it lies (f32), K-major as the converters write it (Q8_0)
-            constexpr uint32_t idesc = idesc_tf32(kTcCols, kTcRows) | (Q8 ? 0u : (1u << 15));
+            // A (the weight) MN-major as it lies
+            constexpr uint32_t idesc = idesc_tf32(kTcCols, kTcRows) | (1u << 15);
             bool ok = true;
             for (int i = 0; i < num_groups; i++) {
                 const int c = i % kConvStages;
@@ -271,14 +233,8 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
                 const uint32_t whi = cs, wlo = cs + S::kWTile, ahi = cs + 2 * S::kWTile, alo = ahi + S::kATile;
 #pragma unroll
                 for (int kk = 0; kk < kTcK / 8; kk++) {
-                    uint64_t dwhi, dwlo;
-                    if constexpr (Q8) {
-                        dwhi = desc_k_sw128(whi) + (uint64_t)((kk * 32) >> 4);
-                        dwlo = desc_k_sw128(wlo) + (uint64_t)((kk * 32) >> 4);
-                    } else {
-                        dwhi = desc_mn_sw128_32b(whi + (uint32_t)(kk * 1024), 4096);
-                        dwlo = desc_mn_sw128_32b(wlo + (uint32_t)(kk * 1024), 4096);
-                    }
+                    const uint64_t dwhi = desc_mn_sw128_32b(whi + (uint32_t)(kk * 1024), 4096);
+                    const uint64_t dwlo = desc_mn_sw128_32b(wlo + (uint32_t)(kk * 1024), 4096);
                     const uint64_t dahi = desc_k_sw128(ahi) + (uint64_t)((kk * 32) >> 4);
                     const uint64_t dalo = desc_k_sw128(alo) + (uint64_t)((kk * 32) >> 4);
                     // four accumulators, one per k-step: four independent chains of MMAs
@@ -300,56 +256,37 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
             const int s = i % kRawStages;
             bool ok = mbar_wait(raw_full(s), (uint32_t)(i / kRawStages) & 1u);
             const uint32_t rs = raw_stage(s);
-            for (int g = 0; g < kG; g++) {
-                const int gi = i * kG + g, c = gi % kConvStages;
-                ok = mbar_wait(conv_empty(c), ((uint32_t)(gi / kConvStages) & 1u) ^ 1u) && ok;
-                if (!ok) {
-                    *abort_flag = 1;
-                    atomicExch(p.error, 1);  // still arrive below so that no one waits for this thread
-                }
-                const uint32_t cs = conv_stage(c);
-                if constexpr (Q8) {
-                    // column n = t % 128 of the record half, 16 of the group's 32 k (piece 2g + t / 128)
-                    const int n = t & 127, half = t >> 7;
-                    const uint32_t piece = (uint32_t)((2 * g + half) ^ (n & 7));
-                    const uint4 q = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
-                    const float sc = *reinterpret_cast<const float*>(base_ptr + (rs - base) + S::kWRaw + (uint32_t)(n * 4 + g) * 4);
-                    auto put = [&](uint32_t word, int j) {
-                        float4 h, l;
-                        split_fast(q8_widen4(word, sc), h, l);
-                        const uint32_t off = (uint32_t)(n * 128 + (((4 * half + j) ^ (n & 7)) * 16));
-                        sts4(cs + off, h.x, h.y, h.z, h.w);
-                        sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
-                    };
-                    put(q.x, 0);
-                    put(q.y, 1);
-                    put(q.z, 2);
-                    put(q.w, 3);
-                } else {
-                    // all of this thread's loads first, so that their latencies overlap
-                    constexpr int J = S::kWRaw / 16 / kConvThreads;
-                    float4 x[J];
-#pragma unroll
-                    for (int j = 0; j < J; j++) x[j] = lds4(rs + (uint32_t)(t + j * kConvThreads) * 16);
-#pragma unroll
-                    for (int j = 0; j < J; j++) {
-                        const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
-                        float4 h, l;
-                        split_fast(x[j], h, l);
-                        sts4(cs + off, h.x, h.y, h.z, h.w);
-                        sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
-                    }
-                }
-                if (t < S::kATile / 16) {
-                    const uint32_t off = (uint32_t)t * 16;
-                    float4 h, l;
-                    split_fast(lds4(rs + S::kOffA + (uint32_t)(g * S::kATile) + off), h, l);
-                    sts4(cs + 2 * S::kWTile + off, h.x, h.y, h.z, h.w);
-                    sts4(cs + 2 * S::kWTile + S::kATile + off, l.x, l.y, l.z, l.w);
-                }
-                fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
-                mbar_arrive_warp(conv_full(c));
+            const int c = i % kConvStages;
+            ok = mbar_wait(conv_empty(c), ((uint32_t)(i / kConvStages) & 1u) ^ 1u) && ok;
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.error, 1);  // still arrive below so that no one waits for this thread
             }
+            const uint32_t cs = conv_stage(c);
+            {
+                // all of this thread's loads first, so that their latencies overlap
+                constexpr int J = S::kWRaw / 16 / kConvThreads;
+                float4 x[J];
+#pragma unroll
+                for (int j = 0; j < J; j++) x[j] = lds4(rs + (uint32_t)(t + j * kConvThreads) * 16);
+#pragma unroll
+                for (int j = 0; j < J; j++) {
+                    const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
+                    float4 h, l;
+                    split_fast(x[j], h, l);
+                    sts4(cs + off, h.x, h.y, h.z, h.w);
+                    sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
+                }
+            }
+            if (t < S::kATile / 16) {
+                const uint32_t off = (uint32_t)t * 16;
+                float4 h, l;
+                split_fast(lds4(rs + S::kOffA + off), h, l);
+                sts4(cs + 2 * S::kWTile + off, h.x, h.y, h.z, h.w);
+                sts4(cs + 2 * S::kWTile + S::kATile + off, l.x, l.y, l.z, l.w);
+            }
+            fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
+            mbar_arrive_warp(conv_full(c));
             mbar_arrive_warp(raw_empty(s));
             if (__any_sync(0xffffffffu, *abort_flag)) break;
         }
@@ -440,13 +377,16 @@ __global__ void __launch_bounds__(TcGemvShape<Q8>::kThreads, 1)
 // (h the value truncated to bf16, m = bf16(x - h), l = bf16(x - h - m): within 2^-24 of x).  The
 // three terms are stacked as the MMA's N = 48 (rows 0-15, 16-31, 32-47), so one kind::f16 MMA per
 // 16 k reads the weight tile once for all of them.  A Q8_0 block's scale multiplies its 32 k only,
-// so each block accumulates into its own TMEM slot (48 columns, eight slots in rotation); four
-// scaler warps read a finished slot, add its three terms, and fold it into their registers as
+// so each block accumulates into its own TMEM slot (48 columns); four scaler warps read a record's
+// four finished slots, add each slot's three terms, and fold it into their registers as
 // sum += scale * block_sum -- the reference's per-block sum times the block's scale
-// (src/kernels.cu:283-348).  A group is 64 k (two blocks): a raw stage (half a tiled record) is two
-// groups.
-constexpr int kQbGroupK = 64;
-constexpr int kQbSlots = 8;          // TMEM block slots of 48 columns
+// (src/kernels.cu:283-348).
+//
+// The unit of work is one raw stage, half a tiled record (128 columns x 128 k): it is converted
+// as a whole and its eight MMAs are issued together, so each stage costs one pass of barrier
+// hand-offs (raw -> converters -> MMA -> scalers).  Those hand-offs, not the arithmetic, set the
+// pace: every one is a chain of long-latency shared-memory and tensor-core operations.
+constexpr int kQbSlots = 8;          // TMEM block slots of 48 columns: two stages' four blocks
 constexpr int kQbN = 3 * kTcRows;    // the MMA's N: three activation terms of 16 rows
 
 struct QbShape {
@@ -455,18 +395,22 @@ struct QbShape {
     static constexpr int kOffA = kWRaw + kScales;
     static constexpr int kARaw = kTcRows * kTcK * 4 * 4;  // A's [16][128] as four [16][32] boxes
     static constexpr int kRawStage = kOffA + kARaw;       // 26 KB
-    static constexpr int kRawStages = 4;
-    static constexpr int kWTile = kTcCols * kQbGroupK * 2;  // [128][64] bf16: 16 KB
-    static constexpr int kBTile = kQbN * kQbGroupK * 2;     // [48][64] bf16: 6 KB
-    static constexpr int kConvStage = kWTile + kBTile;      // 22 KB
+    static constexpr int kRawStages = 3;
+    // a converted stage: K-major, 128-byte swizzled, as two 64-k atom columns per operand
+    static constexpr int kWAtom = kTcCols * 128;          // [128 n][64 k] bf16: 16 KB
+    static constexpr int kBAtom = kQbN * 128;             // [48 rows][64 k] bf16: 6 KB
+    static constexpr int kWTile = 2 * kWAtom;
+    static constexpr int kConvStage = kWTile + 2 * kBAtom;  // 44 KB
     static constexpr int kConvStages = 3;
     static constexpr int kRing = kRawStages * kRawStage + kConvStages * kConvStage;
-    static constexpr int kRecv = 32 * kTcCols * 4;
+    static constexpr int kMaxCluster = 8;              // 8 CTAs' bands of 16 rows: at most 23 rows received
+    static constexpr int kRecv = 24 * kTcCols * 4;
     static constexpr int kBars = 512;
     static constexpr int kSmem = kRing + kRecv + kBars + 1024;
     static constexpr int kThreads = 448;  // producer, MMA, 4 scaler warps, 8 converter warps
     static constexpr uint32_t kTmemCols = 512;
-    static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0, "swizzle atoms aligned");
+    static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0 && kBAtom % 1024 == 0,
+                  "swizzle atoms aligned");
     static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
     static_assert(kQbSlots * kQbN <= (int)kTmemCols, "block slots fit the tensor memory");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
@@ -494,11 +438,11 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
     auto raw_empty = [&](int s) { return bar_base + 8u * (R + s); };
     auto conv_full = [&](int c) { return bar_base + 8u * (2 * R + c); };
     auto conv_empty = [&](int c) { return bar_base + 8u * (2 * R + C + c); };
-    auto acc_full = [&](int t) { return bar_base + 8u * (2 * R + 2 * C + t); };
-    auto acc_empty = [&](int t) { return bar_base + 8u * (2 * R + 2 * C + kQbSlots + t); };
-    const uint32_t recv_bar = bar_base + 8u * (2 * R + 2 * C + 2 * kQbSlots);
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 2 * R + 2 * C + 2 * kQbSlots + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * R + 2 * C + 2 * kQbSlots + 2);
+    auto acc_full = [&](int h) { return bar_base + 8u * (2 * R + 2 * C + h); };       // per half of the slots
+    auto acc_empty = [&](int h) { return bar_base + 8u * (2 * R + 2 * C + 2 + h); };
+    const uint32_t recv_bar = bar_base + 8u * (2 * R + 2 * C + 4);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 2 * R + 2 * C + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * R + 2 * C + 6);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int nc = p.splits * p.terms;
@@ -511,9 +455,7 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
     const float* scales = term ? p.scales[1] : p.scales[0];
     const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
     const uint64_t k1 = min(p.k, k0 + p.slice_len);
-    const int num_kb = k1 > k0 ? (int)((k1 - k0) / kQ8Chunk) : 0;  // raw stages (records)
-    const int num_groups = num_kb * (kQ8Chunk / kQbGroupK);
-    const int num_blocks = num_kb * (kQ8Chunk / 32);
+    const int num_kb = k1 > k0 ? (int)((k1 - k0) / kQ8Chunk) : 0;  // raw stages (record halves)
     const uint64_t rec0 = (n0 >> 8) * p.chunks + k0 / kQ8Chunk;  // this CTA's first record
     const uint64_t half = n0 & 255;
 
@@ -542,9 +484,9 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
             mbar_init(conv_full(c), 8);
             mbar_init(conv_empty(c), 1);
         }
-        for (int t = 0; t < kQbSlots; t++) {
-            mbar_init(acc_full(t), 1);
-            mbar_init(acc_empty(t), 4);  // the scaler warps
+        for (int h = 0; h < 2; h++) {
+            mbar_init(acc_full(h), 1);
+            mbar_init(acc_empty(h), 4);  // the scaler warps
         }
         mbar_init(recv_bar, 1);
         *abort_flag = 0;
@@ -585,159 +527,155 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---- MMA issuer: per 16 k, D[slot of the k's block] (+)= W (bf16) x [A_h; A_m; A_l]^T ----
+        // ---- MMA issuer: stage i's blocks 4i .. 4i + 3 into slot half i % 2, two MMAs per block:
+        //      D[slot] (+)= W (bf16) x [A_h; A_m; A_l]^T ------------------------------------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(kTcCols, kQbN);
-            for (int j = 0; j < num_groups; j++) {
-                const int c = j % C;
-                if (!mbar_wait(conv_full(c), (uint32_t)(j / C) & 1u) || *abort_flag) {
+            for (int i = 0; i < num_kb; i++) {
+                const int c = i % C, h = i % 2;
+                if (!mbar_wait(conv_full(c), (uint32_t)(i / C) & 1u) ||
+                    !mbar_wait(acc_empty(h), ((uint32_t)(i / 2) & 1u) ^ 1u) || *abort_flag) {
                     *abort_flag = 1;
                     atomicExch(p.error, 1);
                     break;
                 }
                 tc_fence_after();
                 const uint32_t cs = conv_stage(c);
-                bool ok = true;
 #pragma unroll
-                for (int kk = 0; kk < kQbGroupK / 16; kk++) {
-                    const int b = j * 2 + kk / 2, slot = b % kQbSlots;
-                    if (kk % 2 == 0) {
-                        if (!mbar_wait(acc_empty(slot), ((uint32_t)(b / kQbSlots) & 1u) ^ 1u)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                    }
-                    const uint64_t dw = desc_k_sw128(cs) + (uint64_t)((kk * 32) >> 4);
-                    const uint64_t da = desc_k_sw128(cs + S::kWTile) + (uint64_t)((kk * 32) >> 4);
-                    mma_bf16(tmem + (uint32_t)(slot * kQbN), dw, da, idesc, (uint32_t)(kk % 2));
-                    if (kk % 2 == 1) tc_commit(acc_full(slot));  // the block's sums are complete
+                for (int kk = 0; kk < kQ8Chunk / 16; kk++) {
+                    const uint32_t koff = (uint32_t)((kk % 4) * 32);  // within the 64-k atom column
+                    const uint64_t dw = desc_k_sw128(cs + (uint32_t)(kk / 4) * S::kWAtom + koff);
+                    const uint64_t da = desc_k_sw128(cs + S::kWTile + (uint32_t)(kk / 4) * S::kBAtom + koff);
+                    mma_bf16(tmem + (uint32_t)((4 * h + kk / 2) * kQbN), dw, da, idesc, (uint32_t)(kk % 2));
                 }
-                if (!ok) {
-                    *abort_flag = 1;
-                    atomicExch(p.error, 1);
-                    break;
-                }
-                tc_commit(conv_empty(c));
+                tc_commit(acc_full(h));    // the stage's four block sums are complete
+                tc_commit(conv_empty(c));  // and its conversion buffer is free
             }
         }
         __syncwarp();
     } else if (warp >= 6) {
-        // ---- converters (8 warps): quants -> bf16 weight tile, activations -> three bf16 terms ----
+        // ---- converters (8 warps): a whole raw stage per pass -----------------------------------
         const int t = threadIdx.x - 192;  // 0..255
         for (int i = 0; i < num_kb; i++) {
-            const int s = i % R;
+            const int s = i % R, c = i % C;
             bool ok = mbar_wait(raw_full(s), (uint32_t)(i / R) & 1u);
-            const uint32_t rs = raw_stage(s);
-            for (int g = 0; g < kQ8Chunk / kQbGroupK; g++) {
-                const int j = i * 2 + g, c = j % C;
-                ok = mbar_wait(conv_empty(c), ((uint32_t)(j / C) & 1u) ^ 1u) && ok;
-                if (!ok) {
-                    *abort_flag = 1;
-                    atomicExch(p.error, 1);
-                }
-                const uint32_t cs = conv_stage(c);
-                // weight row n = t % 128, half hp = t / 128 of the group: pieces 4g + 2hp, 4g + 2hp + 1
-                // of the record row (32 quants) -> bf16 chunks 4hp .. 4hp + 3
-                {
-                    const int n = t & 127, hp = t >> 7;
-                    uint4 q[2];
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const uint32_t piece = (uint32_t)((4 * g + 2 * hp + u) ^ (n & 7));
-                        q[u] = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
-                    }
-                    // two quants -> two bf16 exactly: 0x43 | q & 0x7F is 128 + (q & 0x7F), 0x43 | q & 0x80
-                    // is 128 or 256 by the sign bit; their difference is q
-                    auto wid2 = [](uint32_t w, uint32_t sel) {
-                        const uint32_t y = __byte_perm(w, 0x43u, sel);
-                        uint32_t r;
-                        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(y & 0xFF7FFF7Fu), "r"(y & 0xFF80FF80u));
-                        return r;
-                    };
-                    auto put = [&](uint32_t w0, uint32_t w1, int chunk) {
-                        const uint32_t off = (uint32_t)(n * 128 + ((chunk ^ (n & 7)) * 16));
-                        asm volatile("st.shared::cta.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cs + off),
-                                     "r"(wid2(w0, 0x4140u)), "r"(wid2(w0, 0x4342u)), "r"(wid2(w1, 0x4140u)),
-                                     "r"(wid2(w1, 0x4342u))
-                                     : "memory");
-                    };
-                    // 16 quants = k 16u' .. 16u' + 15 of the group (u' = 2hp + u): chunks 2u', 2u' + 1
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        put(q[u].x, q[u].y, 4 * hp + 2 * u);
-                        put(q[u].z, q[u].w, 4 * hp + 2 * u + 1);
-                    }
-                }
-                // activations: row m = t / 16, 4 k (f = t % 16: k 4f .. 4f + 3) of the group, from the
-                // raw [16][32] f32 box 2g + f / 8 (128-byte swizzle)
-                {
-                    const int m = t >> 4, f = t & 15, fi = f & 7;
-                    const uint32_t box = rs + S::kOffA + (uint32_t)((2 * g + f / 8) * kTcRows * kTcK * 4);
-                    const float4 x = lds4(box + (uint32_t)(m * 128 + ((fi ^ (m & 7)) * 16)));
-                    uint32_t th[2], tm[2], tl[2];
-                    auto terms3 = [&](float xa, float xb, int e) {
-                        const float ha = __uint_as_float(__float_as_uint(xa) & 0xFFFF0000u);  // truncated: no overflow
-                        const float hb = __uint_as_float(__float_as_uint(xb) & 0xFFFF0000u);
-                        const float ra = xa - ha, rb = xb - hb;
-                        const float ma = __bfloat162float(__float2bfloat16_rn(ra));
-                        const float mb2 = __bfloat162float(__float2bfloat16_rn(rb));
-                        th[e] = (__float_as_uint(ha) >> 16) | (__float_as_uint(hb) & 0xFFFF0000u);
-                        tm[e] = bf16x2_rn(ma, mb2);
-                        tl[e] = bf16x2_rn(ra - ma, rb - mb2);
-                    };
-                    terms3(x.x, x.y, 0);
-                    terms3(x.z, x.w, 1);
-                    const uint32_t bt = cs + S::kWTile;
-                    const uint32_t cc = (uint32_t)(f >> 1), hoff = (uint32_t)(f & 1) * 8;
-                    auto put_row = [&](uint32_t row, const uint32_t (&w)[2]) {
-                        const uint32_t off = row * 128 + ((cc ^ (row & 7)) * 16) + hoff;
-                        asm volatile("st.shared::cta.v2.b32 [%0], {%1, %2};" ::"r"(bt + off), "r"(w[0]), "r"(w[1])
-                                     : "memory");
-                    };
-                    put_row((uint32_t)m, th);
-                    put_row((uint32_t)(kTcRows + m), tm);
-                    put_row((uint32_t)(2 * kTcRows + m), tl);
-                }
-                fence_proxy_async();
-                mbar_arrive_warp(conv_full(c));
+            ok = mbar_wait(conv_empty(c), ((uint32_t)(i / C) & 1u) ^ 1u) && ok;
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.error, 1);
             }
+            const uint32_t rs = raw_stage(s), cs = conv_stage(c);
+            // activations first (their loads overlap the weight's): row m = t / 16, k 8f .. 8f + 7
+            // (f = t % 16) from the raw [16][32] f32 box f / 4 (128-byte swizzle) -> bf16 chunk f of
+            // the three term rows m, 16 + m, 32 + m
+            const int m = t >> 4, f = t & 15;
+            float4 x0, x1;
+            {
+                const uint32_t box = rs + S::kOffA + (uint32_t)((f >> 2) * kTcRows * kTcK * 4);
+                const int f0 = (f & 3) * 2;
+                x0 = lds4(box + (uint32_t)(m * 128 + ((f0 ^ (m & 7)) * 16)));
+                x1 = lds4(box + (uint32_t)(m * 128 + (((f0 + 1) ^ (m & 7)) * 16)));
+            }
+            // weight row n = t % 128, k half hp = t / 128 (64 quants, pieces 4hp .. 4hp + 3 of the
+            // record row) -> atom column hp of the converted tile
+            const int n = t & 127, hp = t >> 7;
+            uint4 q[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t piece = (uint32_t)((4 * hp + u) ^ (n & 7));
+                q[u] = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
+            }
+            {
+                uint32_t th[4], tm[4], tl[4];
+                auto terms3 = [&](float xa, float xb, int e) {
+                    const float ha = __uint_as_float(__float_as_uint(xa) & 0xFFFF0000u);  // truncated: no overflow
+                    const float hb = __uint_as_float(__float_as_uint(xb) & 0xFFFF0000u);
+                    const float ra = xa - ha, rb = xb - hb;
+                    const float ma = __bfloat162float(__float2bfloat16_rn(ra));
+                    const float mb2 = __bfloat162float(__float2bfloat16_rn(rb));
+                    th[e] = (__float_as_uint(ha) >> 16) | (__float_as_uint(hb) & 0xFFFF0000u);
+                    tm[e] = bf16x2_rn(ma, mb2);
+                    tl[e] = bf16x2_rn(ra - ma, rb - mb2);
+                };
+                terms3(x0.x, x0.y, 0);
+                terms3(x0.z, x0.w, 1);
+                terms3(x1.x, x1.y, 2);
+                terms3(x1.z, x1.w, 3);
+                const uint32_t bt = cs + S::kWTile + (uint32_t)(f >> 3) * S::kBAtom;
+                const uint32_t cc = (uint32_t)(f & 7);
+                auto put_row = [&](uint32_t row, const uint32_t (&w)[4]) {
+                    const uint32_t off = row * 128 + ((cc ^ (row & 7)) * 16);
+                    asm volatile("st.shared::cta.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(bt + off), "r"(w[0]),
+                                 "r"(w[1]), "r"(w[2]), "r"(w[3])
+                                 : "memory");
+                };
+                put_row((uint32_t)m, th);
+                put_row((uint32_t)(kTcRows + m), tm);
+                put_row((uint32_t)(2 * kTcRows + m), tl);
+            }
+            {
+                // two quants -> two bf16 exactly: 0x43 | q & 0x7F is 128 + (q & 0x7F), 0x43 | q & 0x80
+                // is 128 or 256 by the sign bit; their difference is q
+                auto wid2 = [](uint32_t w, uint32_t sel) {
+                    const uint32_t y = __byte_perm(w, 0x43u, sel);
+                    uint32_t r;
+                    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(y & 0xFF7FFF7Fu), "r"(y & 0xFF80FF80u));
+                    return r;
+                };
+                const uint32_t wt = cs + (uint32_t)hp * S::kWAtom;
+                auto put = [&](uint32_t w0, uint32_t w1, int chunk) {
+                    const uint32_t off = (uint32_t)(n * 128 + ((chunk ^ (n & 7)) * 16));
+                    asm volatile("st.shared::cta.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(wt + off),
+                                 "r"(wid2(w0, 0x4140u)), "r"(wid2(w0, 0x4342u)), "r"(wid2(w1, 0x4140u)),
+                                 "r"(wid2(w1, 0x4342u))
+                                 : "memory");
+                };
+                // 16 quants = k 16u .. 16u + 15 of the atom column: chunks 2u, 2u + 1
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    put(q[u].x, q[u].y, 2 * u);
+                    put(q[u].z, q[u].w, 2 * u + 1);
+                }
+            }
+            fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
+            mbar_arrive_warp(conv_full(c));
             mbar_arrive_warp(raw_empty(s));
             if (__any_sync(0xffffffffu, *abort_flag)) break;
         }
     } else {
-        // ---- warps 2..5: fold each finished block slot into registers: sum += scale * block ------
-        // A record's four scales per column are fetched one record ahead, so their load latency
-        // stays off the chain of slot waits.
+        // ---- warps 2..5: fold each stage's four block slots into registers: sum += scale * block --
+        // A stage's four scales per column are fetched one stage ahead, so their load latency stays
+        // off the chain of slot waits.
         const int q = warp % 4, n = q * 32 + lane;
         bool failed = false;
         auto scale4 = [&](int r) {
             return __ldg(reinterpret_cast<const float4*>(scales + ((rec0 + (uint64_t)r) * 256 + half + n) * 4));
         };
-        float4 sc_cur = make_float4(0.f, 0.f, 0.f, 0.f), sc_nxt = num_kb > 0 ? scale4(0) : sc_cur;
-        for (int b = 0; b < num_blocks; b++) {
-            const int slot = b % kQbSlots;
-            if (b % 4 == 0) {
-                sc_cur = sc_nxt;
-                if (b / 4 + 1 < num_kb) sc_nxt = scale4(b / 4 + 1);
-            }
-            if (!failed && !mbar_wait(acc_full(slot), (uint32_t)(b / kQbSlots) & 1u)) failed = true;
+        float4 sc_nxt = num_kb > 0 ? scale4(0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < num_kb; i++) {
+            const int h = i % 2;
+            const float4 sc = sc_nxt;
+            if (i + 1 < num_kb) sc_nxt = scale4(i + 1);
+            if (!failed && !mbar_wait(acc_full(h), (uint32_t)(i / 2) & 1u)) failed = true;
             failed = __any_sync(0xffffffffu, failed);
-            float v[kQbN];
             if (!failed) {
                 tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * kQbN);
-                tmem_ld16(ta, v);
-                tmem_ld16(ta + 16, v + 16);
-                tmem_ld16(ta + 32, v + 32);
-                tc_wait_ld();
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(4 * h * kQbN);
+#pragma unroll
+                for (int blk = 0; blk < 4; blk++) {
+                    float v[kQbN];
+                    tmem_ld16(ta + (uint32_t)(blk * kQbN), v);
+                    tmem_ld16(ta + (uint32_t)(blk * kQbN + 16), v + 16);
+                    tmem_ld16(ta + (uint32_t)(blk * kQbN + 32), v + 32);
+                    tc_wait_ld();
+                    const float scb = blk == 0 ? sc.x : blk == 1 ? sc.y : blk == 2 ? sc.z : sc.w;
+#pragma unroll
+                    for (int r = 0; r < kTcRows; r++)
+                        acc[r] = fmaf(scb, (v[r] + v[kTcRows + r]) + v[2 * kTcRows + r], acc[r]);
+                }
             }
             tc_fence_before();
-            mbar_arrive_warp(acc_empty(slot));
-            if (failed) continue;
-            const float sc = (b & 3) == 0 ? sc_cur.x : (b & 3) == 1 ? sc_cur.y : (b & 3) == 2 ? sc_cur.z : sc_cur.w;
-#pragma unroll
-            for (int r = 0; r < kTcRows; r++) acc[r] = fmaf(sc, (v[r] + v[kTcRows + r]) + v[2 * kTcRows + r], acc[r]);
+            mbar_arrive_warp(acc_empty(h));
         }
         if (failed) {
             *abort_flag = 1;
@@ -838,26 +776,26 @@ int env_min_rows(const char* name, int dflt) {
     const int x = atoi(e);
     return x <= 0 ? kTcRows + 1 : x;
 }
-// Defaults from measurement at N = K = 4096: packed Q8_0 at 16 rows takes 15 us here against 61 us
-// on the CUDA cores, at 8 rows 15 us against 19 us, one row 15 us against 8 us; f32 at 16 rows 26 us
-// against 21 us -- the f32 form stays off until its per-group pipeline is shorter.
+// Defaults from measurement at N = K = 4096 (six weights back to back): packed Q8_0 takes 11.5 -
+// 11.9 us here for 1 - 16 rows, on the CUDA cores 8.4 / 9.7 / 13.6 / 20.4 us for 1 / 2 / 4 / 6 rows
+// (61 us at 16); f32 at 16 rows 27 us here against 21 us on the CUDA cores -- the f32 form stays
+// off: its tf32 hi / lo terms pass through shared memory three times, which bounds it.
 int tc_min_rows() {
     static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC", kTcRows + 1);
     return v;
 }
 int tc_q8_min_rows() {
-    static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC_Q8", 8);
+    static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC_Q8", 3);
     return v;
 }
 
-template <bool Q8>
 mg_status launch_gemv_tc(Device* d, const k::GemmArgs& g) {
-    using S = TcGemvShape<Q8>;
-    auto kernel = gemv_tc_kernel<Q8>;
+    using S = TcGemvShape;
+    auto kernel = gemv_tc_kernel;
     const uint64_t col_tiles = (g.n + kTcCols - 1) / kTcCols;
     if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
     const int terms = g.gated ? 2 : 1;
-    constexpr uint64_t kStageK = (uint64_t)kTcK * S::kGroups;
+    constexpr uint64_t kStageK = (uint64_t)kTcK;
     const uint64_t kb = (g.k + kStageK - 1) / kStageK;
     uint64_t splits = (uint64_t)d->sm_count / (col_tiles * terms);
     if (splits > (uint64_t)(kMaxCluster / terms)) splits = kMaxCluster / terms;
@@ -872,18 +810,8 @@ mg_status launch_gemv_tc(Device* d, const k::GemmArgs& g) {
     p.n = g.n;
     p.k = g.k;
     p.terms = terms;
-    // A packed weight changes only by an upload, which synchronises: its loads may always start
-    // before the dependency wait.
-    p.b_early = Q8 || g.b_stable ? 1 : 0;
+    p.b_early = g.b_stable ? 1 : 0;
     p.error = d->flags + 2;
-    if constexpr (Q8) {
-        for (int t = 0; t < 2; t++) {
-            const Buffer* w = g.packed[t < terms ? t : 0];
-            p.quants[t] = static_cast<const int8_t*>(w->ptr);
-            p.scales[t] = w->q8_scales;
-        }
-        p.chunks = g.k / kQ8Chunk;
-    }
     auto set_splits = [&](uint64_t sp) {
         p.slice_len = ((kb + sp - 1) / sp) * kStageK;
         p.splits = (int)((g.k + p.slice_len - 1) / p.slice_len);
@@ -927,13 +855,9 @@ mg_status launch_gemv_tc(Device* d, const k::GemmArgs& g) {
     }
     CUtensorMap maps[3];
     MG_TRY(tc_gemv_map(&maps[0], g.a, g.m, g.k, kTcRows));
-    if constexpr (Q8) {
-        maps[1] = maps[2] = maps[0];  // B arrives by bulk copies
-    } else {
-        MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, kTcK, true));
-        if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, kTcK, true));
-        else maps[2] = maps[1];
-    }
+    MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, kTcK, true));
+    if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, kTcK, true));
+    else maps[2] = maps[1];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);
     cfg.blockDim = dim3(S::kThreads, 1, 1);
@@ -965,7 +889,7 @@ bool gemv_tc_eligible(const GemmArgs& g) {
 // (A compact weight takes this path too, reading its f32 values: its results stay bit-identical to
 // the same values stored as f32, which take it as well.)
 
-mg_status gemv_tc(Device* d, const GemmArgs& g) { return launch_gemv_tc<false>(d, g); }
+mg_status gemv_tc(Device* d, const GemmArgs& g) { return launch_gemv_tc(d, g); }
 
 // Every B a tiled packed Q8_0 weight (transposed storage, k a multiple of 128), A K-major with
 // 16-byte rows.
@@ -985,7 +909,7 @@ mg_status gemv_tc_q8(Device* d, const GemmArgs& g) {
     const int terms = g.gated ? 2 : 1;
     const uint64_t kb = g.k / kQ8Chunk;
     uint64_t splits = (uint64_t)d->sm_count / (col_tiles * terms);
-    if (splits > (uint64_t)(kMaxCluster / terms)) splits = kMaxCluster / terms;
+    if (splits > (uint64_t)(S::kMaxCluster / terms)) splits = S::kMaxCluster / terms;
     if (splits > kb) splits = kb;
     if (splits < 1) splits = 1;
     GemvTcArgs p;
