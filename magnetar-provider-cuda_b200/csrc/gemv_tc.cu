@@ -384,8 +384,10 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
 //
 // The unit of work is one raw stage, half a tiled record (128 columns x 128 k): it is converted
 // as a whole and its eight MMAs are issued together, so each stage costs one pass of barrier
-// hand-offs (raw -> converters -> MMA -> scalers).  Those hand-offs, not the arithmetic, set the
-// pace: every one is a chain of long-latency shared-memory and tensor-core operations.
+// hand-offs (raw -> converters -> MMA -> scalers).  The converted weight goes to tensor memory
+// (tcgen05.st), where the MMA reads it as its A operand: shared memory then carries only the raw
+// stage (written by the copy engine, read once by the converters) and the small activation tile,
+// not a second and third pass over the widened weight.
 constexpr int kQbSlots = 8;          // TMEM block slots of 48 columns: two stages' four blocks
 constexpr int kQbN = 3 * kTcRows;    // the MMA's N: three activation terms of 16 rows
 
@@ -395,13 +397,13 @@ struct QbShape {
     static constexpr int kOffA = kWRaw + kScales;
     static constexpr int kARaw = kTcRows * kTcK * 4 * 4;  // A's [16][128] as four [16][32] boxes
     static constexpr int kRawStage = kOffA + kARaw;       // 26 KB
-    static constexpr int kRawStages = 3;
-    // a converted stage: K-major, 128-byte swizzled, as two 64-k atom columns per operand
-    static constexpr int kWAtom = kTcCols * 128;          // [128 n][64 k] bf16: 16 KB
+    static constexpr int kRawStages = 4;
+    // a converted stage: the weight's [128 n][128 k] bf16 in tensor memory (64 columns), the three
+    // activation terms' [48][128] bf16 in shared memory, K-major, 128-byte swizzled, as two 64-k
+    // atom columns
     static constexpr int kBAtom = kQbN * 128;             // [48 rows][64 k] bf16: 6 KB
-    static constexpr int kWTile = 2 * kWAtom;
-    static constexpr int kConvStage = kWTile + 2 * kBAtom;  // 44 KB
-    static constexpr int kConvStages = 3;
+    static constexpr int kConvStage = 2 * kBAtom;
+    static constexpr int kConvStages = 2;
     static constexpr int kRing = kRawStages * kRawStage + kConvStages * kConvStage;
     static constexpr int kMaxCluster = 8;              // 8 CTAs' bands of 16 rows: at most 23 rows received
     static constexpr int kRecv = 24 * kTcCols * 4;
@@ -409,10 +411,12 @@ struct QbShape {
     static constexpr int kSmem = kRing + kRecv + kBars + 1024;
     static constexpr int kThreads = 448;  // producer, MMA, 4 scaler warps, 8 converter warps
     static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kWCol0 = 2 * 4 * kQbN;     // weight stages after the block slots: column 384
+    static constexpr uint32_t kWStageCols = kQ8Chunk / 2;  // 64
     static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0 && kBAtom % 1024 == 0,
                   "swizzle atoms aligned");
     static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
-    static_assert(kQbSlots * kQbN <= (int)kTmemCols, "block slots fit the tensor memory");
+    static_assert(kWCol0 + kConvStages * kWStageCols <= kTmemCols, "slots and weight stages fit the tensor memory");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
@@ -540,13 +544,13 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t cs = conv_stage(c);
+                const uint32_t cs = conv_stage(c), wt = tmem + S::kWCol0 + (uint32_t)c * S::kWStageCols;
 #pragma unroll
                 for (int kk = 0; kk < kQ8Chunk / 16; kk++) {
                     const uint32_t koff = (uint32_t)((kk % 4) * 32);  // within the 64-k atom column
-                    const uint64_t dw = desc_k_sw128(cs + (uint32_t)(kk / 4) * S::kWAtom + koff);
-                    const uint64_t da = desc_k_sw128(cs + S::kWTile + (uint32_t)(kk / 4) * S::kBAtom + koff);
-                    mma_bf16(tmem + (uint32_t)((4 * h + kk / 2) * kQbN), dw, da, idesc, (uint32_t)(kk % 2));
+                    const uint64_t da = desc_k_sw128(cs + (uint32_t)(kk / 4) * S::kBAtom + koff);
+                    mma_bf16_ts(tmem + (uint32_t)((4 * h + kk / 2) * kQbN), wt + (uint32_t)(8 * kk), da, idesc,
+                                (uint32_t)(kk % 2));
                 }
                 tc_commit(acc_full(h));    // the stage's four block sums are complete
                 tc_commit(conv_empty(c));  // and its conversion buffer is free
@@ -556,6 +560,8 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
     } else if (warp >= 6) {
         // ---- converters (8 warps): a whole raw stage per pass -----------------------------------
         const int t = threadIdx.x - 192;  // 0..255
+        // weight row n (a lane of this warp's quarter of the tensor memory), k half hp
+        const int n = (warp % 4) * 32 + lane, hp = (warp - 6) / 4;
         for (int i = 0; i < num_kb; i++) {
             const int s = i % R, c = i % C;
             bool ok = mbar_wait(raw_full(s), (uint32_t)(i / R) & 1u);
@@ -564,10 +570,10 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
                 *abort_flag = 1;
                 atomicExch(p.error, 1);
             }
+            tc_fence_after();  // the MMAs that read this stage's tensor-memory columns have completed
             const uint32_t rs = raw_stage(s), cs = conv_stage(c);
-            // activations first (their loads overlap the weight's): row m = t / 16, k 8f .. 8f + 7
-            // (f = t % 16) from the raw [16][32] f32 box f / 4 (128-byte swizzle) -> bf16 chunk f of
-            // the three term rows m, 16 + m, 32 + m
+            // activations: row m = t / 16, k 8f .. 8f + 7 (f = t % 16) from the raw [16][32] f32 box
+            // f / 4 (128-byte swizzle) -> bf16 chunk f of the three term rows m, 16 + m, 32 + m
             const int m = t >> 4, f = t & 15;
             float4 x0, x1;
             {
@@ -576,14 +582,12 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
                 x0 = lds4(box + (uint32_t)(m * 128 + ((f0 ^ (m & 7)) * 16)));
                 x1 = lds4(box + (uint32_t)(m * 128 + (((f0 + 1) ^ (m & 7)) * 16)));
             }
-            // weight row n = t % 128, k half hp = t / 128 (64 quants, pieces 4hp .. 4hp + 3 of the
-            // record row) -> atom column hp of the converted tile
-            const int n = t & 127, hp = t >> 7;
-            uint4 q[4];
+            // weight: 64 quants of row n (pieces 4hp .. 4hp + 3 of the record row, stored permuted)
+            uint4 qv[4];
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const uint32_t piece = (uint32_t)((4 * hp + u) ^ (n & 7));
-                q[u] = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
+                qv[u] = *reinterpret_cast<const uint4*>(base_ptr + (rs - base) + (uint32_t)n * kQ8Chunk + piece * 16);
             }
             {
                 uint32_t th[4], tm[4], tl[4];
@@ -601,7 +605,7 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
                 terms3(x0.z, x0.w, 1);
                 terms3(x1.x, x1.y, 2);
                 terms3(x1.z, x1.w, 3);
-                const uint32_t bt = cs + S::kWTile + (uint32_t)(f >> 3) * S::kBAtom;
+                const uint32_t bt = cs + (uint32_t)(f >> 3) * S::kBAtom;
                 const uint32_t cc = (uint32_t)(f & 7);
                 auto put_row = [&](uint32_t row, const uint32_t (&w)[4]) {
                     const uint32_t off = row * 128 + ((cc ^ (row & 7)) * 16);
@@ -622,22 +626,20 @@ __global__ void __launch_bounds__(QbShape::kThreads, 1)
                     asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(y & 0xFF7FFF7Fu), "r"(y & 0xFF80FF80u));
                     return r;
                 };
-                const uint32_t wt = cs + (uint32_t)hp * S::kWAtom;
-                auto put = [&](uint32_t w0, uint32_t w1, int chunk) {
-                    const uint32_t off = (uint32_t)(n * 128 + ((chunk ^ (n & 7)) * 16));
-                    asm volatile("st.shared::cta.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(wt + off),
-                                 "r"(wid2(w0, 0x4140u)), "r"(wid2(w0, 0x4342u)), "r"(wid2(w1, 0x4140u)),
-                                 "r"(wid2(w1, 0x4342u))
-                                 : "memory");
-                };
-                // 16 quants = k 16u .. 16u + 15 of the atom column: chunks 2u, 2u + 1
+                // k = 64hp + 16u + e of the stage -> column 32hp + 8u + e / 2 of its tensor-memory stage
+                const uint32_t wt = tmem + ((uint32_t)((warp % 4) * 32) << 16) + S::kWCol0 +
+                                    (uint32_t)c * S::kWStageCols + (uint32_t)(32 * hp);
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    put(q[u].x, q[u].y, 2 * u);
-                    put(q[u].z, q[u].w, 2 * u + 1);
+                    const uint32_t w[8] = {wid2(qv[u].x, 0x4140u), wid2(qv[u].x, 0x4342u), wid2(qv[u].y, 0x4140u),
+                                           wid2(qv[u].y, 0x4342u), wid2(qv[u].z, 0x4140u), wid2(qv[u].z, 0x4342u),
+                                           wid2(qv[u].w, 0x4140u), wid2(qv[u].w, 0x4342u)};
+                    tmem_st8(wt + (uint32_t)(8 * u), w);
                 }
             }
-            fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
+            tc_wait_st();
+            fence_proxy_async();  // the activation tile's generic-proxy writes become visible to the MMA
+            tc_fence_before();
             mbar_arrive_warp(conv_full(c));
             mbar_arrive_warp(raw_empty(s));
             if (__any_sync(0xffffffffu, *abort_flag)) break;
