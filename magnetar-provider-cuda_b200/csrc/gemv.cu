@@ -462,7 +462,14 @@ __device__ __forceinline__ float4 unpack4(uint64_t lo, uint64_t hi) {
 template <int M, bool H = false>
 struct GemvCShape {
     static constexpr bool kTrans = M >= 8;
-    static constexpr int kThreads = (kWarps + 1 + (kTrans ? 1 : 0)) * 32;
+    // Compute warps: eight along k (four k rows of a stage each) times kMW along the rows of A --
+    // at 16 rows two warps share each k slice, eight rows each, so twice the warps hide the latency
+    // of the loads and packed FMAs with half the accumulators per thread.
+    static constexpr int kMW = M >= 16 && !H ? 2 : 1;  // (the compact form measured slower with 2)
+    static constexpr int kCW = kWarps * kMW;
+    static constexpr int kQH = M / 4 / kMW;  // groups of four A rows per warp (row-pair form)
+    static_assert(kWarps * 4 == kChunkRows, "eight warps of four k rows cover a stage");
+    static constexpr int kThreads = (kCW + 1 + (kTrans ? 1 : 0)) * 32;
     // 16 rows hold 64 accumulator registers per thread: one CTA per SM (no spills) with a ring
     // twice as deep; fewer rows, two CTAs per SM.
     static constexpr int kMinBlocks = M >= 16 ? 1 : 2;
@@ -526,7 +533,7 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
     if (threadIdx.x == 0) {
         for (int s = 0; s < kCStages; s++) {
             mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), kWarps);
+            mbar_init(empty_bar(s), S::kCW);
             if (S::kTrans) mbar_init(at_bar(s), 1);
         }
         mbar_init(recv_bar, 1);
@@ -545,10 +552,11 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
 
     // Packed f32 accumulators of this thread's 4 columns: [row][column pair] below 8 rows,
     // [row pair][column] from 8 rows up.
-    uint64_t acc2[2 * M];
+    constexpr int kAcc = S::kTrans ? 8 * S::kQH : 2 * M;
+    uint64_t acc2[kAcc];
 #pragma unroll
-    for (int i = 0; i < 2 * M; i++) acc2[i] = 0ull;
-    if (S::kTrans && warp == kWarps + 1) {
+    for (int i = 0; i < kAcc; i++) acc2[i] = 0ull;
+    if (S::kTrans && warp == S::kCW + 1) {
         // ---- transposer: A [M][32] -> [32][M] per stage (lane = k) ---------------------------
         for (int c = 0; c < chunks; c++) {
             const int s = c % kCStages;
@@ -565,7 +573,7 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
             __syncwarp();
             if (lane == 0) mbar_arrive(at_bar(s));
         }
-    } else if (warp == kWarps) {
+    } else if (warp == S::kCW) {
         // ---- producer: keep the ring full -----------------------------------------------
         if (lane == 0) {
             for (int c = 0; c < chunks; c++) {
@@ -584,7 +592,7 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
             }
         }
         __syncwarp();
-    } else if (warp < kWarps) {
+    } else if (warp < S::kCW) {
         for (int c = 0; c < chunks; c++) {
             const int s = c % kCStages;
             const uint32_t ph = (uint32_t)(c / kCStages) & 1u;
@@ -593,7 +601,8 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
                 break;
             }
             const uint8_t* tile = base_ptr + s * S::kStage;
-            const int rr = warp * 4;  // this warp's 4 rows of the stage
+            const int rr = (warp % kWarps) * 4;  // this warp's k rows of the stage
+            const int rh = warp / kWarps;         // and its share of A's rows
             if constexpr (S::kTrans) {
                 const float* att = atf + s * kChunkRows * M;  // [32][M]
 #pragma unroll
@@ -601,8 +610,8 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
                     const float4 bv = gemv_b4<H>(tile, rr + u, lane);
                     const uint64_t bd[4] = {pack2(bv.x, bv.x), pack2(bv.y, bv.y), pack2(bv.z, bv.z), pack2(bv.w, bv.w)};
 #pragma unroll
-                    for (int q = 0; q < M / 4; q++) {
-                        const float4 a4 = *reinterpret_cast<const float4*>(att + (rr + u) * M + 4 * q);
+                    for (int q = 0; q < S::kQH; q++) {
+                        const float4 a4 = *reinterpret_cast<const float4*>(att + (rr + u) * M + 4 * (rh * S::kQH + q));
                         const uint64_t a01 = pack2(a4.x, a4.y), a23 = pack2(a4.z, a4.w);
 #pragma unroll
                         for (int cc = 0; cc < 4; cc++) {
@@ -637,17 +646,19 @@ __global__ void __launch_bounds__(GemvCShape<M, H>::kThreads, GemvCShape<M, H>::
     }
     // ---- this CTA's partial: the warps' sums in warp order, through the drained ring ----------
     __syncthreads();
-    float* red = reinterpret_cast<float*>(base_ptr);  // [kWarps][M][128]
-    if (warp < kWarps) {
+    float* red = reinterpret_cast<float*>(base_ptr);  // [k warps][M][128]
+    if (warp < S::kCW) {
         if constexpr (S::kTrans) {
+            // acc2[q * 4 + cc] holds rows 2q, 2q + 1 of this warp's share, column cc
+            const int kw = warp % kWarps, r0 = (warp / kWarps) * 4 * S::kQH;
 #pragma unroll
-            for (int q = 0; q < M / 2; q++) {
+            for (int q = 0; q < 2 * S::kQH; q++) {
                 float lo[4], hi[4];
 #pragma unroll
                 for (int cc = 0; cc < 4; cc++)
                     asm("mov.b64 {%0, %1}, %2;" : "=f"(lo[cc]), "=f"(hi[cc]) : "l"(acc2[q * 4 + cc]));
-                *reinterpret_cast<float4*>(red + (warp * M + 2 * q) * kCols + 4 * lane) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-                *reinterpret_cast<float4*>(red + (warp * M + 2 * q + 1) * kCols + 4 * lane) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(red + (kw * M + r0 + 2 * q) * kCols + 4 * lane) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<float4*>(red + (kw * M + r0 + 2 * q + 1) * kCols + 4 * lane) = make_float4(hi[0], hi[1], hi[2], hi[3]);
             }
         } else {
 #pragma unroll
