@@ -187,10 +187,11 @@ template <int BN, int NB, int STAGES, bool A_RAW, int SPLIT, bool B_RAW = false>
 struct TcShape {
     static constexpr int kATile = BM * BK * 4;  // bytes of one A term tile
     static constexpr int kBTile = BN * BK * 4;  // bytes of one B term tile
-    // B_RAW: TMA brings B's raw f32 [BK][BN] tile (N-major, as B lies in memory) behind the B
-    // terms, and the converter warps split and transpose it into the K-major hi / lo terms.
-    static constexpr int kOffBRaw = 2 * kATile + NB * 2 * kBTile;
-    static constexpr int kStage = kOffBRaw + (B_RAW ? kBTile : 0);
+    // B_RAW: TMA brings B's raw f32 [BK][BN] tile MN-major, as B lies in memory (boxes of
+    // [32 k][32 n], 128-byte rows swizzled in 32-byte granules: the MMA's MN-major layout for
+    // 32-bit operands), into the B hi slot; the converter warps split it element by element, hi
+    // in place and lo into the lo slot at the same offsets -- no transpose.
+    static constexpr int kStage = 2 * kATile + NB * 2 * kBTile;
     static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + (B_RAW ? kBTile : NB * 2 * kBTile);  // TMA bytes per stage
     static_assert(!B_RAW || NB == 1, "raw B is for plain matmuls");
     static constexpr int kRing = STAGES * kStage;
@@ -204,8 +205,13 @@ struct TcShape {
     static_assert(SPLIT != kSplitRingRecv || kStaged + kRecvBytes <= kRing, "receive slots fit the drained ring");
     static constexpr int kRecv = SPLIT == kSplitOwnRecv ? kRecvBytes : 0;
     static constexpr int kSmem = kRing + kBars + kRecv + 1024 /* align */;
+    // Tensor memory: the accumulators, then (raw A) each stage's A hi and lo terms, which the
+    // converters store there and the MMAs read as their A operand.
+    static constexpr int kTmemAcc = NB * BN;
+    static constexpr int kTmemUsed = kTmemAcc + (A_RAW ? STAGES * 2 * BK : 0);
+    static_assert(kTmemUsed <= 512, "accumulators and A terms fit the tensor memory");
     static constexpr uint32_t kTmemCols =
-        NB * BN <= 32 ? 32 : NB * BN <= 64 ? 64 : NB * BN <= 128 ? 128 : NB * BN <= 256 ? 256 : 512;
+        kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128 : kTmemUsed <= 256 ? 256 : 512;
     static constexpr int kThreads = (A_RAW || B_RAW) ? 320 : 192;
 };
 
@@ -281,7 +287,9 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         mbar_arrive_expect_tx(full_bar(s), S::kTxBytes - (B_RAW || p.b_terms == 2 ? 0 : NB * S::kBTile));
         const int kx = (kb0 + i) * BK;
         if (B_RAW) {
-            tma_load_2d(st + S::kOffBRaw, map_whi, full_bar(s), n0, kx);  // [BK rows of k][BN columns]
+#pragma unroll
+            for (int j = 0; j < BN / 32; j++)  // [BK rows of k][32 columns] per box
+                tma_load_2d(st + 2 * S::kATile + (uint32_t)(j * 32 * BK * 4), map_whi, full_bar(s), n0 + 32 * j, kx);
             return;
         }
         tma_load_2d(st + 2 * S::kATile, map_whi, full_bar(s), kx, n0);
@@ -303,7 +311,8 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         if (!p.prefetch || i >= num_kb) return;
         const int kx = (kb0 + i) * BK;
         if (B_RAW) {
-            tma_prefetch_2d(map_whi, n0, kx);
+#pragma unroll
+            for (int j = 0; j < BN / 32; j++) tma_prefetch_2d(map_whi, n0 + 32 * j, kx);
         } else {
             tma_prefetch_2d(map_whi, kx, n0);
             if (p.b_terms == 2) tma_prefetch_2d(map_wlo, kx, n0);
@@ -358,7 +367,6 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
             if (!p.b_early) issue_b(i);
             issue_a(i);
         }
-        for (int i = STAGES; i < 2 * STAGES; i++) prefetch(i);
     }
     tc_fence_before();
     __syncthreads();
@@ -369,6 +377,11 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------------
         if (lane == 0) {
+            // The next ring's worth of tiles goes to the L2 once the first stage has landed: issued
+            // with the first stages, these prefetches would compete with them for HBM and delay
+            // the start of the main loop.
+            if (p.prefetch && num_kb > STAGES && mbar_wait(full_bar(0), 0))
+                for (int i = STAGES; i < 2 * STAGES; i++) prefetch(i);
             for (int i = STAGES; i < num_kb; i++) {
                 const int s = i % STAGES;
                 const uint32_t phase = (uint32_t)(i / STAGES) & 1u;
@@ -386,7 +399,8 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
     } else if (warp == 1) {
         // ---- MMA issuer ----------------------------------------------------------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(BM, BN);
+            // raw B is MN-major (bit 16: B transposed)
+            constexpr uint32_t idesc = idesc_tf32(BM, BN) | (B_RAW ? (1u << 16) : 0u);
             const bool two_b = B_RAW || p.b_terms == 2;
             bool ok = true;
             for (int i = 0; i < num_kb; i++) {
@@ -405,18 +419,31 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                 tc_fence_after();
                 const uint32_t st = base + s * S::kStage;
                 const uint64_t ahi = desc_k_sw128(st), alo = desc_k_sw128(st + S::kATile);
+                const uint32_t ta = tmem + (uint32_t)(S::kTmemAcc + s * 2 * BK);  // raw A: hi, then lo
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; kk++) {
                     const uint64_t koff = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes
 #pragma unroll
                     for (int z = 0; z < NB; z++) {
                         const uint32_t bt = st + 2 * S::kATile + z * 2 * S::kBTile;
-                        const uint64_t bhi = desc_k_sw128(bt), blo = desc_k_sw128(bt + S::kBTile);
+                        // K-major terms advance 32 bytes per 8 k; MN-major raw B 8 rows (1 KB), its
+                        // 32-column chunks 4 KB apart
+                        const uint64_t bhi = B_RAW ? desc_mn_sw128_32b(bt + (uint32_t)(kk * 1024), 32 * BK * 4)
+                                                   : desc_k_sw128(bt) + koff;
+                        const uint64_t blo = B_RAW ? desc_mn_sw128_32b(bt + S::kBTile + (uint32_t)(kk * 1024), 32 * BK * 4)
+                                                   : desc_k_sw128(bt + S::kBTile) + koff;
                         const uint32_t d = tmem + (uint32_t)(z * BN);
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                        mma_tf32(d, alo + koff, bhi + koff, idesc, acc);
-                        if (two_b) mma_tf32(d, ahi + koff, blo + koff, idesc, 1u);
-                        mma_tf32(d, ahi + koff, bhi + koff, idesc, 1u);
+                        if (A_RAW) {
+                            const uint32_t ah = ta + (uint32_t)(kk * 8), al = ah + BK;
+                            mma_tf32_ts(d, al, bhi, idesc, acc);
+                            if (two_b) mma_tf32_ts(d, ah, blo, idesc, 1u);
+                            mma_tf32_ts(d, ah, bhi, idesc, 1u);
+                        } else {
+                            mma_tf32(d, alo + koff, bhi, idesc, acc);
+                            if (two_b) mma_tf32(d, ahi + koff, blo, idesc, 1u);
+                            mma_tf32(d, ahi + koff, bhi, idesc, 1u);
+                        }
                     }
                 }
                 tc_commit(empty_bar(s));  // frees the stage once these MMAs have read it
@@ -440,35 +467,43 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                 }
                 const uint32_t st = base + s * S::kStage;
                 if (A_RAW) {
+                    // Row m of the raw A tile (this warp's lane quarter of the tensor memory), k half
+                    // hp: its 16 values split into hi / lo and stored to the stage's A columns.  The
+                    // MMAs that read these columns before have completed: the producer reloaded the
+                    // stage only after they released it.
+                    tc_fence_after();
+                    const int q = warp % 4, hp = (warp - 2) / 4;
+                    const int m = q * 32 + lane;
+                    uint32_t hv[16], lv[16];
 #pragma unroll
-                    for (int j = 0; j < S::kATile / 16 / kConvThreads; j++) {
-                        const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
+                    for (int c = 0; c < 4; c++) {
+                        const int chunk = 4 * hp + c;  // 16-byte chunk of the 128-byte row, swizzled
                         float4 h, l;
-                        split4_fast(lds4(st + off), h, l);
-                        sts4(st + off, h.x, h.y, h.z, h.w);
-                        sts4(st + S::kATile + off, l.x, l.y, l.z, l.w);
+                        split4_fast(lds4(st + (uint32_t)(m * 128 + ((chunk ^ (m & 7)) * 16))), h, l);
+                        hv[4 * c] = __float_as_uint(h.x), hv[4 * c + 1] = __float_as_uint(h.y);
+                        hv[4 * c + 2] = __float_as_uint(h.z), hv[4 * c + 3] = __float_as_uint(h.w);
+                        lv[4 * c] = __float_as_uint(l.x), lv[4 * c + 1] = __float_as_uint(l.y);
+                        lv[4 * c + 2] = __float_as_uint(l.z), lv[4 * c + 3] = __float_as_uint(l.w);
                     }
+                    const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(S::kTmemAcc + s * 2 * BK + 16 * hp);
+                    tmem_st16(ta, hv);
+                    tmem_st16(ta + BK, lv);
                 }
                 if (B_RAW) {
-                    // Column n of the raw tile (BK values of k, BN floats apart) becomes row n of
-                    // the K-major terms: 16-byte chunk c (k = 4c .. 4c+3) at byte
-                    // n * 128 + (c ^ (n % 8)) * 16, the layout TMA's 128-byte swizzle gives.
-                    const float* raw = reinterpret_cast<const float*>(base_ptr + s * S::kStage + S::kOffBRaw);
+                    // element by element: hi in place, lo at the same offset of the lo slot
                     const uint32_t b_hi = st + 2 * S::kATile, b_lo = b_hi + S::kBTile;
 #pragma unroll
-                    for (int j = 0; j < BN * (BK / 4) / kConvThreads; j++) {
-                        const int task = t + j * kConvThreads;
-                        const int n = task % BN, c = task / BN;
-                        const float4 x = make_float4(raw[(4 * c) * BN + n], raw[(4 * c + 1) * BN + n],
-                                                     raw[(4 * c + 2) * BN + n], raw[(4 * c + 3) * BN + n]);
+                    for (int j = 0; j < S::kBTile / 16 / kConvThreads; j++) {
+                        const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
                         float4 h, l;
-                        split4_fast(x, h, l);
-                        const uint32_t off = (uint32_t)(n * 128 + ((c ^ (n & 7)) * 16));
+                        split4_fast(lds4(b_hi + off), h, l);
                         sts4(b_hi + off, h.x, h.y, h.z, h.w);
                         sts4(b_lo + off, l.x, l.y, l.z, l.w);
                     }
                 }
-                fence_proxy_async();  // make the generic-proxy writes visible to tcgen05.mma
+                if (A_RAW) tc_wait_st();  // the A terms are in the tensor memory
+                fence_proxy_async();      // make the generic-proxy writes visible to tcgen05.mma
+                tc_fence_before();
                 mbar_arrive_warp(conv_bar(s));
                 if (__any_sync(0xffffffffu, *abort_flag)) break;
             }
@@ -648,17 +683,17 @@ mg_status make_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t c
     return MG_OK;
 }
 
-// B as it lies in memory, row-major [k, n] f32: box [BK rows x box_cols], no swizzle; rows and
-// columns past the end read as zero.
-mg_status make_raw_b_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n, uint32_t box_cols) {
+// B as it lies in memory, row-major [k, n] f32 (the MN-major operand): box [BK rows x 32 columns],
+// 128-byte rows swizzled in 32-byte granules; rows and columns past the end read as zero.
+mg_status make_raw_b_map(CUtensorMap* map, const float* b, uint64_t k, uint64_t n) {
     auto fn = encode_fn();
     if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
     cuuint64_t dims[2] = {n, k};
     cuuint64_t strides[1] = {n * sizeof(float)};
-    cuuint32_t box[2] = {box_cols, BK};
+    cuuint32_t box[2] = {32, BK};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(b), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
     return MG_OK;
@@ -779,19 +814,24 @@ mg_status launch_bn(Device* d, int bn, const TcParams& p, const CUtensorMap* map
     }
 }
 
-// Raw B: the ring holds B's raw tile as well, so it is shallower; with split k the partials
-// are received in the drained ring.
+// Raw B: its raw tile lands in the B hi slot, so the stage has the size of the terms' stage and
+// the ring the same depth.
 template <bool A_RAW>
 mg_status launch_bn_raw_b(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
-    const bool split = p.splits > 1;
-    if (bn == 128)
-        return split ? launch_tc<128, 1, 2, A_RAW, kSplitRingRecv, true>(d, p, maps)
-                     : launch_tc<128, 1, 2, A_RAW, kNoSplit, true>(d, p, maps);
-    if (bn == 64)
-        return split ? launch_tc<64, 1, 3, A_RAW, kSplitRingRecv, true>(d, p, maps)
-                     : launch_tc<64, 1, 3, A_RAW, kNoSplit, true>(d, p, maps);
-    return split ? launch_tc<32, 1, 4, A_RAW, kSplitRingRecv, true>(d, p, maps)
-                 : launch_tc<32, 1, 4, A_RAW, kNoSplit, true>(d, p, maps);
+    const int mode = p.splits <= 1 ? kNoSplit : p.kb_per_split < 8 ? kSplitOwnRecv : kSplitRingRecv;
+    if (bn == 128) {
+        if (mode == kNoSplit) return launch_tc<128, 1, 3, A_RAW, kNoSplit, true>(d, p, maps);
+        if (mode == kSplitOwnRecv) return launch_tc<128, 1, 2, A_RAW, kSplitOwnRecv, true>(d, p, maps);
+        return launch_tc<128, 1, 3, A_RAW, kSplitRingRecv, true>(d, p, maps);
+    }
+    if (bn == 64) {
+        if (mode == kNoSplit) return launch_tc<64, 1, 4, A_RAW, kNoSplit, true>(d, p, maps);
+        if (mode == kSplitOwnRecv) return launch_tc<64, 1, 3, A_RAW, kSplitOwnRecv, true>(d, p, maps);
+        return launch_tc<64, 1, 4, A_RAW, kSplitRingRecv, true>(d, p, maps);
+    }
+    if (mode == kNoSplit) return launch_tc<32, 1, 5, A_RAW, kNoSplit, true>(d, p, maps);
+    if (mode == kSplitOwnRecv) return launch_tc<32, 1, 4, A_RAW, kSplitOwnRecv, true>(d, p, maps);
+    return launch_tc<32, 1, 5, A_RAW, kSplitRingRecv, true>(d, p, maps);
 }
 
 // k splits per tile at most (MAGNETAR_CUDA_GEMM_MAX_SPLITS, 2..16): the CTAs of one cluster,
@@ -850,14 +890,19 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
         ahi = a_split;
         alo = a_split + g.m * kp;
     }
-    // B raw (split and transposed in the kernel, no separate pass over B): for a plain matmul
-    // with one row of tiles (M <= 128) whose B has no prepared form.  Measured at K = N = 4096:
-    // M = 128 takes 64 us against 97 us with the split pass; with more rows of tiles, or a
-    // prepared weight, the shallower ring it needs costs more than it saves (M = 2048: 0.62 vs
-    // 0.39 ms; a prepared weight at M = 128: 64 vs 43 us).
-    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-    const bool b_raw = count == 1 && nb == 1 && !g.transpose_b && g.n % 4 == 0 && al16(g.b) &&
-                       g.b_prep[0] == nullptr && g.m <= 128;
+    // B raw (split in the kernel, no separate pass over B): for a plain matmul with one row of
+    // tiles (M <= 128) whose B has no prepared form.  Its tiles arrive MN-major as B lies, the MMA
+    // reads them so, and the converters split each element in place (hi) and beside it (lo).
+    // Measured at K = N = 4096, M = 128: 34.5 us against 44.7 us with a split pass.  A prepared
+    // weight keeps its hi / lo form (32.8 us; raw, MAGNETAR_CUDA_GEMM_RAW_WEIGHTS=1: 34.4 us --
+    // the main loop is bound by the 3xTF32 MMAs either way, and the converters' extra pass costs
+    // more than the halved weight traffic saves).
+    static const bool raw_weights = [] {
+        const char* e = getenv("MAGNETAR_CUDA_GEMM_RAW_WEIGHTS");
+        return e && atoi(e) != 0;
+    }();
+    const bool b_raw = count == 1 && nb == 1 && !g.transpose_b && g.n % 4 == 0 && al16(g.b) && !g.packed[0] &&
+                       (g.b_prep[0] == nullptr || raw_weights) && g.m <= 128;
     // B terms: [term or weight] -> hi, lo ([n, kp] each)
     const int nw = nb == 2 ? 2 : count;
     const float* bhi[3];
@@ -939,7 +984,7 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
     }
     for (int w = 0; w < 3; w++) {
         if (b_raw) {
-            if (w == 0) MG_TRY(make_raw_b_map(&maps[2], g.b, g.k, g.n, (uint32_t)bn));
+            if (w == 0) MG_TRY(make_raw_b_map(&maps[2], g.b, g.k, g.n));
             else maps[2 + 2 * w] = maps[2];
             maps[3 + 2 * w] = maps[2];
         } else if (w < nw) {

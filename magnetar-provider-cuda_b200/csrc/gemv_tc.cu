@@ -85,20 +85,6 @@ struct GemvTcArgs {
     int* error;
 };
 
-// Shared-memory descriptor of an MN-major tf32 operand.  For 32-bit elements in MN-major order
-// the MMA takes one layout only: 128-byte rows (32 consecutive values of the M dimension, one row
-// per k) swizzled in 32-byte granules -- granule g of row r at position g ^ (r % 4), the pattern
-// of TMA's 128B_ATOM_32B mode -- four rows per 512-byte atom (SBO between atoms along k), the next
-// 32 of M `lbo` bytes further; layout type SWIZZLE_128B_BASE32B (1).
-__device__ __forceinline__ uint64_t desc_mn_sw128_32b(uint32_t saddr, uint32_t lbo) {
-    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)(512 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)1 << 61;
-    return d;
-}
-
 __device__ __forceinline__ float tf32_rna(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));

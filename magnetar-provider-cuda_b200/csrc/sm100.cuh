@@ -209,6 +209,28 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::tf32, one thread; A's M rows in the lanes, one
+// 32-bit value per column along K.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane from registers (warp-collective).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
 // 8 consecutive 32-bit columns of this thread's TMEM lane from registers (warp-collective; a
 // warp reaches the 32 lanes of its quarter, warp % 4).
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
@@ -253,6 +275,20 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
     d |= (uint64_t)(1024 >> 4) << 32;
     d |= (uint64_t)1 << 46;
     d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Shared-memory descriptor of an MN-major tf32 operand.  For 32-bit elements in MN-major order
+// the MMA takes one layout only: 128-byte rows (32 consecutive values of the M dimension, one row
+// per k) swizzled in 32-byte granules -- granule g of row r at position g ^ (r % 4), the pattern
+// of TMA's 128B_ATOM_32B mode -- four rows per 512-byte atom (SBO between atoms along k), the next
+// 32 of M `lbo` bytes further; layout type SWIZZLE_128B_BASE32B (1).
+__device__ __forceinline__ uint64_t desc_mn_sw128_32b(uint32_t saddr, uint32_t lbo) {
+    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)1 << 61;
     return d;
 }
 
