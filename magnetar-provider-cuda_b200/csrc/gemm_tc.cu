@@ -897,6 +897,7 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
     // weight keeps its hi / lo form (32.8 us; raw, MAGNETAR_CUDA_GEMM_RAW_WEIGHTS=1: 34.4 us --
     // the main loop is bound by the 3xTF32 MMAs either way, and the converters' extra pass costs
     // more than the halved weight traffic saves).
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     static const bool raw_weights = [] {
         const char* e = getenv("MAGNETAR_CUDA_GEMM_RAW_WEIGHTS");
         return e && atoi(e) != 0;
