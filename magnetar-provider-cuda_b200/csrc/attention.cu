@@ -849,9 +849,10 @@ __device__ void combine_head(const DecodeP& p, uint64_t h, float* wts, uint64_t 
 }
 
 // One span of keys of one KV head set; attention_combine_kernel merges the spans.  (Merging in
-// the set's last CTA instead, one launch, measured slower: 0.057 -> 0.068 ms at 32768 keys,
-// since that CTA then combines its G heads one after another while the combine kernel spreads
-// the heads over CTAs.)
+// the set's last CTA instead, one launch, measured slower: 0.057 -> 0.068 ms at 32768 keys with
+// that CTA combining its G heads one after another, 0.056 -> 0.060 ms with all its threads
+// spread over the G heads' columns: the merge then runs after the slowest span's CTA, on one SM
+// per head set, while the combine kernel is already resident and spreads the heads over CTAs.)
 template <int G, int C>
 __global__ void __launch_bounds__(kDecodeThreads) attention_decode_tma_kernel(const __grid_constant__ CUtensorMap map_k,
                                                                              const __grid_constant__ CUtensorMap map_v,
