@@ -197,19 +197,23 @@ __global__ void __launch_bounds__(256) attention_generic_kernel(AttnP p) {
 
 // ---- short key spans: the whole span resident in shared memory ------------------------------
 // When every CTA's admitted keys fit in shared memory (a short sequence, or a short window),
-// the softmax needs no online merge: a CTA of 256 threads serves kShortQ queries of one head,
-// copies the span of K and V once (cp.async), then
-//   1. scores: one thread per key, kShortQ dot products against the broadcast Q rows;
-//   2. one warp per query row: max, exp, sum, and the weights divided by the sum -- the
+// the softmax needs no online merge: a CTA of 256 threads serves kShortQ queries of one head and
+// copies the span of K and V once (cp.async); then each warp takes one query row on its own, with
+// no further CTA-wide barrier:
+//   1. scores: lane u takes keys u, u + 32, ... of the span (its K rows read as 16-byte chunks,
+//      the query row held in registers or read as broadcasts);
+//   2. the row's max, exp, sum and the weights divided by the sum, by warp shuffles -- the
 //      reference's order (src/kernels.cu:1899-1958) -- masked keys weigh exactly 0;
-//   3. P.V: one thread per output column and kShortQ * D / 256 queries.
+//   3. P.V: lane u owns output columns D / 32 * u .. + D / 32 - 1; each key's weight comes from
+//      the lane that holds it by a shuffle, its V row from shared memory.
 // This launches one kernel with ceil(S / 8) * H CTAs and no split pass, so a decoder layer's
 // attention (S = 128) is one short kernel instead of a tensor-core pipeline that would keep
 // only H CTAs busy.
 constexpr int kShortQ = 8;
 constexpr int kShortThreads = 256;
+static_assert(kShortThreads / 32 == kShortQ, "one warp per query row");
 
-// Key capacity limit per head dimension (shared memory: about 560 B a key at D = 64).
+// Key capacity limit per head dimension (shared memory: about 400 B a key at D = 64).
 template <int D>
 constexpr uint32_t short_cap_limit() {
     return D <= 32 ? 512 : D <= 64 ? 384 : 192;
@@ -223,25 +227,26 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Shared-memory plan for `cap` keys: K rows padded to D + 4 floats (an odd number of 16-byte
-// chunks, so one thread per key reads conflict-free), V rows dense, Q, and P [kShortQ][cap].
+// chunks, so a lane per key reads conflict-free), V rows dense, then Q.
 template <int D>
 struct ShortPlan {
     static constexpr int kKStride = D + 4;
     __host__ __device__ static uint32_t off_v(uint32_t cap) { return cap * kKStride * 4; }
     __host__ __device__ static uint32_t off_q(uint32_t cap) { return off_v(cap) + cap * D * 4; }
-    __host__ __device__ static uint32_t off_p(uint32_t cap) { return off_q(cap) + kShortQ * D * 4; }
-    __host__ __device__ static uint32_t bytes(uint32_t cap) { return off_p(cap) + kShortQ * cap * 4; }
+    __host__ __device__ static uint32_t bytes(uint32_t cap) { return off_q(cap) + kShortQ * D * 4; }
 };
 
 template <int D>
 __global__ void __launch_bounds__(kShortThreads) attention_short_kernel(AttnP p, uint32_t cap, int* error) {
     pdl_enter();
     using P = ShortPlan<D>;
+    constexpr int kT = (int)(short_cap_limit<D>() / 32);  // keys per lane at most
+    constexpr int C = D / 32;                              // output columns per lane
+    constexpr bool kQRegs = D <= 64;                       // the query row in registers
     extern __shared__ __align__(16) unsigned char smem[];
     float* ks = reinterpret_cast<float*>(smem);
     float* vs = reinterpret_cast<float*>(smem + P::off_v(cap));
     float* qs = reinterpret_cast<float*>(smem + P::off_q(cap));
-    float* ps = reinterpret_cast<float*>(smem + P::off_p(cap));
     const float ninf = __int_as_float(0xff800000);
     const uint64_t head = blockIdx.y, kvh = head / p.group;
     const uint64_t q0 = (uint64_t)blockIdx.x * kShortQ;
@@ -273,85 +278,84 @@ __global__ void __launch_bounds__(kShortThreads) attention_short_kernel(AttnP p,
     cp_async_wait_all();
     __syncthreads();
 
-    // 1. scores (masked keys -inf), one key per thread
-    uint64_t qlo[kShortQ], qhi[kShortQ];
+    const int qi = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (qi >= nq) return;
+    uint64_t qlo, qhi;
+    key_range(p, p.qpos0 + q0 + qi, qlo, qhi);
+    const float* qrow = qs + qi * D;
+    float4 qr[kQRegs ? C4 : 1];
+    if constexpr (kQRegs) {
 #pragma unroll
-    for (int qi = 0; qi < kShortQ; qi++) {
-        key_range(p, p.qpos0 + q0 + qi, qlo[qi], qhi[qi]);
-        if (qi >= nq) qlo[qi] = qhi[qi] = 0;
+        for (int c = 0; c < C4; c++) qr[c] = reinterpret_cast<const float4*>(qrow)[c];
     }
-    for (int j = threadIdx.x; j < n; j += kShortThreads) {
-        float acc[kShortQ];
+    // 1. scores of this lane's keys (masked: -inf)
+    float sc[kT];
+    float m = ninf;
 #pragma unroll
-        for (int qi = 0; qi < kShortQ; qi++) acc[qi] = 0.0f;
-        const float4* kr = reinterpret_cast<const float4*>(ks + j * P::kKStride);
-#pragma unroll 4
-        for (int c = 0; c < C4; c++) {
-            const float4 kk = kr[c];
+    for (int t = 0; t < kT; t++) {
+        sc[t] = ninf;
+        const int j = 32 * t + lane;
+        if (32 * t >= n) continue;
+        if (j < n) {
+            const float4* kr = reinterpret_cast<const float4*>(ks + j * P::kKStride);
+            float acc = 0.0f;
 #pragma unroll
-            for (int qi = 0; qi < kShortQ; qi++) {
-                const float4 qq = reinterpret_cast<const float4*>(qs + qi * D)[c];
-                acc[qi] += qq.x * kk.x + qq.y * kk.y + qq.z * kk.z + qq.w * kk.w;
+            for (int c = 0; c < C4; c++) {
+                const float4 kk = kr[c];
+                const float4 qq = kQRegs ? qr[kQRegs ? c : 0] : reinterpret_cast<const float4*>(qrow)[c];
+                acc += qq.x * kk.x + qq.y * kk.y + qq.z * kk.z + qq.w * kk.w;
+            }
+            const uint64_t key = span_lo + j;
+            sc[t] = (key >= qlo && key < qhi) ? acc * p.scale : ninf;
+        }
+        m = fmaxf(m, sc[t]);
+    }
+    // 2. softmax over the row: max, exp, sum by shuffles; weights e / sum
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.0f;
+#pragma unroll
+    for (int t = 0; t < kT; t++) {
+        if (32 * t >= n) break;
+        sc[t] = (m == ninf || sc[t] == ninf) ? 0.0f : expf(sc[t] - m);
+        l += sc[t];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+    for (int t = 0; t < kT; t++) {
+        if (32 * t >= n) break;
+        sc[t] = m == ninf ? 0.0f : sc[t] / l;
+    }
+    // 3. P.V: columns C * lane .. C * lane + C - 1, keys in order, two chains
+    float o0[C], o1[C];
+#pragma unroll
+    for (int e = 0; e < C; e++) o0[e] = o1[e] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < kT; t++) {
+        if (32 * t >= n) break;
+        const int kn = min(32, n - 32 * t);
+        const float* vrow0 = vs + (32 * t) * D + C * lane;
+        int u = 0;
+        for (; u + 1 < kn; u += 2) {
+            const float w0 = __shfl_sync(0xffffffffu, sc[t], u), w1 = __shfl_sync(0xffffffffu, sc[t], u + 1);
+            const float* v0 = vrow0 + u * D;
+#pragma unroll
+            for (int e = 0; e < C; e++) {
+                o0[e] += w0 * v0[e];
+                o1[e] += w1 * v0[D + e];
             }
         }
-        const uint64_t key = span_lo + j;
+        if (u < kn) {
+            const float w0 = __shfl_sync(0xffffffffu, sc[t], u);
+            const float* v0 = vrow0 + u * D;
 #pragma unroll
-        for (int qi = 0; qi < kShortQ; qi++)
-            ps[qi * cap + j] = (key >= qlo[qi] && key < qhi[qi]) ? acc[qi] * p.scale : ninf;
-    }
-    __syncthreads();
-
-    // 2. softmax of row `warp`: weights e / sum, all zero for a row with no admitted key
-    {
-        const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-        float* row = ps + warp * cap;
-        float m = ninf;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, row[j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (m == ninf) {
-            for (int j = lane; j < n; j += 32) row[j] = 0.0f;
-        } else {
-            float l = 0.0f;
-            for (int j = lane; j < n; j += 32) {
-                const float e = expf(row[j] - m);
-                row[j] = e;
-                l += e;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            for (int j = lane; j < n; j += 32) row[j] = row[j] / l;
+            for (int e = 0; e < C; e++) o0[e] += w0 * v0[e];
         }
     }
-    __syncthreads();
-
-    // 3. out = P.V, one output column per thread, QPT queries each
-    constexpr int QPT = kShortQ * D / kShortThreads;
-    static_assert(QPT >= 1 && kShortThreads % D == 0, "one column per thread");
-    const int d = threadIdx.x % D, qg = threadIdx.x / D;
-    float acc0[QPT], acc1[QPT];
+    float* orow = p.out + ((q0 + qi) * p.head_count + head) * D + C * lane;
 #pragma unroll
-    for (int i = 0; i < QPT; i++) acc0[i] = acc1[i] = 0.0f;
-    int j = 0;
-    for (; j + 1 < n; j += 2) {
-        const float v0 = vs[j * D + d], v1 = vs[(j + 1) * D + d];
-#pragma unroll
-        for (int i = 0; i < QPT; i++) {
-            const float* prow = ps + (qg * QPT + i) * cap;
-            acc0[i] += prow[j] * v0;
-            acc1[i] += prow[j + 1] * v1;
-        }
-    }
-    if (j < n) {
-        const float v0 = vs[j * D + d];
-#pragma unroll
-        for (int i = 0; i < QPT; i++) acc0[i] += ps[(qg * QPT + i) * cap + j] * v0;
-    }
-#pragma unroll
-    for (int i = 0; i < QPT; i++) {
-        const int qi = qg * QPT + i;
-        if (qi < nq) p.out[((q0 + qi) * p.head_count + head) * D + d] = acc0[i] + acc1[i];
-    }
+    for (int e = 0; e < C; e++) orow[e] = o0[e] + o1[e];
 }
 
 // Largest key span any CTA of the short kernel sees: all keys, or a causal window plus the
