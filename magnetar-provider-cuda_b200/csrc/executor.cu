@@ -1280,6 +1280,53 @@ bool pinned_host(const void* p) {
     return a.type == cudaMemoryTypeHost;
 }
 
+// The address the GPU reaches page-locked host memory at (null: not mapped).
+void* mapped_host(void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
+// A replay's host copy done by the SMs over the mapped address instead of a copy-engine node:
+// a copy engine spends several microseconds starting even a small transfer (256 KB device to
+// host: ~15 us with its synchronisation), while the SMs' loads and stores to host memory go out
+// at once.  16 bytes per thread where both ends are 16-byte aligned, bytes otherwise.  With
+// `flag`, the first thread also moves the device's sticky embedding-id word to the host word
+// and clears it (the replay's flag read and reset).
+__global__ void __launch_bounds__(256) io_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                      uint64_t bytes, int* flag, int* flag_host) {
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x, nth = (uint64_t)gridDim.x * blockDim.x;
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+    const uint64_t n16 = vec ? bytes / 16 : 0;
+    for (uint64_t i = tid; i < n16; i += nth) reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+    for (uint64_t i = n16 * 16 + tid; i < bytes; i += nth) dst[i] = src[i];
+    if (flag && tid == 0) {
+        *flag_host = *flag;
+        *flag = 0;
+    }
+    __threadfence_system();
+}
+
+// Adds an io_copy_kernel node copying `bytes` from src to dst after `deps`.
+bool add_io_copy(cudaGraph_t graph, const cudaGraphNode_t* deps, size_t ndeps, const void* src, void* dst,
+                 uint64_t bytes, int* flag, int* flag_host, cudaGraphNode_t* node) {
+    const uint64_t chunks = (bytes + 15) / 16;
+    unsigned grid = (unsigned)std::min<uint64_t>(148, std::max<uint64_t>(1, (chunks + 255) / 256));
+    const uint8_t* s = static_cast<const uint8_t*>(src);
+    uint8_t* d = static_cast<uint8_t*>(dst);
+    void* args[] = {(void*)&s, (void*)&d, (void*)&bytes, (void*)&flag, (void*)&flag_host};
+    cudaKernelNodeParams kp = {};
+    kp.func = (void*)io_copy_kernel;
+    kp.gridDim = dim3(grid);
+    kp.blockDim = dim3(256);
+    kp.sharedMemBytes = 0;
+    kp.kernelParams = args;
+    return cudaGraphAddKernelNode(node, graph, deps, ndeps, &kp) == cudaSuccess;
+}
+
 // The one-launch graph of a replay with this host I/O (built on first use, kept with the step):
 // null when some host buffer is not pinned (graph copies need page-locked memory) or the graph
 // cannot be built, in which case the replay issues its copies separately.
@@ -1306,8 +1353,12 @@ CapturedStep::IoGraph* io_graph_for(mg_executor* ex, CapturedStep* st, const mg_
         g->device.push_back(bufs[(size_t)i]->ptr);
         if (!io[i].to_device || !io[i].bytes) continue;
         cudaGraphNode_t n;
-        ok = cudaGraphAddMemcpyNode1D(&n, g->graph, nullptr, 0, bufs[(size_t)i]->ptr, io[i].host, io[i].bytes,
-                                      cudaMemcpyHostToDevice) == cudaSuccess;
+        void* mh = mapped_host(io[i].host);
+        if (mh)
+            ok = add_io_copy(g->graph, nullptr, 0, mh, bufs[(size_t)i]->ptr, io[i].bytes, nullptr, nullptr, &n);
+        else
+            ok = cudaGraphAddMemcpyNode1D(&n, g->graph, nullptr, 0, bufs[(size_t)i]->ptr, io[i].host, io[i].bytes,
+                                          cudaMemcpyHostToDevice) == cudaSuccess;
         if (ok) before.push_back(n);
     }
     if (ok && st->advancing) {
@@ -1321,13 +1372,29 @@ CapturedStep::IoGraph* io_graph_for(mg_executor* ex, CapturedStep* st, const mg_
     cudaGraphNode_t step_node = nullptr;
     if (ok)
         ok = cudaGraphAddChildGraphNode(&step_node, g->graph, before.data(), before.size(), st->graph) == cudaSuccess;
+    // The embedding-id word rides along with the first output copy done by the SMs.
+    int* flag_host = st->has_embedding ? static_cast<int*>(mapped_host(d->host_flags)) : nullptr;
+    bool flag_done = false;
     for (int i = 0; ok && i < count; i++) {
         if (io[i].to_device || !io[i].bytes) continue;
         cudaGraphNode_t n;
-        ok = cudaGraphAddMemcpyNode1D(&n, g->graph, &step_node, 1, io[i].host, bufs[(size_t)i]->ptr, io[i].bytes,
-                                      cudaMemcpyDeviceToHost) == cudaSuccess;
+        void* mh = mapped_host(io[i].host);
+        if (mh) {
+            const bool with_flag = flag_host && !flag_done;
+            ok = add_io_copy(g->graph, &step_node, 1, bufs[(size_t)i]->ptr, mh, io[i].bytes, with_flag ? d->flags : nullptr,
+                             with_flag ? flag_host : nullptr, &n);
+            flag_done = flag_done || with_flag;
+        } else {
+            ok = cudaGraphAddMemcpyNode1D(&n, g->graph, &step_node, 1, io[i].host, bufs[(size_t)i]->ptr, io[i].bytes,
+                                          cudaMemcpyDeviceToHost) == cudaSuccess;
+        }
     }
-    if (ok && st->has_embedding) {
+    if (ok && flag_host && !flag_done) {
+        cudaGraphNode_t n;
+        ok = add_io_copy(g->graph, &step_node, 1, nullptr, nullptr, 0, d->flags, flag_host, &n);
+        flag_done = ok;
+    }
+    if (ok && st->has_embedding && !flag_done) {
         // the sticky id flag read back, then reset for the next replay
         cudaGraphNode_t rd, rs;
         ok = cudaGraphAddMemcpyNode1D(&rd, g->graph, &step_node, 1, d->host_flags, d->flags, sizeof(int),
