@@ -711,11 +711,12 @@ def run_ours(args, world, rank, local):
         torch.distributed.destroy_process_group()
 
 
-# DRAM bytes (read + write) per launch of each layer node, from one ncu capture of this bench
-# command (dram__bytes_read.sum + dram__bytes_write.sum; the decoder-layer summary in profiles/),
-# keyed by the node's output id.  Writes stay in the L2 at this size.
-LAYER_NODE_TRAFFIC = {"x": 275712, "h": 285184, "q": 2393344, "k": 2393344, "v": 2393088, "qr": 318208,
-                      "kr": 318208, "a": 821248, "x2": 2655488, "h2": 285184, "g": 11577344, "out": 6636544}
+# DRAM bytes (read + write) per launch of each layer node, from ncu captures of one to three
+# launches of each kernel of this bench command (dram__bytes_read.sum + dram__bytes_write.sum,
+# caches flushed before each; the decoder-layer summary in profiles/), keyed by the node's output
+# id.  Writes stay in the L2 at this size.
+LAYER_NODE_TRAFFIC = {"x": 276480, "h": 285952, "q": 2411008, "k": 2410752, "v": 2410496, "qr": 320000,
+                      "kr": 320000, "a": 837376, "x2": 2673408, "h2": 285952, "g": 11599104, "out": 6654208}
 
 
 def dominant_roofline(cfg, inv, ms, peaks, tf32):
