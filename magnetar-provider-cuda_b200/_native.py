@@ -250,12 +250,30 @@ def range_pairs(ranges):
     return arr, len(flat) // 2
 
 
+def _preload_nccl() -> None:
+    """Loads the NCCL that ships with the framework's wheels (nvidia-nccl), when present, before
+    this library: the library links libnccl.so.2 by its soname, and a process that later imports
+    torch must find the NCCL torch was built against already loaded, not an older system copy
+    this library happened to pull in first."""
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for root in (spec.submodule_search_locations or []) if spec else []:
+        path = os.path.join(root, "lib", "libnccl.so.2")
+        if os.path.exists(path):
+            ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+            return
+
+
 def lib():
     """The loaded library; raises (never falls back) when it is not built."""
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise CudaError(6, f"native library missing at {LIB_PATH}: run __graft_entry__.build()")
+        _preload_nccl()
         L = ctypes.CDLL(LIB_PATH)
         for name, args in SIGNATURES.items():
             fn = getattr(L, name)

@@ -20,6 +20,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "internal.h"
@@ -50,9 +51,11 @@ __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) 
 __device__ __forceinline__ uint32_t pack_bf16(uint16_t a, uint16_t b) { return a | ((uint32_t)b << 16); }
 
 // [rows, cols] f32 -> bf16 hi / lo in the same layout; four 16-byte loads in flight per thread.
+// `clear` (optional): a word zeroed by the first thread (the V pass's max |v| of this call).
 __global__ void __launch_bounds__(256) split_bf16_rows_kernel(const float* __restrict__ src, uint16_t* __restrict__ hi,
-                                                              uint16_t* __restrict__ lo, uint64_t n) {
+                                                              uint16_t* __restrict__ lo, uint64_t n, unsigned* clear) {
     pdl_enter();
+    if (clear && blockIdx.x == 0 && threadIdx.x == 0) *clear = 0u;
     const uint64_t n4 = n / 4, stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n4; i0 += 4 * stride) {
         float4 v[4];
@@ -78,12 +81,15 @@ __global__ void __launch_bounds__(256) split_bf16_rows_kernel(const float* __res
 
 // v [keys, width] f32 -> hi / lo [width, keys_p] bf16 (dst[c][r] = v[r][c]), zero past keys.
 // One CTA per 64 x 64 tile: 16-byte loads along v's rows, and each output row segment (64
-// keys, 128 bytes) written by eight lanes with 16-byte stores.
+// keys, 128 bytes) written by eight lanes with 16-byte stores.  The bits of max |v| (NaN above
+// every number) go to *vmax.
 __global__ void __launch_bounds__(256) split_bf16_transpose_kernel(const float* __restrict__ v, uint64_t keys,
                                                                    uint64_t width, uint16_t* __restrict__ hi,
-                                                                   uint16_t* __restrict__ lo, uint64_t keys_p) {
+                                                                   uint16_t* __restrict__ lo, uint64_t keys_p,
+                                                                   unsigned* vmax) {
     pdl_enter();
     __shared__ float tile[64][65];  // [key][column]
+    unsigned amax = 0u;
     const uint64_t c0 = (uint64_t)blockIdx.x * 64, r0 = (uint64_t)blockIdx.y * 64;
     const bool vec = width % 4 == 0 && c0 + 64 <= width;
     for (int e = threadIdx.x; e < 64 * 16; e += 256) {
@@ -105,7 +111,12 @@ __global__ void __launch_bounds__(256) split_bf16_transpose_kernel(const float* 
         tile[r][4 * q + 1] = x.y;
         tile[r][4 * q + 2] = x.z;
         tile[r][4 * q + 3] = x.w;
+        amax = max(max(amax, max(__float_as_uint(x.x) & 0x7FFFFFFFu, __float_as_uint(x.y) & 0x7FFFFFFFu)),
+                   max(__float_as_uint(x.z) & 0x7FFFFFFFu, __float_as_uint(x.w) & 0x7FFFFFFFu));
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0 && amax) atomicMax(vmax, amax);
     __syncthreads();
     const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
     for (int cc = warp * 4 + lane / 8; cc < 64; cc += 32) {  // 4 columns per warp and turn
@@ -473,6 +484,437 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     }
 }
 
+// 2^x by the SFU's approximate exponential (relative error about 2^-22; -inf gives +0; results
+// below 2^-126 flush to zero -- weights that small do not move an f32 softmax sum).
+__device__ __forceinline__ float ex2_sfu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// ---- two query tiles per CTA; P and the output in tensor memory --------------------------------
+// A CTA serves 256 queries of one head as two 128-row tiles that share every K and V tile it
+// loads.  Tensor memory holds, per query tile t, two 64-key score buffers (columns 256 t and
+// 256 t + 64) and the output accumulator (256 t + 128, D columns).  Warp 0 loads with TMA, warp
+// 1 issues the MMAs, warps 4-7 (tile 0) and 8-11 (tile 1) -- one query row per thread, one
+// tensor-memory lane quarter per warp -- run the softmax.  The softmax writes P as bf16 hi / lo
+// over the scores it has just read (two bf16 per column), and the P.V MMA reads P from tensor
+// memory as its A operand and accumulates into the output there: no P round trip through shared
+// memory and no per-tile fold of P.V into registers.  The MMA warp issues S(j + 2) of a tile
+// right after that tile's P.V(j) (tensor-core operations of one thread run in order), so the
+// score buffer P(j) lived in is rewritten only after P.V(j) has read it.
+//
+// The output accumulates unnormalised (P = 2^(s - m) with a reference max m that moves only when
+// a tile's row max passes it by more than 2^12; the output and sum are then rescaled in tensor
+// memory) and is divided by the sum at the end.  When |V| is large enough for that sum to
+// overflow (the split pass records max |v|), every tile instead rescales the output so that it
+// stays a weighted mean of V rows (the reference's overflow-safety invariant).
+// The reference max of the unnormalised form trails the true row max by at most 2^12: weights
+// stay below 4096, and the output is rescaled only when a tile passes the reference by more.
+constexpr int kAttnLazyLog2 = 12;
+
+struct Attn2Params {
+    float* out;
+    uint64_t seq_len, kv_seq_len, group, out_dim;
+    int causal;
+    int64_t window;  // -1: none
+    uint64_t qpos0;  // position of query 0
+    float scale;
+    int q_pairs;            // CTAs per head: 256 queries each
+    const unsigned* vmax;   // bits of max |v| over V (written by the split pass)
+    unsigned safe_bits;     // from this max on: the weighted-mean form
+    int* error;
+};
+
+template <int D>
+struct Attn2Shape {
+    static constexpr int kQAtom = AQ * 128;          // [128 rows][64 bf16]
+    static constexpr int kQ = (D / 64) * kQAtom;     // one term of one query tile
+    static constexpr int kKAtom = AKV * 128;         // [64 keys][64 bf16]
+    static constexpr int kK = (D / 64) * kKAtom;     // one term of a K tile
+    static constexpr int kV = D * 128;               // one term of a V^T tile: [D][64 keys]
+    static constexpr int kOffQ = 0;                  // [tile][term]
+    static constexpr int kOffK = 4 * kQ;             // [slot][term], double-buffered
+    static constexpr int kOffV = kOffK + 4 * kK;     // [term]
+    static constexpr int kBytes = kOffV + 2 * kV;
+    static constexpr int kSmem = kBytes + 1024;
+    static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kColO = 128;           // within a tile's 256 columns
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAttnTcThreads, 1)
+    attention_tc2_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
+                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
+                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
+                         Attn2Params p) {
+    using S = Attn2Shape<D>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t bars[19];
+    __shared__ uint32_t tmem_slot;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t b0 = smem_u32(bars);
+    const uint32_t q_full = b0, v_full = b0 + 8, v_empty = b0 + 16;
+    auto k_full = [&](int b) { return b0 + 24 + 8u * (uint32_t)b; };
+    auto k_empty = [&](int b) { return b0 + 40 + 8u * (uint32_t)b; };
+    auto s_full = [&](int t, int b) { return b0 + 56 + 8u * (uint32_t)(2 * t + b); };
+    // P(j) of tile t is written on p_full(t, j % 2) and P.V(j) completes on pv_done(t, j % 2): two
+    // barriers each per tile, because the softmax may run one tile ahead of the MMAs (the scores
+    // are double-buffered) -- a parity wait must never meet a barrier two phases ahead of it
+    auto p_full = [&](int t, int b) { return b0 + 88 + 8u * (uint32_t)(2 * t + b); };
+    auto pv_done = [&](int t, int b) { return b0 + 120 + 8u * (uint32_t)(2 * t + b); };
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    // Heavy (late) query pairs first: causal pairs near the end see the most keys.
+    const int qp = p.q_pairs - 1 - (int)blockIdx.x;
+    const uint64_t head = blockIdx.y;
+    const uint64_t kvh = head / p.group;
+    const uint64_t q0 = (uint64_t)qp * 2 * AQ;
+    uint64_t key_lo = 0;
+    if (p.window >= 0) {
+        const uint64_t back = p.window > 0 ? (uint64_t)p.window - 1 : 0;
+        const uint64_t pos = p.qpos0 + q0;
+        key_lo = pos > back ? pos - back : 0;
+    }
+    const uint64_t kv0 = (key_lo / AKV) * AKV;
+    // Key tiles each query tile reads: [kv0, its last admitted key]; the CTA loads the longer run.
+    int n_t[2];
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const uint64_t tq0 = q0 + (uint64_t)t * AQ;
+        n_t[t] = 0;
+        if (tq0 < p.seq_len) {
+            const uint64_t q_last = min(tq0 + AQ, p.seq_len) - 1;
+            const uint64_t key_hi = p.causal ? min(p.kv_seq_len, p.qpos0 + q_last + 1) : p.kv_seq_len;
+            n_t[t] = key_hi > kv0 ? (int)((key_hi - kv0 + AKV - 1) / AKV) : 0;
+        }
+    }
+    const int n_kv = max(n_t[0], n_t[1]);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 19; i++) {
+            const uint32_t bar = b0 + 8u * (uint32_t)i;
+            mbar_init(bar, bar >= p_full(0, 0) && bar <= p_full(1, 1) ? 4 : 1);  // P: the tile's four softmax warps
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tmem_slot), S::kTmemCols);
+        tmem_relinquish();
+    }
+    pdl_enter();  // after the TMEM allocation, as every tensor-memory kernel here does
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer ----------------------------------------------------------------------
+        if (lane == 0 && n_kv > 0) {
+            const int tiles = n_t[1] > 0 ? 2 : 1;
+            mbar_arrive_expect_tx(q_full, (uint32_t)(2 * tiles * S::kQ));
+            for (int t = 0; t < tiles; t++)
+                for (int a = 0; a < D / 64; a++) {
+                    const uint32_t dst = base + S::kOffQ + (uint32_t)(2 * t * S::kQ + a * S::kQAtom);
+                    tma_load_2d(dst, &map_qhi, q_full, (int)(head * D + a * 64), (int)(q0 + (uint64_t)t * AQ));
+                    tma_load_2d(dst + S::kQ, &map_qlo, q_full, (int)(head * D + a * 64), (int)(q0 + (uint64_t)t * AQ));
+                }
+            // K of tile j into slot j % 2, once the scores of tile j - 2 (the slot's last user)
+            // are done: K runs ahead of V.
+            auto load_k = [&](int j) -> bool {
+                const int b = j & 1;
+                if (j >= 2 && !mbar_wait(k_empty(b), (uint32_t)((j - 2) >> 1) & 1u)) return false;
+                const int key = (int)(kv0 + (uint64_t)j * AKV);
+                const uint32_t slot = base + S::kOffK + (uint32_t)(b * 2 * S::kK);
+                mbar_arrive_expect_tx(k_full(b), 2 * S::kK);
+                for (int a = 0; a < D / 64; a++) {
+                    tma_load_2d(slot + a * S::kKAtom, &map_khi, k_full(b), (int)(kvh * D + a * 64), key);
+                    tma_load_2d(slot + S::kK + a * S::kKAtom, &map_klo, k_full(b), (int)(kvh * D + a * 64), key);
+                }
+                return true;
+            };
+            bool ok = load_k(0);
+            for (int j = 0; j < n_kv && ok; j++) {
+                if (j + 1 < n_kv && !load_k(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                if (j > 0 && !mbar_wait(v_empty, (uint32_t)(j - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                const int key0 = (int)(kv0 + (uint64_t)j * AKV);
+                mbar_arrive_expect_tx(v_full, 2 * S::kV);
+                tma_load_2d(base + S::kOffV, &map_vhi, v_full, key0, (int)(kvh * D));
+                tma_load_2d(base + S::kOffV + S::kV, &map_vlo, v_full, key0, (int)(kvh * D));
+            }
+            if (!ok) atomicExch(p.error, 1);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- MMA issuer --------------------------------------------------------------------------
+        if (lane == 0 && n_kv > 0) {
+            constexpr uint32_t idesc_s = idesc_bf16(AQ, AKV);
+            constexpr uint32_t idesc_o = idesc_bf16(AQ, D);
+            // S_t(j) = Q_t K(j)^T into tile t's score buffer j % 2
+            auto issue_s = [&](int t, int j) {
+                const uint32_t tS = tmem + 256u * (uint32_t)t + (uint32_t)(j & 1) * AKV;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t off = (uint32_t)(kk % 4) * 32;
+                    const uint32_t qa = base + S::kOffQ + (uint32_t)(2 * t * S::kQ + (kk / 4) * S::kQAtom) + off;
+                    const uint32_t kb = base + S::kOffK + (uint32_t)((j & 1) * 2 * S::kK + (kk / 4) * S::kKAtom) + off;
+                    const uint64_t qhi = desc_k_sw128(qa), qlo = desc_k_sw128(qa + S::kQ);
+                    const uint64_t khi = desc_k_sw128(kb), klo = desc_k_sw128(kb + S::kK);
+                    mma_bf16(tS, qlo, khi, idesc_s, kk > 0 ? 1u : 0u);
+                    mma_bf16(tS, qhi, klo, idesc_s, 1u);
+                    mma_bf16(tS, qhi, khi, idesc_s, 1u);
+                }
+                tc_commit(s_full(t, j & 1));
+            };
+            bool ok = mbar_wait(q_full, 0);
+            for (int j = 0; j < min(2, n_kv) && ok; j++) {
+                ok = mbar_wait(k_full(j), 0);
+                if (!ok) break;
+                tc_fence_after();
+                for (int t = 0; t < 2; t++)
+                    if (j < n_t[t]) issue_s(t, j);
+                tc_commit(k_empty(j));
+            }
+            for (int j = 0; j < n_kv && ok; j++) {
+                if (!mbar_wait(v_full, (uint32_t)j & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                bool k_ready = false;
+                for (int t = 0; t < 2 && ok; t++) {
+                    if (j < n_t[t]) {
+                        if (!mbar_wait(p_full(t, j & 1), (uint32_t)(j >> 1) & 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // O_t += P_t(j) V(j): P's hi / lo terms from tensor memory (32 columns
+                        // each, two bf16 per column), V^T's from shared memory
+                        const uint32_t tP = tmem + 256u * (uint32_t)t + (uint32_t)(j & 1) * AKV;
+                        const uint32_t tO = tmem + 256u * (uint32_t)t + S::kColO;
+#pragma unroll
+                        for (int kk = 0; kk < AKV / 16; kk++) {
+                            const uint32_t vb = base + S::kOffV + (uint32_t)kk * 32;
+                            const uint64_t vhi = desc_k_sw128(vb), vlo = desc_k_sw128(vb + S::kV);
+                            const uint32_t ahi = tP + (uint32_t)kk * 8, alo = ahi + 32;
+                            mma_bf16_ts(tO, alo, vhi, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                            mma_bf16_ts(tO, ahi, vlo, idesc_o, 1u);
+                            mma_bf16_ts(tO, ahi, vhi, idesc_o, 1u);
+                        }
+                        tc_commit(pv_done(t, j & 1));
+                    }
+                    if (t == 1) tc_commit(v_empty);
+                    if (j + 2 < n_t[t]) {
+                        if (!k_ready) {
+                            if (!mbar_wait(k_full(j & 1), (uint32_t)((j + 2) >> 1) & 1u)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            k_ready = true;
+                        }
+                        issue_s(t, j + 2);
+                    }
+                }
+                if (ok && j + 2 < n_kv) tc_commit(k_empty(j & 1));
+            }
+            if (!ok) atomicExch(p.error, 1);
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ---- softmax: one query row per thread ---------------------------------------------------
+        constexpr float kLog2e = 1.4426950408889634f;
+        const float kNegInf = __int_as_float(0xff800000);
+        const int t = (warp - 4) / 4, qq = warp % 4;
+        const int r = qq * 32 + lane;
+        const uint64_t qi = q0 + (uint64_t)t * AQ + r;
+        const bool live = qi < p.seq_len;
+        const uint64_t qpos = p.qpos0 + qi;
+        const uint64_t row_hi = live ? (p.causal ? min(p.kv_seq_len, qpos + 1) : p.kv_seq_len) : 0;
+        uint64_t row_lo = 0;
+        if (p.window >= 0) {
+            const uint64_t back = p.window > 0 ? (uint64_t)p.window - 1 : 0;
+            row_lo = qpos > back ? qpos - back : 0;
+            if (row_lo > row_hi) row_lo = row_hi;
+        }
+        const float scale2 = p.scale * kLog2e;  // scores in log2 units
+        const bool pos_scale = scale2 > 0.0f;
+        const float sc = pos_scale ? scale2 : 1.0f;  // the factor left for after the max
+        constexpr float kLazy = (float)kAttnLazyLog2;
+        const bool safe = *p.vmax >= p.safe_bits;
+        const uint32_t lane_base = tmem + ((uint32_t)(qq * 32) << 16) + 256u * (uint32_t)t;
+        const int n = n_t[t];
+        float m = kNegInf, l = 0.0f;
+        bool failed = false;
+        // O *= f for this thread's row (warp-collective), once P.V(j - 1) has completed
+        auto rescale_o = [&](int j, float f) {
+            if (!mbar_wait(pv_done(t, (j - 1) & 1), (uint32_t)((j - 1) >> 1) & 1u)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
+            if (failed) return;
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < D; c += 32) {
+                float o[32];
+                tmem_ld32(lane_base + S::kColO + (uint32_t)c, o);
+                tc_wait_ld();
+                uint32_t u0[16], u1[16];
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    u0[e] = __float_as_uint(o[e] * f);
+                    u1[e] = __float_as_uint(o[16 + e] * f);
+                }
+                tmem_st16(lane_base + S::kColO + (uint32_t)c, u0);
+                tmem_st16(lane_base + S::kColO + (uint32_t)c + 16, u1);
+            }
+            tc_wait_st();
+        };
+        for (int j = 0; j < n; j++) {
+            if (!mbar_wait(s_full(t, j & 1), (uint32_t)(j >> 1) & 1u)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
+            if (failed) break;
+            tc_fence_after();
+            const uint32_t tS = lane_base + (uint32_t)(j & 1) * AKV;
+            float s[64];
+            tmem_ld32(tS, s);
+            tmem_ld32(tS + 32, s + 32);
+            tc_wait_ld();
+            const uint64_t key0 = kv0 + (uint64_t)j * AKV;
+            // eight independent running maxima / sums: short dependency chains
+            float mx[8];
+#pragma unroll
+            for (int g = 0; g < 8; g++) mx[g] = kNegInf;
+            // The row max of the raw scores (a positive scale keeps their order; any other
+            // scale is applied first), in log2 units after one multiply.
+            if (!pos_scale)
+#pragma unroll
+                for (int c = 0; c < 64; c++) s[c] *= scale2;
+            if (key0 >= row_lo && key0 + AKV <= row_hi) {  // interior: every key admitted
+#pragma unroll
+                for (int c = 0; c < 64; c++) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++) {
+                    const uint64_t key = key0 + c;
+                    s[c] = (key >= row_lo && key < row_hi) ? s[c] : kNegInf;
+                    mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+                }
+            }
+            const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
+            // weights 2^(s sc - ref) (one FMA and the SFU) for a finite reference; none while the
+            // row has no admitted key
+            auto weights = [&](float ref) {
+                float ps[8];
+#pragma unroll
+                for (int g = 0; g < 8; g++) ps[g] = 0.0f;
+                if (ref != kNegInf) {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) {
+                        s[c] = ex2_sfu(fmaf(s[c], sc, -ref));  // masked (-inf) keys give +0
+                        ps[c & 7] += s[c];
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) s[c] = 0.0f;
+                }
+                return ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            };
+            float pmul = 1.0f, f = 1.0f;
+            bool need = false;
+            if (!safe) {
+                // the reference max moves only when this tile's passes it by more than 2^kLazy
+                need = tmax != kNegInf && (m == kNegInf || tmax > m + kLazy);
+                if (need) {
+                    f = m == kNegInf ? 0.0f : ex2_sfu(m - tmax);
+                    need = m != kNegInf;  // an output that holds only zero weights needs no rescale
+                    m = tmax;
+                    l *= f;
+                }
+                l += weights(m);
+            } else {
+                // the output stays a weighted mean of V rows: O <- O (l a / l_new) + (P / l_new) V
+                const float m_new = fmaxf(m, tmax);
+                const float a = m == kNegInf ? 0.0f : ex2_sfu(m - m_new);
+                const float psum = weights(m_new);
+                const float l_new = l * a + psum;
+                pmul = l_new > 0.0f ? 1.0f / l_new : 0.0f;
+                f = l_new > 0.0f ? (l * a) * pmul : 0.0f;
+                need = true;
+                m = m_new;
+                l = l_new;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, need)) {
+                rescale_o(j, need ? f : 1.0f);
+                if (failed) break;
+            }
+            // P as bf16 hi / lo over the scores just read: 64 keys, two per column; hi in
+            // columns [0, 32), lo in [32, 64) (the lower key in the low half)
+            if (safe)
+#pragma unroll
+                for (int c = 0; c < 64; c++) s[c] *= pmul;
+            uint32_t ph[32], pl[32];
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                const float x0 = s[2 * c], x1 = s[2 * c + 1];
+                const __nv_bfloat162 hb = __floats2bfloat162_rn(x0, x1);
+                const float2 hf2 = __bfloat1622float2(hb);
+                const __nv_bfloat162 lb = __floats2bfloat162_rn(x0 - hf2.x, x1 - hf2.y);
+                ph[c] = *reinterpret_cast<const uint32_t*>(&hb);
+                pl[c] = *reinterpret_cast<const uint32_t*>(&lb);
+            }
+            tmem_st16(tS, *reinterpret_cast<const uint32_t(*)[16]>(ph));
+            tmem_st16(tS + 16, *reinterpret_cast<const uint32_t(*)[16]>(ph + 16));
+            tmem_st16(tS + 32, *reinterpret_cast<const uint32_t(*)[16]>(pl));
+            tmem_st16(tS + 48, *reinterpret_cast<const uint32_t(*)[16]>(pl + 16));
+            tc_wait_st();
+            tc_fence_before();
+            mbar_arrive_warp(p_full(t, j & 1));
+        }
+        // ---- the output row: O / l (or the weighted mean as it stands) ---------------------------
+        bool have = false;
+        if (n > 0 && !failed) {
+            if (!mbar_wait(pv_done(t, (n - 1) & 1), (uint32_t)((n - 1) >> 1) & 1u)) failed = true;
+            failed = __any_sync(0xffffffffu, failed);
+            have = !failed;
+        }
+        if (failed) atomicExch(p.error, 1);
+        const float fin = safe ? 1.0f : (l > 0.0f ? 1.0f / l : 0.0f);
+        if (have) tc_fence_after();
+        float* orow = p.out + qi * p.out_dim + head * D;
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+            float o[32];
+            if (have) {
+                tmem_ld32(lane_base + S::kColO + (uint32_t)c, o);
+                tc_wait_ld();
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; e++) o[e] = 0.0f;
+            }
+            if (live)
+#pragma unroll
+                for (int e = 0; e < 32; e += 4)
+                    *reinterpret_cast<float4*>(orow + c + e) =
+                        make_float4(o[e] * fin, o[e + 1] * fin, o[e + 2] * fin, o[e + 3] * fin);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::kTmemCols);
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -534,6 +976,42 @@ mg_status launch_attention_tc(Device* d, const k::AttentionArgs& a, const CUtens
     return launched(d, "tensor-core attention launch");
 }
 
+template <int D>
+mg_status launch_attention_tc2(Device* d, const k::AttentionArgs& a, const CUtensorMap* maps, const unsigned* vmax) {
+    using S = Attn2Shape<D>;
+    static_assert(S::kSmem <= 227 * 1024 - 256, "shared memory budget");
+    static bool configured[64] = {false};
+    if (!configured[d->ordinal & 63]) {
+        MG_CUDA(cudaFuncSetAttribute(attention_tc2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+                "configuring the attention kernel");
+        configured[d->ordinal & 63] = true;
+    }
+    Attn2Params p;
+    p.out = a.out;
+    p.seq_len = a.seq_len;
+    p.kv_seq_len = a.kv_seq_len;
+    p.group = a.head_count / a.kv_head_count;
+    p.out_dim = a.head_count * a.value_dim;
+    p.causal = a.causal;
+    p.window = a.window;
+    p.qpos0 = a.query_position_offset;
+    p.scale = a.scale;
+    p.q_pairs = (int)((a.seq_len + 2 * AQ - 1) / (2 * AQ));
+    p.vmax = vmax;
+    // The unnormalised sum stays below n_keys * 2^kAttnLazyLog2 * max |v|: the weighted-mean
+    // form from max |v| >= 2^(118 - kAttnLazyLog2 - ceil(log2 n_keys)), keeping 2^10 of headroom
+    // below the f32 limit.
+    int lg = 0;
+    while (lg < 40 && (1ull << lg) < a.kv_seq_len) lg++;
+    const int e = 118 - kAttnLazyLog2 - lg;
+    p.safe_bits = (unsigned)(e + 127) << 23;
+    p.error = d->flags + 2;
+    dim3 grid((unsigned)p.q_pairs, (unsigned)a.head_count);
+    enqueue(d, attention_tc2_kernel<D>, grid, kAttnTcThreads, S::kSmem, maps[0], maps[1], maps[2], maps[3], maps[4],
+                                                                           maps[5], p);
+    return launched(d, "tensor-core attention launch");
+}
+
 }  // namespace
 
 namespace k {
@@ -552,20 +1030,22 @@ mg_status attention_tc(Device* d, const AttentionArgs& a) {
     const uint64_t skv_p = (Skv + 7) & ~7ull;  // V^T rows are 16-byte multiples
     const size_t q_elems = S * qd, k_elems = Skv * kvd, vt_elems = kvd * skv_p;
     uint16_t* ws = nullptr;
-    MG_TRY(scratch(d, 4, 2 * (q_elems + k_elems + vt_elems) * sizeof(uint16_t), (void**)&ws));
+    const size_t terms = 2 * (q_elems + k_elems + vt_elems) * sizeof(uint16_t);
+    MG_TRY(scratch(d, 4, terms + 16, (void**)&ws));
     uint16_t* qhi = ws;
     uint16_t* qlo = qhi + q_elems;
     uint16_t* khi = qlo + q_elems;
     uint16_t* klo = khi + k_elems;
     uint16_t* vhi = klo + k_elems;
     uint16_t* vlo = vhi + vt_elems;
-    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, q_elems / 4), 256, 0, a.q, qhi, qlo, q_elems);
-    MG_TRY(launched(d, "attention split launch"));
-    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, k_elems / 4), 256, 0, a.k, khi, klo, k_elems);
-    MG_TRY(launched(d, "attention split launch"));
+    unsigned* vmax = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(ws) + terms);
     dim3 tg((unsigned)((kvd + 63) / 64), (unsigned)((skv_p + 63) / 64));
     if (tg.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the split pass");
-    enqueue(d, split_bf16_transpose_kernel, tg, 256, 0, a.v, Skv, kvd, vhi, vlo, skv_p);
+    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, q_elems / 4), 256, 0, a.q, qhi, qlo, q_elems, vmax);
+    MG_TRY(launched(d, "attention split launch"));
+    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, k_elems / 4), 256, 0, a.k, khi, klo, k_elems, (unsigned*)nullptr);
+    MG_TRY(launched(d, "attention split launch"));
+    enqueue(d, split_bf16_transpose_kernel, tg, 256, 0, a.v, Skv, kvd, vhi, vlo, skv_p, vmax);
     MG_TRY(launched(d, "attention split launch"));
     const int D = (int)a.head_dim;
     CUtensorMap maps[6];
@@ -575,6 +1055,11 @@ mg_status attention_tc(Device* d, const AttentionArgs& a) {
     MG_TRY(bf16_map(&maps[3], klo, Skv, kvd, kvd, AKV));
     MG_TRY(bf16_map(&maps[4], vhi, kvd, Skv, skv_p, (uint32_t)D));
     MG_TRY(bf16_map(&maps[5], vlo, kvd, Skv, skv_p, (uint32_t)D));
+    static const bool one_tile = [] {
+        const char* e = getenv("MAGNETAR_CUDA_ATTN_ONE_TILE");
+        return e && atoi(e) != 0;
+    }();
+    if (!one_tile) return D == 64 ? launch_attention_tc2<64>(d, a, maps, vmax) : launch_attention_tc2<128>(d, a, maps, vmax);
     const int q_tiles = (int)((S + AQ - 1) / AQ);
     if (D == 64) return launch_attention_tc<64>(d, a, maps, q_tiles);
     return launch_attention_tc<128>(d, a, maps, q_tiles);

@@ -4,20 +4,17 @@
 // The CUDA-core few-row path (gemv.cu) spends two FLOPs of FMA issue per weight value per row:
 // from about eight rows up it is bound by instruction issue, not by reading B.  Here the MMA is
 // turned around so that the weight is the 128-row operand and the activation rows are the
-// MMA's N = 16: D[n][m] = sum_k B[k][n] * A[m][k].  B's row-major [k, n] tile is exactly the
-// MN-major operand layout (n contiguous), so a stage is four TMA boxes of [32 k x 32 n] with
-// 128-byte swizzling in 32-byte granules, used as they land -- no transpose.  Each operand enters as two tf32
-// terms (3xTF32, the f32 contract): eight converter warps split every raw tile into hi
-// (truncated to tf32) and lo = tf32(x - hi), and one thread issues lo*hi + hi*lo + hi*hi into
-// one TMEM accumulator.  The raw ring (what HBM streams into) and the converted buffers (what
-// the MMAs read) are separate, so a raw stage is refilled as soon as the converters have read
-// it.  The k slices of one 128-column tile (and, gated, the gate and up terms) form one
-// thread-block cluster; each CTA stages its [16 x 128] partial, sends each band of rows to
+// MMA's N: D[n][m] = sum_k B[k][n] * A[m][k].  A raw stage is B's [64 k][128 n] as it lies (one
+// unswizzled TMA box) and A's [16][64].  Each operand enters as two tf32 terms (3xTF32, the f32
+// contract): eight converter warps split the weight -- each thread its column n over 32 k --
+// into hi (truncated to tf32) and lo = tf32(x - hi) and store both to tensor memory, where the
+// MMA reads them as its A operand; A's hi and lo rows are stacked as the MMA's N = 32 in shared
+// memory, so one thread issues W_lo [A_hi; A_lo] + W_hi [A_hi; A_lo] per k-step and the hi and lo
+// rows of the accumulator are added at the end.  Shared memory carries only the raw stage and
+// A's small terms.  The k slices of one 128-column tile (and, gated, the gate and up terms) form
+// one thread-block cluster; each CTA stages its [16 x 128] partial, sends each band of rows to
 // the CTA that owns it with one bulk copy, and owners add the partials in split order
 // (deterministic), apply bias / residual / SwiGLU and write.
-//
-// Per weight value the converters spend about four instructions (the FMA path: sixteen FMAs
-// at 16 rows), and the tensor pipe does the multiply, so the kernel streams B at HBM speed.
 //
 // Packed Q8_0 weights (tiled records) take a kernel of their own further down, on bf16 operands:
 // every quant is exactly a bfloat16 value, so only the activations are split.
@@ -41,30 +38,38 @@ using namespace sm100;
 constexpr int kTcCols = 128;     // columns of B per CTA: the MMA's M
 constexpr int kTcK = 32;         // k per conversion group: one 128-byte swizzle row
 constexpr int kTcRows = 16;      // the MMA's N: activation rows (zero past M)
-constexpr int kConvStages = 3;   // converted (hi / lo) groups the MMAs read
 constexpr int kAccs = 4;         // TMEM accumulators: k-step s of a group adds into accumulator s
 constexpr int kConvThreads = 256;
 constexpr int kMaxCluster = 16;  // non-portable cluster size (checked against the GPU at launch)
 constexpr int kQ8Chunk = 128;    // k per tiled Q8_0 record
 
 struct TcGemvShape {
-    // a raw stage is one group of k: [32 k][128 n] as four swizzled boxes, then A's [16][32]
-    static constexpr int kWRaw = kTcK * kTcCols * 4;
-    static constexpr int kARaw = kTcRows * kTcK * 4;
+    // A raw stage is 64 k: B's [64 k][128 n] as it lies (one unswizzled box, n contiguous), then
+    // A's [16][64] as two 128-byte-swizzled [16][32] boxes (K-major, the MMA's B operand).
+    static constexpr int kStageK = 2 * kTcK;
+    static constexpr int kWRaw = kStageK * kTcCols * 4;   // 32 KB
+    static constexpr int kAGroup = kTcRows * kTcK * 4;     // one [16][32] box: 2 KB
     static constexpr int kOffA = kWRaw;
-    static constexpr int kRawStage = kOffA + kARaw;
-    static constexpr int kRawStages = 5;                  // raw bytes in flight from HBM
-    static constexpr int kWTile = kTcK * kTcCols * 4;     // one converted W term: 16 KB
-    static constexpr int kATile = kTcRows * kTcK * 4;     // one converted A term: 2 KB
-    static constexpr int kConvStage = 2 * kWTile + 2 * kATile;  // W hi, W lo, A hi, A lo
+    static constexpr int kRawStage = kOffA + 2 * kAGroup;  // 36 KB
+    static constexpr int kRawStages = 5;                   // raw bytes in flight from HBM
+    // A converted stage: the weight's hi / lo terms in tensor memory (64 + 64 columns of 128
+    // lanes), A's hi / lo terms in shared memory as two K-major [32][32] tiles, one per 32 k:
+    // rows 0-15 hi, rows 16-31 lo ([hi g0][lo g0][hi g1][lo g1]).
+    static constexpr int kConvStage = 4 * kAGroup;         // 8 KB
+    static constexpr int kConvStages = 3;
     static constexpr int kRing = kRawStages * kRawStage + kConvStages * kConvStage;
-    static constexpr int kRecv = 32 * kTcCols * 4;     // the other CTAs' rows of this CTA's band
+    static constexpr int kRecv = 32 * kTcCols * 4;         // the other CTAs' rows of this CTA's band
     static constexpr int kBars = 256;
     static constexpr int kSmem = kRing + kRecv + kBars + 1024;
     static constexpr int kThreads = 320;  // producer, MMA, 8 converter warps
+    static constexpr uint32_t kTmemCols = 512;
+    static constexpr int kN = 2 * kTcRows;                 // the MMA's N: A's hi rows, then its lo rows
+    static constexpr uint32_t kWCol0 = kAccs * kN;         // accumulators first, then the weight stages
+    static constexpr uint32_t kWStageCols = 2 * kStageK;   // hi then lo, one column per k
     static_assert(kRawStage % 1024 == 0 && kConvStage % 1024 == 0 && kOffA % 1024 == 0,
                   "swizzle atoms stay 1024-byte aligned");
-    static_assert(kTcRows * kTcCols * 4 <= kConvStage, "the staged partial fits a drained conversion buffer");
+    static_assert(kTcRows * kTcCols * 4 <= kRawStage, "the staged partial fits a drained raw stage");
+    static_assert(kWCol0 + kConvStages * kWStageCols <= kTmemCols, "accumulators and weight stages fit");
     static_assert(kTcK / 8 == kAccs, "one accumulator per k-step of a group");
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
@@ -103,6 +108,7 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
                    const __grid_constant__ CUtensorMap map_b2, GemvTcArgs p) {
     using S = TcGemvShape;
     constexpr int kRawStages = S::kRawStages;
+    constexpr int kConvStages = S::kConvStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -131,22 +137,20 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
     const CUtensorMap* map_w = term ? &map_b2 : &map_b;
     const uint64_t k0 = (uint64_t)blockIdx.y * p.slice_len;
     const uint64_t k1 = min(p.k, k0 + p.slice_len);
-    const int num_kb = k1 > k0 ? (int)((k1 - k0 + kTcK - 1) / kTcK) : 0;  // raw stages, one group each
-    const int num_groups = num_kb;
+    const int num_kb = k1 > k0 ? (int)((k1 - k0 + S::kStageK - 1) / S::kStageK) : 0;  // raw stages
 
-    // The producer's loads of raw stage i: B (the weight's tiles) arms the stage's barrier for all
-    // its bytes; A follows.
+    // The producer's loads of raw stage i: B (the weight's [64 k][128 n]) arms the stage's barrier
+    // for all its bytes; A's two boxes follow.  Past k (or n) the copies fill zeros.
     auto issue_w = [&](int i) {
         const int s = i % kRawStages;
-        const uint32_t st = raw_stage(s);
         mbar_arrive_expect_tx(raw_full(s), (uint32_t)S::kRawStage);
-        const int ky = (int)(k0 + (uint64_t)i * kTcK);
-#pragma unroll
-        for (int j = 0; j < 4; j++) tma_load_2d(st + (uint32_t)(j * 4096), map_w, raw_full(s), (int)n0 + 32 * j, ky);
+        tma_load_2d(raw_stage(s), map_w, raw_full(s), (int)n0, (int)(k0 + (uint64_t)i * S::kStageK));
     };
     auto issue_a = [&](int i) {
         const int s = i % kRawStages;
-        tma_load_2d(raw_stage(s) + S::kOffA, &map_a, raw_full(s), (int)(k0 + (uint64_t)i * kTcK), 0);
+        const int kx = (int)(k0 + (uint64_t)i * S::kStageK);
+        tma_load_2d(raw_stage(s) + S::kOffA, &map_a, raw_full(s), kx, 0);
+        tma_load_2d(raw_stage(s) + S::kOffA + S::kAGroup, &map_a, raw_full(s), kx + kTcK, 0);
     };
 
     if (threadIdx.x == 0) {
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
             for (int i = 0; i < min(kRawStages, num_kb); i++) issue_w(i);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32((const void*)tmem_slot), kAccs * kTcRows);
+        tmem_alloc(smem_u32((const void*)tmem_slot), S::kTmemCols);
         tmem_relinquish();
     }
     cluster_arrive();  // phase 1: every receive barrier of the cluster is armed
@@ -203,10 +207,11 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
     } else if (warp == 1) {
         // ---- MMA issuer: D[128 n][16 m] += W_lo A_hi + W_hi A_lo + W_hi A_hi --------------------
         if (lane == 0) {
-            // A (the weight) MN-major as it lies
-            constexpr uint32_t idesc = idesc_tf32(kTcCols, kTcRows) | (1u << 15);
+            // the weight terms from tensor memory (its n in the lanes, k along the columns), A's
+            // terms K-major from shared memory
+            constexpr uint32_t idesc = idesc_tf32(kTcCols, S::kN);
             bool ok = true;
-            for (int i = 0; i < num_groups; i++) {
+            for (int i = 0; i < num_kb; i++) {
                 const int c = i % kConvStages;
                 if (!mbar_wait(conv_full(c), (uint32_t)(i / kConvStages) & 1u) || *abort_flag) {
                     *abort_flag = 1;
@@ -216,28 +221,33 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t cs = conv_stage(c);
-                const uint32_t whi = cs, wlo = cs + S::kWTile, ahi = cs + 2 * S::kWTile, alo = ahi + S::kATile;
+                const uint32_t tw = tmem + S::kWCol0 + (uint32_t)c * S::kWStageCols;
 #pragma unroll
-                for (int kk = 0; kk < kTcK / 8; kk++) {
-                    const uint64_t dwhi = desc_mn_sw128_32b(whi + (uint32_t)(kk * 1024), 4096);
-                    const uint64_t dwlo = desc_mn_sw128_32b(wlo + (uint32_t)(kk * 1024), 4096);
-                    const uint64_t dahi = desc_k_sw128(ahi) + (uint64_t)((kk * 32) >> 4);
-                    const uint64_t dalo = desc_k_sw128(alo) + (uint64_t)((kk * 32) >> 4);
-                    // four accumulators, one per k-step: four independent chains of MMAs
-                    const uint32_t acc = tmem + (uint32_t)(kk * kTcRows);
-                    mma_tf32(acc, dwlo, dahi, idesc, i > 0 ? 1u : 0u);
-                    mma_tf32(acc, dwhi, dalo, idesc, 1u);
-                    mma_tf32(acc, dwhi, dahi, idesc, 1u);
+                for (int g = 0; g < 2; g++) {
+#pragma unroll
+                    for (int kk = 0; kk < kTcK / 8; kk++) {
+                        const uint32_t whi = tw + (uint32_t)(g * kTcK + kk * 8), wlo = whi + S::kStageK;
+                        // A's hi and lo rows together: the MMA's N = 32
+                        const uint64_t da = desc_k_sw128(cs + (uint32_t)(g * 2 * S::kAGroup)) + (uint64_t)((kk * 32) >> 4);
+                        // four accumulators, one per k-step of a group: four independent chains;
+                        // W_lo (A_hi + A_lo) + W_hi (A_hi + A_lo), the hi and lo rows added at the end
+                        const uint32_t acc = tmem + (uint32_t)(kk * S::kN);
+                        mma_tf32_ts(acc, wlo, da, idesc, (i > 0 || g > 0) ? 1u : 0u);
+                        mma_tf32_ts(acc, whi, da, idesc, 1u);
+                    }
                 }
-                tc_commit(conv_empty(c));  // frees the conversion buffer once these MMAs have read it
+                tc_commit(conv_empty(c));  // frees the converted terms once these MMAs have read them
             }
-            if (ok && num_groups > 0) tc_commit(accum_bar);
+            if (ok && num_kb > 0) tc_commit(accum_bar);
             else mbar_arrive(accum_bar);  // release the epilogue
         }
         __syncwarp();
     } else {
-        // ---- warps 2..9: split each raw group into hi / lo terms in a conversion buffer --------
+        // ---- warps 2..9: split each raw stage into hi / lo terms: the weight's into tensor
+        //      memory (row n of this warp's lane quarter, one k half), A's into shared memory ------
         const int t = threadIdx.x - 64;
+        const int q = warp % 4, hp = (warp - 2) / 4;
+        const int n = q * 32 + lane;
         for (int i = 0; i < num_kb; i++) {
             const int s = i % kRawStages;
             bool ok = mbar_wait(raw_full(s), (uint32_t)(i / kRawStages) & 1u);
@@ -248,30 +258,43 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
                 *abort_flag = 1;
                 atomicExch(p.error, 1);  // still arrive below so that no one waits for this thread
             }
+            tc_fence_after();  // the MMAs that read these tensor-memory columns before have completed
             const uint32_t cs = conv_stage(c);
-            {
-                // all of this thread's loads first, so that their latencies overlap
-                constexpr int J = S::kWRaw / 16 / kConvThreads;
-                float4 x[J];
+            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + S::kWCol0 + (uint32_t)c * S::kWStageCols +
+                                (uint32_t)(32 * hp);
 #pragma unroll
-                for (int j = 0; j < J; j++) x[j] = lds4(rs + (uint32_t)(t + j * kConvThreads) * 16);
+            for (int h = 0; h < 2; h++) {
+                // k rows 32 hp + 16 h .. + 15 of this thread's column n: one 4-byte load per row
+                // (a warp reads 128 contiguous bytes of each row)
+                float x[16];
 #pragma unroll
-                for (int j = 0; j < J; j++) {
-                    const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
-                    float4 h, l;
-                    split_fast(x[j], h, l);
-                    sts4(cs + off, h.x, h.y, h.z, h.w);
-                    sts4(cs + S::kWTile + off, l.x, l.y, l.z, l.w);
+                for (int j = 0; j < 16; j++) {
+                    const uint32_t row = (uint32_t)(32 * hp + 16 * h + j);
+                    asm volatile("ld.shared::cta.f32 %0, [%1];" : "=f"(x[j]) : "r"(rs + row * (kTcCols * 4) + (uint32_t)n * 4));
                 }
+                uint32_t hv[16], lv[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float hi = __uint_as_float(__float_as_uint(x[j]) & 0xFFFFE000u);
+                    hv[j] = __float_as_uint(hi);
+                    lv[j] = __float_as_uint(tf32_rna(x[j] - hi));
+                }
+                tmem_st16(ta + (uint32_t)(16 * h), hv);
+                tmem_st16(ta + S::kStageK + (uint32_t)(16 * h), lv);
             }
-            if (t < S::kATile / 16) {
+            {
+                // A's two [16][32] boxes: the same swizzled layout in the hi rows and the lo rows
+                // (16 rows are two whole 8-row swizzle atoms)
                 const uint32_t off = (uint32_t)t * 16;
-                float4 h, l;
-                split_fast(lds4(rs + S::kOffA + off), h, l);
-                sts4(cs + 2 * S::kWTile + off, h.x, h.y, h.z, h.w);
-                sts4(cs + 2 * S::kWTile + S::kATile + off, l.x, l.y, l.z, l.w);
+                const uint32_t g = off / S::kAGroup, o = off % S::kAGroup;
+                float4 hi4, lo4;
+                split_fast(lds4(rs + S::kOffA + off), hi4, lo4);
+                sts4(cs + g * 2 * S::kAGroup + o, hi4.x, hi4.y, hi4.z, hi4.w);
+                sts4(cs + g * 2 * S::kAGroup + S::kAGroup + o, lo4.x, lo4.y, lo4.z, lo4.w);
             }
+            tc_wait_st();         // the weight terms are in the tensor memory
             fence_proxy_async();  // the generic-proxy writes become visible to tcgen05.mma
+            tc_fence_before();
             mbar_arrive_warp(conv_full(c));
             mbar_arrive_warp(raw_empty(s));
             if (__any_sync(0xffffffffu, *abort_flag)) break;
@@ -282,30 +305,27 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
         const bool waited = mbar_wait(accum_bar, 0);
         if (!waited) atomicExch(p.error, 1);
         // tcgen05.ld is warp-collective: the whole warp reads the accumulator or none of it.
-        acc_ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_groups > 0);
+        acc_ready = __all_sync(0xffffffffu, waited && !*abort_flag && num_kb > 0);
     }
-    // ---- stage this CTA's partial as [16 m][128 n] in the drained first conversion buffer ------
-    float* staged = reinterpret_cast<float*>(base_ptr + (conv_stage(0) - base));
+    // ---- stage this CTA's partial as [16 m][128 n] in the drained first raw stage ----------------
+    float* staged = reinterpret_cast<float*>(base_ptr + (raw_stage(0) - base));
     if (warp >= 2 && warp < 6) {
         tc_fence_after();
         const int q = warp % 4;
         const int n = q * 32 + lane;
         float v[16];
-        if (acc_ready) {
-            // the accumulators added in order (deterministic)
-            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16), v);
-            tc_wait_ld();
 #pragma unroll
-            for (int a = 1; a < kAccs; a++) {
-                float w[16];
-                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kTcRows), w);
+        for (int j = 0; j < 16; j++) v[j] = 0.0f;
+        if (acc_ready) {
+            // the accumulators added in order, each row's hi and lo column together (deterministic)
+#pragma unroll
+            for (int a = 0; a < kAccs; a++) {
+                float w[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * S::kN), w);
                 tc_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 16; j++) v[j] += w[j];
+                for (int j = 0; j < 16; j++) v[j] += w[j] + w[16 + j];
             }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = 0.0f;
         }
 #pragma unroll
         for (int j = 0; j < kTcRows; j++) staged[j * kTcCols + n] = v[j];
@@ -315,7 +335,7 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kAccs * kTcRows);
+        tmem_dealloc(tmem, S::kTmemCols);
     }
     // ---- exchange: each band of rows to the CTA that owns it ------------------------------------
     cluster_wait();  // phase 1
@@ -325,7 +345,7 @@ __global__ void __launch_bounds__(TcGemvShape::kThreads, 1)
             const int lo = min((int)p.m, o * mb), hi = min((int)p.m, lo + mb);
             if (hi > lo)
                 bulk_copy_to_cluster(mapa(recv + (uint32_t)(rank * mb * kTcCols * 4), (uint32_t)o),
-                                     conv_stage(0) + (uint32_t)(lo * kTcCols * 4), (uint32_t)((hi - lo) * kTcCols * 4),
+                                     raw_stage(0) + (uint32_t)(lo * kTcCols * 4), (uint32_t)((hi - lo) * kTcCols * 4),
                                      mapa(recv_bar, (uint32_t)o));
         }
     }
@@ -740,16 +760,18 @@ PFN_cuTensorMapEncodeTiled_v12000 tc_gemv_encode_fn() {
 // Row-major f32 [rows, cols], box [box_rows x 32 columns], zero past the edges; 128-byte swizzle
 // (a K-major operand: 16-byte granules) or, `mn`, 128-byte swizzle in 32-byte granules (an
 // MN-major tf32 operand).
+// A [rows, cols] f32 matrix in boxes of [box_rows][32] with 128-byte swizzling, or -- plain_cols
+// > 0 -- of [box_rows][plain_cols] as it lies (no swizzle).
 mg_status tc_gemv_map(CUtensorMap* map, const float* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
-                      bool mn = false) {
+                      uint32_t plain_cols = 0) {
     auto fn = tc_gemv_encode_fn();
     if (!fn) return fail(MG_DRIVER_FAILED, "the driver does not provide cuTensorMapEncodeTiled");
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols * sizeof(float)};
-    cuuint32_t box[2] = {32, box_rows};
+    cuuint32_t box[2] = {plain_cols ? plain_cols : 32u, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, plain_cols ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MG_DRIVER_FAILED, "encoding a TMA descriptor failed (CUresult %d)", (int)r);
@@ -766,8 +788,9 @@ int env_min_rows(const char* name, int dflt) {
 }
 // Defaults from measurement at N = K = 4096 (six weights back to back): packed Q8_0 takes 11.5 -
 // 11.9 us here for 1 - 16 rows, on the CUDA cores 8.4 / 9.7 / 13.6 / 20.4 us for 1 / 2 / 4 / 6 rows
-// (61 us at 16); f32 at 16 rows 27 us here against 21 us on the CUDA cores -- the f32 form stays
-// off: its tf32 hi / lo terms pass through shared memory three times, which bounds it.
+// (61 us at 16); f32 takes 18.9 - 19.8 us here for 2 - 16 rows against 13.4 / 14.1 / 14.9 / 19.4 us
+// on the CUDA cores for 2 / 4 / 8 / 16 rows -- the f32 form stays off: its pace is one
+// converter -> MMA hand-off per 64 k (about 1 us per stage per CTA), not HBM.
 int tc_min_rows() {
     static int v = env_min_rows("MAGNETAR_CUDA_FEWROW_TC", kTcRows + 1);
     return v;
@@ -783,7 +806,7 @@ mg_status launch_gemv_tc(Device* d, const k::GemmArgs& g) {
     const uint64_t col_tiles = (g.n + kTcCols - 1) / kTcCols;
     if (col_tiles > 0x7FFFFFFFull) return fail(MG_SHAPE_UNSUPPORTED, "gemv n %llu is too wide", (unsigned long long)g.n);
     const int terms = g.gated ? 2 : 1;
-    constexpr uint64_t kStageK = (uint64_t)kTcK;
+    constexpr uint64_t kStageK = (uint64_t)S::kStageK;
     const uint64_t kb = (g.k + kStageK - 1) / kStageK;
     uint64_t splits = (uint64_t)d->sm_count / (col_tiles * terms);
     if (splits > (uint64_t)(kMaxCluster / terms)) splits = kMaxCluster / terms;
@@ -843,8 +866,8 @@ mg_status launch_gemv_tc(Device* d, const k::GemmArgs& g) {
     }
     CUtensorMap maps[3];
     MG_TRY(tc_gemv_map(&maps[0], g.a, g.m, g.k, kTcRows));
-    MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, kTcK, true));
-    if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, kTcK, true));
+    MG_TRY(tc_gemv_map(&maps[1], g.b, g.k, g.n, S::kStageK, kTcCols));
+    if (g.gated) MG_TRY(tc_gemv_map(&maps[2], g.b2, g.k, g.n, S::kStageK, kTcCols));
     else maps[2] = maps[1];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)col_tiles, (unsigned)p.splits, (unsigned)p.terms);

@@ -106,3 +106,14 @@ def test_tp_shares_tile_the_extent(mpc, extent, parts):
     assert ends[0][0] == 0 and ends[-1][1] == extent
     assert all(ends[i][1] == ends[i + 1][0] for i in range(parts - 1))
     assert all(tp.native_share(extent, parts, m) == ends[m] for m in range(parts))
+
+
+def test_torch_imports_after_the_library_in_a_fresh_process():
+    # The library links libnccl.so.2 by its soname; loading it first must not leave an older
+    # system NCCL in place of the one torch was built against (torch's import then fails).
+    import subprocess
+    import sys
+    code = ("import importlib, sys; sys.path.insert(0, sys.argv[1]); "
+            "importlib.import_module('magnetar-provider-cuda_b200._native').lib(); import torch; print('ok')")
+    res = subprocess.run([sys.executable, "-c", code, ROOT], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]

@@ -342,6 +342,49 @@ def test_fewrow_tensor_core_matmul(kernels, oracle, m, k, n, weight):
     np.testing.assert_array_equal(first, kernels.download(kernels.matmul(da, db)))  # deterministic
 
 
+_FEWROW_TC_CHILD = r"""
+import importlib, json, math, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+mpc = importlib.import_module("magnetar-provider-cuda_b200")
+kernels = mpc.CudaKernels(0)
+r = np.random.default_rng(23)
+out = []
+for m, k, n, gated in [(16, 4096, 4096, 0), (9, 64, 4, 0), (12, 4100, 260, 0), (10, 512, 1376, 1), (16, 1376, 512, 0)]:
+    a = (r.standard_normal((m, k)) / math.sqrt(k)).astype(np.float32)
+    b = r.standard_normal((k, n)).astype(np.float32)
+    da, db = kernels.upload(a), kernels.upload(b)
+    if gated:
+        u = r.standard_normal((k, n)).astype(np.float32)
+        got = kernels.download(kernels.gated_matmul(da, db, kernels.upload(u))).astype(np.float64)
+        g = a.astype(np.float64) @ b.astype(np.float64)
+        exp = g / (1.0 + np.exp(-g)) * (a.astype(np.float64) @ u.astype(np.float64))
+    else:
+        db.set_weight()
+        got = kernels.download(kernels.matmul(da, db)).astype(np.float64)
+        exp = a.astype(np.float64) @ b.astype(np.float64)
+    out.append(float(np.linalg.norm(got - exp) / np.linalg.norm(exp)))
+kernels.close()
+print(json.dumps(out))
+"""
+
+
+def test_fewrow_tensor_core_form_in_a_fresh_process():
+    # The f32 tensor-core few-row form is off by default and chosen once per process
+    # (MAGNETAR_CUDA_FEWROW_TC): a child process with it on checks it against f64 products.
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, MAGNETAR_CUDA_FEWROW_TC="2")
+    res = subprocess.run([sys.executable, "-c", _FEWROW_TC_CHILD, root], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
+    errs = json.loads(res.stdout.strip().splitlines()[-1])
+    assert len(errs) == 5 and max(errs) <= TOL_MATMUL, errs
+
+
 @pytest.mark.parametrize("m,k,n", [(16, 2048, 1000), (8, 512, 1376), (13, 4096, 128)])
 def test_fewrow_tensor_core_epilogues(kernels, oracle, m, k, n):
     r = rng(18)
