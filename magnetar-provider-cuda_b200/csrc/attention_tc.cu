@@ -760,7 +760,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
             failed = __any_sync(0xffffffffu, failed);
             if (failed) return;
             tc_fence_after();
-#pragma unroll
+#pragma unroll 1
             for (int c = 0; c < D; c += 32) {
                 float o[32];
                 tmem_ld32(lane_base + S::kColO + (uint32_t)c, o);
@@ -827,8 +827,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                 }
                 return ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             };
-            float pmul = 1.0f, f = 1.0f;
+            float pmul = 1.0f, f = 1.0f, a = 1.0f;
             bool need = false;
+            const float m_old = m;
             if (!safe) {
                 // the reference max moves only when this tile's passes it by more than 2^kLazy
                 need = tmax != kNegInf && (m == kNegInf || tmax > m + kLazy);
@@ -838,17 +839,19 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                     m = tmax;
                     l *= f;
                 }
-                l += weights(m);
+            } else {
+                m = fmaxf(m, tmax);
+                a = m_old == kNegInf ? 0.0f : ex2_sfu(m_old - m);
+            }
+            const float psum = weights(m);
+            if (!safe) {
+                l += psum;
             } else {
                 // the output stays a weighted mean of V rows: O <- O (l a / l_new) + (P / l_new) V
-                const float m_new = fmaxf(m, tmax);
-                const float a = m == kNegInf ? 0.0f : ex2_sfu(m - m_new);
-                const float psum = weights(m_new);
                 const float l_new = l * a + psum;
                 pmul = l_new > 0.0f ? 1.0f / l_new : 0.0f;
                 f = l_new > 0.0f ? (l * a) * pmul : 0.0f;
                 need = true;
-                m = m_new;
                 l = l_new;
             }
             if (j > 0 && __any_sync(0xffffffffu, need)) {
