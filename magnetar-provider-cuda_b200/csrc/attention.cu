@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kDecodeKeys) attention_decode_kernel(DecodeP p
 // The warps' states are merged once, in warp order, into the span's partial (max, sum,
 // output) for the combine kernel.
 constexpr int kDecodeThreads = 256;
-constexpr int kDecodeStages = 2;
+constexpr int kDecodeStages = 3;  // 2 -> 3: 0.0567 -> 0.0560 ms at 32768 keys
 constexpr int kDecodeTileKeys = 32;  // 4 keys per warp
 constexpr int kDecodeStageBytes = kDecodeTileKeys * 2 * kDecodeMaxDim * 4;  // 64 KB at D = Dv = 256
 
