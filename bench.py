@@ -721,8 +721,8 @@ def run_ours(args, world, rank, local):
 # launches of each kernel of this bench command (dram__bytes_read.sum + dram__bytes_write.sum,
 # caches flushed before each; the decoder-layer summary in profiles/), keyed by the node's output
 # id.  Writes stay in the L2 at this size.
-LAYER_NODE_TRAFFIC = {"x": 276480, "h": 285952, "q": 2411008, "k": 2410752, "v": 2410496, "qr": 320000,
-                      "kr": 320000, "a": 837376, "x2": 2673408, "h2": 285952, "g": 11599104, "out": 6654208}
+LAYER_NODE_TRAFFIC = {"x": 276480, "h": 285952, "q": 1362944, "k": 1362176, "v": 1362176, "qr": 320000,
+                      "kr": 320000, "a": 837376, "x2": 1624576, "h2": 285952, "g": 5961728, "out": 3836672}
 
 
 def dominant_roofline(cfg, inv, ms, peaks, tf32):

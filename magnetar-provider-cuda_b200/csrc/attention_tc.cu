@@ -521,6 +521,8 @@ struct Attn2Params {
     uint64_t qpos0;  // position of query 0
     float scale;
     int q_pairs;            // CTAs per head: 256 queries each
+    const float* q;         // f32 queries [seq_len, q_ld]: each query row is split by its own thread
+    uint64_t q_ld;
     const unsigned* vmax;   // bits of max |v| over V (written by the split pass)
     unsigned safe_bits;     // from this max on: the weighted-mean form
     int* error;
@@ -544,8 +546,7 @@ struct Attn2Shape {
 
 template <int D>
 __global__ void __launch_bounds__(kAttnTcThreads, 1)
-    attention_tc2_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
-                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
+    attention_tc2_kernel(const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
                          const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
                          Attn2Params p) {
     using S = Attn2Shape<D>;
@@ -554,6 +555,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     __shared__ uint32_t tmem_slot;
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* base_ptr = smem_raw + (base - raw);
     const uint32_t b0 = smem_u32(bars);
     const uint32_t q_full = b0, v_full = b0 + 8, v_empty = b0 + 16;
     auto k_full = [&](int b) { return b0 + 24 + 8u * (uint32_t)b; };
@@ -595,7 +597,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < 19; i++) {
             const uint32_t bar = b0 + 8u * (uint32_t)i;
-            mbar_init(bar, bar >= p_full(0, 0) && bar <= p_full(1, 1) ? 4 : 1);  // P: the tile's four softmax warps
+            // P: the tile's four softmax warps; Q: all eight softmax warps
+            mbar_init(bar, bar >= p_full(0, 0) && bar <= p_full(1, 1) ? 4 : bar == q_full ? 8 : 1);
         }
         fence_barrier_init();
     }
@@ -612,14 +615,6 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     if (warp == 0) {
         // ---- TMA producer ----------------------------------------------------------------------
         if (lane == 0 && n_kv > 0) {
-            const int tiles = n_t[1] > 0 ? 2 : 1;
-            mbar_arrive_expect_tx(q_full, (uint32_t)(2 * tiles * S::kQ));
-            for (int t = 0; t < tiles; t++)
-                for (int a = 0; a < D / 64; a++) {
-                    const uint32_t dst = base + S::kOffQ + (uint32_t)(2 * t * S::kQ + a * S::kQAtom);
-                    tma_load_2d(dst, &map_qhi, q_full, (int)(head * D + a * 64), (int)(q0 + (uint64_t)t * AQ));
-                    tma_load_2d(dst + S::kQ, &map_qlo, q_full, (int)(head * D + a * 64), (int)(q0 + (uint64_t)t * AQ));
-                }
             // K of tile j into slot j % 2, once the scores of tile j - 2 (the slot's last user)
             // are done: K runs ahead of V.
             auto load_k = [&](int j) -> bool {
@@ -737,6 +732,34 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         const int r = qq * 32 + lane;
         const uint64_t qi = q0 + (uint64_t)t * AQ + r;
         const bool live = qi < p.seq_len;
+        {
+            // This thread's query row as bf16 hi / lo terms in the MMA's K-major layout: 64
+            // columns per 128-byte row of an atom, 16-byte chunk c at position c ^ (r % 8); zeros
+            // past the sequence.  (Each query row belongs to this CTA alone, so it is split here
+            // rather than by a pass over Q.)
+            const float* qrow = p.q + (live ? qi : 0) * p.q_ld + head * D;
+            uint8_t* qt = base_ptr + S::kOffQ + (size_t)(2 * t) * S::kQ + (size_t)r * 128;
+#pragma unroll
+            for (int c8 = 0; c8 < D / 8; c8++) {  // eight columns: one 16-byte chunk per term
+                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+                if (live) {
+                    x0 = __ldg(reinterpret_cast<const float4*>(qrow + 8 * c8));
+                    x1 = __ldg(reinterpret_cast<const float4*>(qrow + 8 * c8 + 4));
+                }
+                const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                uint16_t h[8], lo[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) split_bf16(xs[e], h[e], lo[e]);
+                const int a = c8 / 8, c = c8 % 8;
+                const size_t off = (size_t)a * S::kQAtom + (size_t)((c ^ (r & 7)) * 16);
+                *reinterpret_cast<uint4*>(qt + off) =
+                    make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
+                *reinterpret_cast<uint4*>(qt + S::kQ + off) = make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]),
+                                                                          pack_bf16(lo[4], lo[5]), pack_bf16(lo[6], lo[7]));
+            }
+            fence_proxy_async();  // the generic-proxy writes are read by tcgen05.mma
+            mbar_arrive_warp(q_full);
+        }
         const uint64_t qpos = p.qpos0 + qi;
         const uint64_t row_hi = live ? (p.causal ? min(p.kv_seq_len, qpos + 1) : p.kv_seq_len) : 0;
         uint64_t row_lo = 0;
@@ -1000,6 +1023,8 @@ mg_status launch_attention_tc2(Device* d, const k::AttentionArgs& a, const CUten
     p.qpos0 = a.query_position_offset;
     p.scale = a.scale;
     p.q_pairs = (int)((a.seq_len + 2 * AQ - 1) / (2 * AQ));
+    p.q = a.q;
+    p.q_ld = a.q_model_dim;
     p.vmax = vmax;
     // The unnormalised sum stays below n_keys * 2^kAttnLazyLog2 * max |v|: the weighted-mean
     // form from max |v| >= 2^(118 - kAttnLazyLog2 - ceil(log2 n_keys)), keeping 2^10 of headroom
@@ -1010,8 +1035,7 @@ mg_status launch_attention_tc2(Device* d, const k::AttentionArgs& a, const CUten
     p.safe_bits = (unsigned)(e + 127) << 23;
     p.error = d->flags + 2;
     dim3 grid((unsigned)p.q_pairs, (unsigned)a.head_count);
-    enqueue(d, attention_tc2_kernel<D>, grid, kAttnTcThreads, S::kSmem, maps[0], maps[1], maps[2], maps[3], maps[4],
-                                                                           maps[5], p);
+    enqueue(d, attention_tc2_kernel<D>, grid, kAttnTcThreads, S::kSmem, maps[2], maps[3], maps[4], maps[5], p);
     return launched(d, "tensor-core attention launch");
 }
 
@@ -1031,7 +1055,12 @@ bool attention_tc_eligible(const AttentionArgs& a) {
 mg_status attention_tc(Device* d, const AttentionArgs& a) {
     const uint64_t S = a.seq_len, Skv = a.kv_seq_len, qd = a.q_model_dim, kvd = a.kv_model_dim;
     const uint64_t skv_p = (Skv + 7) & ~7ull;  // V^T rows are 16-byte multiples
-    const size_t q_elems = S * qd, k_elems = Skv * kvd, vt_elems = kvd * skv_p;
+    static const bool one_tile = [] {
+        const char* e = getenv("MAGNETAR_CUDA_ATTN_ONE_TILE");
+        return e && atoi(e) != 0;
+    }();
+    // Q's terms only for the one-tile kernel: the two-tile kernel splits its query rows itself.
+    const size_t q_elems = one_tile ? S * qd : 0, k_elems = Skv * kvd, vt_elems = kvd * skv_p;
     uint16_t* ws = nullptr;
     const size_t terms = 2 * (q_elems + k_elems + vt_elems) * sizeof(uint16_t);
     MG_TRY(scratch(d, 4, terms + 16, (void**)&ws));
@@ -1044,24 +1073,25 @@ mg_status attention_tc(Device* d, const AttentionArgs& a) {
     unsigned* vmax = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(ws) + terms);
     dim3 tg((unsigned)((kvd + 63) / 64), (unsigned)((skv_p + 63) / 64));
     if (tg.y > 65535) return fail(MG_SHAPE_UNSUPPORTED, "attention has too many keys for the split pass");
-    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, q_elems / 4), 256, 0, a.q, qhi, qlo, q_elems, vmax);
-    MG_TRY(launched(d, "attention split launch"));
-    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, k_elems / 4), 256, 0, a.k, khi, klo, k_elems, (unsigned*)nullptr);
+    if (one_tile) {
+        enqueue(d, split_bf16_rows_kernel, grid_for_n(d, q_elems / 4), 256, 0, a.q, qhi, qlo, q_elems, (unsigned*)nullptr);
+        MG_TRY(launched(d, "attention split launch"));
+    }
+    // the K pass also zeroes the V pass's max |v| word
+    enqueue(d, split_bf16_rows_kernel, grid_for_n(d, k_elems / 4), 256, 0, a.k, khi, klo, k_elems, vmax);
     MG_TRY(launched(d, "attention split launch"));
     enqueue(d, split_bf16_transpose_kernel, tg, 256, 0, a.v, Skv, kvd, vhi, vlo, skv_p, vmax);
     MG_TRY(launched(d, "attention split launch"));
     const int D = (int)a.head_dim;
     CUtensorMap maps[6];
-    MG_TRY(bf16_map(&maps[0], qhi, S, qd, qd, AQ));
-    MG_TRY(bf16_map(&maps[1], qlo, S, qd, qd, AQ));
+    if (one_tile) {
+        MG_TRY(bf16_map(&maps[0], qhi, S, qd, qd, AQ));
+        MG_TRY(bf16_map(&maps[1], qlo, S, qd, qd, AQ));
+    }
     MG_TRY(bf16_map(&maps[2], khi, Skv, kvd, kvd, AKV));
     MG_TRY(bf16_map(&maps[3], klo, Skv, kvd, kvd, AKV));
     MG_TRY(bf16_map(&maps[4], vhi, kvd, Skv, skv_p, (uint32_t)D));
     MG_TRY(bf16_map(&maps[5], vlo, kvd, Skv, skv_p, (uint32_t)D));
-    static const bool one_tile = [] {
-        const char* e = getenv("MAGNETAR_CUDA_ATTN_ONE_TILE");
-        return e && atoi(e) != 0;
-    }();
     if (!one_tile) return D == 64 ? launch_attention_tc2<64>(d, a, maps, vmax) : launch_attention_tc2<128>(d, a, maps, vmax);
     const int q_tiles = (int)((S + AQ - 1) / AQ);
     if (D == 64) return launch_attention_tc<64>(d, a, maps, q_tiles);

@@ -192,8 +192,7 @@ struct TcShape {
     // 32-bit operands), into the B hi slot; the converter warps split it element by element, hi
     // in place and lo into the lo slot at the same offsets -- no transpose.
     static constexpr int kStage = 2 * kATile + NB * 2 * kBTile;
-    static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + (B_RAW ? kBTile : NB * 2 * kBTile);  // TMA bytes per stage
-    static_assert(!B_RAW || NB == 1, "raw B is for plain matmuls");
+    static constexpr int kTxBytes = (A_RAW ? 1 : 2) * kATile + (B_RAW ? NB : NB * 2) * kBTile;  // TMA bytes per stage
     static constexpr int kRing = STAGES * kStage;
     static constexpr int kLd = BN + 4;  // row stride (floats) of a staged tile and of the receive slots
     static_assert(NB * BM * kLd * 4 <= kRing, "the staged tile fits the drained ring");
@@ -288,8 +287,12 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         const int kx = (kb0 + i) * BK;
         if (B_RAW) {
 #pragma unroll
-            for (int j = 0; j < BN / 32; j++)  // [BK rows of k][32 columns] per box
+            for (int j = 0; j < BN / 32; j++) {  // [BK rows of k][32 columns] per box
                 tma_load_2d(st + 2 * S::kATile + (uint32_t)(j * 32 * BK * 4), map_whi, full_bar(s), n0 + 32 * j, kx);
+                if (NB == 2)  // the up weight into the second term's hi slot
+                    tma_load_2d(st + 2 * S::kATile + 2 * S::kBTile + (uint32_t)(j * 32 * BK * 4), &map_b2hi, full_bar(s),
+                                n0 + 32 * j, kx);
+            }
             return;
         }
         tma_load_2d(st + 2 * S::kATile, map_whi, full_bar(s), kx, n0);
@@ -312,7 +315,10 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
         const int kx = (kb0 + i) * BK;
         if (B_RAW) {
 #pragma unroll
-            for (int j = 0; j < BN / 32; j++) tma_prefetch_2d(map_whi, n0 + 32 * j, kx);
+            for (int j = 0; j < BN / 32; j++) {
+                tma_prefetch_2d(map_whi, n0 + 32 * j, kx);
+                if (NB == 2) tma_prefetch_2d(&map_b2hi, n0 + 32 * j, kx);
+            }
         } else {
             tma_prefetch_2d(map_whi, kx, n0);
             if (p.b_terms == 2) tma_prefetch_2d(map_wlo, kx, n0);
@@ -491,14 +497,17 @@ __global__ void __launch_bounds__(TcShape<BN, NB, STAGES, A_RAW, SPLIT, B_RAW>::
                 }
                 if (B_RAW) {
                     // element by element: hi in place, lo at the same offset of the lo slot
-                    const uint32_t b_hi = st + 2 * S::kATile, b_lo = b_hi + S::kBTile;
 #pragma unroll
-                    for (int j = 0; j < S::kBTile / 16 / kConvThreads; j++) {
-                        const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
-                        float4 h, l;
-                        split4_fast(lds4(b_hi + off), h, l);
-                        sts4(b_hi + off, h.x, h.y, h.z, h.w);
-                        sts4(b_lo + off, l.x, l.y, l.z, l.w);
+                    for (int z = 0; z < NB; z++) {
+                        const uint32_t b_hi = st + 2 * S::kATile + (uint32_t)(z * 2 * S::kBTile), b_lo = b_hi + S::kBTile;
+#pragma unroll
+                        for (int j = 0; j < S::kBTile / 16 / kConvThreads; j++) {
+                            const uint32_t off = (uint32_t)(t + j * kConvThreads) * 16;
+                            float4 h, l;
+                            split4_fast(lds4(b_hi + off), h, l);
+                            sts4(b_hi + off, h.x, h.y, h.z, h.w);
+                            sts4(b_lo + off, l.x, l.y, l.z, l.w);
+                        }
                     }
                 }
                 if (A_RAW) tc_wait_st();  // the A terms are in the tensor memory
@@ -834,6 +843,23 @@ mg_status launch_bn_raw_b(Device* d, int bn, const TcParams& p, const CUtensorMa
     return launch_tc<32, 1, 5, A_RAW, kSplitRingRecv, true>(d, p, maps);
 }
 
+template <bool A_RAW>
+mg_status launch_bn_raw_b2(Device* d, int bn, const TcParams& p, const CUtensorMap* maps) {
+    const int mode = p.splits <= 1 ? kNoSplit : p.kb_per_split < 8 ? kSplitOwnRecv : kSplitRingRecv;
+    if (bn == 128 && mode == kNoSplit) return launch_tc<128, 2, 2, A_RAW, kNoSplit, true>(d, p, maps);
+    if (bn == 64) {
+        if (mode == kNoSplit) return launch_tc<64, 2, 3, A_RAW, kNoSplit, true>(d, p, maps);
+        if (mode == kSplitOwnRecv) return launch_tc<64, 2, 2, A_RAW, kSplitOwnRecv, true>(d, p, maps);
+        return launch_tc<64, 2, 3, A_RAW, kSplitRingRecv, true>(d, p, maps);
+    }
+    if (bn == 32) {
+        if (mode == kNoSplit) return launch_tc<32, 2, 4, A_RAW, kNoSplit, true>(d, p, maps);
+        if (mode == kSplitOwnRecv) return launch_tc<32, 2, 3, A_RAW, kSplitOwnRecv, true>(d, p, maps);
+        return launch_tc<32, 2, 4, A_RAW, kSplitRingRecv, true>(d, p, maps);
+    }
+    return fail(MG_EXECUTION_FAILED, "gated matmul tile width %d with split k", bn);
+}
+
 // k splits per tile at most (MAGNETAR_CUDA_GEMM_MAX_SPLITS, 2..16): the CTAs of one cluster,
 // portable up to 8; 16 where the GPU holds such clusters (launch_tc checks).  Measured with 16
 // against 8: 128 x 1376 x 512 (the decoder layer's down projection) 9.3 against 9.9 us; the other
@@ -892,20 +918,33 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
         ahi = a_split;
         alo = a_split + g.m * kp;
     }
-    // B raw (split in the kernel, no separate pass over B): for a plain matmul with one row of
-    // tiles (M <= 128) whose B has no prepared form.  Its tiles arrive MN-major as B lies, the MMA
-    // reads them so, and the converters split each element in place (hi) and beside it (lo).
-    // Measured at K = N = 4096, M = 128: 34.5 us against 44.7 us with a split pass.  A prepared
-    // weight keeps its hi / lo form (32.8 us; raw, MAGNETAR_CUDA_GEMM_RAW_WEIGHTS=1: 34.4 us --
-    // the main loop is bound by the 3xTF32 MMAs either way, and the converters' extra pass costs
-    // more than the halved weight traffic saves).
+    // B raw (split in the kernel, no separate pass over B): with one row of tiles (M <= 128), for
+    // a B that has no prepared form.  Its tiles arrive MN-major as B lies, the MMA reads them so,
+    // and the converters split each element in place (hi) and beside it (lo).  Measured at
+    // K = N = 4096, M = 128: 34.5 us against 44.7 us with a split pass.
+    // A weight's prepared hi / lo form costs twice its f32 bytes per read.  Raw weights halve
+    // that at the same speed for k <= 2048 (the decoder layer's projections: 55.35 vs 55.37 us per
+    // step, the gated node 11.8 vs 12.0 us), while at K = N = 4096 the prepared form is faster
+    // (32.8 vs 34.4 us: the main loop is bound by the 3xTF32 MMAs, and the converters' extra pass
+    // costs more than the halved weight traffic saves).  So weights are read raw up to k = 2048;
+    // MAGNETAR_CUDA_GEMM_RAW_WEIGHTS=0 / 1 reads them prepared / raw at every k.
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-    static const bool raw_weights = [] {
+    static const int raw_weights_env = [] {
         const char* e = getenv("MAGNETAR_CUDA_GEMM_RAW_WEIGHTS");
-        return e && atoi(e) != 0;
+        return e && *e ? (atoi(e) != 0 ? 1 : 0) : -1;
     }();
-    const bool b_raw = count == 1 && nb == 1 && !g.transpose_b && g.n % 4 == 0 && al16(g.b) && !g.packed[0] &&
-                       (g.b_prep[0] == nullptr || raw_weights) && g.m <= 128;
+    const bool raw_weights = raw_weights_env > 0 || (raw_weights_env < 0 && g.k <= 2048);
+    // The same for a gated matmul (gate and up both raw) and a grouped projection (every weight
+    // raw); a weight whose prepared lo term is zero keeps its one-term prepared form.
+    auto raw_ok = [&](const float* b, const float* prep, int one_term) {
+        return b && al16(b) && (prep == nullptr || (raw_weights && !one_term));
+    };
+    bool b_raw = !g.transpose_b && g.n % 4 == 0 && !g.packed[0] && !g.packed[1] && g.m <= 128;
+    if (nb == 2) {
+        b_raw = b_raw && raw_ok(g.b, g.b_prep[0], g.b_one_term[0]) && raw_ok(g.b2, g.b_prep[1], g.b_one_term[1]);
+    } else {
+        for (int w = 0; w < count; w++) b_raw = b_raw && raw_ok(gs[w].b, gs[w].b_prep[0], gs[w].b_one_term[0]);
+    }
     // B terms: [term or weight] -> hi, lo ([n, kp] each)
     const int nw = nb == 2 ? 2 : count;
     const float* bhi[3];
@@ -940,7 +979,9 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
     p.k = g.k;
     p.error = d->flags + 2;
     // raw B may load early when it is a weight (nothing earlier in the stream writes it)
-    p.b_early = (b_raw ? g.b_stable != 0 : stable) ? 1 : 0;
+    bool raw_stable = true;
+    for (int w = 0; w < (nb == 2 ? 1 : count); w++) raw_stable = raw_stable && gs[w].b_stable != 0;
+    p.b_early = (b_raw ? raw_stable : stable) ? 1 : 0;
     p.prefetch = g.m <= 128 ? 1 : 0;
     // One B term when every weight read is a prepared form whose lo term is all zero.
     bool one_term = !b_raw;
@@ -987,9 +1028,10 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
     }
     for (int w = 0; w < 3; w++) {
         if (b_raw) {
-            if (w == 0) MG_TRY(make_raw_b_map(&maps[2], g.b, g.k, g.n));
+            // weight w's raw map in its hi slot (the lo slot unused)
+            if (w < nw) MG_TRY(make_raw_b_map(&maps[2 + 2 * w], nb == 2 ? (w ? g.b2 : g.b) : gs[w].b, g.k, g.n));
             else maps[2 + 2 * w] = maps[2];
-            maps[3 + 2 * w] = maps[2];
+            maps[3 + 2 * w] = maps[2 + 2 * w];
         } else if (w < nw) {
             MG_TRY(make_map(&maps[2 + 2 * w], bhi[w], g.n, kp, kp, bn));
             MG_TRY(make_map(&maps[3 + 2 * w], blo[w], g.n, kp, kp, bn));
@@ -998,6 +1040,7 @@ mg_status gemm_tc_group(Device* d, const GemmArgs* gs, int count, const RopeK* r
             maps[3 + 2 * w] = maps[3];
         }
     }
+    if (b_raw && nb == 2) return a_raw ? launch_bn_raw_b2<true>(d, bn, p, maps) : launch_bn_raw_b2<false>(d, bn, p, maps);
     if (b_raw) return a_raw ? launch_bn_raw_b<true>(d, bn, p, maps) : launch_bn_raw_b<false>(d, bn, p, maps);
     mg_status s;
     if (nb == 2) s = a_raw ? launch_bn<2, true>(d, bn, p, maps) : launch_bn<2, false>(d, bn, p, maps);
