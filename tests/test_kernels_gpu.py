@@ -540,6 +540,61 @@ def test_attention_large_values_stay_finite(kernels):
     assert np.all(np.isfinite(got)) and np.all(np.abs(got / 1e38 - 1) < 1e-4)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_tensor_core_attention_large_values_keep_the_weighted_mean_form(kernels, oracle, d):
+    # src/tests_conformance.rs:884-914 at a length the tensor-core kernel takes: |V| near f32::MAX
+    # would overflow an unnormalised sum, so the kernel keeps the output a weighted mean of V rows.
+    rows = 640
+    q = np.zeros((rows, d), np.float32)
+    v = np.full((rows, d), 1e38, np.float32)
+    got = kernels.download(kernels.attention(kernels.upload(q), kernels.upload(q), kernels.upload(v), 1, d,
+                                             causal=True))
+    assert np.all(np.isfinite(got)) and np.all(np.abs(got / 1e38 - 1) < 1e-4)
+    # large but distinct values: the weighted-mean form against the oracle
+    r = rng(31)
+    q = r.standard_normal((rows, 2 * d)).astype(np.float32)
+    k = r.standard_normal((rows, 2 * d)).astype(np.float32)
+    v = (r.standard_normal((rows, 2 * d)) * 1e30).astype(np.float32)
+    got = kernels.download(kernels.attention(kernels.upload(q), kernels.upload(k), kernels.upload(v), 2, d,
+                                             causal=True))
+    assert rel(got, oracle.attention(q, k, v, 2, d, causal=True)) <= TOL_MATMUL
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_tensor_core_attention_rescales_when_the_row_max_jumps(kernels, oracle, causal):
+    # Scores that grow along the keys by far more than 2^12 in log2 units from one 64-key tile to
+    # the next: the kernel's reference max has to move (and the output be rescaled) many times.
+    rows, d = 700, 128
+    r = rng(32)
+    q = r.standard_normal((rows, d)).astype(np.float32)
+    k = r.standard_normal((rows, d)).astype(np.float32)
+    k *= (1.0 + np.arange(rows, dtype=np.float32) / 16.0)[:, None]
+    v = r.standard_normal((rows, d)).astype(np.float32)
+    got = kernels.download(kernels.attention(kernels.upload(q), kernels.upload(k), kernels.upload(v), 1, d,
+                                             causal=causal))
+    assert rel(got, oracle.attention(q, k, v, 1, d, causal=causal)) <= TOL_MATMUL
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 512, 1376), (96, 2048, 256), (128, 2049, 136), (40, 1376, 512)])
+def test_weights_read_raw_or_prepared(kernels, oracle, m, k, n):
+    # Weights are read raw (split in the GEMM) up to k = 2048 and through their prepared hi / lo
+    # form beyond: plain, gated and residual forms on both sides of the switch.
+    r = rng(33)
+    a = r.standard_normal((m, k)).astype(np.float32)
+    g = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    u = (r.standard_normal((k, n)) * 0.05).astype(np.float32)
+    res = r.standard_normal((m, n)).astype(np.float32)
+    da, dg, du = kernels.upload(a), kernels.upload(g), kernels.upload(u)
+    dg.set_weight()
+    du.set_weight()
+    for _ in range(2):  # the first call builds the prepared forms, the second reads them settled
+        assert rel(kernels.download(kernels.matmul(da, dg)), oracle.matmul(a, g)) <= TOL_MATMUL
+        got = kernels.download(kernels.gated_matmul(da, dg, du))
+        assert rel(got, oracle.gated_matmul(a, g, u)) <= TOL_MATMUL
+        got = kernels.download(kernels.matmul_residual(da, dg, kernels.upload(res)))
+        assert rel(got, oracle.matmul(a, g, addend=res, addend_mode=2)) <= TOL_MATMUL
+
+
 def test_attention_validation(kernels, mpc):
     q = kernels.upload(np.zeros((4, 8), np.float32))
     for kw in (dict(head_count=3, head_dimension=4), dict(head_count=2, head_dimension=4, kv_head_count=3),
