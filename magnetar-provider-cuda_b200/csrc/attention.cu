@@ -298,15 +298,15 @@ __global__ void __launch_bounds__(kShortThreads) attention_short_kernel(AttnP p,
         if (32 * t >= n) continue;
         if (j < n) {
             const float4* kr = reinterpret_cast<const float4*>(ks + j * P::kKStride);
-            float acc = 0.0f;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four independent chains over the columns
 #pragma unroll
             for (int c = 0; c < C4; c++) {
                 const float4 kk = kr[c];
                 const float4 qq = kQRegs ? qr[kQRegs ? c : 0] : reinterpret_cast<const float4*>(qrow)[c];
-                acc += qq.x * kk.x + qq.y * kk.y + qq.z * kk.z + qq.w * kk.w;
+                acc[c & 3] += qq.x * kk.x + qq.y * kk.y + qq.z * kk.z + qq.w * kk.w;
             }
             const uint64_t key = span_lo + j;
-            sc[t] = (key >= qlo && key < qhi) ? acc * p.scale : ninf;
+            sc[t] = (key >= qlo && key < qhi) ? ((acc[0] + acc[1]) + (acc[2] + acc[3])) * p.scale : ninf;
         }
         m = fmaxf(m, sc[t]);
     }
@@ -327,35 +327,36 @@ __global__ void __launch_bounds__(kShortThreads) attention_short_kernel(AttnP p,
         if (32 * t >= n) break;
         sc[t] = m == ninf ? 0.0f : sc[t] / l;
     }
-    // 3. P.V: columns C * lane .. C * lane + C - 1, keys in order, two chains
-    float o0[C], o1[C];
+    // 3. P.V: columns C * lane .. C * lane + C - 1, keys in order, four chains
+    float o[4][C];
 #pragma unroll
-    for (int e = 0; e < C; e++) o0[e] = o1[e] = 0.0f;
+    for (int e = 0; e < C; e++) o[0][e] = o[1][e] = o[2][e] = o[3][e] = 0.0f;
 #pragma unroll
     for (int t = 0; t < kT; t++) {
         if (32 * t >= n) break;
         const int kn = min(32, n - 32 * t);
         const float* vrow0 = vs + (32 * t) * D + C * lane;
         int u = 0;
-        for (; u + 1 < kn; u += 2) {
-            const float w0 = __shfl_sync(0xffffffffu, sc[t], u), w1 = __shfl_sync(0xffffffffu, sc[t], u + 1);
+        for (; u + 3 < kn; u += 4) {
+            float w[4];
+#pragma unroll
+            for (int h = 0; h < 4; h++) w[h] = __shfl_sync(0xffffffffu, sc[t], u + h);
             const float* v0 = vrow0 + u * D;
 #pragma unroll
-            for (int e = 0; e < C; e++) {
-                o0[e] += w0 * v0[e];
-                o1[e] += w1 * v0[D + e];
-            }
+            for (int h = 0; h < 4; h++)
+#pragma unroll
+                for (int e = 0; e < C; e++) o[h][e] += w[h] * v0[h * D + e];
         }
-        if (u < kn) {
+        for (; u < kn; u++) {
             const float w0 = __shfl_sync(0xffffffffu, sc[t], u);
             const float* v0 = vrow0 + u * D;
 #pragma unroll
-            for (int e = 0; e < C; e++) o0[e] += w0 * v0[e];
+            for (int e = 0; e < C; e++) o[0][e] += w0 * v0[e];
         }
     }
     float* orow = p.out + ((q0 + qi) * p.head_count + head) * D + C * lane;
 #pragma unroll
-    for (int e = 0; e < C; e++) orow[e] = o0[e] + o1[e];
+    for (int e = 0; e < C; e++) orow[e] = (o[0][e] + o[1][e]) + (o[2][e] + o[3][e]);
 }
 
 // Largest key span any CTA of the short kernel sees: all keys, or a causal window plus the
