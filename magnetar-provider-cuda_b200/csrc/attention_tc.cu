@@ -652,16 +652,23 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         if (lane == 0 && n_kv > 0) {
             constexpr uint32_t idesc_s = idesc_bf16(AQ, AKV);
             constexpr uint32_t idesc_o = idesc_bf16(AQ, D);
+            // Shared-memory descriptors advance by (byte offset >> 4) in their start-address
+            // field: the operands' descriptors are the region's base descriptor plus constants, so
+            // the issuing thread spends a few adds per MMA (it shares its scheduler with two
+            // softmax warps).
+            const uint64_t dq0 = desc_k_sw128(base + S::kOffQ), dk0 = desc_k_sw128(base + S::kOffK);
+            const uint64_t dv0 = desc_k_sw128(base + S::kOffV);
             // S_t(j) = Q_t K(j)^T into tile t's score buffer j % 2
             auto issue_s = [&](int t, int j) {
                 const uint32_t tS = tmem + 256u * (uint32_t)t + (uint32_t)(j & 1) * AKV;
+                const uint64_t dq = dq0 + (uint64_t)((2 * t * S::kQ) >> 4);
+                const uint64_t dk = dk0 + (uint64_t)(((j & 1) * 2 * S::kK) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t off = (uint32_t)(kk % 4) * 32;
-                    const uint32_t qa = base + S::kOffQ + (uint32_t)(2 * t * S::kQ + (kk / 4) * S::kQAtom) + off;
-                    const uint32_t kb = base + S::kOffK + (uint32_t)((j & 1) * 2 * S::kK + (kk / 4) * S::kKAtom) + off;
-                    const uint64_t qhi = desc_k_sw128(qa), qlo = desc_k_sw128(qa + S::kQ);
-                    const uint64_t khi = desc_k_sw128(kb), klo = desc_k_sw128(kb + S::kK);
+                    const uint32_t off = (uint32_t)(((kk / 4) * S::kQAtom + (kk % 4) * 32) >> 4);
+                    const uint32_t offk = (uint32_t)(((kk / 4) * S::kKAtom + (kk % 4) * 32) >> 4);
+                    const uint64_t qhi = dq + off, qlo = qhi + (uint64_t)(S::kQ >> 4);
+                    const uint64_t khi = dk + offk, klo = khi + (uint64_t)(S::kK >> 4);
                     mma_bf16(tS, qlo, khi, idesc_s, kk > 0 ? 1u : 0u);
                     mma_bf16(tS, qhi, klo, idesc_s, 1u);
                     mma_bf16(tS, qhi, khi, idesc_s, 1u);
@@ -697,8 +704,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
                         const uint32_t tO = tmem + 256u * (uint32_t)t + S::kColO;
 #pragma unroll
                         for (int kk = 0; kk < AKV / 16; kk++) {
-                            const uint32_t vb = base + S::kOffV + (uint32_t)kk * 32;
-                            const uint64_t vhi = desc_k_sw128(vb), vlo = desc_k_sw128(vb + S::kV);
+                            const uint64_t vhi = dv0 + (uint64_t)(kk * 2), vlo = vhi + (uint64_t)(S::kV >> 4);
                             const uint32_t ahi = tP + (uint32_t)kk * 8, alo = ahi + 32;
                             mma_bf16_ts(tO, alo, vhi, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                             mma_bf16_ts(tO, ahi, vlo, idesc_o, 1u);
