@@ -497,20 +497,21 @@ __device__ __forceinline__ float ex2_sfu(float x) {
 // loads.  Tensor memory holds, per query tile t, two 64-key score buffers (columns 256 t and
 // 256 t + 64) and the output accumulator (256 t + 128, D columns).  Warp 0 loads with TMA, warp
 // 1 issues the MMAs, warps 4-7 (tile 0) and 8-11 (tile 1) -- one query row per thread, one
-// tensor-memory lane quarter per warp -- run the softmax.  The softmax writes P as bf16 hi / lo
+// tensor-memory lane quarter per warp -- first split their query rows into the Q tiles, then run
+// the softmax.  The softmax writes P as bf16 hi / lo
 // over the scores it has just read (two bf16 per column), and the P.V MMA reads P from tensor
 // memory as its A operand and accumulates into the output there: no P round trip through shared
 // memory and no per-tile fold of P.V into registers.  The MMA warp issues S(j + 2) of a tile
 // right after that tile's P.V(j) (tensor-core operations of one thread run in order), so the
 // score buffer P(j) lived in is rewritten only after P.V(j) has read it.
 //
-// The output accumulates unnormalised (P = 2^(s - m) with a reference max m that moves only when
-// a tile's row max passes it by more than 2^12; the output and sum are then rescaled in tensor
-// memory) and is divided by the sum at the end.  When |V| is large enough for that sum to
+// The output accumulates unnormalised (P = 2^(s - m), s and m in log2 units, with a reference max
+// m that moves only when a tile's row max exceeds it by more than 12, a factor of 2^12; the
+// output and sum are then rescaled in tensor memory) and is divided by the sum at the end.  When |V| is large enough for that sum to
 // overflow (the split pass records max |v|), every tile instead rescales the output so that it
 // stays a weighted mean of V rows (the reference's overflow-safety invariant).
-// The reference max of the unnormalised form trails the true row max by at most 2^12: weights
-// stay below 4096, and the output is rescaled only when a tile passes the reference by more.
+// The reference max of the unnormalised form trails the true row max by at most 12 in log2 units:
+// weights stay below 2^12 = 4096, and the output is rescaled only when a tile passes it by more.
 constexpr int kAttnLazyLog2 = 12;
 
 struct Attn2Params {
