@@ -591,7 +591,9 @@ def run_ours(args, world, rank, local):
             flush()
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
-            gpu_busy(torch)
+            # the spin (before the start event) outlasts the host's enqueueing of the step even
+            # when several ranks share the host's cores
+            gpu_busy(torch, 200.0 if world == 1 else 1000.0)
             s.record()
             ex.launch_step()
             e.record()
