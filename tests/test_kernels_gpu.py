@@ -385,6 +385,56 @@ def test_fewrow_tensor_core_form_in_a_fresh_process():
     assert len(errs) == 5 and max(errs) <= TOL_MATMUL, errs
 
 
+_SWITCHED_PATHS_CHILD = r"""
+import importlib, json, math, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+mpc = importlib.import_module("magnetar-provider-cuda_b200")
+from oracle import oracle as orc
+orc.build()
+kernels = mpc.CudaKernels(0)
+r = np.random.default_rng(29)
+out = []
+for seq, heads, kvh, d, causal in [(640, 2, 2, 128, True), (384, 4, 2, 64, False), (300, 2, 1, 128, True)]:
+    q = r.standard_normal((seq, heads * d)).astype(np.float32)
+    k = r.standard_normal((seq, kvh * d)).astype(np.float32)
+    v = r.standard_normal((seq, kvh * d)).astype(np.float32)
+    got = kernels.download(kernels.attention(kernels.upload(q), kernels.upload(k), kernels.upload(v), heads, d,
+                                             kv_head_count=kvh, causal=causal))
+    exp = orc.attention(q, k, v, heads, d, kv_head_count=kvh, causal=causal)
+    out.append(float(np.linalg.norm(got - exp) / np.linalg.norm(exp)))
+for m, kk, n in [(128, 512, 1376), (64, 1376, 512)]:
+    a = r.standard_normal((m, kk)).astype(np.float32)
+    g = (r.standard_normal((kk, n)) * 0.05).astype(np.float32)
+    u = (r.standard_normal((kk, n)) * 0.05).astype(np.float32)
+    dg, du = kernels.upload(g), kernels.upload(u)
+    dg.set_weight()
+    du.set_weight()
+    got = kernels.download(kernels.gated_matmul(kernels.upload(a), dg, du))
+    exp = orc.gated_matmul(a, g, u)
+    out.append(float(np.linalg.norm(got - exp) / np.linalg.norm(exp)))
+kernels.close()
+print(json.dumps(out))
+"""
+
+
+@pytest.mark.parametrize("env", [{"MAGNETAR_CUDA_ATTN_ONE_TILE": "1"}, {"MAGNETAR_CUDA_GEMM_RAW_WEIGHTS": "0"},
+                                 {"MAGNETAR_CUDA_GEMM_RAW_WEIGHTS": "1"}])
+def test_switched_paths_in_a_fresh_process(env):
+    # Paths chosen once per process by a switch: the one-query-tile attention kernel (with its Q
+    # split pass) and the GEMM's weight form forced prepared or raw at every k, against the oracle.
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = subprocess.run([sys.executable, "-c", _SWITCHED_PATHS_CHILD, root], env=dict(os.environ, **env),
+                         capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    errs = json.loads(res.stdout.strip().splitlines()[-1])
+    assert len(errs) == 5 and max(errs) <= TOL_MATMUL, errs
+
+
 @pytest.mark.parametrize("m,k,n", [(16, 2048, 1000), (8, 512, 1376), (13, 4096, 128)])
 def test_fewrow_tensor_core_epilogues(kernels, oracle, m, k, n):
     r = rng(18)
