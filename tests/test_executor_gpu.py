@@ -522,6 +522,83 @@ def test_replay_step_with_host_io(executor, oracle, mpc):
     assert e.value.code == "ExecutionFailed"
 
 
+def test_replay_step_with_pinned_host_io(executor, oracle, mpc):
+    # Pinned host buffers take the one-launch form: the step's own nodes with the SMs' copies
+    # before its first nodes and after its last kernels (the output copy hangs off them by
+    # programmatic edges and waits for them in the kernel).  The output buffer is cleared
+    # before each replay so that a copy that ran early would show.
+    torch = pytest.importorskip("torch")
+    layer = importlib.import_module("magnetar-provider-cuda_b200.layer")
+    cfg = layer.DecoderLayerConfig()
+    w = layer.make_inputs(cfg, seed=0)
+    layer.load(executor, w)
+    layer.forward(executor, cfg)
+    layer.capture(executor, cfg)
+    ids_h = torch.empty(cfg.seq, dtype=torch.float32).pin_memory()
+    out_h = torch.empty((cfg.seq, cfg.hidden), dtype=torch.float32).pin_memory()
+    replay = executor.step_io({"ids": ids_h}, {"out": out_h})
+    for seed in (1, 2, 3):
+        ids = np.random.default_rng(seed).integers(0, cfg.vocab, cfg.seq).astype(np.float32)
+        ids_h.numpy()[:] = ids
+        out_h.fill_(float("nan"))
+        replay()
+        got = out_h.numpy().copy()
+        assert rel(got, _oracle_layer(oracle, cfg, dict(w, ids=ids))) <= 1e-4
+        np.testing.assert_array_equal(got, executor.read_tensor("out"))
+    ids_h[0] = -1.0  # the embedding-id word rides along with the output copy
+    with pytest.raises(mpc.CudaError) as e:
+        replay()
+    assert e.value.code == "ShapeUnsupported"
+
+
+def test_pinned_host_io_replays_a_decode_step_at_advancing_offsets(executor, oracle):
+    # The advancing form with pinned host I/O: the replay's offset word is a copy node before the
+    # step's first nodes, the query, key and value rows come in and the attention output goes
+    # out in the same launch, at offsets 0, 1, 2, ...
+    torch = pytest.importorskip("torch")
+    r = np.random.default_rng(9)
+    cap, prefix, heads, kvh, d = 200, 30, 4, 2, 64
+    kc = np.zeros((cap, kvh * d), np.float32)
+    vc = np.zeros((cap, kvh * d), np.float32)
+    kc[:prefix] = r.standard_normal((prefix, kvh * d))
+    vc[:prefix] = r.standard_normal((prefix, kvh * d))
+    executor.write_tensor("kc", kc)
+    executor.write_tensor("vc", vc)
+    pinned = {n: torch.zeros((1, w), dtype=torch.float32).pin_memory()
+              for n, w in (("q", heads * d), ("k", kvh * d), ("v", kvh * d))}
+    for n, x in pinned.items():
+        executor.write_tensor(n, x.numpy())
+    o_h = torch.empty((1, heads * d), dtype=torch.float32).pin_memory()
+    invs = [inv("rope", ["q"], "qr", {"dimension": d, "head_count": heads, "position_offset": prefix}),
+            inv("rope", ["k"], "kr", {"dimension": d, "head_count": kvh, "position_offset": prefix}),
+            inv("kv-write", ["kc", "kr"], "kc", {"row_offset": prefix}),
+            inv("kv-write", ["vc", "v"], "vc", {"row_offset": prefix}),
+            inv("attention", ["qr", "kc", "vc"], "o",
+                {"head_count": heads, "head_dimension": d, "kv_head_count": kvh, "causal": True,
+                 "key_count": prefix + 1})]
+    executor.begin_step_capture(advancing=("position_offset", "row_offset", "key_count"))
+    for i in invs:
+        executor.run(i)
+    executor.end_step_capture()
+    replay = executor.step_io(pinned, {"o": o_h})
+    kc_exp, vc_exp = kc.copy(), vc.copy()
+    for t in range(5):
+        g = np.random.default_rng(200 + t)
+        for n, x in pinned.items():
+            x.numpy()[:] = g.standard_normal(x.shape).astype(np.float32)
+        o_h.fill_(float("nan"))
+        replay(t)
+        pos = prefix + t
+        q, k, v = (pinned[n].numpy() for n in ("q", "k", "v"))
+        qr = oracle.rope(q, base=10000.0, dimension=d, head_count=heads, position_offset=pos)
+        kr = oracle.rope(k, base=10000.0, dimension=d, head_count=kvh, position_offset=pos)
+        kc_exp[pos] = kr[0]
+        vc_exp[pos] = v[0]
+        exp = oracle.attention(qr, kc_exp[:pos + 1], vc_exp[:pos + 1], heads, d, kv_head_count=kvh, causal=True)
+        assert rel(o_h.numpy(), exp) <= 1e-4, t
+    np.testing.assert_array_equal(executor.read_tensor("vc"), vc_exp)
+
+
 def _grow_scratch_and_allocate(mpc, kernels, oracle):
     """Non-captured work that grows every scratch workspace the layer's step uses (a larger
     matmul's A/B splits, attention partials and splits), then allocations that could land on
