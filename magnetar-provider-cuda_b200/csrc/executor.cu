@@ -56,7 +56,7 @@ struct CapturedStep {
     std::map<std::string, uint64_t> embedding_ids;
     uint64_t storage_gen = 0, prep_gen = 0;  // when the recorded state was last known current
     // Replays with host I/O whose host memory is pinned run as one graph launch: the input
-    // copies, the replay offset, the step itself (a child graph), the output copies and the
+    // copies, the replay offset, the step's own nodes (cloned), the output copies and the
     // embedding-flag read and reset, built once per distinct set of host buffers and kept here.
     struct IoGraph {
         std::vector<mg_step_io> io;  // the host side (ids point into `names`)
@@ -1301,8 +1301,10 @@ void* mapped_host(void* p) {
 __global__ void __launch_bounds__(256) io_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                                       uint64_t bytes, int* flag, int* flag_host) {
     // An output copy hangs off the step's last kernels by programmatic edges: it is scheduled
-    // while they finish and waits here for their completion and memory (at once otherwise).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // while they finish and waits here for their completion and memory (at once otherwise).  An
+    // input copy lets the step's first kernels be scheduled while it runs; they wait for it in
+    // their own pdl_enter().
+    pdl_enter();
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x, nth = (uint64_t)gridDim.x * blockDim.x;
     const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
     const uint64_t n16 = vec ? bytes / 16 : 0;
@@ -1333,9 +1335,27 @@ bool graph_ends(cudaGraph_t graph, std::vector<cudaGraphNode_t>& roots, std::vec
     return true;
 }
 
-// Edges from each of `from` to `to`.  With `to_waits` (an io_copy_kernel node, which starts with
-// griddepcontrol.wait) an edge from a kernel node is programmatic, so the copy is scheduled while
-// that kernel finishes; every other edge is a plain one.
+// Whether every kernel node of `graph` is one of the library's own launches: the step counted
+// `kernels` of them while it was captured, and each starts with pdl_enter(), so it waits for an
+// upstream grid before it reads memory and may take a programmatic edge.  (A step captured under
+// a tensor-parallel plan also holds the communication library's kernels.)
+bool only_library_kernels(cudaGraph_t graph, uint64_t kernels) {
+    size_t n = 0;
+    if (cudaGraphGetNodes(graph, nullptr, &n) != cudaSuccess) return false;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (n && cudaGraphGetNodes(graph, nodes.data(), &n) != cudaSuccess) return false;
+    uint64_t count = 0;
+    for (cudaGraphNode_t node : nodes) {
+        cudaGraphNodeType type;
+        if (cudaGraphNodeGetType(node, &type) != cudaSuccess) return false;
+        count += type == cudaGraphNodeTypeKernel;
+    }
+    return count == kernels;
+}
+
+// Edges from each of `from` to `to`.  With `to_waits` (`to` is a kernel node that starts with
+// pdl_enter()) an edge from a kernel node is programmatic, so `to` is scheduled while that kernel
+// finishes and waits for it in the kernel; every other edge is a plain one.
 bool add_edges(cudaGraph_t graph, const std::vector<cudaGraphNode_t>& from, cudaGraphNode_t to, bool to_waits) {
     for (cudaGraphNode_t f : from) {
         cudaGraphEdgeData e = {};
@@ -1390,6 +1410,7 @@ CapturedStep::IoGraph* io_graph_for(mg_executor* ex, CapturedStep* st, const mg_
     bool ok = cudaGraphClone(&g->graph, st->graph) == cudaSuccess;
     std::vector<cudaGraphNode_t> roots, leaves;
     if (ok) ok = graph_ends(g->graph, roots, leaves);
+    const bool roots_wait = ok && only_library_kernels(g->graph, st->kernels);
     std::vector<cudaGraphNode_t> before;
     for (int i = 0; ok && i < count; i++) {
         g->names.push_back(io[i].id);
@@ -1413,7 +1434,11 @@ CapturedStep::IoGraph* io_graph_for(mg_executor* ex, CapturedStep* st, const mg_
                                           cudaMemcpyHostToDevice) == cudaSuccess;
         if (ok) before.push_back(n);
     }
-    for (size_t r = 0; ok && r < roots.size(); r++) ok = add_edges(g->graph, before, roots[r], false);
+    for (size_t r = 0; ok && r < roots.size(); r++) {
+        cudaGraphNodeType type;
+        ok = cudaGraphNodeGetType(roots[r], &type) == cudaSuccess &&
+             add_edges(g->graph, before, roots[r], roots_wait && type == cudaGraphNodeTypeKernel);
+    }
     // what the output copies follow: the step's last nodes (the input copies for an empty step)
     const std::vector<cudaGraphNode_t>& last = leaves.empty() ? before : leaves;
     // The embedding-id word rides along with the first output copy done by the SMs.

@@ -814,6 +814,7 @@ mg_status launch_cluster(Device* d, GemvClusterArgs p, uint64_t col_tiles, const
 // bfloat16 value (nonzero low 16 bits), and dst is then not used.
 __global__ void __launch_bounds__(256) compact_bf16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst,
                                                            uint64_t quads, int* not_exact) {
+    pdl_enter();  // the weight may have just been written by the kernel before this one
     uint32_t low = 0;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += (uint64_t)gridDim.x * blockDim.x) {
         const float4 v = src[i];
