@@ -569,9 +569,11 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     auto pv_done = [&](int t, int b) { return b0 + 120 + 8u * (uint32_t)(2 * t + b); };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-    // Heavy (late) query pairs first: causal pairs near the end see the most keys.
-    const int qp = p.q_pairs - 1 - (int)blockIdx.x;
-    const uint64_t head = blockIdx.y;
+    // Heavy (late) query pairs first across all heads (the grid's x runs over heads): causal
+    // pairs near the end see the most keys, and CTAs start in grid order, so the light pairs fill
+    // the machine's last wave instead of heavy ones.
+    const int qp = p.q_pairs - 1 - (int)blockIdx.y;
+    const uint64_t head = blockIdx.x;
     const uint64_t kvh = head / p.group;
     const uint64_t q0 = (uint64_t)qp * 2 * AQ;
     uint64_t key_lo = 0;
@@ -1041,7 +1043,7 @@ mg_status launch_attention_tc2(Device* d, const k::AttentionArgs& a, const CUten
     const int e = 118 - kAttnLazyLog2 - lg;
     p.safe_bits = (unsigned)(e + 127) << 23;
     p.error = d->flags + 2;
-    dim3 grid((unsigned)p.q_pairs, (unsigned)a.head_count);
+    dim3 grid((unsigned)a.head_count, (unsigned)p.q_pairs);
     enqueue(d, attention_tc2_kernel<D>, grid, kAttnTcThreads, S::kSmem, maps[2], maps[3], maps[4], maps[5], p);
     return launched(d, "tensor-core attention launch");
 }
@@ -1062,10 +1064,12 @@ bool attention_tc_eligible(const AttentionArgs& a) {
 mg_status attention_tc(Device* d, const AttentionArgs& a) {
     const uint64_t S = a.seq_len, Skv = a.kv_seq_len, qd = a.q_model_dim, kvd = a.kv_model_dim;
     const uint64_t skv_p = (Skv + 7) & ~7ull;  // V^T rows are 16-byte multiples
-    static const bool one_tile = [] {
+    static const bool one_tile_env = [] {
         const char* e = getenv("MAGNETAR_CUDA_ATTN_ONE_TILE");
         return e && atoi(e) != 0;
     }();
+    // the two-tile kernel's query pairs run along the grid's y (at most 65,535 of them)
+    const bool one_tile = one_tile_env || (S + 2 * AQ - 1) / (2 * AQ) > 65535;
     // Q's terms only for the one-tile kernel: the two-tile kernel splits its query rows itself.
     const size_t q_elems = one_tile ? S * qd : 0, k_elems = Skv * kvd, vt_elems = kvd * skv_p;
     uint16_t* ws = nullptr;
