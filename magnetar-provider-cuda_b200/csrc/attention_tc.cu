@@ -22,6 +22,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "internal.h"
 #include "sm100.cuh"
@@ -742,29 +743,41 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         const uint64_t qi = q0 + (uint64_t)t * AQ + r;
         const bool live = qi < p.seq_len;
         {
-            // This thread's query row as bf16 hi / lo terms in the MMA's K-major layout: 64
-            // columns per 128-byte row of an atom, 16-byte chunk c at position c ^ (r % 8); zeros
-            // past the sequence.  (Each query row belongs to this CTA alone, so it is split here
-            // rather than by a pass over Q.)
-            const float* qrow = p.q + (live ? qi : 0) * p.q_ld + head * D;
-            uint8_t* qt = base_ptr + S::kOffQ + (size_t)(2 * t) * S::kQ + (size_t)r * 128;
+            // This warp's 32 query rows (the rows its lanes own) as bf16 hi / lo terms in the MMA's
+            // K-major layout: 64 columns per 128-byte row of an atom, 16-byte chunk c at position
+            // c ^ (row % 8); zeros past the sequence.  (Each query row belongs to this CTA alone,
+            // so it is split here rather than by a pass over Q.)  The warp reads one row per load,
+            // each lane D / 32 consecutive columns, so a load touches the row's own cache lines
+            // only; all 32 rows' loads are in flight before the first is split.
+            constexpr int V = D / 32;  // columns per lane: 4 (D = 128) or 2 (D = 64)
+            using Vec = typename std::conditional<V == 4, float4, float2>::type;
+            const uint64_t row0 = q0 + (uint64_t)t * AQ + (uint64_t)qq * 32;
+            Vec xv[32];
 #pragma unroll
-            for (int c8 = 0; c8 < D / 8; c8++) {  // eight columns: one 16-byte chunk per term
-                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-                if (live) {
-                    x0 = __ldg(reinterpret_cast<const float4*>(qrow + 8 * c8));
-                    x1 = __ldg(reinterpret_cast<const float4*>(qrow + 8 * c8 + 4));
+            for (int i = 0; i < 32; i++) {
+                const bool row_live = row0 + i < p.seq_len;
+                const float* src = p.q + (row_live ? row0 + i : 0) * p.q_ld + head * D + lane * V;
+                if (row_live) xv[i] = __ldg(reinterpret_cast<const Vec*>(src));
+                else xv[i] = Vec{};
+            }
+            uint8_t* qt0 = base_ptr + S::kOffQ + (size_t)(2 * t) * S::kQ;
+            const int e0 = lane * V;  // this lane's first column
+            const int a = e0 / 64, c = (e0 % 64) / 8, byte = (e0 % 8) * 2;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const int rr = qq * 32 + i;
+                const size_t off = (size_t)a * S::kQAtom + (size_t)rr * 128 + (size_t)((c ^ (rr & 7)) * 16 + byte);
+                const float* xs = reinterpret_cast<const float*>(&xv[i]);
+                uint16_t h[V], lo[V];
+#pragma unroll
+                for (int e = 0; e < V; e++) split_bf16(xs[e], h[e], lo[e]);
+                if constexpr (V == 4) {
+                    *reinterpret_cast<uint2*>(qt0 + off) = make_uint2(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]));
+                    *reinterpret_cast<uint2*>(qt0 + S::kQ + off) = make_uint2(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]));
+                } else {
+                    *reinterpret_cast<uint32_t*>(qt0 + off) = pack_bf16(h[0], h[1]);
+                    *reinterpret_cast<uint32_t*>(qt0 + S::kQ + off) = pack_bf16(lo[0], lo[1]);
                 }
-                const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                uint16_t h[8], lo[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) split_bf16(xs[e], h[e], lo[e]);
-                const int a = c8 / 8, c = c8 % 8;
-                const size_t off = (size_t)a * S::kQAtom + (size_t)((c ^ (r & 7)) * 16);
-                *reinterpret_cast<uint4*>(qt + off) =
-                    make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
-                *reinterpret_cast<uint4*>(qt + S::kQ + off) = make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]),
-                                                                          pack_bf16(lo[4], lo[5]), pack_bf16(lo[6], lo[7]));
             }
             fence_proxy_async();  // the generic-proxy writes are read by tcgen05.mma
             mbar_arrive_warp(q_full);
