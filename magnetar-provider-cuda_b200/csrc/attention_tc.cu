@@ -936,7 +936,14 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         if (failed) atomicExch(p.error, 1);
         const float fin = safe ? 1.0f : (l > 0.0f ? 1.0f / l : 0.0f);
         if (have) tc_fence_after();
-        float* orow = p.out + qi * p.out_dim + head * D;
+        // The output rows leave through shared memory.  Each thread writes its row into its warp's
+        // staging area -- this tile's query terms, which no MMA reads once P.V of its last key
+        // tile has completed -- with 16-byte chunk k of row i at position k ^ i; then the warp
+        // stores one row per instruction, each lane 16 consecutive bytes (coalesced).
+        constexpr int kChunks = D / 4;               // 16-byte chunks per row
+        constexpr int kRowsPerStore = 32 / kChunks;  // rows one warp store covers
+        uint8_t* stage = base_ptr + S::kOffQ + (size_t)(2 * t) * S::kQ + (size_t)qq * (32 * D * 4);
+        fence_proxy_async();  // after the MMAs' reads of this area, before generic writes
 #pragma unroll
         for (int c = 0; c < D; c += 32) {
             float o[32];
@@ -947,11 +954,21 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 32; e++) o[e] = 0.0f;
             }
-            if (live)
 #pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    *reinterpret_cast<float4*>(orow + c + e) =
-                        make_float4(o[e] * fin, o[e + 1] * fin, o[e + 2] * fin, o[e + 3] * fin);
+            for (int e = 0; e < 32; e += 4) {
+                const int k = (c + e) / 4;
+                *reinterpret_cast<float4*>(stage + (size_t)lane * (D * 4) + (size_t)(((k ^ lane) % kChunks) * 16)) =
+                    make_float4(o[e] * fin, o[e + 1] * fin, o[e + 2] * fin, o[e + 3] * fin);
+            }
+        }
+        __syncwarp();
+        const uint64_t row0 = q0 + (uint64_t)t * AQ + (uint64_t)qq * 32;
+#pragma unroll 4
+        for (int i0 = 0; i0 < 32; i0 += kRowsPerStore) {
+            const int i = i0 + lane / kChunks, k = lane % kChunks;
+            const float4 v = *reinterpret_cast<const float4*>(stage + (size_t)i * (D * 4) + (size_t)(((k ^ i) % kChunks) * 16));
+            if (row0 + i < p.seq_len)
+                *reinterpret_cast<float4*>(p.out + (row0 + i) * p.out_dim + head * D + 4 * k) = v;
         }
     }
 
